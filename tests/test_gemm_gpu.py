@@ -1,0 +1,56 @@
+"""tcgen05 GEMM numerics vs an fp32 PyTorch reference (forward / dgrad / wgrad layouts, batched, odd shapes)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(a, b, a_mn, b_mn):
+    A = a.float().mT if a_mn else a.float()
+    B = b.float() if b_mn else b.float().mT
+    return A @ B
+
+
+def _rel(x, y):
+    return ((x.float() - y.float()).norm() / y.float().norm().clamp_min(1e-12)).item()
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 1024), (200, 136, 72), (1000, 384, 520), (64, 8, 8),
+                                   (4096, 2048, 2048)])
+def test_gemm_layouts(a_mn, b_mn, M, N, K):
+    from trenowanie_generatora_obrazkow_b200.ops.gemm import gemm
+    from trenowanie_generatora_obrazkow_b200.ops._ext import check_errors
+    torch.manual_seed(0)
+    a = torch.randn(*((K, M) if a_mn else (M, K)), device="cuda").bfloat16()
+    b = torch.randn(*((K, N) if b_mn else (N, K)), device="cuda").bfloat16()
+    c = gemm(a, b, a_mn=a_mn, b_mn=b_mn)
+    torch.cuda.synchronize()
+    check_errors()
+    assert _rel(c, _ref(a, b, a_mn, b_mn)) < 1e-2
+
+
+def test_gemm_fp32_accumulate_and_beta():
+    from trenowanie_generatora_obrazkow_b200.ops.gemm import gemm
+    torch.manual_seed(1)
+    a = torch.randn(384, 256, device="cuda").bfloat16()
+    b = torch.randn(384, 320, device="cuda").bfloat16()
+    out = torch.randn(256, 320, device="cuda")
+    ref = out + _ref(a, b, True, True)
+    gemm(a, b, out=out, a_mn=True, b_mn=True, accumulate=True)
+    assert _rel(out, ref) < 1e-3
+    x = torch.randn(3, 128, 256, device="cuda").bfloat16()
+    d = torch.randn(3, 128, 128, device="cuda").bfloat16()
+    c = gemm(x, x, d=d, alpha=0.5, beta=-2.0)
+    ref = 0.5 * (x.float() @ x.float().mT) - 2.0 * d.float()
+    assert _rel(c, ref) < 1e-2
+
+
+def test_gemm_batched_strided():
+    from trenowanie_generatora_obrazkow_b200.ops.gemm import gemm
+    torch.manual_seed(2)
+    base = torch.randn(4, 192, 512, device="cuda").bfloat16()
+    a = base[:, :, :256]  # row stride 512
+    b = torch.randn(4, 256, 192, device="cuda").bfloat16()
+    c = gemm(a, b, b_mn=True)
+    assert _rel(c, a.float() @ b.float()) < 1e-2

@@ -1,0 +1,315 @@
+// Persistent warp-specialised bf16 GEMM for sm_100a: TMA -> SMEM ring -> tcgen05.mma (one elected thread) ->
+// double-buffered TMEM accumulators -> fused epilogue.
+//
+//   C[b, m, n] = alpha * sum_k A[b, m, k] * B[b, n, k]  (+ beta * D[b, m, n])      (bf16 or fp32 output)
+//
+// A and B may each be stored K-major (contraction dim contiguous) or MN-major (output dim contiguous); the
+// instruction descriptor's transpose bits select the shared-memory layout, so the same kernel serves
+//   forward  y  = x  @ W^T   (A K-major,  B K-major)
+//   dgrad    dx = dy @ W     (A K-major,  B MN-major)
+//   wgrad    dW = dy^T @ x   (A MN-major, B MN-major)
+// and the Newton-Schulz products of the Muon optimizer (X X^T, A A, B X).
+//
+// Roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer, warps 2-5 = epilogue
+// (warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31, i.e. rows of the 128-row tile).
+// Replaces the cuBLAS Linear GEMMs (reference aurora/model.py:102-188 under autocast) and the cuBLAS baddbmm of
+// the Newton-Schulz step (reference aurora/ns_triton.py:78).
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tgo {
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+enum GemmEpi { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2 };
+
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KB
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;       // 16 or 32 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (256 or 512 columns)
+};
+
+template <int EPI>
+__device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int b, int row, int col0, const uint32_t (&r)[32]) {
+  if (row >= p.M || col0 >= p.N) return;
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+  const bool full = col0 + 32 <= p.N;
+  if constexpr (EPI == EPI_BF16) {
+    if (p.D != nullptr) {
+      const __nv_bfloat16* d = p.D + (long long)b * p.bsd + (long long)row * p.ldd + col0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (full || col0 + j * 8 < p.N) {
+          uint4 u = *reinterpret_cast<const uint4*>(d + j * 8);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float2 f = __bfloat1622float2(h[e]);
+            v[j * 8 + 2 * e] += p.beta * f.x;
+            v[j * 8 + 2 * e + 1] += p.beta * f.y;
+          }
+        }
+      }
+    }
+    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)b * p.bsc + (long long)row * p.ldc + col0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (full || col0 + j * 8 < p.N) {
+        uint4 u;
+        u.x = pack_bf16x2(v[j * 8 + 0], v[j * 8 + 1]);
+        u.y = pack_bf16x2(v[j * 8 + 2], v[j * 8 + 3]);
+        u.z = pack_bf16x2(v[j * 8 + 4], v[j * 8 + 5]);
+        u.w = pack_bf16x2(v[j * 8 + 6], v[j * 8 + 7]);
+        *reinterpret_cast<uint4*>(c + j * 8) = u;
+      }
+    }
+  } else {
+    float* c = reinterpret_cast<float*>(p.C) + (long long)b * p.bsc + (long long)row * p.ldc + col0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (full || col0 + j * 4 < p.N) {
+        float4 o = make_float4(v[j * 4], v[j * 4 + 1], v[j * 4 + 2], v[j * 4 + 3]);
+        if constexpr (EPI == EPI_F32_ACC) {
+          float4 old = *reinterpret_cast<const float4*>(c + j * 4);
+          o.x += old.x;
+          o.y += old.y;
+          o.z += old.z;
+          o.w += old.w;
+        }
+        *reinterpret_cast<float4*>(c + j * 4) = o;
+      }
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar[2];
+  __shared__ __align__(8) uint64_t tempty_bar[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_sh;
+
+  const int warp = warp_id(), lane = lane_id();
+  const int num_m = (p.M + GEMM_BM - 1) / GEMM_BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int tiles_per_batch = num_m * num_n;
+  const int num_tiles = tiles_per_batch * p.batch;
+  const int num_kb = (p.K + GEMM_BK - 1) / GEMM_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 4);  // one arrival per epilogue warp
+    }
+    abort_sh = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !abort_sh; tile += gridDim.x) {
+        const int b = tile / tiles_per_batch, r = tile % tiles_per_batch;
+        const int m0 = (r / num_n) * GEMM_BM, n0 = (r % num_n) * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+            abort_sh = 1;
+            break;
+          }
+          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sb = sa + Cfg::A_BYTES;
+          mbar_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          const int k0 = kb * GEMM_BK;
+          if constexpr (!A_MN) {
+            tma_load_3d(sa, &tmA, &full_bar[stage], k0, m0, b);
+          } else {
+            tma_load_3d(sa, &tmA, &full_bar[stage], m0, k0, b);
+            tma_load_3d(sa + 8192, &tmA, &full_bar[stage], m0 + 64, k0, b);
+          }
+          if constexpr (!B_MN) {
+            tma_load_3d(sb, &tmB, &full_bar[stage], k0, n0, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sb + j * 8192, &tmB, &full_bar[stage], n0 + j * 64, k0, b);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // On abort, wait (bounded) until the copies already issued have landed before the CTA can exit.
+      if (abort_sh) {
+        for (int s = 0; s < STAGES; ++s) mbar_wait(&full_bar[s], 0, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = idesc_bf16_f32(GEMM_BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !abort_sh; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, p.err, ERR_MBAR_TIMEOUT_MMA)) {
+          abort_sh = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, p.err, ERR_MBAR_TIMEOUT_MMA)) {
+            abort_sh = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sdesc_sw128(sa + k * 2048, 8192, 1024) : sdesc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(sb + k * 2048, 8192, 1024) : sdesc_sw128(sb + k * 32, 16, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);  // frees the stage once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);  // accumulator ready for the epilogue
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&tfull_bar[acc], acc_phase, p.err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        abort_sh = 1;
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      const int b = tile / tiles_per_batch, r = tile % tiles_per_batch;
+      const int m0 = (r / num_n) * GEMM_BM, n0 = (r % num_n) * BN;
+      const int row = m0 + q * 32 + lane;
+      const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tbase + c * 32, v);
+        tmem_ld_wait();
+        gemm_store_chunk<EPI>(p, b, row, n0 + c * 32, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+
+// ----------------------------------------------------------------------------------------------------------------
+// Launch (tensor maps are encoded by the host wrapper in ops.cpp)
+// ----------------------------------------------------------------------------------------------------------------
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    attr_set = true;
+  }
+  const int num_tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * ((p.N + BN - 1) / BN) * p.batch;
+  const int grid = std::max(1, std::min(num_tiles, num_sms()));
+  kern<<<grid, GEMM_THREADS, Cfg::SMEM, stream>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+template <int BN, int EPI>
+static cudaError_t dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                                  const GemmParams& p, cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_gemm<BN, false, false, EPI>(ta, tb, p, s);
+  if (!a_mn && b_mn) return launch_gemm<BN, false, true, EPI>(ta, tb, p, s);
+  if (a_mn && !b_mn) return launch_gemm<BN, true, false, EPI>(ta, tb, p, s);
+  return launch_gemm<BN, true, true, EPI>(ta, tb, p, s);
+}
+
+cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int bn, bool a_mn,
+                        bool b_mn, int epi, cudaStream_t s) {
+  if (bn == 128) {
+    if (epi == EPI_BF16) return dispatch_major<128, EPI_BF16>(a_mn, b_mn, ta, tb, p, s);
+    if (epi == EPI_F32) return dispatch_major<128, EPI_F32>(a_mn, b_mn, ta, tb, p, s);
+    return dispatch_major<128, EPI_F32_ACC>(a_mn, b_mn, ta, tb, p, s);
+  }
+  if (epi == EPI_BF16) return dispatch_major<256, EPI_BF16>(a_mn, b_mn, ta, tb, p, s);
+  if (epi == EPI_F32) return dispatch_major<256, EPI_F32>(a_mn, b_mn, ta, tb, p, s);
+  return dispatch_major<256, EPI_F32_ACC>(a_mn, b_mn, ta, tb, p, s);
+}
+
+}  // namespace tgo
