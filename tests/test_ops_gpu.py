@@ -1,0 +1,142 @@
+"""Fused sm_100a ops (forward and backward) vs fp32 PyTorch references of the same math."""
+import pytest
+import torch
+
+from trenowanie_generatora_obrazkow_b200.ops import fused as Fz
+from trenowanie_generatora_obrazkow_b200.ops import reference as R
+
+pytestmark = pytest.mark.gpu
+
+
+def rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+
+
+@pytest.mark.parametrize("D,T,with_res,with_gate,with_mod", [(2048, 256, True, True, True), (576, 64, True, False, False),
+                                                             (1024, 128, False, False, True), (3072, 96, True, True, True)])
+def test_adanorm(D, T, with_res, with_gate, with_mod):
+    torch.manual_seed(0)
+    B = 3
+    x = torch.randn(B, T, D, device="cuda").bfloat16().requires_grad_()
+    y = torch.randn(B, T, D, device="cuda").bfloat16().requires_grad_() if with_res else None
+    mod = (0.3 * torch.randn(B, 6, D, device="cuda")).bfloat16().requires_grad_()
+    w = (1 + 0.1 * torch.randn(D, device="cuda")).requires_grad_()
+    gout = [torch.randn(B, T, D, device="cuda").bfloat16(), torch.randn(B, T, D, device="cuda").bfloat16()]
+
+    def run(x, y, mod, w, cuda):
+        gate = mod[:, 2] if with_gate else None
+        shift, scale = (mod[:, 0], mod[:, 1]) if with_mod else (None, None)
+        if cuda:
+            return Fz.adanorm(x, y, gate, w, shift, scale)
+        xf = x.float()
+        xn = xf if y is None else xf + (y.float() if gate is None else gate.float()[:, None] * y.float())
+        h = R.rmsnorm(xn, w)
+        if with_mod:
+            h = h * (1 + scale.float()[:, None]) + shift.float()[:, None]
+        return xn, h
+
+    ins = [x, y, mod, w]
+    xs = [t.detach().clone().requires_grad_() if t is not None else None for t in ins]
+    outs = run(*xs, True)
+    if with_res:
+        torch.autograd.backward(list(outs), gout)
+    else:
+        torch.autograd.backward([outs[1]], [gout[1]])
+    xr = [t.detach().clone().requires_grad_() if t is not None else None for t in ins]
+    refs = run(*xr, False)
+    if with_res:
+        torch.autograd.backward(list(refs), [g.float() for g in gout])
+    else:
+        torch.autograd.backward([refs[1]], [gout[1].float()])
+    assert rel(outs[1], refs[1]) < 1.5e-2
+    if with_res:
+        assert rel(outs[0], refs[0]) < 1e-2
+    for a, b in zip(xs, xr):
+        if a is None or b.grad is None:
+            continue
+        assert a.grad is not None
+        assert rel(a.grad, b.grad) < 3e-2, (a.shape, rel(a.grad, b.grad))
+
+
+@pytest.mark.parametrize("hd,hq,hkv,norm,rope,T,kv_mask", [(128, 4, 4, True, True, 256, False),
+                                                          (64, 6, 2, False, True, 77, True),
+                                                          (128, 2, 2, True, False, 130, False),
+                                                          (64, 9, 3, False, True, 64, True)])
+def test_self_attention_core(hd, hq, hkv, norm, rope, T, kv_mask):
+    torch.manual_seed(1)
+    B = 2
+    C = (hq + 2 * hkv) * hd
+    qkv = torch.randn(B, T, C, device="cuda").bfloat16()
+    qw = (1 + 0.1 * torch.randn(hd, device="cuda")) if norm else None
+    kw = (1 + 0.1 * torch.randn(hd, device="cuda")) if norm else None
+    cos, sin = R.rope_1d_table(T, hd, device="cuda") if rope else (None, None)
+    kv_len = torch.tensor([T, max(1, T // 3)], device="cuda", dtype=torch.int32) if kv_mask else None
+    do = torch.randn(B, T, hq * hd, device="cuda").bfloat16()
+
+    a = qkv.clone().requires_grad_()
+    qa = qw.clone().requires_grad_() if norm else None
+    ka = kw.clone().requires_grad_() if norm else None
+    o = Fz.self_attention_core(a, hq, hkv, hd, qa, ka, cos, sin, kv_len)
+    o.backward(do)
+
+    b = qkv.float().cpu().requires_grad_()
+    qb = qw.cpu().requires_grad_() if norm else None
+    kb = kw.cpu().requires_grad_() if norm else None
+    ref = Fz.self_attention_core(b, hq, hkv, hd, qb, kb,
+                                 None if cos is None else cos.cpu(), None if sin is None else sin.cpu(),
+                                 None if kv_len is None else kv_len.cpu())
+    ref.backward(do.float().cpu())
+    assert rel(o.cpu(), ref) < 2e-2
+    assert rel(a.grad.cpu(), b.grad) < 4e-2
+    if norm:
+        assert rel(qa.grad.cpu(), qb.grad) < 4e-2
+        assert rel(ka.grad.cpu(), kb.grad) < 4e-2
+
+
+@pytest.mark.parametrize("D,heads,T,L", [(2048, 16, 256, 128), (576, 9, 100, 40)])
+def test_cross_attention_core(D, heads, T, L):
+    torch.manual_seed(2)
+    B = 3
+    q = torch.randn(B, T, D, device="cuda").bfloat16()
+    kv = torch.randn(B, L, 2 * D, device="cuda").bfloat16()
+    kv_len = torch.tensor([L, 1, L // 2], device="cuda", dtype=torch.int32)
+    do = torch.randn(B, T, D, device="cuda").bfloat16()
+    qa, kva = q.clone().requires_grad_(), kv.clone().requires_grad_()
+    o = Fz.cross_attention_core(qa, kva, heads, kv_len)
+    o.backward(do)
+    qb, kvb = q.float().cpu().requires_grad_(), kv.float().cpu().requires_grad_()
+    ref = Fz.cross_attention_core(qb, kvb, heads, kv_len.cpu())
+    ref.backward(do.float().cpu())
+    assert rel(o.cpu(), ref) < 2e-2
+    assert rel(qa.grad.cpu(), qb.grad) < 4e-2
+    assert rel(kva.grad.cpu(), kvb.grad) < 4e-2
+
+
+def test_swiglu():
+    torch.manual_seed(3)
+    ab = torch.randn(4, 100, 2 * 1536, device="cuda").bfloat16()
+    dg = torch.randn(4, 100, 1536, device="cuda").bfloat16()
+    a = ab.clone().requires_grad_()
+    g = Fz.swiglu(a)
+    g.backward(dg)
+    b = ab.float().clone().requires_grad_()
+    gr = R.swiglu(b)
+    gr.backward(dg.float())
+    assert rel(g, gr) < 1e-2
+    assert rel(a.grad, b.grad) < 2e-2
+
+
+def test_linear_grad_accumulates_fp32():
+    torch.manual_seed(4)
+    lin = torch.nn.Linear(256, 384, bias=False).cuda()
+    x = torch.randn(2, 64, 256, device="cuda").bfloat16().requires_grad_()
+    for _ in range(2):
+        y = Fz.linear(x, lin)
+        y.float().square().mean().backward()
+    xr = x.detach().float().requires_grad_()
+    wr = lin.weight.detach().clone().requires_grad_()
+    for _ in range(2):
+        (xr @ wr.T).square().mean().backward()
+    assert lin.weight.grad.dtype == torch.float32
+    assert rel(lin.weight.grad, wr.grad) < 2e-2
+    assert rel(x.grad, xr.grad) < 2e-2

@@ -24,4 +24,90 @@ struct GemmParams {
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int bn, bool a_mn,
                         bool b_mn, int epi, cudaStream_t s);
 
+
+// ---------------------------------------------------------------- norms (norm.cu)
+struct AdaNormFwdParams {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* y;      // optional residual branch
+  const __nv_bfloat16* gate;   // optional [B, D] (batch stride gate_bs)
+  long long gate_bs;
+  const float* w;
+  const __nv_bfloat16* shift;  // optional [B, D] (batch stride mod_bs)
+  const __nv_bfloat16* scale;
+  long long mod_bs;
+  __nv_bfloat16* x_out;        // x + gate * y (when y is given)
+  __nv_bfloat16* h;
+  float* rstd;
+  int M, D, T, rows_per_cta;
+  float eps;
+};
+struct AdaNormBwdParams {
+  const __nv_bfloat16* dh;
+  const __nv_bfloat16* dxe;    // optional extra gradient into x_new
+  const __nv_bfloat16* xn;     // x_new
+  const float* rstd;
+  const float* w;
+  const __nv_bfloat16* scale;
+  long long mod_bs;
+  const __nv_bfloat16* y;
+  const __nv_bfloat16* gate;
+  long long gate_bs;
+  __nv_bfloat16* dx;
+  __nv_bfloat16* dy;
+  float* partial;              // scratch [B][chunks][4][D]
+  int M, D, T, chunks, rows_per_cta;
+};
+cudaError_t adanorm_fwd_launch(const AdaNormFwdParams& p, cudaStream_t s);
+cudaError_t adanorm_bwd_launch(const AdaNormBwdParams& p, float* dshift, float* dscale, float* dgate, float* dw,
+                               cudaStream_t s);
+
+struct QKNormRopeParams {
+  const __nv_bfloat16* qkv;    // [M, ld_qkv]: hq query heads, then hkv key heads (then values, untouched)
+  long long ld_qkv;
+  const float* q_w;            // optional per-head RMSNorm weights [hd]
+  const float* k_w;
+  const float* cos;            // optional [B?][T][hd] (batch stride rope_bs, 0 = shared)
+  const float* sin;
+  long long rope_bs;
+  __nv_bfloat16* q_out;        // [M, ld_q]
+  long long ld_q;
+  __nv_bfloat16* k_out;
+  long long ld_k;
+  float* rstd_q;               // [M, hq]
+  float* rstd_k;               // [M, hkv]
+  int M, T, hq, hkv, hd;
+  float eps;
+};
+cudaError_t qknorm_rope_fwd_launch(const QKNormRopeParams& p, cudaStream_t s);
+cudaError_t qknorm_rope_bwd_launch(const QKNormRopeParams& p, const __nv_bfloat16* dq, long long ld_dq,
+                                   const __nv_bfloat16* dk, long long ld_dk, __nv_bfloat16* dqkv, long long ld_dqkv,
+                                   float* dwq, float* dwk, cudaStream_t s);
+
+cudaError_t swiglu_fwd_launch(const __nv_bfloat16* ab, __nv_bfloat16* g, long long M, int H, cudaStream_t s);
+cudaError_t swiglu_bwd_launch(const __nv_bfloat16* ab, const __nv_bfloat16* dg, __nv_bfloat16* dab, long long M,
+                              int H, cudaStream_t s);
+
+
+// ---------------------------------------------------------------- attention (attention.cu)
+struct AttnParams {
+  const __nv_bfloat16* q;  // [B][Tq][Hq][hd] with strides (elements)
+  long long q_bs, q_ts, q_hs;
+  const __nv_bfloat16* k;  // [B][Tk][Hkv][hd]
+  long long k_bs, k_ts, k_hs;
+  const __nv_bfloat16* v;
+  long long v_bs, v_ts, v_hs;
+  __nv_bfloat16* o;        // [B][Tq][Hq][hd] (also the layout of dO)
+  long long o_bs, o_ts, o_hs;
+  float* lse;              // [B][Hq][Tq] natural-log sum-exp of the scaled logits
+  const int* kv_len;       // optional [B] valid key count (prefix mask)
+  int B, Tq, Tk, Hq, Hkv, rep, hd;
+  float scale;
+};
+cudaError_t attention_fwd_launch(const AttnParams& p, cudaStream_t s);
+// dq_acc: scratch fp32 [B][Tq][Hq][hd] (zeroed here); delta: scratch fp32 [B][Hq][Tq]; dq (bf16) optional.
+cudaError_t attention_bwd_launch(const AttnParams& p, const __nv_bfloat16* dO, float* delta, float* dq_acc,
+                                 __nv_bfloat16* dq, long long dq_bs, long long dq_ts, long long dq_hs,
+                                 __nv_bfloat16* dk, long long dk_bs, long long dk_ts, long long dk_hs,
+                                 __nv_bfloat16* dv, long long dv_bs, long long dv_ts, long long dv_hs, cudaStream_t s);
+
 }  // namespace tgo

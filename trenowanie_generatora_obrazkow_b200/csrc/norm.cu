@@ -1,0 +1,443 @@
+// Fused normalisation kernels (memory-bound; one pass over the activations each way).
+//
+// adanorm: residual update + RMSNorm + adaLN modulation of a DiT block
+//     x_new = x + gate * y            (gate per (batch, channel); optional; y optional)
+//     h     = rmsnorm(x_new) * w * (1 + scale) + shift                (scale / shift optional)
+//   reference aurora/model.py:27-34 (RMSNorm) and :204-210 (DenoiserBlock modulation and gated residuals).
+//   The backward produces dx, dy and the per-(batch, channel) sums dshift / dscale / dgate and the per-channel dw
+//   through per-CTA partial sums in a scratch buffer and a second reduction pass.
+//
+// qknorm_rope: per-head RMSNorm of q and k (optional) followed by interleaved-pair RoPE (reference
+//   aurora/model.py:37-40, :98-99, :164), reading the fused qkv GEMM output in place.
+//
+// swiglu: g = silu(a) * b on the fused in_proj output [a | b] (reference aurora/model.py:102-110).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tgo {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ void load8(const bf16* p, float (&f)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ void store8(bf16* p, const float (&f)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(f[0], f[1]);
+  u.y = pack_bf16x2(f[2], f[3]);
+  u.z = pack_bf16x2(f[4], f[5]);
+  u.w = pack_bf16x2(f[6], f[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16(v)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide sum; `red` holds 2 x 32 floats, `slot` alternates between consecutive calls so one barrier suffices.
+__device__ __forceinline__ float block_sum(float v, float* red, int slot) {
+  v = warp_sum(v);
+  const int nw = (blockDim.x + 31) >> 5;
+  if (lane_id() == 0) red[slot * 32 + warp_id()] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int i = 0; i < nw; ++i) s += red[slot * 32 + i];
+  return s;
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// adanorm forward
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void adanorm_fwd_kernel(AdaNormFwdParams p) {
+  __shared__ float red[64];
+  const int c0 = threadIdx.x * 8;
+  const bool active = c0 < p.D;
+  float w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = active ? p.w[c0 + i] : 0.f;
+  const int row0 = blockIdx.x * p.rows_per_cta;
+  const int row1 = min(p.M, row0 + p.rows_per_cta);
+  int slot = 0;
+  for (int row = row0; row < row1; ++row, slot ^= 1) {
+    const int b = row / p.T;
+    const long long off = (long long)row * p.D + c0;
+    float x[8];
+    float ss = 0.f;
+    if (active) {
+      load8(p.x + off, x);
+      if (p.y != nullptr) {
+        float y[8];
+        load8(p.y + off, y);
+        if (p.gate != nullptr) {
+          float g[8];
+          load8(p.gate + (long long)b * p.gate_bs + c0, g);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) x[i] = bf16_round(x[i] + bf16_round(g[i] * y[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) x[i] = bf16_round(x[i] + y[i]);
+        }
+        store8(p.x_out + off, x);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+    }
+    const float tot = block_sum(ss, red, slot);
+    const float r = rsqrtf(tot / p.D + p.eps);
+    if (threadIdx.x == 0) p.rstd[row] = r;
+    if (active) {
+      const float rb = bf16_round(r);
+      float h[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = bf16_round(x[i] * rb) * w[i];
+      if (p.scale != nullptr) {
+        float sc[8], sh[8];
+        load8(p.scale + (long long)b * p.mod_bs + c0, sc);
+        load8(p.shift + (long long)b * p.mod_bs + c0, sh);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) h[i] = h[i] * (1.f + sc[i]) + sh[i];
+      }
+      store8(p.h + off, h);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// adanorm backward: row pass (dx, dy, per-CTA partial column sums)
+// partial layout: [B][chunks][4][D] = dshift, dscale, dgate, dw
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void adanorm_bwd_kernel(AdaNormBwdParams p) {
+  __shared__ float red[64];
+  const int c0 = threadIdx.x * 8;
+  const bool active = c0 < p.D;
+  const int b = blockIdx.y, j = blockIdx.x;
+  const int row0 = b * p.T + j * p.rows_per_cta;
+  const int row1 = min((b + 1) * p.T, row0 + p.rows_per_cta);
+  float w[8], sc1[8], g[8];
+  float a_shift[8], a_scale[8], a_gate[8], a_w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    w[i] = active ? p.w[c0 + i] : 0.f;
+    sc1[i] = 1.f;
+    g[i] = 1.f;
+    a_shift[i] = a_scale[i] = a_gate[i] = a_w[i] = 0.f;
+  }
+  if (active && p.scale != nullptr) {
+    load8(p.scale + (long long)b * p.mod_bs + c0, sc1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sc1[i] += 1.f;
+  }
+  if (active && p.gate != nullptr) load8(p.gate + (long long)b * p.gate_bs + c0, g);
+  int slot = 0;
+  for (int row = row0; row < row1; ++row, slot ^= 1) {
+    const long long off = (long long)row * p.D + c0;
+    const float r = p.rstd[row];
+    float n[8], dn[8];
+    float dot = 0.f;
+    if (active) {
+      float dh[8], xn[8];
+      load8(p.dh + off, dh);
+      load8(p.xn + off, xn);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        n[i] = xn[i] * r;
+        const float u = n[i] * w[i];
+        const float du = dh[i] * sc1[i];
+        a_shift[i] += dh[i];
+        a_scale[i] += dh[i] * u;
+        a_w[i] += du * n[i];
+        dn[i] = du * w[i];
+        dot += dn[i] * n[i];
+      }
+    }
+    const float mdot = block_sum(dot, red, slot) / p.D;
+    if (active) {
+      float dx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dx[i] = r * (dn[i] - n[i] * mdot);
+      if (p.dxe != nullptr) {
+        float e[8];
+        load8(p.dxe + off, e);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dx[i] += e[i];
+      }
+      store8(p.dx + off, dx);
+      if (p.y != nullptr && p.gate != nullptr) {
+        float y[8], dy[8];
+        load8(p.y + off, y);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          a_gate[i] += dx[i] * y[i];
+          dy[i] = dx[i] * g[i];
+        }
+        store8(p.dy + off, dy);
+      }
+    }
+  }
+  if (active) {
+    float* dst = p.partial + ((long long)(b * p.chunks + j) * 4) * p.D + c0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      dst[i] = a_shift[i];
+      dst[p.D + i] = a_scale[i];
+      dst[2 * p.D + i] = a_gate[i];
+      dst[3 * p.D + i] = a_w[i];
+    }
+  }
+}
+
+// Reduce the partials: dmod[b][k][c] (k = shift, scale, gate) over chunks, and dw[c] (+=) over batches and chunks.
+__global__ void adanorm_bwd_reduce_kernel(const float* __restrict__ partial, float* __restrict__ dshift,
+                                          float* __restrict__ dscale, float* __restrict__ dgate,
+                                          float* __restrict__ dw, int B, int chunks, int D) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= D) return;
+  float w_acc = 0.f;
+  for (int b = 0; b < B; ++b) {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+    for (int j = 0; j < chunks; ++j) {
+      const float* src = partial + ((long long)(b * chunks + j) * 4) * D + c;
+      s0 += src[0];
+      s1 += src[D];
+      s2 += src[2 * D];
+      w_acc += src[3 * D];
+    }
+    if (dshift) dshift[(long long)b * D + c] = s0;
+    if (dscale) dscale[(long long)b * D + c] = s1;
+    if (dgate) dgate[(long long)b * D + c] = s2;
+  }
+  dw[c] += w_acc;
+}
+
+cudaError_t adanorm_fwd_launch(const AdaNormFwdParams& p, cudaStream_t s) {
+  const int threads = ((p.D / 8 + 31) / 32) * 32;
+  const int grid = (p.M + p.rows_per_cta - 1) / p.rows_per_cta;
+  adanorm_fwd_kernel<<<grid, threads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t adanorm_bwd_launch(const AdaNormBwdParams& p, float* dshift, float* dscale, float* dgate, float* dw,
+                               cudaStream_t s) {
+  const int threads = ((p.D / 8 + 31) / 32) * 32;
+  dim3 grid(p.chunks, p.M / p.T);
+  adanorm_bwd_kernel<<<grid, threads, 0, s>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  adanorm_bwd_reduce_kernel<<<(p.D + 255) / 256, 256, 0, s>>>(p.partial, dshift, dscale, dgate, dw, p.M / p.T,
+                                                                p.chunks, p.D);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// q/k RMSNorm + RoPE.  One warp per (row, head); HD / 32 contiguous elements per lane.
+// ------------------------------------------------------------------------------------------------------------------
+template <int HD>
+__global__ void qknorm_rope_fwd_kernel(QKNormRopeParams p) {
+  constexpr int E = HD / 32;
+  const int heads = p.hq + p.hkv;
+  const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp_id();
+  if (item >= (long long)p.M * heads) return;
+  const int row = (int)(item / heads), hh = (int)(item % heads);
+  const bool is_q = hh < p.hq;
+  const int lane = lane_id();
+  const int e0 = lane * E;
+  const bf16* src = p.qkv + (long long)row * p.ld_qkv + (long long)hh * HD + e0;
+  float x[E];
+#pragma unroll
+  for (int i = 0; i < E; i += 2) {
+    float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + i));
+    x[i] = t.x;
+    x[i + 1] = t.y;
+  }
+  const float* nw = is_q ? p.q_w : p.k_w;
+  float r = 1.f;
+  if (nw != nullptr) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) ss += x[i] * x[i];
+    ss = warp_sum(ss);
+    r = rsqrtf(ss / HD + p.eps);
+    const float rb = bf16_round(r);
+#pragma unroll
+    for (int i = 0; i < E; ++i) x[i] = bf16_round(x[i] * rb) * nw[e0 + i];
+    if (lane == 0) (is_q ? p.rstd_q : p.rstd_k)[(long long)row * (is_q ? p.hq : p.hkv) + (is_q ? hh : hh - p.hq)] = r;
+  }
+  if (p.cos != nullptr) {
+    const int b = row / p.T, t = row % p.T;
+    const float* cs = p.cos + (long long)b * p.rope_bs + (long long)t * HD + e0;
+    const float* sn = p.sin + (long long)b * p.rope_bs + (long long)t * HD + e0;
+#pragma unroll
+    for (int i = 0; i < E; i += 2) {
+      const float a = x[i], c = x[i + 1];
+      x[i] = a * cs[i] - c * sn[i];
+      x[i + 1] = c * cs[i + 1] + a * sn[i + 1];
+    }
+  }
+  bf16* dst = is_q ? p.q_out + (long long)row * p.ld_q + (long long)hh * HD + e0
+                   : p.k_out + (long long)row * p.ld_k + (long long)(hh - p.hq) * HD + e0;
+#pragma unroll
+  for (int i = 0; i < E; i += 2) *reinterpret_cast<__nv_bfloat162*>(dst + i) = __floats2bfloat162_rn(x[i], x[i + 1]);
+}
+
+// Backward: dq / dk (post-RoPE) -> d(pre-norm q / k) written into dqkv; dw_q, dw_k accumulated (+=).
+template <int HD>
+__global__ void qknorm_rope_bwd_kernel(QKNormRopeParams p, const bf16* __restrict__ dq, long long ld_dq,
+                                       const bf16* __restrict__ dk, long long ld_dk, bf16* __restrict__ dqkv,
+                                       long long ld_dqkv, float* __restrict__ dwq, float* __restrict__ dwk) {
+  constexpr int E = HD / 32;
+  __shared__ float s_dw[2][HD];
+  for (int i = threadIdx.x; i < 2 * HD; i += blockDim.x) (&s_dw[0][0])[i] = 0.f;
+  __syncthreads();
+  const int heads = p.hq + p.hkv;
+  const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp_id();
+  const int lane = lane_id();
+  const int e0 = lane * E;
+  if (item < (long long)p.M * heads) {
+    const int row = (int)(item / heads), hh = (int)(item % heads);
+    const bool is_q = hh < p.hq;
+    const bf16* gsrc = is_q ? dq + (long long)row * ld_dq + (long long)hh * HD + e0
+                            : dk + (long long)row * ld_dk + (long long)(hh - p.hq) * HD + e0;
+    float g[E];
+#pragma unroll
+    for (int i = 0; i < E; i += 2) {
+      float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gsrc + i));
+      g[i] = t.x;
+      g[i + 1] = t.y;
+    }
+    if (p.cos != nullptr) {  // transpose of the rotation
+      const int b = row / p.T, t = row % p.T;
+      const float* cs = p.cos + (long long)b * p.rope_bs + (long long)t * HD + e0;
+      const float* sn = p.sin + (long long)b * p.rope_bs + (long long)t * HD + e0;
+#pragma unroll
+      for (int i = 0; i < E; i += 2) {
+        const float a = g[i], c = g[i + 1];
+        g[i] = a * cs[i] + c * sn[i + 1];
+        g[i + 1] = c * cs[i + 1] - a * sn[i];
+      }
+    }
+    const float* nw = is_q ? p.q_w : p.k_w;
+    if (nw != nullptr) {
+      const bf16* src = p.qkv + (long long)row * p.ld_qkv + (long long)hh * HD + e0;
+      float x[E];
+#pragma unroll
+      for (int i = 0; i < E; i += 2) {
+        float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + i));
+        x[i] = t.x;
+        x[i + 1] = t.y;
+      }
+      const float r = (is_q ? p.rstd_q : p.rstd_k)[(long long)row * (is_q ? p.hq : p.hkv) + (is_q ? hh : hh - p.hq)];
+      float dot = 0.f;
+      float* sdw = s_dw[is_q ? 0 : 1];
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        const float n = x[i] * r;
+        atomicAdd(&sdw[e0 + i], g[i] * n);
+        g[i] *= nw[e0 + i];  // dn
+        dot += g[i] * n;
+        x[i] = n;
+      }
+      dot = warp_sum(dot) / HD;
+#pragma unroll
+      for (int i = 0; i < E; ++i) g[i] = r * (g[i] - x[i] * dot);
+    }
+    bf16* dst = dqkv + (long long)row * ld_dqkv + (long long)hh * HD + e0;
+#pragma unroll
+    for (int i = 0; i < E; i += 2) *reinterpret_cast<__nv_bfloat162*>(dst + i) = __floats2bfloat162_rn(g[i], g[i + 1]);
+  }
+  __syncthreads();
+  if (p.q_w != nullptr && dwq != nullptr)
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) atomicAdd(&dwq[i], s_dw[0][i]);
+  if (p.k_w != nullptr && dwk != nullptr)
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) atomicAdd(&dwk[i], s_dw[1][i]);
+}
+
+cudaError_t qknorm_rope_fwd_launch(const QKNormRopeParams& p, cudaStream_t s) {
+  const long long items = (long long)p.M * (p.hq + p.hkv);
+  const int warps = 8;
+  const unsigned grid = (unsigned)((items + warps - 1) / warps);
+  if (p.hd == 128) qknorm_rope_fwd_kernel<128><<<grid, warps * 32, 0, s>>>(p);
+  else if (p.hd == 64) qknorm_rope_fwd_kernel<64><<<grid, warps * 32, 0, s>>>(p);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+cudaError_t qknorm_rope_bwd_launch(const QKNormRopeParams& p, const bf16* dq, long long ld_dq, const bf16* dk,
+                                   long long ld_dk, bf16* dqkv, long long ld_dqkv, float* dwq, float* dwk,
+                                   cudaStream_t s) {
+  const long long items = (long long)p.M * (p.hq + p.hkv);
+  const int warps = 16;
+  const unsigned grid = (unsigned)((items + warps - 1) / warps);
+  if (p.hd == 128)
+    qknorm_rope_bwd_kernel<128><<<grid, warps * 32, 0, s>>>(p, dq, ld_dq, dk, ld_dk, dqkv, ld_dqkv, dwq, dwk);
+  else if (p.hd == 64)
+    qknorm_rope_bwd_kernel<64><<<grid, warps * 32, 0, s>>>(p, dq, ld_dq, dk, ld_dk, dqkv, ld_dqkv, dwq, dwk);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// SwiGLU on [a | b] rows: g = silu(a) * b (silu rounded to bf16 first, as an autocast bf16 silu would be)
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float silu_f(float a) { return a / (1.f + __expf(-a)); }
+
+__global__ void swiglu_fwd_kernel(const bf16* __restrict__ ab, bf16* __restrict__ g, long long M, int H) {
+  const long long n8 = M * (H / 8);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / (H / 8);
+    const int c = (int)(i % (H / 8)) * 8;
+    float a[8], b[8], o[8];
+    load8(ab + row * 2 * H + c, a);
+    load8(ab + row * 2 * H + H + c, b);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = bf16_round(silu_f(a[k])) * b[k];
+    store8(g + row * H + c, o);
+  }
+}
+
+__global__ void swiglu_bwd_kernel(const bf16* __restrict__ ab, const bf16* __restrict__ dg, bf16* __restrict__ dab,
+                                  long long M, int H) {
+  const long long n8 = M * (H / 8);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / (H / 8);
+    const int c = (int)(i % (H / 8)) * 8;
+    float a[8], b[8], d[8], da[8], db[8];
+    load8(ab + row * 2 * H + c, a);
+    load8(ab + row * 2 * H + H + c, b);
+    load8(dg + row * H + c, d);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float sg = 1.f / (1.f + __expf(-a[k]));
+      const float s = a[k] * sg;
+      db[k] = d[k] * s;
+      da[k] = d[k] * b[k] * sg * (1.f + a[k] * (1.f - sg));
+    }
+    store8(dab + row * 2 * H + c, da);
+    store8(dab + row * 2 * H + H + c, db);
+  }
+}
+
+cudaError_t swiglu_fwd_launch(const bf16* ab, bf16* g, long long M, int H, cudaStream_t s) {
+  const long long n8 = M * (H / 8);
+  const int grid = (int)std::min<long long>((n8 + 255) / 256, (long long)num_sms() * 16);
+  swiglu_fwd_kernel<<<grid, 256, 0, s>>>(ab, g, M, H);
+  return cudaGetLastError();
+}
+
+cudaError_t swiglu_bwd_launch(const bf16* ab, const bf16* dg, bf16* dab, long long M, int H, cudaStream_t s) {
+  const long long n8 = M * (H / 8);
+  const int grid = (int)std::min<long long>((n8 + 255) / 256, (long long)num_sms() * 16);
+  swiglu_bwd_kernel<<<grid, 256, 0, s>>>(ab, dg, dab, M, H);
+  return cudaGetLastError();
+}
+
+}  // namespace tgo

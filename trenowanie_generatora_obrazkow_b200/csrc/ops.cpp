@@ -114,6 +114,287 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor C, bool a_mn, bool b_mn, c10::o
   TGO_CHECK_LAUNCH(gemm_launch(ta, tb, p, bn, a_mn, b_mn, epi, at::cuda::getCurrentCUDAStream()));
 }
 
+
+// ------------------------------------------------------------------------------------------------ helpers
+static const __nv_bfloat16* bf16_ptr_or_null(const c10::optional<at::Tensor>& t) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->is_cuda(), "expected a bf16 CUDA tensor");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0, "bf16 operand must be 16-byte aligned");
+  return reinterpret_cast<const __nv_bfloat16*>(t->data_ptr());
+}
+static const float* f32_ptr_or_null(const c10::optional<at::Tensor>& t) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_cuda() && t->is_contiguous(), "expected a contiguous fp32 CUDA tensor");
+  return t->data_ptr<float>();
+}
+static __nv_bfloat16* bfp(const at::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+// [B, D] per-batch row vector (possibly a strided view of a [B, 6, D] modulation tensor): batch stride
+static long long row_vec_stride(const c10::optional<at::Tensor>& t, int64_t D) {
+  if (!t.has_value() || !t->defined()) return 0;
+  TORCH_CHECK(t->dim() == 2 && t->size(1) == D && t->stride(1) == 1, "per-batch vector must be [B, D] contiguous in D");
+  TORCH_CHECK(t->stride(0) % 8 == 0, "per-batch vector batch stride must be a multiple of 8");
+  return t->stride(0);
+}
+
+// ------------------------------------------------------------------------------------------------ adanorm
+std::vector<at::Tensor> adanorm_fwd(at::Tensor x, c10::optional<at::Tensor> y, c10::optional<at::Tensor> gate,
+                                    at::Tensor w, c10::optional<at::Tensor> shift, c10::optional<at::Tensor> scale,
+                                    int64_t T, double eps) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "adanorm: x bf16 contiguous");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t D = x.size(-1), M = x.numel() / D;
+  TORCH_CHECK(D % 8 == 0 && D <= 8192 && M % T == 0, "adanorm: bad shape");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.numel() == D, "adanorm: w fp32 [D]");
+  if (y.has_value() && y->defined()) TORCH_CHECK(y->is_contiguous() && y->sizes() == x.sizes(), "adanorm: y shape");
+  TORCH_CHECK(shift.has_value() == scale.has_value(), "adanorm: shift and scale together");
+  AdaNormFwdParams p{};
+  p.x = bfp(x);
+  p.y = bf16_ptr_or_null(y);
+  p.gate = bf16_ptr_or_null(gate);
+  p.gate_bs = row_vec_stride(gate, D);
+  p.w = w.data_ptr<float>();
+  p.shift = bf16_ptr_or_null(shift);
+  p.scale = bf16_ptr_or_null(scale);
+  p.mod_bs = row_vec_stride(scale, D);
+  TORCH_CHECK(row_vec_stride(shift, D) == p.mod_bs, "adanorm: shift and scale must share a batch stride");
+  at::Tensor x_out;
+  if (p.y != nullptr) {
+    x_out = at::empty_like(x);
+    p.x_out = bfp(x_out);
+  }
+  at::Tensor h = at::empty_like(x);
+  at::Tensor rstd = at::empty({M}, x.options().dtype(at::kFloat));
+  p.h = bfp(h);
+  p.rstd = rstd.data_ptr<float>();
+  p.M = (int)M;
+  p.D = (int)D;
+  p.T = (int)T;
+  p.rows_per_cta = 16;
+  p.eps = (float)eps;
+  TGO_CHECK_LAUNCH(adanorm_fwd_launch(p, at::cuda::getCurrentCUDAStream()));
+  return {x_out, h, rstd};
+}
+
+// Returns dx, dy (only with a gate), dshift, dscale (with modulation), dgate (with a gate); dw is accumulated (+=).
+std::vector<at::Tensor> adanorm_bwd(at::Tensor dh, c10::optional<at::Tensor> dxe, at::Tensor xn, at::Tensor rstd,
+                                    at::Tensor w, at::Tensor dw, c10::optional<at::Tensor> scale,
+                                    c10::optional<at::Tensor> y, c10::optional<at::Tensor> gate, int64_t T) {
+  TORCH_CHECK(dh.is_contiguous() && xn.is_contiguous() && dh.sizes() == xn.sizes(), "adanorm_bwd: shapes");
+  const c10::cuda::CUDAGuard guard(dh.device());
+  const int64_t D = dh.size(-1), M = dh.numel() / D;
+  TORCH_CHECK(M % T == 0, "adanorm_bwd: M % T");
+  const int64_t B = M / T;
+  TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.is_contiguous() && dw.numel() == D, "adanorm_bwd: dw fp32 [D]");
+  if (dxe.has_value() && dxe->defined()) TORCH_CHECK(dxe->is_contiguous() && dxe->sizes() == dh.sizes(), "dxe");
+  AdaNormBwdParams p{};
+  p.dh = bfp(dh);
+  p.dxe = bf16_ptr_or_null(dxe);
+  p.xn = bfp(xn);
+  p.rstd = rstd.data_ptr<float>();
+  p.w = w.data_ptr<float>();
+  p.scale = bf16_ptr_or_null(scale);
+  p.mod_bs = row_vec_stride(scale, D);
+  p.y = bf16_ptr_or_null(y);
+  p.gate = bf16_ptr_or_null(gate);
+  p.gate_bs = row_vec_stride(gate, D);
+  at::Tensor dx = at::empty_like(dh), dy;
+  p.dx = bfp(dx);
+  if (p.gate != nullptr && p.y != nullptr) {
+    dy = at::empty_like(dh);
+    p.dy = bfp(dy);
+  }
+  p.M = (int)M;
+  p.D = (int)D;
+  p.T = (int)T;
+  p.rows_per_cta = 64;
+  p.chunks = (int)((T + p.rows_per_cta - 1) / p.rows_per_cta);
+  at::Tensor partial = at::empty({B, p.chunks, 4, D}, dh.options().dtype(at::kFloat));
+  p.partial = partial.data_ptr<float>();
+  auto fopt = dh.options().dtype(at::kFloat);
+  at::Tensor dshift, dscale, dgate;
+  if (p.scale != nullptr) {
+    dshift = at::empty({B, D}, fopt);
+    dscale = at::empty({B, D}, fopt);
+  }
+  if (p.dy != nullptr) dgate = at::empty({B, D}, fopt);
+  TGO_CHECK_LAUNCH(adanorm_bwd_launch(p, dshift.defined() ? dshift.data_ptr<float>() : nullptr,
+                                      dscale.defined() ? dscale.data_ptr<float>() : nullptr,
+                                      dgate.defined() ? dgate.data_ptr<float>() : nullptr, dw.data_ptr<float>(),
+                                      at::cuda::getCurrentCUDAStream()));
+  return {dx, dy, dshift, dscale, dgate};
+}
+
+// ------------------------------------------------------------------------------------------------ q/k norm + rope
+static QKNormRopeParams qk_params(const at::Tensor& qkv, int64_t hq, int64_t hkv, int64_t hd,
+                                  const c10::optional<at::Tensor>& q_w, const c10::optional<at::Tensor>& k_w,
+                                  const c10::optional<at::Tensor>& cos, const c10::optional<at::Tensor>& sin, int64_t T,
+                                  double eps) {
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.scalar_type() == at::kBFloat16, "qkv: [M, C] bf16");
+  TORCH_CHECK(qkv.size(1) >= (hq + hkv) * hd && qkv.stride(0) % 8 == 0, "qkv: width");
+  QKNormRopeParams p{};
+  p.qkv = bfp(qkv);
+  p.ld_qkv = qkv.stride(0);
+  p.q_w = f32_ptr_or_null(q_w);
+  p.k_w = f32_ptr_or_null(k_w);
+  p.cos = f32_ptr_or_null(cos);
+  p.sin = f32_ptr_or_null(sin);
+  if (p.cos != nullptr) {
+    TORCH_CHECK(cos->size(-1) == hd && cos->size(-2) >= T && sin->sizes() == cos->sizes(), "rope table shape");
+    p.rope_bs = cos->dim() == 3 && cos->size(0) > 1 ? cos->stride(0) : 0;
+    TORCH_CHECK(cos->size(-2) == T, "rope table must have exactly T rows");
+  }
+  p.M = (int)qkv.size(0);
+  p.T = (int)T;
+  p.hq = (int)hq;
+  p.hkv = (int)hkv;
+  p.hd = (int)hd;
+  p.eps = (float)eps;
+  TORCH_CHECK(hd == 64 || hd == 128, "head dim must be 64 or 128");
+  TORCH_CHECK(p.M % T == 0, "rows must be a multiple of T");
+  return p;
+}
+
+std::vector<at::Tensor> qknorm_rope_fwd(at::Tensor qkv, int64_t hq, int64_t hkv, int64_t hd,
+                                        c10::optional<at::Tensor> q_w, c10::optional<at::Tensor> k_w,
+                                        c10::optional<at::Tensor> cos, c10::optional<at::Tensor> sin, int64_t T,
+                                        double eps) {
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  QKNormRopeParams p = qk_params(qkv, hq, hkv, hd, q_w, k_w, cos, sin, T, eps);
+  at::Tensor q = at::empty({qkv.size(0), hq * hd}, qkv.options());
+  at::Tensor k = at::empty({qkv.size(0), hkv * hd}, qkv.options());
+  at::Tensor rq, rk;
+  if (p.q_w != nullptr) rq = at::empty({qkv.size(0), hq}, qkv.options().dtype(at::kFloat));
+  if (p.k_w != nullptr) rk = at::empty({qkv.size(0), hkv}, qkv.options().dtype(at::kFloat));
+  p.q_out = bfp(q);
+  p.ld_q = q.stride(0);
+  p.k_out = bfp(k);
+  p.ld_k = k.stride(0);
+  p.rstd_q = rq.defined() ? rq.data_ptr<float>() : nullptr;
+  p.rstd_k = rk.defined() ? rk.data_ptr<float>() : nullptr;
+  TGO_CHECK_LAUNCH(qknorm_rope_fwd_launch(p, at::cuda::getCurrentCUDAStream()));
+  return {q, k, rq, rk};
+}
+
+// dq [M, hq*hd], dk [M, hkv*hd] -> written into dqkv[:, :(hq+hkv)*hd]; dwq / dwk accumulated (+=) when given.
+void qknorm_rope_bwd(at::Tensor qkv, int64_t hq, int64_t hkv, int64_t hd, c10::optional<at::Tensor> q_w,
+                     c10::optional<at::Tensor> k_w, c10::optional<at::Tensor> cos, c10::optional<at::Tensor> sin,
+                     int64_t T, c10::optional<at::Tensor> rstd_q, c10::optional<at::Tensor> rstd_k, at::Tensor dq,
+                     at::Tensor dk, at::Tensor dqkv, c10::optional<at::Tensor> dwq, c10::optional<at::Tensor> dwk) {
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  QKNormRopeParams p = qk_params(qkv, hq, hkv, hd, q_w, k_w, cos, sin, T, 1e-6);
+  p.rstd_q = rstd_q.has_value() && rstd_q->defined() ? rstd_q->data_ptr<float>() : nullptr;
+  p.rstd_k = rstd_k.has_value() && rstd_k->defined() ? rstd_k->data_ptr<float>() : nullptr;
+  TORCH_CHECK(dq.stride(-1) == 1 && dk.stride(-1) == 1 && dqkv.stride(-1) == 1, "qknorm_rope_bwd: layouts");
+  TGO_CHECK_LAUNCH(qknorm_rope_bwd_launch(p, bfp(dq), dq.stride(0), bfp(dk), dk.stride(0), bfp(dqkv), dqkv.stride(0),
+                                          const_cast<float*>(f32_ptr_or_null(dwq)),
+                                          const_cast<float*>(f32_ptr_or_null(dwk)), at::cuda::getCurrentCUDAStream()));
+}
+
+// ------------------------------------------------------------------------------------------------ swiglu
+at::Tensor swiglu_fwd(at::Tensor ab) {
+  TORCH_CHECK(ab.is_contiguous() && ab.scalar_type() == at::kBFloat16 && ab.size(-1) % 16 == 0, "swiglu: ab");
+  const c10::cuda::CUDAGuard guard(ab.device());
+  const int64_t H = ab.size(-1) / 2, M = ab.numel() / ab.size(-1);
+  auto sizes = ab.sizes().vec();
+  sizes.back() = H;
+  at::Tensor g = at::empty(sizes, ab.options());
+  TGO_CHECK_LAUNCH(swiglu_fwd_launch(bfp(ab), bfp(g), M, (int)H, at::cuda::getCurrentCUDAStream()));
+  return g;
+}
+at::Tensor swiglu_bwd(at::Tensor ab, at::Tensor dg) {
+  TORCH_CHECK(ab.is_contiguous() && dg.is_contiguous(), "swiglu_bwd: contiguous");
+  const c10::cuda::CUDAGuard guard(ab.device());
+  const int64_t H = ab.size(-1) / 2, M = ab.numel() / ab.size(-1);
+  at::Tensor dab = at::empty_like(ab);
+  TGO_CHECK_LAUNCH(swiglu_bwd_launch(bfp(ab), bfp(dg), bfp(dab), M, (int)H, at::cuda::getCurrentCUDAStream()));
+  return dab;
+}
+
+// ------------------------------------------------------------------------------------------------ attention
+static void attn_check4(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 4 && t.stride(3) == 1, name,
+              ": [B, T, H, hd] bf16 with contiguous head dim");
+  TORCH_CHECK(t.stride(0) % 8 == 0 && t.stride(1) % 8 == 0 && t.stride(2) % 8 == 0, name, ": strides % 8");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, ": 16-byte alignment");
+}
+static AttnParams attn_params(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                              const c10::optional<at::Tensor>& kv_len, double scale) {
+  attn_check4(q, "q");
+  attn_check4(k, "k");
+  attn_check4(v, "v");
+  AttnParams p{};
+  p.B = (int)q.size(0);
+  p.Tq = (int)q.size(1);
+  p.Hq = (int)q.size(2);
+  p.hd = (int)q.size(3);
+  p.Tk = (int)k.size(1);
+  p.Hkv = (int)k.size(2);
+  TORCH_CHECK(k.size(0) == p.B && v.sizes() == k.sizes() && k.size(3) == p.hd, "attention: k/v shapes");
+  TORCH_CHECK(p.Hq % p.Hkv == 0, "attention: Hq % Hkv");
+  TORCH_CHECK(p.hd == 64 || p.hd == 128, "attention: head dim 64 or 128");
+  p.rep = p.Hq / p.Hkv;
+  p.q = bfp(q);
+  p.q_bs = q.stride(0);
+  p.q_ts = q.stride(1);
+  p.q_hs = q.stride(2);
+  p.k = bfp(k);
+  p.k_bs = k.stride(0);
+  p.k_ts = k.stride(1);
+  p.k_hs = k.stride(2);
+  p.v = bfp(v);
+  p.v_bs = v.stride(0);
+  p.v_ts = v.stride(1);
+  p.v_hs = v.stride(2);
+  p.kv_len = nullptr;
+  if (kv_len.has_value() && kv_len->defined()) {
+    TORCH_CHECK(kv_len->scalar_type() == at::kInt && kv_len->numel() == p.B && kv_len->is_cuda(), "kv_len: int32 [B]");
+    p.kv_len = kv_len->data_ptr<int>();
+  }
+  p.scale = (float)scale;
+  return p;
+}
+
+// o: optional preallocated [B, Tq, Hq, hd] output (may be a strided view)
+std::vector<at::Tensor> attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, c10::optional<at::Tensor> kv_len,
+                                      double scale, c10::optional<at::Tensor> out) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  AttnParams p = attn_params(q, k, v, kv_len, scale);
+  at::Tensor o = out.has_value() && out->defined() ? *out : at::empty({p.B, p.Tq, p.Hq, p.hd}, q.options());
+  attn_check4(o, "o");
+  at::Tensor lse = at::empty({p.B, p.Hq, p.Tq}, q.options().dtype(at::kFloat));
+  p.o = bfp(o);
+  p.o_bs = o.stride(0);
+  p.o_ts = o.stride(1);
+  p.o_hs = o.stride(2);
+  p.lse = lse.data_ptr<float>();
+  TGO_CHECK_LAUNCH(attention_fwd_launch(p, at::cuda::getCurrentCUDAStream()));
+  return {o, lse};
+}
+
+// Writes dq, dk, dv (preallocated, possibly strided views). dO must have o's layout.
+void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, at::Tensor dO,
+                   c10::optional<at::Tensor> kv_len, double scale, at::Tensor dq, at::Tensor dk, at::Tensor dv) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  AttnParams p = attn_params(q, k, v, kv_len, scale);
+  attn_check4(o, "o");
+  attn_check4(dO, "dO");
+  attn_check4(dq, "dq");
+  attn_check4(dk, "dk");
+  attn_check4(dv, "dv");
+  TORCH_CHECK(dO.strides() == o.strides(), "attention_bwd: dO must have o's strides");
+  p.o = bfp(o);
+  p.o_bs = o.stride(0);
+  p.o_ts = o.stride(1);
+  p.o_hs = o.stride(2);
+  p.lse = lse.data_ptr<float>();
+  at::Tensor delta = at::empty({p.B, p.Hq, p.Tq}, q.options().dtype(at::kFloat));
+  at::Tensor dq_acc = at::empty({p.B, p.Tq, p.Hq, p.hd}, q.options().dtype(at::kFloat));
+  TGO_CHECK_LAUNCH(attention_bwd_launch(p, bfp(dO), delta.data_ptr<float>(), dq_acc.data_ptr<float>(), bfp(dq),
+                                        dq.stride(0), dq.stride(1), dq.stride(2), bfp(dk), dk.stride(0), dk.stride(1),
+                                        dk.stride(2), bfp(dv), dv.stride(0), dv.stride(1), dv.stride(2),
+                                        at::cuda::getCurrentCUDAStream()));
+}
+
 }  // namespace tgo
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -121,4 +402,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &tgo::gemm, "tcgen05 bf16 GEMM: C = alpha * op(A) op(B)^T (+ beta D)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("a_mn"), py::arg("b_mn"), py::arg("D") = c10::nullopt, py::arg("alpha") = 1.0,
         py::arg("beta") = 0.0, py::arg("accumulate") = false, py::arg("err"));
+  m.def("adanorm_fwd", &tgo::adanorm_fwd, "x_new = x + gate*y; h = rmsnorm(x_new)*w*(1+scale)+shift");
+  m.def("adanorm_bwd", &tgo::adanorm_bwd, "backward of adanorm_fwd");
+  m.def("qknorm_rope_fwd", &tgo::qknorm_rope_fwd, "per-head RMSNorm + RoPE of q and k from the qkv rows");
+  m.def("qknorm_rope_bwd", &tgo::qknorm_rope_bwd, "backward of qknorm_rope_fwd into dqkv");
+  m.def("swiglu_fwd", &tgo::swiglu_fwd, "silu(a) * b");
+  m.def("swiglu_bwd", &tgo::swiglu_bwd, "backward of swiglu_fwd");
+  m.def("attention_fwd", &tgo::attention_fwd, "flash attention forward (GQA, key-length mask)");
+  m.def("attention_bwd", &tgo::attention_bwd, "flash attention backward");
 }

@@ -1,0 +1,318 @@
+"""Differentiable fused ops used by the models.
+
+CUDA tensors run the sm_100a kernels (csrc/); CPU tensors run the fp32 oracles of ``reference.py`` under ordinary
+autograd. Each CUDA op is a ``torch.autograd.Function`` whose backward is a hand-written kernel too:
+
+* ``linear``        tcgen05 GEMM forward / dgrad; the weight gradient is accumulated in fp32 straight into
+                    ``weight.grad`` by the GEMM epilogue (the grad never exists in bf16). Weights are read from a
+                    bf16 shadow copy refreshed whenever the fp32 master changes (``bf16_weight``).
+* ``adanorm``       residual update + RMSNorm + adaLN modulation (DenoiserBlock, reference aurora/model.py:204-210).
+* ``self_attention_core``  per-head q/k RMSNorm + RoPE + flash attention, reading q/k/v from the fused qkv rows.
+* ``cross_attention_core`` flash attention against text keys/values with a key-length mask.
+* ``swiglu``        silu(a) * b.
+"""
+import torch
+
+from . import reference as R
+from ._ext import ext
+from .gemm import gemm
+
+# ----------------------------------------------------------------------------------------------------------------
+# bf16 shadow weights and gradient-ready callbacks
+# ----------------------------------------------------------------------------------------------------------------
+_GRAD_HOOKS = []
+
+
+def bf16_weight(p):
+    """bf16 copy of a floating parameter, kept on the parameter object and recomputed when the parameter changed in
+    place (its version counter moved) or moved to another device."""
+    if p.dtype == torch.bfloat16:
+        return p.detach()
+    ent = getattr(p, "_tgo_bf16", None)
+    ver = p._version
+    if ent is None or ent[0] != ver or ent[1].device != p.device or ent[1].shape != p.shape:
+        w = p.detach().to(torch.bfloat16)
+        p._tgo_bf16 = (ver, w)
+        return w
+    return ent[1]
+
+
+def set_bf16_weight(p, w):
+    """Register an externally produced bf16 copy of p (e.g. written by a fused optimizer kernel)."""
+    p._tgo_bf16 = (p._version, w)
+
+
+def add_grad_ready_hook(fn):
+    """fn(param) is called right after a weight gradient was accumulated into ``param.grad`` by a fused op."""
+    _GRAD_HOOKS.append(fn)
+    return fn
+
+
+def remove_grad_ready_hook(fn):
+    if fn in _GRAD_HOOKS:
+        _GRAD_HOOKS.remove(fn)
+
+
+def _grad_buffer(p):
+    if p.grad is None:
+        p.grad = torch.zeros_like(p, dtype=torch.float32)
+    return p.grad
+
+
+def _notify(p):
+    for fn in _GRAD_HOOKS:
+        fn(p)
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# linear
+# ----------------------------------------------------------------------------------------------------------------
+class _LinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, w16):
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.dtype != torch.bfloat16:
+            x2 = x2.to(torch.bfloat16)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        y = gemm(x2, w16)
+        ctx.save_for_backward(x2, w16)
+        ctx.weight = weight
+        ctx.in_shape = x.shape
+        ctx.in_dtype = x.dtype
+        return y.view(*x.shape[:-1], w16.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w16 = ctx.saved_tensors
+        dy2 = dy.reshape(-1, dy.shape[-1])
+        if dy2.dtype != torch.bfloat16:
+            dy2 = dy2.to(torch.bfloat16)
+        if not dy2.is_contiguous():
+            dy2 = dy2.contiguous()
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm(dy2, w16, b_mn=True).view(ctx.in_shape)
+            if ctx.in_dtype != torch.bfloat16:
+                dx = dx.to(ctx.in_dtype)
+        weight = ctx.weight
+        if weight.requires_grad:
+            g = _grad_buffer(weight)
+            gemm(dy2, x2, out=g, a_mn=True, b_mn=True, accumulate=True)
+            _notify(weight)
+        return dx, None, None
+
+
+def linear(x, layer_or_weight, bias=None):
+    """y = x @ W^T (+ b). Accepts an ``nn.Linear`` (its weight and bias) or a weight tensor."""
+    if isinstance(layer_or_weight, torch.nn.Linear):
+        weight, bias = layer_or_weight.weight, layer_or_weight.bias
+    else:
+        weight = layer_or_weight
+    if not x.is_cuda:
+        return torch.nn.functional.linear(x, weight.to(x.dtype), None if bias is None else bias.to(x.dtype))
+    y = _LinearFn.apply(x, weight, bf16_weight(weight))
+    if bias is not None:
+        y = y + bias.to(y.dtype)
+    return y
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# adanorm
+# ----------------------------------------------------------------------------------------------------------------
+def _opt(t):
+    return t if t is not None else None
+
+
+class _AdaNormFn(torch.autograd.Function):
+    """(x, y, gate, w, shift, scale) -> (x_new, h); x_new = x + gate * y (or x + y); only used with y given."""
+
+    @staticmethod
+    def forward(ctx, x, y, gate, w, shift, scale, eps):
+        B, T, D = x.shape
+        x_new, h, rstd = ext().adanorm_fwd(x, y, gate, w, shift, scale, T, eps)
+        ctx.save_for_backward(x_new, rstd, w, scale, y, gate)
+        ctx.T = T
+        ctx.has_mod = shift is not None
+        return x_new, h
+
+    @staticmethod
+    def backward(ctx, dx_new, dh):
+        x_new, rstd, w, scale, y, gate = ctx.saved_tensors
+        if dh is None:
+            dh = torch.zeros_like(x_new)
+        dw = torch.zeros_like(w)
+        dxe = dx_new.contiguous() if dx_new is not None else None
+        dx, dy, dshift, dscale, dgate = ext().adanorm_bwd(dh.contiguous(), dxe, x_new, rstd, w, dw, scale, y, gate,
+                                                          ctx.T)
+        if dy is None:
+            dy = dx  # ungated residual: d(branch) == d(x_new)
+        return dx, dy, dgate, dw, dshift, dscale, None
+
+
+class _NormModFn(torch.autograd.Function):
+    """x -> h = rmsnorm(x) * w * (1 + scale) + shift (no residual update)."""
+
+    @staticmethod
+    def forward(ctx, x, w, shift, scale, eps):
+        B, T, D = x.shape
+        _, h, rstd = ext().adanorm_fwd(x, None, None, w, shift, scale, T, eps)
+        ctx.save_for_backward(x, rstd, w, scale)
+        ctx.T = T
+        return h
+
+    @staticmethod
+    def backward(ctx, dh):
+        x, rstd, w, scale = ctx.saved_tensors
+        dw = torch.zeros_like(w)
+        dx, _, dshift, dscale, _ = ext().adanorm_bwd(dh.contiguous(), None, x, rstd, w, dw, scale, None, None, ctx.T)
+        return dx, dw, dshift, dscale, None
+
+
+def adanorm(x, y, gate, w, shift=None, scale=None, eps=R.EPS):
+    """x_new = x + gate * y (y None: x_new = x; gate None: x + y); h = rmsnorm(x_new) * w * (1 + scale) + shift.
+
+    x, y: [B, T, D]; gate, shift, scale: [B, D] (per-sample rows, may be strided views); w: [D] fp32.
+    Returns (x_new, h).
+    """
+    if not x.is_cuda:
+        xn = x if y is None else (x + (y if gate is None else gate[:, None] * y))
+        h = R.rmsnorm(xn, w, eps)
+        if scale is not None:
+            h = h * (1 + scale[:, None]) + shift[:, None]
+        return xn, h
+    x = x.contiguous()
+    if y is None:
+        return x, _NormModFn.apply(x, w, shift, scale, eps)
+    return _AdaNormFn.apply(x, y.contiguous(), gate, w, shift, scale, eps)
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# attention
+# ----------------------------------------------------------------------------------------------------------------
+def _rope_arg(cos):
+    if cos is None:
+        return None
+    return cos.contiguous().float()
+
+
+class _SelfAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, q_w, k_w, cos, sin, kv_len, hq, hkv, hd, scale, eps):
+        B, T, C = qkv.shape
+        q2 = qkv.view(B * T, C)
+        q, k, rq, rk = ext().qknorm_rope_fwd(q2, hq, hkv, hd, q_w, k_w, cos, sin, T, eps)
+        q4 = q.view(B, T, hq, hd)
+        k4 = k.view(B, T, hkv, hd)
+        v4 = qkv[:, :, (hq + hkv) * hd:(hq + 2 * hkv) * hd].unflatten(-1, (hkv, hd))
+        o, lse = ext().attention_fwd(q4, k4, v4, kv_len, scale, None)
+        ctx.save_for_backward(qkv, q, k, o, lse, rq, rk, q_w, k_w, cos, sin, kv_len)
+        ctx.dims = (hq, hkv, hd, scale)
+        return o.view(B, T, hq * hd)
+
+    @staticmethod
+    def backward(ctx, do):
+        qkv, q, k, o, lse, rq, rk, q_w, k_w, cos, sin, kv_len = ctx.saved_tensors
+        hq, hkv, hd, scale = ctx.dims
+        B, T, C = qkv.shape
+        do = do.contiguous().view(B, T, hq, hd)
+        dqkv = torch.empty_like(qkv)
+        dq = torch.empty_like(q)
+        dk = torch.empty_like(k)
+        dv4 = dqkv[:, :, (hq + hkv) * hd:(hq + 2 * hkv) * hd].unflatten(-1, (hkv, hd))
+        q4, k4 = q.view(B, T, hq, hd), k.view(B, T, hkv, hd)
+        v4 = qkv[:, :, (hq + hkv) * hd:(hq + 2 * hkv) * hd].unflatten(-1, (hkv, hd))
+        ext().attention_bwd(q4, k4, v4, o, lse, do, kv_len, scale, dq.view(B, T, hq, hd), dk.view(B, T, hkv, hd), dv4)
+        dwq = torch.zeros_like(q_w) if q_w is not None else None
+        dwk = torch.zeros_like(k_w) if k_w is not None else None
+        ext().qknorm_rope_bwd(qkv.view(B * T, C), hq, hkv, hd, q_w, k_w, cos, sin, T, rq, rk, dq, dk,
+                              dqkv.view(B * T, C), dwq, dwk)
+        return dqkv, dwq, dwk, None, None, None, None, None, None, None, None
+
+
+def self_attention_core(qkv, heads, kv_heads, head_dim, q_w=None, k_w=None, cos=None, sin=None, kv_len=None,
+                        scale=None, eps=R.EPS):
+    """qkv [B, T, (heads + 2 kv_heads) * head_dim] -> attention output [B, T, heads * head_dim].
+
+    q / k get a per-head RMSNorm when q_w / k_w are given, then RoPE when cos / sin are given ([T, d] or
+    [B, T, d]); keys at positions >= kv_len[b] are masked.
+    """
+    scale = head_dim ** -0.5 if scale is None else scale
+    B, T, _ = qkv.shape
+    if not qkv.is_cuda:
+        q, k, v = qkv.split([heads * head_dim, kv_heads * head_dim, kv_heads * head_dim], dim=-1)
+        q = q.view(B, T, heads, head_dim)
+        k = k.view(B, T, kv_heads, head_dim)
+        v = v.view(B, T, kv_heads, head_dim)
+        if q_w is not None:
+            q, k = R.rmsnorm(q, q_w, eps), R.rmsnorm(k, k_w, eps)
+        if cos is not None:
+            q, k = R.apply_rope(q, cos, sin), R.apply_rope(k, cos, sin)
+        return R.attention(q, k, v, kv_len, scale).reshape(B, T, heads * head_dim)
+    return _SelfAttnFn.apply(qkv.contiguous(), q_w, k_w, _rope_arg(cos), _rope_arg(sin), kv_len, heads, kv_heads,
+                             head_dim, float(scale), eps)
+
+
+class _CrossAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, kv, kv_len, heads, head_dim, scale):
+        B, T, D = q.shape
+        L = kv.shape[1]
+        q4 = q.view(B, T, heads, head_dim)
+        k4 = kv[:, :, :D].unflatten(-1, (heads, head_dim))
+        v4 = kv[:, :, D:].unflatten(-1, (heads, head_dim))
+        o, lse = ext().attention_fwd(q4, k4, v4, kv_len, scale, None)
+        ctx.save_for_backward(q, kv, o, lse, kv_len)
+        ctx.dims = (heads, head_dim, scale)
+        return o.view(B, T, D)
+
+    @staticmethod
+    def backward(ctx, do):
+        q, kv, o, lse, kv_len = ctx.saved_tensors
+        heads, head_dim, scale = ctx.dims
+        B, T, D = q.shape
+        do = do.contiguous().view(B, T, heads, head_dim)
+        dq = torch.empty_like(q)
+        dkv = torch.empty_like(kv)
+        q4 = q.view(B, T, heads, head_dim)
+        k4 = kv[:, :, :D].unflatten(-1, (heads, head_dim))
+        v4 = kv[:, :, D:].unflatten(-1, (heads, head_dim))
+        ext().attention_bwd(q4, k4, v4, o, lse, do, kv_len, scale, dq.view(B, T, heads, head_dim),
+                            dkv[:, :, :D].unflatten(-1, (heads, head_dim)),
+                            dkv[:, :, D:].unflatten(-1, (heads, head_dim)))
+        return dq, dkv, None, None, None, None
+
+
+def cross_attention_core(q, kv, heads, kv_len=None, scale=None):
+    """q [B, T, D] (heads of D / heads), kv [B, L, 2D] = [k | v] -> [B, T, D]; keys >= kv_len[b] masked."""
+    B, T, D = q.shape
+    hd = D // heads
+    scale = hd ** -0.5 if scale is None else scale
+    if not q.is_cuda:
+        k, v = kv.chunk(2, dim=-1)
+        L = kv.shape[1]
+        return R.attention(q.view(B, T, heads, hd), k.reshape(B, L, heads, hd), v.reshape(B, L, heads, hd), kv_len,
+                           scale).reshape(B, T, D)
+    return _CrossAttnFn.apply(q.contiguous(), kv.contiguous(), kv_len, heads, hd, float(scale))
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# swiglu
+# ----------------------------------------------------------------------------------------------------------------
+class _SwiGLUFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ab):
+        ab = ab.contiguous()
+        ctx.save_for_backward(ab)
+        return ext().swiglu_fwd(ab)
+
+    @staticmethod
+    def backward(ctx, dg):
+        (ab,) = ctx.saved_tensors
+        return ext().swiglu_bwd(ab, dg.contiguous())
+
+
+def swiglu(ab):
+    if not ab.is_cuda:
+        return R.swiglu(ab)
+    return _SwiGLUFn.apply(ab)

@@ -1,0 +1,71 @@
+"""Quintic Newton-Schulz orthogonalisation for Muon, batched over same-shape matrices.
+
+Iteration (Keller Jordan's Muon; reference aurora/muon.py:25-39 and aurora/ns_triton.py:63-81):
+    X <- G / (||G||_F + 1e-7) (bf16, transposed so that rows <= cols)
+    5 x:  A = X X^T ;  B = b A + c A A ;  X = a X + B X         (a, b, c) = (3.4445, -4.7750, 2.0315)
+
+On CUDA every product is one launch of the tcgen05 GEMM (csrc/gemm.cu) with the affine terms fused into its
+epilogue (``alpha * acc + beta * D``): A A is formed as A A^T (A is symmetric), and B X reads X MN-major, so no
+transposes are materialised inside the loop.
+"""
+import torch
+
+from ..ops.gemm import gemm
+
+NS_COEFFS = (3.4445, -4.7750, 2.0315)
+
+
+def zeropower_reference(G, steps=5):
+    """fp32-or-bf16 PyTorch version (CPU path and test oracle); works batched."""
+    a, b, c = NS_COEFFS
+    X = G.bfloat16()
+    transposed = G.size(-2) > G.size(-1)
+    if transposed:
+        X = X.mT
+    X = X / (X.norm(dim=(-2, -1), keepdim=True) + 1e-7)
+    for _ in range(steps):
+        A = X @ X.mT
+        B = b * A + c * A @ A
+        X = a * X + B @ X
+    if transposed:
+        X = X.mT
+    return X
+
+
+def zeropower(G, steps=5):
+    """Orthogonalise the last two dims of G (B, m, n) or (m, n); returns bf16."""
+    if not G.is_cuda:
+        return zeropower_reference(G, steps)
+    a, b, c = NS_COEFFS
+    squeeze = G.dim() == 2
+    X = G.unsqueeze(0) if squeeze else G
+    transposed = X.size(-2) > X.size(-1)
+    if transposed:
+        X = X.mT
+    norm = X.float().norm(dim=(-2, -1), keepdim=True)
+    X = (X.float() / (norm + 1e-7)).to(torch.bfloat16).contiguous()
+    n, m, k = X.shape
+    A = torch.empty(n, m, m, device=X.device, dtype=torch.bfloat16)
+    Bm = torch.empty_like(A)
+    Y = torch.empty_like(X)
+    for _ in range(steps):
+        gemm(X, X, out=A)                              # A = X X^T
+        gemm(A, A, out=Bm, d=A, alpha=c, beta=b)       # B = c A A^T + b A
+        gemm(Bm, X, out=Y, b_mn=True, d=X, alpha=1.0, beta=a)  # X = B X + a X
+        X, Y = Y, X
+    if transposed:
+        X = X.mT
+    return X.squeeze(0) if squeeze else X
+
+
+def rownorm(G, eps=1e-7):
+    """Row-wise step of periodic row-wise Muon (arXiv:2608.20818, reference aurora/muon.py:42-52): in the wide
+    orientation every row is scaled to unit norm. Works batched; returns bf16."""
+    X = G.float()
+    transposed = X.size(-2) > X.size(-1)
+    if transposed:
+        X = X.mT
+    X = X / X.norm(dim=-1, keepdim=True).clamp_min(eps)
+    if transposed:
+        X = X.mT
+    return X.bfloat16()
