@@ -1,0 +1,345 @@
+"""Headline benchmark: 1.24B-DiT flow-matching training throughput in latent tokens per second.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
+      bench.py --gpus N --steps K --warmup W
+
+Config: DiT hidden 2048, 24 blocks, 16 heads of 128, SwiGLU 5504 ("MLP 4x" param-matched),
+2-block text refiner (1024 wide) on synthetic frozen-LM states [B, 128, 1024] ~ N(0, 1); 512 px synthetic FLUX.2
+latents (128 channels at 32 x 32 = 1024 tokens / image) ~ N(0, 1); global batch 256 (micro-batch 32, gradient
+accumulation 256 / (32 N)); bf16 compute; Muon (5 Newton-Schulz steps, sharded over ranks) + AdamW; EMA; random
+init. One step = the whole optimizer step over the global batch. Global batch fixed across N: strong scaling.
+Timing: W untimed warm-up steps, then K steps bracketed by barrier + synchronize, CUDA events on the launching
+stream, max over ranks. Every step touches far more than L2 (126 MB) of activations and weights.
+``e2e`` repeats the K steps through ``Trainer.step`` with the step's inputs in pinned host memory (copied to the
+device inside the step) and the loss read back to the host every step.
+``--impl reference`` runs the unmodified reference (installed in baseline/_ref) through its own modules on the
+same config: aurora.model.Denoiser, aurora.slayer.LMTextEncoder (refiner on the same synthetic states),
+train.param_groups (sharded Muon + fused AdamW), DDP with the bf16 compress hook, torch.compile, bf16 autocast.
+"""
+import argparse
+import contextlib
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.path.join(HERE, "baseline", "_ref")
+BASELINE_VALUE = None  # BASELINE.md publishes no number for this metric
+METRIC = "1.24B DiT train latent-tokens/s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", default="1.24b")
+    p.add_argument("--global-batch", type=int, default=256)
+    p.add_argument("--micro-batch", type=int, default=32)
+    p.add_argument("--res", type=int, default=512)
+    p.add_argument("--text-len", type=int, default=128)
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ------------------------------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        sm.sort()
+        med = sm[len(sm) // 2] if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# common harness
+# ------------------------------------------------------------------------------------------------------------------
+def setup_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def timed(step_fn, steps, world, local):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = ClockSampler(local)
+    clk.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step_fn()
+    e.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = clk.stop()
+    ms = torch.tensor([s.elapsed_time(e) / steps], device="cuda")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    return ms.item(), clocks
+
+
+def synthetic_batch(per_rank, res, text_len, lm_dim, device, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    side = res // 16
+    x0 = torch.randn(per_rank, 128, side, side, generator=g)
+    states = torch.randn(per_rank, text_len, lm_dim, generator=g).to(torch.bfloat16)
+    host = {"x0": x0.pin_memory(), "lm_states": states.pin_memory()}
+    dev = {k: v.to(device) for k, v in host.items()}
+    return host, dev
+
+
+def emit(rank, out):
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# our implementation
+# ------------------------------------------------------------------------------------------------------------------
+def run_ours(args):
+    sys.path.insert(0, HERE)
+    from trenowanie_generatora_obrazkow_b200.models.config import benchmark_configs
+    from trenowanie_generatora_obrazkow_b200.ops._ext import check_errors, ext
+    from trenowanie_generatora_obrazkow_b200.train.trainer import TrainConfig, Trainer
+    rank, world, local = setup_dist(args)
+    device = torch.device("cuda", local)
+    den_cfg, te_cfg = benchmark_configs(args.config)
+    from dataclasses import replace
+    den_cfg = replace(den_cfg, latent_size=args.res // 16)
+    cfg = TrainConfig(global_batch=args.global_batch, micro_batch=args.micro_batch, steps=10 ** 6)
+    tr = Trainer(den_cfg, te_cfg, cfg, device)
+    per_rank = args.global_batch // world
+    host, devb = synthetic_batch(per_rank, args.res, args.text_len, te_cfg.lm_dim, device, 1234 + rank)
+    for _ in range(args.warmup):
+        tr.step(devb)
+    torch.cuda.synchronize()
+    check_errors(device)
+    n0 = ext().launch_count()
+    ms, clocks = timed(lambda: tr.step(devb), args.steps, world, local)
+    launches = (ext().launch_count() - n0) // args.steps * args.steps
+    check_errors(device)
+    tokens = args.global_batch * (args.res // 16) ** 2
+    value = tokens / (ms / 1e3)
+    out = {"metric": METRIC, "value": round(value, 1), "unit": "latent-tokens/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
+           "dtype": "bf16", "data": "synthetic (N(0,1) FLUX.2-shaped latents and frozen-LM states), random init",
+           "config": {"model": f"DiT {args.config}: hidden {den_cfg.dim}, {den_cfg.depth} blocks, {den_cfg.heads} "
+                               f"heads, SwiGLU {den_cfg.mlp_hidden}, refiner {te_cfg.dim}x{te_cfg.depth}",
+                      "params_denoiser": tr.n_params()[0], "params_text": tr.n_params()[1],
+                      "global_batch": args.global_batch, "micro_batch": tr.micro, "seq_len": (args.res // 16) ** 2,
+                      "text_len": args.text_len, "res": args.res, "parallelism": f"dp{world}",
+                      "optimizer": "muon(sharded)+adamw", "l2": "inputs larger than L2 (no flush needed)"},
+           "clocks": clocks, "gpu_launches": int(launches), "impl": "ours"}
+    if not args.no_e2e:
+        loss_host = []
+
+        def e2e_step():
+            loss = tr.step(host)
+            loss_host.append(loss.item())
+
+        ms_e2e, _ = timed(e2e_step, args.steps, world, local)
+        x_bytes = host["x0"].numel() * host["x0"].element_size()
+        s_bytes = host["lm_states"].numel() * host["lm_states"].element_size()
+        out["e2e"] = {"value": round(tokens / (ms_e2e / 1e3), 1), "unit": "latent-tokens/s",
+                      "ms_per_step": round(ms_e2e, 2), "h2d_bytes_per_step": (x_bytes + s_bytes) * world,
+                      "d2h_bytes_per_step": 4 * world,
+                      "api": "Trainer.step(batch in pinned host memory) + loss.item()"}
+    emit(rank, out)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# the reference, unmodified, through its own modules
+# ------------------------------------------------------------------------------------------------------------------
+def run_reference(args):
+    if not os.path.isdir(os.path.join(REF, "aurora")):
+        print(json.dumps({"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}))
+        return
+    sys.path.insert(0, REF)
+    import torch.nn as nn
+    import torch.nn.functional as F
+    from torch.nn.parallel import DistributedDataParallel as DDP
+
+    import train as ref_train
+    from aurora.model import Denoiser, DenoiserConfig, LMEncoderConfig
+    from aurora.slayer import LM_NULL, LMTextEncoder
+
+    rank, world, local = setup_dist(args)
+    device = torch.device("cuda", local)
+    torch.backends.cuda.matmul.allow_tf32 = True
+    torch.backends.cudnn.allow_tf32 = True
+    side = args.res // 16
+    den_cfg = DenoiserConfig(dim=2048, depth=24, heads=16, mlp_hidden=5504, text_dim=1024, latent_size=side)
+    te_cfg = LMEncoderConfig(repo="", tok_suffix="", lm_dim=1024, skip_last=0, dim=1024, depth=2, heads=16,
+                             kv_heads=4, head_dim=64, mlp_hidden=2816, max_tokens=args.text_len, backend="states")
+    torch.manual_seed(0)
+    te = LMTextEncoder(te_cfg, with_lm=False)
+    den = Denoiser(den_cfg)
+    te.init_weights()
+    den.init_weights()
+    te.to(device), den.to(device)
+    ref_args = ref_train.resolve_defaults(ref_train.get_args(
+        ["--out", "/tmp/ref_bench", "--batch", str(args.global_batch), "--micro-batch", str(args.micro_batch),
+         "--steps", "1000000", "--te-size", "slayer149", "--te-dim", "1024", "--repa-weight", "0",
+         "--mlm-weight", "0", "--no-wandb"]))
+    opts, _ = ref_train.param_groups(te, den, ref_args)
+    te.compile()
+    den.compile()
+
+    class Step(nn.Module):  # train.FlowModel's flow-matching math, with the LM states passed to the refiner
+        def __init__(self):
+            super().__init__()
+            self.te, self.den = te, den
+
+        def forward(self, x0, ids, states, t, eps):
+            text, valid = self.te(ids, lm_states=states)
+            tt = t.view(-1, 1, 1, 1)
+            v = self.den((1 - tt) * x0 + tt * eps, t, text, valid)
+            return F.mse_loss(v.float(), eps - x0)
+
+    model = Step()
+    if world > 1:
+        model = DDP(model, device_ids=[local], bucket_cap_mb=64, gradient_as_bucket_view=True)
+        from torch.distributed.algorithms.ddp_comm_hooks import default_hooks
+        model.register_comm_hook(None, default_hooks.bf16_compress_hook)
+    params = [p for p in model.parameters() if p.requires_grad]
+    ema_params = list(te.parameters()) + list(den.parameters())
+    ema = [p.detach().clone().float() for p in ema_params] if rank == 0 else None
+    per_rank = args.global_batch // world
+    mb = min(args.micro_batch, per_rank)
+    accum = per_rank // mb
+    host, devb = synthetic_batch(per_rank, args.res, args.text_len, 1024, device, 1234 + rank)
+    ids = torch.randint(0, 60000, (per_rank, args.text_len), device=device)
+    null_row = torch.from_numpy(te.null_ids()).to(device)
+    state = {"step": 0}
+
+    def step(batch):
+        x0_all = batch["x0"].to(device, non_blocking=True)
+        st_all = batch["lm_states"].to(device, non_blocking=True)
+        for m in range(accum):
+            sl = slice(m * mb, (m + 1) * mb)
+            x0 = x0_all[sl].float()
+            b = x0.shape[0]
+            t = torch.sigmoid(torch.randn(b, device=device))
+            eps = torch.randn_like(x0)
+            drop = torch.rand(b, device=device) < ref_args.cfg_drop
+            cond_ids = torch.where(drop[:, None], null_row[: ids.shape[1]], ids[sl])
+            sync = model.no_sync() if (world > 1 and m < accum - 1) else contextlib.nullcontext()
+            with sync:
+                with torch.autocast("cuda", dtype=torch.bfloat16):
+                    loss = model(x0, cond_ids, st_all[sl], t, eps)
+                (loss / accum).backward()
+        torch.nn.utils.clip_grad_norm_(params, ref_args.clip)
+        mult = ref_train.lr_mult(state["step"], ref_args.steps, 0, ref_args.schedule)
+        for o in opts:
+            for g in o.param_groups:
+                g["lr"] = g["base_lr"] * mult
+            o.step()
+            o.zero_grad(set_to_none=True)
+        state["step"] += 1
+        if ema is not None:
+            d = min(ref_args.ema, state["step"] / (9 + state["step"]))
+            torch._foreach_lerp_(ema, [p.detach() for p in ema_params], 1 - d)
+        return loss
+
+    for _ in range(args.warmup):
+        step(devb)
+    torch.cuda.synchronize()
+    ms, clocks = timed(lambda: step(devb), args.steps, world, local)
+    tokens = args.global_batch * side * side
+    value = tokens / (ms / 1e3)
+    out = {"metric": METRIC, "value": round(value, 1), "unit": "latent-tokens/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (N(0,1) FLUX.2-shaped latents and frozen-LM states), random init",
+           "config": {"model": "reference aurora.model.Denoiser 2048x24, 16 heads, SwiGLU 5504, refiner 1024x2",
+                      "global_batch": args.global_batch, "micro_batch": mb, "seq_len": side * side,
+                      "parallelism": f"dp{world}", "compile": True},
+           "clocks": clocks, "impl": "reference"}
+    if not args.no_e2e:
+        def e2e_step():
+            step(host).item()
+
+        ms_e2e, _ = timed(e2e_step, args.steps, world, local)
+        out["e2e"] = {"value": round(tokens / (ms_e2e / 1e3), 1), "unit": "latent-tokens/s",
+                      "ms_per_step": round(ms_e2e, 2)}
+    emit(rank, out)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

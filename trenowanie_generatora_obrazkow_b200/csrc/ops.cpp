@@ -7,13 +7,21 @@
 
 #include "kernels.h"
 
+#include <atomic>
+
 namespace tgo {
 
-#define TGO_CHECK_LAUNCH(expr)                                                             \
+// Number of kernels this extension has launched (for the benchmark's launch accounting).
+static std::atomic<long long> g_launches{0};
+long long launch_count() { return g_launches.load(); }
+
+#define TGO_CHECK_LAUNCH_N(expr, n)                                                        \
   do {                                                                                     \
     cudaError_t _e = (expr);                                                               \
     TORCH_CHECK(_e == cudaSuccess, "kernel launch failed: ", cudaGetErrorString(_e));      \
+    g_launches += (n);                                                                     \
   } while (0)
+#define TGO_CHECK_LAUNCH(expr) TGO_CHECK_LAUNCH_N(expr, 1)
 
 static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -217,10 +225,10 @@ std::vector<at::Tensor> adanorm_bwd(at::Tensor dh, c10::optional<at::Tensor> dxe
     dscale = at::empty({B, D}, fopt);
   }
   if (p.dy != nullptr) dgate = at::empty({B, D}, fopt);
-  TGO_CHECK_LAUNCH(adanorm_bwd_launch(p, dshift.defined() ? dshift.data_ptr<float>() : nullptr,
+  TGO_CHECK_LAUNCH_N(adanorm_bwd_launch(p, dshift.defined() ? dshift.data_ptr<float>() : nullptr,
                                       dscale.defined() ? dscale.data_ptr<float>() : nullptr,
                                       dgate.defined() ? dgate.data_ptr<float>() : nullptr, dw.data_ptr<float>(),
-                                      at::cuda::getCurrentCUDAStream()));
+                                      at::cuda::getCurrentCUDAStream()), 2);
   return {dx, dy, dshift, dscale, dgate};
 }
 
@@ -389,10 +397,10 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::T
   p.lse = lse.data_ptr<float>();
   at::Tensor delta = at::empty({p.B, p.Hq, p.Tq}, q.options().dtype(at::kFloat));
   at::Tensor dq_acc = at::empty({p.B, p.Tq, p.Hq, p.hd}, q.options().dtype(at::kFloat));
-  TGO_CHECK_LAUNCH(attention_bwd_launch(p, bfp(dO), delta.data_ptr<float>(), dq_acc.data_ptr<float>(), bfp(dq),
+  TGO_CHECK_LAUNCH_N(attention_bwd_launch(p, bfp(dO), delta.data_ptr<float>(), dq_acc.data_ptr<float>(), bfp(dq),
                                         dq.stride(0), dq.stride(1), dq.stride(2), bfp(dk), dk.stride(0), dk.stride(1),
                                         dk.stride(2), bfp(dv), dv.stride(0), dv.stride(1), dv.stride(2),
-                                        at::cuda::getCurrentCUDAStream()));
+                                        at::cuda::getCurrentCUDAStream()), 3);
 }
 
 }  // namespace tgo
@@ -402,6 +410,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &tgo::gemm, "tcgen05 bf16 GEMM: C = alpha * op(A) op(B)^T (+ beta D)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("a_mn"), py::arg("b_mn"), py::arg("D") = c10::nullopt, py::arg("alpha") = 1.0,
         py::arg("beta") = 0.0, py::arg("accumulate") = false, py::arg("err"));
+  m.def("launch_count", &tgo::launch_count, "kernels launched by this extension so far");
   m.def("adanorm_fwd", &tgo::adanorm_fwd, "x_new = x + gate*y; h = rmsnorm(x_new)*w*(1+scale)+shift");
   m.def("adanorm_bwd", &tgo::adanorm_bwd, "backward of adanorm_fwd");
   m.def("qknorm_rope_fwd", &tgo::qknorm_rope_fwd, "per-head RMSNorm + RoPE of q and k from the qkv rows");

@@ -1,0 +1,134 @@
+"""Data-parallel gradient reduction with flat gradient buckets.
+
+Reference: DDP with 64 MB buckets, ``gradient_as_bucket_view`` and the bf16 compress hook (train.py:774-791):
+gradients are cast to bf16, all-reduced, divided by the world size and written back in fp32.
+
+Here every trainable parameter's ``.grad`` is a view into one of a few flat fp32 bucket buffers allocated once
+(the fused Linear backward accumulates weight gradients into them directly). Buckets are ordered by reverse
+registration order, i.e. roughly the order backward produces them, and each bucket is reduced as soon as its last
+gradient has been accumulated on the last micro-batch, on a side stream, so the reduction overlaps the rest of the
+backward pass. The transport is pluggable: ``nccl_bf16`` (cast + NCCL all_reduce + scale, the reference's hook) or
+the fused peer-memory kernel of parallel/comm.py.
+"""
+import torch
+import torch.distributed as dist
+
+from ..ops import fused as Fz
+
+
+class GradBuckets:
+    def __init__(self, params, bucket_bytes=256 * 2 ** 20, group=None, comm="nccl_bf16", overlap=True):
+        self.params = [p for p in params if p.requires_grad]
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.comm = comm
+        self.overlap = overlap and self.world > 1
+        dev = self.params[0].device
+        # buckets in reverse order (backward produces the last layers' gradients first)
+        order = list(reversed(self.params))
+        self.buckets, cur, size = [], [], 0
+        for p in order:
+            cur.append(p)
+            size += p.numel() * 4
+            if size >= bucket_bytes:
+                self.buckets.append(cur)
+                cur, size = [], 0
+        if cur:
+            self.buckets.append(cur)
+        self.flat = []
+        self.bucket_of = {}
+        for bi, ps in enumerate(self.buckets):
+            n = sum(p.numel() for p in ps)
+            buf = torch.zeros(n, dtype=torch.float32, device=dev)
+            off = 0
+            for p in ps:
+                p.grad = buf[off:off + p.numel()].view_as(p)
+                self.bucket_of[p] = bi
+                off += p.numel()
+            self.flat.append(buf)
+        self.pending = [0] * len(self.buckets)
+        self.armed = False
+        self.stream = torch.cuda.Stream(device=dev) if dev.type == "cuda" and self.overlap else None
+        self.events = []
+        self._handles = []
+        if self.overlap:
+            Fz.add_grad_ready_hook(self._on_ready)
+            for p in self.params:
+                self._handles.append(p.register_post_accumulate_grad_hook(self._on_ready))
+
+    def close(self):
+        Fz.remove_grad_ready_hook(self._on_ready)
+        for h in self._handles:
+            h.remove()
+
+    def zero(self):
+        for b in self.flat:
+            b.zero_()
+        # autograd may have replaced a .grad it could not accumulate into in place: re-point at the buckets
+        for bi, ps in enumerate(self.buckets):
+            off = 0
+            for p in ps:
+                view = self.flat[bi][off:off + p.numel()].view_as(p)
+                if p.grad is None or p.grad.data_ptr() != view.data_ptr():
+                    p.grad = view
+                off += p.numel()
+
+    def arm(self):
+        """Call before the backward of the last micro-batch: buckets reduce as their gradients complete."""
+        self.pending = [len(ps) for ps in self.buckets]
+        self.armed = True
+        self.events = []
+
+    def _on_ready(self, p):
+        if not self.armed:
+            return
+        bi = self.bucket_of.get(p)
+        if bi is None:
+            return
+        self.pending[bi] -= 1
+        if self.pending[bi] == 0:
+            self._launch(bi)
+
+    def _launch(self, bi):
+        buf = self.flat[bi]
+        if self.stream is not None:
+            ev = torch.cuda.Event()
+            ev.record()
+            with torch.cuda.stream(self.stream):
+                self.stream.wait_event(ev)
+                self._reduce(buf)
+                done = torch.cuda.Event()
+                done.record()
+            self.events.append(done)
+        else:
+            self._reduce(buf)
+
+    def _reduce(self, buf):
+        if self.world == 1:
+            return
+        if self.comm == "nccl_fp32":
+            dist.all_reduce(buf, group=self.group)
+            buf.div_(self.world)
+        else:
+            lo = buf.to(torch.bfloat16)
+            dist.all_reduce(lo, group=self.group)
+            buf.copy_(lo).div_(self.world)
+
+    def finish(self):
+        """Wait for the reductions (reduce any bucket that did not fire) before the optimizer reads the grads."""
+        if self.world == 1:
+            self.armed = False
+            return
+        if self.overlap:
+            for bi, n in enumerate(self.pending):
+                if n > 0:  # a parameter without a gradient this step (unused branch)
+                    self.pending[bi] = 0
+                    self._launch(bi)
+            if self.stream is not None:
+                cur = torch.cuda.current_stream()
+                for ev in self.events:
+                    cur.wait_event(ev)
+        else:
+            for buf in self.flat:
+                self._reduce(buf)
+        self.armed = False
