@@ -47,6 +47,8 @@ def parse():
     p.add_argument("--res", type=int, default=512)
     p.add_argument("--text-len", type=int, default=128)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--profile-dir", default="", help="profile one step after warm-up (torch.profiler), print the "
+                   "kernel table and write traces there; the timed numbers are taken without the profiler")
     return p.parse_args()
 
 
@@ -177,6 +179,16 @@ def run_ours(args):
         tr.step(devb)
     torch.cuda.synchronize()
     check_errors(device)
+    if args.profile_dir:
+        from trenowanie_generatora_obrazkow_b200.utils.profiling import TrainingProfile, export_profile, \
+            summarize_kernels
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CPU,
+                                                torch.profiler.ProfilerActivity.CUDA]) as prof:
+            tr.step(devb)
+            torch.cuda.synchronize()
+        table, total = export_profile(prof, args.profile_dir, rank)
+        if rank == 0:
+            print(summarize_kernels(table[:40], total), flush=True)
     n0 = ext().launch_count()
     ms, clocks = timed(lambda: tr.step(devb), args.steps, world, local)
     launches = (ext().launch_count() - n0) // args.steps * args.steps

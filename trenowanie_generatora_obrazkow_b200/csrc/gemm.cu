@@ -264,6 +264,190 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
 
 // ----------------------------------------------------------------------------------------------------------------
+// 2-CTA variant: a cluster of two CTAs (one TPC) computes a 256 x 256 tile with tcgen05.mma.cta_group::2.
+// CTA r of the pair loads rows [m0 + 128 r, +128) of A and rows [n0 + 128 r, +128) of B into its own shared memory
+// (plain TMA loads, completing on the leader CTA's "full" barrier); the leader's single MMA thread issues
+// 256 x 256 x 16 MMAs that read both CTAs' tiles; each CTA's TMEM holds its 128 rows x 256 columns.  Per CTA a
+// k-block moves 32 KB for 4.2 MFLOP (vs 48 KB for the 1-CTA 128 x 256 tile), which is what keeps L2 -> SM traffic
+// below the L2 bandwidth at full tensor rate.
+// ----------------------------------------------------------------------------------------------------------------
+constexpr int G2_BN = 256;               // N of the pair's tile; each CTA holds 128 columns of B
+constexpr int G2_A_BYTES = 128 * 64 * 2; // 16 KB
+constexpr int G2_B_BYTES = 128 * 64 * 2; // 16 KB
+constexpr int G2_STAGE_BYTES = G2_A_BYTES + G2_B_BYTES;
+constexpr int G2_STAGES = 6;
+constexpr int G2_SMEM = G2_STAGES * G2_STAGE_BYTES + 1024;
+constexpr int G2_TMEM_COLS = 512;        // two 256-column accumulators
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[G2_STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[G2_STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar[2];
+  __shared__ __align__(8) uint64_t tempty_bar[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_sh;
+
+  const int warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
+  const int num_m = (p.M + 255) / 256;
+  const int num_n = (p.N + G2_BN - 1) / G2_BN;
+  const int tiles_per_batch = num_m * num_n;
+  const int num_tiles = tiles_per_batch * p.batch;
+  const int num_kb = (p.K + GEMM_BK - 1) / GEMM_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < G2_STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);   // leader only: one arrive.expect_tx for both CTAs' bytes
+      mbar_init(&empty_bar[s], 1);  // both: the leader's multicast commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);  // both: the leader's multicast commit
+      mbar_init(&tempty_bar[a], 8); // leader only: 4 epilogue warps x 2 CTAs
+    }
+    abort_sh = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&tmem_base_sh, G2_TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // peer barriers initialised and TMEM allocated before any cross-CTA traffic
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs) ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = cluster; tile < num_tiles && !abort_sh; tile += n_clusters) {
+        const int b = tile / tiles_per_batch, r = tile % tiles_per_batch;
+        const int m0 = (r / num_n) * 256 + rank * 128, n0 = (r % num_n) * G2_BN + rank * 128;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+            abort_sh = 1;
+            break;
+          }
+          uint8_t* sa = smem + stage * G2_STAGE_BYTES;
+          uint8_t* sb = sa + G2_A_BYTES;
+          if (leader) mbar_expect_tx(&full_bar[stage], 2 * G2_STAGE_BYTES);
+          const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          const int k0 = kb * GEMM_BK;
+          if constexpr (!A_MN) {
+            tma_load_3d_pair(sa, &tmA, fb, k0, m0, b);
+          } else {
+            tma_load_3d_pair(sa, &tmA, fb, m0, k0, b);
+            tma_load_3d_pair(sa + 8192, &tmA, fb, m0 + 64, k0, b);
+          }
+          if constexpr (!B_MN) {
+            tma_load_3d_pair(sb, &tmB, fb, k0, n0, b);
+          } else {
+            tma_load_3d_pair(sb, &tmB, fb, n0, k0, b);
+            tma_load_3d_pair(sb + 8192, &tmB, fb, n0 + 64, k0, b);
+          }
+          if (++stage == G2_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (leader CTA only) ----------------
+      constexpr uint32_t idesc = idesc_bf16_f32(256, G2_BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = cluster; tile < num_tiles && !abort_sh; tile += n_clusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, p.err, ERR_MBAR_TIMEOUT_MMA)) {
+          abort_sh = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * G2_BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, p.err, ERR_MBAR_TIMEOUT_MMA)) {
+            abort_sh = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * G2_STAGE_BYTES);
+          const uint32_t sb = sa + G2_A_BYTES;
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sdesc_sw128(sa + k * 2048, 8192, 1024) : sdesc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(sb + k * 2048, 8192, 1024) : sdesc_sw128(sb + k * 32, 16, 1024);
+            umma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair_mc(&empty_bar[stage], 0x3);  // frees this stage in both CTAs
+          if (++stage == G2_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(&tfull_bar[acc], 0x3);  // both CTAs' accumulators ready
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    const int q = warp & 3;
+    int local = 0;
+    for (int tile = cluster; tile < num_tiles; tile += n_clusters, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&tfull_bar[acc], acc_phase, p.err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        abort_sh = 1;
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      const int b = tile / tiles_per_batch, r = tile % tiles_per_batch;
+      const int m0 = (r / num_n) * 256 + rank * 128, n0 = (r % num_n) * G2_BN;
+      const int row = m0 + q * 32 + lane;
+      const uint32_t tbase = tmem_base + acc * G2_BN + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < G2_BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tbase + c * 32, v);
+        tmem_ld_wait();
+        gemm_store_chunk<EPI>(p, b, row, n0 + c * 32, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA frees TMEM or exits while the pair still has MMAs / remote arrivals in flight
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, G2_TMEM_COLS);
+  }
+}
+
+// ----------------------------------------------------------------------------------------------------------------
 // Launch (tensor maps are encoded by the host wrapper in ops.cpp)
 // ----------------------------------------------------------------------------------------------------------------
 int num_sms() {
@@ -300,8 +484,37 @@ static cudaError_t dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, c
   return launch_gemm<BN, true, true, EPI>(ta, tb, p, s);
 }
 
+template <bool A_MN, bool B_MN, int EPI>
+static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                                    cudaStream_t stream) {
+  auto kern = gemm_tcgen05_pair_kernel<A_MN, B_MN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G2_SMEM);
+    attr_set = true;
+  }
+  const int num_tiles = ((p.M + 255) / 256) * ((p.N + G2_BN - 1) / G2_BN) * p.batch;
+  const int grid = std::max(2, std::min(2 * num_tiles, (num_sms() / 2) * 2));
+  kern<<<grid, GEMM_THREADS, G2_SMEM, stream>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+template <int EPI>
+static cudaError_t dispatch_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                                 const GemmParams& p, cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_gemm_pair<false, false, EPI>(ta, tb, p, s);
+  if (!a_mn && b_mn) return launch_gemm_pair<false, true, EPI>(ta, tb, p, s);
+  if (a_mn && !b_mn) return launch_gemm_pair<true, false, EPI>(ta, tb, p, s);
+  return launch_gemm_pair<true, true, EPI>(ta, tb, p, s);
+}
+
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int bn, bool a_mn,
                         bool b_mn, int epi, cudaStream_t s) {
+  if (bn == 0) {  // 2-CTA kernel (tensor maps built with 128-row / 64-row boxes per CTA)
+    if (epi == EPI_BF16) return dispatch_pair<EPI_BF16>(a_mn, b_mn, ta, tb, p, s);
+    if (epi == EPI_F32) return dispatch_pair<EPI_F32>(a_mn, b_mn, ta, tb, p, s);
+    return dispatch_pair<EPI_F32_ACC>(a_mn, b_mn, ta, tb, p, s);
+  }
   if (bn == 128) {
     if (epi == EPI_BF16) return dispatch_major<128, EPI_BF16>(a_mn, b_mn, ta, tb, p, s);
     if (epi == EPI_F32) return dispatch_major<128, EPI_F32>(a_mn, b_mn, ta, tb, p, s);

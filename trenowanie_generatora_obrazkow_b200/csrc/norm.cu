@@ -11,6 +11,8 @@
 //   aurora/model.py:37-40, :98-99, :164), reading the fused qkv GEMM output in place.
 //
 // swiglu: g = silu(a) * b on the fused in_proj output [a | b] (reference aurora/model.py:102-110).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -196,27 +198,25 @@ __global__ void adanorm_bwd_kernel(AdaNormBwdParams p) {
   }
 }
 
-// Reduce the partials: dmod[b][k][c] (k = shift, scale, gate) over chunks, and dw[c] (+=) over batches and chunks.
+// Reduce the partials: one thread per (sample, channel) sums its chunks; dw[c] += (atomically) over samples.
 __global__ void adanorm_bwd_reduce_kernel(const float* __restrict__ partial, float* __restrict__ dshift,
                                           float* __restrict__ dscale, float* __restrict__ dgate,
                                           float* __restrict__ dw, int B, int chunks, int D) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.y;
   if (c >= D) return;
-  float w_acc = 0.f;
-  for (int b = 0; b < B; ++b) {
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f;
-    for (int j = 0; j < chunks; ++j) {
-      const float* src = partial + ((long long)(b * chunks + j) * 4) * D + c;
-      s0 += src[0];
-      s1 += src[D];
-      s2 += src[2 * D];
-      w_acc += src[3 * D];
-    }
-    if (dshift) dshift[(long long)b * D + c] = s0;
-    if (dscale) dscale[(long long)b * D + c] = s1;
-    if (dgate) dgate[(long long)b * D + c] = s2;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  for (int j = 0; j < chunks; ++j) {
+    const float* src = partial + ((long long)(b * chunks + j) * 4) * D + c;
+    s0 += src[0];
+    s1 += src[D];
+    s2 += src[2 * D];
+    s3 += src[3 * D];
   }
-  dw[c] += w_acc;
+  if (dshift) dshift[(long long)b * D + c] = s0;
+  if (dscale) dscale[(long long)b * D + c] = s1;
+  if (dgate) dgate[(long long)b * D + c] = s2;
+  atomicAdd(&dw[c], s3);
 }
 
 cudaError_t adanorm_fwd_launch(const AdaNormFwdParams& p, cudaStream_t s) {
@@ -233,8 +233,8 @@ cudaError_t adanorm_bwd_launch(const AdaNormBwdParams& p, float* dshift, float* 
   adanorm_bwd_kernel<<<grid, threads, 0, s>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  adanorm_bwd_reduce_kernel<<<(p.D + 255) / 256, 256, 0, s>>>(p.partial, dshift, dscale, dgate, dw, p.M / p.T,
-                                                                p.chunks, p.D);
+  adanorm_bwd_reduce_kernel<<<dim3((p.D + 127) / 128, p.M / p.T), 128, 0, s>>>(p.partial, dshift, dscale, dgate,
+                                                                               dw, p.M / p.T, p.chunks, p.D);
   return cudaGetLastError();
 }
 
@@ -290,6 +290,8 @@ __global__ void qknorm_rope_fwd_kernel(QKNormRopeParams p) {
 }
 
 // Backward: dq / dk (post-RoPE) -> d(pre-norm q / k) written into dqkv; dw_q, dw_k accumulated (+=).
+// Persistent grid: each warp walks (row, head) items with a grid stride and keeps its dw partials in registers;
+// one shared-memory reduction and one global atomic per element and CTA at the end.
 template <int HD>
 __global__ void qknorm_rope_bwd_kernel(QKNormRopeParams p, const bf16* __restrict__ dq, long long ld_dq,
                                        const bf16* __restrict__ dk, long long ld_dk, bf16* __restrict__ dqkv,
@@ -299,10 +301,14 @@ __global__ void qknorm_rope_bwd_kernel(QKNormRopeParams p, const bf16* __restric
   for (int i = threadIdx.x; i < 2 * HD; i += blockDim.x) (&s_dw[0][0])[i] = 0.f;
   __syncthreads();
   const int heads = p.hq + p.hkv;
-  const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp_id();
+  const long long total = (long long)p.M * heads;
   const int lane = lane_id();
   const int e0 = lane * E;
-  if (item < (long long)p.M * heads) {
+  float acc_q[E], acc_k[E];
+#pragma unroll
+  for (int i = 0; i < E; ++i) acc_q[i] = acc_k[i] = 0.f;
+  const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp_id(); item < total; item += nwarps) {
     const int row = (int)(item / heads), hh = (int)(item % heads);
     const bool is_q = hh < p.hq;
     const bf16* gsrc = is_q ? dq + (long long)row * ld_dq + (long long)hh * HD + e0
@@ -337,11 +343,11 @@ __global__ void qknorm_rope_bwd_kernel(QKNormRopeParams p, const bf16* __restric
       }
       const float r = (is_q ? p.rstd_q : p.rstd_k)[(long long)row * (is_q ? p.hq : p.hkv) + (is_q ? hh : hh - p.hq)];
       float dot = 0.f;
-      float* sdw = s_dw[is_q ? 0 : 1];
 #pragma unroll
       for (int i = 0; i < E; ++i) {
         const float n = x[i] * r;
-        atomicAdd(&sdw[e0 + i], g[i] * n);
+        if (is_q) acc_q[i] += g[i] * n;
+        else acc_k[i] += g[i] * n;
         g[i] *= nw[e0 + i];  // dn
         dot += g[i] * n;
         x[i] = n;
@@ -353,6 +359,11 @@ __global__ void qknorm_rope_bwd_kernel(QKNormRopeParams p, const bf16* __restric
     bf16* dst = dqkv + (long long)row * ld_dqkv + (long long)hh * HD + e0;
 #pragma unroll
     for (int i = 0; i < E; i += 2) *reinterpret_cast<__nv_bfloat162*>(dst + i) = __floats2bfloat162_rn(g[i], g[i + 1]);
+  }
+#pragma unroll
+  for (int i = 0; i < E; ++i) {
+    atomicAdd(&s_dw[0][e0 + i], acc_q[i]);
+    atomicAdd(&s_dw[1][e0 + i], acc_k[i]);
   }
   __syncthreads();
   if (p.q_w != nullptr && dwq != nullptr)
@@ -376,7 +387,7 @@ cudaError_t qknorm_rope_bwd_launch(const QKNormRopeParams& p, const bf16* dq, lo
                                    cudaStream_t s) {
   const long long items = (long long)p.M * (p.hq + p.hkv);
   const int warps = 16;
-  const unsigned grid = (unsigned)((items + warps - 1) / warps);
+  const unsigned grid = (unsigned)std::min<long long>((items + warps - 1) / warps, (long long)num_sms() * 4);
   if (p.hd == 128)
     qknorm_rope_bwd_kernel<128><<<grid, warps * 32, 0, s>>>(p, dq, ld_dq, dk, ld_dk, dqkv, ld_dqkv, dwq, dwk);
   else if (p.hd == 64)

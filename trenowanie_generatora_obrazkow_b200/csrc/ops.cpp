@@ -55,6 +55,9 @@ static CUtensorMap make_tmap_bf16_sw128(const void* base, uint64_t inner, uint64
   return m;
 }
 
+static bool g_gemm_pair_enabled = false;  // measured slower than the 1-CTA kernel on most shapes so far
+void set_gemm_pair(bool on) { g_gemm_pair_enabled = on; }
+
 static int* err_ptr(const at::Tensor& err) {
   TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt && err.numel() >= 1, "err must be a CUDA int32 tensor");
   return err.data_ptr<int>();
@@ -89,12 +92,16 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor C, bool a_mn, bool b_mn, c10::o
     if (!accumulate) C.zero_();
     return;
   }
-  const int bn = N <= 128 ? 128 : 256;
+  // 2-CTA kernel (256 x 256 tiles over a CTA pair) when there are enough such tiles to fill the GPU; otherwise
+  // the 1-CTA kernel with 128 x 256 (or 128 x 128 for N <= 128) tiles.
+  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256) * batch;
+  const bool use_pair = g_gemm_pair_enabled && M >= 256 && N >= 256 && pair_tiles >= num_sms() / 2;
+  const int bn = use_pair ? 0 : (N <= 128 ? 128 : 256);
   const uint64_t bsA = batched ? A.stride(0) : 0, bsB = batched ? B.stride(0) : 0;
   CUtensorMap ta = make_tmap_bf16_sw128(A.data_ptr(), A.size(-1), A.size(-2), batch, A.stride(-2), bsA,
                                         a_mn ? 64 : 128);
   CUtensorMap tb = make_tmap_bf16_sw128(B.data_ptr(), B.size(-1), B.size(-2), batch, B.stride(-2), bsB,
-                                        b_mn ? 64 : bn);
+                                        b_mn ? 64 : (use_pair ? 128 : bn));
   GemmParams p;
   p.M = (int)M;
   p.N = (int)N;
@@ -214,7 +221,7 @@ std::vector<at::Tensor> adanorm_bwd(at::Tensor dh, c10::optional<at::Tensor> dxe
   p.M = (int)M;
   p.D = (int)D;
   p.T = (int)T;
-  p.rows_per_cta = 64;
+  p.rows_per_cta = 32;
   p.chunks = (int)((T + p.rows_per_cta - 1) / p.rows_per_cta);
   at::Tensor partial = at::empty({B, p.chunks, 4, D}, dh.options().dtype(at::kFloat));
   p.partial = partial.data_ptr<float>();
@@ -410,6 +417,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &tgo::gemm, "tcgen05 bf16 GEMM: C = alpha * op(A) op(B)^T (+ beta D)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("a_mn"), py::arg("b_mn"), py::arg("D") = c10::nullopt, py::arg("alpha") = 1.0,
         py::arg("beta") = 0.0, py::arg("accumulate") = false, py::arg("err"));
+  m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");
   m.def("launch_count", &tgo::launch_count, "kernels launched by this extension so far");
   m.def("adanorm_fwd", &tgo::adanorm_fwd, "x_new = x + gate*y; h = rmsnorm(x_new)*w*(1+scale)+shift");
   m.def("adanorm_bwd", &tgo::adanorm_bwd, "backward of adanorm_fwd");
