@@ -110,4 +110,8 @@ cudaError_t attention_bwd_launch(const AttnParams& p, const __nv_bfloat16* dO, f
                                  __nv_bfloat16* dk, long long dk_bs, long long dk_ts, long long dk_hs,
                                  __nv_bfloat16* dv, long long dv_bs, long long dv_ts, long long dv_hs, cudaStream_t s);
 
+// tcgen05 forward (attention_tc.cu); tensor maps: 4-D {hd, T, H, B}, boxes {64, 128 | 64, 1, 1}, 128-byte swizzle
+cudaError_t attention_fwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                                    const AttnParams& p, int* err, cudaStream_t s);
+
 }  // namespace tgo

@@ -55,6 +55,26 @@ static CUtensorMap make_tmap_bf16_sw128(const void* base, uint64_t inner, uint64
   return m;
 }
 
+// 4-D bf16 tensor map {hd, T, H, B} (strides in elements) with a {64, box_rows, 1, 1} box, 128-byte swizzle.
+static CUtensorMap make_tmap_bhtd(const void* base, uint64_t hd, uint64_t T, uint64_t H, uint64_t B, uint64_t ts,
+                                  uint64_t hs, uint64_t bs, uint32_t box_rows) {
+  CUtensorMap m;
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base address must be 16-byte aligned");
+  TORCH_CHECK(ts % 8 == 0 && hs % 8 == 0 && bs % 8 == 0, "TMA strides must be multiples of 16 bytes");
+  cuuint64_t dims[4] = {hd, T, H, B};
+  cuuint64_t strides[3] = {ts * 2, (H > 1 ? hs : ts * T) * 2, (B > 1 ? bs : ts * T * H) * 2};
+  cuuint32_t box[4] = {64, box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = tmap_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (4-D) failed with code ", (int)r);
+  return m;
+}
+
+static bool g_attention_tc = true;
+void set_attention_tc(bool on) { g_attention_tc = on; }
+
 static bool g_gemm_pair_enabled = false;  // measured slower than the 1-CTA kernel on most shapes so far
 void set_gemm_pair(bool on) { g_gemm_pair_enabled = on; }
 
@@ -371,7 +391,7 @@ static AttnParams attn_params(const at::Tensor& q, const at::Tensor& k, const at
 
 // o: optional preallocated [B, Tq, Hq, hd] output (may be a strided view)
 std::vector<at::Tensor> attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, c10::optional<at::Tensor> kv_len,
-                                      double scale, c10::optional<at::Tensor> out) {
+                                      double scale, c10::optional<at::Tensor> out, at::Tensor err) {
   const c10::cuda::CUDAGuard guard(q.device());
   AttnParams p = attn_params(q, k, v, kv_len, scale);
   at::Tensor o = out.has_value() && out->defined() ? *out : at::empty({p.B, p.Tq, p.Hq, p.hd}, q.options());
@@ -382,7 +402,14 @@ std::vector<at::Tensor> attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, 
   p.o_ts = o.stride(1);
   p.o_hs = o.stride(2);
   p.lse = lse.data_ptr<float>();
-  TGO_CHECK_LAUNCH(attention_fwd_launch(p, at::cuda::getCurrentCUDAStream()));
+  if (g_attention_tc) {
+    CUtensorMap tq = make_tmap_bhtd(p.q, p.hd, p.Tq, p.Hq, p.B, p.q_ts, p.q_hs, p.q_bs, 128);
+    CUtensorMap tk = make_tmap_bhtd(p.k, p.hd, p.Tk, p.Hkv, p.B, p.k_ts, p.k_hs, p.k_bs, 64);
+    CUtensorMap tv = make_tmap_bhtd(p.v, p.hd, p.Tk, p.Hkv, p.B, p.v_ts, p.v_hs, p.v_bs, 64);
+    TGO_CHECK_LAUNCH(attention_fwd_tc_launch(tq, tk, tv, p, err_ptr(err), at::cuda::getCurrentCUDAStream()));
+  } else {
+    TGO_CHECK_LAUNCH(attention_fwd_launch(p, at::cuda::getCurrentCUDAStream()));
+  }
   return {o, lse};
 }
 
@@ -417,6 +444,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &tgo::gemm, "tcgen05 bf16 GEMM: C = alpha * op(A) op(B)^T (+ beta D)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("a_mn"), py::arg("b_mn"), py::arg("D") = c10::nullopt, py::arg("alpha") = 1.0,
         py::arg("beta") = 0.0, py::arg("accumulate") = false, py::arg("err"));
+  m.def("set_attention_tc", &tgo::set_attention_tc, "use the tcgen05 attention forward (default) or mma.sync");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");
   m.def("launch_count", &tgo::launch_count, "kernels launched by this extension so far");
   m.def("adanorm_fwd", &tgo::adanorm_fwd, "x_new = x + gate*y; h = rmsnorm(x_new)*w*(1+scale)+shift");

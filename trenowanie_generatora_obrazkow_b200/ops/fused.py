@@ -14,7 +14,7 @@ autograd. Each CUDA op is a ``torch.autograd.Function`` whose backward is a hand
 import torch
 
 from . import reference as R
-from ._ext import ext
+from ._ext import err_buf, ext
 from .gemm import gemm
 
 # ----------------------------------------------------------------------------------------------------------------
@@ -205,7 +205,7 @@ class _SelfAttnFn(torch.autograd.Function):
         q4 = q.view(B, T, hq, hd)
         k4 = k.view(B, T, hkv, hd)
         v4 = qkv[:, :, (hq + hkv) * hd:(hq + 2 * hkv) * hd].unflatten(-1, (hkv, hd))
-        o, lse = ext().attention_fwd(q4, k4, v4, kv_len, scale, None)
+        o, lse = ext().attention_fwd(q4, k4, v4, kv_len, scale, None, err_buf(q4.device))
         ctx.save_for_backward(qkv, q, k, o, lse, rq, rk, q_w, k_w, cos, sin, kv_len)
         ctx.dims = (hq, hkv, hd, scale)
         return o.view(B, T, hq * hd)
@@ -261,7 +261,7 @@ class _CrossAttnFn(torch.autograd.Function):
         q4 = q.view(B, T, heads, head_dim)
         k4 = kv[:, :, :D].unflatten(-1, (heads, head_dim))
         v4 = kv[:, :, D:].unflatten(-1, (heads, head_dim))
-        o, lse = ext().attention_fwd(q4, k4, v4, kv_len, scale, None)
+        o, lse = ext().attention_fwd(q4, k4, v4, kv_len, scale, None, err_buf(q4.device))
         ctx.save_for_backward(q, kv, o, lse, kv_len)
         ctx.dims = (heads, head_dim, scale)
         return o.view(B, T, D)
