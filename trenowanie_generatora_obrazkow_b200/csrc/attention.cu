@@ -546,6 +546,27 @@ static cudaError_t bwd_impl(const AttnParams& p, const bf16* dO, float* delta, f
   return cudaGetLastError();
 }
 
+// delta = rowsum(dO * O) and a zeroed dQ accumulator (shared by both backward kernels)
+cudaError_t attention_bwd_prep_launch(const AttnParams& p, const bf16* dO, float* delta, float* dq_acc, cudaStream_t s) {
+  const long long items = (long long)p.B * p.Tq * p.Hq;
+  if (p.hd == 128) flash_bwd_delta_kernel<128><<<(unsigned)((items + 7) / 8), 256, 0, s>>>(p, dO, delta);
+  else if (p.hd == 64) flash_bwd_delta_kernel<64><<<(unsigned)((items + 7) / 8), 256, 0, s>>>(p, dO, delta);
+  else return cudaErrorInvalidValue;
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)p.B * p.Tq * p.Hq * p.hd, s);
+}
+
+cudaError_t attention_dq_convert_launch(const AttnParams& p, const float* dq_acc, bf16* dq, long long bs, long long ts,
+                                        long long hs, cudaStream_t s) {
+  const long long n8 = (long long)p.B * p.Tq * p.Hq * (p.hd / 8);
+  const int grid = (int)std::min<long long>((n8 + 255) / 256, (long long)num_sms() * 16);
+  if (p.hd == 128) dq_convert_kernel<128><<<grid, 256, 0, s>>>(p, dq_acc, dq, bs, ts, hs);
+  else if (p.hd == 64) dq_convert_kernel<64><<<grid, 256, 0, s>>>(p, dq_acc, dq, bs, ts, hs);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
 cudaError_t attention_bwd_launch(const AttnParams& p, const bf16* dO, float* delta, float* dq_acc, bf16* dq,
                                  long long dq_bs, long long dq_ts, long long dq_hs, bf16* dk, long long dk_bs,
                                  long long dk_ts, long long dk_hs, bf16* dv, long long dv_bs, long long dv_ts,

@@ -110,6 +110,16 @@ cudaError_t attention_bwd_launch(const AttnParams& p, const __nv_bfloat16* dO, f
                                  __nv_bfloat16* dk, long long dk_bs, long long dk_ts, long long dk_hs,
                                  __nv_bfloat16* dv, long long dv_bs, long long dv_ts, long long dv_hs, cudaStream_t s);
 
+cudaError_t attention_bwd_prep_launch(const AttnParams& p, const __nv_bfloat16* dO, float* delta, float* dq_acc,
+                                      cudaStream_t s);
+cudaError_t attention_dq_convert_launch(const AttnParams& p, const float* dq_acc, __nv_bfloat16* dq, long long bs,
+                                        long long ts, long long hs, cudaStream_t s);
+// tcgen05 backward (head dim 128); dq_acc zeroed and delta computed by attention_bwd_prep_launch
+cudaError_t attention_bwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                                    const CUtensorMap& tdo, const AttnParams& p, const float* delta, float* dq_acc,
+                                    __nv_bfloat16* dk, long long dk_bs, long long dk_ts, long long dk_hs,
+                                    __nv_bfloat16* dv, long long dv_bs, long long dv_ts, long long dv_hs, int* err,
+                                    cudaStream_t s);
 // tcgen05 forward (attention_tc.cu); tensor maps: 4-D {hd, T, H, B}, boxes {64, 128 | 64, 1, 1}, 128-byte swizzle
 cudaError_t attention_fwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                     const AttnParams& p, int* err, cudaStream_t s);

@@ -415,7 +415,8 @@ std::vector<at::Tensor> attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, 
 
 // Writes dq, dk, dv (preallocated, possibly strided views). dO must have o's layout.
 void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, at::Tensor dO,
-                   c10::optional<at::Tensor> kv_len, double scale, at::Tensor dq, at::Tensor dk, at::Tensor dv) {
+                   c10::optional<at::Tensor> kv_len, double scale, at::Tensor dq, at::Tensor dk, at::Tensor dv,
+                   at::Tensor err) {
   const c10::cuda::CUDAGuard guard(q.device());
   AttnParams p = attn_params(q, k, v, kv_len, scale);
   attn_check4(o, "o");
@@ -431,10 +432,24 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::T
   p.lse = lse.data_ptr<float>();
   at::Tensor delta = at::empty({p.B, p.Hq, p.Tq}, q.options().dtype(at::kFloat));
   at::Tensor dq_acc = at::empty({p.B, p.Tq, p.Hq, p.hd}, q.options().dtype(at::kFloat));
-  TGO_CHECK_LAUNCH_N(attention_bwd_launch(p, bfp(dO), delta.data_ptr<float>(), dq_acc.data_ptr<float>(), bfp(dq),
-                                        dq.stride(0), dq.stride(1), dq.stride(2), bfp(dk), dk.stride(0), dk.stride(1),
-                                        dk.stride(2), bfp(dv), dv.stride(0), dv.stride(1), dv.stride(2),
-                                        at::cuda::getCurrentCUDAStream()), 3);
+  if (g_attention_tc && p.hd == 128) {
+    cudaStream_t st = at::cuda::getCurrentCUDAStream();
+    CUtensorMap tq = make_tmap_bhtd(p.q, p.hd, p.Tq, p.Hq, p.B, p.q_ts, p.q_hs, p.q_bs, 64);
+    CUtensorMap tk = make_tmap_bhtd(p.k, p.hd, p.Tk, p.Hkv, p.B, p.k_ts, p.k_hs, p.k_bs, 128);
+    CUtensorMap tv = make_tmap_bhtd(p.v, p.hd, p.Tk, p.Hkv, p.B, p.v_ts, p.v_hs, p.v_bs, 128);
+    CUtensorMap tdo = make_tmap_bhtd(dO.data_ptr(), p.hd, p.Tq, p.Hq, p.B, dO.stride(1), dO.stride(2), dO.stride(0), 64);
+    TGO_CHECK_LAUNCH(attention_bwd_prep_launch(p, bfp(dO), delta.data_ptr<float>(), dq_acc.data_ptr<float>(), st));
+    TGO_CHECK_LAUNCH(attention_bwd_tc_launch(tq, tk, tv, tdo, p, delta.data_ptr<float>(), dq_acc.data_ptr<float>(),
+                                             bfp(dk), dk.stride(0), dk.stride(1), dk.stride(2), bfp(dv), dv.stride(0),
+                                             dv.stride(1), dv.stride(2), err_ptr(err), st));
+    TGO_CHECK_LAUNCH(attention_dq_convert_launch(p, dq_acc.data_ptr<float>(), bfp(dq), dq.stride(0), dq.stride(1),
+                                                 dq.stride(2), st));
+  } else {
+    TGO_CHECK_LAUNCH_N(attention_bwd_launch(p, bfp(dO), delta.data_ptr<float>(), dq_acc.data_ptr<float>(), bfp(dq),
+                                          dq.stride(0), dq.stride(1), dq.stride(2), bfp(dk), dk.stride(0), dk.stride(1),
+                                          dk.stride(2), bfp(dv), dv.stride(0), dv.stride(1), dv.stride(2),
+                                          at::cuda::getCurrentCUDAStream()), 3);
+  }
 }
 
 }  // namespace tgo

@@ -222,7 +222,8 @@ class _SelfAttnFn(torch.autograd.Function):
         dv4 = dqkv[:, :, (hq + hkv) * hd:(hq + 2 * hkv) * hd].unflatten(-1, (hkv, hd))
         q4, k4 = q.view(B, T, hq, hd), k.view(B, T, hkv, hd)
         v4 = qkv[:, :, (hq + hkv) * hd:(hq + 2 * hkv) * hd].unflatten(-1, (hkv, hd))
-        ext().attention_bwd(q4, k4, v4, o, lse, do, kv_len, scale, dq.view(B, T, hq, hd), dk.view(B, T, hkv, hd), dv4)
+        ext().attention_bwd(q4, k4, v4, o, lse, do, kv_len, scale, dq.view(B, T, hq, hd), dk.view(B, T, hkv, hd), dv4,
+                            err_buf(q.device))
         dwq = torch.zeros_like(q_w) if q_w is not None else None
         dwk = torch.zeros_like(k_w) if k_w is not None else None
         ext().qknorm_rope_bwd(qkv.view(B * T, C), hq, hkv, hd, q_w, k_w, cos, sin, T, rq, rk, dq, dk,
@@ -279,7 +280,7 @@ class _CrossAttnFn(torch.autograd.Function):
         v4 = kv[:, :, D:].unflatten(-1, (heads, head_dim))
         ext().attention_bwd(q4, k4, v4, o, lse, do, kv_len, scale, dq.view(B, T, heads, head_dim),
                             dkv[:, :, :D].unflatten(-1, (heads, head_dim)),
-                            dkv[:, :, D:].unflatten(-1, (heads, head_dim)))
+                            dkv[:, :, D:].unflatten(-1, (heads, head_dim)), err_buf(q.device))
         return dq, dkv, None, None, None, None
 
 
