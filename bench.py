@@ -47,6 +47,10 @@ def parse():
     p.add_argument("--res", type=int, default=512)
     p.add_argument("--text-len", type=int, default=128)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--sample-batch", type=int, default=8, help="prompts per GPU for the sampling measurement "
+                   "(1024 px, 50 Euler steps, CFG 3, shift 6); 0 = skip it")
+    p.add_argument("--sample-res", type=int, default=1024)
+    p.add_argument("--sample-steps", type=int, default=50)
     p.add_argument("--profile-dir", default="", help="profile one step after warm-up (torch.profiler), print the "
                    "kernel table and write traces there; the timed numbers are taken without the profiler")
     return p.parse_args()
@@ -153,6 +157,19 @@ def synthetic_batch(per_rank, res, text_len, lm_dim, device, seed):
     return host, dev
 
 
+def measure_sampling(run_batch, args, world, local):
+    """Second headline metric: img/s of 1024 px, 50-step CFG sampling (one prompt batch per rank, whole-job
+    images / max-over-ranks device time). run_batch(steps) samples one batch of args.sample_batch prompts."""
+    run_batch(1)  # warm-up at the sampling shapes
+    torch.cuda.synchronize()
+    ms, clocks = timed(lambda: run_batch(args.sample_steps), 1, world, local)
+    images = args.sample_batch * world
+    return {"metric": "1024px 50-step CFG img/s", "value": round(images / (ms / 1e3), 3), "unit": "img/s",
+            "ms_per_batch": round(ms, 1), "images_per_rank": args.sample_batch, "res": args.sample_res,
+            "steps": args.sample_steps, "cfg": 3.0, "shift": 6.0, "clocks": clocks,
+            "timed": "denoising loop on device (VAE decode not included: no FLUX.2 VAE weights offline)"}
+
+
 def emit(rank, out):
     if rank == 0:
         print(json.dumps(out), flush=True)
@@ -220,6 +237,17 @@ def run_ours(args):
                       "ms_per_step": round(ms_e2e, 2), "h2d_bytes_per_step": (x_bytes + s_bytes) * world,
                       "d2h_bytes_per_step": 4 * world,
                       "api": "Trainer.step(batch in pinned host memory) + loss.item()"}
+    if args.sample_batch > 0:
+        from trenowanie_generatora_obrazkow_b200.sampling.euler import encode_prompts, prompt_noise, sample_latents
+        side = args.sample_res // 16
+        g = torch.Generator(device="cpu").manual_seed(99 + rank)
+        sst = torch.randn(args.sample_batch, args.text_len, te_cfg.lm_dim, generator=g).to(device, torch.bfloat16)
+        tr.te.eval(), tr.den.eval()
+        text, lens, null, nlen = encode_prompts(tr.te, lm_states=sst)
+        noise = prompt_noise(args.sample_batch, den_cfg.latent_channels, side, 0, rank * args.sample_batch, device)
+        out["sampling"] = measure_sampling(
+            lambda steps: sample_latents(tr.den, text, lens, null, nlen, steps=steps, cfg=3.0, shift=6.0,
+                                         latent_size=side, noise=noise), args, world, local)
     emit(rank, out)
     if world > 1:
         dist.destroy_process_group()
@@ -340,6 +368,36 @@ def run_reference(args):
         ms_e2e, _ = timed(e2e_step, args.steps, world, local)
         out["e2e"] = {"value": round(tokens / (ms_e2e / 1e3), 1), "unit": "latent-tokens/s",
                       "ms_per_step": round(ms_e2e, 2)}
+    if args.sample_batch > 0:
+        # the denoising loop of aurora/fid.py:sample with the reference's modules (its sample() derives text from
+        # token ids through the frozen LM, which is replaced by synthetic states here)
+        ss = args.sample_res // 16
+        g = torch.Generator(device="cpu").manual_seed(99 + rank)
+        nb = args.sample_batch
+        sst = torch.randn(nb, args.text_len, 1024, generator=g).to(device, torch.bfloat16)
+        s_ids = torch.randint(0, 60000, (nb, args.text_len), device=device)
+        te.eval(), den.eval()
+        u = torch.linspace(1.0, 0.0, args.sample_steps + 1, device=device)
+        shift = 6.0
+        ts_all = shift * u / (1 + (shift - 1) * u)
+        gz = torch.Generator(device=device).manual_seed(rank * nb)
+        z0 = torch.randn(nb, 128, ss, ss, device=device, generator=gz)
+
+        @torch.no_grad()
+        def ref_sample(steps):
+            z = z0.clone()
+            ts = ts_all if steps == args.sample_steps else torch.linspace(1.0, 0.0, steps + 1, device=device)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                text, valid = te(torch.cat([null_row[: s_ids.shape[1]].expand(nb, -1), s_ids]),
+                                 lm_states=torch.cat([sst, sst]))
+                for k in range(steps):
+                    t0, t1 = ts[k], ts[k + 1]
+                    v = den(torch.cat([z, z]), t0.expand(2 * nb), text, valid).float()
+                    v_u, v_c = v.chunk(2)
+                    z = z + (t1 - t0) * (v_u + 3.0 * (v_c - v_u))
+            return z
+
+        out["sampling"] = measure_sampling(ref_sample, args, world, local)
     emit(rank, out)
     if world > 1:
         dist.destroy_process_group()

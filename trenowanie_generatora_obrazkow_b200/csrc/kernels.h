@@ -124,4 +124,8 @@ cudaError_t attention_bwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk
 cudaError_t attention_fwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                     const AttnParams& p, int* err, cudaStream_t s);
 
+// ---------------------------------------------------------------- elementwise (elementwise.cu)
+cudaError_t euler_cfg_launch(const __nv_bfloat16* out, float* z, int B, int T, int C, float dt, float w,
+                             cudaStream_t s);
+
 }  // namespace tgo

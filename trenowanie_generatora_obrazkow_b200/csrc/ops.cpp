@@ -452,6 +452,18 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::T
   }
 }
 
+// ------------------------------------------------------------------------------------------------ sampler
+// z [B, C, H, W] fp32 (in place) += dt * (v_u + w (v_c - v_u)), v from the token-major [2B, H*W, C] output
+void euler_cfg(at::Tensor out, at::Tensor z, double dt, double w) {
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16 && out.dim() == 3, "euler_cfg: out bf16 [2B,T,C]");
+  TORCH_CHECK(z.is_contiguous() && z.scalar_type() == at::kFloat && z.dim() == 4, "euler_cfg: z fp32 [B,C,H,W]");
+  const int64_t B = z.size(0), C = z.size(1), T = z.size(2) * z.size(3);
+  TORCH_CHECK(out.size(0) == 2 * B && out.size(1) == T && out.size(2) == C, "euler_cfg: shapes");
+  const c10::cuda::CUDAGuard guard(z.device());
+  TGO_CHECK_LAUNCH(euler_cfg_launch(bfp(out), z.data_ptr<float>(), (int)B, (int)T, (int)C, (float)dt, (float)w,
+                                    at::cuda::getCurrentCUDAStream()));
+}
+
 }  // namespace tgo
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -459,6 +471,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &tgo::gemm, "tcgen05 bf16 GEMM: C = alpha * op(A) op(B)^T (+ beta D)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("a_mn"), py::arg("b_mn"), py::arg("D") = c10::nullopt, py::arg("alpha") = 1.0,
         py::arg("beta") = 0.0, py::arg("accumulate") = false, py::arg("err"));
+  m.def("euler_cfg", &tgo::euler_cfg, "fused classifier-free-guidance Euler step from token-major velocities");
   m.def("set_attention_tc", &tgo::set_attention_tc, "use the tcgen05 attention forward (default) or mma.sync");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");
   m.def("launch_count", &tgo::launch_count, "kernels launched by this extension so far");

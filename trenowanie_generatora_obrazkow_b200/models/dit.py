@@ -160,7 +160,7 @@ class Denoiser(nn.Module):
             tok = tok.to(torch.bfloat16).contiguous()
         return Fz.linear(tok, self.patch_in)
 
-    def head(self, x, pending, shape):
+    def head(self, x, pending, shape, tokens_out=False):
         b, c, h, w = shape
         if x.is_cuda:
             y, g = pending if pending is not None else (None, None)
@@ -168,6 +168,8 @@ class Denoiser(nn.Module):
         else:
             hn = self.norm(_flush(x, pending))
         out = Fz.linear(hn, self.patch_out)
+        if tokens_out:
+            return out
         return out.transpose(1, 2).reshape(b, c, h, w)
 
     def run_blocks(self, x, pending, t6, text, text_len, cos, sin, lo=0, hi=None, hidden_at=0):
@@ -184,10 +186,12 @@ class Denoiser(nn.Module):
                 hidden = _flush(x, pending)
         return x, pending, hidden
 
-    def forward(self, z_t, t, text, text_valid=None, hidden_at=0, cond=None, text_len=None, rope=None):
+    def forward(self, z_t, t, text, text_valid=None, hidden_at=0, cond=None, text_len=None, rope=None,
+                tokens_out=False):
         """z_t (B, C, H, W); t (B,); text (B, L, text_dim); text_valid (B, L) bool or text_len (B,) int32.
         hidden_at > 0: also return the token states after that many blocks (REPA).
-        rope: optional (cos, sin) [B, T, d] per-sample tables (RPE-2D random positions)."""
+        rope: optional (cos, sin) [B, T, d] per-sample tables (RPE-2D random positions).
+        tokens_out: return the velocity token-major (B, H*W, C) as computed (the sampler's fused update reads it)."""
         b, c, h, w = z_t.shape
         if text_len is None:
             text_len = R.valid_to_len(text_valid) if text_valid is not None else None
@@ -199,7 +203,7 @@ class Denoiser(nn.Module):
         t6 = self.modulation(t, cond, 16 * h)
         cos, sin = rope if rope is not None else self.rope(h, w, z_t.device)
         x, pending, hidden = self.run_blocks(x, None, t6, text, text_len, cos, sin, hidden_at=hidden_at)
-        out = self.head(x, pending, z_t.shape)
+        out = self.head(x, pending, z_t.shape, tokens_out)
         return out if not hidden_at else (out, hidden)
 
     # ---------------------------------------------------------------------------------------------- init

@@ -1,0 +1,70 @@
+"""Frozen language-model backends that turn caption token ids into the hidden states the refiner consumes.
+
+The reference runs a frozen pretrained LM (SlayerLab/Slayer149 GPT or the Poziomka MoE through transformers,
+aurora/slayer.py:30-146, :238-432) on each caption batch, outside the trainable parameters. Backends here:
+
+* ``hf``     a transformers causal LM loaded from a local directory (``cfg.repo`` must be a path or a cached
+             model id; there is no network on the training boxes): first ``num_layers - skip_last`` layers, bf16,
+             the last hidden state.
+* ``random`` a fixed random embedding table of the LM's width (seeded): stands in for a pretrained LM in smoke
+             runs and tests where no weights exist. Rows of PAD / NULL ids get zeros.
+* ``states`` none: the caller passes states directly (the synthetic benchmarks).
+The LM is never registered as a submodule, so it stays out of state dicts, optimizers and gradient reduction.
+"""
+import torch
+
+LM_PAD, LM_NULL = 65535, 65534
+
+
+class RandomFrozenLM:
+    def __init__(self, lm_dim, vocab=65536, seed=0, device=None, dtype=torch.bfloat16):
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        self.table = torch.randn(vocab, lm_dim, generator=g).to(device=device, dtype=dtype)
+
+    def to(self, device):
+        self.table = self.table.to(device)
+        return self
+
+    @torch.no_grad()
+    def states(self, ids):
+        special = ids.eq(LM_PAD) | ids.eq(LM_NULL)
+        h = self.table[ids.clamp(max=self.table.shape[0] - 1).masked_fill(special, 0)]
+        return h.masked_fill(special[..., None], 0)
+
+
+class HFFrozenLM:
+    def __init__(self, repo, skip_last=0, device=None):
+        from transformers import AutoModelForCausalLM
+        model = AutoModelForCausalLM.from_pretrained(repo, torch_dtype=torch.bfloat16, trust_remote_code=True,
+                                                     local_files_only=True)
+        layers = model.model.layers
+        keep = len(layers) - skip_last
+        model.model.layers = layers[:keep]
+        self.model = model.model.to(device).eval().requires_grad_(False)
+
+    def to(self, device):
+        self.model.to(device)
+        return self
+
+    @torch.no_grad()
+    def states(self, ids):
+        real = ids.masked_fill(ids.eq(LM_PAD) | ids.eq(LM_NULL), 0)
+        return self.model(input_ids=real, use_cache=False).last_hidden_state
+
+
+def build_frozen_lm(cfg, device=None, allow_random=False):
+    backend = getattr(cfg, "backend", "states")
+    if backend == "states":
+        return None
+    if backend == "random" or allow_random:
+        try:
+            if backend == "hf":
+                return HFFrozenLM(cfg.repo, cfg.skip_last, device)
+        except Exception:
+            if not allow_random:
+                raise
+        return RandomFrozenLM(cfg.lm_dim, device=device)
+    if backend == "hf":
+        return HFFrozenLM(cfg.repo, cfg.skip_last, device)
+    raise RuntimeError(f"frozen LM backend {backend!r} needs pretrained weights that are not available offline; "
+                       "use --te-size 13m / 27m, synthetic states, or --random-lm for a smoke run")

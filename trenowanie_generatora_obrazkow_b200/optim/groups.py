@@ -87,7 +87,8 @@ class EMA:
 
     @torch.no_grad()
     def update(self, step, decay=None):
-        d = min(decay if decay is not None else self.decay, step / (9 + step))
+        """Per-step update with decay min(ema, step / (9 + step)), or with an explicit ``decay`` (DiLoCo syncs)."""
+        d = decay if decay is not None else min(self.decay, step / (9 + step))
         src = [p.detach().float() if p.device == s.device else p.detach().float().to(s.device, non_blocking=True)
                for p, s in zip(self.params, self.shadow)]
         torch._foreach_lerp_(self.shadow, src, 1 - d)

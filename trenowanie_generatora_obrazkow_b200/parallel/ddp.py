@@ -20,7 +20,8 @@ class GradBuckets:
     def __init__(self, params, bucket_bytes=256 * 2 ** 20, group=None, comm="nccl_bf16", overlap=True):
         self.params = [p for p in params if p.requires_grad]
         self.group = group
-        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        # comm "none": local gradients only (DiLoCo inner steps)
+        self.world = dist.get_world_size(group) if (dist.is_initialized() and comm != "none") else 1
         self.comm = comm
         self.overlap = overlap and self.world > 1
         dev = self.params[0].device

@@ -1,21 +1,27 @@
 """Flow-matching trainer: one optimizer step over a global batch (micro-batches, gradient accumulation, gradient
-reduction, clipping, LR schedule, Muon + AdamW, EMA).
+reduction, clipping, LR schedule, Muon + AdamW, EMA, DiLoCo outer syncs).
 
 Reference hot loop: train.py:906-966 (DDP) — per micro-batch logit-normal t, Gaussian noise, caption dropout to the
-null prompt, forward/backward of loss / accum; then clip_grad_norm_, LR multiplier, optimizer steps, EMA lerp.
-The public entry point is ``Trainer.step(batch)``; batch tensors may live in (pinned) host memory, in which case
-they are copied to the device inside the step.
+null prompt, MLM every mlm_every steps (from-scratch text encoder), forward/backward of loss / accum; then
+clip_grad_norm_, LR multiplier, optimizer steps, EMA lerp; DiLoCo: an outer sync every H steps instead of a
+per-step gradient all-reduce.
+The public entry point is ``Trainer.step(batch)``. A batch holds ``x0`` latents and either ``ids`` (caption token
+ids: a from-scratch text encoder, or a frozen-LM backend that turns them into states) or ``lm_states`` (optional
+``valid`` / ``is_null``). Tensors may live in (pinned) host memory; they are copied inside the step.
 """
 import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
 
 from ..models import build_models
+from ..models.frozen_lm import LM_NULL, LM_PAD, build_frozen_lm
+from ..models.text import LMTextEncoder
 from ..optim import EMA, build_optimizers, lr_mult, set_lr
 from ..parallel.ddp import GradBuckets
-from .flow import FlowModel, drop_captions
+from . import diloco as D
+from .flow import FlowModel, drop_captions, make_mlm
 
 
 @dataclass
@@ -44,51 +50,80 @@ class TrainConfig:
     ema_on_all_ranks: bool = False
     cfg_drop: float = 0.1
     t_shift: float = 1.0
+    mlm_weight: float = 0.05
+    mlm_every: int = 4
+    mlm_prob: float = 0.15
     grad_comm: str = "nccl_bf16"
     shard_muon: bool = True
+    diloco: int = 0
+    outer_lr: float = 0.7
+    outer_momentum: float = 0.9
+    outer_comm: str = "bf16"
+    offload: bool = False
     seed: int = 0
     act_checkpoint: bool = False
+    random_lm: bool = False
 
-    def derived(self):
+    def derived(self, world=1):
         ratio = self.global_batch / 256
-        lr_scale = 1.0 if self.no_lr_batch_scaling else math.sqrt(ratio)
+        lr_ratio = self.global_batch / world / 256 if self.diloco else ratio
+        lr_scale = 1.0 if self.no_lr_batch_scaling else math.sqrt(lr_ratio)
         ema = self.ema if self.ema is not None else 0.9995 ** ratio
         return lr_scale, ema
 
 
 class Trainer:
-    def __init__(self, den_cfg, te_cfg, cfg: TrainConfig, device, group=None):
+    def __init__(self, den_cfg, te_cfg, cfg: TrainConfig, device, group=None, models=None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.distributed = dist.is_available() and dist.is_initialized()
         self.rank = dist.get_rank(group) if self.distributed else 0
         self.world = dist.get_world_size(group) if self.distributed else 1
         self.group = group
-        assert cfg.global_batch % (cfg.micro_batch * self.world) == 0 or cfg.global_batch < cfg.micro_batch * self.world
-        self.per_rank = cfg.global_batch // self.world
+        self.den_cfg, self.te_cfg = den_cfg, te_cfg
+        self.per_rank = max(1, cfg.global_batch // self.world)
         self.micro = min(cfg.micro_batch, self.per_rank)
-        self.accum = self.per_rank // self.micro
+        self.accum = max(1, self.per_rank // self.micro)
         torch.manual_seed(cfg.seed)  # identical init on every rank
-        te, den = build_models(den_cfg, te_cfg, device=self.device)
-        self.te, self.den = te, den
+        te, den = models if models is not None else build_models(den_cfg, te_cfg, device=self.device)
+        self.te, self.den = te.to(self.device), den.to(self.device)
         self.den.checkpoint_blocks = cfg.act_checkpoint
-        self.model = FlowModel(te, den)
-        lr_scale, ema = self.cfg.derived()
-        named = [(pre, n, p) for pre, mod in (("te", te), ("den", den)) for n, p in mod.named_parameters()]
-        self.params = [p for _, _, p in named if p.requires_grad]
-        self.buckets = GradBuckets(self.params, group=group, comm=cfg.grad_comm) if self.device.type == "cuda" \
-            else None
+        self.lm_te = isinstance(te, LMTextEncoder)
+        if self.lm_te:
+            te.checkpoint_blocks = cfg.act_checkpoint
+        self.frozen_lm = build_frozen_lm(te_cfg, self.device, cfg.random_lm) if self.lm_te else None
+        mlm = 0.0 if self.lm_te else cfg.mlm_weight
+        self.model = FlowModel(te, den, mlm_weight=mlm)
+        lr_scale, ema = cfg.derived(self.world)
+        self.named = [(pre, n, p) for pre, mod in (("te", te), ("den", den)) for n, p in mod.named_parameters()]
+        self.params = [p for _, _, p in self.named if p.requires_grad]
+        reduce_grads = not cfg.diloco
+        self.buckets = None
+        if self.device.type == "cuda":
+            self.buckets = GradBuckets(self.params, group=group, comm=cfg.grad_comm if reduce_grads else "none")
         mdt = torch.bfloat16 if cfg.muon_momentum_dtype == "bf16" else None
         self.opts, self.counts = build_optimizers(
-            named, optimizer=cfg.optimizer, lr_muon=cfg.lr_muon, lr_emb=cfg.lr_emb, lr_adam=cfg.lr_adam,
+            self.named, optimizer=cfg.optimizer, lr_muon=cfg.lr_muon, lr_emb=cfg.lr_emb, lr_adam=cfg.lr_adam,
             lr_hidden=cfg.lr_hidden, lr_scale=lr_scale, wd=cfg.wd, beta2=cfg.beta2, momentum=cfg.momentum,
             ns_steps=cfg.ns_steps, cmuon=cfg.cmuon, muon_period=cfg.muon_period, muon_gamma=cfg.muon_gamma,
-            momentum_dtype=mdt, shard=cfg.shard_muon, group=group)
+            momentum_dtype=mdt, shard=cfg.shard_muon and not cfg.diloco, group=group)
+        self.ema_decay = ema
+        self.global_params = self.outer_opt = None
+        if cfg.diloco:
+            if self.distributed and self.world > 1:
+                for p in self.params:
+                    dist.broadcast(p.data, src=dist.get_global_rank(group, 0) if group is not None else 0,
+                                   group=group)
+            self.global_params = D.make_global(self.params, cfg.offload)
+            self.outer_opt = D.make_outer_opt(self.global_params, cfg.outer_lr, cfg.outer_momentum)
         self.ema = EMA(self.params, ema) if (self.rank == 0 or cfg.ema_on_all_ranks) else None
         self.step_idx = 0
         self.gen = torch.Generator(device=self.device)
         self.gen.manual_seed(cfg.seed * 1000 + self.rank)
         self.last_gnorm = None
+        self.last = {}
+        if not self.lm_te:
+            self.null_row = torch.as_tensor(te.null_ids(), device=self.device)
 
     def n_params(self):
         return sum(p.numel() for p in self.den.parameters()), sum(p.numel() for p in self.te.parameters())
@@ -98,39 +133,59 @@ class Trainer:
             return None
         return t.to(self.device, non_blocking=True) if t.device != self.device else t
 
+    def _text_inputs(self, batch, sl, b):
+        """Text-encoder keyword arguments for micro-batch slice sl, with caption dropout and MLM applied."""
+        cfg = self.cfg
+        if "ids" in batch and not self.lm_te:
+            ids = self._to_dev(batch["ids"][sl])
+            drop = torch.rand(b, device=self.device, generator=self.gen) < cfg.cfg_drop
+            cond_ids = torch.where(drop[:, None], self.null_row[: ids.shape[1]], ids)
+            kw = dict(ids=cond_ids)
+            if self.model.mlm_weight > 0 and self.step_idx % cfg.mlm_every == 0:
+                kw["mlm_ids"], kw["mlm_labels"] = make_mlm(ids, cfg.mlm_prob, self.gen)
+            return kw
+        if "ids" in batch:
+            ids = self._to_dev(batch["ids"][sl])
+            valid = ids.ne(LM_PAD)
+            is_null = ids[:, 0].eq(LM_NULL)
+            states = self.frozen_lm.states(ids)
+        else:
+            states = self._to_dev(batch["lm_states"][sl])
+            valid = self._to_dev(batch["valid"][sl]) if batch.get("valid") is not None else \
+                torch.ones(b, states.shape[1], dtype=torch.bool, device=self.device)
+            is_null = self._to_dev(batch["is_null"][sl]) if batch.get("is_null") is not None else None
+        if cfg.cfg_drop > 0:
+            is_null, valid = drop_captions(is_null, valid, cfg.cfg_drop, self.gen)
+        return dict(lm_states=states, valid=valid, is_null=is_null)
+
     def step(self, batch):
-        """batch: dict with x0 (B, C, H, W) latents, lm_states (B, L, lm_dim), optional valid (B, L) bool and
-        is_null (B,) bool; B = global_batch / world. Returns the mean flow-matching loss (device scalar)."""
+        """One optimizer step over this rank's share of the global batch. Returns the mean flow-matching loss
+        (device scalar); ``self.last`` holds the MLM loss and the gradient norm."""
         cfg = self.cfg
         x0_all = self._to_dev(batch["x0"])
-        st_all = self._to_dev(batch["lm_states"])
-        valid_all = self._to_dev(batch.get("valid"))
-        null_all = self._to_dev(batch.get("is_null"))
         if self.buckets is not None:
             self.buckets.zero()
         else:
             for p in self.params:
                 p.grad = None
         acc = torch.zeros((), device=self.device)
+        acc_mlm = torch.zeros((), device=self.device)
         for m in range(self.accum):
             sl = slice(m * self.micro, (m + 1) * self.micro)
             x0 = x0_all[sl].float()
             b = x0.shape[0]
-            states = st_all[sl]
-            valid = valid_all[sl] if valid_all is not None else torch.ones(b, states.shape[1], dtype=torch.bool,
-                                                                         device=self.device)
-            is_null = null_all[sl] if null_all is not None else None
-            if cfg.cfg_drop > 0:
-                is_null, valid = drop_captions(is_null, valid, cfg.cfg_drop, self.gen)
+            kw = self._text_inputs(batch, sl, b)
             t = torch.sigmoid(torch.randn(b, device=self.device, generator=self.gen))
             if cfg.t_shift != 1.0:
                 t = cfg.t_shift * t / (1 + (cfg.t_shift - 1) * t)
             eps = torch.randn(x0.shape, device=self.device, generator=self.gen)
             if self.buckets is not None and m == self.accum - 1:
                 self.buckets.arm()
-            loss, l_fm, _, _ = self.model(x0, t, eps, lm_states=states, valid=valid, is_null=is_null)
+            loss, l_fm, l_mlm, _ = self.model(x0, t, eps, **kw)
             (loss / self.accum).backward()
             acc += l_fm / self.accum
+            if l_mlm is not None:
+                acc_mlm += l_mlm / self.accum
         if self.buckets is not None:
             self.buckets.finish()
         self.last_gnorm = torch.nn.utils.clip_grad_norm_(self.params, cfg.clip, foreach=True)
@@ -138,6 +193,14 @@ class Trainer:
         for o in self.opts:
             o.step()
         self.step_idx += 1
-        if self.ema is not None:
+        if cfg.diloco:
+            if self.step_idx % cfg.diloco == 0 or self.step_idx == cfg.steps:
+                D.outer_sync(self.global_params, self.params, self.outer_opt, self.world, cfg.outer_comm,
+                             self.group)
+                if self.ema is not None:
+                    n = self.step_idx // cfg.diloco
+                    self.ema.update(self.step_idx, D.ema_decay_at_sync(self.ema_decay, cfg.diloco, n))
+        elif self.ema is not None:
             self.ema.update(self.step_idx)
+        self.last = dict(mlm=acc_mlm, gnorm=self.last_gnorm)
         return acc
