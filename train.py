@@ -1,0 +1,328 @@
+"""Flow-matching DiT training (DDP or DiLoCo), the single-model trainer of this framework.
+
+  # 8 GPUs, data prepared in the shard format (data/shards.py), from-scratch text encoder with MLM
+  torchrun --nproc_per_node 8 train.py --data data/aurora --out runs/aurora --size 253m --te-size 27m
+  # no data at hand: synthetic latents / captions of the same shapes
+  python train.py --synthetic 4096 --out runs/smoke --size 50m --te-size 13m --steps 20
+  # DiLoCo / MuLoCo: every GPU trains its own copy, outer sync every 16 steps
+  torchrun --nproc_per_node 8 train.py --data ... --out ... --diloco 16
+
+Flag names follow the reference's train.py (train.py:42-184); derived defaults (LR batch scaling, steps, EMA
+decay, cadences, refiner width, REPA layer) follow its resolve_defaults (train.py:549-586). Checkpoints are
+written in the reference's layout (latest.pt, snap_<step>.pt, merge/step_<step>.pt) and resume from either
+framework's files.
+"""
+import argparse
+import json
+import math
+import os
+import time
+from dataclasses import asdict, replace
+
+import torch
+import torch.distributed as dist
+
+from trenowanie_generatora_obrazkow_b200.data.shards import (ShardStore, TrainStream, load_val, select_shards,
+                                                             val_groups)
+from trenowanie_generatora_obrazkow_b200.models import (SIZES, TE_SIZES, DenoiserConfig, LMEncoderConfig,
+                                                        make_configs, te_config_from_dict)
+from trenowanie_generatora_obrazkow_b200.train.evaluate import evaluate, weight_sq, wrms_stats
+from trenowanie_generatora_obrazkow_b200.train.trainer import TrainConfig, Trainer
+from trenowanie_generatora_obrazkow_b200.utils import checkpoint as ckpt
+from trenowanie_generatora_obrazkow_b200.utils.logging import RunLogger
+from trenowanie_generatora_obrazkow_b200.utils.flops import PEAK_TFLOPS, peak_tflops, train_flops_per_sample
+
+
+def build_parser():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    a = p.add_argument
+    a("--data", default="data/aurora")
+    a("--synthetic", type=int, default=0, help="train on N synthetic samples (no data directory needed)")
+    a("--out", required=True)
+    a("--size", choices=sorted(SIZES), default="253m")
+    a("--depth", type=int, default=None)
+    a("--res", type=int, default=256, help="image resolution in px (latent side = res / 16)")
+    a("--te-size", choices=sorted(TE_SIZES), default="27m")
+    a("--te-dim", type=int, default=None)
+    a("--te-depth", type=int, default=None)
+    a("--te-experts", type=int, default=None)
+    a("--te-quant", choices=["", "int8"], default=None)
+    a("--random-lm", action="store_true", help="frozen-LM encoders: a fixed random embedding stands in for the LM")
+    a("--ema-cpu", action="store_true")
+    a("--pl-prob", type=float, default=0.0)
+    a("--repa-weight", type=float, default=0.0)
+    a("--repa-layer", type=int, default=None)
+    a("--optimizer", choices=["muon", "adamw"], default="muon")
+    a("--lr-hidden", type=float, default=None)
+    a("--beta2", type=float, default=None)
+    a("--steps", type=int, default=None)
+    a("--batch", type=int, default=2048)
+    a("--fraction", type=float, default=0.1)
+    a("--micro-batch", type=int, default=64)
+    a("--warmup-frac", type=float, default=0.02)
+    a("--lr-muon", type=float, default=1e-2)
+    a("--lr-emb", type=float, default=5e-4)
+    a("--lr-adam", type=float, default=3e-4)
+    a("--no-lr-batch-scaling", action="store_true")
+    a("--wd", type=float, default=None)
+    a("--schedule", choices=["constant", "cosine"], default="constant")
+    a("--momentum", type=float, default=0.95)
+    a("--ns-steps", type=int, default=5)
+    a("--cmuon", action="store_true")
+    a("--muon-period", type=int, default=1)
+    a("--muon-gamma", type=float, default=0.15)
+    a("--clip", type=float, default=1.0)
+    a("--ema", type=float, default=None)
+    a("--cfg-drop", type=float, default=0.1)
+    a("--t-shift", type=float, default=1.0)
+    a("--mlm-weight", type=float, default=0.05)
+    a("--mlm-every", type=int, default=4)
+    a("--mlm-prob", type=float, default=0.15)
+    a("--grad-comm", choices=["fp32", "bf16"], default="bf16")
+    a("--diloco", type=int, default=0)
+    a("--outer-lr", type=float, default=0.7)
+    a("--outer-momentum", type=float, default=0.9)
+    a("--offload", action="store_true")
+    a("--outer-comm", choices=["bf16", "fp32"], default="bf16")
+    a("--muon-momentum-dtype", choices=["fp32", "bf16"], default="fp32")
+    a("--act-checkpoint", action="store_true")
+    a("--workers", type=int, default=4)
+    a("--seed", type=int, default=0)
+    a("--log-every", type=int, default=None)
+    a("--eval-every", type=int, default=None)
+    a("--ckpt-every", type=int, default=None)
+    a("--merge-every", type=int, default=None)
+    a("--merge-start", type=float, default=0.8)
+    a("--keep-every", type=int, default=None)
+    a("--val-samples", type=int, default=4096)
+    a("--peak-tflops", type=float, default=0)
+    a("--wandb", default="trenowanie_generatora_obrazkow")
+    a("--no-wandb", action="store_true")
+    a("--eval-only", action="store_true")
+    a("--init", default="", help="start from this checkpoint's EMA weights (ignored on resume)")
+    a("--freeze-den", action="store_true")
+    return p
+
+
+def resolve_defaults(args, world=1):
+    ratio = args.batch / 256
+    if args.steps is None:
+        args.steps = max(1, round(247_805 * args.fraction / ratio))
+    lr_ratio = args.batch / world / 256 if args.diloco else ratio
+    args.lr_scale = 1.0 if args.no_lr_batch_scaling else math.sqrt(lr_ratio)
+    if args.ema is None:
+        args.ema = 0.9995 ** ratio
+    args.log_every = args.log_every or min(100, max(1, args.steps // 40))
+    args.eval_every = max(1, args.steps // 20) if args.eval_every is None else args.eval_every
+    args.ckpt_every = max(1, args.steps // 50) if args.ckpt_every is None else args.ckpt_every
+    args.merge_every = max(1, args.steps // 25) if args.merge_every is None else args.merge_every
+    args.keep_every = max(1, args.steps // 10) if args.keep_every is None else args.keep_every
+    if args.wd is None:
+        args.wd = 0.1 if args.optimizer == "adamw" else 0.01
+    if args.lr_hidden is None:
+        args.lr_hidden = 1e-4 * 768 / SIZES[args.size].dim
+    lm = isinstance(TE_SIZES[args.te_size], LMEncoderConfig)
+    if lm and args.te_dim is None and TE_SIZES[args.te_size].backend != "states":
+        args.te_dim = SIZES[args.size].dim // 2
+    if lm:
+        args.mlm_weight = 0.0
+    if args.repa_layer is None:
+        args.repa_layer = max(1, round(0.3 * (args.depth or SIZES[args.size].depth)))
+    if args.diloco:
+        up = lambda n: n and -(-n // args.diloco) * args.diloco
+        args.eval_every, args.ckpt_every = up(args.eval_every), up(args.ckpt_every)
+        args.merge_every, args.keep_every = up(args.merge_every), up(args.keep_every)
+    return args
+
+
+class SyntheticStream:
+    """Random latents + caption rows of the configured shapes (no data directory)."""
+
+    def __init__(self, n, side, te_cfg, micro, rank, seed):
+        self.n, self.side, self.te_cfg, self.micro = n, side, te_cfg, micro
+        self.g = torch.Generator().manual_seed(seed * 1000 + rank)
+
+    def __iter__(self):
+        L = self.te_cfg.max_tokens
+        lm = isinstance(self.te_cfg, LMEncoderConfig)
+        while True:
+            lat = torch.randn(self.micro, 128, self.side, self.side, generator=self.g).half()
+            if lm and self.te_cfg.backend == "states":
+                yield lat, torch.randn(self.micro, L, self.te_cfg.lm_dim, generator=self.g).bfloat16()
+                continue
+            ids = torch.randint(6, 8000 if not lm else 60000, (self.micro, L), generator=self.g)
+            n = torch.randint(3, L, (self.micro,), generator=self.g)
+            pad = 65535 if lm else 0
+            ids[torch.arange(L)[None] >= n[:, None]] = pad
+            yield lat, ids
+
+
+def main():
+    distributed = "RANK" in os.environ
+    if distributed:
+        backend = os.environ.get("DIST_BACKEND", "nccl")
+        local = int(os.environ.get("LOCAL_RANK", 0))
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local % torch.cuda.device_count())
+        dist.init_process_group(backend)
+        rank, world = dist.get_rank(), dist.get_world_size()
+    else:
+        rank, world, local = 0, 1, 0
+    args = resolve_defaults(build_parser().parse_args(), world)
+    device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+    master = rank == 0
+    os.makedirs(args.out, exist_ok=True)
+    log = print if master else (lambda *a, **k: None)
+
+    den_cfg, te_cfg = make_configs(args.size, args.te_size, args.te_dim, args.te_depth, args.depth,
+                                   args.te_experts, args.te_quant)
+    den_cfg = replace(den_cfg, latent_size=args.res // 16)
+    ckpt_path = os.path.join(args.out, "latest.pt")
+    resume = ckpt.load(ckpt_path) if os.path.exists(ckpt_path) else None
+    if resume is not None:  # the checkpoint's architecture wins
+        den_cfg = DenoiserConfig(**resume["den_config"])
+        te_cfg = te_config_from_dict(resume["te_config"])
+    tc = TrainConfig(global_batch=args.batch, micro_batch=args.micro_batch, steps=args.steps,
+                     warmup=int(args.warmup_frac * args.steps), schedule=args.schedule, optimizer=args.optimizer,
+                     lr_muon=args.lr_muon, lr_emb=args.lr_emb, lr_adam=args.lr_adam, lr_hidden=args.lr_hidden,
+                     no_lr_batch_scaling=args.no_lr_batch_scaling, wd=args.wd, beta2=args.beta2,
+                     momentum=args.momentum, ns_steps=args.ns_steps, cmuon=args.cmuon, muon_period=args.muon_period,
+                     muon_gamma=args.muon_gamma, muon_momentum_dtype=args.muon_momentum_dtype, clip=args.clip,
+                     ema=args.ema, cfg_drop=args.cfg_drop, t_shift=args.t_shift, mlm_weight=args.mlm_weight,
+                     mlm_every=args.mlm_every, mlm_prob=args.mlm_prob,
+                     grad_comm="nccl_fp32" if args.grad_comm == "fp32" else "nccl_bf16", diloco=args.diloco,
+                     outer_lr=args.outer_lr, outer_momentum=args.outer_momentum, outer_comm=args.outer_comm,
+                     offload=args.offload, seed=args.seed, act_checkpoint=args.act_checkpoint,
+                     random_lm=args.random_lm)
+    tr = Trainer(den_cfg, te_cfg, tc, device)
+    te, den = tr.te, tr.den
+    if args.freeze_den:
+        den.requires_grad_(False)
+    step, samples = 0, 0
+    if resume is not None:
+        ckpt.load_weights(resume, te, den)
+        if resume.get("opts"):
+            for o, s in zip(tr.opts, resume["opts"]):
+                ckpt.load_opt_state(o, s)
+        if tr.ema is not None and resume.get("ema"):
+            for s, e in zip(tr.ema.shadow, resume["ema"]):
+                s.copy_(e.to(s.device))
+        if tr.outer_opt is not None and resume.get("outer"):
+            ckpt.load_opt_state(tr.outer_opt, resume["outer"])
+        step, samples = int(resume["step"]), int(resume.get("samples", 0))
+        tr.step_idx = step
+        log(f"resumed from {ckpt_path} at step {step}")
+    elif args.init:
+        init = ckpt.load(args.init)
+        ckpt.load_weights(init, te, den, use_ema=bool(init.get("ema")))
+        log(f"init: weights from {args.init} (step {init.get('step')})")
+    del resume
+    n_den, n_te = tr.n_params()
+    log(f"params: denoiser {n_den / 1e6:.1f}M, text encoder {n_te / 1e6:.1f}M (trainable)")
+
+    # ---- data --------------------------------------------------------------------------------------------
+    side = args.res // 16
+    val = None
+    groups = ()
+    if args.synthetic:
+        stream = SyntheticStream(args.synthetic, side, te_cfg, tr.micro, rank, args.seed)
+        loader = iter(stream)
+        if master:
+            vs = SyntheticStream(args.synthetic, side, te_cfg, min(args.val_samples, 64), 10 ** 6, args.seed + 1)
+            val = next(iter(vs))
+    else:
+        tok_suffix = getattr(te_cfg, "tok_suffix", "")
+        null_row = te.null_ids()
+        train_names, val_names = select_shards(args.data, args.fraction, tok_suffix)
+        store = ShardStore(args.data, train_names, tok_suffix, null_row,
+                           lat_kind="lat" if side == 16 else f"lat{args.res}")
+        stream = TrainStream(store, tr.micro, rank, world, args.seed, start_micro=samples // (tr.micro * world))
+        loader = iter(torch.utils.data.DataLoader(stream, batch_size=None, num_workers=args.workers,
+                                                  pin_memory=device.type == "cuda",
+                                                  persistent_workers=args.workers > 0))
+        if master and val_names:
+            val = load_val(args.data, val_names, args.val_samples, tok_suffix, null_row)
+            groups = val_groups(args.data, val_names, args.val_samples)
+        log(f"train: {len(train_names)} shards / {len(store):,} images, val: {len(val_names)} shards")
+    lm_states_key = isinstance(te_cfg, LMEncoderConfig) and te_cfg.backend == "states"
+
+    logger = RunLogger(args.out, vars(args), enabled=master and not args.no_wandb, project=args.wandb)
+    peak = args.peak_tflops or (peak_tflops(torch.cuda.get_device_name(device)) if device.type == "cuda" else 0)
+    flops_sample = train_flops_per_sample(den_cfg, te_cfg, side * side)
+
+    def save():
+        if not master:
+            return
+        ckpt.save_latest(ckpt_path, step, samples, den_cfg, te_cfg, te, den, tr.opts, tr.ema, vars(args),
+                         outer=tr.outer_opt.state_dict() if tr.outer_opt is not None else None)
+        if args.keep_every and step % args.keep_every == 0:
+            ckpt.save_snapshot(args.out, step, den_cfg, te_cfg, te, den, tr.ema)
+
+    def run_eval():
+        if val is None:
+            return {}
+        swap = [p.detach().clone() for p in tr.params] if tr.ema is not None else None
+        if swap is not None:
+            tr.ema.copy_to()
+        res = evaluate(te, den, val, device, groups=groups)
+        if swap is not None:
+            with torch.no_grad():
+                for p, s in zip(tr.params, swap):
+                    p.copy_(s)
+        return res
+
+    if args.eval_only:
+        log(json.dumps(run_eval(), indent=1))
+        if distributed:
+            dist.destroy_process_group()
+        return
+
+    t0, acc, nacc = time.time(), 0.0, 0
+    while step < args.steps:
+        micros = [next(loader) for _ in range(tr.accum)]
+        x0 = torch.cat([m[0] for m in micros])
+        second = torch.cat([m[1] for m in micros])
+        batch = {"x0": x0, ("lm_states" if lm_states_key else "ids"): second}
+        loss = tr.step(batch)
+        step += 1
+        samples += args.batch
+        acc += loss.detach()
+        nacc += 1
+        if step % args.log_every == 0 or step == args.steps:
+            l = acc.clone()
+            if distributed:
+                dist.all_reduce(l)
+                l /= world
+            torch.cuda.synchronize() if device.type == "cuda" else None
+            dt = time.time() - t0
+            img_s = nacc * args.batch / dt
+            tflops = img_s * flops_sample / world / 1e12
+            stats = {"train/loss": (l / nacc).item(), "train/grad_norm": float(tr.last_gnorm), "train/img_s": img_s,
+                     "train/tflops_per_gpu": tflops, "train/samples": samples}
+            if peak:
+                stats["train/mfu"] = tflops / peak
+            if float(tr.last.get("mlm", 0)) > 0:
+                stats["train/mlm"] = float(tr.last["mlm"])
+            stats.update(wrms_stats(weight_sq(tr.named, device)))
+            log(f"step {step}/{args.steps} loss {stats['train/loss']:.4f} gnorm {stats['train/grad_norm']:.3f} "
+                f"{img_s:.1f} img/s {tflops:.1f} TFLOPS/GPU" + (f" MFU {100 * stats['train/mfu']:.1f}%" if peak else ""))
+            logger.log(stats, step)
+            t0, acc, nacc = time.time(), 0.0, 0
+        if args.eval_every and (step % args.eval_every == 0 or step == args.steps) and master:
+            res = run_eval()
+            if res:
+                log(" ".join(f"{k} {v:.4f}" for k, v in res.items()))
+                logger.log(res, step)
+        if args.merge_every and step >= args.merge_start * args.steps and step % args.merge_every == 0 and master:
+            ckpt.save_merge(args.out, step, args.steps, den_cfg, te_cfg, te, den)
+        if step % args.ckpt_every == 0 or step == args.steps:
+            save()
+            if distributed:
+                dist.barrier()
+    logger.close()
+    if distributed:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
