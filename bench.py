@@ -47,6 +47,8 @@ def parse():
     p.add_argument("--res", type=int, default=512)
     p.add_argument("--text-len", type=int, default=128)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--grad-comm", default="p2p", choices=["p2p", "nccl_bf16", "nccl_fp32"],
+                   help="gradient reduction: the fused peer-memory kernel (p2p) or NCCL")
     p.add_argument("--sample-batch", type=int, default=8, help="prompts per GPU for the sampling measurement "
                    "(1024 px, 50 Euler steps, CFG 3, shift 6); 0 = skip it")
     p.add_argument("--sample-res", type=int, default=1024)
@@ -188,7 +190,8 @@ def run_ours(args):
     den_cfg, te_cfg = benchmark_configs(args.config)
     from dataclasses import replace
     den_cfg = replace(den_cfg, latent_size=args.res // 16)
-    cfg = TrainConfig(global_batch=args.global_batch, micro_batch=args.micro_batch, steps=10 ** 6)
+    cfg = TrainConfig(global_batch=args.global_batch, micro_batch=args.micro_batch, steps=10 ** 6,
+                      grad_comm=args.grad_comm)
     tr = Trainer(den_cfg, te_cfg, cfg, device)
     per_rank = args.global_batch // world
     host, devb = synthetic_batch(per_rank, args.res, args.text_len, te_cfg.lm_dim, device, 1234 + rank)
@@ -221,7 +224,8 @@ def run_ours(args):
                       "params_denoiser": tr.n_params()[0], "params_text": tr.n_params()[1],
                       "global_batch": args.global_batch, "micro_batch": tr.micro, "seq_len": (args.res // 16) ** 2,
                       "text_len": args.text_len, "res": args.res, "parallelism": f"dp{world}",
-                      "optimizer": "muon(sharded)+adamw", "l2": "inputs larger than L2 (no flush needed)"},
+                      "optimizer": "muon(sharded)+adamw", "grad_comm": args.grad_comm,
+                      "l2": "inputs larger than L2 (no flush needed)"},
            "clocks": clocks, "gpu_launches": int(launches), "impl": "ours"}
     if not args.no_e2e:
         loss_host = []

@@ -1,0 +1,59 @@
+"""Tooling on CPU: WSM / QAM coefficients, merge.py, sample_ckpt.py with export, checkpoint helpers."""
+import glob
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+from trenowanie_generatora_obrazkow_b200.optim.merge import merge_coefficients
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_wsm_mean_is_uniform_and_qam_sums_to_one():
+    assert merge_coefficients("mean", 5, "wsm") == pytest.approx([0.2] * 5)
+    for scheme in ("mean", "1-sqrt", "cosine"):
+        for method in ("wsm", "qam"):
+            c = merge_coefficients(scheme, 6, method)
+            assert sum(c) == pytest.approx(1.0) and min(c) >= -1e-9
+    assert merge_coefficients("cosine", 1) == [1.0]
+
+
+def test_qam_matches_polynomial_product():
+    w = [0.9, 0.5, 0.2]
+    import numpy as np
+    poly = np.array([1.0])
+    for wj in w:
+        poly = np.convolve(poly, [1 - wj, wj])
+    from trenowanie_generatora_obrazkow_b200.optim import merge as M
+    old = M.decay_profile
+    M.decay_profile = lambda scheme, k: w
+    try:
+        assert M.merge_coefficients("mean", 4, "qam") == pytest.approx(list(poly))
+    finally:
+        M.decay_profile = old
+
+
+def _py(script, *args):
+    r = subprocess.run([sys.executable, os.path.join(ROOT, script), *args], cwd=ROOT, capture_output=True, text=True,
+                       timeout=600, env=dict(os.environ, CUDA_VISIBLE_DEVICES=""))
+    assert r.returncode == 0, r.stderr[-3000:]
+    return r.stdout
+
+
+def test_train_merge_sample_export_chain(tmp_path):
+    run = str(tmp_path / "run")
+    _py("train.py", "--synthetic", "64", "--out", run, "--size", "50m", "--te-size", "13m", "--batch", "2",
+        "--micro-batch", "2", "--steps", "5", "--eval-every", "0", "--merge-every", "1", "--merge-start", "0.2",
+        "--no-wandb")
+    assert len(glob.glob(os.path.join(run, "merge", "step_*.pt"))) >= 3
+    out = _py("merge.py", run, "--synthetic-val", "16", "--windows", "0.6", "--schemes", "mean")
+    assert "best:" in out and os.path.exists(os.path.join(run, "merged.pt"))
+    so = str(tmp_path / "samples")
+    _py("sample_ckpt.py", os.path.join(run, "merged.pt"), "--out-dir", so, "--steps", "2", "--prompt", "a cat",
+        "--export")
+    assert os.path.exists(os.path.join(so, "transformer", "diffusion_pytorch_model.safetensors"))
+    # the export reloads through the directory path
+    _py("sample_ckpt.py", so, "--out-dir", str(tmp_path / "s2"), "--steps", "1", "--prompt", "x")

@@ -128,4 +128,20 @@ cudaError_t attention_fwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk
 cudaError_t euler_cfg_launch(const __nv_bfloat16* out, float* z, int B, int T, int C, float dt, float w,
                              cudaStream_t s);
 
+// ---------------------------------------------------------------- peer-memory collectives (comm.cu)
+constexpr int kMaxPeers = 8;
+struct PeerAllReduceParams {
+  float* grads;                        // local fp32 gradients [n], averaged in place
+  long long n, slice;                  // slice = per-rank share (multiple of 8); buffers hold world * slice
+  int rank, world;
+  __nv_bfloat16* staging[kMaxPeers];   // every rank's bf16 staging buffer (peer addresses from CUDA IPC)
+  __nv_bfloat16* result[kMaxPeers];    // every rank's bf16 result buffer
+  uint32_t* flags[kMaxPeers];          // every rank's flag array: C (phase 0) + world * C (phase 1) words
+  uint32_t epoch;
+  float scale;
+  unsigned long long timeout_ns;
+  int* err;
+};
+cudaError_t allreduce_bf16_launch(const PeerAllReduceParams& p, int blocks, cudaStream_t s);
+
 }  // namespace tgo

@@ -464,6 +464,66 @@ void euler_cfg(at::Tensor out, at::Tensor z, double dt, double w) {
                                     at::cuda::getCurrentCUDAStream()));
 }
 
+// ------------------------------------------------------------------------------------------------ peer memory
+// Device buffers shared between the ranks of one node: allocated with cudaMalloc (zeroed), exported as a CUDA IPC
+// handle, opened by the peers.  Pointers travel as integers.
+static void cuda_ok(cudaError_t e, const char* what) { TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e)); }
+
+std::tuple<int64_t, py::bytes> symm_alloc(int64_t nbytes, int64_t device) {
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  void* p = nullptr;
+  cuda_ok(cudaMalloc(&p, (size_t)nbytes), "cudaMalloc (peer buffer)");
+  cuda_ok(cudaMemset(p, 0, (size_t)nbytes), "cudaMemset (peer buffer)");
+  cudaIpcMemHandle_t h;
+  cuda_ok(cudaIpcGetMemHandle(&h, p), "cudaIpcGetMemHandle");
+  return {reinterpret_cast<int64_t>(p), py::bytes(reinterpret_cast<const char*>(&h), sizeof(h))};
+}
+void symm_free(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  cuda_ok(cudaFree(reinterpret_cast<void*>(ptr)), "cudaFree (peer buffer)");
+}
+int64_t ipc_open(py::bytes handle, int64_t device) {
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  std::string hs = handle;
+  TORCH_CHECK(hs.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, hs.data(), sizeof(h));
+  void* p = nullptr;
+  cuda_ok(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return reinterpret_cast<int64_t>(p);
+}
+void ipc_close(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  cuda_ok(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)), "cudaIpcCloseMemHandle");
+}
+
+// In-place bf16-transport average of fp32 grads [n] over `world` ranks through peer buffers.
+void allreduce_bf16(at::Tensor grads, std::vector<int64_t> staging, std::vector<int64_t> result,
+                    std::vector<int64_t> flags, int64_t rank, int64_t world, int64_t slice, int64_t epoch, double scale,
+                    int64_t blocks, int64_t timeout_ns, at::Tensor err) {
+  TORCH_CHECK(grads.is_cuda() && grads.scalar_type() == at::kFloat && grads.is_contiguous(), "grads: fp32 CUDA");
+  TORCH_CHECK(world >= 1 && world <= kMaxPeers && (int64_t)staging.size() == world &&
+              (int64_t)result.size() == world && (int64_t)flags.size() == world, "allreduce: peer lists");
+  TORCH_CHECK(slice % 8 == 0 && slice * world >= grads.numel(), "allreduce: slice");
+  const c10::cuda::CUDAGuard guard(grads.device());
+  PeerAllReduceParams p{};
+  p.grads = grads.data_ptr<float>();
+  p.n = grads.numel();
+  p.slice = slice;
+  p.rank = (int)rank;
+  p.world = (int)world;
+  for (int i = 0; i < world; ++i) {
+    p.staging[i] = reinterpret_cast<__nv_bfloat16*>(staging[i]);
+    p.result[i] = reinterpret_cast<__nv_bfloat16*>(result[i]);
+    p.flags[i] = reinterpret_cast<uint32_t*>(flags[i]);
+  }
+  p.epoch = (uint32_t)epoch;
+  p.scale = (float)scale;
+  p.timeout_ns = (unsigned long long)timeout_ns;
+  p.err = err_ptr(err);
+  TGO_CHECK_LAUNCH(allreduce_bf16_launch(p, (int)blocks, at::cuda::getCurrentCUDAStream()));
+}
+
 }  // namespace tgo
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -472,6 +532,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("C"), py::arg("a_mn"), py::arg("b_mn"), py::arg("D") = c10::nullopt, py::arg("alpha") = 1.0,
         py::arg("beta") = 0.0, py::arg("accumulate") = false, py::arg("err"));
   m.def("euler_cfg", &tgo::euler_cfg, "fused classifier-free-guidance Euler step from token-major velocities");
+  m.def("symm_alloc", &tgo::symm_alloc, "zeroed device buffer + its CUDA IPC handle");
+  m.def("symm_free", &tgo::symm_free);
+  m.def("ipc_open", &tgo::ipc_open, "map a peer's buffer from its IPC handle");
+  m.def("ipc_close", &tgo::ipc_close);
+  m.def("allreduce_bf16", &tgo::allreduce_bf16, "fused cast + reduce-scatter + all-gather over peer memory");
   m.def("set_attention_tc", &tgo::set_attention_tc, "use the tcgen05 attention forward (default) or mma.sync");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");
   m.def("launch_count", &tgo::launch_count, "kernels launched by this extension so far");

@@ -7,8 +7,9 @@ Here every trainable parameter's ``.grad`` is a view into one of a few flat fp32
 (the fused Linear backward accumulates weight gradients into them directly). Buckets are ordered by reverse
 registration order, i.e. roughly the order backward produces them, and each bucket is reduced as soon as its last
 gradient has been accumulated on the last micro-batch, on a side stream, so the reduction overlaps the rest of the
-backward pass. The transport is pluggable: ``nccl_bf16`` (cast + NCCL all_reduce + scale, the reference's hook) or
-the fused peer-memory kernel of parallel/comm.py.
+backward pass. The transport is pluggable: ``nccl_bf16`` (cast + NCCL all_reduce + scale, the reference's hook),
+``nccl_fp32``, or ``p2p``: the fused peer-memory kernel of parallel/comm.py (one launch per bucket does the bf16
+cast, the reduce-scatter over NVLink loads, the scaled all-gather over NVLink stores and the cast back).
 """
 import torch
 import torch.distributed as dist
@@ -36,6 +37,10 @@ class GradBuckets:
                 cur, size = [], 0
         if cur:
             self.buckets.append(cur)
+        self.p2p = None
+        if comm == "p2p" and self.world > 1:
+            from .comm import PeerAllReduce
+            self.p2p = PeerAllReduce(max(sum(p.numel() for p in ps) for ps in self.buckets), group=group, device=dev)
         self.flat = []
         self.bucket_of = {}
         for bi, ps in enumerate(self.buckets):
@@ -58,6 +63,9 @@ class GradBuckets:
                 self._handles.append(p.register_post_accumulate_grad_hook(self._on_ready))
 
     def close(self):
+        if self.p2p is not None:
+            self.p2p.close()
+            self.p2p = None
         Fz.remove_grad_ready_hook(self._on_ready)
         for h in self._handles:
             h.remove()
@@ -107,7 +115,9 @@ class GradBuckets:
     def _reduce(self, buf):
         if self.world == 1:
             return
-        if self.comm == "nccl_fp32":
+        if self.p2p is not None:  # fused cast + reduce-scatter + all-gather over NVLink peer memory
+            self.p2p(buf)
+        elif self.comm == "nccl_fp32":
             dist.all_reduce(buf, group=self.group)
             buf.div_(self.world)
         else:
