@@ -47,6 +47,12 @@ def parse():
     p.add_argument("--res", type=int, default=512)
     p.add_argument("--text-len", type=int, default=128)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--moe", action="store_true", help="BASELINE config 4: every other MLP -> 8 experts, top-2, "
+                   "expert hidden 4096, expert-parallel over the GPUs")
+    p.add_argument("--pp", type=int, default=1, help="pipeline stages (BASELINE config 3: --pp 4 on 8 GPUs, "
+                   "--res 1024 --microbatches 8 --pp-micro 4)")
+    p.add_argument("--microbatches", type=int, default=8)
+    p.add_argument("--pp-micro", type=int, default=4)
     p.add_argument("--grad-comm", default="p2p", choices=["p2p", "nccl_bf16", "nccl_fp32"],
                    help="gradient reduction: the fused peer-memory kernel (p2p) or NCCL")
     p.add_argument("--sample-batch", type=int, default=8, help="prompts per GPU for the sampling measurement "
@@ -191,7 +197,7 @@ def run_ours(args):
     from dataclasses import replace
     den_cfg = replace(den_cfg, latent_size=args.res // 16)
     cfg = TrainConfig(global_batch=args.global_batch, micro_batch=args.micro_batch, steps=10 ** 6,
-                      grad_comm=args.grad_comm)
+                      grad_comm=args.grad_comm, moe_experts=8 if args.moe else 0)
     tr = Trainer(den_cfg, te_cfg, cfg, device)
     per_rank = args.global_batch // world
     host, devb = synthetic_batch(per_rank, args.res, args.text_len, te_cfg.lm_dim, device, 1234 + rank)
@@ -225,6 +231,7 @@ def run_ours(args):
                       "global_batch": args.global_batch, "micro_batch": tr.micro, "seq_len": (args.res // 16) ** 2,
                       "text_len": args.text_len, "res": args.res, "parallelism": f"dp{world}",
                       "optimizer": "muon(sharded)+adamw", "grad_comm": args.grad_comm,
+                      "moe": "8 experts top-2 hidden 4096 every other block, expert-parallel" if args.moe else None,
                       "l2": "inputs larger than L2 (no flush needed)"},
            "clocks": clocks, "gpu_launches": int(launches), "impl": "ours"}
     if not args.no_e2e:
@@ -407,8 +414,53 @@ def run_reference(args):
         dist.destroy_process_group()
 
 
+def run_pp(args):
+    """1F1B pipeline x data parallel: latent tokens / s of the whole job."""
+    sys.path.insert(0, HERE)
+    from dataclasses import replace
+    from trenowanie_generatora_obrazkow_b200.models.config import benchmark_configs
+    from trenowanie_generatora_obrazkow_b200.ops._ext import check_errors, ext
+    from trenowanie_generatora_obrazkow_b200.train.pp_trainer import PPTrainer
+    from trenowanie_generatora_obrazkow_b200.train.trainer import TrainConfig
+    rank, world, local = setup_dist(args)
+    device = torch.device("cuda", local)
+    den_cfg, te_cfg = benchmark_configs(args.config)
+    side = args.res // 16
+    den_cfg = replace(den_cfg, latent_size=side)
+    dp = world // args.pp
+    n = args.microbatches * args.pp_micro
+    cfg = TrainConfig(global_batch=n * dp, micro_batch=args.pp_micro, steps=10 ** 6, grad_comm=args.grad_comm)
+    tr = PPTrainer(den_cfg, te_cfg, cfg, device, args.pp, args.microbatches)
+    host, devb = synthetic_batch(n if tr.first else 1, args.res, args.text_len, te_cfg.lm_dim, device, 1234 + rank)
+    batch = dict(devb, n=n, side=side, text_len=args.text_len)
+    for _ in range(args.warmup):
+        tr.step(batch)
+    torch.cuda.synchronize()
+    check_errors(device)
+    n0 = ext().launch_count()
+    ms, clocks = timed(lambda: tr.step(batch), args.steps, world, local)
+    launches = (ext().launch_count() - n0)
+    check_errors(device)
+    tokens = n * dp * side * side
+    value = tokens / (ms / 1e3)
+    out = {"metric": METRIC, "value": round(value, 1), "unit": "latent-tokens/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (N(0,1) FLUX.2-shaped latents and frozen-LM states), random init",
+           "config": {"model": f"DiT {args.config}", "global_batch": n * dp, "microbatches": args.microbatches,
+                      "micro_batch": args.pp_micro, "seq_len": side * side, "res": args.res,
+                      "parallelism": f"pp{args.pp}xdp{dp}", "schedule": "1F1B", "grad_comm": args.grad_comm,
+                      "l2": "inputs larger than L2 (no flush needed)"},
+           "clocks": clocks, "gpu_launches_rank0": int(launches), "impl": "ours"}
+    emit(rank, out)
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.pp > 1:
+        run_pp(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

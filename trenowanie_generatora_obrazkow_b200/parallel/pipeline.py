@@ -185,7 +185,7 @@ class OneFOneB:
         return [dist.P2POp(dist.isend, b.contiguous(), self.pipe[peer], self.group) for b in bufs]
 
     # ---- one step --------------------------------------------------------------------------------------------
-    def step(self, M, first_inputs=None, targets=None, side=None, loss_scale=1.0):
+    def step(self, M, first_inputs=None, targets=None, side=None, loss_scale=1.0, before_last_backward=None):
         """first_inputs(i) -> (z_t, t, text_kw) on stage 0; targets: list of M token-major targets on the last
         stage. Returns the summed loss (last stage) or None."""
         s, pp = self.s, self.pp
@@ -215,6 +215,8 @@ class OneFOneB:
             return [out.detach(), t6.detach(), text.detach(), tl]
 
         def backward(i, grads):
+            if i == M - 1 and before_last_backward is not None:
+                before_last_backward()  # e.g. arm the gradient buckets: they reduce as this backward completes them
             ins, outs, _ = saved.pop(i)
             if last:
                 outs.backward()

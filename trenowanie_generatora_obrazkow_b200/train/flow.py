@@ -33,9 +33,10 @@ def make_mlm(ids, prob, generator=None):
 class FlowModel(nn.Module):
     """Text encoder + denoiser in one module (one gradient bucket set, one checkpoint)."""
 
-    def __init__(self, te, den, mlm_weight=0.0, repa_proj=None, repa_layer=0, repa_weight=0.0):
+    def __init__(self, te, den, mlm_weight=0.0, repa_proj=None, repa_layer=0, repa_weight=0.0, moe_aux_weight=0.0):
         super().__init__()
         self.te, self.den, self.mlm_weight = te, den, mlm_weight
+        self.moe_aux_weight = moe_aux_weight
         self.repa_proj, self.repa_layer, self.repa_weight = repa_proj, repa_layer, repa_weight
 
     def encode_text(self, ids=None, lm_states=None, valid=None, is_null=None):
@@ -59,6 +60,11 @@ class FlowModel(nn.Module):
             v = self.den(z_t, t, text, text_valid, cond=cond, rope=rope)
         loss_fm = F.mse_loss(v.float(), target)
         loss = loss_fm
+        if self.moe_aux_weight > 0:
+            from ..models.moe import moe_aux_loss
+            aux = moe_aux_loss(self.den)
+            if aux is not None:
+                loss = loss + self.moe_aux_weight * aux
         if loss_repa is not None:
             loss = loss + self.repa_weight * loss_repa
             loss_repa = loss_repa.detach()

@@ -1,0 +1,119 @@
+"""PP x DP flow-matching trainer (reference train_pp.py main loop, 2082-2352, without the OPD / server roles).
+
+Rank layout: rank = replica * pp + stage. Each rank builds only its stage (parallel/pipeline.py), the same seed on
+every replica of a stage, and broadcasts its weights over the stage group. One ``step``:
+  stage 0 draws t / noise / caption dropout for the M micro-batches, sends the targets to the last stage, the 1F1B
+  schedule runs the forwards / backwards, gradients are reduced over the stage group (bucketed, overlapped with the
+  backward), the clipping norm is all-reduced over the pipe, Muon (sharded over the stage group) + AdamW step, and
+  replica 0 keeps the EMA of its stage.
+"""
+import math
+
+import torch
+import torch.distributed as dist
+
+from ..models.text import LMTextEncoder
+from ..optim import EMA, build_optimizers, lr_mult, set_lr
+from ..parallel.ddp import GradBuckets
+from ..parallel.pipeline import (OneFOneB, StageModel, clip_with_norm, grid_layout, pipe_grad_norm, recv_targets,
+                                 send_targets, stage_ranges)
+from .flow import drop_captions
+from .trainer import TrainConfig
+
+
+class PPTrainer:
+    def __init__(self, den_cfg, te_cfg, cfg: TrainConfig, device, pp, microbatches, te_cost=1.0):
+        self.cfg, self.device = cfg, torch.device(device)
+        self.rank, self.world = dist.get_rank(), dist.get_world_size()
+        self.pp, self.M = pp, microbatches
+        self.dp, pipes, stages = grid_layout(self.world, pp)
+        self.stage, self.replica = self.rank % pp, self.rank // pp
+        self.pipe = pipes[self.replica]
+        # every rank creates every group (collective), keeps its own
+        self.pipe_group = self.stage_group = None
+        for ranks in pipes:
+            g = dist.new_group(ranks)
+            if self.rank in ranks:
+                self.pipe_group = g
+        for ranks in stages:
+            g = dist.new_group(ranks)
+            if self.rank in ranks:
+                self.stage_group = g
+        self.den_cfg, self.te_cfg = den_cfg, te_cfg
+        lo, hi = stage_ranges(den_cfg.depth, pp, te_cost)[self.stage]
+        self.first, self.last = self.stage == 0, self.stage == pp - 1
+        self.model = StageModel(den_cfg, te_cfg, lo, hi, self.first, self.last, self.device,
+                                seed=cfg.seed * 1000 + self.stage)
+        for p in self.model.parameters():  # identical replicas of a stage
+            dist.broadcast(p.data, src=stages[self.stage][0], group=self.stage_group)
+        self.named = self.model.full_named_parameters()
+        self.params = [p for _, _, p in self.named if p.requires_grad]
+        self.buckets = GradBuckets(self.params, group=self.stage_group, comm=cfg.grad_comm)
+        ratio = cfg.global_batch / 256
+        lr_scale = 1.0 if cfg.no_lr_batch_scaling else math.sqrt(ratio)
+        self.opts, _ = build_optimizers(self.named, optimizer=cfg.optimizer, lr_muon=cfg.lr_muon, lr_emb=cfg.lr_emb,
+                                        lr_adam=cfg.lr_adam, lr_hidden=cfg.lr_hidden, lr_scale=lr_scale, wd=cfg.wd,
+                                        beta2=cfg.beta2, momentum=cfg.momentum, ns_steps=cfg.ns_steps,
+                                        cmuon=cfg.cmuon, muon_period=cfg.muon_period, muon_gamma=cfg.muon_gamma,
+                                        shard=cfg.shard_muon, group=self.stage_group)
+        ema = cfg.ema if cfg.ema is not None else 0.9995 ** ratio
+        self.ema = EMA(self.params, ema) if self.replica == 0 else None
+        self.gen = torch.Generator(device=self.device)
+        self.gen.manual_seed(cfg.seed * 1000 + self.replica)
+        self.step_idx = 0
+        self.sched = None
+
+    def _schedule(self, mb, side, L):
+        dt = torch.bfloat16 if self.device.type == "cuda" else torch.float32
+        d = self.den_cfg
+        shapes = dict(x=(mb, side * side, d.dim), t6=(mb, 6, d.dim), text=(mb, L, d.text_dim), dtype=dt)
+        return OneFOneB(self.model, self.pipe, self.stage, shapes, self.device)
+
+    def step(self, batch):
+        """batch (stage 0 of every replica): x0 (M * mb, C, h, w) and lm_states (M * mb, L, D) [+ valid, is_null].
+        Other stages pass the same keys with shapes only used for sizing (or None). Returns the loss on the last
+        stage (device scalar), else None."""
+        cfg, M = self.cfg, self.M
+        x0_all = batch["x0"].to(self.device, non_blocking=True) if self.first else None
+        n = batch["n"]
+        mb = n // M
+        side = batch["side"]
+        L = batch["text_len"]
+        C = self.den_cfg.latent_channels
+        self.buckets.zero()
+        inputs, targets = [], None
+        if self.first:
+            st_all = batch["lm_states"].to(self.device, non_blocking=True)
+            targets = []
+            for i in range(M):
+                sl = slice(i * mb, (i + 1) * mb)
+                x0 = x0_all[sl].float()
+                t = torch.sigmoid(torch.randn(mb, device=self.device, generator=self.gen))
+                if cfg.t_shift != 1.0:
+                    t = cfg.t_shift * t / (1 + (cfg.t_shift - 1) * t)
+                eps = torch.randn(x0.shape, device=self.device, generator=self.gen)
+                valid = torch.ones(mb, L, dtype=torch.bool, device=self.device)
+                is_null, valid = drop_captions(None, valid, cfg.cfg_drop, self.gen)
+                tt = t.view(-1, 1, 1, 1)
+                inputs.append(((1 - tt) * x0 + tt * eps, t, dict(lm_states=st_all[sl], valid=valid,
+                                                                  is_null=is_null)))
+                targets.append((eps - x0).flatten(2).transpose(1, 2).contiguous())
+            if self.pp > 1:
+                send_targets(targets, self.pipe)
+                targets = None
+        elif self.last:
+            targets = recv_targets(M, (mb, side * side, C), torch.float32, self.device, self.pipe)
+        if self.sched is None or self.sched.shapes["x"][0] != mb:
+            self.sched = self._schedule(mb, side, L)
+        loss = self.sched.step(M, (lambda i: inputs[i]) if self.first else None, targets, side, 1.0 / M,
+                               before_last_backward=self.buckets.arm)
+        self.buckets.finish()
+        norm = pipe_grad_norm(self.params, self.pipe_group)
+        clip_with_norm(self.params, norm, cfg.clip)
+        set_lr(self.opts, lr_mult(self.step_idx, cfg.steps, cfg.warmup, cfg.schedule))
+        for o in self.opts:
+            o.step()
+        self.step_idx += 1
+        if self.ema is not None:
+            self.ema.update(self.step_idx)
+        return loss

@@ -63,6 +63,13 @@ class TrainConfig:
     seed: int = 0
     act_checkpoint: bool = False
     random_lm: bool = False
+    moe_experts: int = 0          # > 0: every moe_every-th block's MLP becomes an MoE layer
+    moe_top_k: int = 2
+    moe_hidden: int = 4096
+    moe_every: int = 2
+    moe_capacity: float = 1.25
+    moe_aux_weight: float = 0.01
+    expert_parallel: bool = True  # experts sharded over the data-parallel group
 
     def derived(self, world=1):
         ratio = self.global_batch / 256
@@ -87,20 +94,36 @@ class Trainer:
         torch.manual_seed(cfg.seed)  # identical init on every rank
         te, den = models if models is not None else build_models(den_cfg, te_cfg, device=self.device)
         self.te, self.den = te.to(self.device), den.to(self.device)
+        self.expert_params = []
+        if cfg.moe_experts:
+            from ..models.moe import MoEMLP, moe_denoiser
+            ep_group = dist.group.WORLD if (cfg.expert_parallel and self.distributed and self.world > 1) else None
+            moe_denoiser(den, cfg.moe_experts, cfg.moe_top_k, cfg.moe_hidden, cfg.moe_every, cfg.moe_capacity, ep_group)
+            torch.manual_seed(cfg.seed * 7919 + (self.rank if ep_group is not None else 0))
+            for m in den.modules():  # each rank's experts are different experts
+                if isinstance(m, MoEMLP):
+                    m.reset_parameters()
+                    with torch.no_grad():  # the router is replicated: same init everywhere
+                        g = torch.Generator().manual_seed(cfg.seed + 17)
+                        m.router.weight.copy_(torch.randn(m.router.weight.shape, generator=g) * 0.02)
+                    if ep_group is not None:
+                        self.expert_params += [m.w_in, m.w_out]
         self.den.checkpoint_blocks = cfg.act_checkpoint
         self.lm_te = isinstance(te, LMTextEncoder)
         if self.lm_te:
             te.checkpoint_blocks = cfg.act_checkpoint
         self.frozen_lm = build_frozen_lm(te_cfg, self.device, cfg.random_lm) if self.lm_te else None
         mlm = 0.0 if self.lm_te else cfg.mlm_weight
-        self.model = FlowModel(te, den, mlm_weight=mlm)
+        self.model = FlowModel(te, den, mlm_weight=mlm, moe_aux_weight=cfg.moe_aux_weight if cfg.moe_experts else 0.0)
         lr_scale, ema = cfg.derived(self.world)
         self.named = [(pre, n, p) for pre, mod in (("te", te), ("den", den)) for n, p in mod.named_parameters()]
         self.params = [p for _, _, p in self.named if p.requires_grad]
         reduce_grads = not cfg.diloco
         self.buckets = None
-        if self.device.type == "cuda":
-            self.buckets = GradBuckets(self.params, group=group, comm=cfg.grad_comm if reduce_grads else "none")
+        eids = {id(p) for p in self.expert_params}
+        if self.device.type == "cuda":  # expert-parallel weights are not replicated: never averaged
+            self.buckets = GradBuckets([p for p in self.params if id(p) not in eids], group=group,
+                                       comm=cfg.grad_comm if reduce_grads else "none")
         mdt = torch.bfloat16 if cfg.muon_momentum_dtype == "bf16" else None
         self.opts, self.counts = build_optimizers(
             self.named, optimizer=cfg.optimizer, lr_muon=cfg.lr_muon, lr_emb=cfg.lr_emb, lr_adam=cfg.lr_adam,
@@ -168,6 +191,9 @@ class Trainer:
         else:
             for p in self.params:
                 p.grad = None
+        for p in self.expert_params:
+            if p.grad is not None:
+                p.grad.zero_()
         acc = torch.zeros((), device=self.device)
         acc_mlm = torch.zeros((), device=self.device)
         for m in range(self.accum):
@@ -188,6 +214,8 @@ class Trainer:
                 acc_mlm += l_mlm / self.accum
         if self.buckets is not None:
             self.buckets.finish()
+        if self.expert_params and self.world > 1:  # their gradients summed every rank's loss: make it the mean
+            torch._foreach_mul_([p.grad for p in self.expert_params if p.grad is not None], 1.0 / self.world)
         self.last_gnorm = torch.nn.utils.clip_grad_norm_(self.params, cfg.clip, foreach=True)
         set_lr(self.opts, lr_mult(self.step_idx, cfg.steps, cfg.warmup, cfg.schedule))
         for o in self.opts:
