@@ -140,6 +140,34 @@ __global__ void __launch_bounds__(512) allreduce_bf16_kernel(PeerAllReduceParams
   }
 }
 
+// ------------------------------------------------------------------------------------------------------------------
+// peer_copy: stream a local buffer into another GPU's buffer with NVLink stores (the OPD weight snapshot
+// broadcast), then publish `version` in the destination's version word. Completion across CTAs: every CTA adds 1 to
+// a local arrival counter after a system fence; the CTA that brings it to version * gridDim.x (the counter is never
+// reset, so successive versions need no clearing) writes the version word with a release store.
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) peer_copy_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src,
+                                                        long long n16, uint32_t* dst_version,
+                                                        unsigned long long* counter, uint32_t version) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n16; i += (long long)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned long long target = (unsigned long long)version * gridDim.x;
+    if (atomicAdd(counter, 1ull) + 1 == target) flag_store_release(dst_version, version);
+  }
+}
+
+cudaError_t peer_copy_launch(void* dst, const void* src, long long nbytes, uint32_t* dst_version,
+                             unsigned long long* counter, uint32_t version, int blocks, cudaStream_t s) {
+  if (nbytes % 16 != 0 || (reinterpret_cast<uintptr_t>(dst) & 15) || (reinterpret_cast<uintptr_t>(src) & 15))
+    return cudaErrorInvalidValue;
+  peer_copy_kernel<<<blocks, 512, 0, s>>>(reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(src),
+                                          nbytes / 16, dst_version, counter, version);
+  return cudaGetLastError();
+}
+
 cudaError_t allreduce_bf16_launch(const PeerAllReduceParams& p, int blocks, cudaStream_t s) {
   allreduce_bf16_kernel<<<blocks, 512, 0, s>>>(p);
   return cudaGetLastError();

@@ -143,5 +143,7 @@ struct PeerAllReduceParams {
   int* err;
 };
 cudaError_t allreduce_bf16_launch(const PeerAllReduceParams& p, int blocks, cudaStream_t s);
+cudaError_t peer_copy_launch(void* dst, const void* src, long long nbytes, uint32_t* dst_version,
+                             unsigned long long* counter, uint32_t version, int blocks, cudaStream_t s);
 
 }  // namespace tgo

@@ -524,6 +524,16 @@ void allreduce_bf16(at::Tensor grads, std::vector<int64_t> staging, std::vector<
   TGO_CHECK_LAUNCH(allreduce_bf16_launch(p, (int)blocks, at::cuda::getCurrentCUDAStream()));
 }
 
+// src (contiguous CUDA tensor) -> dst (a peer's mapped buffer), then dst_version := version (see comm.cu)
+void peer_copy(int64_t dst, at::Tensor src, int64_t dst_version, int64_t counter, int64_t version, int64_t blocks) {
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous(), "peer_copy: contiguous CUDA source");
+  const c10::cuda::CUDAGuard guard(src.device());
+  TGO_CHECK_LAUNCH(peer_copy_launch(reinterpret_cast<void*>(dst), src.data_ptr(), src.numel() * src.element_size(),
+                                    reinterpret_cast<uint32_t*>(dst_version),
+                                    reinterpret_cast<unsigned long long*>(counter), (uint32_t)version, (int)blocks,
+                                    at::cuda::getCurrentCUDAStream()));
+}
+
 }  // namespace tgo
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -536,6 +546,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_free", &tgo::symm_free);
   m.def("ipc_open", &tgo::ipc_open, "map a peer's buffer from its IPC handle");
   m.def("ipc_close", &tgo::ipc_close);
+  m.def("peer_copy", &tgo::peer_copy, "NVLink copy into a peer's buffer + version word (weight snapshots)");
   m.def("allreduce_bf16", &tgo::allreduce_bf16, "fused cast + reduce-scatter + all-gather over peer memory");
   m.def("set_attention_tc", &tgo::set_attention_tc, "use the tcgen05 attention forward (default) or mma.sync");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");

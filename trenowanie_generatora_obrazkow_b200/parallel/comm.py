@@ -20,6 +20,7 @@ class PeerBuffers:
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        self.group_ranks = dist.get_process_group_ranks(group) if group is not None else list(range(self.world))
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.local, self.ptrs, self._opened = {}, {}, []
         handles = {}

@@ -1,0 +1,219 @@
+"""MPMD service roles for on-policy distillation: teacher servers, rollout actors, and the student-to-actor weight
+snapshot broadcast (reference aurora/klein.py:198-320, aurora/opd_actor.py, train_pp.py:1146-1326).
+
+Layout: ranks [0, L) learners, [L, L + A) rollout actors, [L + A, world) teachers. Control messages (small int64
+headers) travel over a Gloo group, so servers can receive from any learner; tensors travel over the default group
+(NCCL on GPUs). Protocols:
+
+* Teacher: header [KIND_VELOCITY, B, C, h, w, L, D] from a learner, then x (B, C, h, w) fp32, t (B,), LM states
+  (B, L, D), valid (B, L) uint8; reply: the teacher's CFG velocity (B, C, h, w) fp32. A learner spreads a batch over
+  the teacher ranks (a rotating first rank per request). KIND_STOP ends the server.
+* Actor: header [KIND_ROLLOUT, B, C, h, w, L, D, step, version] with noise / LM states / valid; the actor generates
+  the rollout states with the snapshot it holds and replies with (states (B m, C, h, w), t (B m,)). It refuses a
+  job whose required snapshot version is newer than its own (the learner always sends the snapshot first).
+* Snapshot: learner 0 flattens the student's parameters and streams them into every actor's mapped buffer with the
+  peer-copy kernel (NVLink stores, then a version word), then tells each actor (Gloo) the version; on CPU the flat
+  tensor is sent over the process group instead. Versions only grow; an actor applies a snapshot only between jobs.
+"""
+import torch
+import torch.distributed as dist
+
+KIND_STOP, KIND_VELOCITY, KIND_ROLLOUT, KIND_SNAPSHOT = 0, 1, 2, 3
+HDR = 10
+
+
+class RoleLayout:
+    def __init__(self, world, learners, actors=0, teachers=0):
+        assert learners + actors + teachers == world, "learners + actors + teachers must equal the world size"
+        self.learners = list(range(learners))
+        self.actors = list(range(learners, learners + actors))
+        self.teachers = list(range(learners + actors, world))
+
+    def role(self, rank):
+        if rank in self.learners:
+            return "learner"
+        return "actor" if rank in self.actors else "teacher"
+
+
+def _hdr(*vals):
+    h = torch.zeros(HDR, dtype=torch.int64)
+    h[:len(vals)] = torch.tensor(vals, dtype=torch.int64)
+    return h
+
+
+class TeacherServer:
+    def __init__(self, teacher, device, control_group, dtype=torch.float32):
+        self.teacher, self.device, self.ctl, self.dtype = teacher, device, control_group, dtype
+
+    def serve(self):
+        served = 0
+        while True:
+            h = torch.zeros(HDR, dtype=torch.int64)
+            src = dist.recv(h, group=self.ctl)
+            kind, B, C, hh, w, L, D = h[:7].tolist()
+            if kind == KIND_STOP:
+                return served
+            x = torch.empty(B, C, hh, w, device=self.device)
+            t = torch.empty(B, device=self.device)
+            st = torch.empty(B, L, D, device=self.device, dtype=self.dtype)
+            valid = torch.empty(B, L, device=self.device, dtype=torch.uint8)
+            for buf in (x, t, st, valid):
+                dist.recv(buf, src=src)
+            v = self.teacher.velocity(x, t, dict(lm_states=st, valid=valid.bool())).float().contiguous()
+            dist.send(v, dst=src)
+            served += 1
+
+
+class TeacherClient:
+    def __init__(self, teachers, control_group, rank):
+        self.teachers, self.ctl, self.rank = teachers, control_group, rank
+        self.turn = rank
+
+    def velocity(self, x, t, text_kw):
+        """Split the batch over the teacher ranks, send every part, then collect the replies in order."""
+        st, valid = text_kw["lm_states"], text_kw["valid"]
+        B = x.shape[0]
+        n = len(self.teachers)
+        parts = [(i * B // n, (i + 1) * B // n) for i in range(n)]
+        order = [self.teachers[(self.turn + i) % n] for i in range(n)]
+        self.turn += 1
+        replies = []
+        for (b0, b1), dst in zip(parts, order):
+            if b1 <= b0:
+                continue
+            xs = x[b0:b1].float().contiguous()
+            dist.send(_hdr(KIND_VELOCITY, b1 - b0, *xs.shape[1:], *st.shape[1:]), dst=dst, group=self.ctl)
+            for buf in (xs, t[b0:b1].float().contiguous(), st[b0:b1].contiguous(),
+                        valid[b0:b1].to(torch.uint8).contiguous()):
+                dist.send(buf, dst=dst)
+            replies.append((b0, b1, dst))
+        out = torch.empty(B, *x.shape[1:], device=x.device)
+        for b0, b1, dst in replies:
+            buf = torch.empty(b1 - b0, *x.shape[1:], device=x.device)
+            dist.recv(buf, src=dst)
+            out[b0:b1] = buf
+        return out
+
+    def stop(self):
+        for dst in self.teachers:
+            dist.send(_hdr(KIND_STOP), dst=dst, group=self.ctl)
+
+
+def flat_params(params):
+    return torch.cat([p.detach().reshape(-1).float() for p in params])
+
+
+@torch.no_grad()
+def load_flat(params, flat):
+    off = 0
+    for p in params:
+        n = p.numel()
+        p.copy_(flat[off:off + n].view_as(p).to(p.dtype))
+        off += n
+
+
+class SnapshotSender:
+    """Learner 0 -> actors. On CUDA: peer-copy kernel into each actor's IPC-mapped buffer; else process-group
+    sends."""
+
+    def __init__(self, params, actors, control_group, peer_buffers=None):
+        self.params, self.actors, self.ctl = list(params), actors, control_group
+        self.n = sum(p.numel() for p in self.params)
+        self.pb = peer_buffers
+        self.version = 0
+        self.counter = None
+        if self.pb is not None:
+            self.counter = torch.zeros(1, dtype=torch.int64, device=self.params[0].device)
+
+    def send(self):
+        self.version += 1
+        flat = flat_params(self.params)
+        for dst in self.actors:
+            dist.send(_hdr(KIND_SNAPSHOT, self.version, self.n), dst=dst, group=self.ctl)
+            if self.pb is not None:
+                from ..ops._ext import ext
+                j = self.pb.group_ranks.index(dst)
+                ext().peer_copy(self.pb.ptrs["flat"][j], flat, self.pb.ptrs["version"][j], self.counter.data_ptr(),
+                                self.version, 64)
+                torch.cuda.current_stream().synchronize()
+                dist.send(_hdr(KIND_SNAPSHOT, self.version), dst=dst, group=self.ctl)  # data landed
+            else:
+                dist.send(flat, dst=dst)
+        return self.version
+
+
+class RolloutActor:
+    """Holds a student copy; applies snapshots; serves rollout jobs from learners."""
+
+    def __init__(self, te, den, params, device, control_group, opd_kwargs, peer_buffers=None, local_flat=None):
+        self.te, self.den, self.params, self.device, self.ctl = te, den, list(params), device, control_group
+        self.kw = opd_kwargs
+        self.version = 0
+        self.pb, self.local_flat = peer_buffers, local_flat
+        self.n = sum(p.numel() for p in self.params)
+
+    def _apply_snapshot(self, src, version):
+        if self.pb is None:
+            flat = torch.empty(self.n, device=self.device)
+            dist.recv(flat, src=src)
+        else:
+            h = torch.zeros(HDR, dtype=torch.int64)
+            dist.recv(h, src=src, group=self.ctl)  # the learner finished the peer copy
+            flat = self.local_flat
+            assert h[1].item() == version
+        load_flat(self.params, flat)
+        self.version = version
+
+    @torch.no_grad()
+    def serve(self):
+        from ..ops.reference import valid_to_len
+        from ..train.opd import dance_picks, diffusion_picks, opd_grid, rollout
+        jobs = 0
+        while True:
+            h = torch.zeros(HDR, dtype=torch.int64)
+            src = dist.recv(h, group=self.ctl)
+            kind = int(h[0])
+            if kind == KIND_STOP:
+                return jobs
+            if kind == KIND_SNAPSHOT:
+                self._apply_snapshot(src, int(h[1]))
+                continue
+            _, B, C, hh, w, L, D, step, need = h[:9].tolist()
+            if need > self.version:
+                raise RuntimeError(f"actor holds snapshot {self.version}, job needs {need}")
+            noise = torch.empty(B, C, hh, w, device=self.device)
+            st = torch.empty(B, L, D, device=self.device, dtype=self.kw.get("dtype", torch.float32))
+            valid = torch.empty(B, L, device=self.device, dtype=torch.uint8)
+            for buf in (noise, st, valid):
+                dist.recv(buf, src=src)
+            K, m = self.kw["K"], self.kw["m"]
+            g = torch.Generator().manual_seed(self.kw["seed"] * 1_000_003 + src * 1009 + step + 7)
+            picks = dance_picks(B, m, K, self.kw["beta"], self.kw["seed"], src, step) if self.kw["method"] == "dance" \
+                else diffusion_picks(B, m, K, g)
+            ts = opd_grid(K, self.kw["shift"], torch.rand((), generator=g).item(), self.device)
+            text, v = self.te(lm_states=st, valid=valid.bool())
+            states = rollout(self.den, text, valid_to_len(v), noise, ts, picks, self.kw["mb"]).flatten(0, 1)
+            t = ts[picks.to(self.device)].flatten().contiguous()
+            dist.send(states.contiguous(), dst=src)
+            dist.send(t, dst=src)
+            jobs += 1
+
+
+class ActorClient:
+    def __init__(self, actor, control_group, m):
+        self.actor, self.ctl, self.m = actor, control_group, m
+
+    def rollouts(self, noise, lm_states, valid, step, version):
+        B = noise.shape[0]
+        dist.send(_hdr(KIND_ROLLOUT, B, *noise.shape[1:], *lm_states.shape[1:], step, version), dst=self.actor,
+                  group=self.ctl)
+        for buf in (noise.float().contiguous(), lm_states.contiguous(), valid.to(torch.uint8).contiguous()):
+            dist.send(buf, dst=self.actor)
+        states = torch.empty(B * self.m, *noise.shape[1:], device=noise.device)
+        t = torch.empty(B * self.m, device=noise.device)
+        dist.recv(states, src=self.actor)
+        dist.recv(t, src=self.actor)
+        return states, t
+
+    def stop(self):
+        dist.send(_hdr(KIND_STOP), dst=self.actor, group=self.ctl)
