@@ -99,6 +99,8 @@ SIZES = {
                             latent_size=32),
     # the CPU test DiT: hidden 576, 12 blocks, 9 heads, MLP 4x (SwiGLU 1536), 256 tokens
     "tiny": DenoiserConfig(dim=576, depth=12, heads=9, mlp_hidden=swiglu_hidden(576), text_dim=576, latent_size=16),
+    # a few-MB model for smoke runs and multi-process CPU tests of the entry points
+    "nano": DenoiserConfig(dim=128, depth=4, heads=2, mlp_hidden=384, text_dim=128, latent_size=8),
     # the MoE benchmark backbone is "1.24b" with every other MLP replaced by experts (models/moe.py)
     # the 4B OPD teacher: hidden 3072, 32 blocks, 24 heads of 128
     "teacher-4b": DenoiserConfig(dim=3072, depth=32, heads=24, mlp_hidden=swiglu_hidden(3072), text_dim=1024,
@@ -115,6 +117,8 @@ TE_SIZES = {
     # synthetic frozen-LM states of width 1024 (128 tokens) -> 2-block refiner (benchmark configurations)
     "states1024": LMEncoderConfig(repo="", tok_suffix="", lm_dim=1024, skip_last=0, dim=1024, depth=2, heads=16,
                                   kv_heads=4, head_dim=64, mlp_hidden=2816, max_tokens=128, backend="states"),
+    "states-nano": LMEncoderConfig(repo="", tok_suffix="", lm_dim=64, skip_last=0, dim=128, depth=1, heads=2,
+                                   kv_heads=1, head_dim=64, mlp_hidden=384, max_tokens=16, backend="states"),
     "states1024-64": LMEncoderConfig(repo="", tok_suffix="", lm_dim=1024, skip_last=0, dim=576, depth=2, heads=9,
                                      kv_heads=3, head_dim=64, mlp_hidden=1536, max_tokens=64, backend="states"),
 }
