@@ -4,7 +4,7 @@
   python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
       bench.py --gpus N --steps K --warmup W
 
-Config: DiT hidden 2048, 24 blocks, 16 heads of 128, SwiGLU 5504 ("MLP 4x" param-matched),
+Config (the headline "1.24B DiT" training config): DiT hidden 2048, 24 blocks, 16 heads of 128, SwiGLU 5504 ("MLP 4x" param-matched),
 2-block text refiner (1024 wide) on synthetic frozen-LM states [B, 128, 1024] ~ N(0, 1); 512 px synthetic FLUX.2
 latents (128 channels at 32 x 32 = 1024 tokens / image) ~ N(0, 1); global batch 256 (micro-batch 32, gradient
 accumulation 256 / (32 N)); bf16 compute; Muon (5 Newton-Schulz steps, sharded over ranks) + AdamW; EMA; random
@@ -31,7 +31,7 @@ import torch.distributed as dist
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF = os.path.join(HERE, "baseline", "_ref")
-BASELINE_VALUE = None  # BASELINE.md publishes no number for this metric
+BASELINE_VALUE = None  # the reference publishes no number for this metric
 METRIC = "1.24B DiT train latent-tokens/s"
 
 
@@ -47,9 +47,9 @@ def parse():
     p.add_argument("--res", type=int, default=512)
     p.add_argument("--text-len", type=int, default=128)
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--moe", action="store_true", help="BASELINE config 4: every other MLP -> 8 experts, top-2, "
+    p.add_argument("--moe", action="store_true", help="MoE config: every other MLP -> 8 experts, top-2, "
                    "expert hidden 4096, expert-parallel over the GPUs")
-    p.add_argument("--pp", type=int, default=1, help="pipeline stages (BASELINE config 3: --pp 4 on 8 GPUs, "
+    p.add_argument("--pp", type=int, default=1, help="pipeline stages (pipeline config: --pp 4 on 8 GPUs, "
                    "--res 1024 --microbatches 8 --pp-micro 4)")
     p.add_argument("--microbatches", type=int, default=8)
     p.add_argument("--pp-micro", type=int, default=4)
@@ -415,7 +415,7 @@ def run_reference(args):
 
 
 def run_pp(args):
-    """1F1B pipeline x data parallel: latent tokens / s of the whole job."""
+    """1F1B pipeline x data parallel (the pipeline config): latent tokens / s of the whole job."""
     sys.path.insert(0, HERE)
     from dataclasses import replace
     from trenowanie_generatora_obrazkow_b200.models.config import benchmark_configs

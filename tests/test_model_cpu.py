@@ -114,7 +114,7 @@ def test_every_param_gets_gradient_after_steps():
 
 
 def test_tiny_baseline_config_train_step():
-    """BASELINE config 1 on CPU: tiny DiT (576 x 12, 9 heads), 256 tokens, text [4, 64, 1024]: one step with
+    """The tiny headline config on CPU: tiny DiT (576 x 12, 9 heads), 256 tokens, text [4, 64, 1024]: one step with
     Muon (5 NS steps) on the hidden matrices and AdamW elsewhere; the loss is finite and the weights move."""
     from trenowanie_generatora_obrazkow_b200.optim import build_optimizers
     torch.manual_seed(0)

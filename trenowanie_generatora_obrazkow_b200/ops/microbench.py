@@ -1,0 +1,267 @@
+"""Per-kernel micro-benchmark of the fused sm_100a ops on the 1.24B DiT shapes, with a library baseline per op.
+
+    python -m trenowanie_generatora_obrazkow_b200.ops.microbench --op all
+    python -m trenowanie_generatora_obrazkow_b200.ops.microbench --op gemm_qkv --small --iters 2 --warmup 1
+
+Every op is timed with CUDA events on the launching stream, one event pair per launch, after ``--warmup`` untimed
+launches; a 256 MiB buffer (twice the L2) is rewritten between timed launches so each launch starts cold. The report
+is one JSON line per op: median milliseconds, achieved TFLOP/s (contractions) or GB/s (bandwidth-bound ops, counted
+as the algorithmic bytes: every input read once, every output written once), the fraction of the measured peaks in
+MEASURED_PEAKS.json (copy bandwidth, cuBLAS bf16 burst) when that file is found, and the same figures for the library
+path that computes the same result (cuBLAS through torch.matmul, cuDNN / flash SDPA, eager PyTorch elementwise).
+``--small`` shrinks the batch to keep a single launch short (for profiler captures). The reference has no counterpart
+(its kernels are Triton / torch.compile generated).
+"""
+import argparse
+import json
+import os
+import statistics
+
+import torch
+import torch.nn.functional as F
+
+from . import reference as R
+from ._ext import err_buf, ext
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def measured_peaks():
+    for d in (os.getcwd(), os.path.dirname(os.path.dirname(HERE))):
+        p = os.path.join(d, "MEASURED_PEAKS.json")
+        if os.path.exists(p):
+            with open(p) as f:
+                return json.load(f)
+    return {}
+
+
+_FLUSH = None
+
+
+def flush_l2():
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    _FLUSH.fill_(1)
+
+
+def time_op(fn, iters, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        flush_l2()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    return statistics.median(times)
+
+
+def _bf16(*shape, scale=1.0):
+    return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# op builders: each returns (ours, library, flops, bytes)
+# ------------------------------------------------------------------------------------------------------------------
+def gemm_case(M, N, K):
+    a, b = _bf16(M, K), _bf16(N, K)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    err = err_buf(a.device)
+
+    def ours():
+        ext().gemm(a, b, out, False, False, None, 1.0, 0.0, False, err)
+
+    def lib():
+        torch.matmul(a, b.t(), out=out)
+
+    return ours, lib, 2.0 * M * N * K, 2 * (M * K + N * K + M * N)
+
+
+def attn_case(B, T, H, hd, backward):
+    q, k, v = (_bf16(B, T, H, hd) for _ in range(3))
+    kv_len = torch.full((B,), T, dtype=torch.int32, device="cuda")
+    scale = hd ** -0.5
+    err = err_buf(q.device)
+    o, lse = ext().attention_fwd(q, k, v, kv_len, scale, None, err)
+    do = _bf16(B, T, H, hd)
+    dq, dk, dv = (torch.empty_like(q) for _ in range(3))
+    qt, kt, vt = (x.transpose(1, 2).contiguous().requires_grad_(backward) for x in (q, k, v))
+    fl = 4.0 * B * H * T * T * hd
+    if not backward:
+        def ours():
+            ext().attention_fwd(q, k, v, kv_len, scale, o, err)
+
+        def lib():
+            F.scaled_dot_product_attention(qt, kt, vt, scale=scale)
+
+        return ours, lib, fl, 2 * 4 * B * T * H * hd
+
+    ot = F.scaled_dot_product_attention(qt, kt, vt, scale=scale)
+    dot = do.transpose(1, 2).contiguous()
+
+    def ours():
+        ext().attention_bwd(q, k, v, o, lse, do, kv_len, scale, dq, dk, dv, err)
+
+    def lib():
+        torch.autograd.grad(ot, (qt, kt, vt), dot, retain_graph=True)
+
+    return ours, lib, 2.5 * fl, 2 * 8 * B * T * H * hd
+
+
+def adanorm_case(B, T, D, backward):
+    x, y = _bf16(B, T, D), _bf16(B, T, D)
+    gate, shift, scale = (torch.randn(B, D, device="cuda", dtype=torch.bfloat16) * 0.1 for _ in range(3))
+    w = torch.ones(D, device="cuda")
+    x_new, h, rstd = ext().adanorm_fwd(x, y, gate, w, shift, scale, T, R.EPS)
+    dh, dxn = _bf16(B, T, D), _bf16(B, T, D)
+    dw = torch.zeros_like(w)
+    if not backward:
+        def ours():
+            ext().adanorm_fwd(x, y, gate, w, shift, scale, T, R.EPS)
+
+        def lib():
+            xn = x + gate[:, None] * y
+            (F.rms_norm(xn.float(), (D,), w, R.EPS) * (1 + scale[:, None]) + shift[:, None]).to(torch.bfloat16)
+
+        return ours, lib, 0.0, 2 * 4 * B * T * D
+
+    def ours():
+        ext().adanorm_bwd(dh, dxn, x_new, rstd, w, dw, scale, y, gate, T)
+
+    xr = x_new.float().requires_grad_(True)
+    hr = F.rms_norm(xr, (D,), w, R.EPS) * (1 + scale[:, None].float()) + shift[:, None].float()
+
+    def lib():
+        torch.autograd.grad(hr, xr, dh.float(), retain_graph=True)
+
+    return ours, lib, 0.0, 2 * 6 * B * T * D
+
+
+def swiglu_case(M, H, backward):
+    ab = _bf16(M, 2 * H)
+    dg = _bf16(M, H)
+    if not backward:
+        return (lambda: ext().swiglu_fwd(ab)), (lambda: R.swiglu(ab)), 0.0, 2 * 3 * M * H
+    abr = ab.detach().requires_grad_(True)
+    g = R.swiglu(abr)
+    return ((lambda: ext().swiglu_bwd(ab, dg)), (lambda: torch.autograd.grad(g, abr, dg, retain_graph=True)), 0.0,
+            2 * 5 * M * H)
+
+
+def qknorm_case(B, T, H, hd, backward):
+    C = 3 * H * hd
+    qkv = _bf16(B * T, C)
+    qw, kw = torch.ones(hd, device="cuda"), torch.ones(hd, device="cuda")
+    cos, sin = R.rope_1d_table(T, hd, device="cuda")
+    q, k, rq, rk = ext().qknorm_rope_fwd(qkv, H, H, hd, qw, kw, cos, sin, T, R.EPS)
+    dq, dk = torch.randn_like(q), torch.randn_like(k)
+    dqkv = torch.empty_like(qkv)
+    dwq, dwk = torch.zeros_like(qw), torch.zeros_like(kw)
+    qv = qkv[:, :2 * H * hd].view(B, T, 2 * H, hd)
+    if not backward:
+        def lib():
+            R.apply_rope(F.rms_norm(qv.float(), (hd,), qw, R.EPS), cos, sin).to(torch.bfloat16)
+
+        return ((lambda: ext().qknorm_rope_fwd(qkv, H, H, hd, qw, kw, cos, sin, T, R.EPS)), lib, 0.0,
+                2 * 4 * B * T * H * hd)
+
+    def ours():
+        ext().qknorm_rope_bwd(qkv, H, H, hd, qw, kw, cos, sin, T, rq, rk, dq, dk, dqkv, dwq, dwk)
+
+    xr = qv.float().requires_grad_(True)
+    nr = F.rms_norm(xr, (hd,), qw, R.EPS)
+
+    def lib():
+        torch.autograd.grad(nr, xr, torch.cat([dq.view(B, T, H, hd), dk.view(B, T, H, hd)], 2).float(), retain_graph=True)
+
+    return ours, lib, 0.0, 2 * 9 * B * T * H * hd
+
+
+def euler_case(B, side, C):
+    T = side * side
+    z = torch.randn(B, C, side, side, device="cuda")
+    v = _bf16(2 * B, T, C)
+
+    def ours():
+        ext().euler_cfg(v, z, 0.02, 3.0)
+
+    def lib():
+        vu, vc = v.float().chunk(2)
+        z.add_((vu + 3.0 * (vc - vu)).transpose(1, 2).reshape(z.shape), alpha=0.02)
+
+    return ours, lib, 0.0, 4 * 2 * B * C * T + 2 * 2 * B * T * C
+
+
+def cases(small):
+    B = 8 if small else 32
+    T, D, H, hd, MLP = 1024, 2048, 16, 128, 5504
+    M = B * T
+    return {
+        "gemm_qkv": lambda: gemm_case(M, 3 * D, D),
+        "gemm_out": lambda: gemm_case(M, D, D),
+        "gemm_mlp_up": lambda: gemm_case(M, 2 * MLP, D),
+        "gemm_mlp_down": lambda: gemm_case(M, D, MLP),
+        "attn_fwd": lambda: attn_case(B, T, H, hd, False),
+        "attn_bwd": lambda: attn_case(B, T, H, hd, True),
+        "adanorm_fwd": lambda: adanorm_case(B, T, D, False),
+        "adanorm_bwd": lambda: adanorm_case(B, T, D, True),
+        "qknorm_rope_fwd": lambda: qknorm_case(B, T, H, hd, False),
+        "qknorm_rope_bwd": lambda: qknorm_case(B, T, H, hd, True),
+        "swiglu_fwd": lambda: swiglu_case(M, MLP, False),
+        "swiglu_bwd": lambda: swiglu_case(M, MLP, True),
+        "euler_cfg": lambda: euler_case(8, 64, 128),
+    }
+
+
+def report(name, fn_ours, fn_lib, flops, nbytes, iters, warmup, peaks, library=True):
+    row = {"op": name}
+    for tag, fn in (("ours", fn_ours), ("library", fn_lib if library else None)):
+        if fn is None:
+            continue
+        ms = time_op(fn, iters, warmup)
+        r = {"ms": round(ms, 4)}
+        if flops:
+            tf = flops / ms / 1e9
+            r["tflops"] = round(tf, 1)
+            if peaks.get("bf16_tflops"):
+                r["frac_of_measured_bf16"] = round(tf / peaks["bf16_tflops"], 3)
+        else:
+            gbs = nbytes / ms / 1e6
+            r["gbs"] = round(gbs, 1)
+            if peaks.get("hbm_gbs"):
+                r["frac_of_measured_hbm"] = round(gbs / peaks["hbm_gbs"], 3)
+        row[tag] = r
+    return row
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("--op", default="all", help="comma-separated op names, or 'all'")
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--small", action="store_true")
+    p.add_argument("--no-library", action="store_true", help="time only our kernels (profiler captures)")
+    a = p.parse_args(argv)
+    torch.manual_seed(0)
+    peaks = measured_peaks()
+    table = cases(a.small)
+    names = list(table) if a.op == "all" else a.op.split(",")
+    rows = []
+    for n in names:
+        ours, lib, flops, nbytes = table[n]()
+        row = report(n, ours, lib, flops, nbytes, a.iters, a.warmup, peaks, not a.no_library)
+        from ._ext import check_errors
+        check_errors()
+        print(json.dumps(row), flush=True)
+        rows.append(row)
+        torch.cuda.empty_cache()
+    return rows
+
+
+if __name__ == "__main__":
+    main()
