@@ -53,6 +53,9 @@ def parse():
                    "--res 1024 --microbatches 8 --pp-micro 4)")
     p.add_argument("--microbatches", type=int, default=8)
     p.add_argument("--pp-micro", type=int, default=4)
+    p.add_argument("--muon-comm", default="sharded", choices=["sharded", "gather"],
+                   help="sharded: Muon gradients reduce-scattered to their owners and updates all-gathered into the "
+                        "parameter update over peer memory; gather: all-reduce every gradient, all-gather updates")
     p.add_argument("--grad-comm", default="p2p", choices=["p2p", "nccl_bf16", "nccl_fp32"],
                    help="gradient reduction: the fused peer-memory kernel (p2p) or NCCL")
     p.add_argument("--sample-batch", type=int, default=8, help="prompts per GPU for the sampling measurement "
@@ -197,7 +200,7 @@ def run_ours(args):
     from dataclasses import replace
     den_cfg = replace(den_cfg, latent_size=args.res // 16)
     cfg = TrainConfig(global_batch=args.global_batch, micro_batch=args.micro_batch, steps=10 ** 6,
-                      grad_comm=args.grad_comm, moe_experts=8 if args.moe else 0)
+                      grad_comm=args.grad_comm, moe_experts=8 if args.moe else 0, muon_comm=args.muon_comm)
     tr = Trainer(den_cfg, te_cfg, cfg, device)
     per_rank = args.global_batch // world
     host, devb = synthetic_batch(per_rank, args.res, args.text_len, te_cfg.lm_dim, device, 1234 + rank)
@@ -230,7 +233,7 @@ def run_ours(args):
                       "params_denoiser": tr.n_params()[0], "params_text": tr.n_params()[1],
                       "global_batch": args.global_batch, "micro_batch": tr.micro, "seq_len": (args.res // 16) ** 2,
                       "text_len": args.text_len, "res": args.res, "parallelism": f"dp{world}",
-                      "optimizer": "muon(sharded)+adamw", "grad_comm": args.grad_comm,
+                      "optimizer": "muon(sharded)+adamw", "grad_comm": args.grad_comm, "muon_comm": args.muon_comm,
                       "moe": "8 experts top-2 hidden 4096 every other block, expert-parallel" if args.moe else None,
                       "l2": "inputs larger than L2 (no flush needed)"},
            "clocks": clocks, "gpu_launches": int(launches), "impl": "ours"}

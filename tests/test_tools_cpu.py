@@ -57,3 +57,43 @@ def test_train_merge_sample_export_chain(tmp_path):
     assert os.path.exists(os.path.join(so, "transformer", "diffusion_pytorch_model.safetensors"))
     # the export reloads through the directory path
     _py("sample_ckpt.py", so, "--out-dir", str(tmp_path / "s2"), "--steps", "1", "--prompt", "x")
+
+
+def test_export_import_roundtrip(tmp_path):
+    """train.py checkpoint -> export.py (diffusers layout) -> import_homeimg.py init checkpoint -> same weights; the
+    exported transformer loads strictly into the reference's Denoiser when the reference is installed."""
+    import json
+
+    from safetensors.torch import load_file
+    run = str(tmp_path / "run")
+    _py("train.py", "--synthetic", "32", "--out", run, "--size", "50m", "--te-size", "13m", "--batch", "2",
+        "--micro-batch", "2", "--steps", "2", "--eval-every", "0", "--no-wandb")
+    ex = str(tmp_path / "export")
+    _py("export.py", os.path.join(run, "latest.pt"), ex, "--time-shift", "3")
+    index = json.load(open(os.path.join(ex, "model_index.json")))
+    assert index["transformer"][1] == "AuroraDenoiser" and index["weights"] == "EMA"
+    tcfg = json.load(open(os.path.join(ex, "transformer", "config.json")))
+    assert tcfg["time_shift"] == 3.0 and tcfg["dim"] == 640
+    init = str(tmp_path / "init.pt")
+    _py("import_homeimg.py", ex, init)
+    ck = torch.load(os.path.join(run, "latest.pt"), weights_only=False)
+    ini = torch.load(init, weights_only=False)
+    den_params = list(ck["den"].keys())
+    n_te = len(ck["te"])
+    # the export holds the EMA: the imported live weights equal the checkpoint's EMA list
+    for i, k in enumerate(den_params):
+        assert torch.equal(ini["den"][k], ck["ema"][n_te + i])
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if os.path.isdir(os.path.join(ref, "aurora")):
+        sys.path.insert(0, ref)
+        try:
+            from aurora.model import Denoiser, DenoiserConfig as RefCfg
+            fields = {k: v for k, v in tcfg.items() if k in RefCfg.__dataclass_fields__}
+            Denoiser(RefCfg(**fields)).load_state_dict(
+                load_file(os.path.join(ex, "transformer", "diffusion_pytorch_model.safetensors")))
+        finally:
+            sys.path.remove(ref)
+    # the init checkpoint trains
+    _py("train.py", "--synthetic", "32", "--out", str(tmp_path / "run2"), "--init", init, "--size", "50m",
+        "--te-size", "13m", "--batch", "2",
+        "--micro-batch", "2", "--steps", "1", "--eval-every", "0", "--no-wandb")

@@ -79,6 +79,11 @@ def build_parser():
     a("--mlm-every", type=int, default=4)
     a("--mlm-prob", type=float, default=0.15)
     a("--grad-comm", choices=["fp32", "bf16"], default="bf16")
+    a("--grad-transport", choices=["auto", "nccl", "p2p"], default="auto",
+      help="bf16 gradient averaging through NCCL or the peer-memory kernel (auto: p2p on CUDA)")
+    a("--muon-comm", choices=["auto", "gather", "sharded"], default="auto",
+      help="sharded: Muon gradients reduce-scattered to their owners, updates all-gathered into the parameter "
+           "update (auto: sharded with bf16 gradients on CUDA)")
     a("--diloco", type=int, default=0)
     a("--outer-lr", type=float, default=0.7)
     a("--outer-momentum", type=float, default=0.9)
@@ -182,6 +187,11 @@ def main():
     if resume is not None:  # the checkpoint's architecture wins
         den_cfg = DenoiserConfig(**resume["den_config"])
         te_cfg = te_config_from_dict(resume["te_config"])
+    cuda = device.type == "cuda"
+    transport = args.grad_transport if args.grad_transport != "auto" else ("p2p" if cuda else "nccl")
+    grad_comm = "nccl_fp32" if args.grad_comm == "fp32" else ("p2p" if transport == "p2p" else "nccl_bf16")
+    muon_comm = args.muon_comm if args.muon_comm != "auto" else \
+        ("sharded" if cuda and args.grad_comm == "bf16" else "gather")
     tc = TrainConfig(global_batch=args.batch, micro_batch=args.micro_batch, steps=args.steps,
                      warmup=int(args.warmup_frac * args.steps), schedule=args.schedule, optimizer=args.optimizer,
                      lr_muon=args.lr_muon, lr_emb=args.lr_emb, lr_adam=args.lr_adam, lr_hidden=args.lr_hidden,
@@ -190,7 +200,7 @@ def main():
                      muon_gamma=args.muon_gamma, muon_momentum_dtype=args.muon_momentum_dtype, clip=args.clip,
                      ema=args.ema, cfg_drop=args.cfg_drop, t_shift=args.t_shift, mlm_weight=args.mlm_weight,
                      mlm_every=args.mlm_every, mlm_prob=args.mlm_prob,
-                     grad_comm="nccl_fp32" if args.grad_comm == "fp32" else "nccl_bf16", diloco=args.diloco,
+                     grad_comm=grad_comm, muon_comm=muon_comm, diloco=args.diloco,
                      outer_lr=args.outer_lr, outer_momentum=args.outer_momentum, outer_comm=args.outer_comm,
                      offload=args.offload, seed=args.seed, act_checkpoint=args.act_checkpoint,
                      random_lm=args.random_lm)
@@ -204,6 +214,7 @@ def main():
         if resume.get("opts"):
             for o, s in zip(tr.opts, resume["opts"]):
                 ckpt.load_opt_state(o, s)
+            tr.after_load()
         if tr.ema is not None and resume.get("ema"):
             for s, e in zip(tr.ema.shadow, resume["ema"]):
                 s.copy_(e.to(s.device))
@@ -251,6 +262,7 @@ def main():
     flops_sample = train_flops_per_sample(den_cfg, te_cfg, side * side)
 
     def save():
+        tr.before_save()  # collective: every rank takes part
         if not master:
             return
         ckpt.save_latest(ckpt_path, step, samples, den_cfg, te_cfg, te, den, tr.opts, tr.ema, vars(args),

@@ -146,4 +146,53 @@ cudaError_t allreduce_bf16_launch(const PeerAllReduceParams& p, int blocks, cuda
 cudaError_t peer_copy_launch(void* dst, const void* src, long long nbytes, uint32_t* dst_version,
                              unsigned long long* counter, uint32_t version, int blocks, cudaStream_t s);
 
+
+// Sharded Muon over peer memory (muon_comm.cu). Flag arrays: RS 2 x world x blocks words per rank (ready, done),
+// AG world x blocks words per rank; blocks x world <= kMuonMaxFlags.
+constexpr int kMuonMaxFlags = 1024;
+struct MuonRSParams {
+  const float* grads;                  // this rank's fp32 gradient bucket [n] (16-byte aligned)
+  long long n;
+  __nv_bfloat16* staging[kMaxPeers];   // every rank's bf16 staging (>= n elements)
+  uint32_t* flags[kMaxPeers];          // every rank's RS flag array
+  const long long* segs;               // [nsegs][3]: (bucket offset, owned-buffer offset, length) of my segments
+  int nsegs;
+  long long owned;                     // sum of the segment lengths
+  float* g_owned;                      // fp32 reduced gradients of my matrices
+  float scale;                         // 1 / world
+  float* sumsq;                        // += sum of squares of the reduced values (may be null)
+  int rank, world;
+  uint32_t epoch, prev_epoch;          // prev_epoch 0: no earlier launch to wait for
+  unsigned long long timeout_ns;
+  int* err;
+};
+struct MuonMomentumParams {
+  const float* g;                      // reduced gradients [n]
+  long long n;
+  float* buf_f32;                      // momentum, fp32 ...
+  __nv_bfloat16* buf_bf16;             // ... or bf16 with stochastic rounding (exactly one is non-null)
+  __nv_bfloat16* x_out;                // Newton-Schulz input [n]
+  const float* coef;                   // gradient-clip coefficient (device scalar: no host round trip)
+  float mu;                            // momentum
+  int nesterov;
+  unsigned long long seed;
+};
+struct MuonAGParams {
+  __nv_bfloat16* upd[kMaxPeers];       // every rank's update buffer (the whole Muon space)
+  uint32_t* flags[kMaxPeers];          // every rank's AG flag array
+  const long long* own;                // [nown][2]: (offset, length) of my owned ranges in the Muon space
+  int nown;
+  long long owned;
+  const long long* segs;               // [nsegs][4]: (fp32 param ptr, bf16 shadow ptr or 0, offset, length)
+  const float* coefs;                  // [nsegs][2]: (alpha, decay): p = p * decay + alpha * U
+  int nsegs;
+  int rank, world;
+  uint32_t epoch;
+  unsigned long long timeout_ns;
+  int* err;
+};
+cudaError_t muon_rs_launch(const MuonRSParams& p, int blocks, cudaStream_t s);
+cudaError_t muon_momentum_launch(const MuonMomentumParams& p, cudaStream_t s);
+cudaError_t muon_ag_apply_launch(const MuonAGParams& p, int blocks, cudaStream_t s);
+
 }  // namespace tgo

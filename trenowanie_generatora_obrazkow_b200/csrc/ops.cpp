@@ -524,6 +524,107 @@ void allreduce_bf16(at::Tensor grads, std::vector<int64_t> staging, std::vector<
   TGO_CHECK_LAUNCH(allreduce_bf16_launch(p, (int)blocks, at::cuda::getCurrentCUDAStream()));
 }
 
+// ---- sharded Muon over peer memory (muon_comm.cu) ----
+// A bf16 tensor over device memory this process allocated elsewhere (a peer-visible buffer); no ownership.
+at::Tensor tensor_from_ptr(int64_t ptr, int64_t n, int64_t device) {
+  return at::from_blob(reinterpret_cast<void*>(ptr), {n},
+                       at::TensorOptions().dtype(at::kBFloat16).device(at::kCUDA, (c10::DeviceIndex)device));
+}
+
+static void peer_list(const std::vector<int64_t>& v, int64_t world, const char* what) {
+  TORCH_CHECK(world >= 1 && world <= kMaxPeers && (int64_t)v.size() == world, what, ": one pointer per rank");
+}
+
+void muon_rs(at::Tensor grads, std::vector<int64_t> staging, std::vector<int64_t> flags, at::Tensor segs,
+             int64_t owned, at::Tensor g_owned, at::Tensor sumsq, int64_t rank, int64_t world, int64_t epoch,
+             int64_t prev_epoch, int64_t blocks, int64_t timeout_ns, at::Tensor err) {
+  TORCH_CHECK(grads.is_cuda() && grads.scalar_type() == at::kFloat && grads.is_contiguous(), "muon_rs: grads");
+  TORCH_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 3 &&
+              segs.is_contiguous(), "muon_rs: segs int64 [n, 3] on the device");
+  TORCH_CHECK(g_owned.scalar_type() == at::kFloat && g_owned.is_contiguous() && g_owned.numel() >= owned,
+              "muon_rs: g_owned");
+  TORCH_CHECK(sumsq.scalar_type() == at::kFloat && sumsq.numel() >= 1, "muon_rs: sumsq");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(grads.data_ptr()) % 16 == 0, "muon_rs: grads must be 16-byte aligned");
+  peer_list(staging, world, "muon_rs staging");
+  peer_list(flags, world, "muon_rs flags");
+  TORCH_CHECK(blocks >= 1 && blocks * world <= kMuonMaxFlags, "muon_rs: blocks");
+  const c10::cuda::CUDAGuard guard(grads.device());
+  MuonRSParams p{};
+  p.grads = grads.data_ptr<float>();
+  p.n = grads.numel();
+  for (int i = 0; i < world; ++i) {
+    p.staging[i] = reinterpret_cast<__nv_bfloat16*>(staging[i]);
+    p.flags[i] = reinterpret_cast<uint32_t*>(flags[i]);
+  }
+  p.segs = reinterpret_cast<const long long*>(segs.data_ptr<int64_t>());
+  p.nsegs = (int)segs.size(0);
+  p.owned = owned;
+  p.g_owned = g_owned.data_ptr<float>();
+  p.scale = 1.f / (float)world;
+  p.sumsq = sumsq.data_ptr<float>();
+  p.rank = (int)rank;
+  p.world = (int)world;
+  p.epoch = (uint32_t)epoch;
+  p.prev_epoch = (uint32_t)prev_epoch;
+  p.timeout_ns = (unsigned long long)timeout_ns;
+  p.err = err_ptr(err);
+  TGO_CHECK_LAUNCH(muon_rs_launch(p, (int)blocks, at::cuda::getCurrentCUDAStream()));
+}
+
+void muon_momentum(at::Tensor g, at::Tensor buf, at::Tensor x_out, at::Tensor coef, double mu, bool nesterov,
+                   int64_t seed) {
+  TORCH_CHECK(coef.is_cuda() && coef.scalar_type() == at::kFloat && coef.numel() == 1, "muon_momentum: coef");
+  TORCH_CHECK(g.is_cuda() && g.scalar_type() == at::kFloat && g.is_contiguous(), "muon_momentum: g");
+  TORCH_CHECK(buf.is_contiguous() && buf.numel() == g.numel() &&
+              (buf.scalar_type() == at::kFloat || buf.scalar_type() == at::kBFloat16), "muon_momentum: buf");
+  TORCH_CHECK(x_out.is_contiguous() && x_out.scalar_type() == at::kBFloat16 && x_out.numel() == g.numel(),
+              "muon_momentum: x_out");
+  const c10::cuda::CUDAGuard guard(g.device());
+  MuonMomentumParams p{};
+  p.g = g.data_ptr<float>();
+  p.n = g.numel();
+  if (buf.scalar_type() == at::kFloat) p.buf_f32 = buf.data_ptr<float>();
+  else p.buf_bf16 = bfp(buf);
+  p.x_out = bfp(x_out);
+  p.coef = coef.data_ptr<float>();
+  p.mu = (float)mu;
+  p.nesterov = nesterov ? 1 : 0;
+  p.seed = (unsigned long long)seed;
+  TGO_CHECK_LAUNCH(muon_momentum_launch(p, at::cuda::getCurrentCUDAStream()));
+}
+
+void muon_ag_apply(std::vector<int64_t> upd, std::vector<int64_t> flags, at::Tensor own, int64_t owned,
+                   at::Tensor segs, at::Tensor coefs, int64_t rank, int64_t world,
+                   int64_t epoch, int64_t blocks, int64_t timeout_ns, at::Tensor err) {
+  TORCH_CHECK(own.is_cuda() && own.scalar_type() == at::kLong && own.dim() == 2 && own.size(1) == 2 &&
+              own.is_contiguous(), "muon_ag_apply: own int64 [n, 2] on the device");
+  TORCH_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 4 &&
+              segs.is_contiguous(), "muon_ag_apply: segs int64 [n, 4] on the device");
+  TORCH_CHECK(coefs.is_cuda() && coefs.scalar_type() == at::kFloat && coefs.is_contiguous() &&
+              coefs.numel() == 2 * segs.size(0), "muon_ag_apply: coefs fp32 [n, 2] on the device");
+  peer_list(upd, world, "muon_ag_apply upd");
+  peer_list(flags, world, "muon_ag_apply flags");
+  TORCH_CHECK(blocks >= 1 && blocks * world <= kMuonMaxFlags, "muon_ag_apply: blocks");
+  const c10::cuda::CUDAGuard guard(own.device());
+  MuonAGParams p{};
+  for (int i = 0; i < world; ++i) {
+    p.upd[i] = reinterpret_cast<__nv_bfloat16*>(upd[i]);
+    p.flags[i] = reinterpret_cast<uint32_t*>(flags[i]);
+  }
+  p.own = reinterpret_cast<const long long*>(own.data_ptr<int64_t>());
+  p.nown = (int)own.size(0);
+  p.owned = owned;
+  p.segs = reinterpret_cast<const long long*>(segs.data_ptr<int64_t>());
+  p.coefs = coefs.data_ptr<float>();
+  p.nsegs = (int)segs.size(0);
+  p.rank = (int)rank;
+  p.world = (int)world;
+  p.epoch = (uint32_t)epoch;
+  p.timeout_ns = (unsigned long long)timeout_ns;
+  p.err = err_ptr(err);
+  TGO_CHECK_LAUNCH(muon_ag_apply_launch(p, (int)blocks, at::cuda::getCurrentCUDAStream()));
+}
+
 // src (contiguous CUDA tensor) -> dst (a peer's mapped buffer), then dst_version := version (see comm.cu)
 void peer_copy(int64_t dst, at::Tensor src, int64_t dst_version, int64_t counter, int64_t version, int64_t blocks) {
   TORCH_CHECK(src.is_cuda() && src.is_contiguous(), "peer_copy: contiguous CUDA source");
@@ -548,6 +649,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &tgo::ipc_close);
   m.def("peer_copy", &tgo::peer_copy, "NVLink copy into a peer's buffer + version word (weight snapshots)");
   m.def("allreduce_bf16", &tgo::allreduce_bf16, "fused cast + reduce-scatter + all-gather over peer memory");
+  m.def("tensor_from_ptr", &tgo::tensor_from_ptr, "bf16 view of raw device memory (not owned)");
+  m.def("muon_rs", &tgo::muon_rs, "sharded Muon: gradient bucket reduce-scatter to the matrix owners (NVLink)");
+  m.def("muon_momentum", &tgo::muon_momentum, "sharded Muon: owner momentum + Nesterov -> bf16 NS input");
+  m.def("muon_ag_apply", &tgo::muon_ag_apply, "sharded Muon: update all-gather fused with the parameter update");
   m.def("set_attention_tc", &tgo::set_attention_tc, "use the tcgen05 attention forward (default) or mma.sync");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");
   m.def("launch_count", &tgo::launch_count, "kernels launched by this extension so far");

@@ -18,8 +18,10 @@ from ..ops import fused as Fz
 
 
 class GradBuckets:
-    def __init__(self, params, bucket_bytes=256 * 2 ** 20, group=None, comm="nccl_bf16", overlap=True):
+    def __init__(self, params, bucket_bytes=256 * 2 ** 20, group=None, comm="nccl_bf16", overlap=True, reducer=None):
+        """``reducer(bucket_index, flat_fp32)`` replaces the all-reduce (e.g. the sharded-Muon reduce-scatter)."""
         self.params = [p for p in params if p.requires_grad]
+        self.reducer = reducer
         self.group = group
         # comm "none": local gradients only (DiLoCo inner steps)
         self.world = dist.get_world_size(group) if (dist.is_initialized() and comm != "none") else 1
@@ -53,6 +55,7 @@ class GradBuckets:
                 off += p.numel()
             self.flat.append(buf)
         self.pending = [0] * len(self.buckets)
+        self.next_launch = len(self.buckets)
         self.armed = False
         self.stream = torch.cuda.Stream(device=dev) if dev.type == "cuda" and self.overlap else None
         self.events = []
@@ -85,6 +88,7 @@ class GradBuckets:
     def arm(self):
         """Call before the backward of the last micro-batch: buckets reduce as their gradients complete."""
         self.pending = [len(ps) for ps in self.buckets]
+        self.next_launch = 0
         self.armed = True
         self.events = []
 
@@ -95,8 +99,10 @@ class GradBuckets:
         if bi is None:
             return
         self.pending[bi] -= 1
-        if self.pending[bi] == 0:
-            self._launch(bi)
+        # launch in bucket order, so every rank issues its collectives (or peer-memory launches) in the same order
+        while self.next_launch < len(self.buckets) and self.pending[self.next_launch] == 0:
+            self._launch(self.next_launch)
+            self.next_launch += 1
 
     def _launch(self, bi):
         buf = self.flat[bi]
@@ -105,15 +111,18 @@ class GradBuckets:
             ev.record()
             with torch.cuda.stream(self.stream):
                 self.stream.wait_event(ev)
-                self._reduce(buf)
+                self._reduce(buf, bi)
                 done = torch.cuda.Event()
                 done.record()
             self.events.append(done)
         else:
-            self._reduce(buf)
+            self._reduce(buf, bi)
 
-    def _reduce(self, buf):
+    def _reduce(self, buf, bi):
         if self.world == 1:
+            return
+        if self.reducer is not None:
+            self.reducer(bi, buf)
             return
         if self.p2p is not None:  # fused cast + reduce-scatter + all-gather over NVLink peer memory
             self.p2p(buf)
@@ -131,15 +140,15 @@ class GradBuckets:
             self.armed = False
             return
         if self.overlap:
-            for bi, n in enumerate(self.pending):
-                if n > 0:  # a parameter without a gradient this step (unused branch)
-                    self.pending[bi] = 0
-                    self._launch(bi)
+            while self.next_launch < len(self.buckets):  # buckets with a parameter that got no gradient this step
+                self.pending[self.next_launch] = 0
+                self._launch(self.next_launch)
+                self.next_launch += 1
             if self.stream is not None:
                 cur = torch.cuda.current_stream()
                 for ev in self.events:
                     cur.wait_event(ev)
         else:
-            for buf in self.flat:
-                self._reduce(buf)
+            for bi, buf in enumerate(self.flat):
+                self._reduce(buf, bi)
         self.armed = False

@@ -19,6 +19,7 @@ from ..models import build_models
 from ..models.frozen_lm import LM_NULL, LM_PAD, build_frozen_lm
 from ..models.text import LMTextEncoder
 from ..optim import EMA, build_optimizers, lr_mult, set_lr
+from ..optim.muon import Muon
 from ..parallel.ddp import GradBuckets
 from . import diloco as D
 from .flow import FlowModel, drop_captions, make_mlm
@@ -55,6 +56,7 @@ class TrainConfig:
     mlm_prob: float = 0.15
     grad_comm: str = "nccl_bf16"
     shard_muon: bool = True
+    muon_comm: str = "gather"     # "sharded": owner reduce-scatter + owner-only momentum/NS + fused update all-gather
     diloco: int = 0
     outer_lr: float = 0.7
     outer_momentum: float = 0.9
@@ -119,17 +121,30 @@ class Trainer:
         self.named = [(pre, n, p) for pre, mod in (("te", te), ("den", den)) for n, p in mod.named_parameters()]
         self.params = [p for _, _, p in self.named if p.requires_grad]
         reduce_grads = not cfg.diloco
-        self.buckets = None
         eids = {id(p) for p in self.expert_params}
-        if self.device.type == "cuda":  # expert-parallel weights are not replicated: never averaged
-            self.buckets = GradBuckets([p for p in self.params if id(p) not in eids], group=group,
-                                       comm=cfg.grad_comm if reduce_grads else "none")
         mdt = torch.bfloat16 if cfg.muon_momentum_dtype == "bf16" else None
         self.opts, self.counts = build_optimizers(
             self.named, optimizer=cfg.optimizer, lr_muon=cfg.lr_muon, lr_emb=cfg.lr_emb, lr_adam=cfg.lr_adam,
             lr_hidden=cfg.lr_hidden, lr_scale=lr_scale, wd=cfg.wd, beta2=cfg.beta2, momentum=cfg.momentum,
             ns_steps=cfg.ns_steps, cmuon=cfg.cmuon, muon_period=cfg.muon_period, muon_gamma=cfg.muon_gamma,
             momentum_dtype=mdt, shard=cfg.shard_muon and not cfg.diloco, group=group)
+        self.muon = next((o for o in self.opts if isinstance(o, Muon)), None)
+        self.muon_comm = None
+        self.buckets = self.muon_buckets = None
+        sharded = (cfg.muon_comm == "sharded" and self.muon is not None and reduce_grads and self.world > 1
+                   and self.muon.world == self.world)
+        if self.device.type == "cuda" or self.world > 1:  # expert-parallel weights are not replicated: never averaged
+            dense = [p for p in self.params if id(p) not in eids]
+            if sharded:
+                from ..parallel.muon_comm import MuonShardedComm
+                mids = {id(p) for g in self.muon.param_groups for p in g["params"]}
+                transport = "p2p" if cfg.grad_comm == "p2p" else "torch"
+                self.muon_comm = MuonShardedComm(self.muon, group=group, device=self.device, transport=transport)
+                self.muon_buckets = GradBuckets([p for p in dense if id(p) in mids], group=group,
+                                                comm="nccl_bf16", reducer=self.muon_comm.reduce_bucket)
+                self.muon_comm.attach_buckets(self.muon_buckets)
+                dense = [p for p in dense if id(p) not in mids]
+            self.buckets = GradBuckets(dense, group=group, comm=cfg.grad_comm if reduce_grads else "none")
         self.ema_decay = ema
         self.global_params = self.outer_opt = None
         if cfg.diloco:
@@ -147,6 +162,23 @@ class Trainer:
         self.last = {}
         if not self.lm_te:
             self.null_row = torch.as_tensor(te.null_ids(), device=self.device)
+
+    def before_save(self):
+        """All ranks: bring sharded optimizer state into the optimizers' state dicts (collective)."""
+        if self.muon_comm is not None:
+            self.muon_comm.export_momentum()
+
+    def after_load(self):
+        """All ranks, after the optimizers' ``load_state_dict``: take this rank's shards."""
+        if self.muon_comm is not None:
+            self.muon_comm.import_momentum()
+
+    def close(self):
+        for b in (self.buckets, self.muon_buckets):
+            if b is not None:
+                b.close()
+        if self.muon_comm is not None:
+            self.muon_comm.close()
 
     def n_params(self):
         return sum(p.numel() for p in self.den.parameters()), sum(p.numel() for p in self.te.parameters())
@@ -186,6 +218,9 @@ class Trainer:
         (device scalar); ``self.last`` holds the MLM loss and the gradient norm."""
         cfg = self.cfg
         x0_all = self._to_dev(batch["x0"])
+        if self.muon_buckets is not None:
+            self.muon_buckets.zero()
+            self.muon_comm.begin_step()
         if self.buckets is not None:
             self.buckets.zero()
         else:
@@ -207,6 +242,8 @@ class Trainer:
             eps = torch.randn(x0.shape, device=self.device, generator=self.gen)
             if self.buckets is not None and m == self.accum - 1:
                 self.buckets.arm()
+                if self.muon_buckets is not None:
+                    self.muon_buckets.arm()
             loss, l_fm, l_mlm, _ = self.model(x0, t, eps, **kw)
             (loss / self.accum).backward()
             acc += l_fm / self.accum
@@ -214,12 +251,29 @@ class Trainer:
                 acc_mlm += l_mlm / self.accum
         if self.buckets is not None:
             self.buckets.finish()
+        if self.muon_buckets is not None:
+            self.muon_buckets.finish()
         if self.expert_params and self.world > 1:  # their gradients summed every rank's loss: make it the mean
             torch._foreach_mul_([p.grad for p in self.expert_params if p.grad is not None], 1.0 / self.world)
-        self.last_gnorm = torch.nn.utils.clip_grad_norm_(self.params, cfg.clip, foreach=True)
+        coef = None
+        if self.muon_comm is None:
+            self.last_gnorm = torch.nn.utils.clip_grad_norm_(self.params, cfg.clip, foreach=True)
+        else:  # Muon gradients exist reduced only on their owners: norm = other grads + all-reduced owned squares
+            others = [p.grad for p in self.buckets.params if p.grad is not None] + \
+                [p.grad for p in self.expert_params if p.grad is not None]
+            sq = self.muon_comm.owned_sumsq().reshape(())
+            if others:
+                sq = sq + torch.stack(torch._foreach_norm(others)).square().sum()
+            self.last_gnorm = sq.sqrt()
+            coef = (cfg.clip / (self.last_gnorm + 1e-6)).clamp(max=1.0)
+            if others:
+                torch._foreach_mul_(others, coef)
         set_lr(self.opts, lr_mult(self.step_idx, cfg.steps, cfg.warmup, cfg.schedule))
         for o in self.opts:
-            o.step()
+            if o is self.muon and self.muon_comm is not None:
+                self.muon_comm.step(coef)
+            else:
+                o.step()
         self.step_idx += 1
         if cfg.diloco:
             if self.step_idx % cfg.diloco == 0 or self.step_idx == cfg.steps:
