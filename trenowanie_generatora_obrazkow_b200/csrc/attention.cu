@@ -245,7 +245,8 @@ __global__ void __launch_bounds__(FA_FWD_THREADS, 1) flash_fwd_kernel(AttnParams
 // backward preprocessing: delta[b, h, t] = sum_d dO * O
 // ------------------------------------------------------------------------------------------------------------------
 template <int HD>
-__global__ void flash_bwd_delta_kernel(AttnParams p, const bf16* __restrict__ dO, float* __restrict__ delta) {
+__global__ void flash_bwd_delta_kernel(AttnParams p, const bf16* __restrict__ dO, float* __restrict__ delta,
+                                       float* __restrict__ lse2) {
   const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp_id();
   const long long total = (long long)p.B * p.Tq * p.Hq;
   if (item >= total) return;
@@ -265,7 +266,11 @@ __global__ void flash_bwd_delta_kernel(AttnParams p, const bf16* __restrict__ dO
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) delta[((long long)b * p.Hq + h) * p.Tq + t] = s;
+  if (lane == 0) {
+    const long long idx = ((long long)b * p.Hq + h) * p.Tq + t;
+    delta[idx] = s;
+    if (lse2 != nullptr) lse2[idx] = p.lse[idx] * 1.4426950408889634f;  // log-sum-exp in base-2 units
+  }
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -523,7 +528,7 @@ static cudaError_t bwd_impl(const AttnParams& p, const bf16* dO, float* delta, f
                             cudaStream_t s) {
   {
     const long long items = (long long)p.B * p.Tq * p.Hq;
-    flash_bwd_delta_kernel<HD><<<(unsigned)((items + 7) / 8), 256, 0, s>>>(p, dO, delta);
+    flash_bwd_delta_kernel<HD><<<(unsigned)((items + 7) / 8), 256, 0, s>>>(p, dO, delta, nullptr);
   }
   cudaError_t e = cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)p.B * p.Tq * p.Hq * HD, s);
   if (e != cudaSuccess) return e;
@@ -547,10 +552,11 @@ static cudaError_t bwd_impl(const AttnParams& p, const bf16* dO, float* delta, f
 }
 
 // delta = rowsum(dO * O) and a zeroed dQ accumulator (shared by both backward kernels)
-cudaError_t attention_bwd_prep_launch(const AttnParams& p, const bf16* dO, float* delta, float* dq_acc, cudaStream_t s) {
+cudaError_t attention_bwd_prep_launch(const AttnParams& p, const bf16* dO, float* delta, float* dq_acc, cudaStream_t s,
+                                      float* lse2) {
   const long long items = (long long)p.B * p.Tq * p.Hq;
-  if (p.hd == 128) flash_bwd_delta_kernel<128><<<(unsigned)((items + 7) / 8), 256, 0, s>>>(p, dO, delta);
-  else if (p.hd == 64) flash_bwd_delta_kernel<64><<<(unsigned)((items + 7) / 8), 256, 0, s>>>(p, dO, delta);
+  if (p.hd == 128) flash_bwd_delta_kernel<128><<<(unsigned)((items + 7) / 8), 256, 0, s>>>(p, dO, delta, lse2);
+  else if (p.hd == 64) flash_bwd_delta_kernel<64><<<(unsigned)((items + 7) / 8), 256, 0, s>>>(p, dO, delta, lse2);
   else return cudaErrorInvalidValue;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

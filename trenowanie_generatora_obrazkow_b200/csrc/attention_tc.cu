@@ -1,16 +1,21 @@
 // Flash attention forward on the 5th-generation tensor cores (tcgen05 + TMEM), head dims 64 and 128.
 //
-// CTA = 128 query rows of one (batch, head); 192 threads:
-//   warp 0        TMA loads: Q once, then K / V tiles of 64 keys into a 2-stage ring
-//   warp 1        TMEM allocation (256 columns) and the single MMA-issuing thread:
-//                   S_j = Q K_j^T  (M 128, N 64, K hd)  -> TMEM, double buffered (columns 0 / 64)
-//                   O  += P_j V_j  (M 128, N hd, K 64)  -> TMEM columns 128 .. 128 + hd
-//   warps 2-5     softmax: thread = query row = TMEM lane; reads its S row (tcgen05.ld), online softmax in
-//                 exp2 form, writes P (bf16) into a 128-byte-swizzled shared tile the next MMA reads as its A
-//                 operand; rescales its O row in TMEM only when its running max grew by more than 2^8 (the
-//                 stale max is used consistently, so the result is exact); final O / l and log-sum-exp.
-// S_{j+1} is issued before P_j V_j, so the tensor core works on the next tile while the softmax warps work on
-// this one; two CTAs per SM (112 KB shared, 256 TMEM columns each) interleave as well.
+// CTA = two tiles of 128 query rows of one (batch, head); 320 threads, one CTA per SM:
+//   warp 0        TMA loads: both Q tiles once, then K and V tiles of 64 keys into 4-stage rings with their own
+//                 barriers (K_{j+1} is requested before V_j: a K tile is free once S of both Q tiles is computed,
+//                 a V tile only after both P V products)
+//   warp 1        TMEM allocation (512 columns) and the single MMA-issuing thread, per K / V tile j:
+//                   S_g(j+1) = Q_g K_{j+1}^T  (M 128, N 64, K hd) -> TMEM, two buffers per Q tile (g * 128 + 0 / 64)
+//                   O_g += P_g(j) V_j          (M 128, N hd, K 64) -> TMEM 256 + g * hd, P read from TMEM
+//   warps 2-5/6-9 softmax of Q tile 0 / 1: thread = query row = TMEM lane; reads its S row (tcgen05.ld), online
+//                 softmax in exp2 form, writes P (bf16 pairs) back over the first 32 columns of its S buffer
+//                 (tcgen05.st), where the P V MMA reads it as its A operand; rescales its O row in TMEM only when
+//                 its running max grew by more than 2^8 (the stale max is used consistently, so the result is
+//                 exact); before writing P it waits for the previous P V of its tile (see the note at the store);
+//                 final O / l and log-sum-exp.
+// S(j+1) is issued before P(j) V_j, so the tensor core works on the next tile while the softmax warps work on this
+// one; the two Q tiles share every K / V tile (half the L2 traffic per FLOP of one tile per CTA) and the 4-stage
+// rings keep three tiles of loads in flight.
 // Key masking by per-sample valid length; grouped-query attention by head mapping. Output and LSE layout match
 // the mma.sync kernel in attention.cu, so the backward there consumes them unchanged.
 #include <algorithm>
@@ -22,13 +27,31 @@ namespace tgo {
 
 namespace {
 
-constexpr int TQ = 128;      // query rows per CTA
-constexpr int TK = 64;       // keys per tile
-constexpr int THREADS = 192;
-constexpr int TMEM_COLS = 256;
-constexpr int S_COL = 0;     // S buffers at columns 0 and 64
-constexpr int O_COL = 128;   // O at columns 128 .. 128 + hd
+constexpr int TQ = 128;      // query rows per Q tile (one softmax warpgroup)
+constexpr int NQ = 2;        // Q tiles per CTA
+constexpr int TK = 64;       // keys per K / V tile
+constexpr int KV_STAGES = 4; // K and V rings
+constexpr int THREADS = 320; // warp 0 TMA, warp 1 MMA, warps 2-5 softmax of Q tile 0, warps 6-9 of Q tile 1
+constexpr int TMEM_COLS = 512;
+constexpr int O_COL = 256;   // Q tile g: S buffers at g * 128 + {0, 64}; O at 256 + g * hd
 constexpr float kRescaleThreshold = 8.f;  // log2 units
+
+// Optional per-phase timeline of one CTA (clock64 per event and iteration), for profiling the pipelines: off
+// unless attention_set_trace() installed a buffer. Slot = event * 64 + (iteration & 63).
+struct TraceCfg {
+  long long* buf;
+  int cta;
+};
+__device__ TraceCfg g_attn_trace;
+__device__ __forceinline__ bool trace_this_cta() {
+  const TraceCfg t = g_attn_trace;
+  return t.buf != nullptr &&
+         (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) == t.cta;
+}
+#define ATTN_TRACE(on, ev, it)                                                  \
+  do {                                                                          \
+    if (on) g_attn_trace.buf[(ev) * 64 + ((it) & 63)] = (long long)clock64();   \
+  } while (0)
 
 __device__ __forceinline__ float ex2(float x) {  // hardware 2^x (MUFU)
   float y;
@@ -38,25 +61,23 @@ __device__ __forceinline__ float ex2(float x) {  // hardware 2^x (MUFU)
 
 template <int HD>
 struct FwdSmem {
-  static constexpr int Q_BYTES = TQ * HD * 2;          // HD / 64 blocks of 128 rows x 128 B
+  static constexpr int Q_BYTES = TQ * HD * 2;          // per Q tile: HD / 64 blocks of 128 rows x 128 B
   static constexpr int KV_BYTES = TK * HD * 2;         // HD / 64 blocks of 64 rows x 128 B
-  static constexpr int P_BYTES = TQ * TK * 2;          // 128 rows x 128 B
   static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = Q_OFF + Q_BYTES;
-  static constexpr int V_OFF = K_OFF + 2 * KV_BYTES;
-  static constexpr int P_OFF = V_OFF + 2 * KV_BYTES;
-  static constexpr int BAR_OFF = P_OFF + P_BYTES;
-  static constexpr int TOTAL = BAR_OFF + 256;
+  static constexpr int K_OFF = Q_OFF + NQ * Q_BYTES;
+  static constexpr int V_OFF = K_OFF + KV_STAGES * KV_BYTES;
+  static constexpr int BAR_OFF = V_OFF + KV_STAGES * KV_BYTES;
+  static constexpr int TOTAL = BAR_OFF + 512;
 };
 
 struct FwdBars {
   uint64_t q_full;
-  uint64_t kv_full[2];
-  uint64_t kv_empty[2];
-  uint64_t s_full[2];
-  uint64_t s_empty[2];
-  uint64_t p_full;
-  uint64_t pv_done;
+  uint64_t k_full[KV_STAGES], k_empty[KV_STAGES];  // K tile free once S of both Q tiles is computed
+  uint64_t v_full[KV_STAGES], v_empty[KV_STAGES];  // V tile free once P V of both Q tiles is computed
+  uint64_t s_full[NQ][2];                          // S_j of Q tile g in TMEM buffer j & 1
+  uint64_t s_free[NQ][2];                          // P V of the tile that last used the buffer finished
+  uint64_t p_full[NQ][2];                          // softmax wrote P_j over S_j: 128 arrivals
+  uint64_t pv_done[NQ];                            // one phase per P V
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -64,10 +85,11 @@ struct FwdBars {
 }  // namespace
 
 template <int HD>
-__global__ void __launch_bounds__(THREADS, 2)
+__global__ void __launch_bounds__(THREADS, 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, AttnParams p, int* err) {
   using L = FwdSmem<HD>;
+  static_assert(sizeof(FwdBars) <= 512, "barrier block");
   extern __shared__ __align__(1024) uint8_t smem[];
   FwdBars* bars = reinterpret_cast<FwdBars*>(smem + L::BAR_OFF);
   const int warp = warp_id(), lane = lane_id();
@@ -77,21 +99,27 @@ __global__ void __launch_bounds__(THREADS, 2)
   }
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / p.rep;
-  const int q0 = qb * TQ;
+  const int q0 = qb * (NQ * TQ);
   int kv_end = p.Tk;
   if (p.kv_len != nullptr) kv_end = min(kv_end, p.kv_len[b]);
   const int n_tiles = max(0, (kv_end + TK - 1) / TK);
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->kv_full[i], 1);
-      mbar_init(&bars->kv_empty[i], 1);
-      mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->s_empty[i], 128);
+    for (int i = 0; i < KV_STAGES; ++i) {
+      mbar_init(&bars->k_full[i], 1);
+      mbar_init(&bars->k_empty[i], 1);
+      mbar_init(&bars->v_full[i], 1);
+      mbar_init(&bars->v_empty[i], 1);
     }
-    mbar_init(&bars->p_full, 128);
-    mbar_init(&bars->pv_done, 1);
+    for (int g = 0; g < NQ; ++g) {
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&bars->s_full[g][i], 1);
+        mbar_init(&bars->s_free[g][i], 1);
+        mbar_init(&bars->p_full[g][i], 128);
+      }
+      mbar_init(&bars->pv_done[g], 1);
+    }
     bars->abort_flag = 0;
     fence_barrier_init();
   }
@@ -104,53 +132,80 @@ __global__ void __launch_bounds__(THREADS, 2)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   volatile int* abort_flag = &bars->abort_flag;
+  const bool tr = trace_this_cta();
 
   if (warp == 0) {
     if (lane == 0 && n_tiles > 0) {
-      // ---------------- TMA loads ----------------
+      // ---------------- TMA loads: both Q tiles, then K_{j+1} ahead of V_j ----------------
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      mbar_expect_tx(&bars->q_full, L::Q_BYTES);
+      mbar_expect_tx(&bars->q_full, NQ * L::Q_BYTES);
 #pragma unroll
-      for (int blk = 0; blk < HD / 64; ++blk)
-        tma_load_4d(smem + L::Q_OFF + blk * TQ * 128, &tmQ, &bars->q_full, blk * 64, q0, h, b);
-      for (int j = 0; j < n_tiles && !*abort_flag; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&bars->kv_empty[st], ((j >> 1) & 1) ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
-          *abort_flag = 1;
+      for (int g = 0; g < NQ; ++g)
+#pragma unroll
+        for (int blk = 0; blk < HD / 64; ++blk)
+          tma_load_4d(smem + L::Q_OFF + g * L::Q_BYTES + blk * TQ * 128, &tmQ, &bars->q_full, blk * 64,
+                      q0 + g * TQ, h, b);
+      auto load_k = [&](int j) -> bool {
+        const int st = j % KV_STAGES, ph = (j / KV_STAGES) & 1;
+        if (!mbar_wait(&bars->k_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) return false;
+        mbar_expect_tx(&bars->k_full[st], L::KV_BYTES);
+#pragma unroll
+        for (int blk = 0; blk < HD / 64; ++blk)
+          tma_load_4d(smem + L::K_OFF + st * L::KV_BYTES + blk * TK * 128, &tmK, &bars->k_full[st], blk * 64,
+                      j * TK, hk, b);
+        return true;
+      };
+      bool ok = load_k(0);
+      for (int j = 0; j < n_tiles && ok && !*abort_flag; ++j) {
+        if (j + 1 < n_tiles && !load_k(j + 1)) {
+          ok = false;
           break;
         }
-        mbar_expect_tx(&bars->kv_full[st], 2 * L::KV_BYTES);
-#pragma unroll
-        for (int blk = 0; blk < HD / 64; ++blk) {
-          tma_load_4d(smem + L::K_OFF + st * L::KV_BYTES + blk * TK * 128, &tmK, &bars->kv_full[st], blk * 64,
-                      j * TK, hk, b);
-          tma_load_4d(smem + L::V_OFF + st * L::KV_BYTES + blk * TK * 128, &tmV, &bars->kv_full[st], blk * 64,
-                      j * TK, hk, b);
+        const int st = j % KV_STAGES, ph = (j / KV_STAGES) & 1;
+        if (!mbar_wait(&bars->v_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
         }
+        ATTN_TRACE(tr, 16, j);
+        mbar_expect_tx(&bars->v_full[st], L::KV_BYTES);
+#pragma unroll
+        for (int blk = 0; blk < HD / 64; ++blk)
+          tma_load_4d(smem + L::V_OFF + st * L::KV_BYTES + blk * TK * 128, &tmV, &bars->v_full[st], blk * 64,
+                      j * TK, hk, b);
       }
+      if (!ok) *abort_flag = 1;
     }
   } else if (warp == 1) {
     if (lane == 0 && n_tiles > 0) {
-      // ---------------- MMA issue ----------------
+      // ---------------- MMA issue: S_0(j+1), S_1(j+1), then P_0 V_j, P_1 V_j ----------------
       constexpr uint32_t idesc_s = idesc_bf16_f32(TQ, TK, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(TQ, HD, false, true);
-      const uint32_t sq = smem_u32(smem + L::Q_OFF);
-      const uint32_t sp = smem_u32(smem + L::P_OFF);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&bars->kv_full[st], (j >> 1) & 1, err, ERR_MBAR_TIMEOUT_MMA)) return false;
-        if (!mbar_wait(&bars->s_empty[st], ((j >> 1) & 1) ^ 1, err, ERR_MBAR_TIMEOUT_MMA)) return false;
-        tc_fence_after();
-        const uint32_t sk = smem_u32(smem + L::K_OFF + st * L::KV_BYTES);
+      // precomputed descriptors (constant offsets are added per MMA)
+      const uint64_t q_desc0 = sdesc_sw128(smem_u32(smem + L::Q_OFF), 16, 1024);
+      const uint64_t k_desc0 = sdesc_sw128(smem_u32(smem + L::K_OFF), 16, 1024);
+      const uint64_t v_desc0 = sdesc_sw128(smem_u32(smem + L::V_OFF), TK * 128, 1024);
+      auto issue_s = [&](int j) -> bool {  // S_g(j) = Q_g K_j^T for both Q tiles
+        const int ks = j % KV_STAGES, st = j & 1;
+        if (!mbar_wait(&bars->k_full[ks], (j / KV_STAGES) & 1, err, ERR_MBAR_TIMEOUT_MMA)) return false;
+        ATTN_TRACE(tr, 18, j);
+        const uint64_t kd = sdesc_add(k_desc0, ks * L::KV_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t blk = kk >> 2, sub = (kk & 3) * 32;
-          umma_f16(tmem + S_COL + st * TK, sdesc_sw128(sq + blk * TQ * 128 + sub, 16, 1024),
-                   sdesc_sw128(sk + blk * TK * 128 + sub, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        for (int g = 0; g < NQ; ++g) {
+          if (!mbar_wait(&bars->s_free[g][st], ((j >> 1) & 1) ^ 1, err, ERR_MBAR_TIMEOUT_MMA)) return false;
+          tc_fence_after();
+          const uint32_t d = tmem + g * 128 + st * TK;
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t blk = kk >> 2, sub = (kk & 3) * 32;
+            umma_f16(d, sdesc_add(q_desc0, g * L::Q_BYTES + blk * TQ * 128 + sub),
+                     sdesc_add(kd, blk * TK * 128 + sub), idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&bars->s_full[g][st]);
         }
-        umma_commit(&bars->s_full[st]);
+        umma_commit(&bars->k_empty[ks]);
+        ATTN_TRACE(tr, 20, j);
         return true;
       };
       bool ok = mbar_wait(&bars->q_full, 0, err, ERR_MBAR_TIMEOUT_MMA) && issue_s(0);
@@ -159,62 +214,84 @@ __global__ void __launch_bounds__(THREADS, 2)
           ok = false;
           break;
         }
-        if (!mbar_wait(&bars->p_full, j & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
+        const int ks = j % KV_STAGES, st = j & 1;
+        if (!mbar_wait(&bars->v_full[ks], (j / KV_STAGES) & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t sv = smem_u32(smem + L::V_OFF + (j & 1) * L::KV_BYTES);
+        const uint64_t vd = sdesc_add(v_desc0, ks * L::KV_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < TK / 16; ++kk)
-          umma_f16(tmem + O_COL, sdesc_sw128(sp + kk * 32, 16, 1024), sdesc_sw128(sv + kk * 2048, TK * 128, 1024),
-                   idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&bars->kv_empty[j & 1]);
-        umma_commit(&bars->pv_done);
+        for (int g = 0; g < NQ && ok; ++g) {
+          if (!mbar_wait(&bars->p_full[g][st], (j >> 1) & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          ATTN_TRACE(tr, 21 + g, j);
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < TK / 16; ++kk)  // O_g += P_g V_j, P read from TMEM (8 columns per 16 keys)
+            umma_f16_tmem_a(tmem + O_COL + g * HD, tmem + g * 128 + st * TK + kk * 8, sdesc_add(vd, kk * 2048),
+                            idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&bars->s_free[g][st]);
+          umma_commit(&bars->pv_done[g]);
+        }
+        if (ok) umma_commit(&bars->v_empty[ks]);
       }
       if (!ok) *abort_flag = 1;
     }
   } else {
-    // ---------------- softmax / epilogue ----------------
+    // ---------------- softmax / epilogue of Q tile g ----------------
+    const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // TMEM lane == query row within the tile
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_base = tmem + lane_base + g * 128, o_base = tmem + lane_base + O_COL + g * HD;
     const float sl2 = p.scale * 1.4426950408889634f;
+    const bool tw = tr && (threadIdx.x == 64 + g * 128);
     float m = -INFINITY, l = 0.f;
-    uint8_t* prow = smem + L::P_OFF + row * 128;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int st = j & 1;
       int w_ok = 1;
-      if (lane == 0) w_ok = mbar_wait(&bars->s_full[st], (j >> 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
+      if (lane == 0) w_ok = mbar_wait(&bars->s_full[g][st], (j >> 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
       w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
       if (!w_ok) {
         ok = false;
         break;
       }
+      ATTN_TRACE(tw, 23 + 4 * g, j);
       __syncwarp();
       tc_fence_after();
       uint32_t sr[2][32];
-      tmem_ld_32x32b_x32(tmem + lane_base + S_COL + st * TK, sr[0]);
-      tmem_ld_32x32b_x32(tmem + lane_base + S_COL + st * TK + 32, sr[1]);
+      tmem_ld_32x32b_x32(s_base + st * TK, sr[0]);
+      tmem_ld_32x32b_x32(s_base + st * TK + 32, sr[1]);
       tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&bars->s_empty[st]);
+      ATTN_TRACE(tw, 24 + 4 * g, j);
+      // raw logits: the running max m is kept in log2 units (sl2 > 0, so max and scaling commute) and
+      // p = 2^(s sl2 - m) is one FFMA + ex2 per element; keys past kv_end exist only in the last tile
       const int kbase = j * TK;
       float smax = -INFINITY;
+      if (kbase + TK <= kv_end) {
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = kbase + c * 32 + i;
-          float v = __uint_as_float(sr[c][i]) * sl2;
-          if (key >= kv_end) v = -INFINITY;
-          sr[c][i] = __float_as_uint(v);
-          smax = fmaxf(smax, v);
-        }
-      // PV_{j-1} must be complete before P is overwritten and before O is touched
-      if (j > 0) {
-        if (lane == 0) w_ok = mbar_wait(&bars->pv_done, (j - 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
+          for (int i = 0; i < 32; ++i) smax = fmaxf(smax, __uint_as_float(sr[c][i]));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (kbase + c * 32 + i >= kv_end) sr[c][i] = __float_as_uint(-INFINITY);
+            smax = fmaxf(smax, __uint_as_float(sr[c][i]));
+          }
+      }
+      smax *= sl2;
+      const float m_new = fmaxf(m, smax);
+      const bool need = (j > 0) && (m_new > m + kRescaleThreshold);
+      bool waited = false;
+      if (__any_sync(0xffffffffu, need)) {
+        // rescale this warp's O rows to the new running max; P V of the previous tile must have finished
+        if (lane == 0) w_ok = mbar_wait(&bars->pv_done[g], (j - 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
         w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
         if (!w_ok) {
           ok = false;
@@ -222,20 +299,17 @@ __global__ void __launch_bounds__(THREADS, 2)
         }
         __syncwarp();
         tc_fence_after();
-      }
-      const float m_new = fmaxf(m, smax);
-      const bool need = (j > 0) && (m_new > m + kRescaleThreshold);
-      if (__any_sync(0xffffffffu, need)) {
-        // rescale this warp's O rows to the new running max
+        waited = true;
+        ATTN_TRACE(tw, 25 + 4 * g, j);
         const float corr = (m == -INFINITY) ? 0.f : ex2(m - m_new);
 #pragma unroll 1
         for (int c = 0; c < HD / 32; ++c) {
           uint32_t o[32];
-          tmem_ld_32x32b_x32(tmem + lane_base + O_COL + c * 32, o);
+          tmem_ld_32x32b_x32(o_base + c * 32, o);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
-          tmem_st_32x32b_x32(tmem + lane_base + O_COL + c * 32, o);
+          tmem_st_32x32b_x32(o_base + c * 32, o);
         }
         tmem_st_wait();
         l *= corr;
@@ -244,40 +318,49 @@ __global__ void __launch_bounds__(THREADS, 2)
         m = m_new;
       }
       const float mu = (m == -INFINITY) ? 0.f : m;
-      float rs = 0.f;
+      float rs0 = 0.f, rs1 = 0.f;
+      uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {  // 8 keys -> one 16-byte chunk
-          uint32_t pk[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float a = ex2(__uint_as_float(sr[c][ch * 8 + 2 * e]) - mu);
-            const float bq = ex2(__uint_as_float(sr[c][ch * 8 + 2 * e + 1]) - mu);
-            __nv_bfloat162 pr = __floats2bfloat162_rn(a, bq);
-            const float2 back = __bfloat1622float2(pr);
-            rs += back.x + back.y;
-            pk[e] = *reinterpret_cast<uint32_t*>(&pr);
-          }
-          const int chunk = c * 4 + ch;
-          *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        for (int e = 0; e < 16; ++e) {
+          const float a = ex2(fmaf(__uint_as_float(sr[c][2 * e]), sl2, -mu));
+          const float bq = ex2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, -mu));
+          rs0 += a;
+          rs1 += bq;
+          pk[c * 16 + e] = pack_bf16x2(a, bq);
         }
       }
+      const float rs = rs0 + rs1;
       l += rs;
-      fence_proxy_async_smem();
+      // No tcgen05.st while this tile's previous P V (an MMA reading its A operand from these TMEM lanes) is in
+      // flight: with that overlap the products came out wrong on B200, so wait for it here, after the exponentials.
+      if (j > 0 && !waited) {
+        if (lane == 0) w_ok = mbar_wait(&bars->pv_done[g], (j - 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
+        w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+        if (!w_ok) {
+          ok = false;
+          break;
+        }
+        __syncwarp();
+        tc_fence_after();
+      }
+      tmem_st_32x32b_x32(s_base + st * TK, pk);  // P_j over the first 32 columns of S_j
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars->p_full);
+      ATTN_TRACE(tw, 26 + 4 * g, j);
+      mbar_arrive(&bars->p_full[g][st]);
     }
     // epilogue: O / l -> bf16, log-sum-exp
     if (ok && n_tiles > 0) {
       int w_ok = 1;
-      if (lane == 0) w_ok = mbar_wait(&bars->pv_done, (n_tiles - 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
+      if (lane == 0) w_ok = mbar_wait(&bars->pv_done[g], (n_tiles - 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
       w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
       ok = w_ok != 0;
       __syncwarp();
       tc_fence_after();
     }
-    const int t = q0 + row;
+    const int t = q0 + g * TQ + row;
     const float inv = (l > 0.f) ? 1.f / l : 0.f;
     if (ok) {
       __nv_bfloat16* dst = p.o + (long long)b * p.o_bs + (long long)t * p.o_ts + (long long)h * p.o_hs;
@@ -285,7 +368,7 @@ __global__ void __launch_bounds__(THREADS, 2)
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
         if (n_tiles > 0) {
-          tmem_ld_32x32b_x32(tmem + lane_base + O_COL + c * 32, o);
+          tmem_ld_32x32b_x32(o_base + c * 32, o);
           tmem_ld_wait();
         } else {
 #pragma unroll
@@ -327,7 +410,7 @@ static cudaError_t fwd_tc_impl(const CUtensorMap& tq, const CUtensorMap& tk, con
     cudaFuncSetAttribute(flash_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
     set = true;
   }
-  dim3 grid((p.Tq + TQ - 1) / TQ, p.Hq, p.B);
+  dim3 grid((p.Tq + NQ * TQ - 1) / (NQ * TQ), p.Hq, p.B);
   flash_fwd_tc_kernel<HD><<<grid, THREADS, L::TOTAL, s>>>(tq, tk, tv, p, err);
   return cudaGetLastError();
 }
@@ -347,42 +430,47 @@ cudaError_t attention_fwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk
 // Per iteration (Q_i, dO_i: 64 queries):
 //   MMA1  S^T  = K Q_i^T          M 128 keys, N 64, K 128      TMEM cols   0 ..  63
 //   MMA2  dP^T = V dO_i^T         M 128 keys, N 64, K 128      TMEM cols  64 .. 127
-//   softmax warps (thread = key): P^T = 2^(S^T scale log2e - lse log2e), dS^T = P^T (dP^T - delta) -> bf16 tiles
-//   MMA3  dV  += P^T dO_i         M 128 keys, N 128, K 64      TMEM cols 256 .. 383
+//   softmax warps (thread = key): P^T = 2^(S^T scale log2e - lse log2e) -> bf16 pairs into TMEM (cols 192 + 32 b),
+//                                 dS^T = P^T (dP^T - delta) -> bf16 K-major shared tile (double buffered)
+//   MMA3  dV  += P^T dO_i         M 128 keys, N 128, K 64      A from TMEM, TMEM cols 256 .. 383
 //   MMA4  dK  += dS^T Q_i         M 128 keys, N 128, K 64      TMEM cols 384 .. 511
 //   MMA5  dQ^T = K^T dS^T         M 128 (head dim), N 64, K 128 keys   TMEM cols 128 .. 191
-//   dQ warps (thread = head-dim lane): dQ^T row -> scale -> red.global.add into the fp32 dQ accumulator
-// Operand majors: K / V / Q / dO tiles are TMA-loaded once in the [token][head_dim] layout and read K-major or
-// MN-major as each product needs; P^T / dS^T are written K-major (queries contiguous) and double buffered, so the
-// softmax of iteration i+1 overlaps MMA3-5 of iteration i, and MMA1/2 of iteration i+1 overlap the softmax of i.
-// Warps: 0 TMA, 1 MMA (+ TMEM), 2-5 softmax + final dK / dV, 6-9 dQ drain.
+//   dQ warps (thread = head-dim lane): dQ^T -> scale -> fp32 [query][head dim] shared tiles -> TMA reduce-add into
+//                                      the fp32 dQ accumulator (cp.reduce.async.bulk.tensor, two 32-query halves)
+// Q / dO tiles (and the tile's lse / delta rows, bulk-copied) stream through a 3-stage ring released by MMA3-5, so the
+// loads run two iterations ahead. The softmax of iteration i+1 overlaps MMA3-5 of iteration i, except for its
+// P^T store, which waits for them (a tcgen05.st into the TMEM lanes that an in-flight MMA reads its A operand from
+// gave wrong products on B200; see the forward kernel). MMA1/2 of iteration i+1 are issued before MMA3-5 of i.
+// Warps: 0 TMA, 1 MMA (+ TMEM), 2-9 softmax (two warps per TMEM lane quarter, 32 queries each) + final dV / dK,
+// 10-13 dQ drain. The softmax reads lse in base-2 units (lse2 = lse log2 e, written by the delta kernel).
 // ==================================================================================================================
 namespace {
 
 constexpr int BK_KEYS = 128;
 constexpr int BQ = 64;
-constexpr int BWD_THREADS = 320;
+constexpr int BWD_THREADS = 448;  // warp 0 TMA, 1 MMA, 2-9 softmax (two per TMEM lane quarter), 10-13 dQ
+constexpr int QST = 3;  // Q / dO ring stages
 
 struct BwdSmem {  // head dim 128
   static constexpr int K_OFF = 0;                              // 2 blocks x 128 rows x 128 B
   static constexpr int V_OFF = K_OFF + 32768;
-  static constexpr int Q_OFF = V_OFF + 32768;                  // 2 stages x (2 blocks x 64 rows x 128 B)
-  static constexpr int DO_OFF = Q_OFF + 2 * 16384;
-  static constexpr int PT_OFF = DO_OFF + 2 * 16384;            // 2 buffers x 128 rows x 128 B
-  static constexpr int DS_OFF = PT_OFF + 2 * 16384;
-  static constexpr int STAT_OFF = DS_OFF + 2 * 16384;          // lse / delta: 2 slots x 2 x 64 floats
-  static constexpr int BAR_OFF = STAT_OFF + 1024;
+  static constexpr int Q_OFF = V_OFF + 32768;                  // QST stages x (2 blocks x 64 rows x 128 B)
+  static constexpr int DO_OFF = Q_OFF + QST * 16384;
+  static constexpr int DS_OFF = DO_OFF + QST * 16384;          // 2 buffers x 128 rows x 128 B
+  static constexpr int DQ_OFF = DS_OFF + 2 * 16384;            // 2 halves x 32 queries x 128 fp32
+  static constexpr int STAT_OFF = DQ_OFF + 32768;              // QST slots x (lse[64], delta[64]) fp32
+  static constexpr int BAR_OFF = STAT_OFF + QST * 512;
   static constexpr int TOTAL = BAR_OFF + 256;
 };
 
 struct BwdBars {
   uint64_t kv_full;
-  uint64_t q_full[2];
-  uint64_t q_empty[2];
+  uint64_t q_full[QST];
+  uint64_t q_empty[QST];
   uint64_t s_full;
   uint64_t s_empty;
-  uint64_t p_full[2];
-  uint64_t p_empty[2];
+  uint64_t p_full;      // softmax wrote P^T (TMEM) and dS^T (shared): 128 arrivals
+  uint64_t mma_done;    // MMA3-5 of an iteration completed (one phase per iteration)
   uint64_t dq_full;
   uint64_t dq_empty;
   uint64_t acc_done;
@@ -390,7 +478,8 @@ struct BwdBars {
   int abort_flag;
 };
 
-__device__ __forceinline__ void softmax_group_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void softmax_group_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void drain_group_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   int ok = 1;
@@ -405,14 +494,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     flash_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                        AttnParams p, const float* __restrict__ delta, float* __restrict__ dq_acc,
-                        __nv_bfloat16* __restrict__ dk, long long dk_bs, long long dk_ts, long long dk_hs,
+                        const __grid_constant__ CUtensorMap tmdQ, AttnParams p, const float* __restrict__ delta,
+                        const float* __restrict__ lse2, __nv_bfloat16* __restrict__ dk, long long dk_bs, long long dk_ts, long long dk_hs,
                         __nv_bfloat16* __restrict__ dv, long long dv_bs, long long dv_ts, long long dv_hs, int* err) {
   constexpr int HD = 128;
   using L = BwdSmem;
+  static_assert(L::TOTAL <= 232448, "shared memory");
   extern __shared__ __align__(1024) uint8_t smem[];
   BwdBars* bars = reinterpret_cast<BwdBars*>(smem + L::BAR_OFF);
-  float* stat = reinterpret_cast<float*>(smem + L::STAT_OFF);  // [slot][0: lse*log2e | 1: delta][64]
   const int warp = warp_id(), lane = lane_id();
   if ((smem_u32(smem) & 1023) != 0) {
     if (threadIdx.x == 0) record_error(err, ERR_BAD_ARGS);
@@ -425,17 +514,18 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   const bool active = k0 < kv_end;
   const int n_qt = (p.Tq + BQ - 1) / BQ;
   const int n_it = active ? p.rep * n_qt : 0;
+  const bool bulk_stats = (p.Tq % 4) == 0;  // 16-byte aligned rows: lse / delta arrive with the Q tile
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < QST; ++i) {
       mbar_init(&bars->q_full[i], 1);
       mbar_init(&bars->q_empty[i], 1);
-      mbar_init(&bars->p_full[i], 128);
-      mbar_init(&bars->p_empty[i], 1);
     }
     mbar_init(&bars->s_full, 1);
-    mbar_init(&bars->s_empty, 128);
+    mbar_init(&bars->s_empty, 256);
+    mbar_init(&bars->p_full, 256);
+    mbar_init(&bars->mma_done, 1);
     mbar_init(&bars->dq_full, 1);
     mbar_init(&bars->dq_empty, 128);
     mbar_init(&bars->acc_done, 1);
@@ -451,6 +541,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   volatile int* abort_flag = &bars->abort_flag;
+  const bool tr = trace_this_cta();
 
   if (warp == 0) {
     if (lane == 0 && n_it > 0) {
@@ -466,17 +557,25 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         tma_load_4d(smem + L::V_OFF + blk * 16384, &tmV, &bars->kv_full, blk * 64, k0, hk, b);
       }
       for (int i = 0; i < n_it && !*abort_flag; ++i) {
-        const int st = i & 1;
+        const int st = i % QST;
         const int h = hk * p.rep + i / n_qt, q0 = (i % n_qt) * BQ;
-        if (!mbar_wait(&bars->q_empty[st], ((i >> 1) & 1) ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+        if (!mbar_wait(&bars->q_empty[st], ((i / QST) & 1) ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
           *abort_flag = 1;
           break;
         }
-        mbar_expect_tx(&bars->q_full[st], 2 * 16384);
+        ATTN_TRACE(tr, 0, i);
+        const int nq = min(BQ, p.Tq - q0);
+        const uint32_t stat_bytes = bulk_stats ? (uint32_t)nq * 4u : 0u;
+        mbar_expect_tx(&bars->q_full[st], 2 * 16384 + 2 * stat_bytes);
 #pragma unroll
         for (int blk = 0; blk < 2; ++blk) {
           tma_load_4d(smem + L::Q_OFF + st * 16384 + blk * 8192, &tmQ, &bars->q_full[st], blk * 64, q0, h, b);
           tma_load_4d(smem + L::DO_OFF + st * 16384 + blk * 8192, &tmdO, &bars->q_full[st], blk * 64, q0, h, b);
+        }
+        if (bulk_stats) {
+          const long long row = ((long long)b * p.Hq + h) * p.Tq + q0;
+          bulk_load(smem + L::STAT_OFF + st * 512, lse2 + row, stat_bytes, &bars->q_full[st]);
+          bulk_load(smem + L::STAT_OFF + st * 512 + 256, delta + row, stat_bytes, &bars->q_full[st]);
         }
       }
     }
@@ -486,161 +585,195 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       constexpr uint32_t id_s = idesc_bf16_f32(128, BQ, false, false);   // S^T, dP^T
       constexpr uint32_t id_kv = idesc_bf16_f32(128, HD, false, true);   // dV, dK
       constexpr uint32_t id_q = idesc_bf16_f32(128, BQ, true, true);     // dQ^T
-      const uint32_t sK = smem_u32(smem + L::K_OFF), sV = smem_u32(smem + L::V_OFF);
+      // precomputed descriptors; stage and k offsets are added per MMA
+      const uint64_t dK_km = sdesc_sw128(smem_u32(smem + L::K_OFF), 16, 1024);      // K as K-major A (S^T)
+      const uint64_t dV_km = sdesc_sw128(smem_u32(smem + L::V_OFF), 16, 1024);      // V as K-major A (dP^T)
+      const uint64_t dK_mn = sdesc_sw128(smem_u32(smem + L::K_OFF), 16384, 1024);   // K as MN-major A (dQ^T)
+      const uint64_t dQ_km = sdesc_sw128(smem_u32(smem + L::Q_OFF), 16, 1024);      // Q as K-major B (S^T)
+      const uint64_t dQ_mn = sdesc_sw128(smem_u32(smem + L::Q_OFF), 8192, 1024);   // Q as MN-major B (dK)
+      const uint64_t dO_km = sdesc_sw128(smem_u32(smem + L::DO_OFF), 16, 1024);     // dO as K-major B (dP^T)
+      const uint64_t dO_mn = sdesc_sw128(smem_u32(smem + L::DO_OFF), 8192, 1024);   // dO as MN-major B (dV)
+      const uint64_t dS_km = sdesc_sw128(smem_u32(smem + L::DS_OFF), 16, 1024);     // dS^T as K-major A (dK)
+      const uint64_t dS_mn = sdesc_sw128(smem_u32(smem + L::DS_OFF), 8192, 1024);   // dS^T as MN-major B (dQ^T)
       auto issue_s = [&](int i) -> bool {
-        const int st = i & 1;
-        if (!mbar_wait(&bars->q_full[st], (i >> 1) & 1, err, ERR_MBAR_TIMEOUT_MMA)) return false;
+        const int st = i % QST;
+        if (!mbar_wait(&bars->q_full[st], (i / QST) & 1, err, ERR_MBAR_TIMEOUT_MMA)) return false;
+        ATTN_TRACE(tr, 2, i);
         if (i > 0 && !mbar_wait(&bars->s_empty, (i - 1) & 1, err, ERR_MBAR_TIMEOUT_MMA)) return false;
+        ATTN_TRACE(tr, 3, i);
         tc_fence_after();
-        const uint32_t sQ = smem_u32(smem + L::Q_OFF + st * 16384), sdO = smem_u32(smem + L::DO_OFF + st * 16384);
+        const uint32_t so = st * 16384;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t blk = kk >> 2, sub = (kk & 3) * 32;
-          umma_f16(tmem + 0, sdesc_sw128(sK + blk * 16384 + sub, 16, 1024),
-                   sdesc_sw128(sQ + blk * 8192 + sub, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + 0, sdesc_add(dK_km, blk * 16384 + sub), sdesc_add(dQ_km, so + blk * 8192 + sub), id_s,
+                   kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t blk = kk >> 2, sub = (kk & 3) * 32;
-          umma_f16(tmem + 64, sdesc_sw128(sV + blk * 16384 + sub, 16, 1024),
-                   sdesc_sw128(sdO + blk * 8192 + sub, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + 64, sdesc_add(dV_km, blk * 16384 + sub), sdesc_add(dO_km, so + blk * 8192 + sub), id_s,
+                   kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->s_full);
+        ATTN_TRACE(tr, 4, i);
         return true;
       };
       bool ok = mbar_wait(&bars->kv_full, 0, err, ERR_MBAR_TIMEOUT_MMA) && issue_s(0);
       for (int i = 0; i < n_it && ok; ++i) {
-        const int st = i & 1;
+        const int st = i % QST, pb = i & 1;
         if (i + 1 < n_it && !issue_s(i + 1)) {
           ok = false;
           break;
         }
-        if (!mbar_wait(&bars->p_full[st], (i >> 1) & 1, err, ERR_MBAR_TIMEOUT_MMA) ||
-            !mbar_wait(&bars->dq_empty, (i & 1) ^ 1, err, ERR_MBAR_TIMEOUT_MMA)) {
+        if (!mbar_wait(&bars->p_full, i & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
+        ATTN_TRACE(tr, 5, i);
+        if (!mbar_wait(&bars->dq_empty, (i & 1) ^ 1, err, ERR_MBAR_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        ATTN_TRACE(tr, 6, i);
         tc_fence_after();
-        const uint32_t sQ = smem_u32(smem + L::Q_OFF + st * 16384), sdO = smem_u32(smem + L::DO_OFF + st * 16384);
-        const uint32_t sPT = smem_u32(smem + L::PT_OFF + st * 16384), sDS = smem_u32(smem + L::DS_OFF + st * 16384);
+        const uint32_t so = st * 16384, dso = pb * 16384;
 #pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk)  // dV += P^T dO
-          umma_f16(tmem + 256, sdesc_sw128(sPT + kk * 32, 16, 1024), sdesc_sw128(sdO + kk * 2048, 8192, 1024), id_kv,
-                   (i > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BQ / 16; ++kk)  // dV += P^T dO, P^T read from TMEM (8 columns per 16 queries)
+          umma_f16_tmem_a(tmem + 256, tmem + 192 + pb * 32 + kk * 8, sdesc_add(dO_mn, so + kk * 2048), id_kv,
+                          (i > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)  // dK += dS^T Q
-          umma_f16(tmem + 384, sdesc_sw128(sDS + kk * 32, 16, 1024), sdesc_sw128(sQ + kk * 2048, 8192, 1024), id_kv,
+          umma_f16(tmem + 384, sdesc_add(dS_km, dso + kk * 32), sdesc_add(dQ_mn, so + kk * 2048), id_kv,
                    (i > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < BK_KEYS / 16; ++kk)  // dQ^T = K^T dS^T
-          umma_f16(tmem + 128, sdesc_sw128(sK + kk * 2048, 16384, 1024), sdesc_sw128(sDS + kk * 2048, 8192, 1024),
-                   id_q, kk > 0 ? 1u : 0u);
-        umma_commit(&bars->p_empty[st]);
+          umma_f16(tmem + 128, sdesc_add(dK_mn, kk * 2048), sdesc_add(dS_mn, dso + kk * 2048), id_q,
+                   kk > 0 ? 1u : 0u);
         umma_commit(&bars->q_empty[st]);
+        umma_commit(&bars->mma_done);
         umma_commit(&bars->dq_full);
+        ATTN_TRACE(tr, 7, i);
       }
       if (ok) umma_commit(&bars->acc_done);
       else *abort_flag = 1;
     }
-  } else if (warp < 6) {
-    // ---------------- softmax (thread = key row), final dK / dV ----------------
-    const int quarter = warp & 3;
+  } else if (warp < 10) {
+    // ---------------- softmax (thread = key row, one half of the 64 queries), final dV (half 0) / dK (half 1) ----
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
-    const int tid = threadIdx.x - 64;  // 0..127
+    const int tid = threadIdx.x - 64;  // 0..255
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const float sl2 = p.scale * 1.4426950408889634f;
     const bool key_ok = k0 + r < kv_end;
+    const bool tw = tr && threadIdx.x == 64;
     bool ok = true;
     for (int i = 0; i < n_it; ++i) {
-      const int st = i & 1;
+      const int st = i % QST, pb = i & 1;
       const int h = hk * p.rep + i / n_qt, q0 = (i % n_qt) * BQ;
-      {  // stage lse (pre-scaled by log2 e) and delta of this query tile
-        float* slot = stat + st * 128;
-        const int q = tid & 63;
-        const bool in = q0 + q < p.Tq;
-        const long long idx = ((long long)b * p.Hq + h) * p.Tq + q0 + q;
-        if (tid < 64) slot[q] = in ? p.lse[idx] * 1.4426950408889634f : INFINITY;
-        else slot[64 + q] = in ? delta[idx] : 0.f;
+      const int nq = min(BQ, p.Tq - q0);
+      float* slot = reinterpret_cast<float*>(smem + L::STAT_OFF + st * 512);  // lse * log2 e [64], delta [64]
+      if (!bulk_stats) {  // staged by the threads; out-of-range queries get P = 0
+        if (tid < 128) {
+          const int q = tid & 63;
+          const bool in = q < nq;
+          const long long idx = ((long long)b * p.Hq + h) * p.Tq + q0 + q;
+          if (tid < 64) slot[q] = in ? lse2[idx] : INFINITY;
+          else slot[64 + q] = in ? delta[idx] : 0.f;
+        }
+        softmax_group_sync();
+      } else {
+        if (!warp_wait(&bars->q_full[st], (i / QST) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE)) {
+          ok = false;  // the bulk-copied rows of this stage have landed
+          break;
+        }
+        if (nq < BQ) {  // tail tile: pad the rows past the end
+          if (tid < BQ - nq) {
+            slot[nq + tid] = INFINITY;
+            slot[64 + nq + tid] = 0.f;
+          }
+          softmax_group_sync();
+        }
       }
-      softmax_group_sync();
+      ATTN_TRACE(tw, 8, i);
       if (!warp_wait(&bars->s_full, i & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
+      ATTN_TRACE(tw, 9, i);
       tc_fence_after();
-      uint32_t sv[2][32], dp[2][32];
-      tmem_ld_32x32b_x32(tmem + lane_base + 0, sv[0]);
-      tmem_ld_32x32b_x32(tmem + lane_base + 32, sv[1]);
-      tmem_ld_32x32b_x32(tmem + lane_base + 64, dp[0]);
-      tmem_ld_32x32b_x32(tmem + lane_base + 96, dp[1]);
+      uint32_t sv[32], dp[32];
+      tmem_ld_32x32b_x32(tmem + lane_base + half * 32, sv);
+      tmem_ld_32x32b_x32(tmem + lane_base + 64 + half * 32, dp);
       tmem_ld_wait();
+      ATTN_TRACE(tw, 10, i);
       tc_fence_before();
       mbar_arrive(&bars->s_empty);
-      if (!warp_wait(&bars->p_empty[st], ((i >> 1) & 1) ^ 1, err, ERR_MBAR_TIMEOUT_EPILOGUE)) {
+      // P^T and dS^T of this thread's 32 queries, packed in registers before waiting for the previous MMA3-5
+      uint32_t pk[16], dk4[16];
+      const float* ls = slot + half * 32;
+      const float* dl = slot + 64 + half * 32;
+      if (key_ok) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = ex2(__uint_as_float(sv[2 * e]) * sl2 - ls[2 * e]);
+          const float p1 = ex2(__uint_as_float(sv[2 * e + 1]) * sl2 - ls[2 * e + 1]);
+          pk[e] = pack_bf16x2(p0, p1);
+          dk4[e] = pack_bf16x2(p0 * (__uint_as_float(dp[2 * e]) - dl[2 * e]),
+                               p1 * (__uint_as_float(dp[2 * e + 1]) - dl[2 * e + 1]));
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pk[e] = dk4[e] = 0u;
+      }
+      // MMA3-5 of iteration i-1 must be done: they read this dS^T buffer's other use and the P^T TMEM lanes
+      if (i > 0 && !warp_wait(&bars->mma_done, (i - 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
-      const float* slot = stat + st * 128;
-      uint8_t* pt_row = smem + L::PT_OFF + st * 16384 + r * 128;
-      uint8_t* ds_row = smem + L::DS_OFF + st * 16384 + r * 128;
+      ATTN_TRACE(tw, 11, i);
+      tc_fence_after();
+      uint8_t* ds_row = smem + L::DS_OFF + pb * 16384 + r * 128;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          uint32_t pk[4], dk4[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float pv[2], dsv[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int qi = c * 32 + ch * 8 + 2 * e + u;
-              float pr = ex2(__uint_as_float(sv[c][ch * 8 + 2 * e + u]) * sl2 - slot[qi]);
-              pr = key_ok ? pr : 0.f;
-              pv[u] = pr;
-              dsv[u] = pr * (__uint_as_float(dp[c][ch * 8 + 2 * e + u]) - slot[64 + qi]);
-            }
-            pk[e] = pack_bf16x2(pv[0], pv[1]);
-            dk4[e] = pack_bf16x2(dsv[0], dsv[1]);
-          }
-          const int chunk = c * 4 + ch;
-          const int off = (chunk ^ (r & 7)) << 4;
-          *reinterpret_cast<uint4*>(pt_row + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          *reinterpret_cast<uint4*>(ds_row + off) = make_uint4(dk4[0], dk4[1], dk4[2], dk4[3]);
-        }
+      for (int c = 0; c < 4; ++c) {
+        const int chunk = half * 4 + c;
+        *reinterpret_cast<uint4*>(ds_row + ((chunk ^ (r & 7)) << 4)) =
+            make_uint4(dk4[4 * c], dk4[4 * c + 1], dk4[4 * c + 2], dk4[4 * c + 3]);
       }
+      tmem_st_32x32b_x16(tmem + lane_base + 192 + pb * 32 + half * 16, pk);
+      tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&bars->p_full[st]);
+      ATTN_TRACE(tw, 12, i);
+      mbar_arrive(&bars->p_full);
     }
     if (ok && n_it > 0) ok = warp_wait(&bars->acc_done, 0, err, ERR_MBAR_TIMEOUT_EPILOGUE);
     tc_fence_after();
     const int key = k0 + r;
     if (ok) {
+      const int which = half;  // 0: dV, 1: dK (scaled)
+      __nv_bfloat16* dst = which == 0 ? dv + (long long)b * dv_bs + (long long)key * dv_ts + (long long)hk * dv_hs
+                                      : dk + (long long)b * dk_bs + (long long)key * dk_ts + (long long)hk * dk_hs;
+      const float mul = which == 0 ? 1.f : p.scale;
 #pragma unroll 1
-      for (int which = 0; which < 2; ++which) {  // 0: dV, 1: dK (scaled)
-        __nv_bfloat16* dst = which == 0 ? dv + (long long)b * dv_bs + (long long)key * dv_ts + (long long)hk * dv_hs
-                                        : dk + (long long)b * dk_bs + (long long)key * dk_ts + (long long)hk * dk_hs;
-        const float mul = which == 0 ? 1.f : p.scale;
-#pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
-          uint32_t o[32];
-          if (n_it > 0) {
-            tmem_ld_32x32b_x32(tmem + lane_base + 256 + which * 128 + c * 32, o);
-            tmem_ld_wait();
-          } else {
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t o[32];
+        if (n_it > 0) {
+          tmem_ld_32x32b_x32(tmem + lane_base + 256 + which * 128 + c * 32, o);
+          tmem_ld_wait();
+        } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = 0u;
-          }
-          if (key < p.Tk) {
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
+        if (key < p.Tk) {
 #pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) {
-              uint4 u;
-              u.x = pack_bf16x2(__uint_as_float(o[v4 * 8 + 0]) * mul, __uint_as_float(o[v4 * 8 + 1]) * mul);
-              u.y = pack_bf16x2(__uint_as_float(o[v4 * 8 + 2]) * mul, __uint_as_float(o[v4 * 8 + 3]) * mul);
-              u.z = pack_bf16x2(__uint_as_float(o[v4 * 8 + 4]) * mul, __uint_as_float(o[v4 * 8 + 5]) * mul);
-              u.w = pack_bf16x2(__uint_as_float(o[v4 * 8 + 6]) * mul, __uint_as_float(o[v4 * 8 + 7]) * mul);
-              *reinterpret_cast<uint4*>(dst + c * 32 + v4 * 8) = u;
-            }
+          for (int v4 = 0; v4 < 4; ++v4) {
+            uint4 u;
+            u.x = pack_bf16x2(__uint_as_float(o[v4 * 8 + 0]) * mul, __uint_as_float(o[v4 * 8 + 1]) * mul);
+            u.y = pack_bf16x2(__uint_as_float(o[v4 * 8 + 2]) * mul, __uint_as_float(o[v4 * 8 + 3]) * mul);
+            u.z = pack_bf16x2(__uint_as_float(o[v4 * 8 + 4]) * mul, __uint_as_float(o[v4 * 8 + 5]) * mul);
+            u.w = pack_bf16x2(__uint_as_float(o[v4 * 8 + 6]) * mul, __uint_as_float(o[v4 * 8 + 7]) * mul);
+            *reinterpret_cast<uint4*>(dst + c * 32 + v4 * 8) = u;
           }
         }
       }
@@ -648,16 +781,19 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       *abort_flag = 1;
     }
   } else {
-    // ---------------- dQ drain (thread = head-dim lane) ----------------
+    // ---------------- dQ drain (thread = head-dim lane): TMEM -> shared fp32 tile -> TMA reduce-add ----------------
     const int quarter = warp & 3;
     const int d = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const bool leader = threadIdx.x == 320;
+    float* stage = reinterpret_cast<float*>(smem + L::DQ_OFF);  // [2 halves][32 queries][128]
     for (int i = 0; i < n_it; ++i) {
       const int h = hk * p.rep + i / n_qt, q0 = (i % n_qt) * BQ;
       if (!warp_wait(&bars->dq_full, i & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE)) {
         *abort_flag = 1;
         break;
       }
+      ATTN_TRACE(tr && leader, 13, i);
       tc_fence_after();
       uint32_t v[2][32];
       tmem_ld_32x32b_x32(tmem + lane_base + 128, v[0]);
@@ -665,15 +801,25 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(&bars->dq_empty);
-      float* base = dq_acc + ((long long)b * p.Tq) * p.Hq * HD + (long long)h * HD + d;
+      ATTN_TRACE(tr && leader, 14, i);
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
-#pragma unroll 8
-        for (int q = 0; q < 32; ++q) {
-          const int t = q0 + c * 32 + q;
-          if (t < p.Tq) atomicAdd(base + (long long)t * p.Hq * HD, __uint_as_float(v[c][q]) * p.scale);
+      for (int half = 0; half < 2; ++half) {
+        if (q0 + half * 32 >= p.Tq) break;
+        if (leader) bulk_wait_group_read<1>();  // this half's reduce from the previous iteration has read smem
+        drain_group_sync();
+        float* dst = stage + half * 32 * HD + d;
+#pragma unroll
+        for (int q = 0; q < 32; ++q) dst[q * HD] = __uint_as_float(v[half][q]) * p.scale;
+        fence_proxy_async_smem();
+        drain_group_sync();
+        if (leader) {
+          tma_reduce_add_4d(&tmdQ, stage + half * 32 * HD, 0, h, q0 + half * 32, b);
+          bulk_commit_group();
         }
+      }
+      ATTN_TRACE(tr && leader, 15, i);
     }
+    if (leader) bulk_wait_group_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -683,11 +829,17 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   }
 }
 
+cudaError_t attention_set_trace(long long* buf, int cta) {
+  TraceCfg t{buf, cta};
+  return cudaMemcpyToSymbol(g_attn_trace, &t, sizeof(t));
+}
+
 cudaError_t attention_bwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                                    const CUtensorMap& tdo, const AttnParams& p, const float* delta, float* dq_acc,
-                                    __nv_bfloat16* dk, long long dk_bs, long long dk_ts, long long dk_hs,
-                                    __nv_bfloat16* dv, long long dv_bs, long long dv_ts, long long dv_hs, int* err,
-                                    cudaStream_t s) {
+                                    const CUtensorMap& tdo, const CUtensorMap& tdq, const AttnParams& p,
+                                    const float* delta, const float* lse2, __nv_bfloat16* dk, long long dk_bs,
+                                    long long dk_ts,
+                                    long long dk_hs, __nv_bfloat16* dv, long long dv_bs, long long dv_ts,
+                                    long long dv_hs, int* err, cudaStream_t s) {
   if (p.hd != 128) return cudaErrorInvalidValue;
   static bool set = false;
   if (!set) {
@@ -695,8 +847,8 @@ cudaError_t attention_bwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk
     set = true;
   }
   dim3 grid((p.Tk + BK_KEYS - 1) / BK_KEYS, p.Hkv, p.B);
-  flash_bwd_tc_kernel<<<grid, BWD_THREADS, BwdSmem::TOTAL, s>>>(tq, tk, tv, tdo, p, delta, dq_acc, dk, dk_bs, dk_ts,
-                                                               dk_hs, dv, dv_bs, dv_ts, dv_hs, err);
+  flash_bwd_tc_kernel<<<grid, BWD_THREADS, BwdSmem::TOTAL, s>>>(tq, tk, tv, tdo, tdq, p, delta, lse2, dk, dk_bs,
+                                                               dk_ts, dk_hs, dv, dv_bs, dv_ts, dv_hs, err);
   return cudaGetLastError();
 }
 

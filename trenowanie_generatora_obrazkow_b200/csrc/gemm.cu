@@ -184,6 +184,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc = idesc_bf16_f32(GEMM_BM, BN, A_MN, B_MN);
+      // descriptors of stage 0; a 16-element k step is 32 B (K-major) or 2 KB (MN-major), in 16-byte units
+      const uint64_t a_desc0 = A_MN ? sdesc_sw128(smem_u32(smem), 8192, 1024) : sdesc_sw128(smem_u32(smem), 16, 1024);
+      const uint64_t b_desc0 = B_MN ? sdesc_sw128(smem_u32(smem) + Cfg::A_BYTES, 8192, 1024)
+                                    : sdesc_sw128(smem_u32(smem) + Cfg::A_BYTES, 16, 1024);
+      constexpr uint64_t A_KSTEP = A_MN ? 128 : 2, B_KSTEP = B_MN ? 128 : 2;
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -204,14 +209,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
-          const uint32_t sb = sa + Cfg::A_BYTES;
+          const uint64_t ad = sdesc_add(a_desc0, stage * Cfg::STAGE_BYTES);
+          const uint64_t bd = sdesc_add(b_desc0, stage * Cfg::STAGE_BYTES);
 #pragma unroll
-          for (int k = 0; k < GEMM_BK / 16; ++k) {
-            const uint64_t ad = A_MN ? sdesc_sw128(sa + k * 2048, 8192, 1024) : sdesc_sw128(sa + k * 32, 16, 1024);
-            const uint64_t bd = B_MN ? sdesc_sw128(sb + k * 2048, 8192, 1024) : sdesc_sw128(sb + k * 32, 16, 1024);
-            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < GEMM_BK / 16; ++k)
+            umma_f16(d_tmem, ad + k * A_KSTEP, bd + k * B_KSTEP, idesc, (kb | k) != 0 ? 1u : 0u);
           umma_commit(&empty_bar[stage]);  // frees the stage once these MMAs have read it
           if (++stage == STAGES) {
             stage = 0;
@@ -368,6 +370,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0 && leader) {
       // ---------------- MMA issuer (leader CTA only) ----------------
       constexpr uint32_t idesc = idesc_bf16_f32(256, G2_BN, A_MN, B_MN);
+      const uint64_t a_desc0 = A_MN ? sdesc_sw128(smem_u32(smem), 8192, 1024) : sdesc_sw128(smem_u32(smem), 16, 1024);
+      const uint64_t b_desc0 = B_MN ? sdesc_sw128(smem_u32(smem) + G2_A_BYTES, 8192, 1024)
+                                    : sdesc_sw128(smem_u32(smem) + G2_A_BYTES, 16, 1024);
+      constexpr uint64_t A_KSTEP = A_MN ? 128 : 2, B_KSTEP = B_MN ? 128 : 2;
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -388,13 +394,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * G2_STAGE_BYTES);
-          const uint32_t sb = sa + G2_A_BYTES;
+          const uint64_t ad = sdesc_add(a_desc0, stage * G2_STAGE_BYTES);
+          const uint64_t bd = sdesc_add(b_desc0, stage * G2_STAGE_BYTES);
 #pragma unroll
           for (int k = 0; k < GEMM_BK / 16; ++k) {
-            const uint64_t ad = A_MN ? sdesc_sw128(sa + k * 2048, 8192, 1024) : sdesc_sw128(sa + k * 32, 16, 1024);
-            const uint64_t bd = B_MN ? sdesc_sw128(sb + k * 2048, 8192, 1024) : sdesc_sw128(sb + k * 32, 16, 1024);
-            umma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_pair(d_tmem, ad + k * A_KSTEP, bd + k * B_KSTEP, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit_pair_mc(&empty_bar[stage], 0x3);  // frees this stage in both CTAs
           if (++stage == G2_STAGES) {

@@ -110,16 +110,18 @@ cudaError_t attention_bwd_launch(const AttnParams& p, const __nv_bfloat16* dO, f
                                  __nv_bfloat16* dk, long long dk_bs, long long dk_ts, long long dk_hs,
                                  __nv_bfloat16* dv, long long dv_bs, long long dv_ts, long long dv_hs, cudaStream_t s);
 
+// lse2 (optional, [B][Hq][Tq]): receives lse * log2(e) for the tcgen05 backward
 cudaError_t attention_bwd_prep_launch(const AttnParams& p, const __nv_bfloat16* dO, float* delta, float* dq_acc,
-                                      cudaStream_t s);
+                                      cudaStream_t s, float* lse2 = nullptr);
 cudaError_t attention_dq_convert_launch(const AttnParams& p, const float* dq_acc, __nv_bfloat16* dq, long long bs,
                                         long long ts, long long hs, cudaStream_t s);
-// tcgen05 backward (head dim 128); dq_acc zeroed and delta computed by attention_bwd_prep_launch
+// tcgen05 backward (head dim 128); dq_acc zeroed and delta computed by attention_bwd_prep_launch. tdq: 4-D fp32 map
+// of dq_acc {hd, Hq, Tq, B} with a {128, 1, 32, 1} box, no swizzle (the dQ tiles are TMA reduce-added into it).
 cudaError_t attention_bwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                                    const CUtensorMap& tdo, const AttnParams& p, const float* delta, float* dq_acc,
-                                    __nv_bfloat16* dk, long long dk_bs, long long dk_ts, long long dk_hs,
-                                    __nv_bfloat16* dv, long long dv_bs, long long dv_ts, long long dv_hs, int* err,
-                                    cudaStream_t s);
+                                    const CUtensorMap& tdo, const CUtensorMap& tdq, const AttnParams& p,
+                                    const float* delta, const float* lse2, __nv_bfloat16* dk, long long dk_bs, long long dk_ts,
+                                    long long dk_hs, __nv_bfloat16* dv, long long dv_bs, long long dv_ts,
+                                    long long dv_hs, int* err, cudaStream_t s);
 // tcgen05 forward (attention_tc.cu); tensor maps: 4-D {hd, T, H, B}, boxes {64, 128 | 64, 1, 1}, 128-byte swizzle
 cudaError_t attention_fwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                     const AttnParams& p, int* err, cudaStream_t s);
@@ -191,6 +193,7 @@ struct MuonAGParams {
   unsigned long long timeout_ns;
   int* err;
 };
+cudaError_t attention_set_trace(long long* buf, int cta);  // profiling timeline (null: off)
 cudaError_t muon_rs_launch(const MuonRSParams& p, int blocks, cudaStream_t s);
 cudaError_t muon_momentum_launch(const MuonMomentumParams& p, cudaStream_t s);
 cudaError_t muon_ag_apply_launch(const MuonAGParams& p, int blocks, cudaStream_t s);

@@ -55,6 +55,22 @@ static CUtensorMap make_tmap_bf16_sw128(const void* base, uint64_t inner, uint64
   return m;
 }
 
+// 4-D fp32 map of the dQ accumulator [B][Tq][Hq][hd] as {hd, Hq, Tq, B}, box {hd, 1, 32, 1}, no swizzle: the
+// backward kernel reduce-adds 32-query x hd tiles into it.
+static CUtensorMap make_tmap_dq(const float* base, uint64_t hd, uint64_t H, uint64_t T, uint64_t B) {
+  CUtensorMap m;
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base address must be 16-byte aligned");
+  cuuint64_t dims[4] = {hd, H, T, B};
+  cuuint64_t strides[3] = {hd * 4, H * hd * 4, T * H * hd * 4};
+  cuuint32_t box[4] = {(cuuint32_t)hd, 1, 32, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = tmap_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (dQ accumulator) failed with code ", (int)r);
+  return m;
+}
+
 // 4-D bf16 tensor map {hd, T, H, B} (strides in elements) with a {64, box_rows, 1, 1} box, 128-byte swizzle.
 static CUtensorMap make_tmap_bhtd(const void* base, uint64_t hd, uint64_t T, uint64_t H, uint64_t B, uint64_t ts,
                                   uint64_t hs, uint64_t bs, uint32_t box_rows) {
@@ -430,7 +446,8 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::T
   p.o_ts = o.stride(1);
   p.o_hs = o.stride(2);
   p.lse = lse.data_ptr<float>();
-  at::Tensor delta = at::empty({p.B, p.Hq, p.Tq}, q.options().dtype(at::kFloat));
+  at::Tensor delta = at::empty({2, p.B, p.Hq, p.Tq}, q.options().dtype(at::kFloat));  // delta, lse * log2(e)
+  float* lse2 = delta.data_ptr<float>() + (long long)p.B * p.Hq * p.Tq;
   at::Tensor dq_acc = at::empty({p.B, p.Tq, p.Hq, p.hd}, q.options().dtype(at::kFloat));
   if (g_attention_tc && p.hd == 128) {
     cudaStream_t st = at::cuda::getCurrentCUDAStream();
@@ -438,10 +455,12 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::T
     CUtensorMap tk = make_tmap_bhtd(p.k, p.hd, p.Tk, p.Hkv, p.B, p.k_ts, p.k_hs, p.k_bs, 128);
     CUtensorMap tv = make_tmap_bhtd(p.v, p.hd, p.Tk, p.Hkv, p.B, p.v_ts, p.v_hs, p.v_bs, 128);
     CUtensorMap tdo = make_tmap_bhtd(dO.data_ptr(), p.hd, p.Tq, p.Hq, p.B, dO.stride(1), dO.stride(2), dO.stride(0), 64);
-    TGO_CHECK_LAUNCH(attention_bwd_prep_launch(p, bfp(dO), delta.data_ptr<float>(), dq_acc.data_ptr<float>(), st));
-    TGO_CHECK_LAUNCH(attention_bwd_tc_launch(tq, tk, tv, tdo, p, delta.data_ptr<float>(), dq_acc.data_ptr<float>(),
-                                             bfp(dk), dk.stride(0), dk.stride(1), dk.stride(2), bfp(dv), dv.stride(0),
-                                             dv.stride(1), dv.stride(2), err_ptr(err), st));
+    TGO_CHECK_LAUNCH(attention_bwd_prep_launch(p, bfp(dO), delta.data_ptr<float>(), dq_acc.data_ptr<float>(), st,
+                                               lse2));
+    CUtensorMap tdq = make_tmap_dq(dq_acc.data_ptr<float>(), p.hd, p.Hq, p.Tq, p.B);
+    TGO_CHECK_LAUNCH(attention_bwd_tc_launch(tq, tk, tv, tdo, tdq, p, delta.data_ptr<float>(), lse2, bfp(dk), dk.stride(0),
+                                             dk.stride(1), dk.stride(2), bfp(dv), dv.stride(0), dv.stride(1),
+                                             dv.stride(2), err_ptr(err), st));
     TGO_CHECK_LAUNCH(attention_dq_convert_launch(p, dq_acc.data_ptr<float>(), bfp(dq), dq.stride(0), dq.stride(1),
                                                  dq.stride(2), st));
   } else {
@@ -522,6 +541,16 @@ void allreduce_bf16(at::Tensor grads, std::vector<int64_t> staging, std::vector<
   p.timeout_ns = (unsigned long long)timeout_ns;
   p.err = err_ptr(err);
   TGO_CHECK_LAUNCH(allreduce_bf16_launch(p, (int)blocks, at::cuda::getCurrentCUDAStream()));
+}
+
+// Attention pipeline timeline of one CTA (clock64 per phase event and iteration, int64 [32 * 64]); None: off.
+void attention_trace(c10::optional<at::Tensor> buf, int64_t cta) {
+  long long* ptr = nullptr;
+  if (buf.has_value() && buf->defined()) {
+    TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->numel() >= 32 * 64, "trace buffer");
+    ptr = reinterpret_cast<long long*>(buf->data_ptr<int64_t>());
+  }
+  TORCH_CHECK(attention_set_trace(ptr, (int)cta) == cudaSuccess, "attention_set_trace failed");
 }
 
 // ---- sharded Muon over peer memory (muon_comm.cu) ----
@@ -649,6 +678,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &tgo::ipc_close);
   m.def("peer_copy", &tgo::peer_copy, "NVLink copy into a peer's buffer + version word (weight snapshots)");
   m.def("allreduce_bf16", &tgo::allreduce_bf16, "fused cast + reduce-scatter + all-gather over peer memory");
+  m.def("attention_trace", &tgo::attention_trace, "install / remove the attention timeline buffer (profiling)");
   m.def("tensor_from_ptr", &tgo::tensor_from_ptr, "bf16 view of raw device memory (not owned)");
   m.def("muon_rs", &tgo::muon_rs, "sharded Muon: gradient bucket reduce-scatter to the matrix owners (NVLink)");
   m.def("muon_momentum", &tgo::muon_momentum, "sharded Muon: owner momentum + Nesterov -> bf16 NS input");
