@@ -43,14 +43,17 @@ struct TraceCfg {
   int cta;
 };
 __device__ TraceCfg g_attn_trace;
-__device__ __forceinline__ bool trace_this_cta() {
+// The buffer pointer is read once per CTA (trace_buffer) so that recording an event is one clock read and one
+// store: reloading a __device__ variable after every asm with a memory clobber distorted the timeline.
+__device__ __forceinline__ long long* trace_buffer() {
   const TraceCfg t = g_attn_trace;
-  return t.buf != nullptr &&
-         (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) == t.cta;
+  return (t.buf != nullptr && (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) == t.cta)
+             ? t.buf
+             : nullptr;
 }
 #define ATTN_TRACE(on, ev, it)                                                  \
   do {                                                                          \
-    if (on) g_attn_trace.buf[(ev) * 64 + ((it) & 63)] = (long long)clock64();   \
+    if (on) trace_buf[(ev) * 64 + ((it) & 63)] = (long long)clock64();          \
   } while (0)
 
 __device__ __forceinline__ float ex2(float x) {  // hardware 2^x (MUFU)
@@ -132,7 +135,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   volatile int* abort_flag = &bars->abort_flag;
-  const bool tr = trace_this_cta();
+  long long* const trace_buf = trace_buffer();
+  const bool tr = trace_buf != nullptr;
 
   if (warp == 0) {
     if (lane == 0 && n_tiles > 0) {
@@ -541,7 +545,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   volatile int* abort_flag = &bars->abort_flag;
-  const bool tr = trace_this_cta();
+  long long* const trace_buf = trace_buffer();
+  const bool tr = trace_buf != nullptr;
 
   if (warp == 0) {
     if (lane == 0 && n_it > 0) {
