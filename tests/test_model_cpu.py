@@ -136,3 +136,33 @@ def test_tiny_baseline_config_train_step():
         o.step()
     assert torch.isfinite(loss)
     assert not torch.equal(before, den.blocks[0].attn.qkv.weight)
+
+
+def test_slayer_gpt_matches_reference():
+    """models/slayer.GPT loads the reference GPT's state dict strictly and gives the same hidden states."""
+    import os
+    import sys
+    ref = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "aurora")):
+        pytest.skip("reference not installed")
+    sys.path.insert(0, ref)
+    try:
+        from types import SimpleNamespace
+
+        from aurora.slayer import GPT as RefGPT
+    finally:
+        sys.path.remove(ref)
+    from trenowanie_generatora_obrazkow_b200.models.slayer import GPT, GPTConfig
+    cfg = GPTConfig(vocab=512, n_layer=3, n_embd=96, n_head=4, block=64)
+    torch.manual_seed(0)
+    ref_model = RefGPT(cfg.vocab, cfg.n_layer, cfg.n_embd, cfg.n_head, cfg.block, SimpleNamespace(**vars(cfg)))
+    with torch.no_grad():
+        for n, p in ref_model.named_parameters():
+            if n.endswith("vr_lambda"):
+                p.fill_(0.3)
+    ours = GPT(cfg)
+    ours.load_state_dict(ref_model.state_dict(), strict=True)
+    idx = torch.randint(0, cfg.vocab, (2, 17))
+    with torch.no_grad():
+        a, b = ref_model.hidden(idx, 2), ours.hidden(idx, 2)
+    assert torch.allclose(a, b, atol=1e-5), (a - b).abs().max()

@@ -78,7 +78,9 @@ def build_parser():
     a("--mlm-weight", type=float, default=0.05)
     a("--mlm-every", type=int, default=4)
     a("--mlm-prob", type=float, default=0.15)
-    a("--grad-comm", choices=["fp32", "bf16"], default="bf16")
+    a("--grad-comm", choices=["fp32", "bf16", "powersgd"], default="bf16",
+      help="powersgd: low-rank gradient compression with error feedback (prefer --optimizer adamw)")
+    a("--powersgd-rank", type=int, default=8)
     a("--grad-transport", choices=["auto", "nccl", "p2p"], default="auto",
       help="bf16 gradient averaging through NCCL or the peer-memory kernel (auto: p2p on CUDA)")
     a("--muon-comm", choices=["auto", "gather", "sharded"], default="auto",
@@ -189,7 +191,8 @@ def main():
         te_cfg = te_config_from_dict(resume["te_config"])
     cuda = device.type == "cuda"
     transport = args.grad_transport if args.grad_transport != "auto" else ("p2p" if cuda else "nccl")
-    grad_comm = "nccl_fp32" if args.grad_comm == "fp32" else ("p2p" if transport == "p2p" else "nccl_bf16")
+    grad_comm = "nccl_fp32" if args.grad_comm == "fp32" else "powersgd" if args.grad_comm == "powersgd" else \
+        ("p2p" if transport == "p2p" else "nccl_bf16")
     muon_comm = args.muon_comm if args.muon_comm != "auto" else \
         ("sharded" if cuda and args.grad_comm == "bf16" else "gather")
     tc = TrainConfig(global_batch=args.batch, micro_batch=args.micro_batch, steps=args.steps,
@@ -201,6 +204,7 @@ def main():
                      ema=args.ema, cfg_drop=args.cfg_drop, t_shift=args.t_shift, mlm_weight=args.mlm_weight,
                      mlm_every=args.mlm_every, mlm_prob=args.mlm_prob,
                      grad_comm=grad_comm, muon_comm=muon_comm, diloco=args.diloco,
+                     powersgd_rank=args.powersgd_rank, powersgd_start=max(2, int(args.warmup_frac * args.steps)),
                      outer_lr=args.outer_lr, outer_momentum=args.outer_momentum, outer_comm=args.outer_comm,
                      offload=args.offload, seed=args.seed, act_checkpoint=args.act_checkpoint,
                      random_lm=args.random_lm)

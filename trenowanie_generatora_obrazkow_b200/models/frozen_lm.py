@@ -3,6 +3,8 @@
 The reference runs a frozen pretrained LM (SlayerLab/Slayer149 GPT or the Poziomka MoE through transformers,
 aurora/slayer.py:30-146, :238-432) on each caption batch, outside the trainable parameters. Backends here:
 
+* ``slayer`` the Slayer GPT (models/slayer.py) from a local directory (config.json + model.safetensors): the
+             residual stream after ``n_layer - skip_last`` blocks, as the reference's LMTextEncoder reads it.
 * ``hf``     a transformers causal LM loaded from a local directory (``cfg.repo`` must be a path or a cached
              model id; there is no network on the training boxes): first ``num_layers - skip_last`` layers, bf16,
              the last hidden state.
@@ -52,6 +54,23 @@ class HFFrozenLM:
         return self.model(input_ids=real, use_cache=False).last_hidden_state
 
 
+class SlayerFrozenLM:
+    def __init__(self, repo, skip_last=0, device=None, model=None):
+        from .slayer import load_gpt
+        self.model = model if model is not None else load_gpt(repo)[0]
+        self.model = self.model.to(device=device, dtype=torch.bfloat16).eval().requires_grad_(False)
+        self.n_blocks = len(self.model.blocks) - skip_last
+
+    def to(self, device):
+        self.model.to(device)
+        return self
+
+    @torch.no_grad()
+    def states(self, ids):
+        real = ids.masked_fill(ids.eq(LM_PAD) | ids.eq(LM_NULL), 0).long()
+        return self.model.hidden(real, self.n_blocks)
+
+
 def build_frozen_lm(cfg, device=None, allow_random=False):
     backend = getattr(cfg, "backend", "states")
     if backend == "states":
@@ -60,11 +79,15 @@ def build_frozen_lm(cfg, device=None, allow_random=False):
         try:
             if backend == "hf":
                 return HFFrozenLM(cfg.repo, cfg.skip_last, device)
+            if backend == "slayer":
+                return SlayerFrozenLM(cfg.repo, cfg.skip_last, device)
         except Exception:
             if not allow_random:
                 raise
         return RandomFrozenLM(cfg.lm_dim, device=device)
     if backend == "hf":
         return HFFrozenLM(cfg.repo, cfg.skip_last, device)
+    if backend == "slayer":
+        return SlayerFrozenLM(cfg.repo, cfg.skip_last, device)
     raise RuntimeError(f"frozen LM backend {backend!r} needs pretrained weights that are not available offline; "
                        "use --te-size 13m / 27m, synthetic states, or --random-lm for a smoke run")

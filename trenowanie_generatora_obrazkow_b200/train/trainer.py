@@ -57,6 +57,8 @@ class TrainConfig:
     grad_comm: str = "nccl_bf16"
     shard_muon: bool = True
     muon_comm: str = "gather"     # "sharded": owner reduce-scatter + owner-only momentum/NS + fused update all-gather
+    powersgd_rank: int = 8        # grad_comm "powersgd": rank of the gradient approximation
+    powersgd_start: int = 10      # plain averaging for this many steps first
     diloco: int = 0
     outer_lr: float = 0.7
     outer_momentum: float = 0.9
@@ -144,7 +146,14 @@ class Trainer:
                                                 comm="nccl_bf16", reducer=self.muon_comm.reduce_bucket)
                 self.muon_comm.attach_buckets(self.muon_buckets)
                 dense = [p for p in dense if id(p) not in mids]
-            self.buckets = GradBuckets(dense, group=group, comm=cfg.grad_comm if reduce_grads else "none")
+            self.powersgd = None
+            if cfg.grad_comm == "powersgd" and reduce_grads:
+                from ..parallel.powersgd import PowerSGD
+                self.buckets = GradBuckets(dense, group=group, comm="nccl_fp32")
+                self.powersgd = PowerSGD(self.buckets, cfg.powersgd_rank, cfg.powersgd_start, group, cfg.seed)
+                self.buckets.reducer = self.powersgd
+            else:
+                self.buckets = GradBuckets(dense, group=group, comm=cfg.grad_comm if reduce_grads else "none")
         self.ema_decay = ema
         self.global_params = self.outer_opt = None
         if cfg.diloco:
@@ -162,6 +171,16 @@ class Trainer:
         self.last = {}
         if not self.lm_te:
             self.null_row = torch.as_tensor(te.null_ids(), device=self.device)
+
+    def memory_report(self):
+        from ..utils.memory import report
+        grads = [p.grad for p in self.params if p.grad is not None]
+        extra = {}
+        if self.muon_comm is not None:
+            extra["muon_shards"] = [self.muon_comm.g_owned, self.muon_comm.x_in, self.muon_comm.momentum]
+        if self.global_params is not None:
+            extra["diloco_global"] = list(self.global_params)
+        return report(self.rank, params=self.params, grads=grads, opts=self.opts, ema=self.ema, extra=extra)
 
     def before_save(self):
         """All ranks: bring sharded optimizer state into the optimizers' state dicts (collective)."""
@@ -251,6 +270,8 @@ class Trainer:
                 acc_mlm += l_mlm / self.accum
         if self.buckets is not None:
             self.buckets.finish()
+            if getattr(self, "powersgd", None) is not None:
+                self.powersgd.next_step()
         if self.muon_buckets is not None:
             self.muon_buckets.finish()
         if self.expert_params and self.world > 1:  # their gradients summed every rank's loss: make it the mean
