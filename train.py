@@ -50,8 +50,15 @@ def build_parser():
     a("--random-lm", action="store_true", help="frozen-LM encoders: a fixed random embedding stands in for the LM")
     a("--ema-cpu", action="store_true")
     a("--pl-prob", type=float, default=0.0)
-    a("--repa-weight", type=float, default=0.0)
+    a("--repa-weight", type=float, default=0.0,
+      help="REPA loss weight (0 = off; the reference's 0.5 needs DINOv2 targets, see --repa-target)")
     a("--repa-layer", type=int, default=None)
+    a("--repa-frac", type=float, default=0.25)
+    a("--repa-until", type=float, default=0.4)
+    a("--repa-every", type=int, default=1)
+    a("--irepa", action="store_true", help="iREPA: 3x3 conv projector + spatially normalised targets")
+    a("--repa-target", default="latent",
+      help="a local FLUX.2 VAE directory (decoder + DINOv2 targets) or 'latent' (offline stand-in target)")
     a("--optimizer", choices=["muon", "adamw"], default="muon")
     a("--lr-hidden", type=float, default=None)
     a("--beta2", type=float, default=None)
@@ -205,6 +212,9 @@ def main():
                      mlm_every=args.mlm_every, mlm_prob=args.mlm_prob,
                      grad_comm=grad_comm, muon_comm=muon_comm, diloco=args.diloco,
                      powersgd_rank=args.powersgd_rank, powersgd_start=max(2, int(args.warmup_frac * args.steps)),
+                     repa_weight=args.repa_weight, repa_layer=args.repa_layer, repa_frac=args.repa_frac,
+                     repa_until=args.repa_until, repa_every=args.repa_every, repa_target=args.repa_target,
+                     irepa=args.irepa,
                      outer_lr=args.outer_lr, outer_momentum=args.outer_momentum, outer_comm=args.outer_comm,
                      offload=args.offload, seed=args.seed, act_checkpoint=args.act_checkpoint,
                      random_lm=args.random_lm)
@@ -222,6 +232,8 @@ def main():
         if tr.ema is not None and resume.get("ema"):
             for s, e in zip(tr.ema.shadow, resume["ema"]):
                 s.copy_(e.to(s.device))
+        if tr.repa_proj is not None and resume.get("repa_proj"):
+            tr.repa_proj.load_state_dict(resume["repa_proj"])
         if tr.outer_opt is not None and resume.get("outer"):
             ckpt.load_opt_state(tr.outer_opt, resume["outer"])
         step, samples = int(resume["step"]), int(resume.get("samples", 0))
@@ -270,7 +282,8 @@ def main():
         if not master:
             return
         ckpt.save_latest(ckpt_path, step, samples, den_cfg, te_cfg, te, den, tr.opts, tr.ema, vars(args),
-                         outer=tr.outer_opt.state_dict() if tr.outer_opt is not None else None)
+                         outer=tr.outer_opt.state_dict() if tr.outer_opt is not None else None,
+                         repa_proj=tr.repa_proj)
         if args.keep_every and step % args.keep_every == 0:
             ckpt.save_snapshot(args.out, step, den_cfg, te_cfg, te, den, tr.ema)
 

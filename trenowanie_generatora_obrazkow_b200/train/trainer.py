@@ -57,6 +57,13 @@ class TrainConfig:
     grad_comm: str = "nccl_bf16"
     shard_muon: bool = True
     muon_comm: str = "gather"     # "sharded": owner reduce-scatter + owner-only momentum/NS + fused update all-gather
+    repa_weight: float = 0.0      # > 0: REPA alignment of the block-repa_layer hidden state
+    repa_layer: int = 0
+    repa_frac: float = 0.25
+    repa_until: float = 0.4
+    repa_every: int = 1
+    repa_target: str = "latent"   # "latent" (offline stand-in) or a FLUX.2 VAE directory (DINOv2 targets)
+    irepa: bool = False
     powersgd_rank: int = 8        # grad_comm "powersgd": rank of the gradient approximation
     powersgd_start: int = 10      # plain averaging for this many steps first
     diloco: int = 0
@@ -118,9 +125,19 @@ class Trainer:
             te.checkpoint_blocks = cfg.act_checkpoint
         self.frozen_lm = build_frozen_lm(te_cfg, self.device, cfg.random_lm) if self.lm_te else None
         mlm = 0.0 if self.lm_te else cfg.mlm_weight
-        self.model = FlowModel(te, den, mlm_weight=mlm, moe_aux_weight=cfg.moe_aux_weight if cfg.moe_experts else 0.0)
+        self.repa_proj = self.repa_target = None
+        if cfg.repa_weight > 0:
+            from .repa import LatentTarget, REPATarget, make_projector
+            self.repa_target = LatentTarget(den_cfg.latent_channels, spatial_norm=cfg.irepa, seed=cfg.seed,
+                                            device=self.device) if cfg.repa_target == "latent" else \
+                REPATarget(cfg.repa_target, device=self.device, spatial_norm=cfg.irepa)
+            self.repa_proj = make_projector(den_cfg.dim, self.repa_target.dim, conv=cfg.irepa).to(self.device)
+        self.model = FlowModel(te, den, mlm_weight=mlm, moe_aux_weight=cfg.moe_aux_weight if cfg.moe_experts else 0.0,
+                               repa_proj=self.repa_proj, repa_layer=cfg.repa_layer, repa_weight=cfg.repa_weight)
         lr_scale, ema = cfg.derived(self.world)
         self.named = [(pre, n, p) for pre, mod in (("te", te), ("den", den)) for n, p in mod.named_parameters()]
+        if self.repa_proj is not None:  # projector: AdamW, outside the EMA and the exported model
+            self.named += [("repa_proj", n, p) for n, p in self.repa_proj.named_parameters()]
         self.params = [p for _, _, p in self.named if p.requires_grad]
         reduce_grads = not cfg.diloco
         eids = {id(p) for p in self.expert_params}
@@ -163,7 +180,8 @@ class Trainer:
                                    group=group)
             self.global_params = D.make_global(self.params, cfg.offload)
             self.outer_opt = D.make_outer_opt(self.global_params, cfg.outer_lr, cfg.outer_momentum)
-        self.ema = EMA(self.params, ema) if (self.rank == 0 or cfg.ema_on_all_ranks) else None
+        model_params = [p for pre, _, p in self.named if pre in ("te", "den") and p.requires_grad]
+        self.ema = EMA(model_params, ema) if (self.rank == 0 or cfg.ema_on_all_ranks) else None
         self.step_idx = 0
         self.gen = torch.Generator(device=self.device)
         self.gen.manual_seed(cfg.seed * 1000 + self.rank)
@@ -250,6 +268,7 @@ class Trainer:
                 p.grad.zero_()
         acc = torch.zeros((), device=self.device)
         acc_mlm = torch.zeros((), device=self.device)
+        acc_repa = torch.zeros((), device=self.device)
         for m in range(self.accum):
             sl = slice(m * self.micro, (m + 1) * self.micro)
             x0 = x0_all[sl].float()
@@ -263,7 +282,13 @@ class Trainer:
                 self.buckets.arm()
                 if self.muon_buckets is not None:
                     self.muon_buckets.arm()
-            loss, l_fm, l_mlm, _ = self.model(x0, t, eps, **kw)
+            if self.repa_target is not None:
+                from .repa import repa_active
+                if repa_active(self.step_idx, cfg.steps, cfg.repa_until, cfg.repa_every):
+                    kw["repa_target"] = self.repa_target(x0[: max(1, round(cfg.repa_frac * b))])
+            loss, l_fm, l_mlm, l_repa = self.model(x0, t, eps, **kw)
+            if l_repa is not None:
+                acc_repa += l_repa / self.accum
             (loss / self.accum).backward()
             acc += l_fm / self.accum
             if l_mlm is not None:
@@ -305,5 +330,5 @@ class Trainer:
                     self.ema.update(self.step_idx, D.ema_decay_at_sync(self.ema_decay, cfg.diloco, n))
         elif self.ema is not None:
             self.ema.update(self.step_idx)
-        self.last = dict(mlm=acc_mlm, gnorm=self.last_gnorm)
+        self.last = dict(mlm=acc_mlm, gnorm=self.last_gnorm, repa=acc_repa)
         return acc
