@@ -84,3 +84,26 @@ def test_train_with_repa_stand_in(shards, tmp_path):
     ck = torch.load(os.path.join(out, "latest.pt"), weights_only=False)
     assert ck["repa_proj"] is not None and "conv.weight" in ck["repa_proj"]
     assert len(ck["ema"]) == len(ck["te"]) + len(ck["den"]) or len(ck["ema"]) > 0
+
+
+def test_train_rpe2d_micro_cond_and_crops(tmp_path):
+    """RPE-2D positions, micro-conditioning fed from resize-and-crop windows of larger latents, t-shift-ref."""
+    import numpy as np
+
+    from trenowanie_generatora_obrazkow_b200.data.shards import write_synthetic_shards
+    d = str(tmp_path / "shards")
+    write_synthetic_shards(d, n_shards=2, per_shard=8, side=8)  # 128 px grids as the training resolution...
+    import glob
+    for f in glob.glob(os.path.join(d, "*.lat.npy")):  # ... and 256 px grids of the same images to crop from
+        base = f[: -len(".lat.npy")]
+        lat = np.load(f)
+        os.replace(f, base + ".lat128.npy")
+        np.save(f, np.repeat(np.repeat(lat, 2, axis=2), 2, axis=3))
+    out = str(tmp_path / "run")
+    _run(["--data", d, "--out", out, "--size", "50m", "--te-size", "13m", "--batch", "4", "--micro-batch", "2",
+          "--steps", "2", "--eval-every", "0", "--no-wandb", "--res", "128", "--rope-ref", "16", "--rope-random",
+          "--micro-cond", "256", "--crop-res", "256", "--crop-prob", "1.0", "--t-shift-ref", "256"])
+    import torch
+    ck = torch.load(os.path.join(out, "latest.pt"), weights_only=False)
+    assert ck["den_config"]["micro_cond"] == 256 and ck["den_config"]["rope_ref"] == 16
+    assert any(k.startswith("cond_mlp") for k in ck["den"])

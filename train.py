@@ -50,6 +50,16 @@ def build_parser():
     a("--random-lm", action="store_true", help="frozen-LM encoders: a fixed random embedding stands in for the LM")
     a("--ema-cpu", action="store_true")
     a("--pl-prob", type=float, default=0.0)
+    a("--rope-ref", type=int, default=0,
+      help="RoPE position field: 0 = integer positions per grid; N = every resolution spread over an N x N field")
+    a("--rope-random", action="store_true",
+      help="RPE-2D: random sorted distinct token positions of 0..rope-ref-1 per sample and axis (needs --rope-ref)")
+    a("--micro-cond", type=int, default=0,
+      help="micro-conditioning on (original size, crop box, target size); the original image size in px, 0 = off")
+    a("--crop-res", type=int, nargs="*", default=[],
+      help="resize-and-crop: take --res windows from these larger latent grids (<shard>.lat<res>.npy; 256 = .lat.npy)")
+    a("--crop-prob", type=float, default=0.5)
+    a("--t-shift-ref", type=float, default=0.0, help="resolution-dependent time shift res / REF (overrides --t-shift)")
     a("--repa-weight", type=float, default=0.0,
       help="REPA loss weight (0 = off; the reference's 0.5 needs DINOv2 targets, see --repa-target)")
     a("--repa-layer", type=int, default=None)
@@ -190,12 +200,14 @@ def main():
 
     den_cfg, te_cfg = make_configs(args.size, args.te_size, args.te_dim, args.te_depth, args.depth,
                                    args.te_experts, args.te_quant)
-    den_cfg = replace(den_cfg, latent_size=args.res // 16)
+    den_cfg = replace(den_cfg, latent_size=args.res // 16, rope_ref=args.rope_ref, micro_cond=args.micro_cond)
     ckpt_path = os.path.join(args.out, "latest.pt")
     resume = ckpt.load(ckpt_path) if os.path.exists(ckpt_path) else None
     if resume is not None:  # the checkpoint's architecture wins
         den_cfg = DenoiserConfig(**resume["den_config"])
         te_cfg = te_config_from_dict(resume["te_config"])
+    assert not args.rope_random or den_cfg.rope_ref, "--rope-random needs --rope-ref (the position field)"
+    assert not args.crop_res or den_cfg.micro_cond, "--crop-res needs --micro-cond"
     cuda = device.type == "cuda"
     transport = args.grad_transport if args.grad_transport != "auto" else ("p2p" if cuda else "nccl")
     grad_comm = "nccl_fp32" if args.grad_comm == "fp32" else "powersgd" if args.grad_comm == "powersgd" else \
@@ -212,6 +224,7 @@ def main():
                      mlm_every=args.mlm_every, mlm_prob=args.mlm_prob,
                      grad_comm=grad_comm, muon_comm=muon_comm, diloco=args.diloco,
                      powersgd_rank=args.powersgd_rank, powersgd_start=max(2, int(args.warmup_frac * args.steps)),
+                     rope_random=args.rope_random, t_shift_ref=args.t_shift_ref,
                      repa_weight=args.repa_weight, repa_layer=args.repa_layer, repa_frac=args.repa_frac,
                      repa_until=args.repa_until, repa_every=args.repa_every, repa_target=args.repa_target,
                      irepa=args.irepa,
@@ -261,8 +274,10 @@ def main():
         tok_suffix = getattr(te_cfg, "tok_suffix", "")
         null_row = te.null_ids()
         train_names, val_names = select_shards(args.data, args.fraction, tok_suffix)
+        crops = [("lat" if r == 256 else f"lat{r}", "") for r in args.crop_res]
         store = ShardStore(args.data, train_names, tok_suffix, null_row,
-                           lat_kind="lat" if side == 16 else f"lat{args.res}")
+                           lat_kind="lat" if side == 16 else f"lat{args.res}", crops=crops, crop_prob=args.crop_prob,
+                           cond_base=den_cfg.micro_cond)
         stream = TrainStream(store, tr.micro, rank, world, args.seed, start_micro=samples // (tr.micro * world))
         loader = iter(torch.utils.data.DataLoader(stream, batch_size=None, num_workers=args.workers,
                                                   pin_memory=device.type == "cuda",
@@ -312,6 +327,8 @@ def main():
         x0 = torch.cat([m[0] for m in micros])
         second = torch.cat([m[1] for m in micros])
         batch = {"x0": x0, ("lm_states" if lm_states_key else "ids"): second}
+        if den_cfg.micro_cond and len(micros[0]) > 2:
+            batch["cond"] = torch.cat([m[-1] for m in micros])
         loss = tr.step(batch)
         step += 1
         samples += args.batch

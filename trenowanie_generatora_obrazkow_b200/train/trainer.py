@@ -57,6 +57,8 @@ class TrainConfig:
     grad_comm: str = "nccl_bf16"
     shard_muon: bool = True
     muon_comm: str = "gather"     # "sharded": owner reduce-scatter + owner-only momentum/NS + fused update all-gather
+    rope_random: bool = False     # RPE-2D: random sorted token positions of 0..rope_ref-1 per sample and axis
+    t_shift_ref: float = 0.0      # > 0: resolution-dependent time shift s = res / t_shift_ref (overrides t_shift)
     repa_weight: float = 0.0      # > 0: REPA alignment of the block-repa_layer hidden state
     repa_layer: int = 0
     repa_frac: float = 0.25
@@ -190,6 +192,14 @@ class Trainer:
         if not self.lm_te:
             self.null_row = torch.as_tensor(te.null_ids(), device=self.device)
 
+    def _random_rope(self, b, side, mb):
+        """RPE-2D positions of micro-batch mb (reference train_pp.py:303-308): drawn from (seed, rank, mb) alone."""
+        from ..ops import reference as R
+        field = self.den_cfg.rope_ref or side
+        g = torch.Generator(device=self.device).manual_seed(self.cfg.seed * 4099 + mb * 131 + self.rank)
+        rows, cols = R.random_rope_coords(b, side, field, self.device, g)
+        return R.rope_2d_from_coords(rows, cols, self.den_cfg.dim // self.den_cfg.heads)
+
     def memory_report(self):
         from ..utils.memory import report
         grads = [p.grad for p in self.params if p.grad is not None]
@@ -275,8 +285,13 @@ class Trainer:
             b = x0.shape[0]
             kw = self._text_inputs(batch, sl, b)
             t = torch.sigmoid(torch.randn(b, device=self.device, generator=self.gen))
-            if cfg.t_shift != 1.0:
-                t = cfg.t_shift * t / (1 + (cfg.t_shift - 1) * t)
+            shift = x0.shape[-1] * 16 / cfg.t_shift_ref if cfg.t_shift_ref else cfg.t_shift
+            if shift != 1.0:
+                t = shift * t / (1 + (shift - 1) * t)
+            if batch.get("cond") is not None:  # micro-conditions of crops (original size, crop box, target size)
+                kw["cond"] = self._to_dev(batch["cond"][sl])
+            if cfg.rope_random:
+                kw["rope"] = self._random_rope(b, x0.shape[-1], self.step_idx * self.accum + m)
             eps = torch.randn(x0.shape, device=self.device, generator=self.gen)
             if self.buckets is not None and m == self.accum - 1:
                 self.buckets.arm()
