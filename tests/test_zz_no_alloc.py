@@ -74,7 +74,7 @@ def test_noalloc_matches_regular_entry_point_twice():
 def test_noalloc_rejects_oversized_problem():
     lib, f = _entry()
     cap = lib.tgo_noalloc_scratch_floats()
-    D = 8192
+    D = 4096
     B = cap // (4 * D) + 1  # one chunk per sample no longer fits
     x = torch.zeros(B, D, device="cuda", dtype=torch.bfloat16)
     w = torch.ones(D, device="cuda")

@@ -72,7 +72,7 @@ long long tgo_noalloc_scratch_floats() { return kNoAllocScratchFloats; }
 const char* tgo_noalloc_error_string(int code) {
   switch (code) {
     case TGO_NOALLOC_OK: return "ok";
-    case TGO_NOALLOC_BAD_ARGS: return "invalid arguments (null pointer, D % 8 != 0, D > 8192, or M % T != 0)";
+    case TGO_NOALLOC_BAD_ARGS: return "invalid arguments (null pointer, D % 8 != 0, D > 4096, or M % T != 0)";
     case TGO_NOALLOC_TOO_LARGE:
       return "problem too large for the fixed scratch array (needs B * 4 * D floats at least; capacity "
              "4194304 floats)";
@@ -93,7 +93,7 @@ int tgo_adanorm_bwd_noalloc(const void* dh, const void* dxe, const void* xn, con
                             void* dx, void* dy, float* dshift, float* dscale, float* dgate, float* dw, int M, int D,
                             int T, cudaStream_t stream) {
   if (dh == nullptr || xn == nullptr || rstd == nullptr || w == nullptr || dx == nullptr || dw == nullptr ||
-      M <= 0 || D <= 0 || T <= 0 || D % 8 != 0 || D > 8192 || M % T != 0)
+      M <= 0 || D <= 0 || T <= 0 || D % 8 != 0 || D > 4096 || M % T != 0)
     return TGO_NOALLOC_BAD_ARGS;
   if (scale != nullptr && (dshift == nullptr || dscale == nullptr)) return TGO_NOALLOC_BAD_ARGS;
   if (gate != nullptr && y != nullptr && (dy == nullptr || dgate == nullptr)) return TGO_NOALLOC_BAD_ARGS;

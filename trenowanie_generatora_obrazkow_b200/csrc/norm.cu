@@ -118,13 +118,43 @@ __global__ void adanorm_fwd_kernel(AdaNormFwdParams p) {
 // adanorm backward: row pass (dx, dy, per-CTA partial column sums)
 // partial layout: [B][chunks][4][D] = dshift, dscale, dgate, dw
 // ------------------------------------------------------------------------------------------------------------------
-__global__ void adanorm_bwd_kernel(AdaNormBwdParams p) {
-  __shared__ float red[64];
+// Two rows per iteration: both rows' inputs are loaded up front (raw bf16, 16 bytes per tensor and thread) so
+// twice the loads are in flight, and the two row dot products share one block reduction (half the barriers).
+__device__ __forceinline__ float2 block_sum2(float a, float b, float* red, int slot) {
+  a = warp_sum(a);
+  b = warp_sum(b);
+  const int nw = (blockDim.x + 31) >> 5;
+  if (lane_id() == 0) {
+    red[slot * 64 + warp_id()] = a;
+    red[slot * 64 + 32 + warp_id()] = b;
+  }
+  __syncthreads();
+  float sa = 0.f, sb = 0.f;
+  for (int i = 0; i < nw; ++i) {
+    sa += red[slot * 64 + i];
+    sb += red[slot * 64 + 32 + i];
+  }
+  return make_float2(sa, sb);
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__global__ void __launch_bounds__(512) adanorm_bwd_kernel(AdaNormBwdParams p) {
+  __shared__ float red[128];
   const int c0 = threadIdx.x * 8;
   const bool active = c0 < p.D;
   const int b = blockIdx.y, j = blockIdx.x;
   const int row0 = b * p.T + j * p.rows_per_cta;
   const int row1 = min((b + 1) * p.T, row0 + p.rows_per_cta);
+  const bool has_dxe = p.dxe != nullptr, has_y = p.y != nullptr && p.gate != nullptr;
   float w[8], sc1[8], g[8];
   float a_shift[8], a_scale[8], a_gate[8], a_w[8];
 #pragma unroll
@@ -140,43 +170,62 @@ __global__ void adanorm_bwd_kernel(AdaNormBwdParams p) {
     for (int i = 0; i < 8; ++i) sc1[i] += 1.f;
   }
   if (active && p.gate != nullptr) load8(p.gate + (long long)b * p.gate_bs + c0, g);
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
   int slot = 0;
-  for (int row = row0; row < row1; ++row, slot ^= 1) {
-    const long long off = (long long)row * p.D + c0;
-    const float r = p.rstd[row];
-    float n[8], dn[8];
-    float dot = 0.f;
-    if (active) {
+  for (int row = row0; row < row1; row += 2, slot ^= 1) {
+    const bool two = row + 1 < row1;
+    uint4 u_dh[2], u_xn[2], u_e[2], u_y[2];
+    float r[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {  // issue every load of both rows first
+      const bool ok = active && (k == 0 || two);
+      const long long off = (long long)(row + k) * p.D + c0;
+      u_dh[k] = ok ? *reinterpret_cast<const uint4*>(p.dh + off) : zero;
+      u_xn[k] = ok ? *reinterpret_cast<const uint4*>(p.xn + off) : zero;
+      u_e[k] = (ok && has_dxe) ? *reinterpret_cast<const uint4*>(p.dxe + off) : zero;
+      u_y[k] = (ok && has_y) ? *reinterpret_cast<const uint4*>(p.y + off) : zero;
+      r[k] = (k == 0 || two) ? p.rstd[row + k] : 0.f;
+    }
+    float dot[2] = {0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
       float dh[8], xn[8];
-      load8(p.dh + off, dh);
-      load8(p.xn + off, xn);
+      unpack8(u_dh[k], dh);
+      unpack8(u_xn[k], xn);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        n[i] = xn[i] * r;
-        const float u = n[i] * w[i];
+        const float n = xn[i] * r[k];
         const float du = dh[i] * sc1[i];
         a_shift[i] += dh[i];
-        a_scale[i] += dh[i] * u;
-        a_w[i] += du * n[i];
-        dn[i] = du * w[i];
-        dot += dn[i] * n[i];
+        a_scale[i] += dh[i] * n * w[i];
+        a_w[i] += du * n;
+        dot[k] += du * w[i] * n;
       }
     }
-    const float mdot = block_sum(dot, red, slot) / p.D;
-    if (active) {
-      float dx[8];
+    const float2 tot = block_sum2(dot[0], dot[1], red, slot);
+    const float mdot[2] = {tot.x / p.D, tot.y / p.D};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) dx[i] = r * (dn[i] - n[i] * mdot);
-      if (p.dxe != nullptr) {
+    for (int k = 0; k < 2; ++k) {
+      if (!active || (k == 1 && !two)) continue;
+      const long long off = (long long)(row + k) * p.D + c0;
+      float dh[8], xn[8], dx[8];
+      unpack8(u_dh[k], dh);
+      unpack8(u_xn[k], xn);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float n = xn[i] * r[k];
+        dx[i] = r[k] * (dh[i] * sc1[i] * w[i] - n * mdot[k]);
+      }
+      if (has_dxe) {
         float e[8];
-        load8(p.dxe + off, e);
+        unpack8(u_e[k], e);
 #pragma unroll
         for (int i = 0; i < 8; ++i) dx[i] += e[i];
       }
       store8(p.dx + off, dx);
-      if (p.y != nullptr && p.gate != nullptr) {
+      if (has_y) {
         float y[8], dy[8];
-        load8(p.y + off, y);
+        unpack8(u_y[k], y);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           a_gate[i] += dx[i] * y[i];

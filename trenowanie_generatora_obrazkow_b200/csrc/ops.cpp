@@ -91,7 +91,7 @@ static CUtensorMap make_tmap_bhtd(const void* base, uint64_t hd, uint64_t T, uin
 static bool g_attention_tc = true;
 void set_attention_tc(bool on) { g_attention_tc = on; }
 
-static bool g_gemm_pair_enabled = false;  // measured slower than the 1-CTA kernel on most shapes so far
+static bool g_gemm_pair_enabled = true;  // 256 x 256 CTA-pair tiles: 3-6 % faster on the training shapes
 void set_gemm_pair(bool on) { g_gemm_pair_enabled = on; }
 
 static int* err_ptr(const at::Tensor& err) {
@@ -236,6 +236,7 @@ std::vector<at::Tensor> adanorm_bwd(at::Tensor dh, c10::optional<at::Tensor> dxe
   TORCH_CHECK(M % T == 0, "adanorm_bwd: M % T");
   const int64_t B = M / T;
   TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.is_contiguous() && dw.numel() == D, "adanorm_bwd: dw fp32 [D]");
+  TORCH_CHECK(D <= 4096, "adanorm_bwd: D <= 4096 (one thread per 8 channels, at most 512 threads)");
   if (dxe.has_value() && dxe->defined()) TORCH_CHECK(dxe->is_contiguous() && dxe->sizes() == dh.sizes(), "dxe");
   AdaNormBwdParams p{};
   p.dh = bfp(dh);

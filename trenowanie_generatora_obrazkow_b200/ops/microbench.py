@@ -68,18 +68,26 @@ def _bf16(*shape, scale=1.0):
 # ------------------------------------------------------------------------------------------------------------------
 # op builders: each returns (ours, library, flops, bytes)
 # ------------------------------------------------------------------------------------------------------------------
-def gemm_case(M, N, K):
-    a, b = _bf16(M, K), _bf16(N, K)
-    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+def gemm_case(M, N, K, a_mn=False, b_mn=False, accumulate=False):
+    """C[M, N] = op(A) op(B)^T; a_mn / b_mn: the operand is stored K-rows (MN-major), as in dgrad / wgrad;
+    accumulate: fp32 C += (the weight-gradient epilogue)."""
+    a = _bf16(K, M) if a_mn else _bf16(M, K)
+    b = _bf16(K, N) if b_mn else _bf16(N, K)
+    out = torch.zeros(M, N, dtype=torch.float32 if accumulate else torch.bfloat16, device="cuda")
     err = err_buf(a.device)
+    A = a.t() if a_mn else a
+    B = b if b_mn else b.t()
 
     def ours():
-        ext().gemm(a, b, out, False, False, None, 1.0, 0.0, False, err)
+        ext().gemm(a, b, out, a_mn, b_mn, None, 1.0, 0.0, accumulate, err)
 
     def lib():
-        torch.matmul(a, b.t(), out=out)
+        if accumulate:
+            out.add_(torch.matmul(A, B))
+        else:
+            torch.matmul(A, B, out=out)
 
-    return ours, lib, 2.0 * M * N * K, 2 * (M * K + N * K + M * N)
+    return ours, lib, 2.0 * M * N * K, 2 * (M * K + N * K) + out.element_size() * M * N * (2 if accumulate else 1)
 
 
 def attn_case(B, T, H, hd, backward):
@@ -206,6 +214,9 @@ def cases(small):
         "gemm_out": lambda: gemm_case(M, D, D),
         "gemm_mlp_up": lambda: gemm_case(M, 2 * MLP, D),
         "gemm_mlp_down": lambda: gemm_case(M, D, MLP),
+        "dgrad_qkv": lambda: gemm_case(M, D, 3 * D, b_mn=True),
+        "wgrad_qkv": lambda: gemm_case(3 * D, D, M, a_mn=True, b_mn=True, accumulate=True),
+        "wgrad_mlp_down": lambda: gemm_case(D, MLP, M, a_mn=True, b_mn=True, accumulate=True),
         "attn_fwd": lambda: attn_case(B, T, H, hd, False),
         "attn_bwd": lambda: attn_case(B, T, H, hd, True),
         "adanorm_fwd": lambda: adanorm_case(B, T, D, False),
@@ -246,8 +257,11 @@ def main(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--small", action="store_true")
     p.add_argument("--no-library", action="store_true", help="time only our kernels (profiler captures)")
+    p.add_argument("--gemm-pair", type=int, default=-1, help="1 / 0: force the 2-CTA GEMM on / off")
     a = p.parse_args(argv)
     torch.manual_seed(0)
+    if a.gemm_pair >= 0:
+        ext().set_gemm_pair(bool(a.gemm_pair))
     peaks = measured_peaks()
     table = cases(a.small)
     names = list(table) if a.op == "all" else a.op.split(",")
