@@ -244,32 +244,55 @@ __global__ void __launch_bounds__(FA_FWD_THREADS, 1) flash_fwd_kernel(AttnParams
 // ------------------------------------------------------------------------------------------------------------------
 // backward preprocessing: delta[b, h, t] = sum_d dO * O
 // ------------------------------------------------------------------------------------------------------------------
+// HD / 8 lanes per (b, t, h) row, 16-byte loads, four rows per thread in flight (grid-stride), shuffle reduction
+// inside each row's lane group.
 template <int HD>
-__global__ void flash_bwd_delta_kernel(AttnParams p, const bf16* __restrict__ dO, float* __restrict__ delta,
-                                       float* __restrict__ lse2) {
-  const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp_id();
-  const long long total = (long long)p.B * p.Tq * p.Hq;
-  if (item >= total) return;
-  const int h = (int)(item % p.Hq);
-  const long long bt = item / p.Hq;
-  const int t = (int)(bt % p.Tq), b = (int)(bt / p.Tq);
-  constexpr int E = HD / 32;
-  const int lane = lane_id();
-  const bf16* og = p.o + (long long)b * p.o_bs + (long long)t * p.o_ts + (long long)h * p.o_hs + lane * E;
-  const bf16* dg = dO + (long long)b * p.o_bs + (long long)t * p.o_ts + (long long)h * p.o_hs + lane * E;
-  float s = 0.f;
+__global__ void __launch_bounds__(256) flash_bwd_delta_kernel(AttnParams p, const bf16* __restrict__ dO,
+                                                              float* __restrict__ delta, float* __restrict__ lse2) {
+  constexpr int LPR = HD / 8;  // lanes per row
+  constexpr int U = 4;
+  // 32-bit index arithmetic (the launcher checks B * Tq * Hq < 2^31): 64-bit divisions per row cost more than the
+  // memory traffic of the row
+  const int total = p.B * p.Tq * p.Hq;
+  const int rows_per_pass = gridDim.x * (blockDim.x / LPR);
+  const int first = blockIdx.x * (blockDim.x / LPR) + threadIdx.x / LPR;
+  const int sub = threadIdx.x % LPR;
+  for (int base = first; base < total; base += U * rows_per_pass) {
+    uint4 a[U], d[U];
+    int hh[U], tt[U], bb[U];
 #pragma unroll
-  for (int i = 0; i < E; i += 2) {
-    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(og + i));
-    const float2 d = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dg + i));
-    s += a.x * d.x + a.y * d.y;
-  }
+    for (int u = 0; u < U; ++u) {
+      const int item = base + u * rows_per_pass;
+      a[u] = d[u] = make_uint4(0u, 0u, 0u, 0u);
+      hh[u] = item % p.Hq;
+      const int bt = item / p.Hq;
+      tt[u] = bt % p.Tq;
+      bb[u] = item < total ? bt / p.Tq : -1;
+      if (bb[u] >= 0) {
+        const long long off =
+            (long long)bb[u] * p.o_bs + (long long)tt[u] * p.o_ts + (long long)hh[u] * p.o_hs + sub * 8;
+        a[u] = *reinterpret_cast<const uint4*>(p.o + off);
+        d[u] = *reinterpret_cast<const uint4*>(dO + off);
+      }
+    }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) {
-    const long long idx = ((long long)b * p.Hq + h) * p.Tq + t;
-    delta[idx] = s;
-    if (lse2 != nullptr) lse2[idx] = p.lse[idx] * 1.4426950408889634f;  // log-sum-exp in base-2 units
+    for (int u = 0; u < U; ++u) {
+      const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&a[u]);
+      const __nv_bfloat162* hd = reinterpret_cast<const __nv_bfloat162*>(&d[u]);
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 x = __bfloat1622float2(ha[k]), y = __bfloat1622float2(hd[k]);
+        s += x.x * y.x + x.y * y.y;
+      }
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (sub == 0 && bb[u] >= 0) {
+        const long long idx = ((long long)bb[u] * p.Hq + hh[u]) * p.Tq + tt[u];
+        delta[idx] = s;
+        if (lse2 != nullptr) lse2[idx] = p.lse[idx] * 1.4426950408889634f;  // log-sum-exp in base-2 units
+      }
+    }
   }
 }
 
@@ -502,6 +525,13 @@ __global__ void dq_convert_kernel(AttnParams p, const float* __restrict__ acc, b
 // ------------------------------------------------------------------------------------------------------------------
 // launchers
 // ------------------------------------------------------------------------------------------------------------------
+// delta kernel grid: 256 threads cover 256 / (hd / 8) rows per pass; at most 8 resident blocks per SM worth
+static unsigned delta_grid(long long items, int hd) {  // items < 2^31 (checked by the callers)
+  const long long rows_per_block = 256 / (hd / 8);
+  const long long want = (items + rows_per_block - 1) / rows_per_block;
+  return (unsigned)std::min<long long>(want, (long long)num_sms() * 8);
+}
+
 template <int HD>
 static cudaError_t fwd_impl(const AttnParams& p, cudaStream_t s) {
   const int smem = (FA_BM + 4 * FA_BN) * HD * 2;
@@ -528,7 +558,8 @@ static cudaError_t bwd_impl(const AttnParams& p, const bf16* dO, float* delta, f
                             cudaStream_t s) {
   {
     const long long items = (long long)p.B * p.Tq * p.Hq;
-    flash_bwd_delta_kernel<HD><<<(unsigned)((items + 7) / 8), 256, 0, s>>>(p, dO, delta, nullptr);
+    if (items >= (1ll << 31)) return cudaErrorInvalidValue;
+    flash_bwd_delta_kernel<HD><<<delta_grid(items, HD), 256, 0, s>>>(p, dO, delta, nullptr);
   }
   cudaError_t e = cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)p.B * p.Tq * p.Hq * HD, s);
   if (e != cudaSuccess) return e;
@@ -555,8 +586,9 @@ static cudaError_t bwd_impl(const AttnParams& p, const bf16* dO, float* delta, f
 cudaError_t attention_bwd_prep_launch(const AttnParams& p, const bf16* dO, float* delta, float* dq_acc, cudaStream_t s,
                                       float* lse2) {
   const long long items = (long long)p.B * p.Tq * p.Hq;
-  if (p.hd == 128) flash_bwd_delta_kernel<128><<<(unsigned)((items + 7) / 8), 256, 0, s>>>(p, dO, delta, lse2);
-  else if (p.hd == 64) flash_bwd_delta_kernel<64><<<(unsigned)((items + 7) / 8), 256, 0, s>>>(p, dO, delta, lse2);
+  if (items >= (1ll << 31)) return cudaErrorInvalidValue;
+  if (p.hd == 128) flash_bwd_delta_kernel<128><<<delta_grid(items, 128), 256, 0, s>>>(p, dO, delta, lse2);
+  else if (p.hd == 64) flash_bwd_delta_kernel<64><<<delta_grid(items, 64), 256, 0, s>>>(p, dO, delta, lse2);
   else return cudaErrorInvalidValue;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

@@ -60,8 +60,13 @@ __device__ __forceinline__ float block_sum(float v, float* red, int slot) {
 // ------------------------------------------------------------------------------------------------------------------
 // adanorm forward
 // ------------------------------------------------------------------------------------------------------------------
-__global__ void adanorm_fwd_kernel(AdaNormFwdParams p) {
-  __shared__ float red[64];
+__device__ __forceinline__ float2 block_sum2(float a, float b, float* red, int slot);
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]);
+
+// Two rows per iteration: every load of both rows is issued first and their sums of squares share one block
+// reduction (half the barriers, twice the loads in flight).
+__global__ void __launch_bounds__(1024) adanorm_fwd_kernel(AdaNormFwdParams p) {
+  __shared__ float red[128];
   const int c0 = threadIdx.x * 8;
   const bool active = c0 < p.D;
   float w[8];
@@ -69,39 +74,54 @@ __global__ void adanorm_fwd_kernel(AdaNormFwdParams p) {
   for (int i = 0; i < 8; ++i) w[i] = active ? p.w[c0 + i] : 0.f;
   const int row0 = blockIdx.x * p.rows_per_cta;
   const int row1 = min(p.M, row0 + p.rows_per_cta);
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
   int slot = 0;
-  for (int row = row0; row < row1; ++row, slot ^= 1) {
-    const int b = row / p.T;
-    const long long off = (long long)row * p.D + c0;
-    float x[8];
-    float ss = 0.f;
-    if (active) {
-      load8(p.x + off, x);
+  for (int row = row0; row < row1; row += 2, slot ^= 1) {
+    const bool two = row + 1 < row1;
+    uint4 ux[2], uy[2], ug[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const bool ok = active && (k == 0 || two);
+      const long long off = (long long)(row + k) * p.D + c0;
+      const int b = (row + k) / p.T;
+      ux[k] = ok ? *reinterpret_cast<const uint4*>(p.x + off) : zero;
+      uy[k] = (ok && p.y != nullptr) ? *reinterpret_cast<const uint4*>(p.y + off) : zero;
+      ug[k] = (ok && p.y != nullptr && p.gate != nullptr)
+                  ? *reinterpret_cast<const uint4*>(p.gate + (long long)b * p.gate_bs + c0) : zero;
+    }
+    float x[2][8], ss[2] = {0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      unpack8(ux[k], x[k]);
       if (p.y != nullptr) {
         float y[8];
-        load8(p.y + off, y);
+        unpack8(uy[k], y);
         if (p.gate != nullptr) {
           float g[8];
-          load8(p.gate + (long long)b * p.gate_bs + c0, g);
+          unpack8(ug[k], g);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) x[i] = bf16_round(x[i] + bf16_round(g[i] * y[i]));
+          for (int i = 0; i < 8; ++i) x[k][i] = bf16_round(x[k][i] + bf16_round(g[i] * y[i]));
         } else {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) x[i] = bf16_round(x[i] + y[i]);
+          for (int i = 0; i < 8; ++i) x[k][i] = bf16_round(x[k][i] + y[i]);
         }
-        store8(p.x_out + off, x);
+        if (active && (k == 0 || two)) store8(p.x_out + (long long)(row + k) * p.D + c0, x[k]);
       }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+      for (int i = 0; i < 8; ++i) ss[k] += x[k][i] * x[k][i];
     }
-    const float tot = block_sum(ss, red, slot);
-    const float r = rsqrtf(tot / p.D + p.eps);
-    if (threadIdx.x == 0) p.rstd[row] = r;
-    if (active) {
+    const float2 tot = block_sum2(ss[0], ss[1], red, slot);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (k == 1 && !two) break;
+      const float r = rsqrtf((k == 0 ? tot.x : tot.y) / p.D + p.eps);
+      if (threadIdx.x == 0) p.rstd[row + k] = r;
+      if (!active) continue;
+      const int b = (row + k) / p.T;
       const float rb = bf16_round(r);
       float h[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) h[i] = bf16_round(x[i] * rb) * w[i];
+      for (int i = 0; i < 8; ++i) h[i] = bf16_round(x[k][i] * rb) * w[i];
       if (p.scale != nullptr) {
         float sc[8], sh[8];
         load8(p.scale + (long long)b * p.mod_bs + c0, sc);
@@ -109,7 +129,7 @@ __global__ void adanorm_fwd_kernel(AdaNormFwdParams p) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) h[i] = h[i] * (1.f + sc[i]) + sh[i];
       }
-      store8(p.h + off, h);
+      store8(p.h + (long long)(row + k) * p.D + c0, h);
     }
   }
 }
@@ -288,129 +308,148 @@ cudaError_t adanorm_bwd_launch(const AdaNormBwdParams& p, float* dshift, float* 
 }
 
 // ------------------------------------------------------------------------------------------------------------------
-// q/k RMSNorm + RoPE.  One warp per (row, head); HD / 32 contiguous elements per lane.
+// q/k RMSNorm + RoPE. HD / 8 lanes per (row, head) item, 8 contiguous elements (16 bytes) per lane, so a warp
+// covers 32 / (HD / 8) items; RoPE pairs (even, odd) never straddle lanes.
 // ------------------------------------------------------------------------------------------------------------------
-template <int HD>
-__global__ void qknorm_rope_fwd_kernel(QKNormRopeParams p) {
-  constexpr int E = HD / 32;
-  const int heads = p.hq + p.hkv;
-  const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp_id();
-  if (item >= (long long)p.M * heads) return;
-  const int row = (int)(item / heads), hh = (int)(item % heads);
-  const bool is_q = hh < p.hq;
-  const int lane = lane_id();
-  const int e0 = lane * E;
-  const bf16* src = p.qkv + (long long)row * p.ld_qkv + (long long)hh * HD + e0;
-  float x[E];
+template <int LPH>
+__device__ __forceinline__ float group_sum(float v) {  // sum over aligned groups of LPH lanes
 #pragma unroll
-  for (int i = 0; i < E; i += 2) {
-    float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + i));
-    x[i] = t.x;
-    x[i + 1] = t.y;
+  for (int o = LPH / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ void load8f(const float* p, float (&f)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  f[0] = a.x, f[1] = a.y, f[2] = a.z, f[3] = a.w, f[4] = b.x, f[5] = b.y, f[6] = b.z, f[7] = b.w;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256) qknorm_rope_fwd_kernel(QKNormRopeParams p) {
+  constexpr int LPH = HD / 8, IPW = 32 / LPH;
+  const int heads = p.hq + p.hkv;
+  const long long total = (long long)p.M * heads;
+  const long long item = ((long long)blockIdx.x * (blockDim.x >> 5) + warp_id()) * IPW + lane_id() / LPH;
+  const bool valid = item < total;  // invalid lanes still take part in the shuffles
+  const int row = valid ? (int)(item / heads) : 0, hh = valid ? (int)(item % heads) : 0;
+  const bool is_q = hh < p.hq;
+  const int e0 = (lane_id() % LPH) * 8;
+  float x[8];
+  if (valid) load8(p.qkv + (long long)row * p.ld_qkv + (long long)hh * HD + e0, x);
+  else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = 0.f;
   }
   const float* nw = is_q ? p.q_w : p.k_w;
-  float r = 1.f;
   if (nw != nullptr) {
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < E; ++i) ss += x[i] * x[i];
-    ss = warp_sum(ss);
-    r = rsqrtf(ss / HD + p.eps);
+    for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+    ss = group_sum<LPH>(ss);
+    const float r = rsqrtf(ss / HD + p.eps);
     const float rb = bf16_round(r);
+    float w8[8];
+    load8f(nw + e0, w8);
 #pragma unroll
-    for (int i = 0; i < E; ++i) x[i] = bf16_round(x[i] * rb) * nw[e0 + i];
-    if (lane == 0) (is_q ? p.rstd_q : p.rstd_k)[(long long)row * (is_q ? p.hq : p.hkv) + (is_q ? hh : hh - p.hq)] = r;
+    for (int i = 0; i < 8; ++i) x[i] = bf16_round(x[i] * rb) * w8[i];
+    if (valid && e0 == 0) (is_q ? p.rstd_q : p.rstd_k)[(long long)row * (is_q ? p.hq : p.hkv) + (is_q ? hh : hh - p.hq)] = r;
   }
-  if (p.cos != nullptr) {
+  if (p.cos != nullptr && valid) {
     const int b = row / p.T, t = row % p.T;
-    const float* cs = p.cos + (long long)b * p.rope_bs + (long long)t * HD + e0;
-    const float* sn = p.sin + (long long)b * p.rope_bs + (long long)t * HD + e0;
+    float cs[8], sn[8];
+    load8f(p.cos + (long long)b * p.rope_bs + (long long)t * HD + e0, cs);
+    load8f(p.sin + (long long)b * p.rope_bs + (long long)t * HD + e0, sn);
 #pragma unroll
-    for (int i = 0; i < E; i += 2) {
+    for (int i = 0; i < 8; i += 2) {
       const float a = x[i], c = x[i + 1];
       x[i] = a * cs[i] - c * sn[i];
       x[i + 1] = c * cs[i + 1] + a * sn[i + 1];
     }
   }
-  bf16* dst = is_q ? p.q_out + (long long)row * p.ld_q + (long long)hh * HD + e0
-                   : p.k_out + (long long)row * p.ld_k + (long long)(hh - p.hq) * HD + e0;
-#pragma unroll
-  for (int i = 0; i < E; i += 2) *reinterpret_cast<__nv_bfloat162*>(dst + i) = __floats2bfloat162_rn(x[i], x[i + 1]);
+  if (valid) {
+    bf16* dst = is_q ? p.q_out + (long long)row * p.ld_q + (long long)hh * HD + e0
+                     : p.k_out + (long long)row * p.ld_k + (long long)(hh - p.hq) * HD + e0;
+    store8(dst, x);
+  }
 }
 
 // Backward: dq / dk (post-RoPE) -> d(pre-norm q / k) written into dqkv; dw_q, dw_k accumulated (+=).
-// Persistent grid: each warp walks (row, head) items with a grid stride and keeps its dw partials in registers;
+// Persistent grid: each lane group walks (row, head) items with a grid stride and keeps its dw partials in registers;
 // one shared-memory reduction and one global atomic per element and CTA at the end.
 template <int HD>
-__global__ void qknorm_rope_bwd_kernel(QKNormRopeParams p, const bf16* __restrict__ dq, long long ld_dq,
-                                       const bf16* __restrict__ dk, long long ld_dk, bf16* __restrict__ dqkv,
-                                       long long ld_dqkv, float* __restrict__ dwq, float* __restrict__ dwk) {
-  constexpr int E = HD / 32;
+__global__ void __launch_bounds__(512) qknorm_rope_bwd_kernel(QKNormRopeParams p, const bf16* __restrict__ dq,
+                                                              long long ld_dq, const bf16* __restrict__ dk,
+                                                              long long ld_dk, bf16* __restrict__ dqkv,
+                                                              long long ld_dqkv, float* __restrict__ dwq,
+                                                              float* __restrict__ dwk) {
+  constexpr int LPH = HD / 8, IPW = 32 / LPH;
   __shared__ float s_dw[2][HD];
   for (int i = threadIdx.x; i < 2 * HD; i += blockDim.x) (&s_dw[0][0])[i] = 0.f;
   __syncthreads();
   const int heads = p.hq + p.hkv;
   const long long total = (long long)p.M * heads;
-  const int lane = lane_id();
-  const int e0 = lane * E;
-  float acc_q[E], acc_k[E];
+  const int e0 = (lane_id() % LPH) * 8;
+  float acc_q[8], acc_k[8];
 #pragma unroll
-  for (int i = 0; i < E; ++i) acc_q[i] = acc_k[i] = 0.f;
-  const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp_id(); item < total; item += nwarps) {
-    const int row = (int)(item / heads), hh = (int)(item % heads);
+  for (int i = 0; i < 8; ++i) acc_q[i] = acc_k[i] = 0.f;
+  const long long stride = (long long)gridDim.x * (blockDim.x >> 5) * IPW;
+  const long long first = ((long long)blockIdx.x * (blockDim.x >> 5) + warp_id()) * IPW + lane_id() / LPH;
+  // every lane of a warp runs the same number of iterations (shuffles inside); items past the end are masked
+  const long long warp_first = first - lane_id() / LPH;
+  for (long long wbase = warp_first; wbase < total; wbase += stride) {
+    const long long item = wbase + lane_id() / LPH;
+    const bool valid = item < total;
+    const int row = valid ? (int)(item / heads) : 0, hh = valid ? (int)(item % heads) : 0;
     const bool is_q = hh < p.hq;
-    const bf16* gsrc = is_q ? dq + (long long)row * ld_dq + (long long)hh * HD + e0
-                            : dk + (long long)row * ld_dk + (long long)(hh - p.hq) * HD + e0;
-    float g[E];
+    float g[8];
+    if (valid) {
+      const bf16* gsrc = is_q ? dq + (long long)row * ld_dq + (long long)hh * HD + e0
+                              : dk + (long long)row * ld_dk + (long long)(hh - p.hq) * HD + e0;
+      load8(gsrc, g);
+    } else {
 #pragma unroll
-    for (int i = 0; i < E; i += 2) {
-      float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gsrc + i));
-      g[i] = t.x;
-      g[i + 1] = t.y;
+      for (int i = 0; i < 8; ++i) g[i] = 0.f;
     }
-    if (p.cos != nullptr) {  // transpose of the rotation
+    if (p.cos != nullptr && valid) {  // transpose of the rotation
       const int b = row / p.T, t = row % p.T;
-      const float* cs = p.cos + (long long)b * p.rope_bs + (long long)t * HD + e0;
-      const float* sn = p.sin + (long long)b * p.rope_bs + (long long)t * HD + e0;
+      float cs[8], sn[8];
+      load8f(p.cos + (long long)b * p.rope_bs + (long long)t * HD + e0, cs);
+      load8f(p.sin + (long long)b * p.rope_bs + (long long)t * HD + e0, sn);
 #pragma unroll
-      for (int i = 0; i < E; i += 2) {
+      for (int i = 0; i < 8; i += 2) {
         const float a = g[i], c = g[i + 1];
         g[i] = a * cs[i] + c * sn[i + 1];
         g[i + 1] = c * cs[i + 1] - a * sn[i];
       }
     }
     const float* nw = is_q ? p.q_w : p.k_w;
-    if (nw != nullptr) {
-      const bf16* src = p.qkv + (long long)row * p.ld_qkv + (long long)hh * HD + e0;
-      float x[E];
+    if (nw != nullptr) {  // uniform per warp: q_w and k_w are both given or both absent
+      float x[8], w8[8];
+      if (valid) load8(p.qkv + (long long)row * p.ld_qkv + (long long)hh * HD + e0, x);
+      else {
 #pragma unroll
-      for (int i = 0; i < E; i += 2) {
-        float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + i));
-        x[i] = t.x;
-        x[i + 1] = t.y;
+        for (int i = 0; i < 8; ++i) x[i] = 0.f;
       }
-      const float r = (is_q ? p.rstd_q : p.rstd_k)[(long long)row * (is_q ? p.hq : p.hkv) + (is_q ? hh : hh - p.hq)];
+      load8f(nw + e0, w8);
+      const float r = valid ? (is_q ? p.rstd_q : p.rstd_k)[(long long)row * (is_q ? p.hq : p.hkv) +
+                                                           (is_q ? hh : hh - p.hq)]
+                            : 0.f;
       float dot = 0.f;
 #pragma unroll
-      for (int i = 0; i < E; ++i) {
+      for (int i = 0; i < 8; ++i) {
         const float n = x[i] * r;
         if (is_q) acc_q[i] += g[i] * n;
         else acc_k[i] += g[i] * n;
-        g[i] *= nw[e0 + i];  // dn
+        g[i] *= w8[i];  // dn
         dot += g[i] * n;
         x[i] = n;
       }
-      dot = warp_sum(dot) / HD;
+      dot = group_sum<LPH>(dot) / HD;
 #pragma unroll
-      for (int i = 0; i < E; ++i) g[i] = r * (g[i] - x[i] * dot);
+      for (int i = 0; i < 8; ++i) g[i] = r * (g[i] - x[i] * dot);
     }
-    bf16* dst = dqkv + (long long)row * ld_dqkv + (long long)hh * HD + e0;
-#pragma unroll
-    for (int i = 0; i < E; i += 2) *reinterpret_cast<__nv_bfloat162*>(dst + i) = __floats2bfloat162_rn(g[i], g[i + 1]);
+    if (valid) store8(dqkv + (long long)row * ld_dqkv + (long long)hh * HD + e0, g);
   }
 #pragma unroll
-  for (int i = 0; i < E; ++i) {
+  for (int i = 0; i < 8; ++i) {
     atomicAdd(&s_dw[0][e0 + i], acc_q[i]);
     atomicAdd(&s_dw[1][e0 + i], acc_k[i]);
   }
@@ -423,10 +462,10 @@ __global__ void qknorm_rope_bwd_kernel(QKNormRopeParams p, const bf16* __restric
 
 cudaError_t qknorm_rope_fwd_launch(const QKNormRopeParams& p, cudaStream_t s) {
   const long long items = (long long)p.M * (p.hq + p.hkv);
-  const int warps = 8;
-  const unsigned grid = (unsigned)((items + warps - 1) / warps);
-  if (p.hd == 128) qknorm_rope_fwd_kernel<128><<<grid, warps * 32, 0, s>>>(p);
-  else if (p.hd == 64) qknorm_rope_fwd_kernel<64><<<grid, warps * 32, 0, s>>>(p);
+  const int per_block = 8 * (32 / (p.hd / 8));  // 8 warps
+  const unsigned grid = (unsigned)((items + per_block - 1) / per_block);
+  if (p.hd == 128) qknorm_rope_fwd_kernel<128><<<grid, 256, 0, s>>>(p);
+  else if (p.hd == 64) qknorm_rope_fwd_kernel<64><<<grid, 256, 0, s>>>(p);
   else return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
@@ -435,12 +474,12 @@ cudaError_t qknorm_rope_bwd_launch(const QKNormRopeParams& p, const bf16* dq, lo
                                    long long ld_dk, bf16* dqkv, long long ld_dqkv, float* dwq, float* dwk,
                                    cudaStream_t s) {
   const long long items = (long long)p.M * (p.hq + p.hkv);
-  const int warps = 16;
-  const unsigned grid = (unsigned)std::min<long long>((items + warps - 1) / warps, (long long)num_sms() * 4);
+  const int per_block = 16 * (32 / (p.hd / 8));  // 16 warps
+  const unsigned grid = (unsigned)std::min<long long>((items + per_block - 1) / per_block, (long long)num_sms() * 4);
   if (p.hd == 128)
-    qknorm_rope_bwd_kernel<128><<<grid, warps * 32, 0, s>>>(p, dq, ld_dq, dk, ld_dk, dqkv, ld_dqkv, dwq, dwk);
+    qknorm_rope_bwd_kernel<128><<<grid, 512, 0, s>>>(p, dq, ld_dq, dk, ld_dk, dqkv, ld_dqkv, dwq, dwk);
   else if (p.hd == 64)
-    qknorm_rope_bwd_kernel<64><<<grid, warps * 32, 0, s>>>(p, dq, ld_dq, dk, ld_dk, dqkv, ld_dqkv, dwq, dwk);
+    qknorm_rope_bwd_kernel<64><<<grid, 512, 0, s>>>(p, dq, ld_dq, dk, ld_dk, dqkv, ld_dqkv, dwq, dwk);
   else return cudaErrorInvalidValue;
   return cudaGetLastError();
 }

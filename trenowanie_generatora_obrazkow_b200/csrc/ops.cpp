@@ -288,6 +288,7 @@ static QKNormRopeParams qk_params(const at::Tensor& qkv, int64_t hq, int64_t hkv
   p.ld_qkv = qkv.stride(0);
   p.q_w = f32_ptr_or_null(q_w);
   p.k_w = f32_ptr_or_null(k_w);
+  TORCH_CHECK((p.q_w == nullptr) == (p.k_w == nullptr), "qknorm_rope: q and k norm weights both or neither");
   p.cos = f32_ptr_or_null(cos);
   p.sin = f32_ptr_or_null(sin);
   if (p.cos != nullptr) {
@@ -336,7 +337,8 @@ void qknorm_rope_bwd(at::Tensor qkv, int64_t hq, int64_t hkv, int64_t hd, c10::o
   QKNormRopeParams p = qk_params(qkv, hq, hkv, hd, q_w, k_w, cos, sin, T, 1e-6);
   p.rstd_q = rstd_q.has_value() && rstd_q->defined() ? rstd_q->data_ptr<float>() : nullptr;
   p.rstd_k = rstd_k.has_value() && rstd_k->defined() ? rstd_k->data_ptr<float>() : nullptr;
-  TORCH_CHECK(dq.stride(-1) == 1 && dk.stride(-1) == 1 && dqkv.stride(-1) == 1, "qknorm_rope_bwd: layouts");
+  TORCH_CHECK(dq.stride(-1) == 1 && dk.stride(-1) == 1 && dqkv.stride(-1) == 1 && dq.stride(0) % 8 == 0 &&
+                  dk.stride(0) % 8 == 0 && dqkv.stride(0) % 8 == 0, "qknorm_rope_bwd: layouts (16-byte rows)");
   TGO_CHECK_LAUNCH(qknorm_rope_bwd_launch(p, bfp(dq), dq.stride(0), bfp(dk), dk.stride(0), bfp(dqkv), dqkv.stride(0),
                                           const_cast<float*>(f32_ptr_or_null(dwq)),
                                           const_cast<float*>(f32_ptr_or_null(dwk)), at::cuda::getCurrentCUDAStream()));
