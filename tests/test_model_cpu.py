@@ -166,3 +166,46 @@ def test_slayer_gpt_matches_reference():
     with torch.no_grad():
         a, b = ref_model.hidden(idx, 2), ours.hidden(idx, 2)
     assert torch.allclose(a, b, atol=1e-5), (a - b).abs().max()
+
+
+def test_slayer_packed_states_match_padded():
+    """Packed captions (varlen causal attention, positions restarting per caption) give the padded LM's states for
+    every real token, zeros at pads and on null-prompt rows."""
+    from trenowanie_generatora_obrazkow_b200.models.frozen_lm import LM_NULL, LM_PAD, SlayerFrozenLM
+    from trenowanie_generatora_obrazkow_b200.models.slayer import GPT, GPTConfig
+    torch.manual_seed(0)
+    cfg = GPTConfig(vocab=300, n_layer=3, n_embd=64, n_head=4, block=64)
+    gpt = GPT(cfg)
+    with torch.no_grad():
+        for blk in gpt.blocks[1:]:
+            blk.vr_lambda.fill_(0.25)
+    lm_pad = SlayerFrozenLM(None, skip_last=1, model=gpt, dtype=torch.float32, packed=False)
+    lm_pack = SlayerFrozenLM(None, skip_last=1, model=gpt, dtype=torch.float32, packed=True, max_tokens=20)
+    ids = torch.randint(0, 300, (4, 12))
+    lens = [12, 5, 1, 9]
+    for r, n in enumerate(lens):
+        ids[r, n:] = LM_PAD
+    ids[2, 0] = LM_NULL  # a null prompt: not run
+    a, b = lm_pad.states(ids), lm_pack.states(ids)
+    assert b.shape == a.shape
+    for r, n in enumerate(lens):
+        if r == 2:
+            assert b[r].abs().max() == 0
+            continue
+        assert torch.allclose(a[r, :n], b[r, :n], atol=1e-5), (r, (a[r, :n] - b[r, :n]).abs().max())
+        assert n == ids.shape[1] or b[r, n:].abs().max() == 0
+
+
+def test_varlen_attention_oracle_matches_per_sequence_sdpa():
+    from trenowanie_generatora_obrazkow_b200.ops import reference as R
+    torch.manual_seed(1)
+    lens = [7, 1, 13]
+    cu = torch.tensor([0, 7, 8, 21], dtype=torch.int32)
+    q, k, v = torch.randn(21, 4, 16), torch.randn(21, 2, 16), torch.randn(21, 2, 16)
+    out = R.varlen_attention(q, k, v, cu, causal=True, scale=0.25)
+    for (a, n) in zip([0, 7, 8], lens):
+        qs, ks, vs = q[a:a + n], k[a:a + n].repeat_interleave(2, 1), v[a:a + n].repeat_interleave(2, 1)
+        s = torch.einsum("qhd,khd->hqk", qs, ks) * 0.25
+        s = s.masked_fill(torch.ones(n, n, dtype=torch.bool).triu(1), float("-inf"))
+        ref = torch.einsum("hqk,khd->qhd", s.softmax(-1), vs)
+        assert torch.allclose(out[a:a + n], ref, atol=1e-5)

@@ -140,3 +140,37 @@ def test_linear_grad_accumulates_fp32():
     assert lin.weight.grad.dtype == torch.float32
     assert rel(lin.weight.grad, wr.grad) < 2e-2
     assert rel(x.grad, xr.grad) < 2e-2
+
+
+@pytest.mark.parametrize("hd,hq,hkv,lens,causal", [(64, 12, 12, [37, 300, 1, 129, 512], True),
+                                                    (128, 8, 2, [256, 3, 77, 400], True),
+                                                    (128, 4, 4, [100, 260, 17], False)])
+def test_varlen_attention(hd, hq, hkv, lens, causal):
+    """Packed variable-length (causal) tcgen05 attention against the fp32 per-sequence oracle."""
+    torch.manual_seed(0)
+    T = sum(lens)
+    cu = torch.tensor([0] + lens).cumsum(0).to(torch.int32)
+    qkv = torch.randn(T, hq + 2 * hkv, hd, device="cuda").bfloat16()
+    q, k, v = qkv.split([hq, hkv, hkv], dim=1)
+    out = Fz.varlen_attention(q, k, v, cu.cuda(), causal=causal)
+    ref = R.varlen_attention(q.float(), k.float(), v.float(), cu, causal=causal, scale=hd ** -0.5)
+    err = (out.float() - ref).abs().max().item()
+    assert err < 2e-2, err
+
+
+def test_slayer_packed_states_gpu():
+    """The frozen Slayer LM packed on the GPU (varlen kernel) matches its padded causal-SDPA states."""
+    from trenowanie_generatora_obrazkow_b200.models.frozen_lm import LM_PAD, SlayerFrozenLM
+    from trenowanie_generatora_obrazkow_b200.models.slayer import GPT, GPTConfig
+    torch.manual_seed(0)
+    gpt = GPT(GPTConfig(vocab=1000, n_layer=2, n_embd=256, n_head=4, block=128))
+    lm = SlayerFrozenLM(None, model=gpt, device="cuda", packed=False)
+    ids = torch.randint(0, 1000, (3, 96), device="cuda")
+    lens = [96, 40, 7]
+    for r, n in enumerate(lens):
+        ids[r, n:] = LM_PAD
+    a = lm.states(ids)
+    b = lm.states_packed(ids)
+    for r, n in enumerate(lens):
+        d = (a[r, :n].float() - b[r, :n].float()).abs().max().item()
+        assert d < 0.1 * a[r, :n].float().abs().max().item(), (r, d)

@@ -107,3 +107,21 @@ def test_train_rpe2d_micro_cond_and_crops(tmp_path):
     ck = torch.load(os.path.join(out, "latest.pt"), weights_only=False)
     assert ck["den_config"]["micro_cond"] == 256 and ck["den_config"]["rope_ref"] == 16
     assert any(k.startswith("cond_mlp") for k in ck["den"])
+
+
+def test_train_multi_res(tmp_path):
+    """Mixed-resolution steps: 128 px and 256 px groups (their own latents and micro-batch sizes) in every step."""
+    import numpy as np
+
+    from trenowanie_generatora_obrazkow_b200.data.shards import write_synthetic_shards
+    d = str(tmp_path / "shards")
+    write_synthetic_shards(d, n_shards=2, per_shard=8, side=16)
+    import glob
+    for f in glob.glob(os.path.join(d, "*.lat.npy")):  # the same images at 128 px
+        lat = np.load(f)
+        np.save(f[: -len(".lat.npy")] + ".lat128.npy", lat.reshape(*lat.shape[:2], 8, 2, 8, 2).mean((3, 5)))
+    out = str(tmp_path / "run")
+    _run(["--data", d, "--out", out, "--size", "50m", "--te-size", "13m", "--batch", "6", "--steps", "2",
+          "--eval-every", "0", "--no-wandb", "--res", "256", "--multi-res", "128", "256", "--multi-res-mbs", "2",
+          "1", "--multi-res-mb", "2", "2", "--t-shift-ref", "256", "--workers", "0"])
+    assert os.path.exists(os.path.join(out, "latest.pt"))

@@ -60,6 +60,11 @@ def build_parser():
       help="resize-and-crop: take --res windows from these larger latent grids (<shard>.lat<res>.npy; 256 = .lat.npy)")
     a("--crop-prob", type=float, default=0.5)
     a("--t-shift-ref", type=float, default=0.0, help="resolution-dependent time shift res / REF (overrides --t-shift)")
+    a("--multi-res", type=int, nargs="*", default=[],
+      help="mixed-resolution steps: these resolutions in every step (--res = the largest); latents of each from "
+           "<shard>.lat<res>.npy (.lat.npy at 256)")
+    a("--multi-res-mbs", type=int, nargs="*", default=[], help="--multi-res: micro-batches per GPU and step at each")
+    a("--multi-res-mb", type=int, nargs="*", default=[], help="--multi-res: images per micro-batch at each")
     a("--repa-weight", type=float, default=0.0,
       help="REPA loss weight (0 = off; the reference's 0.5 needs DINOv2 targets, see --repa-target)")
     a("--repa-layer", type=int, default=None)
@@ -193,6 +198,16 @@ def main():
     else:
         rank, world, local = 0, 1, 0
     args = resolve_defaults(build_parser().parse_args(), world)
+    mr_groups = list(zip(args.multi_res, args.multi_res_mbs, args.multi_res_mb))
+    if args.multi_res:
+        assert len(args.multi_res) == len(args.multi_res_mbs) == len(args.multi_res_mb), \
+            "--multi-res, --multi-res-mbs and --multi-res-mb need one value per resolution"
+        assert max(args.multi_res) == args.res and all(r % 16 == 0 for r in args.multi_res), \
+            "--multi-res: --res must be the largest resolution, all multiples of 16"
+        assert not (args.repa_weight or args.crop_res or args.diloco), "--multi-res: no REPA / crops / DiLoCo"
+        per = sum(n * b for _, n, b in mr_groups)
+        assert args.batch == world * per, f"--multi-res: {per} images per GPU and step, so --batch must be {world * per}"
+        args.micro_batch = max(b for _, _, b in mr_groups)
     device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
     master = rank == 0
     os.makedirs(args.out, exist_ok=True)
@@ -264,9 +279,12 @@ def main():
     side = args.res // 16
     val = None
     groups = ()
+    group_loaders = []
     if args.synthetic:
         stream = SyntheticStream(args.synthetic, side, te_cfg, tr.micro, rank, args.seed)
         loader = iter(stream)
+        group_loaders = [iter(SyntheticStream(args.synthetic, r // 16, te_cfg, b, rank, args.seed + 17 * i))
+                         for i, (r, _, b) in enumerate(mr_groups)]
         if master:
             vs = SyntheticStream(args.synthetic, side, te_cfg, min(args.val_samples, 64), 10 ** 6, args.seed + 1)
             val = next(iter(vs))
@@ -282,6 +300,12 @@ def main():
         loader = iter(torch.utils.data.DataLoader(stream, batch_size=None, num_workers=args.workers,
                                                   pin_memory=device.type == "cuda",
                                                   persistent_workers=args.workers > 0))
+        for i, (r, _, b) in enumerate(mr_groups):  # one stream per resolution, its own micro-batch size
+            st = ShardStore(args.data, train_names, tok_suffix, null_row, lat_kind="lat" if r == 256 else f"lat{r}",
+                            cond_base=den_cfg.micro_cond)
+            ts = TrainStream(st, b, rank, world, args.seed + 17 * i, start_micro=step * mr_groups[i][1])
+            group_loaders.append(iter(torch.utils.data.DataLoader(ts, batch_size=None, num_workers=1,
+                                                                  pin_memory=device.type == "cuda")))
         if master and val_names:
             val = load_val(args.data, val_names, args.val_samples, tok_suffix, null_row)
             groups = val_groups(args.data, val_names, args.val_samples)
@@ -322,13 +346,23 @@ def main():
         return
 
     t0, acc, nacc = time.time(), 0.0, 0
-    while step < args.steps:
-        micros = [next(loader) for _ in range(tr.accum)]
-        x0 = torch.cat([m[0] for m in micros])
-        second = torch.cat([m[1] for m in micros])
-        batch = {"x0": x0, ("lm_states" if lm_states_key else "ids"): second}
+    def gather(micros):
+        batch = {"x0": torch.cat([m[0] for m in micros]),
+                 ("lm_states" if lm_states_key else "ids"): torch.cat([m[1] for m in micros])}
         if den_cfg.micro_cond and len(micros[0]) > 2:
             batch["cond"] = torch.cat([m[-1] for m in micros])
+        return batch
+
+    while step < args.steps:
+        if mr_groups:
+            groups = []
+            for (r, n, b), it in zip(mr_groups, group_loaders):
+                g = gather([next(it) for _ in range(n)])
+                g["mb"] = b
+                groups.append(g)
+            batch = {"groups": groups}
+        else:
+            batch = gather([next(loader) for _ in range(tr.accum)])
         loss = tr.step(batch)
         step += 1
         samples += args.batch

@@ -247,32 +247,31 @@ __global__ void __launch_bounds__(FA_FWD_THREADS, 1) flash_fwd_kernel(AttnParams
 // HD / 8 lanes per (b, t, h) row, 16-byte loads, four rows per thread in flight (grid-stride), shuffle reduction
 // inside each row's lane group.
 template <int HD>
-__global__ void __launch_bounds__(256) flash_bwd_delta_kernel(AttnParams p, const bf16* __restrict__ dO,
-                                                              float* __restrict__ delta, float* __restrict__ lse2) {
+__global__ void __launch_bounds__(256, 4) flash_bwd_delta_kernel(AttnParams p, const bf16* __restrict__ dO,
+                                                                 float* __restrict__ delta, float* __restrict__ lse2) {
   constexpr int LPR = HD / 8;  // lanes per row
   constexpr int U = 4;
   // 32-bit index arithmetic (the launcher checks B * Tq * Hq < 2^31): 64-bit divisions per row cost more than the
-  // memory traffic of the row
+  // memory traffic of the row.  Four rows in flight per lane group, four CTAs per SM (64 registers).
   const int total = p.B * p.Tq * p.Hq;
   const int rows_per_pass = gridDim.x * (blockDim.x / LPR);
   const int first = blockIdx.x * (blockDim.x / LPR) + threadIdx.x / LPR;
   const int sub = threadIdx.x % LPR;
   for (int base = first; base < total; base += U * rows_per_pass) {
     uint4 a[U], d[U];
-    int hh[U], tt[U], bb[U];
+    int idx[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int item = base + u * rows_per_pass;
       a[u] = d[u] = make_uint4(0u, 0u, 0u, 0u);
-      hh[u] = item % p.Hq;
-      const int bt = item / p.Hq;
-      tt[u] = bt % p.Tq;
-      bb[u] = item < total ? bt / p.Tq : -1;
-      if (bb[u] >= 0) {
-        const long long off =
-            (long long)bb[u] * p.o_bs + (long long)tt[u] * p.o_ts + (long long)hh[u] * p.o_hs + sub * 8;
+      idx[u] = -1;
+      if (item < total) {
+        const int h = item % p.Hq, bt = item / p.Hq;
+        const int b = bt / p.Tq, t = bt - b * p.Tq;
+        const long long off = (long long)b * p.o_bs + (long long)t * p.o_ts + (long long)h * p.o_hs + sub * 8;
         a[u] = *reinterpret_cast<const uint4*>(p.o + off);
         d[u] = *reinterpret_cast<const uint4*>(dO + off);
+        idx[u] = (b * p.Hq + h) * p.Tq + t;
       }
     }
 #pragma unroll
@@ -287,10 +286,9 @@ __global__ void __launch_bounds__(256) flash_bwd_delta_kernel(AttnParams p, cons
       }
 #pragma unroll
       for (int o = LPR / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (sub == 0 && bb[u] >= 0) {
-        const long long idx = ((long long)bb[u] * p.Hq + hh[u]) * p.Tq + tt[u];
-        delta[idx] = s;
-        if (lse2 != nullptr) lse2[idx] = p.lse[idx] * 1.4426950408889634f;  // log-sum-exp in base-2 units
+      if (sub == 0 && idx[u] >= 0) {
+        delta[idx[u]] = s;
+        if (lse2 != nullptr) lse2[idx[u]] = p.lse[idx[u]] * 1.4426950408889634f;  // log-sum-exp in base-2 units
       }
     }
   }
@@ -529,7 +527,7 @@ __global__ void dq_convert_kernel(AttnParams p, const float* __restrict__ acc, b
 static unsigned delta_grid(long long items, int hd) {  // items < 2^31 (checked by the callers)
   const long long rows_per_block = 256 / (hd / 8);
   const long long want = (items + rows_per_block - 1) / rows_per_block;
-  return (unsigned)std::min<long long>(want, (long long)num_sms() * 8);
+  return (unsigned)std::min<long long>(want, (long long)num_sms() * 16);
 }
 
 template <int HD>

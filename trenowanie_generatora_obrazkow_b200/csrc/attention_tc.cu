@@ -18,6 +18,9 @@
 // rings keep three tiles of loads in flight.
 // Key masking by per-sample valid length; grouped-query attention by head mapping. Output and LSE layout match
 // the mma.sync kernel in attention.cu, so the backward there consumes them unchanged.
+// Packed variable-length sequences (cu_seqlens) and causal masking serve the frozen caption LM (inference): a CTA
+// reads its sequence's offset, loads its Q / K / V tiles from there, masks keys past the sequence (and, when
+// causal, keys after each row's query) and stores only its sequence's rows; a causal CTA stops at its diagonal.
 #include <algorithm>
 
 #include "common.cuh"
@@ -103,8 +106,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / p.rep;
   const int q0 = qb * (NQ * TQ);
-  int kv_end = p.Tk;
+  // varlen: sequence b occupies tokens [seq0, seq0 + len) of the packed axis (batch coordinate 0 of the maps)
+  int seq0 = 0, tb = b, q_len = p.Tq, kv_end = p.Tk;
+  if (p.cu_seqlens != nullptr) {
+    seq0 = p.cu_seqlens[b];
+    q_len = kv_end = p.cu_seqlens[b + 1] - seq0;
+    tb = 0;
+  }
   if (p.kv_len != nullptr) kv_end = min(kv_end, p.kv_len[b]);
+  if (p.causal) kv_end = min(kv_end, q0 + NQ * TQ);  // no key after the CTA's last query row
+  if (q0 >= q_len) kv_end = 0;
   const int n_tiles = max(0, (kv_end + TK - 1) / TK);
 
   if (threadIdx.x == 0) {
@@ -150,7 +161,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int blk = 0; blk < HD / 64; ++blk)
           tma_load_4d(smem + L::Q_OFF + g * L::Q_BYTES + blk * TQ * 128, &tmQ, &bars->q_full, blk * 64,
-                      q0 + g * TQ, h, b);
+                      seq0 + q0 + g * TQ, h, tb);
       auto load_k = [&](int j) -> bool {
         const int st = j % KV_STAGES, ph = (j / KV_STAGES) & 1;
         if (!mbar_wait(&bars->k_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) return false;
@@ -158,7 +169,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int blk = 0; blk < HD / 64; ++blk)
           tma_load_4d(smem + L::K_OFF + st * L::KV_BYTES + blk * TK * 128, &tmK, &bars->k_full[st], blk * 64,
-                      j * TK, hk, b);
+                      seq0 + j * TK, hk, tb);
         return true;
       };
       bool ok = load_k(0);
@@ -177,7 +188,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int blk = 0; blk < HD / 64; ++blk)
           tma_load_4d(smem + L::V_OFF + st * L::KV_BYTES + blk * TK * 128, &tmV, &bars->v_full[st], blk * 64,
-                      j * TK, hk, b);
+                      seq0 + j * TK, hk, tb);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -252,6 +263,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t s_base = tmem + lane_base + g * 128, o_base = tmem + lane_base + O_COL + g * HD;
     const float sl2 = p.scale * 1.4426950408889634f;
     const bool tw = tr && (threadIdx.x == 64 + g * 128);
+    const int qpos = q0 + g * TQ + row;                        // query index within the sequence
+    const int key_lim = p.causal ? min(kv_end, qpos + 1) : kv_end;  // this row's keys: [0, key_lim)
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
@@ -272,10 +285,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_ld_wait();
       ATTN_TRACE(tw, 24 + 4 * g, j);
       // raw logits: the running max m is kept in log2 units (sl2 > 0, so max and scaling commute) and
-      // p = 2^(s sl2 - m) is one FFMA + ex2 per element; keys past kv_end exist only in the last tile
+      // p = 2^(s sl2 - m) is one FFMA + ex2 per element; keys past key_lim exist only in the last tile (and, when
+      // causal, in the tiles that cross the diagonal)
       const int kbase = j * TK;
       float smax = -INFINITY;
-      if (kbase + TK <= kv_end) {
+      if (kbase + TK <= key_lim) {
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -285,7 +299,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            if (kbase + c * 32 + i >= kv_end) sr[c][i] = __float_as_uint(-INFINITY);
+            if (kbase + c * 32 + i >= key_lim) sr[c][i] = __float_as_uint(-INFINITY);
             smax = fmaxf(smax, __uint_as_float(sr[c][i]));
           }
       }
@@ -364,10 +378,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       tc_fence_after();
     }
-    const int t = q0 + g * TQ + row;
+    const int t = qpos;
     const float inv = (l > 0.f) ? 1.f / l : 0.f;
     if (ok) {
-      __nv_bfloat16* dst = p.o + (long long)b * p.o_bs + (long long)t * p.o_ts + (long long)h * p.o_hs;
+      __nv_bfloat16* dst = p.o + (long long)tb * p.o_bs + (long long)(seq0 + t) * p.o_ts + (long long)h * p.o_hs;
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
@@ -378,7 +392,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
-        if (t < p.Tq) {
+        if (t < q_len) {
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
             uint4 u;
@@ -390,9 +404,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
-      if (t < p.Tq && p.lse != nullptr)
-        p.lse[((long long)b * p.Hq + h) * p.Tq + t] =
-            (l > 0.f) ? (m + log2f(l)) * 0.6931471805599453f : INFINITY;
+      if (t < q_len && p.lse != nullptr) {
+        const long long li = p.cu_seqlens != nullptr ? (long long)h * p.total + seq0 + t
+                                                     : ((long long)b * p.Hq + h) * p.Tq + t;
+        p.lse[li] = (l > 0.f) ? (m + log2f(l)) * 0.6931471805599453f : INFINITY;
+      }
     } else {
       *abort_flag = 1;
     }

@@ -102,6 +102,11 @@ struct AttnParams {
   const int* kv_len;       // optional [B] valid key count (prefix mask)
   int B, Tq, Tk, Hq, Hkv, rep, hd;
   float scale;
+  // Packed variable-length sequences (tcgen05 forward only): cu_seqlens [B + 1] token offsets of the B sequences
+  // along one packed token axis (the tensors' batch extent is 1, Tq = Tk = the longest sequence, lse is
+  // [Hq][total]).  causal: key index <= query index, both counted from the start of the sequence.
+  const int* cu_seqlens;
+  int total, causal;
 };
 cudaError_t attention_fwd_launch(const AttnParams& p, cudaStream_t s);
 // dq_acc: scratch fp32 [B][Tq][Hq][hd] (zeroed here); delta: scratch fp32 [B][Hq][Tq]; dq (bf16) optional.

@@ -432,6 +432,55 @@ std::vector<at::Tensor> attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, 
   return {o, lse};
 }
 
+// Packed variable-length causal / bidirectional attention (inference): q [total, Hq, hd], k / v [total, Hkv, hd],
+// cu_seqlens int32 [n + 1] on the device (offsets of the n sequences), max_len = the longest sequence.
+// Returns o [total, Hq, hd] and lse [Hq, total].
+std::vector<at::Tensor> attention_varlen_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu_seqlens,
+                                             int64_t max_len, double scale, bool causal, at::Tensor err) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(g_attention_tc, "attention_varlen_fwd: needs the tcgen05 attention path");
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.sizes() == k.sizes(), "attention_varlen_fwd: q [T, Hq, hd], k / v [T, Hkv, hd]");
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 &&
+                  v.scalar_type() == at::kBFloat16, "attention_varlen_fwd: bf16 CUDA tensors");
+  TORCH_CHECK(q.stride(2) == 1 && k.stride(2) == 1 && v.stride(2) == 1, "attention_varlen_fwd: unit head-dim stride");
+  TORCH_CHECK(k.size(0) == q.size(0) && k.size(2) == q.size(2), "attention_varlen_fwd: q / k token or head-dim mismatch");
+  TORCH_CHECK(cu_seqlens.is_cuda() && cu_seqlens.scalar_type() == at::kInt && cu_seqlens.dim() == 1 &&
+                  cu_seqlens.numel() >= 2 && cu_seqlens.is_contiguous(), "cu_seqlens: contiguous int32 [n + 1] on the device");
+  TORCH_CHECK(max_len > 0 && max_len <= q.size(0), "attention_varlen_fwd: max_len");
+  AttnParams p{};
+  p.B = (int)cu_seqlens.numel() - 1;
+  p.total = (int)q.size(0);
+  p.Tq = p.Tk = (int)max_len;
+  p.Hq = (int)q.size(1);
+  p.Hkv = (int)k.size(1);
+  p.hd = (int)q.size(2);
+  TORCH_CHECK(p.Hq % p.Hkv == 0 && (p.hd == 64 || p.hd == 128), "attention_varlen_fwd: Hq % Hkv, head dim 64 / 128");
+  p.rep = p.Hq / p.Hkv;
+  p.q = bfp(q);
+  p.q_ts = q.stride(0);
+  p.q_hs = q.stride(1);
+  p.k = bfp(k);
+  p.k_ts = k.stride(0);
+  p.k_hs = k.stride(1);
+  p.v = bfp(v);
+  p.v_ts = v.stride(0);
+  p.v_hs = v.stride(1);
+  p.scale = (float)scale;
+  p.cu_seqlens = cu_seqlens.data_ptr<int>();
+  p.causal = causal ? 1 : 0;
+  at::Tensor o = at::empty({p.total, p.Hq, p.hd}, q.options());
+  at::Tensor lse = at::empty({p.Hq, p.total}, q.options().dtype(at::kFloat));
+  p.o = bfp(o);
+  p.o_ts = o.stride(0);
+  p.o_hs = o.stride(1);
+  p.lse = lse.data_ptr<float>();
+  CUtensorMap tq = make_tmap_bhtd(p.q, p.hd, p.total, p.Hq, 1, p.q_ts, p.q_hs, 0, 128);
+  CUtensorMap tk = make_tmap_bhtd(p.k, p.hd, p.total, p.Hkv, 1, p.k_ts, p.k_hs, 0, 64);
+  CUtensorMap tv = make_tmap_bhtd(p.v, p.hd, p.total, p.Hkv, 1, p.v_ts, p.v_hs, 0, 64);
+  TGO_CHECK_LAUNCH(attention_fwd_tc_launch(tq, tk, tv, p, err_ptr(err), at::cuda::getCurrentCUDAStream()));
+  return {o, lse};
+}
+
 // Writes dq, dk, dv (preallocated, possibly strided views). dO must have o's layout.
 void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, at::Tensor dO,
                    c10::optional<at::Tensor> kv_len, double scale, at::Tensor dq, at::Tensor dk, at::Tensor dv,
@@ -697,4 +746,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &tgo::swiglu_bwd, "backward of swiglu_fwd");
   m.def("attention_fwd", &tgo::attention_fwd, "flash attention forward (GQA, key-length mask)");
   m.def("attention_bwd", &tgo::attention_bwd, "flash attention backward");
+  m.def("attention_varlen_fwd", &tgo::attention_varlen_fwd,
+        "packed variable-length (optionally causal) attention forward on tcgen05");
 }

@@ -55,11 +55,16 @@ class HFFrozenLM:
 
 
 class SlayerFrozenLM:
-    def __init__(self, repo, skip_last=0, device=None, model=None):
+    """packed: on CUDA, captions run packed without padding (varlen causal attention) up to max_tokens real tokens
+    per LM call; null-prompt rows are not run (zeros), as the refiner replaces them by its learned null vector."""
+
+    def __init__(self, repo, skip_last=0, device=None, model=None, dtype=torch.bfloat16, packed=None,
+                 max_tokens=8192):
         from .slayer import load_gpt
         self.model = model if model is not None else load_gpt(repo)[0]
-        self.model = self.model.to(device=device, dtype=torch.bfloat16).eval().requires_grad_(False)
+        self.model = self.model.to(device=device, dtype=dtype).eval().requires_grad_(False)
         self.n_blocks = len(self.model.blocks) - skip_last
+        self.packed, self.max_tokens = packed, max_tokens
 
     def to(self, device):
         self.model.to(device)
@@ -67,8 +72,39 @@ class SlayerFrozenLM:
 
     @torch.no_grad()
     def states(self, ids):
+        packed = self.packed if self.packed is not None else self.model.tok.weight.is_cuda
+        if packed:
+            return self.states_packed(ids)
         real = ids.masked_fill(ids.eq(LM_PAD) | ids.eq(LM_NULL), 0).long()
         return self.model.hidden(real, self.n_blocks)
+
+    @torch.no_grad()
+    def states_packed(self, ids):
+        """(B, T) caption rows -> (B, T, n_embd) states; zeros at pads and null-prompt rows."""
+        return packed_states(lambda seqs: self.model.hidden_packed(seqs, self.n_blocks), ids,
+                             self.model.cfg.n_embd, self.max_tokens, self.model.tok.weight.dtype)
+
+
+def packed_states(run, ids, width, max_tokens=8192, dtype=torch.bfloat16):
+    """Scatter the packed LM states of the real tokens of the real (non-null) rows of ids back into (B, T, width).
+    run(list of 1-D CPU id tensors) -> (sum of lengths, width); calls are cut at max_tokens real tokens."""
+    B, T = ids.shape
+    ids_c = ids.cpu()
+    keep = ids_c.ne(LM_PAD) & ids_c[:, :1].ne(LM_NULL)
+    lens = keep.sum(1)
+    seqs = [q for q in ids_c[keep].split(lens.tolist()) if len(q)]
+    out = torch.zeros(B * T, width, device=ids.device, dtype=dtype)
+    if seqs:
+        flat, pack, n = [], [], 0
+        for q in seqs + [None]:
+            if q is None or (pack and n + len(q) > max_tokens):
+                flat.append(run(pack))
+                pack, n = [], 0
+            if q is not None:
+                pack.append(q)
+                n += len(q)
+        out.index_copy_(0, keep.flatten().nonzero().flatten().to(ids.device), torch.cat(flat).to(out.device, dtype))
+    return out.view(B, T, width)
 
 
 def build_frozen_lm(cfg, device=None, allow_random=False):

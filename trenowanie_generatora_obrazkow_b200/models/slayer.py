@@ -7,7 +7,10 @@ values are mixed into every later block with a learned scalar) and a SwiGLU (gat
 final norm. Module and parameter names match the reference so its ``model.safetensors`` loads strictly.
 
 The LM is frozen inference: it runs once per caption batch outside the training step (or on a separate LM rank), so
-it uses PyTorch matmuls and causal SDPA rather than the training kernels.
+it uses PyTorch matmuls. Two attention paths: padded rows with causal SDPA (``hidden``), and captions packed back
+to back without padding (``hidden_packed``, reference aurora/slayer.py:326-432 for its HF LM): positions restart per
+caption and the sm_100a varlen causal attention kernel keeps attention inside each caption, so the matmuls see only
+real tokens. For real tokens both paths give the same states (up to bf16 rounding).
 """
 import json
 import os
@@ -64,6 +67,16 @@ def rope_pairs(x, theta):
     return torch.stack((a * c - b * s, a * s + b * c), dim=-1).flatten(-2)
 
 
+def rope_pairs_at(x, pos, theta):
+    """rope_pairs for packed tokens: x [T, H, D] at per-token positions pos [T]."""
+    D = x.shape[-1]
+    inv = theta ** (-torch.arange(0, D, 2, device=x.device, dtype=torch.float32) / D)
+    ang = pos.to(torch.float32)[:, None] * inv[None]
+    c, s = ang.cos().to(x.dtype)[:, None], ang.sin().to(x.dtype)[:, None]
+    a, b = x[..., 0::2], x[..., 1::2]
+    return torch.stack((a * c - b * s, a * s + b * c), dim=-1).flatten(-2)
+
+
 class SwiGLU(nn.Module):
     def __init__(self, d, hidden):
         super().__init__()
@@ -108,6 +121,24 @@ class Block(nn.Module):
         x = x + self.proj(y)
         return x + self.mlp(self.ln2(x)), v_first
 
+    def forward_packed(self, x, pos, cu, max_len, v_first=None):
+        """x [T, D] of captions packed back to back (offsets cu, positions pos restarting per caption)."""
+        from ..ops.fused import varlen_attention
+        T, D = x.shape
+        q, k, v = (t.view(T, self.nh, D // self.nh) for t in self.qkv(self.ln1(x)).split(D, dim=-1))
+        if self.cfg.qk_norm:
+            q, k = self.q_norm(q), self.k_norm(k)
+        if self.cfg.pos == "rope":
+            q, k = rope_pairs_at(q, pos, self.cfg.rope_theta), rope_pairs_at(k, pos, self.cfg.rope_theta)
+        if self.cfg.value_residual:
+            if self.first:
+                v_first = v
+            else:
+                v = v + self.vr_lambda * v_first
+        y = varlen_attention(q, k, v, cu, max_len, causal=True).to(x.dtype).reshape(T, D)
+        x = x + self.proj(y)
+        return x + self.mlp(self.ln2(x)), v_first
+
 
 class GPT(nn.Module):
     def __init__(self, cfg: GPTConfig):
@@ -133,6 +164,47 @@ class GPT(nn.Module):
 
     def forward(self, idx):
         return self.head(self.lnf(self.hidden(idx, len(self.blocks))))
+
+    @torch.no_grad()
+    def run_slice(self, x, lo, hi):
+        """Blocks [lo, hi) for a pipeline's LM layer split. lo == 0: x are ids. Otherwise x is the previous
+        slice's carry: the residual stream and block 0's values side by side (B, T, 2 n_embd), since the value
+        residual of every later block reads them. Returns the carry, or the residual stream when hi is the end."""
+        v_first = None
+        if lo == 0:
+            x = self.tok(x.long())
+            if self.cfg.pos != "rope":
+                x = x + self.pos(torch.arange(x.shape[1], device=x.device))[None]
+        else:
+            D = self.cfg.n_embd
+            B, T = x.shape[:2]
+            x, vf = x[..., :D], x[..., D:]
+            if self.cfg.value_residual:
+                v_first = vf.reshape(B, T, self.cfg.n_head, D // self.cfg.n_head).transpose(1, 2)
+        for blk in self.blocks[lo:hi]:
+            x, v_first = blk(x, v_first)
+        if hi >= len(self.blocks):
+            return x
+        B, T, D = x.shape
+        vf = v_first.transpose(1, 2).reshape(B, T, D) if v_first is not None else torch.zeros_like(x)
+        return torch.cat([x, vf.to(x.dtype)], dim=-1)
+
+    @torch.no_grad()
+    def hidden_packed(self, seqs, n_blocks):
+        """Residual stream after n_blocks blocks for captions given as 1-D id tensors, run as one packed sequence
+        -> (sum of lengths, n_embd), captions back to back."""
+        dev = self.tok.weight.device
+        lens = [len(q) for q in seqs]
+        ids = torch.cat(list(seqs)).to(dev, non_blocking=True).long()
+        pos = torch.cat([torch.arange(n) for n in lens]).to(dev, non_blocking=True)
+        cu = torch.tensor([0] + lens).cumsum(0).to(dev, dtype=torch.int32)
+        x = self.tok(ids)
+        if self.cfg.pos != "rope":
+            x = x + self.pos(pos)
+        v_first = None
+        for blk in self.blocks[:n_blocks]:
+            x, v_first = blk.forward_packed(x, pos, cu, max(lens), v_first)
+        return x
 
 
 def load_gpt(path):

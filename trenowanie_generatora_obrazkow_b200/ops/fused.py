@@ -10,6 +10,7 @@ autograd. Each CUDA op is a ``torch.autograd.Function`` whose backward is a hand
 * ``self_attention_core``  per-head q/k RMSNorm + RoPE + flash attention, reading q/k/v from the fused qkv rows.
 * ``cross_attention_core`` flash attention against text keys/values with a key-length mask.
 * ``swiglu``        silu(a) * b.
+* ``varlen_attention`` packed variable-length (causal) attention for the frozen caption LM (inference only).
 """
 import torch
 
@@ -295,6 +296,21 @@ def cross_attention_core(q, kv, heads, kv_len=None, scale=None):
         return R.attention(q.view(B, T, heads, hd), k.reshape(B, L, heads, hd), v.reshape(B, L, heads, hd), kv_len,
                            scale).reshape(B, T, D)
     return _CrossAttnFn.apply(q.contiguous(), kv.contiguous(), kv_len, heads, hd, float(scale))
+
+
+@torch.no_grad()
+def varlen_attention(q, k, v, cu_seqlens, max_len=None, causal=True, scale=None):
+    """Captions packed back to back without padding (reference aurora/slayer.py:326-342, varlen flash attention):
+    q [T, Hq, d], k / v [T, Hkv, d], cu_seqlens int32 [n + 1]; attention stays inside each sequence."""
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    if not q.is_cuda:
+        return R.varlen_attention(q, k, v, cu_seqlens, causal, scale)
+    if max_len is None:
+        max_len = int((cu_seqlens[1:] - cu_seqlens[:-1]).max())
+    cu = cu_seqlens.to(device=q.device, dtype=torch.int32).contiguous()
+    o, _ = ext().attention_varlen_fwd(q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16), cu,
+                                      int(max_len), float(scale), bool(causal), err_buf(q.device))
+    return o
 
 
 # ----------------------------------------------------------------------------------------------------------------

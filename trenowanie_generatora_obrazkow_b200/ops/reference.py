@@ -116,6 +116,21 @@ def attention(q, k, v, kv_len=None, scale=None):
     return o.transpose(1, 2)
 
 
+def varlen_attention(q, k, v, cu_seqlens, causal=True, scale=None):
+    """Packed sequences: q [T, Hq, d], k / v [T, Hkv, d], cu_seqlens [n + 1] token offsets; attention stays inside
+    each sequence (causal: key <= query position) -> [T, Hq, d]."""
+    out = torch.empty_like(q)
+    cu = [int(c) for c in cu_seqlens.tolist()]
+    for a, b in zip(cu[:-1], cu[1:]):
+        if b <= a:
+            continue
+        qh, kh, vh = (x[a:b].transpose(0, 1) for x in (q, k, v))
+        rep = qh.shape[0] // kh.shape[0]
+        kh, vh = kh.repeat_interleave(rep, 0), vh.repeat_interleave(rep, 0)
+        out[a:b] = F.scaled_dot_product_attention(qh, kh, vh, is_causal=causal, scale=scale).transpose(0, 1)
+    return out
+
+
 def swiglu(ab):
     a, b = ab.chunk(2, dim=-1)
     return F.silu(a) * b

@@ -260,11 +260,29 @@ class Trainer:
             is_null, valid = drop_captions(is_null, valid, cfg.cfg_drop, self.gen)
         return dict(lm_states=states, valid=valid, is_null=is_null)
 
+    def _micro_items(self, batch):
+        """(x0 micro-batch, source dict, row slice of the source) for every micro-batch of the step: fixed
+        micro-batches of ``batch["x0"]``, or with ``batch["groups"]`` (mixed-resolution training, reference
+        train_pp.py:1227-1240, 2239-2255) each group's own resolution and micro-batch size ``mb``."""
+        groups = batch.get("groups")
+        if not groups:
+            x0_all = self._to_dev(batch["x0"])
+            for m in range(self.accum):
+                sl = slice(m * self.micro, (m + 1) * self.micro)
+                yield x0_all[sl], batch, sl
+            return
+        for g in groups:
+            x0 = self._to_dev(g["x0"])
+            for i in range(0, x0.shape[0], g["mb"]):
+                sl = slice(i, i + g["mb"])
+                yield x0[sl], g, sl
+
     def step(self, batch):
         """One optimizer step over this rank's share of the global batch. Returns the mean flow-matching loss
         (device scalar); ``self.last`` holds the MLM loss and the gradient norm."""
         cfg = self.cfg
-        x0_all = self._to_dev(batch["x0"])
+        items = list(self._micro_items(batch))
+        total = sum(x0.shape[0] for x0, _, _ in items)
         if self.muon_buckets is not None:
             self.muon_buckets.zero()
             self.muon_comm.begin_step()
@@ -279,21 +297,21 @@ class Trainer:
         acc = torch.zeros((), device=self.device)
         acc_mlm = torch.zeros((), device=self.device)
         acc_repa = torch.zeros((), device=self.device)
-        for m in range(self.accum):
-            sl = slice(m * self.micro, (m + 1) * self.micro)
-            x0 = x0_all[sl].float()
+        for m, (x0, src, sl) in enumerate(items):
+            x0 = x0.float()
             b = x0.shape[0]
-            kw = self._text_inputs(batch, sl, b)
+            w = b / total  # the step's loss is the mean over its images, whatever the micro-batch sizes
+            kw = self._text_inputs(src, sl, b)
             t = torch.sigmoid(torch.randn(b, device=self.device, generator=self.gen))
             shift = x0.shape[-1] * 16 / cfg.t_shift_ref if cfg.t_shift_ref else cfg.t_shift
             if shift != 1.0:
                 t = shift * t / (1 + (shift - 1) * t)
-            if batch.get("cond") is not None:  # micro-conditions of crops (original size, crop box, target size)
-                kw["cond"] = self._to_dev(batch["cond"][sl])
+            if src.get("cond") is not None:  # micro-conditions of crops (original size, crop box, target size)
+                kw["cond"] = self._to_dev(src["cond"][sl])
             if cfg.rope_random:
-                kw["rope"] = self._random_rope(b, x0.shape[-1], self.step_idx * self.accum + m)
+                kw["rope"] = self._random_rope(b, x0.shape[-1], self.step_idx * len(items) + m)
             eps = torch.randn(x0.shape, device=self.device, generator=self.gen)
-            if self.buckets is not None and m == self.accum - 1:
+            if self.buckets is not None and m == len(items) - 1:
                 self.buckets.arm()
                 if self.muon_buckets is not None:
                     self.muon_buckets.arm()
@@ -303,11 +321,11 @@ class Trainer:
                     kw["repa_target"] = self.repa_target(x0[: max(1, round(cfg.repa_frac * b))])
             loss, l_fm, l_mlm, l_repa = self.model(x0, t, eps, **kw)
             if l_repa is not None:
-                acc_repa += l_repa / self.accum
-            (loss / self.accum).backward()
-            acc += l_fm / self.accum
+                acc_repa += l_repa * w
+            (loss * w).backward()
+            acc += l_fm * w
             if l_mlm is not None:
-                acc_mlm += l_mlm / self.accum
+                acc_mlm += l_mlm * w
         if self.buckets is not None:
             self.buckets.finish()
             if getattr(self, "powersgd", None) is not None:
