@@ -54,3 +54,23 @@ class LatentEncoder(_VAE):
             z = pack_2x2(self.vae.encode(x).latent_dist.mode().float())
             out.append((z - self.mean) / self.std)
         return torch.cat(out)
+
+
+class PatchEncoder:
+    """Stand-in image encoder with the FLUX.2 latent shape, for runs without the VAE weights (service-rank and
+    loader plumbing, tests): every 16 x 16 RGB patch goes through a fixed, seeded linear map to ``channels``
+    values, so (B, 3, H, W) uint8 -> (B, channels, H / 16, W / 16) float32, roughly unit variance."""
+
+    def __init__(self, channels=128, patch=16, seed=0, device=None):
+        g = torch.Generator().manual_seed(seed + 7)
+        n = 3 * patch * patch
+        self.patch = patch
+        self.proj = (torch.randn(channels, n, generator=g) / n ** 0.5).to(device)
+
+    @torch.no_grad()
+    def __call__(self, img):
+        x = img.float() / 127.5 - 1
+        B, _, H, W = x.shape
+        cols = torch.nn.functional.unfold(x, self.patch, stride=self.patch)  # (B, 3 p p, h w)
+        z = self.proj.to(x.device) @ cols
+        return (z * 3.0).view(B, -1, H // self.patch, W // self.patch)

@@ -21,24 +21,28 @@ from .flow import drop_captions
 from .trainer import TrainConfig
 
 
+def pp_groups(world, pp):
+    """Process groups of the PP x DP grid over learner ranks [0, world): (pipe group per replica, stage group per
+    stage). A collective over the default group: every rank calls it, service ranks too."""
+    _, pipes, stages = grid_layout(world, pp)
+    return [dist.new_group(r) for r in pipes], [dist.new_group(r) for r in stages]
+
+
 class PPTrainer:
-    def __init__(self, den_cfg, te_cfg, cfg: TrainConfig, device, pp, microbatches, te_cost=1.0):
+    """``world``: the learner ranks [0, world) (service ranks after them take no part); ``groups``: the result of
+    ``pp_groups(world, pp)`` when the caller created them already (service ranks in the job)."""
+
+    def __init__(self, den_cfg, te_cfg, cfg: TrainConfig, device, pp, microbatches, te_cost=1.0, world=None,
+                 groups=None):
         self.cfg, self.device = cfg, torch.device(device)
-        self.rank, self.world = dist.get_rank(), dist.get_world_size()
+        self.rank = dist.get_rank()
+        self.world = world or dist.get_world_size()
         self.pp, self.M = pp, microbatches
         self.dp, pipes, stages = grid_layout(self.world, pp)
         self.stage, self.replica = self.rank % pp, self.rank // pp
         self.pipe = pipes[self.replica]
-        # every rank creates every group (collective), keeps its own
-        self.pipe_group = self.stage_group = None
-        for ranks in pipes:
-            g = dist.new_group(ranks)
-            if self.rank in ranks:
-                self.pipe_group = g
-        for ranks in stages:
-            g = dist.new_group(ranks)
-            if self.rank in ranks:
-                self.stage_group = g
+        pipe_groups, stage_groups = groups if groups is not None else pp_groups(self.world, pp)
+        self.pipe_group, self.stage_group = pipe_groups[self.replica], stage_groups[self.stage]
         self.den_cfg, self.te_cfg = den_cfg, te_cfg
         lo, hi = stage_ranges(den_cfg.depth, pp, te_cost)[self.stage]
         self.first, self.last = self.stage == 0, self.stage == pp - 1
@@ -92,8 +96,10 @@ class PPTrainer:
                 if cfg.t_shift != 1.0:
                     t = cfg.t_shift * t / (1 + (cfg.t_shift - 1) * t)
                 eps = torch.randn(x0.shape, device=self.device, generator=self.gen)
-                valid = torch.ones(mb, L, dtype=torch.bool, device=self.device)
-                is_null, valid = drop_captions(None, valid, cfg.cfg_drop, self.gen)
+                valid = batch["valid"][sl].to(self.device) if batch.get("valid") is not None else \
+                    torch.ones(mb, L, dtype=torch.bool, device=self.device)
+                is_null = batch["is_null"][sl].to(self.device) if batch.get("is_null") is not None else None
+                is_null, valid = drop_captions(is_null, valid, cfg.cfg_drop, self.gen)
                 tt = t.view(-1, 1, 1, 1)
                 inputs.append(((1 - tt) * x0 + tt * eps, t, dict(lm_states=st_all[sl], valid=valid,
                                                                   is_null=is_null)))
@@ -103,7 +109,7 @@ class PPTrainer:
                 targets = None
         elif self.last:
             targets = recv_targets(M, (mb, side * side, C), torch.float32, self.device, self.pipe)
-        if self.sched is None or self.sched.shapes["x"][0] != mb:
+        if self.sched is None or self.sched.shapes["x"][:2] != (mb, side * side) or self.sched.shapes["text"][1] != L:
             self.sched = self._schedule(mb, side, L)
         loss = self.sched.step(M, (lambda i: inputs[i]) if self.first else None, targets, side, 1.0 / M,
                                before_last_backward=self.buckets.arm)
