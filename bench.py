@@ -49,6 +49,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--moe", action="store_true", help="MoE config: every other MLP -> 8 experts, top-2, "
                    "expert hidden 4096, expert-parallel over the GPUs")
+    p.add_argument("--moe-transport", default="p2p", choices=["p2p", "nccl"],
+                   help="--moe expert exchange: peer memory fused with the expert GEMMs (p2p) or NCCL all_to_all")
     p.add_argument("--pp", type=int, default=1, help="pipeline stages (pipeline config: --pp 4 on 8 GPUs, "
                    "--res 1024 --microbatches 8 --pp-micro 4)")
     p.add_argument("--microbatches", type=int, default=8)
@@ -200,7 +202,8 @@ def run_ours(args):
     from dataclasses import replace
     den_cfg = replace(den_cfg, latent_size=args.res // 16)
     cfg = TrainConfig(global_batch=args.global_batch, micro_batch=args.micro_batch, steps=10 ** 6,
-                      grad_comm=args.grad_comm, moe_experts=8 if args.moe else 0, muon_comm=args.muon_comm)
+                      grad_comm=args.grad_comm, moe_experts=8 if args.moe else 0, muon_comm=args.muon_comm,
+                      moe_transport=args.moe_transport)
     tr = Trainer(den_cfg, te_cfg, cfg, device)
     per_rank = args.global_batch // world
     host, devb = synthetic_batch(per_rank, args.res, args.text_len, te_cfg.lm_dim, device, 1234 + rank)
@@ -234,7 +237,8 @@ def run_ours(args):
                       "global_batch": args.global_batch, "micro_batch": tr.micro, "seq_len": (args.res // 16) ** 2,
                       "text_len": args.text_len, "res": args.res, "parallelism": f"dp{world}",
                       "optimizer": "muon(sharded)+adamw", "grad_comm": args.grad_comm, "muon_comm": args.muon_comm,
-                      "moe": "8 experts top-2 hidden 4096 every other block, expert-parallel" if args.moe else None,
+                      "moe": (f"8 experts top-2 hidden 4096 every other block, expert-parallel, {args.moe_transport} "
+                              "exchange") if args.moe else None,
                       "l2": "inputs larger than L2 (no flush needed)"},
            "clocks": clocks, "gpu_launches": int(launches), "impl": "ours"}
     if not args.no_e2e:

@@ -24,3 +24,32 @@ def test_moe_gpu_matches_cpu():
     assert rel(hg.grad, hc.grad) < 4e-2
     assert rel(gpu.w_in.grad, cpu.w_in.grad) < 4e-2
     assert rel(gpu.w_out.grad, cpu.w_out.grad) < 4e-2
+
+
+def test_moe_peer_exchange_matches_nccl_path_one_gpu():
+    """The peer-memory exchange fused with the expert GEMMs (here with one rank: dispatch to itself, flag waits,
+    scatter epilogue, combine) against the all_to_all path, over several steps (epochs, back-pressure) and a
+    no-grad forward in between."""
+    from trenowanie_generatora_obrazkow_b200.ops._ext import check_errors
+    torch.manual_seed(1)
+    ref = MoEMLP(512, 256, experts=4, top_k=2, capacity_factor=3.0, transport="nccl").cuda()
+    fus = MoEMLP(512, 256, experts=4, top_k=2, capacity_factor=3.0, transport="p2p").cuda()
+    fus.load_state_dict(ref.state_dict())
+    for it in range(3):
+        h = torch.randn(2, 300, 512, device="cuda").bfloat16()
+        outs, grads = [], []
+        for m in (ref, fus):
+            m.zero_grad(set_to_none=True)
+            x = h.clone().requires_grad_()
+            o = m(x)
+            o.float().square().mean().backward()
+            outs.append(o.float())
+            grads.append((x.grad.float(), m.w_in.grad.clone(), m.w_out.grad.clone(), m.router.weight.grad.clone()))
+        check_errors()
+        rel = lambda a, b: ((a - b).norm() / b.norm().clamp(min=1e-12)).item()
+        assert rel(outs[1], outs[0]) < 1e-2, it
+        for a, b in zip(grads[1], grads[0]):
+            assert rel(a.float(), b.float()) < 3e-2, it
+        with torch.no_grad():
+            fus(h)
+        check_errors()

@@ -16,7 +16,7 @@
 // the Newton-Schulz step (reference aurora/ns_triton.py:78).
 #include <algorithm>
 
-#include "common.cuh"
+#include "comm.cuh"
 #include "kernels.h"
 
 namespace tgo {
@@ -26,6 +26,7 @@ constexpr int GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
 
 enum GemmEpi { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2 };
+enum GemmPeerMode { PEER_NONE = 0, PEER_WAIT_A = 1, PEER_SCATTER_C = 2 };
 
 
 template <int BN>
@@ -37,6 +38,27 @@ struct GemmCfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (256 or 512 columns)
 };
+
+// MoE scatter: the bf16 row goes to its source rank's combine buffer (a peer address)
+__device__ __forceinline__ void gemm_store_chunk_peer(const GemmParams& p, int b, int row, int col0,
+                                                      const uint32_t (&r)[32]) {
+  if (row >= p.M || col0 >= p.N) return;
+  const int s = row / p.peer.src_rows;
+  __nv_bfloat16* c = p.peer.out[s] + ((long long)(p.peer.b_base + b) * p.peer.src_rows + (row - s * p.peer.src_rows)) *
+                                         p.ldc + col0;
+  const bool full = col0 + 32 <= p.N;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (full || col0 + j * 8 < p.N) {
+      uint4 u;
+      u.x = pack_bf16x2(__uint_as_float(r[j * 8 + 0]) * p.alpha, __uint_as_float(r[j * 8 + 1]) * p.alpha);
+      u.y = pack_bf16x2(__uint_as_float(r[j * 8 + 2]) * p.alpha, __uint_as_float(r[j * 8 + 3]) * p.alpha);
+      u.z = pack_bf16x2(__uint_as_float(r[j * 8 + 4]) * p.alpha, __uint_as_float(r[j * 8 + 5]) * p.alpha);
+      u.w = pack_bf16x2(__uint_as_float(r[j * 8 + 6]) * p.alpha, __uint_as_float(r[j * 8 + 7]) * p.alpha);
+      *reinterpret_cast<uint4*>(c + j * 8) = u;
+    }
+  }
+}
 
 template <int EPI>
 __device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int b, int row, int col0, const uint32_t (&r)[32]) {
@@ -93,7 +115,7 @@ __device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int b, int
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, int PEER = PEER_NONE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         GemmParams p) {
@@ -145,9 +167,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // ---------------- TMA producer ----------------
       int stage = 0;
       uint32_t phase = 0;
+      uint32_t arrived = 0;  // PEER_WAIT_A: bit s = the rows of source s are in place
       for (int tile = blockIdx.x; tile < num_tiles && !abort_sh; tile += gridDim.x) {
         const int b = tile / tiles_per_batch, r = tile % tiles_per_batch;
         const int m0 = (r / num_n) * GEMM_BM, n0 = (r % num_n) * BN;
+        if constexpr (PEER == PEER_WAIT_A) {
+          const int src = m0 / p.peer.src_rows;
+          if (!((arrived >> src) & 1u)) {
+            if (!flag_wait(p.peer.arrive + src, p.peer.epoch, global_ns() + p.peer.timeout_ns, p.err)) {
+              abort_sh = 1;
+              break;
+            }
+            arrived |= 1u << src;
+            // the rows were written by another GPU's generic-proxy stores: order them before the TMA reads
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+          }
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.err, ERR_MBAR_TIMEOUT_PRODUCER)) {
             abort_sh = 1;
@@ -249,11 +284,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         uint32_t v[32];
         tmem_ld_32x32b_x32(tbase + c * 32, v);
         tmem_ld_wait();
-        gemm_store_chunk<EPI>(p, b, row, n0 + c * 32, v);
+        if constexpr (PEER == PEER_SCATTER_C) {
+          gemm_store_chunk_peer(p, b, row, n0 + c * 32, v);
+        } else {
+          gemm_store_chunk<EPI>(p, b, row, n0 + c * 32, v);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if constexpr (PEER == PEER_SCATTER_C) {
+        // this warp's 32 rows of the tile are stored: count it; the warp completing its source raises the flag
+        if (lane == 0) {
+          const int src = m0 / p.peer.src_rows;
+          __threadfence_system();
+          if (atomicAdd(p.peer.done_count + src, 1u) + 1u == p.peer.tile_warps_per_src)
+            flag_store_release(p.peer.done_flag[src], p.peer.epoch);
+        }
+      }
     }
   }
   tc_fence_before();
@@ -510,6 +558,41 @@ static cudaError_t dispatch_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, co
   if (!a_mn && b_mn) return launch_gemm_pair<false, true, EPI>(ta, tb, p, s);
   if (a_mn && !b_mn) return launch_gemm_pair<true, false, EPI>(ta, tb, p, s);
   return launch_gemm_pair<true, true, EPI>(ta, tb, p, s);
+}
+
+template <bool B_MN, int PEER>
+static cudaError_t launch_gemm_peer(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                                   cudaStream_t s) {
+  using Cfg = GemmCfg<256>;
+  auto kern = gemm_tcgen05_kernel<256, false, B_MN, EPI_BF16, PEER>;
+  static bool set = false;
+  if (!set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    if (e != cudaSuccess) return e;
+    set = true;
+  }
+  const int tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * ((p.N + 255) / 256) * p.batch;
+  kern<<<std::min(tiles, num_sms()), GEMM_THREADS, Cfg::SMEM, s>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_peer_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, bool b_mn,
+                             int peer_mode, cudaStream_t s) {
+  if (p.peer.src_rows <= 0 || p.peer.src_rows % GEMM_BM != 0 || p.M % p.peer.src_rows != 0 ||
+      p.M / p.peer.src_rows > kMaxPeers)
+    return cudaErrorInvalidValue;
+  if (peer_mode == PEER_WAIT_A) {
+    if (p.peer.arrive == nullptr) return cudaErrorInvalidValue;
+    return b_mn ? launch_gemm_peer<true, PEER_WAIT_A>(ta, tb, p, s) : launch_gemm_peer<false, PEER_WAIT_A>(ta, tb, p, s);
+  }
+  if (peer_mode == PEER_SCATTER_C) {
+    if (p.peer.done_count == nullptr) return cudaErrorInvalidValue;
+    cudaError_t e = cudaMemsetAsync(p.peer.done_count, 0, sizeof(unsigned) * (p.M / p.peer.src_rows), s);
+    if (e != cudaSuccess) return e;
+    return b_mn ? launch_gemm_peer<true, PEER_SCATTER_C>(ta, tb, p, s)
+                : launch_gemm_peer<false, PEER_SCATTER_C>(ta, tb, p, s);
+  }
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int bn, bool a_mn,

@@ -10,7 +10,27 @@ namespace tgo {
 
 int num_sms();
 
+constexpr int kMaxPeers = 8;
+
 // ---------------------------------------------------------------- GEMM (gemm.cu)
+// Expert-parallel MoE exchange inside the GEMM (all zero: off). The A rows of every batch come from the source
+// ranks in blocks of src_rows (a multiple of the 128-row tile): with `arrive`, the producer waits until
+// arrive[s] == epoch before loading an A tile of source s (the rows were stored into this GPU by the source's
+// dispatch kernel). With `out`, the epilogue stores row m of batch b into source s = m / src_rows at
+// out[s] + ((b_base + b) * src_rows + m % src_rows) * ldc (that source's [experts, src_rows, N] combine buffer),
+// counts its finished tile warps in done_count[s] (local, zeroed before the launch) and the warp that completes
+// source s sets *done_flag[s] = epoch there.
+struct GemmPeer {
+  int src_rows;
+  uint32_t epoch;
+  const uint32_t* arrive;
+  __nv_bfloat16* out[kMaxPeers];
+  int b_base;
+  unsigned* done_count;
+  uint32_t* done_flag[kMaxPeers];
+  unsigned tile_warps_per_src;
+  unsigned long long timeout_ns;
+};
 struct GemmParams {
   int M, N, K, batch;
   void* C;
@@ -19,10 +39,15 @@ struct GemmParams {
   long long ldd, bsd;
   float alpha, beta;
   int* err;
+  GemmPeer peer;
 };
 // epi: 0 = bf16 store, 1 = fp32 store, 2 = fp32 accumulate (C += alpha * A B^T)
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int bn, bool a_mn,
                         bool b_mn, int epi, cudaStream_t s);
+// MoE exchange GEMM (bf16 output, A K-major, 128 x 256 tiles): peer_mode 1 = wait for A rows (p.peer.arrive),
+// 2 = scatter C rows to the sources (p.peer.out)
+cudaError_t gemm_peer_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, bool b_mn,
+                             int peer_mode, cudaStream_t s);
 
 
 // ---------------------------------------------------------------- norms (norm.cu)
@@ -136,7 +161,6 @@ cudaError_t euler_cfg_launch(const __nv_bfloat16* out, float* z, int B, int T, i
                              cudaStream_t s);
 
 // ---------------------------------------------------------------- peer-memory collectives (comm.cu)
-constexpr int kMaxPeers = 8;
 struct PeerAllReduceParams {
   float* grads;                        // local fp32 gradients [n], averaged in place
   long long n, slice;                  // slice = per-rank share (multiple of 8); buffers hold world * slice
@@ -198,6 +222,38 @@ struct MuonAGParams {
   unsigned long long timeout_ns;
   int* err;
 };
+// MoE dispatch / combine over peer memory (moe_comm.cu). Static capacity: this rank's dispatch holds C rows per
+// expert; expert e = r * local + j lives on rank r, whose receive buffer is [local][world][C][D] (source-major
+// within an expert, so an expert's rows from source s are one contiguous block of C rows).
+struct MoEDispatchParams {
+  const __nv_bfloat16* x;              // [N, D] token rows (forward) or output gradients (backward)
+  const int* src_tok;                  // [E * C] token of each of this rank's slots (-1: empty slot -> zeros)
+  const float* scale;                  // optional [E * C] row scale (routing weight, backward)
+  __nv_bfloat16* recv[kMaxPeers];      // every rank's receive buffer
+  uint32_t* arrive[kMaxPeers];         // every rank's arrive flags [world]: word `rank` is set on the owner
+  const uint32_t* free_flags;          // optional local [world]: owner r released its receive rows for epoch - 1
+  unsigned* counter;                   // local [world] finished-CTA counters (zeroed before the launch)
+  int E, local, C, D, rank, world;
+  uint32_t epoch;
+  unsigned long long timeout_ns;
+  int* err;
+};
+struct MoECombineParams {
+  const __nv_bfloat16* ybuf;           // local [E * C, D] rows written by the owners
+  const int* slot;                     // [N, k] slot of every assignment (-1: dropped)
+  const float* w;                      // optional [N, k] weights (forward combine)
+  const uint32_t* done;                // local [world] flags set by the owners
+  __nv_bfloat16* out;                  // [N, D]
+  int N, k, D, world;
+  uint32_t epoch;
+  unsigned long long timeout_ns;
+  int* err;
+};
+cudaError_t moe_dispatch_launch(const MoEDispatchParams& p, int blocks_per_owner, cudaStream_t s);
+cudaError_t moe_combine_launch(const MoECombineParams& p, cudaStream_t s);
+// owner side: tell every source that this rank's receive rows may be overwritten (free_peer[s][rank] = epoch)
+cudaError_t moe_release_launch(uint32_t* const* free_peer, int rank, int world, uint32_t epoch, cudaStream_t s);
+
 cudaError_t attention_set_trace(long long* buf, int cta);  // profiling timeline (null: off)
 cudaError_t muon_rs_launch(const MuonRSParams& p, int blocks, cudaStream_t s);
 cudaError_t muon_momentum_launch(const MuonMomentumParams& p, cudaStream_t s);

@@ -138,7 +138,7 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor C, bool a_mn, bool b_mn, c10::o
                                         a_mn ? 64 : 128);
   CUtensorMap tb = make_tmap_bf16_sw128(B.data_ptr(), B.size(-1), B.size(-2), batch, B.stride(-2), bsB,
                                         b_mn ? 64 : (use_pair ? 128 : bn));
-  GemmParams p;
+  GemmParams p{};
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
@@ -185,6 +185,136 @@ static long long row_vec_stride(const c10::optional<at::Tensor>& t, int64_t D) {
   TORCH_CHECK(t->dim() == 2 && t->size(1) == D && t->stride(1) == 1, "per-batch vector must be [B, D] contiguous in D");
   TORCH_CHECK(t->stride(0) % 8 == 0, "per-batch vector batch stride must be a multiple of 8");
   return t->stride(0);
+}
+
+// Expert GEMM of the peer-memory MoE exchange (A [batch, M, K] K-major bf16 = the local receive buffer or local
+// activations; B [batch, N, K] or, b_mn, [batch, K, N]). mode 1: wait for the A rows of each source (arrive flags
+// at `arrive`), output to C. mode 2: scatter the output rows to the sources' combine buffers `out_ptrs` (row stride
+// N), raising their done flags `done_flag_ptrs` when a source's rows are complete.
+void gemm_peer(at::Tensor A, at::Tensor B, c10::optional<at::Tensor> C, bool b_mn, int64_t mode, int64_t src_rows,
+               int64_t epoch, int64_t arrive, std::vector<int64_t> out_ptrs, int64_t b_base,
+               c10::optional<at::Tensor> done_count, std::vector<int64_t> done_flag_ptrs, int64_t timeout_ns,
+               at::Tensor err) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16,
+              "gemm_peer: bf16 CUDA operands");
+  TORCH_CHECK(A.dim() == 3 && B.dim() == 3 && A.size(0) == B.size(0), "gemm_peer: [batch, rows, cols] operands");
+  TORCH_CHECK(A.stride(-1) == 1 && B.stride(-1) == 1, "gemm_peer: inner dim must be contiguous");
+  const c10::cuda::CUDAGuard guard(A.device());
+  const int64_t batch = A.size(0), M = A.size(1), K = A.size(2);
+  const int64_t N = b_mn ? B.size(2) : B.size(1);
+  TORCH_CHECK((b_mn ? B.size(1) : B.size(2)) == K, "gemm_peer: contraction mismatch");
+  TORCH_CHECK(K % 8 == 0 && N % 8 == 0 && B.size(-1) % 8 == 0, "gemm_peer: dims must be multiples of 8");
+  TORCH_CHECK(src_rows > 0 && src_rows % 128 == 0 && M % src_rows == 0 && M / src_rows <= kMaxPeers,
+              "gemm_peer: src_rows must be a multiple of 128 dividing M");
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.batch = (int)batch;
+  p.alpha = 1.f;
+  p.err = err_ptr(err);
+  p.peer.src_rows = (int)src_rows;
+  p.peer.epoch = (uint32_t)epoch;
+  p.peer.timeout_ns = (unsigned long long)timeout_ns;
+  if (mode == 1) {
+    TORCH_CHECK(C.has_value() && C->defined() && C->scalar_type() == at::kBFloat16 && C->dim() == 3 &&
+                    C->size(0) == batch && C->size(1) == M && C->size(2) == N && C->stride(-1) == 1,
+                "gemm_peer: C [batch, M, N] bf16");
+    TORCH_CHECK(arrive != 0, "gemm_peer: arrive flags");
+    p.C = C->data_ptr();
+    p.ldc = C->stride(1);
+    p.bsc = C->stride(0);
+    TORCH_CHECK(p.ldc % 8 == 0 && reinterpret_cast<uintptr_t>(p.C) % 16 == 0, "gemm_peer: C alignment");
+    p.peer.arrive = reinterpret_cast<const uint32_t*>(arrive);
+  } else {
+    TORCH_CHECK(mode == 2, "gemm_peer: mode 1 (wait) or 2 (scatter)");
+    const int64_t nsrc = M / src_rows;
+    TORCH_CHECK((int64_t)out_ptrs.size() == nsrc && (int64_t)done_flag_ptrs.size() == nsrc, "gemm_peer: one "
+                "output buffer and one done flag per source");
+    TORCH_CHECK(done_count.has_value() && done_count->is_cuda() && done_count->scalar_type() == at::kInt &&
+                    done_count->numel() >= nsrc, "gemm_peer: done_count int32 [sources]");
+    p.ldc = N;
+    for (int64_t s = 0; s < nsrc; ++s) {
+      p.peer.out[s] = reinterpret_cast<__nv_bfloat16*>(out_ptrs[s]);
+      p.peer.done_flag[s] = reinterpret_cast<uint32_t*>(done_flag_ptrs[s]);
+      TORCH_CHECK(out_ptrs[s] % 16 == 0, "gemm_peer: output buffers must be 16-byte aligned");
+    }
+    p.peer.b_base = (int)b_base;
+    p.peer.done_count = reinterpret_cast<unsigned*>(done_count->data_ptr<int>());
+    p.peer.tile_warps_per_src = (unsigned)((src_rows / 128) * ((N + 255) / 256) * batch * 4);
+  }
+  CUtensorMap ta = make_tmap_bf16_sw128(A.data_ptr(), K, M, batch, A.stride(1), A.stride(0), 128);
+  CUtensorMap tb = make_tmap_bf16_sw128(B.data_ptr(), B.size(2), B.size(1), batch, B.stride(1), B.stride(0),
+                                        b_mn ? 64 : 256);
+  TGO_CHECK_LAUNCH(gemm_peer_launch(ta, tb, p, b_mn, (int)mode, at::cuda::getCurrentCUDAStream()));
+}
+
+void moe_dispatch(at::Tensor x, at::Tensor src_tok, c10::optional<at::Tensor> scale, std::vector<int64_t> recv_ptrs,
+                  std::vector<int64_t> arrive_ptrs, int64_t free_flags, at::Tensor counter, int64_t E, int64_t local,
+                  int64_t C, int64_t rank, int64_t epoch, int64_t timeout_ns, int64_t blocks, at::Tensor err) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2,
+              "moe_dispatch: x [N, D] bf16 contiguous");
+  TORCH_CHECK(src_tok.is_cuda() && src_tok.scalar_type() == at::kInt && src_tok.numel() == E * C &&
+                  src_tok.is_contiguous(), "moe_dispatch: src_tok int32 [E * C]");
+  TORCH_CHECK(counter.is_cuda() && counter.scalar_type() == at::kInt, "moe_dispatch: counter int32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int world = (int)recv_ptrs.size();
+  TORCH_CHECK(world >= 1 && world <= kMaxPeers && (int)arrive_ptrs.size() == world && counter.numel() >= world,
+              "moe_dispatch: one receive buffer and arrive flag array per rank");
+  MoEDispatchParams p{};
+  p.x = bfp(x);
+  p.src_tok = src_tok.data_ptr<int>();
+  p.scale = f32_ptr_or_null(scale);
+  if (p.scale != nullptr) TORCH_CHECK(scale->numel() == E * C, "moe_dispatch: scale [E * C]");
+  for (int r = 0; r < world; ++r) {
+    p.recv[r] = reinterpret_cast<__nv_bfloat16*>(recv_ptrs[r]);
+    p.arrive[r] = reinterpret_cast<uint32_t*>(arrive_ptrs[r]);
+    TORCH_CHECK(recv_ptrs[r] % 16 == 0, "moe_dispatch: receive buffers must be 16-byte aligned");
+  }
+  p.free_flags = reinterpret_cast<const uint32_t*>(free_flags);
+  p.counter = reinterpret_cast<unsigned*>(counter.data_ptr<int>());
+  p.E = (int)E;
+  p.local = (int)local;
+  p.C = (int)C;
+  p.D = (int)x.size(1);
+  p.rank = (int)rank;
+  p.world = world;
+  p.epoch = (uint32_t)epoch;
+  p.timeout_ns = (unsigned long long)timeout_ns;
+  p.err = err_ptr(err);
+  TGO_CHECK_LAUNCH(moe_dispatch_launch(p, (int)blocks, at::cuda::getCurrentCUDAStream()));
+}
+
+void moe_combine(int64_t ybuf, at::Tensor slot, c10::optional<at::Tensor> w, int64_t done, at::Tensor out,
+                 int64_t world, int64_t epoch, int64_t timeout_ns, at::Tensor err) {
+  TORCH_CHECK(slot.is_cuda() && slot.scalar_type() == at::kInt && slot.dim() == 2 && slot.is_contiguous(),
+              "moe_combine: slot int32 [N, k]");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.dim() == 2 &&
+                  out.size(0) == slot.size(0), "moe_combine: out [N, D] bf16");
+  const c10::cuda::CUDAGuard guard(out.device());
+  MoECombineParams p{};
+  p.ybuf = reinterpret_cast<const __nv_bfloat16*>(ybuf);
+  p.slot = slot.data_ptr<int>();
+  p.w = f32_ptr_or_null(w);
+  if (p.w != nullptr) TORCH_CHECK(w->sizes() == slot.sizes(), "moe_combine: w [N, k]");
+  p.done = reinterpret_cast<const uint32_t*>(done);
+  p.out = bfp(out);
+  p.N = (int)slot.size(0);
+  p.k = (int)slot.size(1);
+  p.D = (int)out.size(1);
+  p.world = (int)world;
+  p.epoch = (uint32_t)epoch;
+  p.timeout_ns = (unsigned long long)timeout_ns;
+  p.err = err_ptr(err);
+  TGO_CHECK_LAUNCH(moe_combine_launch(p, at::cuda::getCurrentCUDAStream()));
+}
+
+void moe_release(std::vector<int64_t> free_ptrs, int64_t rank, int64_t epoch) {
+  TORCH_CHECK(!free_ptrs.empty() && (int)free_ptrs.size() <= kMaxPeers, "moe_release: one flag array per rank");
+  uint32_t* f[kMaxPeers] = {};
+  for (size_t r = 0; r < free_ptrs.size(); ++r) f[r] = reinterpret_cast<uint32_t*>(free_ptrs[r]);
+  TGO_CHECK_LAUNCH(moe_release_launch(f, (int)rank, (int)free_ptrs.size(), (uint32_t)epoch,
+                                      at::cuda::getCurrentCUDAStream()));
 }
 
 // ------------------------------------------------------------------------------------------------ adanorm
@@ -746,6 +876,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &tgo::swiglu_bwd, "backward of swiglu_fwd");
   m.def("attention_fwd", &tgo::attention_fwd, "flash attention forward (GQA, key-length mask)");
   m.def("attention_bwd", &tgo::attention_bwd, "flash attention backward");
+  m.def("gemm_peer", &tgo::gemm_peer, "MoE expert GEMM: wait for peer-dispatched A rows, or scatter C to peers");
+  m.def("moe_dispatch", &tgo::moe_dispatch, "MoE dispatch: token gather + stores into the owners' receive buffers");
+  m.def("moe_combine", &tgo::moe_combine, "MoE combine: weighted gather-sum of the rows the owners returned");
+  m.def("moe_release", &tgo::moe_release, "MoE: release this rank's receive rows to every source");
   m.def("attention_varlen_fwd", &tgo::attention_varlen_fwd,
         "packed variable-length (optionally causal) attention forward on tcgen05");
 }

@@ -10,9 +10,12 @@ the Triton grouped GEMM aurora/moe_triton.py); this is the benchmark's MoE-DiT c
   beyond it are dropped, as in GShard / Switch). Dispatch is an index copy into [E, C, D]; the experts run as ONE
   batched tcgen05 GEMM per projection (E is the batch dimension), so there is no host synchronisation and no
   per-expert launch.
-* Expert parallelism: with a process group of size W (E % W == 0), rank r owns experts [r E/W, (r+1) E/W). The
-  [E, C, D] dispatch buffer is exchanged with one all_to_all (fixed splits: no count exchange needed), the local
-  experts run on [W, C, D] rows each, and a second all_to_all returns the outputs for the weighted combine.
+* Expert parallelism: with a process group of size W (E % W == 0), rank r owns experts [r E/W, (r+1) E/W).
+  ``transport="p2p"`` (CUDA): the dispatch and combine run over NVLink peer memory, fused with the token gather,
+  the expert GEMMs (which wait for arriving rows tile by tile and store their outputs into the sources' memory)
+  and the weighted sum (parallel/moe_comm.py). ``transport="nccl"``: the [E, C, D] dispatch buffer is exchanged
+  with one all_to_all (fixed splits: no count exchange needed), the local experts run on [W, C, D] rows each, and
+  a second all_to_all returns the outputs for the weighted combine.
 """
 import math
 
@@ -57,10 +60,10 @@ def batched_linear(x, w):
 
 
 class MoEMLP(nn.Module):
-    def __init__(self, dim, hidden, experts=8, top_k=2, capacity_factor=1.25, group=None):
+    def __init__(self, dim, hidden, experts=8, top_k=2, capacity_factor=1.25, group=None, transport="p2p"):
         super().__init__()
         self.dim, self.hidden, self.E, self.k, self.cf = dim, hidden, experts, top_k, capacity_factor
-        self.group = group
+        self.group, self.transport, self.exchange = group, transport, None
         self.world = dist.get_world_size(group) if group is not None else 1
         self.rank = dist.get_rank(group) if group is not None else 0
         assert experts % self.world == 0
@@ -77,8 +80,31 @@ class MoEMLP(nn.Module):
         nn.init.normal_(self.w_in, std=self.dim ** -0.5)
         nn.init.normal_(self.w_out, std=self.hidden ** -0.5)
 
-    def capacity(self, n_tokens):
-        return max(8, int(math.ceil(self.cf * n_tokens * self.k / self.E / 8)) * 8)
+    def capacity(self, n_tokens, multiple=8):
+        return max(multiple, int(math.ceil(self.cf * n_tokens * self.k / self.E / multiple)) * multiple)
+
+    def _fused(self, x):
+        return self.transport == "p2p" and x.is_cuda and self.dim % 64 == 0 and self.hidden % 64 == 0
+
+    def _forward_fused(self, x2, w, idx):
+        """Peer-memory exchange fused with the expert GEMMs (parallel/moe_comm.py)."""
+        from ..parallel.moe_comm import MoEPeerExchange, exchange_experts
+        N = x2.shape[0]
+        C = self.capacity(N, 128)
+        if self.exchange is None or self.exchange.C != C:
+            self.exchange = MoEPeerExchange(self.E, self.local, C, self.dim, self.hidden, self.group, x2.device)
+        flat_e = idx.reshape(-1)
+        onehot = F.one_hot(flat_e, self.E)
+        pos = (onehot.cumsum(0) - onehot).gather(1, flat_e[:, None]).squeeze(1)
+        keep = pos < C
+        slot = torch.where(keep, flat_e * C + pos, torch.full_like(pos, -1))
+        tok = torch.arange(N, device=x2.device).repeat_interleave(self.k)
+        src_tok = torch.full((self.E * C,), -1, dtype=torch.int32, device=x2.device)
+        src_tok[slot[keep]] = tok[keep].to(torch.int32)
+        slot_w = torch.zeros(self.E * C, dtype=torch.float32, device=x2.device)
+        slot_w[slot[keep]] = w.detach().reshape(-1)[keep].float()
+        return exchange_experts(x2, w, self.w_in, self.w_out, self.exchange, src_tok,
+                                slot.view(N, self.k).to(torch.int32).contiguous(), slot_w)
 
     def route(self, x2):
         logits = F.linear(x2.float(), self.router.weight.float())
@@ -101,6 +127,8 @@ class MoEMLP(nn.Module):
         x2 = h.reshape(-1, self.dim)
         N = x2.shape[0]
         w, idx = self.route(x2)
+        if self._fused(x2):
+            return self._forward_fused(x2, w, idx).view(shape)
         C = self.capacity(N)
         flat_e = idx.reshape(-1)                                    # [N k]
         onehot = F.one_hot(flat_e, self.E)
@@ -143,11 +171,12 @@ def moe_dense_reference(mlp, h):
     return out.view(h.shape)
 
 
-def moe_denoiser(den, experts=8, top_k=2, expert_hidden=4096, every=2, capacity_factor=1.25, group=None):
+def moe_denoiser(den, experts=8, top_k=2, expert_hidden=4096, every=2, capacity_factor=1.25, group=None,
+                 transport="p2p"):
     """Replace the MLP of every `every`-th block (odd blocks for every=2) with an MoE MLP, in place."""
     for i, blk in enumerate(den.blocks):
         if i % every == every - 1:
-            blk.mlp = MoEMLP(den.config.dim, expert_hidden, experts, top_k, capacity_factor, group).to(
+            blk.mlp = MoEMLP(den.config.dim, expert_hidden, experts, top_k, capacity_factor, group, transport).to(
                 den.patch_in.weight.device)
     return den
 

@@ -18,8 +18,9 @@ class PeerBuffers:
 
     def __init__(self, sizes, group=None, device=None):
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        single = not dist.is_initialized()  # one process: the buffers are only this GPU's
+        self.rank = 0 if single else dist.get_rank(group)
+        self.world = 1 if single else dist.get_world_size(group)
         self.group_ranks = dist.get_process_group_ranks(group) if group is not None else list(range(self.world))
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.local, self.ptrs, self._opened = {}, {}, []
@@ -28,8 +29,10 @@ class PeerBuffers:
             ptr, h = ext().symm_alloc(int(nbytes), self.device.index)
             self.local[name] = ptr
             handles[name] = h
-        gathered = [None] * self.world
-        dist.all_gather_object(gathered, handles, group=group)
+        gathered = [handles]
+        if not single:
+            gathered = [None] * self.world
+            dist.all_gather_object(gathered, handles, group=group)
         for name in sizes:
             row = []
             for peer in range(self.world):
@@ -43,10 +46,13 @@ class PeerBuffers:
 
     def close(self):
         torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)  # nobody may still access a peer's memory
+        multi = dist.is_initialized() and self.world > 1
+        if multi:
+            dist.barrier(group=self.group)  # nobody may still access a peer's memory
         for p in self._opened:
             ext().ipc_close(p, self.device.index)
-        dist.barrier(group=self.group)
+        if multi:
+            dist.barrier(group=self.group)
         for p in self.local.values():
             ext().symm_free(p, self.device.index)
         self._opened, self.local, self.ptrs = [], {}, {}

@@ -82,6 +82,7 @@ class TrainConfig:
     moe_every: int = 2
     moe_capacity: float = 1.25
     moe_aux_weight: float = 0.01
+    moe_transport: str = "p2p"    # expert exchange: "p2p" (peer memory fused with the expert GEMMs) or "nccl"
     expert_parallel: bool = True  # experts sharded over the data-parallel group
 
     def derived(self, world=1):
@@ -111,7 +112,9 @@ class Trainer:
         if cfg.moe_experts:
             from ..models.moe import MoEMLP, moe_denoiser
             ep_group = dist.group.WORLD if (cfg.expert_parallel and self.distributed and self.world > 1) else None
-            moe_denoiser(den, cfg.moe_experts, cfg.moe_top_k, cfg.moe_hidden, cfg.moe_every, cfg.moe_capacity, ep_group)
+            transport = cfg.moe_transport if not cfg.act_checkpoint else "nccl"  # recomputed blocks: no epochs
+            moe_denoiser(den, cfg.moe_experts, cfg.moe_top_k, cfg.moe_hidden, cfg.moe_every, cfg.moe_capacity, ep_group,
+                         transport)
             torch.manual_seed(cfg.seed * 7919 + (self.rank if ep_group is not None else 0))
             for m in den.modules():  # each rank's experts are different experts
                 if isinstance(m, MoEMLP):
