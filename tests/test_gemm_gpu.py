@@ -54,3 +54,36 @@ def test_gemm_batched_strided():
     b = torch.randn(4, 256, 192, device="cuda").bfloat16()
     c = gemm(a, b, b_mn=True)
     assert _rel(c, a.float() @ b.float()) < 1e-2
+
+
+@pytest.mark.parametrize("b_mn", [False, True])
+def test_gemm_grouped_device_schedule(b_mn):
+    """Grouped GEMM with the tile schedule built on the device: uneven, empty and sub-tile groups, routing-weight row
+    scale, against fp32 per-group products."""
+    from trenowanie_generatora_obrazkow_b200.ops.gemm import gemm_grouped
+    torch.manual_seed(0)
+    counts = [300, 0, 5, 128, 257, 0]
+    K, N = 512, 384
+    M = sum(counts)
+    off = torch.tensor([0] + counts).cumsum(0).to(torch.int32)
+    a = torch.randn(M, K, device="cuda").bfloat16()
+    b = torch.randn(len(counts), K, N, device="cuda").bfloat16() if b_mn else \
+        torch.randn(len(counts), N, K, device="cuda").bfloat16()
+    rs = torch.rand(M, device="cuda")
+    out = gemm_grouped(a, b, off.cuda(), b_mn=b_mn, row_scale=rs)
+    ref = gemm_grouped(a.cpu().float(), b.cpu().float(), off, b_mn=b_mn, row_scale=rs.cpu())
+    err = ((out.float().cpu() - ref).norm() / ref.norm()).item()
+    assert err < 1e-2, err
+
+
+def test_fused_moe_inference_gpu():
+    from trenowanie_generatora_obrazkow_b200.models.moe_infer import FusedMoE
+    torch.manual_seed(2)
+    E, H, I = 16, 256, 384
+    router = torch.randn(E, H) * 0.1
+    gu, dn = torch.randn(E, 2 * I, H) * H ** -0.5, torch.randn(E, H, I) * I ** -0.5
+    x = torch.randn(500, H)
+    ref = FusedMoE(router, gu, dn, 4)(x)  # CPU path (fp32 grouped products)
+    got = FusedMoE(router, gu, dn, 4).to("cuda")(x.cuda().bfloat16())
+    err = ((got.float().cpu() - ref).norm() / ref.norm()).item()
+    assert err < 2e-2, err

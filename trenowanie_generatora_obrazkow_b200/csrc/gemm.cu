@@ -26,7 +26,7 @@ constexpr int GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
 
 enum GemmEpi { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2 };
-enum GemmPeerMode { PEER_NONE = 0, PEER_WAIT_A = 1, PEER_SCATTER_C = 2 };
+enum GemmPeerMode { PEER_NONE = 0, PEER_WAIT_A = 1, PEER_SCATTER_C = 2, GROUPED = 3 };
 
 
 template <int BN>
@@ -64,8 +64,9 @@ template <int EPI>
 __device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int b, int row, int col0, const uint32_t (&r)[32]) {
   if (row >= p.M || col0 >= p.N) return;
   float v[32];
+  const float a = p.row_scale != nullptr ? p.alpha * p.row_scale[row] : p.alpha;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * a;
   const bool full = col0 + 32 <= p.N;
   if constexpr (EPI == EPI_BF16) {
     if (p.D != nullptr) {
@@ -134,10 +135,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int num_m = (p.M + GEMM_BM - 1) / GEMM_BM;
   const int num_n = (p.N + BN - 1) / BN;
   const int tiles_per_batch = num_m * num_n;
-  const int num_tiles = tiles_per_batch * p.batch;
+  int num_tiles = tiles_per_batch * p.batch;
   const int num_kb = (p.K + GEMM_BK - 1) / GEMM_BK;
+  // GROUPED: row-block prefix over the groups (device-side schedule: no host read of the group sizes)
+  __shared__ int grp_off[PEER == GROUPED ? kMaxGroups + 1 : 1];
+  __shared__ int grp_mb[PEER == GROUPED ? kMaxGroups + 1 : 1];
 
   if (threadIdx.x == 0) {
+    if constexpr (PEER == GROUPED) {
+      int acc = 0;
+      for (int g = 0; g <= p.batch; ++g) {
+        grp_off[g] = p.group_offsets[g];
+        grp_mb[g] = acc;
+        if (g < p.batch) acc += (p.group_offsets[g + 1] - p.group_offsets[g] + GEMM_BM - 1) / GEMM_BM;
+      }
+    }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
@@ -161,6 +173,30 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
+  if constexpr (PEER == GROUPED) num_tiles = grp_mb[p.batch] * num_n;
+  // tile -> (batch / group b, first row m0 within it, first column n0, A / C row base, valid rows)
+  auto decode = [&](int tile, int& b, int& m0, int& n0, int& row_base, int& rows) {
+    if constexpr (PEER == GROUPED) {
+      const int mb = tile / num_n;
+      n0 = (tile % num_n) * BN;
+      int lo = 0, hi = p.batch - 1;  // last group whose first row block is <= mb
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (grp_mb[mid] <= mb) lo = mid; else hi = mid - 1;
+      }
+      b = lo;
+      m0 = (mb - grp_mb[lo]) * GEMM_BM;
+      row_base = grp_off[lo];
+      rows = grp_off[lo + 1] - grp_off[lo];
+    } else {
+      b = tile / tiles_per_batch;
+      const int r = tile % tiles_per_batch;
+      m0 = (r / num_n) * GEMM_BM;
+      n0 = (r % num_n) * BN;
+      row_base = 0;
+      rows = p.M;
+    }
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -169,8 +205,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       uint32_t phase = 0;
       uint32_t arrived = 0;  // PEER_WAIT_A: bit s = the rows of source s are in place
       for (int tile = blockIdx.x; tile < num_tiles && !abort_sh; tile += gridDim.x) {
-        const int b = tile / tiles_per_batch, r = tile % tiles_per_batch;
-        const int m0 = (r / num_n) * GEMM_BM, n0 = (r % num_n) * BN;
+        int b, m0, n0, row_base, rows;
+        decode(tile, b, m0, n0, row_base, rows);
+        (void)rows;
         if constexpr (PEER == PEER_WAIT_A) {
           const int src = m0 / p.peer.src_rows;
           if (!((arrived >> src) & 1u)) {
@@ -192,7 +229,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           uint8_t* sb = sa + Cfg::A_BYTES;
           mbar_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
           const int k0 = kb * GEMM_BK;
-          if constexpr (!A_MN) {
+          if constexpr (PEER == GROUPED) {
+            tma_load_3d(sa, &tmA, &full_bar[stage], k0, row_base + m0, 0);  // rows past the group: not stored
+          } else if constexpr (!A_MN) {
             tma_load_3d(sa, &tmA, &full_bar[stage], k0, m0, b);
           } else {
             tma_load_3d(sa, &tmA, &full_bar[stage], m0, k0, b);
@@ -275,8 +314,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       __syncwarp();
       tc_fence_after();
-      const int b = tile / tiles_per_batch, r = tile % tiles_per_batch;
-      const int m0 = (r / num_n) * GEMM_BM, n0 = (r % num_n) * BN;
+      int b, m0, n0, row_base, rows;
+      decode(tile, b, m0, n0, row_base, rows);
       const int row = m0 + q * 32 + lane;
       const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
@@ -286,6 +325,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tmem_ld_wait();
         if constexpr (PEER == PEER_SCATTER_C) {
           gemm_store_chunk_peer(p, b, row, n0 + c * 32, v);
+        } else if constexpr (PEER == GROUPED) {
+          if (row < rows) gemm_store_chunk<EPI>(p, 0, row_base + row, n0 + c * 32, v);
         } else {
           gemm_store_chunk<EPI>(p, b, row, n0 + c * 32, v);
         }
@@ -573,6 +614,25 @@ static cudaError_t launch_gemm_peer(const CUtensorMap& ta, const CUtensorMap& tb
   }
   const int tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * ((p.N + 255) / 256) * p.batch;
   kern<<<std::min(tiles, num_sms()), GEMM_THREADS, Cfg::SMEM, s>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_grouped_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, bool b_mn,
+                                cudaStream_t s) {
+  if (p.batch < 1 || p.batch > kMaxGroups || p.group_offsets == nullptr) return cudaErrorInvalidValue;
+  using Cfg = GemmCfg<256>;
+  auto kern = b_mn ? gemm_tcgen05_kernel<256, false, true, EPI_BF16, GROUPED>
+                   : gemm_tcgen05_kernel<256, false, false, EPI_BF16, GROUPED>;
+  static bool set[2] = {false, false};
+  if (!set[b_mn]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    if (e != cudaSuccess) return e;
+    set[b_mn] = true;
+  }
+  // the tile count is known on the device only: a persistent grid, bounded by the worst case
+  const long long worst = ((long long)(p.M + GEMM_BM - 1) / GEMM_BM + p.batch) * ((p.N + 255) / 256);
+  const int grid = (int)std::max(1LL, std::min<long long>(worst, num_sms()));
+  kern<<<grid, GEMM_THREADS, Cfg::SMEM, s>>>(ta, tb, p);
   return cudaGetLastError();
 }
 

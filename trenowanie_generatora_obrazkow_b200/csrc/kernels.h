@@ -40,10 +40,18 @@ struct GemmParams {
   float alpha, beta;
   int* err;
   GemmPeer peer;
+  // grouped mode (gemm_grouped_launch): A rows [offsets[g], offsets[g + 1]) use B batch g; C rows as A's
+  const int* group_offsets;            // device [batch + 1], batch = groups (<= kMaxGroups)
+  const float* row_scale;              // optional [M]: output row r scaled by row_scale[r]
 };
+constexpr int kMaxGroups = 256;
 // epi: 0 = bf16 store, 1 = fp32 store, 2 = fp32 accumulate (C += alpha * A B^T)
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int bn, bool a_mn,
                         bool b_mn, int epi, cudaStream_t s);
+// Grouped GEMM with a device-side tile schedule (no host synchronisation on the group sizes): bf16 output,
+// A [M, K] K-major with the rows of group g at [offsets[g], offsets[g + 1]), B [groups, N, K] (or, b_mn, [groups, K, N]).
+cudaError_t gemm_grouped_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, bool b_mn,
+                                cudaStream_t s);
 // MoE exchange GEMM (bf16 output, A K-major, 128 x 256 tiles): peer_mode 1 = wait for A rows (p.peer.arrive),
 // 2 = scatter C rows to the sources (p.peer.out)
 cudaError_t gemm_peer_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, bool b_mn,

@@ -249,6 +249,44 @@ void gemm_peer(at::Tensor A, at::Tensor B, c10::optional<at::Tensor> C, bool b_m
   TGO_CHECK_LAUNCH(gemm_peer_launch(ta, tb, p, b_mn, (int)mode, at::cuda::getCurrentCUDAStream()));
 }
 
+// Grouped GEMM (device-side schedule): A [M, K] bf16 rows sorted by group, offsets int32 [G + 1] on the device,
+// B [G, N, K] (or, b_mn, [G, K, N]) bf16, C [M, N] bf16; optional row_scale fp32 [M] multiplies output rows.
+void gemm_grouped(at::Tensor A, at::Tensor B, at::Tensor offsets, at::Tensor C, bool b_mn,
+                  c10::optional<at::Tensor> row_scale, at::Tensor err) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda() && A.scalar_type() == at::kBFloat16 &&
+                  B.scalar_type() == at::kBFloat16 && C.scalar_type() == at::kBFloat16, "gemm_grouped: bf16 CUDA");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 3 && C.dim() == 2 && A.stride(1) == 1 && B.stride(2) == 1 &&
+                  C.stride(1) == 1, "gemm_grouped: A [M, K], B [G, ., .], C [M, N], inner dims contiguous");
+  TORCH_CHECK(offsets.is_cuda() && offsets.scalar_type() == at::kInt && offsets.is_contiguous() &&
+                  offsets.numel() == B.size(0) + 1, "gemm_grouped: offsets int32 [G + 1] on the device");
+  const c10::cuda::CUDAGuard guard(A.device());
+  const int64_t M = A.size(0), K = A.size(1), G = B.size(0);
+  const int64_t N = b_mn ? B.size(2) : B.size(1);
+  TORCH_CHECK((b_mn ? B.size(1) : B.size(2)) == K, "gemm_grouped: contraction mismatch");
+  TORCH_CHECK(C.size(0) == M && C.size(1) == N, "gemm_grouped: C shape");
+  TORCH_CHECK(G >= 1 && G <= kMaxGroups, "gemm_grouped: 1 .. 256 groups");
+  TORCH_CHECK(K % 8 == 0 && N % 8 == 0 && B.size(2) % 8 == 0 && C.stride(0) % 8 == 0 && A.stride(0) % 8 == 0,
+              "gemm_grouped: dims / strides must be multiples of 8");
+  if (M == 0) return;
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.batch = (int)G;
+  p.C = C.data_ptr();
+  p.ldc = C.stride(0);
+  p.alpha = 1.f;
+  p.err = err_ptr(err);
+  p.group_offsets = offsets.data_ptr<int>();
+  p.row_scale = f32_ptr_or_null(row_scale);
+  if (p.row_scale != nullptr) TORCH_CHECK(row_scale->numel() == M, "gemm_grouped: row_scale [M]");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(p.C) % 16 == 0, "gemm_grouped: C alignment");
+  CUtensorMap ta = make_tmap_bf16_sw128(A.data_ptr(), K, M, 1, A.stride(0), 0, 128);
+  CUtensorMap tb = make_tmap_bf16_sw128(B.data_ptr(), B.size(2), B.size(1), G, B.stride(1), B.stride(0),
+                                        b_mn ? 64 : 256);
+  TGO_CHECK_LAUNCH(gemm_grouped_launch(ta, tb, p, b_mn, at::cuda::getCurrentCUDAStream()));
+}
+
 void moe_dispatch(at::Tensor x, at::Tensor src_tok, c10::optional<at::Tensor> scale, std::vector<int64_t> recv_ptrs,
                   std::vector<int64_t> arrive_ptrs, int64_t free_flags, at::Tensor counter, int64_t E, int64_t local,
                   int64_t C, int64_t rank, int64_t epoch, int64_t timeout_ns, int64_t blocks, at::Tensor err) {
@@ -876,6 +914,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &tgo::swiglu_bwd, "backward of swiglu_fwd");
   m.def("attention_fwd", &tgo::attention_fwd, "flash attention forward (GQA, key-length mask)");
   m.def("attention_bwd", &tgo::attention_bwd, "flash attention backward");
+  m.def("gemm_grouped", &tgo::gemm_grouped, "grouped GEMM with a device-side tile schedule (MoE experts)");
   m.def("gemm_peer", &tgo::gemm_peer, "MoE expert GEMM: wait for peer-dispatched A rows, or scatter C to peers");
   m.def("moe_dispatch", &tgo::moe_dispatch, "MoE dispatch: token gather + stores into the owners' receive buffers");
   m.def("moe_combine", &tgo::moe_combine, "MoE combine: weighted gather-sum of the rows the owners returned");

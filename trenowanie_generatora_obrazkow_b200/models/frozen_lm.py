@@ -35,7 +35,10 @@ class RandomFrozenLM:
 
 
 class HFFrozenLM:
-    def __init__(self, repo, skip_last=0, device=None):
+    """fused_moe: the LM's mixture-of-experts blocks run as stacked experts + grouped GEMMs (models/moe_infer.py),
+    optionally with int8 expert weights (quant="int8")."""
+
+    def __init__(self, repo, skip_last=0, device=None, fused_moe=True, quant=""):
         from transformers import AutoModelForCausalLM
         model = AutoModelForCausalLM.from_pretrained(repo, torch_dtype=torch.bfloat16, trust_remote_code=True,
                                                      local_files_only=True)
@@ -43,6 +46,9 @@ class HFFrozenLM:
         keep = len(layers) - skip_last
         model.model.layers = layers[:keep]
         self.model = model.model.to(device).eval().requires_grad_(False)
+        if fused_moe:
+            from .moe_infer import patch_moe_blocks
+            patch_moe_blocks(self.model, quant=quant)
 
     def to(self, device):
         self.model.to(device)
@@ -122,7 +128,7 @@ def build_frozen_lm(cfg, device=None, allow_random=False):
                 raise
         return RandomFrozenLM(cfg.lm_dim, device=device)
     if backend == "hf":
-        return HFFrozenLM(cfg.repo, cfg.skip_last, device)
+        return HFFrozenLM(cfg.repo, cfg.skip_last, device, quant=getattr(cfg, "quant", ""))
     if backend == "slayer":
         return SlayerFrozenLM(cfg.repo, cfg.skip_last, device)
     raise RuntimeError(f"frozen LM backend {backend!r} needs pretrained weights that are not available offline; "

@@ -1,0 +1,113 @@
+"""Fused MoE inference for the frozen caption LM's mixture-of-experts layers (reference aurora/hf_compat.py:62-169,
+which replaces the transformers per-expert loop with stacked weights and a Triton grouped GEMM).
+
+``FusedMoE`` holds the experts stacked: gate and up projections as one (E, 2I, H) weight (one GEMM computes both),
+down projections as (E, H, I), optionally int8 with a per-(expert, output column) scale, dequantised per call.
+A forward: router logits in fp32 -> top-k -> assignments sorted by expert (stable) -> token rows gathered in that
+order -> grouped GEMM (gate | up) -> SwiGLU -> grouped GEMM (down) with the routing weight as a per-row epilogue
+scale -> rows summed back per token. The grouped GEMM's tile schedule comes from the expert offsets on the device
+(ops/gemm.py:gemm_grouped), so there is no host synchronisation and one launch per projection, whatever the
+routing.
+
+``patch_moe_blocks(model)`` finds transformers-style MoE blocks (a ``gate`` linear router and an ``experts`` list
+of gate_proj / up_proj / down_proj MLPs, plus optional ``shared_experts``) and replaces their forward.
+"""
+import torch
+import torch.nn.functional as F
+
+from ..ops import fused as Fz
+from ..ops.gemm import gemm_grouped
+
+
+def _quant_int8(w):
+    """Per-(expert, output row) symmetric int8: w (E, N, K) -> (int8 (E, N, K), scale (E, N))."""
+    s = w.float().abs().amax(-1).clamp(min=1e-8) / 127.0
+    return (w.float() / s[..., None]).round().clamp(-127, 127).to(torch.int8), s
+
+
+class FusedMoE:
+    def __init__(self, router_w, gate_up, down, top_k, norm_topk=True, quant=""):
+        self.router_w = router_w.float()
+        self.E, self.k, self.norm = router_w.shape[0], top_k, norm_topk
+        self.quant = quant
+        if quant == "int8":
+            self.gu, self.gu_s = _quant_int8(gate_up)
+            self.dn, self.dn_s = _quant_int8(down)
+        else:  # bf16 once on a GPU (to()), the given precision on the CPU
+            self.gu, self.dn = gate_up, down
+
+    @classmethod
+    def from_block(cls, block, top_k=None, norm_topk=None, quant=""):
+        ex = block.experts
+        gate_up = torch.stack([torch.cat([e.gate_proj.weight, e.up_proj.weight], 0) for e in ex]).detach()
+        down = torch.stack([e.down_proj.weight for e in ex]).detach()
+        k = top_k or getattr(block, "top_k", None) or getattr(getattr(block, "config", None), "num_experts_per_tok", 2)
+        norm = norm_topk if norm_topk is not None else getattr(getattr(block, "config", None), "norm_topk_prob", True)
+        return cls(block.gate.weight.detach(), gate_up, down, k, norm, quant)
+
+    def to(self, device):
+        cuda = torch.device(device).type == "cuda"
+        for name in ("router_w", "gu", "dn", "gu_s", "dn_s"):
+            if hasattr(self, name):
+                t = getattr(self, name).to(device)
+                if cuda and name in ("gu", "dn") and t.is_floating_point():
+                    t = t.to(torch.bfloat16)
+                setattr(self, name, t)
+        return self
+
+    def _weights(self):
+        if self.quant == "int8":
+            return ((self.gu.float() * self.gu_s[..., None]).to(torch.bfloat16),
+                    (self.dn.float() * self.dn_s[..., None]).to(torch.bfloat16))
+        return self.gu, self.dn
+
+    def route(self, x):
+        probs = F.linear(x.float(), self.router_w).softmax(-1)
+        w, idx = probs.topk(self.k, dim=-1)
+        if self.norm:
+            w = w / w.sum(-1, keepdim=True)
+        return w, idx
+
+    @torch.no_grad()
+    def __call__(self, x):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        N = x2.shape[0]
+        w, idx = self.route(x2)
+        flat = idx.reshape(-1)
+        order = flat.argsort(stable=True)
+        tok = order // self.k
+        counts = torch.bincount(flat, minlength=self.E)
+        offsets = torch.zeros(self.E + 1, dtype=torch.int32, device=x.device)
+        offsets[1:] = counts.cumsum(0)
+        xs = x2.to(torch.bfloat16 if x.is_cuda else torch.float32)[tok]
+        gu, dn = (w_.to(xs.dtype) for w_ in self._weights())
+        ab = gemm_grouped(xs, gu, offsets)
+        h = Fz.swiglu(ab)
+        y = gemm_grouped(h.to(xs.dtype), dn, offsets, row_scale=w.reshape(-1)[order])
+        out = torch.zeros(N, shape[-1], dtype=torch.float32, device=x.device)
+        out.index_add_(0, tok, y.float())
+        return out.to(x.dtype).view(shape)
+
+
+def patch_moe_blocks(model, quant=""):
+    """Replace the forward of every transformers-style MoE block of ``model`` by FusedMoE (+ its shared experts).
+    Returns the number of blocks patched."""
+    n = 0
+    for mod in model.modules():
+        ex = getattr(mod, "experts", None)
+        gate = getattr(mod, "gate", None)
+        if ex is None or gate is None or not hasattr(gate, "weight") or len(ex) == 0:
+            continue
+        if not all(hasattr(e, a) for e in ex for a in ("gate_proj", "up_proj", "down_proj")):
+            continue
+        fused = FusedMoE.from_block(mod, quant=quant).to(gate.weight.device)
+        shared = getattr(mod, "shared_experts", None)
+
+        def forward(hidden_states, *a, _f=fused, _s=shared, **k):
+            out = _f(hidden_states)
+            return out + _s(hidden_states) if _s is not None else out
+        mod.forward = forward
+        mod._fused_moe = fused
+        n += 1
+    return n

@@ -50,3 +50,27 @@ def linear_wgrad(dy2d, x2d, out=None, accumulate=False):
     if out is None:
         out = torch.empty(dy2d.shape[-1], x2d.shape[-1], device=dy2d.device, dtype=torch.float32)
     return gemm(dy2d, x2d, out=out, a_mn=True, b_mn=True, accumulate=accumulate)
+
+
+def gemm_grouped(a, b, offsets, b_mn=False, row_scale=None):
+    """Grouped GEMM: rows [offsets[g], offsets[g + 1]) of a (M, K) times group g of b (G, N, K) (b_mn: (G, K, N))
+    -> (M, N). On CUDA one persistent tcgen05 launch whose tile schedule is derived from ``offsets`` on the device
+    (reference aurora/moe_triton.py:13-107: grouped expert GEMM with a device-built block schedule); row_scale (M,)
+    multiplies the output rows (routing weights)."""
+    G = b.shape[0]
+    N = b.shape[-1] if b_mn else b.shape[-2]
+    if not a.is_cuda:
+        out = torch.zeros(a.shape[0], N, dtype=torch.float32)
+        off = [int(v) for v in offsets.tolist()]
+        for g in range(G):
+            lo, hi = off[g], off[g + 1]
+            if hi > lo:
+                w = b[g].float() if b_mn else b[g].float().T
+                out[lo:hi] = a[lo:hi].float() @ w
+        if row_scale is not None:
+            out *= row_scale.float()[:, None]
+        return out.to(a.dtype)
+    out = torch.empty(a.shape[0], N, device=a.device, dtype=torch.bfloat16)
+    ext().gemm_grouped(a.contiguous(), b.contiguous(), offsets.to(device=a.device, dtype=torch.int32).contiguous(),
+                       out, b_mn, None if row_scale is None else row_scale.float().contiguous(), err_buf(a.device))
+    return out
