@@ -394,7 +394,14 @@ def run_reference(args):
         nb = args.sample_batch
         sst = torch.randn(nb, args.text_len, 1024, generator=g).to(device, torch.bfloat16)
         s_ids = torch.randint(0, 60000, (nb, args.text_len), device=device)
-        te.eval(), den.eval()
+        te.eval()
+        # the reference's RoPE tables are (non-persistent) buffers sized by latent_size: a denoiser built for the
+        # sampling resolution takes the trained weights (the same state dict at any resolution)
+        from dataclasses import replace as _replace
+        den_s = Denoiser(_replace(den_cfg, latent_size=ss))
+        den_s.load_state_dict(den.state_dict())
+        den_s.to(device).eval()
+        den_s.compile()
         u = torch.linspace(1.0, 0.0, args.sample_steps + 1, device=device)
         shift = 6.0
         ts_all = shift * u / (1 + (shift - 1) * u)
@@ -410,7 +417,7 @@ def run_reference(args):
                                  lm_states=torch.cat([sst, sst]))
                 for k in range(steps):
                     t0, t1 = ts[k], ts[k + 1]
-                    v = den(torch.cat([z, z]), t0.expand(2 * nb), text, valid).float()
+                    v = den_s(torch.cat([z, z]), t0.expand(2 * nb), text, valid).float()
                     v_u, v_c = v.chunk(2)
                     z = z + (t1 - t0) * (v_u + 3.0 * (v_c - v_u))
             return z

@@ -60,6 +60,9 @@ def build_parser():
       help="resize-and-crop: take --res windows from these larger latent grids (<shard>.lat<res>.npy; 256 = .lat.npy)")
     a("--crop-prob", type=float, default=0.5)
     a("--t-shift-ref", type=float, default=0.0, help="resolution-dependent time shift res / REF (overrides --t-shift)")
+    a("--text-bucket", type=int, default=0, choices=[0, 8, 16, 32, 64, 128],
+      help="trim each micro-batch's captions to its longest one, rounded up to this multiple (0 = off)")
+    a("--length-sort", action="store_true", help="micro-batches of similar caption length (with --text-bucket)")
     a("--multi-res", type=int, nargs="*", default=[],
       help="mixed-resolution steps: these resolutions in every step (--res = the largest); latents of each from "
            "<shard>.lat<res>.npy (.lat.npy at 256)")
@@ -242,7 +245,7 @@ def main():
                      rope_random=args.rope_random, t_shift_ref=args.t_shift_ref,
                      repa_weight=args.repa_weight, repa_layer=args.repa_layer, repa_frac=args.repa_frac,
                      repa_until=args.repa_until, repa_every=args.repa_every, repa_target=args.repa_target,
-                     irepa=args.irepa,
+                     irepa=args.irepa, text_bucket=args.text_bucket, length_sort=args.length_sort,
                      outer_lr=args.outer_lr, outer_momentum=args.outer_momentum, outer_comm=args.outer_comm,
                      offload=args.offload, seed=args.seed, act_checkpoint=args.act_checkpoint,
                      random_lm=args.random_lm)

@@ -25,6 +25,20 @@ from . import diloco as D
 from .flow import FlowModel, drop_captions, make_mlm
 
 
+def trim_ids(ids, multiple):
+    """Drop the all-padding tail columns of right-padded caption rows, keeping a multiple of ``multiple`` columns
+    (reference aurora/slayer.py:276-281): the LM and the text attention then run on the real caption lengths."""
+    n = int(ids.ne(LM_PAD).sum(1).max()) if ids.numel() else 1
+    return ids[:, :min(ids.shape[1], max(multiple, -(-n // multiple) * multiple))]
+
+
+def length_sorted(ids, parts, generator=None):
+    """Row indices of ``parts`` micro-batches of similar caption length: sorted by length, shuffled inside each
+    part (reference aurora/slayer.py:284-292). Gradient accumulation sums over all parts, so the step is the same."""
+    order = ids.ne(LM_PAD).sum(1).argsort(stable=True)
+    return [part[torch.randperm(len(part), generator=generator)] for part in order.chunk(parts)]
+
+
 @dataclass
 class TrainConfig:
     global_batch: int = 256
@@ -83,6 +97,8 @@ class TrainConfig:
     moe_capacity: float = 1.25
     moe_aux_weight: float = 0.01
     moe_transport: str = "p2p"    # expert exchange: "p2p" (peer memory fused with the expert GEMMs) or "nccl"
+    text_bucket: int = 0          # > 0: trim each micro-batch's caption tokens to its longest caption, rounded up
+    length_sort: bool = False     # group the step's samples into micro-batches of similar caption length
     expert_parallel: bool = True  # experts sharded over the data-parallel group
 
     def derived(self, world=1):
@@ -189,6 +205,7 @@ class Trainer:
         self.ema = EMA(model_params, ema) if (self.rank == 0 or cfg.ema_on_all_ranks) else None
         self.step_idx = 0
         self.gen = torch.Generator(device=self.device)
+        self.cpu_gen = torch.Generator().manual_seed(cfg.seed * 7 + self.rank)  # host-side shuffles
         self.gen.manual_seed(cfg.seed * 1000 + self.rank)
         self.last_gnorm = None
         self.last = {}
@@ -250,13 +267,22 @@ class Trainer:
                 kw["mlm_ids"], kw["mlm_labels"] = make_mlm(ids, cfg.mlm_prob, self.gen)
             return kw
         if "ids" in batch:
-            ids = self._to_dev(batch["ids"][sl])
+            ids = batch["ids"][sl]
+            if cfg.text_bucket:
+                ids = trim_ids(ids, cfg.text_bucket)
+            ids = self._to_dev(ids)
             valid = ids.ne(LM_PAD)
             is_null = ids[:, 0].eq(LM_NULL)
             states = self.frozen_lm.states(ids)
         else:
-            states = self._to_dev(batch["lm_states"][sl])
-            valid = self._to_dev(batch["valid"][sl]) if batch.get("valid") is not None else \
+            states = batch["lm_states"][sl]
+            valid = batch["valid"][sl] if batch.get("valid") is not None else None
+            if cfg.text_bucket and valid is not None:
+                n = int(valid.sum(1).max()) if valid.numel() else 1
+                w = min(states.shape[1], max(cfg.text_bucket, -(-n // cfg.text_bucket) * cfg.text_bucket))
+                states, valid = states[:, :w], valid[:, :w]
+            states = self._to_dev(states)
+            valid = self._to_dev(valid) if valid is not None else \
                 torch.ones(b, states.shape[1], dtype=torch.bool, device=self.device)
             is_null = self._to_dev(batch["is_null"][sl]) if batch.get("is_null") is not None else None
         if cfg.cfg_drop > 0:
@@ -270,6 +296,10 @@ class Trainer:
         groups = batch.get("groups")
         if not groups:
             x0_all = self._to_dev(batch["x0"])
+            if self.cfg.length_sort and batch.get("ids") is not None:
+                for idx in length_sorted(batch["ids"], self.accum, self.cpu_gen):
+                    yield x0_all[idx.to(x0_all.device)], batch, idx
+                return
             for m in range(self.accum):
                 sl = slice(m * self.micro, (m + 1) * self.micro)
                 yield x0_all[sl], batch, sl
