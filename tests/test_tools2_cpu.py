@@ -1,0 +1,79 @@
+"""prepare_lowres.py (latent-pool method, resume), prepare_monet.py (slimming + shortest caption) and blimp_eval.py
+(minimal-pair scoring) on small local inputs."""
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def test_prepare_lowres_latent_pool(tmp_path):
+    import prepare_lowres
+    d = tmp_path / "shards"
+    d.mkdir()
+    for i in range(3):
+        np.save(d / f"s{i}.lat.npy", np.random.randn(5, 128, 16, 16).astype(np.float16))
+    prepare_lowres.main(["--data", str(d), "--latent-pool", "--sizes", "128", "64", "--batch", "2",
+                         "--device", "cpu"])
+    a = np.load(d / "s1.lat128.npy")
+    src = np.load(d / "s1.lat.npy").astype(np.float32)
+    assert a.shape == (5, 128, 8, 8) and np.load(d / "s1.lat64.npy").shape == (5, 128, 4, 4)
+    assert np.allclose(a, src.reshape(5, 128, 8, 2, 8, 2).mean((3, 5)), atol=2e-3)
+    m = os.path.getmtime(d / "s1.lat128.npy")
+    prepare_lowres.main(["--data", str(d), "--latent-pool", "--sizes", "128", "64", "--device", "cpu"])
+    assert os.path.getmtime(d / "s1.lat128.npy") == m  # resumed: nothing rewritten
+
+
+def test_prepare_monet_slims_and_picks_the_shortest_caption(tmp_path):
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+
+    import prepare_monet
+    src = tmp_path / "raw" / "part-0"
+    src.mkdir(parents=True)
+    t = pa.table({"prompt": ["p1", "p2"], "embedding_clip": [[0.1, 0.2], [0.3, 0.4]],
+                  "caption_florence-2-large": ["a  long caption with   many words", ""],
+                  "caption_internvl-3-8b": ["short one", "only this"]})
+    pq.write_table(t, src / "f.parquet")
+    prepare_monet.main(["--src", str(tmp_path / "raw"), "--out", str(tmp_path / "out"), "--workers", "1"])
+    out = pq.read_table(tmp_path / "out" / "part-0" / "f.parquet")
+    assert "embedding_clip" not in out.column_names
+    assert out["caption_short"].to_pylist() == ["short one", "only this"]
+
+
+def test_blimp_eval_scores_pairs(tmp_path):
+    from safetensors.torch import save_model
+    from tokenizers import Tokenizer, models, pre_tokenizers
+
+    import blimp_eval
+    from trenowanie_generatora_obrazkow_b200.models.slayer import GPT, GPTConfig
+    words = "the cat dog sees sleep sleeps a".split()
+    vocab = {"<|endoftext|>": 0, "[UNK]": 1, **{w: i + 2 for i, w in enumerate(words)}}
+    tok = Tokenizer(models.WordLevel(vocab, unk_token="[UNK]"))
+    tok.pre_tokenizer = pre_tokenizers.Whitespace()
+    tok.save(str(tmp_path / "tok.json"))
+    cfg = dict(vocab=16, n_layer=1, n_embd=32, n_head=2, block=16)
+    mdir = tmp_path / "lm"
+    mdir.mkdir()
+    json.dump(cfg, open(mdir / "config.json", "w"))
+    torch.manual_seed(0)
+    save_model(GPT(GPTConfig(**cfg)), str(mdir / "model.safetensors"))
+    data = tmp_path / "blimp"
+    data.mkdir()
+    with open(data / "agreement.jsonl", "w") as f:
+        for g, b in [("the cat sleeps", "the cat sleep"), ("a dog sees the cat", "a dog see the cat")]:
+            f.write(json.dumps({"sentence_good": g, "sentence_bad": b}) + "\n")
+    res = blimp_eval.main([str(mdir), "--data", str(data), "--tokenizer", str(tmp_path / "tok.json"),
+                           "--device", "cpu", "--out", str(tmp_path / "r.json")])
+    acc = res[str(mdir)]["accuracy"]
+    assert 0.0 <= acc <= 1.0 and set(res[str(mdir)]["paradigms"]) == {"agreement"}
+    sc = blimp_eval.Scorer(str(mdir), str(tmp_path / "tok.json"), "cpu")
+    ids = torch.tensor([[0, 2, 3, 7]])
+    lp = torch.log_softmax(sc.logits(ids).float(), -1)
+    want = sum(lp[0, i, ids[0, i + 1]].item() for i in range(3))
+    assert abs(sc(["the cat sleeps"])[0] - want) < 1e-4
