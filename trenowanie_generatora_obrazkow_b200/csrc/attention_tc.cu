@@ -65,6 +65,20 @@ __device__ __forceinline__ float ex2(float x) {  // hardware 2^x (MUFU)
   return y;
 }
 
+// 2^x for x <= 0 on the FMA pipe, so that the MUFU unit (16 results / clk / SM, the same rate at which head-dim-128
+// attention consumes exponentials at full tensor throughput) is not the softmax's bottleneck. Cody-Waite style
+// split x = n + f with round-to-nearest through the 1.5 * 2^23 shifter (f in [-0.5, 0.5]); 2^f by a degree-3
+// polynomial fitted for relative error on that interval (iteratively reweighted least squares on Chebyshev nodes:
+// max relative error 7.5e-5, below the bf16 rounding of P); 2^n added to the exponent field. Inputs below -125
+// clamp there (2^-125 instead of 0: negligible against a row sum >= 1).
+__device__ __forceinline__ float ex2_fma(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.0551716573f, f, 0.2426111400f), f, 0.6932609677f), f, 0.9999280572f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 template <int HD>
 struct FwdSmem {
   static constexpr int Q_BYTES = TQ * HD * 2;          // per Q tile: HD / 64 blocks of 128 rows x 128 B
@@ -342,8 +356,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int c = 0; c < 2; ++c) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float a = ex2(fmaf(__uint_as_float(sr[c][2 * e]), sl2, -mu));
-          const float bq = ex2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, -mu));
+          // about a third of the exponentials on the FMA pipe, the rest on MUFU
+          const float xa = fmaf(__uint_as_float(sr[c][2 * e]), sl2, -mu);
+          const float xb = fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, -mu);
+          const float a = (e % 3 == 2) ? ex2_fma(xa) : ex2(xa);
+          const float bq = (e % 3 == 2) ? ex2_fma(xb) : ex2(xb);
           rs0 += a;
           rs1 += bq;
           pk[c * 16 + e] = pack_bf16x2(a, bq);

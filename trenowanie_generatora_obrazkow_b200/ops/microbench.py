@@ -219,6 +219,7 @@ def cases(small):
         "wgrad_mlp_down": lambda: gemm_case(D, MLP, M, a_mn=True, b_mn=True, accumulate=True),
         "attn_fwd": lambda: attn_case(B, T, H, hd, False),
         "attn_bwd": lambda: attn_case(B, T, H, hd, True),
+        "attn_fwd_4k": lambda: attn_case(4 if small else 16, 4096, H, hd, False),  # 1024 px sampling (CFG batch)
         "adanorm_fwd": lambda: adanorm_case(B, T, D, False),
         "adanorm_bwd": lambda: adanorm_case(B, T, D, True),
         "qknorm_rope_fwd": lambda: qknorm_case(B, T, H, hd, False),
