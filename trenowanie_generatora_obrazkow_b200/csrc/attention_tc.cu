@@ -32,11 +32,11 @@ namespace {
 
 constexpr int TQ = 128;      // query rows per Q tile (one softmax warpgroup)
 constexpr int NQ = 2;        // Q tiles per CTA
-constexpr int TK = 64;       // keys per K / V tile
-constexpr int KV_STAGES = 4; // K and V rings
+constexpr int TK = 128;      // keys per K / V tile
+constexpr int KV_STAGES = 2; // K and V rings
 constexpr int THREADS = 320; // warp 0 TMA, warp 1 MMA, warps 2-5 softmax of Q tile 0, warps 6-9 of Q tile 1
 constexpr int TMEM_COLS = 512;
-constexpr int O_COL = 256;   // Q tile g: S buffers at g * 128 + {0, 64}; O at 256 + g * hd
+constexpr int O_COL = 256;   // Q tile g: S / P at g * 128 (P: bf16 pairs in the first 64 columns); O at 256 + g * hd
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
 // Optional per-phase timeline of one CTA (clock64 per event and iteration), for profiling the pipelines: off
@@ -65,24 +65,10 @@ __device__ __forceinline__ float ex2(float x) {  // hardware 2^x (MUFU)
   return y;
 }
 
-// 2^x for x <= 0 on the FMA pipe, so that the MUFU unit (16 results / clk / SM, the same rate at which head-dim-128
-// attention consumes exponentials at full tensor throughput) is not the softmax's bottleneck. Cody-Waite style
-// split x = n + f with round-to-nearest through the 1.5 * 2^23 shifter (f in [-0.5, 0.5]); 2^f by a degree-3
-// polynomial fitted for relative error on that interval (iteratively reweighted least squares on Chebyshev nodes:
-// max relative error 7.5e-5, below the bf16 rounding of P); 2^n added to the exponent field. Inputs below -125
-// clamp there (2^-125 instead of 0: negligible against a row sum >= 1).
-__device__ __forceinline__ float ex2_fma(float x) {
-  x = fmaxf(x, -125.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.0551716573f, f, 0.2426111400f), f, 0.6932609677f), f, 0.9999280572f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 template <int HD>
 struct FwdSmem {
   static constexpr int Q_BYTES = TQ * HD * 2;          // per Q tile: HD / 64 blocks of 128 rows x 128 B
-  static constexpr int KV_BYTES = TK * HD * 2;         // HD / 64 blocks of 64 rows x 128 B
+  static constexpr int KV_BYTES = TK * HD * 2;         // HD / 64 blocks of 128 rows x 128 B
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + NQ * Q_BYTES;
   static constexpr int V_OFF = K_OFF + KV_STAGES * KV_BYTES;
@@ -94,16 +80,23 @@ struct FwdBars {
   uint64_t q_full;
   uint64_t k_full[KV_STAGES], k_empty[KV_STAGES];  // K tile free once S of both Q tiles is computed
   uint64_t v_full[KV_STAGES], v_empty[KV_STAGES];  // V tile free once P V of both Q tiles is computed
-  uint64_t s_full[NQ][2];                          // S_j of Q tile g in TMEM buffer j & 1
-  uint64_t s_free[NQ][2];                          // P V of the tile that last used the buffer finished
-  uint64_t p_full[NQ][2];                          // softmax wrote P_j over S_j: 128 arrivals
-  uint64_t pv_done[NQ];                            // one phase per P V
+  uint64_t s_full[NQ];                             // S_g(j) in TMEM (and, by issue order, P_g(j-1) V done)
+  uint64_t p_full[NQ];                             // softmax wrote P_g(j) over S_g(j): 128 arrivals
+  uint64_t pv_done[NQ];                            // one phase per P_g(j) V_j
   uint32_t tmem_base;
   int abort_flag;
 };
 
 }  // namespace
 
+// Schedule (one MMA-issuing thread, tensor-pipe order):  S_0(0) S_1(0) | PV_0(0) S_0(1) PV_1(0) S_1(1) | PV_0(1) ...
+// S_g(j+1) is issued right after P_g(j) V_j, into the same TMEM columns: the tensor pipe runs them in order, so when
+// S_g(j+1) is complete the P V that read P_g(j) is complete too. The softmax of Q tile g therefore rescales O_g and
+// overwrites S_g with P_g without waiting for its own P V; while it works, the tensor core runs the other tile's
+// P V and next S (the two softmax warpgroups alternate, like the tensor core's two halves of work). Before a
+// tcgen05.st into TMEM the softmax waits for the other tile's P V that may still be reading its A operand from TMEM
+// (a tcgen05.st into TMEM lanes under an in-flight TS-MMA gave wrong products on B200); in the steady state that
+// P V finished long before the exponentials do.
 template <int HD>
 __global__ void __launch_bounds__(THREADS, 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -141,11 +134,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&bars->v_empty[i], 1);
     }
     for (int g = 0; g < NQ; ++g) {
-      for (int i = 0; i < 2; ++i) {
-        mbar_init(&bars->s_full[g][i], 1);
-        mbar_init(&bars->s_free[g][i], 1);
-        mbar_init(&bars->p_full[g][i], 128);
-      }
+      mbar_init(&bars->s_full[g], 1);
+      mbar_init(&bars->p_full[g], 128);
       mbar_init(&bars->pv_done[g], 1);
     }
     bars->abort_flag = 0;
@@ -165,7 +155,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0 && n_tiles > 0) {
-      // ---------------- TMA loads: both Q tiles, then K_{j+1} ahead of V_j ----------------
+      // ---------------- TMA loads: both Q tiles, then K_j and V_j into 2-stage rings ----------------
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
@@ -176,23 +166,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int blk = 0; blk < HD / 64; ++blk)
           tma_load_4d(smem + L::Q_OFF + g * L::Q_BYTES + blk * TQ * 128, &tmQ, &bars->q_full, blk * 64,
                       seq0 + q0 + g * TQ, h, tb);
-      auto load_k = [&](int j) -> bool {
+      bool ok = true;
+      for (int j = 0; j < n_tiles && ok && !*abort_flag; ++j) {
         const int st = j % KV_STAGES, ph = (j / KV_STAGES) & 1;
-        if (!mbar_wait(&bars->k_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) return false;
+        if (!mbar_wait(&bars->k_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
         mbar_expect_tx(&bars->k_full[st], L::KV_BYTES);
 #pragma unroll
         for (int blk = 0; blk < HD / 64; ++blk)
           tma_load_4d(smem + L::K_OFF + st * L::KV_BYTES + blk * TK * 128, &tmK, &bars->k_full[st], blk * 64,
                       seq0 + j * TK, hk, tb);
-        return true;
-      };
-      bool ok = load_k(0);
-      for (int j = 0; j < n_tiles && ok && !*abort_flag; ++j) {
-        if (j + 1 < n_tiles && !load_k(j + 1)) {
-          ok = false;
-          break;
-        }
-        const int st = j % KV_STAGES, ph = (j / KV_STAGES) & 1;
         if (!mbar_wait(&bars->v_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
@@ -208,50 +193,43 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && n_tiles > 0) {
-      // ---------------- MMA issue: S_0(j+1), S_1(j+1), then P_0 V_j, P_1 V_j ----------------
+      // ---------------- MMA issue ----------------
       constexpr uint32_t idesc_s = idesc_bf16_f32(TQ, TK, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(TQ, HD, false, true);
-      // precomputed descriptors (constant offsets are added per MMA)
       const uint64_t q_desc0 = sdesc_sw128(smem_u32(smem + L::Q_OFF), 16, 1024);
       const uint64_t k_desc0 = sdesc_sw128(smem_u32(smem + L::K_OFF), 16, 1024);
       const uint64_t v_desc0 = sdesc_sw128(smem_u32(smem + L::V_OFF), TK * 128, 1024);
-      auto issue_s = [&](int j) -> bool {  // S_g(j) = Q_g K_j^T for both Q tiles
-        const int ks = j % KV_STAGES, st = j & 1;
-        if (!mbar_wait(&bars->k_full[ks], (j / KV_STAGES) & 1, err, ERR_MBAR_TIMEOUT_MMA)) return false;
-        ATTN_TRACE(tr, 18, j);
+      auto issue_s = [&](int g, int j) {  // S_g(j) = Q_g K_j^T into TMEM columns g * 128
+        const int ks = j % KV_STAGES;
         const uint64_t kd = sdesc_add(k_desc0, ks * L::KV_BYTES);
 #pragma unroll
-        for (int g = 0; g < NQ; ++g) {
-          if (!mbar_wait(&bars->s_free[g][st], ((j >> 1) & 1) ^ 1, err, ERR_MBAR_TIMEOUT_MMA)) return false;
-          tc_fence_after();
-          const uint32_t d = tmem + g * 128 + st * TK;
-#pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t blk = kk >> 2, sub = (kk & 3) * 32;
-            umma_f16(d, sdesc_add(q_desc0, g * L::Q_BYTES + blk * TQ * 128 + sub),
-                     sdesc_add(kd, blk * TK * 128 + sub), idesc_s, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&bars->s_full[g][st]);
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t blk = kk >> 2, sub = (kk & 3) * 32;
+          umma_f16(tmem + g * 128, sdesc_add(q_desc0, g * L::Q_BYTES + blk * TQ * 128 + sub),
+                   sdesc_add(kd, blk * TK * 128 + sub), idesc_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bars->k_empty[ks]);
-        ATTN_TRACE(tr, 20, j);
-        return true;
+        umma_commit(&bars->s_full[g]);
+        if (g == NQ - 1) umma_commit(&bars->k_empty[ks]);  // K_j read by both Q tiles
       };
-      bool ok = mbar_wait(&bars->q_full, 0, err, ERR_MBAR_TIMEOUT_MMA) && issue_s(0);
+      bool ok = mbar_wait(&bars->q_full, 0, err, ERR_MBAR_TIMEOUT_MMA) &&
+                mbar_wait(&bars->k_full[0], 0, err, ERR_MBAR_TIMEOUT_MMA);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        ATTN_TRACE(tr, 20, 0);
+      }
       for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + 1 < n_tiles && !issue_s(j + 1)) {
+        const int vs = j % KV_STAGES, vph = (j / KV_STAGES) & 1;
+        const int kn = (j + 1) % KV_STAGES, knph = ((j + 1) / KV_STAGES) & 1;
+        if (!mbar_wait(&bars->v_full[vs], vph, err, ERR_MBAR_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
-        const int ks = j % KV_STAGES, st = j & 1;
-        if (!mbar_wait(&bars->v_full[ks], (j / KV_STAGES) & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
-          ok = false;
-          break;
-        }
-        const uint64_t vd = sdesc_add(v_desc0, ks * L::KV_BYTES);
+        const uint64_t vd = sdesc_add(v_desc0, vs * L::KV_BYTES);
 #pragma unroll
         for (int g = 0; g < NQ && ok; ++g) {
-          if (!mbar_wait(&bars->p_full[g][st], (j >> 1) & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
+          if (!mbar_wait(&bars->p_full[g], j & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
             ok = false;
             break;
           }
@@ -259,12 +237,20 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < TK / 16; ++kk)  // O_g += P_g V_j, P read from TMEM (8 columns per 16 keys)
-            umma_f16_tmem_a(tmem + O_COL + g * HD, tmem + g * 128 + st * TK + kk * 8, sdesc_add(vd, kk * 2048),
-                            idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&bars->s_free[g][st]);
+            umma_f16_tmem_a(tmem + O_COL + g * HD, tmem + g * 128 + kk * 8, sdesc_add(vd, kk * 2048), idesc_o,
+                            (j > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&bars->pv_done[g]);
+          if (g == NQ - 1) umma_commit(&bars->v_empty[vs]);  // V_j read by both Q tiles
+          if (j + 1 < n_tiles) {
+            if (g == 0 && !mbar_wait(&bars->k_full[kn], knph, err, ERR_MBAR_TIMEOUT_MMA)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(g, j + 1);  // same TMEM columns as P_g(j): in tensor-pipe order after the P V above
+          }
         }
-        if (ok) umma_commit(&bars->v_empty[ks]);
+        ATTN_TRACE(tr, 20, j + 1);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -277,63 +263,83 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t s_base = tmem + lane_base + g * 128, o_base = tmem + lane_base + O_COL + g * HD;
     const float sl2 = p.scale * 1.4426950408889634f;
     const bool tw = tr && (threadIdx.x == 64 + g * 128);
-    const int qpos = q0 + g * TQ + row;                        // query index within the sequence
+    const int qpos = q0 + g * TQ + row;                             // query index within the sequence
     const int key_lim = p.causal ? min(kv_end, qpos + 1) : kv_end;  // this row's keys: [0, key_lim)
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
+    auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
       int w_ok = 1;
-      if (lane == 0) w_ok = mbar_wait(&bars->s_full[g][st], (j >> 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
+      if (lane == 0) w_ok = mbar_wait(bar, parity, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
       w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
-      if (!w_ok) {
+      __syncwarp();
+      return w_ok != 0;
+    };
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!warp_wait(&bars->s_full[g], j & 1)) {
         ok = false;
         break;
       }
       ATTN_TRACE(tw, 23 + 4 * g, j);
-      __syncwarp();
       tc_fence_after();
-      uint32_t sr[2][32];
-      tmem_ld_32x32b_x32(s_base + st * TK, sr[0]);
-      tmem_ld_32x32b_x32(s_base + st * TK + 32, sr[1]);
-      tmem_ld_wait();
-      ATTN_TRACE(tw, 24 + 4 * g, j);
       // raw logits: the running max m is kept in log2 units (sl2 > 0, so max and scaling commute) and
       // p = 2^(s sl2 - m) is one FFMA + ex2 per element; keys past key_lim exist only in the last tile (and, when
-      // causal, in the tiles that cross the diagonal)
+      // causal, in the tiles that cross the diagonal). The four TMEM loads of the row are issued together (one
+      // wait: a tcgen05.ld round trip is long while the tensor core works on TMEM), and P is packed in place over
+      // the consumed S registers (element pair e of a chunk -> register e), which keeps the row in 128 registers.
       const int kbase = j * TK;
-      float smax = -INFINITY;
-      if (kbase + TK <= key_lim) {
+      const bool full_tile = kbase + TK <= key_lim;
+      uint32_t sr[4][32];
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(s_base + c * 32, sr[c]);
+      tmem_ld_wait();
+      ATTN_TRACE(tw, 24 + 4 * g, j);
+      if (!full_tile) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) smax = fmaxf(smax, __uint_as_float(sr[c][i]));
-      } else {
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
+          for (int i = 0; i < 32; ++i)
             if (kbase + c * 32 + i >= key_lim) sr[c][i] = __float_as_uint(-INFINITY);
-            smax = fmaxf(smax, __uint_as_float(sr[c][i]));
-          }
       }
-      smax *= sl2;
-      const float m_new = fmaxf(m, smax);
-      const bool need = (j > 0) && (m_new > m + kRescaleThreshold);
-      bool waited = false;
-      if (__any_sync(0xffffffffu, need)) {
-        // rescale this warp's O rows to the new running max; P V of the previous tile must have finished
-        if (lane == 0) w_ok = mbar_wait(&bars->pv_done[g], (j - 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
-        w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
-        if (!w_ok) {
-          ok = false;
-          break;
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          mx0 = fmaxf(mx0, __uint_as_float(sr[c][i]));
+          mx1 = fmaxf(mx1, __uint_as_float(sr[c][i + 1]));
         }
-        __syncwarp();
-        tc_fence_after();
-        waited = true;
+      const float smax = fmaxf(mx0, mx1) * sl2;
+      const float m_new = fmaxf(m, smax);
+      const bool rescale = (j > 0) && (m_new > m + kRescaleThreshold);
+      const float corr = rescale ? ((m == -INFINITY) ? 0.f : ex2(m - m_new)) : 1.f;
+      if (rescale || j == 0) m = m_new;
+      const float mu = (m == -INFINITY) ? 0.f : m;
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float a = ex2(fmaf(__uint_as_float(sr[c][2 * e]), sl2, -mu));
+          const float bq = ex2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, -mu));
+          rs0 += a;
+          rs1 += bq;
+          sr[c][e] = pack_bf16x2(a, bq);  // e <= 2e: the pair was read above
+        }
+      }
+      l = l * corr + (rs0 + rs1);
+      // the other Q tile's P V may still read its A operand from TMEM: let it finish before any tcgen05.st here
+      // (tile 0 at j waits for P_1(j-1) V, tile 1 for P_0(j) V; the later P V of that tile cannot start before
+      // this tile's P is written, so the barrier cannot be a phase ahead)
+      const int og = 1 - g;
+      const int oj = (g == 0) ? j - 1 : j;
+      if (oj >= 0 && oj < n_tiles && !warp_wait(&bars->pv_done[og], oj & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O_g is stable here: P_g(j-1) V completed before S_g(j) (tensor-pipe order), P_g(j) V is not issued yet
         ATTN_TRACE(tw, 25 + 4 * g, j);
-        const float corr = (m == -INFINITY) ? 0.f : ex2(m - m_new);
 #pragma unroll 1
         for (int c = 0; c < HD / 32; ++c) {
           uint32_t o[32];
@@ -343,56 +349,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
           tmem_st_32x32b_x32(o_base + c * 32, o);
         }
-        tmem_st_wait();
-        l *= corr;
-        m = m_new;
-      } else if (j == 0) {
-        m = m_new;
       }
-      const float mu = (m == -INFINITY) ? 0.f : m;
-      float rs0 = 0.f, rs1 = 0.f;
-      uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          // about a third of the exponentials on the FMA pipe, the rest on MUFU
-          const float xa = fmaf(__uint_as_float(sr[c][2 * e]), sl2, -mu);
-          const float xb = fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, -mu);
-          const float a = (e % 3 == 2) ? ex2_fma(xa) : ex2(xa);
-          const float bq = (e % 3 == 2) ? ex2_fma(xb) : ex2(xb);
-          rs0 += a;
-          rs1 += bq;
-          pk[c * 16 + e] = pack_bf16x2(a, bq);
-        }
-      }
-      const float rs = rs0 + rs1;
-      l += rs;
-      // No tcgen05.st while this tile's previous P V (an MMA reading its A operand from these TMEM lanes) is in
-      // flight: with that overlap the products came out wrong on B200, so wait for it here, after the exponentials.
-      if (j > 0 && !waited) {
-        if (lane == 0) w_ok = mbar_wait(&bars->pv_done[g], (j - 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
-        w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
-        if (!w_ok) {
-          ok = false;
-          break;
-        }
-        __syncwarp();
-        tc_fence_after();
-      }
-      tmem_st_32x32b_x32(s_base + st * TK, pk);  // P_j over the first 32 columns of S_j
+      for (int c = 0; c < 4; ++c)  // P_g(j): 128 keys as bf16 pairs, chunk c in columns c * 16 .. + 15
+        tmem_st_32x32b_x16(s_base + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&sr[c][0]));
       tmem_st_wait();
       tc_fence_before();
       ATTN_TRACE(tw, 26 + 4 * g, j);
-      mbar_arrive(&bars->p_full[g][st]);
+      mbar_arrive(&bars->p_full[g]);
     }
     // epilogue: O / l -> bf16, log-sum-exp
     if (ok && n_tiles > 0) {
-      int w_ok = 1;
-      if (lane == 0) w_ok = mbar_wait(&bars->pv_done[g], (n_tiles - 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
-      w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
-      ok = w_ok != 0;
-      __syncwarp();
+      ok = warp_wait(&bars->pv_done[g], (n_tiles - 1) & 1);
       tc_fence_after();
     }
     const int t = qpos;

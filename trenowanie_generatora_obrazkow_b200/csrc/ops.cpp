@@ -591,8 +591,8 @@ std::vector<at::Tensor> attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, 
   p.lse = lse.data_ptr<float>();
   if (g_attention_tc) {
     CUtensorMap tq = make_tmap_bhtd(p.q, p.hd, p.Tq, p.Hq, p.B, p.q_ts, p.q_hs, p.q_bs, 128);
-    CUtensorMap tk = make_tmap_bhtd(p.k, p.hd, p.Tk, p.Hkv, p.B, p.k_ts, p.k_hs, p.k_bs, 64);
-    CUtensorMap tv = make_tmap_bhtd(p.v, p.hd, p.Tk, p.Hkv, p.B, p.v_ts, p.v_hs, p.v_bs, 64);
+    CUtensorMap tk = make_tmap_bhtd(p.k, p.hd, p.Tk, p.Hkv, p.B, p.k_ts, p.k_hs, p.k_bs, 128);
+    CUtensorMap tv = make_tmap_bhtd(p.v, p.hd, p.Tk, p.Hkv, p.B, p.v_ts, p.v_hs, p.v_bs, 128);
     TGO_CHECK_LAUNCH(attention_fwd_tc_launch(tq, tk, tv, p, err_ptr(err), at::cuda::getCurrentCUDAStream()));
   } else {
     TGO_CHECK_LAUNCH(attention_fwd_launch(p, at::cuda::getCurrentCUDAStream()));
@@ -643,8 +643,8 @@ std::vector<at::Tensor> attention_varlen_fwd(at::Tensor q, at::Tensor k, at::Ten
   p.o_hs = o.stride(1);
   p.lse = lse.data_ptr<float>();
   CUtensorMap tq = make_tmap_bhtd(p.q, p.hd, p.total, p.Hq, 1, p.q_ts, p.q_hs, 0, 128);
-  CUtensorMap tk = make_tmap_bhtd(p.k, p.hd, p.total, p.Hkv, 1, p.k_ts, p.k_hs, 0, 64);
-  CUtensorMap tv = make_tmap_bhtd(p.v, p.hd, p.total, p.Hkv, 1, p.v_ts, p.v_hs, 0, 64);
+  CUtensorMap tk = make_tmap_bhtd(p.k, p.hd, p.total, p.Hkv, 1, p.k_ts, p.k_hs, 0, 128);
+  CUtensorMap tv = make_tmap_bhtd(p.v, p.hd, p.total, p.Hkv, 1, p.v_ts, p.v_hs, 0, 128);
   TGO_CHECK_LAUNCH(attention_fwd_tc_launch(tq, tk, tv, p, err_ptr(err), at::cuda::getCurrentCUDAStream()));
   return {o, lse};
 }
