@@ -34,7 +34,9 @@ constexpr int TQ = 128;      // query rows per Q tile (one softmax warpgroup)
 constexpr int NQ = 2;        // Q tiles per CTA
 constexpr int TK = 128;      // keys per K / V tile
 constexpr int KV_STAGES = 2; // K and V rings
-constexpr int THREADS = 320; // warp 0 TMA, warp 1 MMA, warps 2-5 softmax of Q tile 0, warps 6-9 of Q tile 1
+// warp 0 TMA, warp 1 MMA, then WPQ softmax warps per TMEM lane quarter for Q tile 0, then for Q tile 1
+template <int WPQ>
+constexpr int fwd_threads() { return 64 + NQ * 128 * WPQ; }
 constexpr int TMEM_COLS = 512;
 constexpr int O_COL = 256;   // Q tile g: S / P at g * 128 (P: bf16 pairs in the first 64 columns); O at 256 + g * hd
 constexpr float kRescaleThreshold = 8.f;  // log2 units
@@ -97,11 +99,18 @@ struct FwdBars {
 // tcgen05.st into TMEM the softmax waits for the other tile's P V that may still be reading its A operand from TMEM
 // (a tcgen05.st into TMEM lanes under an in-flight TS-MMA gave wrong products on B200); in the steady state that
 // P V finished long before the exponentials do.
-template <int HD>
-__global__ void __launch_bounds__(THREADS, 1)
+// WPQ = softmax warps per TMEM lane quarter and Q tile: with 2, the two warps of a quarter split the 128 key
+// columns (64 each) and exchange their row maxima through shared memory (a 64-thread named barrier per pair).
+template <int HD, int WPQ>
+__global__ void __launch_bounds__(fwd_threads<WPQ>(), 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, AttnParams p, int* err) {
   using L = FwdSmem<HD>;
+  constexpr int COLS = TK / WPQ;  // S columns of one softmax thread
+  constexpr int NCH = COLS / 32;
+  constexpr int OCOLS = HD / WPQ;  // O columns of one softmax thread (rescale, epilogue)
+  __shared__ float xch_max[2][NQ][TQ][WPQ];
+  __shared__ float xch_l[NQ][TQ][WPQ];
   static_assert(sizeof(FwdBars) <= 512, "barrier block");
   extern __shared__ __align__(1024) uint8_t smem[];
   FwdBars* bars = reinterpret_cast<FwdBars*>(smem + L::BAR_OFF);
@@ -135,7 +144,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int g = 0; g < NQ; ++g) {
       mbar_init(&bars->s_full[g], 1);
-      mbar_init(&bars->p_full[g], 128);
+      mbar_init(&bars->p_full[g], 128 * WPQ);
       mbar_init(&bars->pv_done[g], 1);
     }
     bars->abort_flag = 0;
@@ -256,16 +265,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ---------------- softmax / epilogue of Q tile g ----------------
-    const int g = (warp - 2) >> 2;
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // TMEM lane == query row within the tile
+    const int sw = warp - 2;
+    const int g = sw / (4 * WPQ);
+    const int half = (sw % (4 * WPQ)) / 4;  // which share of the key / O columns (0 when WPQ == 1)
+    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;    // TMEM lane == query row within the tile
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const uint32_t s_base = tmem + lane_base + g * 128, o_base = tmem + lane_base + O_COL + g * HD;
+    const uint32_t s_base = tmem + lane_base + g * 128 + half * COLS;
+    const uint32_t p_base = tmem + lane_base + g * 128 + half * (COLS / 2);
+    const uint32_t o_base = tmem + lane_base + O_COL + g * HD + half * OCOLS;
     const float sl2 = p.scale * 1.4426950408889634f;
-    const bool tw = tr && (threadIdx.x == 64 + g * 128);
+    const bool tw = tr && (threadIdx.x == 64 + g * 128 * WPQ);
     const int qpos = q0 + g * TQ + row;                             // query index within the sequence
     const int key_lim = p.causal ? min(kv_end, qpos + 1) : kv_end;  // this row's keys: [0, key_lim)
-    float m = -INFINITY, l = 0.f;
+    const int pair_bar = 1 + g * 4 + quarter;                       // named barrier of the WPQ warps of a quarter
+    float m = -INFINITY, l = 0.f;  // l: this thread's share of the row sum
     bool ok = true;
     auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
       int w_ok = 1;
@@ -274,74 +288,88 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       return w_ok != 0;
     };
+    auto pair_sync = [&]() {
+      if constexpr (WPQ > 1) asm volatile("bar.sync %0, %1;" ::"r"(pair_bar), "r"(32 * WPQ) : "memory");
+    };
+    // A failed (timed-out) wait does not leave the loop: both warps of a pair must reach every pair barrier, so a
+    // failed warp skips the work of the remaining tiles and keeps synchronising.
     for (int j = 0; j < n_tiles; ++j) {
-      if (!warp_wait(&bars->s_full[g], j & 1)) {
-        ok = false;
-        break;
-      }
+      if (ok && !warp_wait(&bars->s_full[g], j & 1)) ok = false;
       ATTN_TRACE(tw, 23 + 4 * g, j);
       tc_fence_after();
       // raw logits: the running max m is kept in log2 units (sl2 > 0, so max and scaling commute) and
       // p = 2^(s sl2 - m) is one FFMA + ex2 per element; keys past key_lim exist only in the last tile (and, when
-      // causal, in the tiles that cross the diagonal). The four TMEM loads of the row are issued together (one
+      // causal, in the tiles that cross the diagonal). The TMEM loads of the row share are issued together (one
       // wait: a tcgen05.ld round trip is long while the tensor core works on TMEM), and P is packed in place over
-      // the consumed S registers (element pair e of a chunk -> register e), which keeps the row in 128 registers.
-      const int kbase = j * TK;
-      const bool full_tile = kbase + TK <= key_lim;
-      uint32_t sr[4][32];
+      // the consumed S registers (element pair e of a chunk -> register e).
+      const int kbase = j * TK + half * COLS;
+      const bool full_tile = kbase + COLS <= key_lim;
+      uint32_t sr[NCH][32];
+      if (ok) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(s_base + c * 32, sr[c]);
-      tmem_ld_wait();
+        for (int c = 0; c < NCH; ++c) tmem_ld_32x32b_x32(s_base + c * 32, sr[c]);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sr[c][i] = 0u;
+      }
       ATTN_TRACE(tw, 24 + 4 * g, j);
       if (!full_tile) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < NCH; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             if (kbase + c * 32 + i >= key_lim) sr[c][i] = __float_as_uint(-INFINITY);
       }
-      float mx0 = -INFINITY, mx1 = -INFINITY;
+      // short dependency chains: 8 partial maxima, then a tree
+      float mx[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          mx0 = fmaxf(mx0, __uint_as_float(sr[c][i]));
-          mx1 = fmaxf(mx1, __uint_as_float(sr[c][i + 1]));
-        }
-      const float smax = fmaxf(mx0, mx1) * sl2;
+      for (int c = 0; c < NCH; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sr[c][i]));
+      float rmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      if constexpr (WPQ > 1) {  // row max over the shares (double-buffered slots: a slot is rewritten two tiles on)
+        xch_max[j & 1][g][row][half] = rmax;
+        pair_sync();
+#pragma unroll
+        for (int k = 0; k < WPQ; ++k) rmax = fmaxf(rmax, xch_max[j & 1][g][row][k]);
+      }
+      const float smax = rmax * sl2;
       const float m_new = fmaxf(m, smax);
       const bool rescale = (j > 0) && (m_new > m + kRescaleThreshold);
       const float corr = rescale ? ((m == -INFINITY) ? 0.f : ex2(m - m_new)) : 1.f;
       if (rescale || j == 0) m = m_new;
       const float mu = (m == -INFINITY) ? 0.f : m;
-      float rs0 = 0.f, rs1 = 0.f;
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};  // 4 partial sums: short FADD chains
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < NCH; ++c) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const float a = ex2(fmaf(__uint_as_float(sr[c][2 * e]), sl2, -mu));
           const float bq = ex2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, -mu));
-          rs0 += a;
-          rs1 += bq;
+          rs[(e & 1) * 2] += a;
+          rs[(e & 1) * 2 + 1] += bq;
           sr[c][e] = pack_bf16x2(a, bq);  // e <= 2e: the pair was read above
         }
       }
-      l = l * corr + (rs0 + rs1);
+      l = l * corr + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+      ATTN_TRACE(tw, 25 + 4 * g, j);
       // the other Q tile's P V may still read its A operand from TMEM: let it finish before any tcgen05.st here
       // (tile 0 at j waits for P_1(j-1) V, tile 1 for P_0(j) V; the later P V of that tile cannot start before
       // this tile's P is written, so the barrier cannot be a phase ahead)
       const int og = 1 - g;
       const int oj = (g == 0) ? j - 1 : j;
-      if (oj >= 0 && oj < n_tiles && !warp_wait(&bars->pv_done[og], oj & 1)) {
-        ok = false;
-        break;
-      }
+      if (ok && oj >= 0 && oj < n_tiles && !warp_wait(&bars->pv_done[og], oj & 1)) ok = false;
+      if (!ok) continue;  // nothing to store; the pair barrier of the next tile is still reached
       tc_fence_after();
       if (__any_sync(0xffffffffu, rescale)) {
         // O_g is stable here: P_g(j-1) V completed before S_g(j) (tensor-pipe order), P_g(j) V is not issued yet
-        ATTN_TRACE(tw, 25 + 4 * g, j);
 #pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
+        for (int c = 0; c < OCOLS / 32; ++c) {
           uint32_t o[32];
           tmem_ld_32x32b_x32(o_base + c * 32, o);
           tmem_ld_wait();
@@ -351,8 +379,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
 #pragma unroll
-      for (int c = 0; c < 4; ++c)  // P_g(j): 128 keys as bf16 pairs, chunk c in columns c * 16 .. + 15
-        tmem_st_32x32b_x16(s_base + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&sr[c][0]));
+      for (int c = 0; c < NCH; ++c)  // P_g(j): this share's keys as bf16 pairs, chunk c in columns c * 16 .. + 15
+        tmem_st_32x32b_x16(p_base + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&sr[c][0]));
       tmem_st_wait();
       tc_fence_before();
       ATTN_TRACE(tw, 26 + 4 * g, j);
@@ -363,12 +391,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       ok = warp_wait(&bars->pv_done[g], (n_tiles - 1) & 1);
       tc_fence_after();
     }
+    if constexpr (WPQ > 1) {  // the row sum over the shares (every thread of the pair reaches this point)
+      xch_l[g][row][half] = l;
+      pair_sync();
+      float lt = 0.f;
+#pragma unroll
+      for (int k = 0; k < WPQ; ++k) lt += xch_l[g][row][k];
+      l = lt;
+    }
     const int t = qpos;
     const float inv = (l > 0.f) ? 1.f / l : 0.f;
     if (ok) {
-      __nv_bfloat16* dst = p.o + (long long)tb * p.o_bs + (long long)(seq0 + t) * p.o_ts + (long long)h * p.o_hs;
+      __nv_bfloat16* dst = p.o + (long long)tb * p.o_bs + (long long)(seq0 + t) * p.o_ts + (long long)h * p.o_hs +
+                           half * OCOLS;
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < OCOLS / 32; ++c) {
         uint32_t o[32];
         if (n_tiles > 0) {
           tmem_ld_32x32b_x32(o_base + c * 32, o);
@@ -389,7 +426,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
-      if (t < q_len && p.lse != nullptr) {
+      if (half == 0 && t < q_len && p.lse != nullptr) {
         const long long li = p.cu_seqlens != nullptr ? (long long)h * p.total + seq0 + t
                                                      : ((long long)b * p.Hq + h) * p.Tq + t;
         p.lse[li] = (l > 0.f) ? (m + log2f(l)) * 0.6931471805599453f : INFINITY;
@@ -406,24 +443,33 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-template <int HD>
+template <int HD, int WPQ>
 static cudaError_t fwd_tc_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                const AttnParams& p, int* err, cudaStream_t s) {
   using L = FwdSmem<HD>;
   static bool set = false;
   if (!set) {
-    cudaFuncSetAttribute(flash_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+    cudaFuncSetAttribute(flash_fwd_tc_kernel<HD, WPQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
     set = true;
   }
   dim3 grid((p.Tq + NQ * TQ - 1) / (NQ * TQ), p.Hq, p.B);
-  flash_fwd_tc_kernel<HD><<<grid, THREADS, L::TOTAL, s>>>(tq, tk, tv, p, err);
+  flash_fwd_tc_kernel<HD, WPQ><<<grid, fwd_threads<WPQ>(), L::TOTAL, s>>>(tq, tk, tv, p, err);
   return cudaGetLastError();
+}
+
+static int g_fwd_wpq = 1;
+cudaError_t attention_set_fwd_split(int wpq) {
+  if (wpq != 1 && wpq != 2) return cudaErrorInvalidValue;
+  g_fwd_wpq = wpq;
+  return cudaSuccess;
 }
 
 cudaError_t attention_fwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                     const AttnParams& p, int* err, cudaStream_t s) {
-  if (p.hd == 128) return fwd_tc_impl<128>(tq, tk, tv, p, err, s);
-  if (p.hd == 64) return fwd_tc_impl<64>(tq, tk, tv, p, err, s);
+  if (p.hd == 128) return g_fwd_wpq == 2 ? fwd_tc_impl<128, 2>(tq, tk, tv, p, err, s)
+                                         : fwd_tc_impl<128, 1>(tq, tk, tv, p, err, s);
+  if (p.hd == 64) return g_fwd_wpq == 2 ? fwd_tc_impl<64, 2>(tq, tk, tv, p, err, s)
+                                        : fwd_tc_impl<64, 1>(tq, tk, tv, p, err, s);
   return cudaErrorInvalidValue;
 }
 
