@@ -174,3 +174,16 @@ def test_slayer_packed_states_gpu():
     for r, n in enumerate(lens):
         d = (a[r, :n].float() - b[r, :n].float()).abs().max().item()
         assert d < 0.1 * a[r, :n].float().abs().max().item(), (r, d)
+
+
+@pytest.mark.parametrize("M,D,H", [(300, 512, 384), (4096, 2048, 5504)])
+def test_up_swiglu_fused_matches_separate_ops(M, D, H):
+    """Up projection + SwiGLU in one GEMM epilogue (inference) against the GEMM followed by the SwiGLU kernel."""
+    torch.manual_seed(0)
+    layer = torch.nn.Linear(D, 2 * H, bias=False).cuda()
+    x = torch.randn(M, D, device="cuda").bfloat16()
+    with torch.no_grad():
+        fused = Fz.up_swiglu(x, layer)
+        ref = Fz.swiglu(Fz.linear(x, layer))
+    err = ((fused.float() - ref.float()).norm() / ref.float().norm()).item()
+    assert fused.shape == (M, H) and err < 1e-2, err

@@ -34,9 +34,7 @@ constexpr int TQ = 128;      // query rows per Q tile (one softmax warpgroup)
 constexpr int NQ = 2;        // Q tiles per CTA
 constexpr int TK = 128;      // keys per K / V tile
 constexpr int KV_STAGES = 2; // K and V rings
-// warp 0 TMA, warp 1 MMA, then WPQ softmax warps per TMEM lane quarter for Q tile 0, then for Q tile 1
-template <int WPQ>
-constexpr int fwd_threads() { return 64 + NQ * 128 * WPQ; }
+constexpr int THREADS = 320; // warp 0 TMA, warp 1 MMA, warps 2-5 softmax of Q tile 0, warps 6-9 of Q tile 1
 constexpr int TMEM_COLS = 512;
 constexpr int O_COL = 256;   // Q tile g: S / P at g * 128 (P: bf16 pairs in the first 64 columns); O at 256 + g * hd
 constexpr float kRescaleThreshold = 8.f;  // log2 units
@@ -79,38 +77,63 @@ struct FwdSmem {
 };
 
 struct FwdBars {
-  uint64_t q_full;
+  uint64_t q_full, q_empty;                        // Q tiles of the current item loaded / read by its last S
   uint64_t k_full[KV_STAGES], k_empty[KV_STAGES];  // K tile free once S of both Q tiles is computed
   uint64_t v_full[KV_STAGES], v_empty[KV_STAGES];  // V tile free once P V of both Q tiles is computed
   uint64_t s_full[NQ];                             // S_g(j) in TMEM (and, by issue order, P_g(j-1) V done)
   uint64_t p_full[NQ];                             // softmax wrote P_g(j) over S_g(j): 128 arrivals
   uint64_t pv_done[NQ];                            // one phase per P_g(j) V_j
+  uint64_t o_free[NQ];                             // the epilogue read O_g of the item: 128 arrivals
   uint32_t tmem_base;
   int abort_flag;
 };
 
+// One work item: two 128-row query tiles of one (batch, head); its key range and KV tile count.
+struct FwdItem {
+  int h, b, hk, q0, seq0, tb, q_len, kv_end, n_tiles;
+};
+__device__ __forceinline__ FwdItem fwd_item(const AttnParams& p, int item, int n_qb) {
+  FwdItem w;
+  const int qb = item % n_qb, r = item / n_qb;
+  w.h = r % p.Hq;
+  w.b = r / p.Hq;
+  w.hk = w.h / p.rep;
+  w.q0 = qb * (NQ * TQ);
+  // varlen: sequence b occupies tokens [seq0, seq0 + len) of the packed axis (batch coordinate 0 of the maps)
+  w.seq0 = 0;
+  w.tb = w.b;
+  w.q_len = p.Tq;
+  w.kv_end = p.Tk;
+  if (p.cu_seqlens != nullptr) {
+    w.seq0 = p.cu_seqlens[w.b];
+    w.q_len = w.kv_end = p.cu_seqlens[w.b + 1] - w.seq0;
+    w.tb = 0;
+  }
+  if (p.kv_len != nullptr) w.kv_end = min(w.kv_end, p.kv_len[w.b]);
+  if (p.causal) w.kv_end = min(w.kv_end, w.q0 + NQ * TQ);  // no key after the item's last query row
+  if (w.q0 >= w.q_len) w.kv_end = 0;
+  w.n_tiles = max(0, (w.kv_end + TK - 1) / TK);
+  return w;
+}
+
 }  // namespace
 
+// Persistent: one CTA per SM walks the work items (query block fastest, so neighbouring CTAs share K / V in L2).
+// Barrier phases run on across items (a global KV-tile counter), so the TMA loads, MMAs and softmax of the next
+// item start while the softmax warps still write the previous item's output: short-key items (cross-attention
+// against 128 text tokens) are no longer one prologue and one epilogue per CTA.
 // Schedule (one MMA-issuing thread, tensor-pipe order):  S_0(0) S_1(0) | PV_0(0) S_0(1) PV_1(0) S_1(1) | PV_0(1) ...
 // S_g(j+1) is issued right after P_g(j) V_j, into the same TMEM columns: the tensor pipe runs them in order, so when
 // S_g(j+1) is complete the P V that read P_g(j) is complete too. The softmax of Q tile g therefore rescales O_g and
 // overwrites S_g with P_g without waiting for its own P V; while it works, the tensor core runs the other tile's
-// P V and next S (the two softmax warpgroups alternate, like the tensor core's two halves of work). Before a
-// tcgen05.st into TMEM the softmax waits for the other tile's P V that may still be reading its A operand from TMEM
-// (a tcgen05.st into TMEM lanes under an in-flight TS-MMA gave wrong products on B200); in the steady state that
-// P V finished long before the exponentials do.
-// WPQ = softmax warps per TMEM lane quarter and Q tile: with 2, the two warps of a quarter split the 128 key
-// columns (64 each) and exchange their row maxima through shared memory (a 64-thread named barrier per pair).
-template <int HD, int WPQ>
-__global__ void __launch_bounds__(fwd_threads<WPQ>(), 1)
+// P V and next S. Before a tcgen05.st into TMEM the softmax waits for the other tile's P V that may still be
+// reading its A operand from TMEM (a tcgen05.st into TMEM lanes under an in-flight TS-MMA gave wrong products on
+// B200); in the steady state that P V finished long before the exponentials do.
+template <int HD>
+__global__ void __launch_bounds__(THREADS, 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, AttnParams p, int* err) {
   using L = FwdSmem<HD>;
-  constexpr int COLS = TK / WPQ;  // S columns of one softmax thread
-  constexpr int NCH = COLS / 32;
-  constexpr int OCOLS = HD / WPQ;  // O columns of one softmax thread (rescale, epilogue)
-  __shared__ float xch_max[2][NQ][TQ][WPQ];
-  __shared__ float xch_l[NQ][TQ][WPQ];
   static_assert(sizeof(FwdBars) <= 512, "barrier block");
   extern __shared__ __align__(1024) uint8_t smem[];
   FwdBars* bars = reinterpret_cast<FwdBars*>(smem + L::BAR_OFF);
@@ -119,23 +142,12 @@ __global__ void __launch_bounds__(fwd_threads<WPQ>(), 1)
     if (threadIdx.x == 0) record_error(err, ERR_BAD_ARGS);
     return;
   }
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int hk = h / p.rep;
-  const int q0 = qb * (NQ * TQ);
-  // varlen: sequence b occupies tokens [seq0, seq0 + len) of the packed axis (batch coordinate 0 of the maps)
-  int seq0 = 0, tb = b, q_len = p.Tq, kv_end = p.Tk;
-  if (p.cu_seqlens != nullptr) {
-    seq0 = p.cu_seqlens[b];
-    q_len = kv_end = p.cu_seqlens[b + 1] - seq0;
-    tb = 0;
-  }
-  if (p.kv_len != nullptr) kv_end = min(kv_end, p.kv_len[b]);
-  if (p.causal) kv_end = min(kv_end, q0 + NQ * TQ);  // no key after the CTA's last query row
-  if (q0 >= q_len) kv_end = 0;
-  const int n_tiles = max(0, (kv_end + TK - 1) / TK);
+  const int n_qb = (p.Tq + NQ * TQ - 1) / (NQ * TQ);
+  const int n_items = n_qb * p.Hq * p.B;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_empty, 1);
     for (int i = 0; i < KV_STAGES; ++i) {
       mbar_init(&bars->k_full[i], 1);
       mbar_init(&bars->k_empty[i], 1);
@@ -144,8 +156,9 @@ __global__ void __launch_bounds__(fwd_threads<WPQ>(), 1)
     }
     for (int g = 0; g < NQ; ++g) {
       mbar_init(&bars->s_full[g], 1);
-      mbar_init(&bars->p_full[g], 128 * WPQ);
+      mbar_init(&bars->p_full[g], 128);
       mbar_init(&bars->pv_done[g], 1);
+      mbar_init(&bars->o_free[g], 128);
     }
     bars->abort_flag = 0;
     fence_barrier_init();
@@ -163,53 +176,63 @@ __global__ void __launch_bounds__(fwd_threads<WPQ>(), 1)
   const bool tr = trace_buf != nullptr;
 
   if (warp == 0) {
-    if (lane == 0 && n_tiles > 0) {
-      // ---------------- TMA loads: both Q tiles, then K_j and V_j into 2-stage rings ----------------
+    if (lane == 0) {
+      // ---------------- TMA loads: per item both Q tiles, then K_j and V_j into 2-stage rings ----------------
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      mbar_expect_tx(&bars->q_full, NQ * L::Q_BYTES);
-#pragma unroll
-      for (int g = 0; g < NQ; ++g)
-#pragma unroll
-        for (int blk = 0; blk < HD / 64; ++blk)
-          tma_load_4d(smem + L::Q_OFF + g * L::Q_BYTES + blk * TQ * 128, &tmQ, &bars->q_full, blk * 64,
-                      seq0 + q0 + g * TQ, h, tb);
       bool ok = true;
-      for (int j = 0; j < n_tiles && ok && !*abort_flag; ++j) {
-        const int st = j % KV_STAGES, ph = (j / KV_STAGES) & 1;
-        if (!mbar_wait(&bars->k_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+      int items = 0, gt = 0;  // non-empty items loaded, global KV tile counter
+      for (int item = blockIdx.x; item < n_items && ok && !*abort_flag; item += gridDim.x) {
+        const FwdItem w = fwd_item(p, item, n_qb);
+        if (w.n_tiles == 0) continue;
+        if (items > 0 && !mbar_wait(&bars->q_empty, (items - 1) & 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
         }
-        mbar_expect_tx(&bars->k_full[st], L::KV_BYTES);
+        mbar_expect_tx(&bars->q_full, NQ * L::Q_BYTES);
 #pragma unroll
-        for (int blk = 0; blk < HD / 64; ++blk)
-          tma_load_4d(smem + L::K_OFF + st * L::KV_BYTES + blk * TK * 128, &tmK, &bars->k_full[st], blk * 64,
-                      seq0 + j * TK, hk, tb);
-        if (!mbar_wait(&bars->v_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
-          ok = false;
-          break;
+        for (int g = 0; g < NQ; ++g)
+#pragma unroll
+          for (int blk = 0; blk < HD / 64; ++blk)
+            tma_load_4d(smem + L::Q_OFF + g * L::Q_BYTES + blk * TQ * 128, &tmQ, &bars->q_full, blk * 64,
+                        w.seq0 + w.q0 + g * TQ, w.h, w.tb);
+        for (int j = 0; j < w.n_tiles && ok; ++j, ++gt) {
+          const int st = gt % KV_STAGES, ph = (gt / KV_STAGES) & 1;
+          if (!mbar_wait(&bars->k_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bars->k_full[st], L::KV_BYTES);
+#pragma unroll
+          for (int blk = 0; blk < HD / 64; ++blk)
+            tma_load_4d(smem + L::K_OFF + st * L::KV_BYTES + blk * TK * 128, &tmK, &bars->k_full[st], blk * 64,
+                        w.seq0 + j * TK, w.hk, w.tb);
+          if (!mbar_wait(&bars->v_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          ATTN_TRACE(tr, 16, gt);
+          mbar_expect_tx(&bars->v_full[st], L::KV_BYTES);
+#pragma unroll
+          for (int blk = 0; blk < HD / 64; ++blk)
+            tma_load_4d(smem + L::V_OFF + st * L::KV_BYTES + blk * TK * 128, &tmV, &bars->v_full[st], blk * 64,
+                        w.seq0 + j * TK, w.hk, w.tb);
         }
-        ATTN_TRACE(tr, 16, j);
-        mbar_expect_tx(&bars->v_full[st], L::KV_BYTES);
-#pragma unroll
-        for (int blk = 0; blk < HD / 64; ++blk)
-          tma_load_4d(smem + L::V_OFF + st * L::KV_BYTES + blk * TK * 128, &tmV, &bars->v_full[st], blk * 64,
-                      seq0 + j * TK, hk, tb);
+        ++items;
       }
       if (!ok) *abort_flag = 1;
     }
   } else if (warp == 1) {
-    if (lane == 0 && n_tiles > 0) {
+    if (lane == 0) {
       // ---------------- MMA issue ----------------
       constexpr uint32_t idesc_s = idesc_bf16_f32(TQ, TK, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(TQ, HD, false, true);
       const uint64_t q_desc0 = sdesc_sw128(smem_u32(smem + L::Q_OFF), 16, 1024);
       const uint64_t k_desc0 = sdesc_sw128(smem_u32(smem + L::K_OFF), 16, 1024);
       const uint64_t v_desc0 = sdesc_sw128(smem_u32(smem + L::V_OFF), TK * 128, 1024);
-      auto issue_s = [&](int g, int j) {  // S_g(j) = Q_g K_j^T into TMEM columns g * 128
-        const int ks = j % KV_STAGES;
+      auto issue_s = [&](int g, int gtile, bool last_s) {  // S_g = Q_g K^T into TMEM columns g * 128
+        const int ks = gtile % KV_STAGES;
         const uint64_t kd = sdesc_add(k_desc0, ks * L::KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
@@ -218,68 +241,78 @@ __global__ void __launch_bounds__(fwd_threads<WPQ>(), 1)
                    sdesc_add(kd, blk * TK * 128 + sub), idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->s_full[g]);
-        if (g == NQ - 1) umma_commit(&bars->k_empty[ks]);  // K_j read by both Q tiles
-      };
-      bool ok = mbar_wait(&bars->q_full, 0, err, ERR_MBAR_TIMEOUT_MMA) &&
-                mbar_wait(&bars->k_full[0], 0, err, ERR_MBAR_TIMEOUT_MMA);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
-        ATTN_TRACE(tr, 20, 0);
-      }
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int vs = j % KV_STAGES, vph = (j / KV_STAGES) & 1;
-        const int kn = (j + 1) % KV_STAGES, knph = ((j + 1) / KV_STAGES) & 1;
-        if (!mbar_wait(&bars->v_full[vs], vph, err, ERR_MBAR_TIMEOUT_MMA)) {
-          ok = false;
-          break;
+        if (g == NQ - 1) {
+          umma_commit(&bars->k_empty[ks]);        // K read by both Q tiles
+          if (last_s) umma_commit(&bars->q_empty);  // the item's Q tiles are read for the last time
         }
-        const uint64_t vd = sdesc_add(v_desc0, vs * L::KV_BYTES);
-#pragma unroll
-        for (int g = 0; g < NQ && ok; ++g) {
-          if (!mbar_wait(&bars->p_full[g], j & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
+      };
+      bool ok = true;
+      int items = 0, gt = 0;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const FwdItem w = fwd_item(p, item, n_qb);
+        const int n = w.n_tiles;
+        if (n == 0) continue;
+        ok = mbar_wait(&bars->q_full, items & 1, err, ERR_MBAR_TIMEOUT_MMA) &&
+             mbar_wait(&bars->k_full[gt % KV_STAGES], (gt / KV_STAGES) & 1, err, ERR_MBAR_TIMEOUT_MMA);
+        if (!ok) break;
+        tc_fence_after();
+        issue_s(0, gt, false);  // after the previous item's last P_0 V in tensor-pipe order (same TMEM columns)
+        issue_s(1, gt, n == 1);
+        ATTN_TRACE(tr, 20, gt);
+        for (int j = 0; j < n && ok; ++j) {
+          const int gj = gt + j;
+          const int vs = gj % KV_STAGES, vph = (gj / KV_STAGES) & 1;
+          const int kn = (gj + 1) % KV_STAGES, knph = ((gj + 1) / KV_STAGES) & 1;
+          if (!mbar_wait(&bars->v_full[vs], vph, err, ERR_MBAR_TIMEOUT_MMA)) {
             ok = false;
             break;
           }
-          ATTN_TRACE(tr, 21 + g, j);
-          tc_fence_after();
+          const uint64_t vd = sdesc_add(v_desc0, vs * L::KV_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < TK / 16; ++kk)  // O_g += P_g V_j, P read from TMEM (8 columns per 16 keys)
-            umma_f16_tmem_a(tmem + O_COL + g * HD, tmem + g * 128 + kk * 8, sdesc_add(vd, kk * 2048), idesc_o,
-                            (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&bars->pv_done[g]);
-          if (g == NQ - 1) umma_commit(&bars->v_empty[vs]);  // V_j read by both Q tiles
-          if (j + 1 < n_tiles) {
-            if (g == 0 && !mbar_wait(&bars->k_full[kn], knph, err, ERR_MBAR_TIMEOUT_MMA)) {
+          for (int g = 0; g < NQ && ok; ++g) {
+            if (!mbar_wait(&bars->p_full[g], gj & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
               ok = false;
               break;
             }
+            // the first P V of an item overwrites O_g: the previous item's epilogue must have read it
+            if (j == 0 && items > 0 && !mbar_wait(&bars->o_free[g], (items - 1) & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
+              ok = false;
+              break;
+            }
+            ATTN_TRACE(tr, 21 + g, gj);
             tc_fence_after();
-            issue_s(g, j + 1);  // same TMEM columns as P_g(j): in tensor-pipe order after the P V above
+#pragma unroll
+            for (int kk = 0; kk < TK / 16; ++kk)  // O_g += P_g V_j, P read from TMEM (8 columns per 16 keys)
+              umma_f16_tmem_a(tmem + O_COL + g * HD, tmem + g * 128 + kk * 8, sdesc_add(vd, kk * 2048), idesc_o,
+                              (j > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&bars->pv_done[g]);
+            if (g == NQ - 1) umma_commit(&bars->v_empty[vs]);  // V_j read by both Q tiles
+            if (j + 1 < n) {
+              if (g == 0 && !mbar_wait(&bars->k_full[kn], knph, err, ERR_MBAR_TIMEOUT_MMA)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_s(g, gj + 1, j + 2 == n);  // same TMEM columns as P_g(j): after the P V above in pipe order
+            }
           }
+          ATTN_TRACE(tr, 20, gj + 1);
         }
-        ATTN_TRACE(tr, 20, j + 1);
+        gt += n;
+        ++items;
       }
       if (!ok) *abort_flag = 1;
     }
   } else {
     // ---------------- softmax / epilogue of Q tile g ----------------
-    const int sw = warp - 2;
-    const int g = sw / (4 * WPQ);
-    const int half = (sw % (4 * WPQ)) / 4;  // which share of the key / O columns (0 when WPQ == 1)
-    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
-    const int row = quarter * 32 + lane;    // TMEM lane == query row within the tile
+    const int g = (warp - 2) >> 2;
+    const int quarter = warp & 3;         // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;  // TMEM lane == query row within the tile
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const uint32_t s_base = tmem + lane_base + g * 128 + half * COLS;
-    const uint32_t p_base = tmem + lane_base + g * 128 + half * (COLS / 2);
-    const uint32_t o_base = tmem + lane_base + O_COL + g * HD + half * OCOLS;
+    const uint32_t s_base = tmem + lane_base + g * 128;
+    const uint32_t o_base = tmem + lane_base + O_COL + g * HD;
     const float sl2 = p.scale * 1.4426950408889634f;
-    const bool tw = tr && (threadIdx.x == 64 + g * 128 * WPQ);
-    const int qpos = q0 + g * TQ + row;                             // query index within the sequence
-    const int key_lim = p.causal ? min(kv_end, qpos + 1) : kv_end;  // this row's keys: [0, key_lim)
-    const int pair_bar = 1 + g * 4 + quarter;                       // named barrier of the WPQ warps of a quarter
-    float m = -INFINITY, l = 0.f;  // l: this thread's share of the row sum
+    const bool tw = tr && (threadIdx.x == 64 + g * 128);
     bool ok = true;
     auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
       int w_ok = 1;
@@ -288,133 +321,133 @@ __global__ void __launch_bounds__(fwd_threads<WPQ>(), 1)
       __syncwarp();
       return w_ok != 0;
     };
-    auto pair_sync = [&]() {
-      if constexpr (WPQ > 1) asm volatile("bar.sync %0, %1;" ::"r"(pair_bar), "r"(32 * WPQ) : "memory");
+    // output row of this thread for an item (recomputed where needed: fewer live registers in the tile loop)
+    auto out_row = [&](const FwdItem& w, int qpos) {
+      return p.o + (long long)w.tb * p.o_bs + (long long)(w.seq0 + qpos) * p.o_ts + (long long)w.h * p.o_hs;
     };
-    // A failed (timed-out) wait does not leave the loop: both warps of a pair must reach every pair barrier, so a
-    // failed warp skips the work of the remaining tiles and keeps synchronising.
-    for (int j = 0; j < n_tiles; ++j) {
-      if (ok && !warp_wait(&bars->s_full[g], j & 1)) ok = false;
-      ATTN_TRACE(tw, 23 + 4 * g, j);
-      tc_fence_after();
-      // raw logits: the running max m is kept in log2 units (sl2 > 0, so max and scaling commute) and
-      // p = 2^(s sl2 - m) is one FFMA + ex2 per element; keys past key_lim exist only in the last tile (and, when
-      // causal, in the tiles that cross the diagonal). The TMEM loads of the row share are issued together (one
-      // wait: a tcgen05.ld round trip is long while the tensor core works on TMEM), and P is packed in place over
-      // the consumed S registers (element pair e of a chunk -> register e).
-      const int kbase = j * TK + half * COLS;
-      const bool full_tile = kbase + COLS <= key_lim;
-      uint32_t sr[NCH][32];
-      if (ok) {
+    auto lse_index = [&](const FwdItem& w, int qpos) {
+      return p.cu_seqlens != nullptr ? (long long)w.h * p.total + w.seq0 + qpos
+                                     : ((long long)w.b * p.Hq + w.h) * p.Tq + qpos;
+    };
+    int gt = 0;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      int n, key_lim;
+      {
+        const FwdItem w = fwd_item(p, item, n_qb);
+        n = w.n_tiles;
+        const int qpos = w.q0 + g * TQ + row;                       // query index within the sequence
+        key_lim = p.causal ? min(w.kv_end, qpos + 1) : w.kv_end;    // this row's keys: [0, key_lim)
+        if (n == 0) {  // no keys (kv_len 0): zero rows; no barrier takes part
+          if (qpos < w.q_len) {
+            __nv_bfloat16* dst = out_row(w, qpos);
+            for (int c = 0; c < HD; c += 8) *reinterpret_cast<uint4*>(dst + c) = make_uint4(0u, 0u, 0u, 0u);
+            if (p.lse != nullptr) p.lse[lse_index(w, qpos)] = INFINITY;
+          }
+          continue;
+        }
+      }
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < n; ++j) {
+        const int gj = gt + j;
+        if (!warp_wait(&bars->s_full[g], gj & 1)) {
+          ok = false;
+          break;
+        }
+        ATTN_TRACE(tw, 23 + 4 * g, gj);
+        tc_fence_after();
+        // raw logits: the running max m is kept in log2 units (sl2 > 0, so max and scaling commute) and
+        // p = 2^(s sl2 - m) is one FFMA + ex2 per element; keys past key_lim exist only in the last tile (and,
+        // when causal, in the tiles that cross the diagonal). The four TMEM loads of the row are issued together
+        // (one wait: a tcgen05.ld round trip is long while the tensor core works on TMEM), and P is packed in
+        // place over the consumed S registers (element pair e of a chunk -> register e).
+        const int kbase = j * TK;
+        const bool full_tile = kbase + TK <= key_lim;
+        uint32_t sr[4][32];
 #pragma unroll
-        for (int c = 0; c < NCH; ++c) tmem_ld_32x32b_x32(s_base + c * 32, sr[c]);
+        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(s_base + c * 32, sr[c]);
         tmem_ld_wait();
-      } else {
+        ATTN_TRACE(tw, 24 + 4 * g, gj);
+        if (!full_tile) {
 #pragma unroll
-        for (int c = 0; c < NCH; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) sr[c][i] = 0u;
-      }
-      ATTN_TRACE(tw, 24 + 4 * g, j);
-      if (!full_tile) {
-#pragma unroll
-        for (int c = 0; c < NCH; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (kbase + c * 32 + i >= key_lim) sr[c][i] = __float_as_uint(-INFINITY);
-      }
-      // short dependency chains: 8 partial maxima, then a tree
-      float mx[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < NCH; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sr[c][i]));
-      float rmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      if constexpr (WPQ > 1) {  // row max over the shares (double-buffered slots: a slot is rewritten two tiles on)
-        xch_max[j & 1][g][row][half] = rmax;
-        pair_sync();
-#pragma unroll
-        for (int k = 0; k < WPQ; ++k) rmax = fmaxf(rmax, xch_max[j & 1][g][row][k]);
-      }
-      const float smax = rmax * sl2;
-      const float m_new = fmaxf(m, smax);
-      const bool rescale = (j > 0) && (m_new > m + kRescaleThreshold);
-      const float corr = rescale ? ((m == -INFINITY) ? 0.f : ex2(m - m_new)) : 1.f;
-      if (rescale || j == 0) m = m_new;
-      const float mu = (m == -INFINITY) ? 0.f : m;
-      float rs[4] = {0.f, 0.f, 0.f, 0.f};  // 4 partial sums: short FADD chains
-#pragma unroll
-      for (int c = 0; c < NCH; ++c) {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float a = ex2(fmaf(__uint_as_float(sr[c][2 * e]), sl2, -mu));
-          const float bq = ex2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, -mu));
-          rs[(e & 1) * 2] += a;
-          rs[(e & 1) * 2 + 1] += bq;
-          sr[c][e] = pack_bf16x2(a, bq);  // e <= 2e: the pair was read above
+            for (int i = 0; i < 32; ++i)
+              if (kbase + c * 32 + i >= key_lim) sr[c][i] = __float_as_uint(-INFINITY);
         }
-      }
-      l = l * corr + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
-      ATTN_TRACE(tw, 25 + 4 * g, j);
-      // the other Q tile's P V may still read its A operand from TMEM: let it finish before any tcgen05.st here
-      // (tile 0 at j waits for P_1(j-1) V, tile 1 for P_0(j) V; the later P V of that tile cannot start before
-      // this tile's P is written, so the barrier cannot be a phase ahead)
-      const int og = 1 - g;
-      const int oj = (g == 0) ? j - 1 : j;
-      if (ok && oj >= 0 && oj < n_tiles && !warp_wait(&bars->pv_done[og], oj & 1)) ok = false;
-      if (!ok) continue;  // nothing to store; the pair barrier of the next tile is still reached
-      tc_fence_after();
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O_g is stable here: P_g(j-1) V completed before S_g(j) (tensor-pipe order), P_g(j) V is not issued yet
-#pragma unroll 1
-        for (int c = 0; c < OCOLS / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(o_base + c * 32, o);
-          tmem_ld_wait();
+        float mx[8];  // short dependency chains: 8 partial maxima, then a tree
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
-          tmem_st_32x32b_x32(o_base + c * 32, o);
+        for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sr[c][i]));
+        const float smax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
+        const float m_new = fmaxf(m, smax);
+        const bool rescale = (j > 0) && (m_new > m + kRescaleThreshold);
+        const float corr = rescale ? ((m == -INFINITY) ? 0.f : ex2(m - m_new)) : 1.f;
+        if (rescale || j == 0) m = m_new;
+        const float mu = (m == -INFINITY) ? 0.f : m;
+        float rs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float a = ex2(fmaf(__uint_as_float(sr[c][2 * e]), sl2, -mu));
+            const float bq = ex2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, -mu));
+            rs[(e & 1) * 2] += a;
+            rs[(e & 1) * 2 + 1] += bq;
+            sr[c][e] = pack_bf16x2(a, bq);  // e <= 2e: the pair was read above
+          }
         }
-      }
-#pragma unroll
-      for (int c = 0; c < NCH; ++c)  // P_g(j): this share's keys as bf16 pairs, chunk c in columns c * 16 .. + 15
-        tmem_st_32x32b_x16(p_base + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&sr[c][0]));
-      tmem_st_wait();
-      tc_fence_before();
-      ATTN_TRACE(tw, 26 + 4 * g, j);
-      mbar_arrive(&bars->p_full[g]);
-    }
-    // epilogue: O / l -> bf16, log-sum-exp
-    if (ok && n_tiles > 0) {
-      ok = warp_wait(&bars->pv_done[g], (n_tiles - 1) & 1);
-      tc_fence_after();
-    }
-    if constexpr (WPQ > 1) {  // the row sum over the shares (every thread of the pair reaches this point)
-      xch_l[g][row][half] = l;
-      pair_sync();
-      float lt = 0.f;
-#pragma unroll
-      for (int k = 0; k < WPQ; ++k) lt += xch_l[g][row][k];
-      l = lt;
-    }
-    const int t = qpos;
-    const float inv = (l > 0.f) ? 1.f / l : 0.f;
-    if (ok) {
-      __nv_bfloat16* dst = p.o + (long long)tb * p.o_bs + (long long)(seq0 + t) * p.o_ts + (long long)h * p.o_hs +
-                           half * OCOLS;
+        l = l * corr + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+        ATTN_TRACE(tw, 25 + 4 * g, gj);
+        // the other Q tile's P V may still read its A operand from TMEM: let it finish before any tcgen05.st here
+        // (tile 0 waits for the P_1 V of the previous KV tile, tile 1 for the P_0 V of this one; the later P V of
+        // that tile cannot start before this tile's P is written, so the barrier cannot be a phase ahead)
+        const int oj = (g == 0) ? gj - 1 : gj;
+        if (oj >= 0 && !warp_wait(&bars->pv_done[1 - g], oj & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O_g is stable: P_g(j-1) V completed before S_g(j) (tensor-pipe order), P_g(j) V is not issued yet
 #pragma unroll 1
-      for (int c = 0; c < OCOLS / 32; ++c) {
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(o_base + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+            tmem_st_32x32b_x32(o_base + c * 32, o);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c)  // P_g(j): 128 keys as bf16 pairs, chunk c in columns c * 16 .. + 15
+          tmem_st_32x32b_x16(s_base + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&sr[c][0]));
+        tmem_st_wait();
+        tc_fence_before();
+        ATTN_TRACE(tw, 26 + 4 * g, gj);
+        mbar_arrive(&bars->p_full[g]);
+      }
+      if (!ok) break;
+      // epilogue: O / l -> bf16, log-sum-exp; then O_g is released to the next item's first P V
+      if (!warp_wait(&bars->pv_done[g], (gt + n - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      const FwdItem w = fwd_item(p, item, n_qb);
+      const int qpos = w.q0 + g * TQ + row;
+      __nv_bfloat16* dst = out_row(w, qpos);
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
-        if (n_tiles > 0) {
-          tmem_ld_32x32b_x32(o_base + c * 32, o);
-          tmem_ld_wait();
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = 0u;
-        }
-        if (t < q_len) {
+        tmem_ld_32x32b_x32(o_base + c * 32, o);
+        tmem_ld_wait();
+        if (qpos < w.q_len) {
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
             uint4 u;
@@ -426,14 +459,13 @@ __global__ void __launch_bounds__(fwd_threads<WPQ>(), 1)
           }
         }
       }
-      if (half == 0 && t < q_len && p.lse != nullptr) {
-        const long long li = p.cu_seqlens != nullptr ? (long long)h * p.total + seq0 + t
-                                                     : ((long long)b * p.Hq + h) * p.Tq + t;
-        p.lse[li] = (l > 0.f) ? (m + log2f(l)) * 0.6931471805599453f : INFINITY;
-      }
-    } else {
-      *abort_flag = 1;
+      tc_fence_before();
+      mbar_arrive(&bars->o_free[g]);
+      if (qpos < w.q_len && p.lse != nullptr)
+        p.lse[lse_index(w, qpos)] = (l > 0.f) ? (m + log2f(l)) * 0.6931471805599453f : INFINITY;
+      gt += n;
     }
+    if (!ok) *abort_flag = 1;
   }
   tc_fence_before();
   __syncthreads();
@@ -443,33 +475,29 @@ __global__ void __launch_bounds__(fwd_threads<WPQ>(), 1)
   }
 }
 
-template <int HD, int WPQ>
+template <int HD>
 static cudaError_t fwd_tc_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                const AttnParams& p, int* err, cudaStream_t s) {
   using L = FwdSmem<HD>;
   static bool set = false;
   if (!set) {
-    cudaFuncSetAttribute(flash_fwd_tc_kernel<HD, WPQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+    cudaFuncSetAttribute(flash_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
     set = true;
   }
-  dim3 grid((p.Tq + NQ * TQ - 1) / (NQ * TQ), p.Hq, p.B);
-  flash_fwd_tc_kernel<HD, WPQ><<<grid, fwd_threads<WPQ>(), L::TOTAL, s>>>(tq, tk, tv, p, err);
+  const long long items = (long long)((p.Tq + NQ * TQ - 1) / (NQ * TQ)) * p.Hq * p.B;
+  if (items <= 0) return cudaSuccess;
+  if (items >= (1ll << 31)) return cudaErrorInvalidValue;
+  const int grid = (int)std::min<long long>(items, num_sms());
+  flash_fwd_tc_kernel<HD><<<grid, THREADS, L::TOTAL, s>>>(tq, tk, tv, p, err);
   return cudaGetLastError();
 }
 
-static int g_fwd_wpq = 1;
-cudaError_t attention_set_fwd_split(int wpq) {
-  if (wpq != 1 && wpq != 2) return cudaErrorInvalidValue;
-  g_fwd_wpq = wpq;
-  return cudaSuccess;
-}
+cudaError_t attention_set_fwd_split(int wpq) { return wpq == 1 ? cudaSuccess : cudaErrorInvalidValue; }
 
 cudaError_t attention_fwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                     const AttnParams& p, int* err, cudaStream_t s) {
-  if (p.hd == 128) return g_fwd_wpq == 2 ? fwd_tc_impl<128, 2>(tq, tk, tv, p, err, s)
-                                         : fwd_tc_impl<128, 1>(tq, tk, tv, p, err, s);
-  if (p.hd == 64) return g_fwd_wpq == 2 ? fwd_tc_impl<64, 2>(tq, tk, tv, p, err, s)
-                                        : fwd_tc_impl<64, 1>(tq, tk, tv, p, err, s);
+  if (p.hd == 128) return fwd_tc_impl<128>(tq, tk, tv, p, err, s);
+  if (p.hd == 64) return fwd_tc_impl<64>(tq, tk, tv, p, err, s);
   return cudaErrorInvalidValue;
 }
 

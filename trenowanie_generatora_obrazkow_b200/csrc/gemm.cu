@@ -25,7 +25,7 @@ constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
 
-enum GemmEpi { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2 };
+enum GemmEpi { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2, EPI_SWIGLU = 3 };
 enum GemmPeerMode { PEER_NONE = 0, PEER_WAIT_A = 1, PEER_SCATTER_C = 2, GROUPED = 3 };
 
 
@@ -38,6 +38,34 @@ struct GemmCfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (256 or 512 columns)
 };
+
+// SwiGLU epilogue: the B rows are interleaved in blocks of 128 (gate block k, then up block k), so a 256-column tile
+// holds 128 gate and the 128 matching up columns; out[row, n0 / 2 + j] = silu(gate_j) * up_j (bf16), rounded as the
+// separate GEMM + SwiGLU kernels round it (bf16 products, bf16 silu).
+__device__ __forceinline__ void gemm_store_swiglu(const GemmParams& p, int b, int row, int col0,
+                                                  const uint32_t (&gt)[32], const uint32_t (&ut)[32]) {
+  if (row >= p.M || col0 >= p.N / 2) return;
+  __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)b * p.bsc + (long long)row * p.ldc + col0;
+  const bool full = col0 + 32 <= p.N / 2;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (full || col0 + j * 8 < p.N / 2) {
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float a = __bfloat162float(__float2bfloat16(__uint_as_float(gt[j * 8 + e])));
+        const float u = __bfloat162float(__float2bfloat16(__uint_as_float(ut[j * 8 + e])));
+        o[e] = __bfloat162float(__float2bfloat16(a / (1.f + __expf(-a)))) * u;
+      }
+      uint4 w;
+      w.x = pack_bf16x2(o[0], o[1]);
+      w.y = pack_bf16x2(o[2], o[3]);
+      w.z = pack_bf16x2(o[4], o[5]);
+      w.w = pack_bf16x2(o[6], o[7]);
+      *reinterpret_cast<uint4*>(c + j * 8) = w;
+    }
+  }
+}
 
 // MoE scatter: the bf16 row goes to its source rank's combine buffer (a peer address)
 __device__ __forceinline__ void gemm_store_chunk_peer(const GemmParams& p, int b, int row, int col0,
@@ -318,6 +346,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       decode(tile, b, m0, n0, row_base, rows);
       const int row = m0 + q * 32 + lane;
       const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
+      if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t gv[32], uv[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, gv);
+          tmem_ld_32x32b_x32(tbase + BN / 2 + c * 32, uv);
+          tmem_ld_wait();
+          gemm_store_swiglu(p, b, row, n0 / 2 + c * 32, gv, uv);
+        }
+      } else
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
@@ -519,12 +557,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       const int m0 = (r / num_n) * 256 + rank * 128, n0 = (r % num_n) * G2_BN;
       const int row = m0 + q * 32 + lane;
       const uint32_t tbase = tmem_base + acc * G2_BN + ((uint32_t)(q * 32) << 16);
+      if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll 1
-      for (int c = 0; c < G2_BN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tbase + c * 32, v);
-        tmem_ld_wait();
-        gemm_store_chunk<EPI>(p, b, row, n0 + c * 32, v);
+        for (int c = 0; c < G2_BN / 64; ++c) {
+          uint32_t gv[32], uv[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, gv);
+          tmem_ld_32x32b_x32(tbase + G2_BN / 2 + c * 32, uv);
+          tmem_ld_wait();
+          gemm_store_swiglu(p, b, row, n0 / 2 + c * 32, gv, uv);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < G2_BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, v);
+          tmem_ld_wait();
+          gemm_store_chunk<EPI>(p, b, row, n0 + c * 32, v);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -657,6 +706,11 @@ cudaError_t gemm_peer_launch(const CUtensorMap& ta, const CUtensorMap& tb, const
 
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int bn, bool a_mn,
                         bool b_mn, int epi, cudaStream_t s) {
+  if (epi == EPI_SWIGLU) {  // forward only (A and B K-major), 256-column tiles
+    if (a_mn || b_mn || (bn != 0 && bn != 256) || p.N % 256 != 0) return cudaErrorInvalidValue;
+    return bn == 0 ? launch_gemm_pair<false, false, EPI_SWIGLU>(ta, tb, p, s)
+                   : launch_gemm<256, false, false, EPI_SWIGLU>(ta, tb, p, s);
+  }
   if (bn == 0) {  // 2-CTA kernel (tensor maps built with 128-row / 64-row boxes per CTA)
     if (epi == EPI_BF16) return dispatch_pair<EPI_BF16>(a_mn, b_mn, ta, tb, p, s);
     if (epi == EPI_F32) return dispatch_pair<EPI_F32>(a_mn, b_mn, ta, tb, p, s);

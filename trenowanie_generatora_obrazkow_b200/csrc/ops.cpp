@@ -190,6 +190,35 @@ static long long row_vec_stride(const c10::optional<at::Tensor>& t, int64_t D) {
   return t->stride(0);
 }
 
+// Up projection + SwiGLU in one GEMM: A [M, K] bf16, B [2H, K] bf16 with the gate / up rows interleaved in blocks
+// of 128 (gate block k at rows 256 k .. 256 k + 127, up block k right after), C [M, H] = silu(A Wg^T) * (A Wu^T).
+void gemm_swiglu(at::Tensor A, at::Tensor B, at::Tensor C, at::Tensor err) {
+  TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 &&
+                  C.scalar_type() == at::kBFloat16, "gemm_swiglu: bf16 CUDA tensors");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1,
+              "gemm_swiglu: 2-D row-major operands");
+  const c10::cuda::CUDAGuard guard(A.device());
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K && N % 256 == 0 && C.size(0) == M && C.size(1) * 2 == N, "gemm_swiglu: shapes");
+  TORCH_CHECK(K % 8 == 0 && A.stride(0) % 8 == 0 && C.stride(0) % 8 == 0, "gemm_swiglu: alignment");
+  if (M == 0) return;
+  const int64_t pair_tiles = ((M + 255) / 256) * (N / 256);
+  const bool use_pair = g_gemm_pair_enabled && M >= 256 && pair_tiles >= num_sms() / 2;
+  CUtensorMap ta = make_tmap_bf16_sw128(A.data_ptr(), K, M, 1, A.stride(0), 0, 128);
+  CUtensorMap tb = make_tmap_bf16_sw128(B.data_ptr(), K, N, 1, B.stride(0), 0, use_pair ? 128 : 256);
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.batch = 1;
+  p.C = C.data_ptr();
+  p.ldc = C.stride(0);
+  p.alpha = 1.f;
+  p.err = err_ptr(err);
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(p.C) % 16 == 0, "gemm_swiglu: C alignment");
+  TGO_CHECK_LAUNCH(gemm_launch(ta, tb, p, use_pair ? 0 : 256, false, false, 3, at::cuda::getCurrentCUDAStream()));
+}
+
 // Expert GEMM of the peer-memory MoE exchange (A [batch, M, K] K-major bf16 = the local receive buffer or local
 // activations; B [batch, N, K] or, b_mn, [batch, K, N]). mode 1: wait for the A rows of each source (arrive flags
 // at `arrive`), output to C. mode 2: scatter the output rows to the sources' combine buffers `out_ptrs` (row stride
@@ -919,6 +948,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &tgo::swiglu_bwd, "backward of swiglu_fwd");
   m.def("attention_fwd", &tgo::attention_fwd, "flash attention forward (GQA, key-length mask)");
   m.def("attention_bwd", &tgo::attention_bwd, "flash attention backward");
+  m.def("gemm_swiglu", &tgo::gemm_swiglu, "up projection + SwiGLU in one GEMM (gate / up rows interleaved)");
   m.def("gemm_grouped", &tgo::gemm_grouped, "grouped GEMM with a device-side tile schedule (MoE experts)");
   m.def("gemm_peer", &tgo::gemm_peer, "MoE expert GEMM: wait for peer-dispatched A rows, or scatter C to peers");
   m.def("moe_dispatch", &tgo::moe_dispatch, "MoE dispatch: token gather + stores into the owners' receive buffers");

@@ -36,7 +36,7 @@ class SwiGLU(nn.Module):
         self.out_proj = nn.Linear(hidden, dim, bias=False)
 
     def forward(self, h):
-        return Fz.linear(Fz.swiglu(Fz.linear(h, self.in_proj)), self.out_proj)
+        return Fz.linear(Fz.up_swiglu(h, self.in_proj), self.out_proj)
 
 
 class SelfAttention(nn.Module):

@@ -38,6 +38,33 @@ def bf16_weight(p):
     return ent[1]
 
 
+def swiglu_weight(p):
+    """bf16 copy of a (2H, D) gate | up weight with the gate and up rows interleaved in blocks of 128 (the layout of
+    the fused up projection + SwiGLU GEMM), cached like bf16_weight."""
+    ent = getattr(p, "_tgo_swiglu", None)
+    ver = p._version
+    if ent is None or ent[0] != ver or ent[1].device != p.device:
+        H = p.shape[0] // 2
+        w = p.detach().to(torch.bfloat16)
+        w = torch.stack([w[:H].view(H // 128, 128, -1), w[H:].view(H // 128, 128, -1)], 1).reshape(2 * H, -1)
+        p._tgo_swiglu = (ver, w.contiguous())
+        return p._tgo_swiglu[1]
+    return ent[1]
+
+
+def up_swiglu(x, layer):
+    """silu(x Wg^T) * (x Wu^T) for an nn.Linear of (2H, D) gate | up rows. On CUDA without autograd (sampling) and
+    H % 128 == 0: one GEMM whose epilogue applies the SwiGLU (the (M, 2H) product never reaches memory)."""
+    w = layer.weight
+    H = w.shape[0] // 2
+    if x.is_cuda and not (torch.is_grad_enabled() and (x.requires_grad or w.requires_grad)) and H % 128 == 0:
+        x2 = x.reshape(-1, x.shape[-1]).to(torch.bfloat16).contiguous()
+        out = torch.empty(x2.shape[0], H, device=x.device, dtype=torch.bfloat16)
+        ext().gemm_swiglu(x2, swiglu_weight(w), out, err_buf(x.device))
+        return out.view(*x.shape[:-1], H)
+    return swiglu(linear(x, layer))
+
+
 def set_bf16_weight(p, w):
     """Register an externally produced bf16 copy of p (e.g. written by a fused optimizer kernel)."""
     p._tgo_bf16 = (p._version, w)

@@ -90,16 +90,18 @@ def gemm_case(M, N, K, a_mn=False, b_mn=False, accumulate=False):
     return ours, lib, 2.0 * M * N * K, 2 * (M * K + N * K) + out.element_size() * M * N * (2 if accumulate else 1)
 
 
-def attn_case(B, T, H, hd, backward):
-    q, k, v = (_bf16(B, T, H, hd) for _ in range(3))
-    kv_len = torch.full((B,), T, dtype=torch.int32, device="cuda")
+def attn_case(B, T, H, hd, backward, Tk=None):
+    Tk = Tk or T
+    q = _bf16(B, T, H, hd)
+    k, v = (_bf16(B, Tk, H, hd) for _ in range(2))
+    kv_len = torch.full((B,), Tk, dtype=torch.int32, device="cuda")
     scale = hd ** -0.5
     err = err_buf(q.device)
     o, lse = ext().attention_fwd(q, k, v, kv_len, scale, None, err)
     do = _bf16(B, T, H, hd)
     dq, dk, dv = (torch.empty_like(q) for _ in range(3))
     qt, kt, vt = (x.transpose(1, 2).contiguous().requires_grad_(backward) for x in (q, k, v))
-    fl = 4.0 * B * H * T * T * hd
+    fl = 4.0 * B * H * T * Tk * hd
     if not backward:
         def ours():
             ext().attention_fwd(q, k, v, kv_len, scale, o, err)
@@ -107,7 +109,7 @@ def attn_case(B, T, H, hd, backward):
         def lib():
             F.scaled_dot_product_attention(qt, kt, vt, scale=scale)
 
-        return ours, lib, fl, 2 * 4 * B * T * H * hd
+        return ours, lib, fl, 2 * (2 * B * T + 2 * B * Tk) * H * hd
 
     ot = F.scaled_dot_product_attention(qt, kt, vt, scale=scale)
     dot = do.transpose(1, 2).contiguous()
@@ -220,6 +222,7 @@ def cases(small):
         "attn_fwd": lambda: attn_case(B, T, H, hd, False),
         "attn_bwd": lambda: attn_case(B, T, H, hd, True),
         "attn_fwd_4k": lambda: attn_case(4 if small else 16, 4096, H, hd, False),  # 1024 px sampling (CFG batch)
+        "attn_cross_4k": lambda: attn_case(4 if small else 16, 4096, H, hd, False, Tk=128),  # text cross-attention
         "adanorm_fwd": lambda: adanorm_case(B, T, D, False),
         "adanorm_bwd": lambda: adanorm_case(B, T, D, True),
         "qknorm_rope_fwd": lambda: qknorm_case(B, T, H, hd, False),
