@@ -123,6 +123,43 @@ def attn_case(B, T, H, hd, backward, Tk=None):
     return ours, lib, 2.5 * fl, 2 * 8 * B * T * H * hd
 
 
+def swiglu_gemm_case(M, D, H):
+    """Up projection + SwiGLU in one GEMM (sampling path) vs the library GEMM followed by silu * up."""
+    x = _bf16(M, D)
+    w = _bf16(2 * H, D, scale=D ** -0.5)
+    out = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+
+    def ours():
+        ext().gemm_swiglu(x, w, out, err_buf(x.device))
+
+    def lib():
+        ab = x @ w.T
+        F.silu(ab[:, :H]) * ab[:, H:]
+
+    return ours, lib, 2.0 * M * 2 * H * D, 2 * (M * D + 2 * H * D + M * H)
+
+
+def grouped_gemm_case(M, N, K, groups):
+    """Grouped GEMM with the device-side tile schedule (uneven groups) vs one library GEMM per group."""
+    from .gemm import gemm_grouped
+    a = _bf16(M, K)
+    b = _bf16(groups, N, K, scale=K ** -0.5)
+    g = torch.Generator().manual_seed(3)
+    cuts = torch.sort(torch.randint(0, M, (groups - 1,), generator=g)).values
+    off = torch.cat([torch.tensor([0]), cuts, torch.tensor([M])]).to(torch.int32)
+    offd = off.cuda()
+    bounds = off.tolist()
+
+    def ours():
+        gemm_grouped(a, b, offd)
+
+    def lib():
+        for e in range(groups):
+            a[bounds[e]:bounds[e + 1]] @ b[e].T
+
+    return ours, lib, 2.0 * M * N * K, 2 * (M * K + groups * N * K + M * N)
+
+
 def adanorm_case(B, T, D, backward):
     x, y = _bf16(B, T, D), _bf16(B, T, D)
     gate, shift, scale = (torch.randn(B, D, device="cuda", dtype=torch.bfloat16) * 0.1 for _ in range(3))
@@ -230,6 +267,8 @@ def cases(small):
         "swiglu_fwd": lambda: swiglu_case(M, MLP, False),
         "swiglu_bwd": lambda: swiglu_case(M, MLP, True),
         "euler_cfg": lambda: euler_case(8, 64, 128),
+        "gemm_swiglu": lambda: swiglu_gemm_case(M, D, MLP),
+        "gemm_grouped": lambda: grouped_gemm_case(M, 8192, D, 8),  # MoE experts: up projection of hidden 4096
     }
 
 
