@@ -9,11 +9,20 @@ import numpy as np
 import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-sys.path.insert(0, ROOT)
+
+
+def _script(name):
+    """This repository's root script ``name``.py as a module (the installed reference has scripts of the same
+    names, which another test may have imported first)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(f"_repo_{name}", os.path.join(ROOT, name + ".py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
 
 
 def test_prepare_lowres_latent_pool(tmp_path):
-    import prepare_lowres
+    prepare_lowres = _script("prepare_lowres")
     d = tmp_path / "shards"
     d.mkdir()
     for i in range(3):
@@ -33,7 +42,7 @@ def test_prepare_monet_slims_and_picks_the_shortest_caption(tmp_path):
     import pyarrow as pa
     import pyarrow.parquet as pq
 
-    import prepare_monet
+    prepare_monet = _script("prepare_monet")
     src = tmp_path / "raw" / "part-0"
     src.mkdir(parents=True)
     t = pa.table({"prompt": ["p1", "p2"], "embedding_clip": [[0.1, 0.2], [0.3, 0.4]],
@@ -50,7 +59,7 @@ def test_blimp_eval_scores_pairs(tmp_path):
     from safetensors.torch import save_model
     from tokenizers import Tokenizer, models, pre_tokenizers
 
-    import blimp_eval
+    blimp_eval = _script("blimp_eval")
     from trenowanie_generatora_obrazkow_b200.models.slayer import GPT, GPTConfig
     words = "the cat dog sees sleep sleeps a".split()
     vocab = {"<|endoftext|>": 0, "[UNK]": 1, **{w: i + 2 for i, w in enumerate(words)}}
