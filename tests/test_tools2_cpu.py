@@ -86,3 +86,33 @@ def test_blimp_eval_scores_pairs(tmp_path):
     lp = torch.log_softmax(sc.logits(ids).float(), -1)
     want = sum(lp[0, i, ids[0, i + 1]].item() for i in range(3))
     assert abs(sc(["the cat sleeps"])[0] - want) < 1e-4
+
+
+def test_translate_and_export_captions(tmp_path):
+    """Caption translation with a stand-in engine (upper-cases text, placeholders kept, except one caption whose
+    placeholder it drops: that one is retranslated without protection), then the dataset export."""
+    tr = _script("translate_captions")
+    ex = _script("export_captions")
+
+    def generate(prompts):
+        outs = []
+        for p in prompts:
+            text = p.split("\n\n", 1)[1]
+            outs.append(text.replace("<<0>>", "") if "DROP" in text.upper() and "<<0>>" in text else text.upper())
+        return outs
+
+    t = tr.Translator(generate, lambda text: tr.PROMPT.format(src="English", tgt="Polish", text=text))
+    d = tmp_path / "shards"
+    d.mkdir()
+    caps = [["a sign that says \"Open\"", "a cat"], ["drop \"Keep\" here", "a cat"]]
+    json.dump(caps, open(d / "s0.caps.json", "w"))
+    tr.main(["--data", str(d)], translator=t)
+    out = json.load(open(d / "s0.caps_pl.json"))
+    assert out[0][0] == 'A SIGN THAT SAYS "Open"' and out[0][1] == "A CAT" and out[1][1] == "A CAT"
+    assert out[1][0] == 'drop "Keep" here'.upper()  # retried without placeholders
+    st = json.load(open(d / "s0.caps_pl.stats.json"))
+    assert st["captions"] == 3 and st["quoted"] == 2 and st["retried"] == 1
+    n = ex.main(["--data", str(d), "--out", str(tmp_path / "export")])
+    import pyarrow.parquet as pq
+    rows = pq.read_table(tmp_path / "export" / "data" / "train-00000.parquet").to_pylist()
+    assert n == 2 and rows[1]["captions_pl"][1] == "A CAT" and os.path.exists(tmp_path / "export" / "README.md")
