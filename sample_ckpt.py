@@ -41,7 +41,7 @@ def load(src, raw=False, res=None, rope_ref=None):
             den_cfg = DenoiserConfig(**{k: v for k, v in json.load(f).items()
                                         if k in DenoiserConfig.__dataclass_fields__})
         with open(os.path.join(src, "text_encoder", "config.json")) as f:
-            te_cfg = te_config_from_dict(json.load(f))
+            te_cfg = te_config_from_dict({k: v for k, v in json.load(f).items() if not k.startswith("_")})
         ck = dict(te=load_file(os.path.join(src, "text_encoder", "diffusion_pytorch_model.safetensors")),
                   den=load_file(os.path.join(src, "transformer", "diffusion_pytorch_model.safetensors")))
     if res:
