@@ -87,3 +87,36 @@ def test_guidance_variants_and_eval_grid(tmp_path):
     rec = eg.main([ex, "--prompts", str(tmp_path / "p.json"), "--seeds", "0", "1", "--steps", "2",
                    "--methods", "cfg:3", "cfgzero:3|shift=2", f"ag:{ex}:2", "--out-dir", str(tmp_path / "g")])
     assert len(rec) == 6 and os.path.exists(tmp_path / "g" / "grid_latent_preview.png")
+
+
+def test_web_app_generates_png(tmp_path):
+    """app.py: the form page and POST /generate (a latent preview PNG without a VAE) through FastAPI's test client."""
+    import importlib.util
+    import io
+    import os
+    import sys
+
+    from fastapi.testclient import TestClient
+    from PIL import Image
+    torch.manual_seed(0)
+    den_cfg = DenoiserConfig(dim=64, depth=2, heads=1, mlp_hidden=128, text_dim=64, latent_channels=16,
+                             latent_size=4)
+    te_cfg = TextEncoderConfig(vocab_size=64, dim=64, depth=1, heads=1, kv_heads=1, mlp_hidden=128, max_tokens=12)
+    te, den = build_models(den_cfg, te_cfg)
+    ck = dict(den_config=asdict(den_cfg), te_config=asdict(te_cfg), te=te.state_dict(), den=den.state_dict(),
+              ema=None, step=1, args={})
+    tok = str(tmp_path / "tokenizer.json")
+    _tokenizer(tok)
+    ex = str(tmp_path / "export")
+    export_checkpoint(ck, ex, tokenizer_json=tok)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    spec = importlib.util.spec_from_file_location("_repo_app", os.path.join(root, "app.py"))
+    app_mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(app_mod)
+    client = TestClient(app_mod.build_app(HomeIMGPipeline.from_pretrained(ex, device="cpu"), default_res=64,
+                                          steps=2))
+    assert "HomeIMG" in client.get("/").text
+    r = client.post("/generate", json={"prompt": "a red fox", "steps": 2, "guidance": 3.0, "seed": 7, "res": 64})
+    assert r.status_code == 200 and r.headers["x-seed"] == "7"
+    assert Image.open(io.BytesIO(r.content)).size == (4, 4)
