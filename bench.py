@@ -64,6 +64,7 @@ def parse():
                    "(1024 px, 50 Euler steps, CFG 3, shift 6); 0 = skip it")
     p.add_argument("--sample-res", type=int, default=1024)
     p.add_argument("--sample-steps", type=int, default=50)
+    p.add_argument("--sample-only", action="store_true", help="skip the training measurement: sampling img/s only")
     p.add_argument("--profile-dir", default="", help="profile one step after warm-up (torch.profiler), print the "
                    "kernel table and write traces there; the timed numbers are taken without the profiler")
     return p.parse_args()
@@ -183,6 +184,22 @@ def measure_sampling(run_batch, args, world, local):
             "timed": "denoising loop on device (VAE decode not included: no FLUX.2 VAE weights offline)"}
 
 
+def profile_sampling(run_batch, args, rank, steps=2):
+    """With --profile-dir: torch.profiler table of `steps` sampling steps (after the warm-up; not a timed number)."""
+    if not args.profile_dir:
+        return
+    acts = [torch.profiler.ProfilerActivity.CPU, torch.profiler.ProfilerActivity.CUDA]
+    with torch.profiler.profile(activities=acts) as prof:
+        run_batch(steps)
+        torch.cuda.synchronize()
+    if rank == 0:
+        os.makedirs(args.profile_dir, exist_ok=True)
+        prof.export_chrome_trace(os.path.join(args.profile_dir, f"sampling_{args.impl}.json"))
+        print(f"sampling profile ({steps} denoiser steps, batch {2 * args.sample_batch} with CFG):", flush=True)
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=45, max_name_column_width=90),
+              flush=True)
+
+
 def emit(rank, out):
     if rank == 0:
         print(json.dumps(out), flush=True)
@@ -206,6 +223,8 @@ def run_ours(args):
                       moe_transport=args.moe_transport)
     tr = Trainer(den_cfg, te_cfg, cfg, device)
     per_rank = args.global_batch // world
+    if args.sample_only:
+        return sample_ours(args, tr, den_cfg, te_cfg, rank, world, local, device, {"impl": "ours"})
     host, devb = synthetic_batch(per_rank, args.res, args.text_len, te_cfg.lm_dim, device, 1234 + rank)
     for _ in range(args.warmup):
         tr.step(devb)
@@ -255,6 +274,11 @@ def run_ours(args):
                       "ms_per_step": round(ms_e2e, 2), "h2d_bytes_per_step": (x_bytes + s_bytes) * world,
                       "d2h_bytes_per_step": 4 * world,
                       "api": "Trainer.step(batch in pinned host memory) + loss.item()"}
+    sample_ours(args, tr, den_cfg, te_cfg, rank, world, local, device, out)
+
+
+def sample_ours(args, tr, den_cfg, te_cfg, rank, world, local, device, out):
+    """Sampling img/s through sampling.euler.sample_latents (fused CFG + Euler update), then emit the line."""
     if args.sample_batch > 0:
         from trenowanie_generatora_obrazkow_b200.sampling.euler import encode_prompts, prompt_noise, sample_latents
         side = args.sample_res // 16
@@ -263,9 +287,13 @@ def run_ours(args):
         tr.te.eval(), tr.den.eval()
         text, lens, null, nlen = encode_prompts(tr.te, lm_states=sst)
         noise = prompt_noise(args.sample_batch, den_cfg.latent_channels, side, 0, rank * args.sample_batch, device)
-        out["sampling"] = measure_sampling(
-            lambda steps: sample_latents(tr.den, text, lens, null, nlen, steps=steps, cfg=3.0, shift=6.0,
-                                         latent_size=side, noise=noise), args, world, local)
+
+        def run_batch(steps):
+            return sample_latents(tr.den, text, lens, null, nlen, steps=steps, cfg=3.0, shift=6.0,
+                                  latent_size=side, noise=noise)
+
+        out["sampling"] = measure_sampling(run_batch, args, world, local)
+        profile_sampling(run_batch, args, rank)
     emit(rank, out)
     if world > 1:
         dist.destroy_process_group()
@@ -336,56 +364,58 @@ def run_reference(args):
     null_row = torch.from_numpy(te.null_ids()).to(device)
     state = {"step": 0}
 
-    def step(batch):
-        x0_all = batch["x0"].to(device, non_blocking=True)
-        st_all = batch["lm_states"].to(device, non_blocking=True)
-        for m in range(accum):
-            sl = slice(m * mb, (m + 1) * mb)
-            x0 = x0_all[sl].float()
-            b = x0.shape[0]
-            t = torch.sigmoid(torch.randn(b, device=device))
-            eps = torch.randn_like(x0)
-            drop = torch.rand(b, device=device) < ref_args.cfg_drop
-            cond_ids = torch.where(drop[:, None], null_row[: ids.shape[1]], ids[sl])
-            sync = model.no_sync() if (world > 1 and m < accum - 1) else contextlib.nullcontext()
-            with sync:
-                with torch.autocast("cuda", dtype=torch.bfloat16):
-                    loss = model(x0, cond_ids, st_all[sl], t, eps)
-                (loss / accum).backward()
-        torch.nn.utils.clip_grad_norm_(params, ref_args.clip)
-        mult = ref_train.lr_mult(state["step"], ref_args.steps, 0, ref_args.schedule)
-        for o in opts:
-            for g in o.param_groups:
-                g["lr"] = g["base_lr"] * mult
-            o.step()
-            o.zero_grad(set_to_none=True)
-        state["step"] += 1
-        if ema is not None:
-            d = min(ref_args.ema, state["step"] / (9 + state["step"]))
-            torch._foreach_lerp_(ema, [p.detach() for p in ema_params], 1 - d)
-        return loss
+    out = {"impl": "reference"}
+    if not args.sample_only:  # training measurement
+        def step(batch):
+            x0_all = batch["x0"].to(device, non_blocking=True)
+            st_all = batch["lm_states"].to(device, non_blocking=True)
+            for m in range(accum):
+                sl = slice(m * mb, (m + 1) * mb)
+                x0 = x0_all[sl].float()
+                b = x0.shape[0]
+                t = torch.sigmoid(torch.randn(b, device=device))
+                eps = torch.randn_like(x0)
+                drop = torch.rand(b, device=device) < ref_args.cfg_drop
+                cond_ids = torch.where(drop[:, None], null_row[: ids.shape[1]], ids[sl])
+                sync = model.no_sync() if (world > 1 and m < accum - 1) else contextlib.nullcontext()
+                with sync:
+                    with torch.autocast("cuda", dtype=torch.bfloat16):
+                        loss = model(x0, cond_ids, st_all[sl], t, eps)
+                    (loss / accum).backward()
+            torch.nn.utils.clip_grad_norm_(params, ref_args.clip)
+            mult = ref_train.lr_mult(state["step"], ref_args.steps, 0, ref_args.schedule)
+            for o in opts:
+                for g in o.param_groups:
+                    g["lr"] = g["base_lr"] * mult
+                o.step()
+                o.zero_grad(set_to_none=True)
+            state["step"] += 1
+            if ema is not None:
+                d = min(ref_args.ema, state["step"] / (9 + state["step"]))
+                torch._foreach_lerp_(ema, [p.detach() for p in ema_params], 1 - d)
+            return loss
 
-    for _ in range(args.warmup):
-        step(devb)
-    torch.cuda.synchronize()
-    ms, clocks = timed(lambda: step(devb), args.steps, world, local)
-    tokens = args.global_batch * side * side
-    value = tokens / (ms / 1e3)
-    out = {"metric": METRIC, "value": round(value, 1), "unit": "latent-tokens/s", "n_gpus": world,
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True,
-           "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-           "data": "synthetic (N(0,1) FLUX.2-shaped latents and frozen-LM states), random init",
-           "config": {"model": "reference aurora.model.Denoiser 2048x24, 16 heads, SwiGLU 5504, refiner 1024x2",
-                      "global_batch": args.global_batch, "micro_batch": mb, "seq_len": side * side,
-                      "parallelism": f"dp{world}", "compile": True},
-           "clocks": clocks, "impl": "reference"}
-    if not args.no_e2e:
-        def e2e_step():
-            step(host).item()
+        for _ in range(args.warmup):
+            step(devb)
+        torch.cuda.synchronize()
+        ms, clocks = timed(lambda: step(devb), args.steps, world, local)
+        tokens = args.global_batch * side * side
+        value = tokens / (ms / 1e3)
+        out = {"metric": METRIC, "value": round(value, 1), "unit": "latent-tokens/s", "n_gpus": world,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True,
+               "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+               "data": "synthetic (N(0,1) FLUX.2-shaped latents and frozen-LM states), random init",
+               "config": {"model": "reference aurora.model.Denoiser 2048x24, 16 heads, SwiGLU 5504, refiner 1024x2",
+                          "global_batch": args.global_batch, "micro_batch": mb, "seq_len": side * side,
+                          "parallelism": f"dp{world}", "compile": True},
+               "clocks": clocks, "impl": "reference"}
+        if not args.no_e2e:
+            def e2e_step():
+                step(host).item()
 
-        ms_e2e, _ = timed(e2e_step, args.steps, world, local)
-        out["e2e"] = {"value": round(tokens / (ms_e2e / 1e3), 1), "unit": "latent-tokens/s",
-                      "ms_per_step": round(ms_e2e, 2)}
+            ms_e2e, _ = timed(e2e_step, args.steps, world, local)
+            out["e2e"] = {"value": round(tokens / (ms_e2e / 1e3), 1), "unit": "latent-tokens/s",
+                          "ms_per_step": round(ms_e2e, 2)}
     if args.sample_batch > 0:
         # the denoising loop of aurora/fid.py:sample with the reference's modules (its sample() derives text from
         # token ids through the frozen LM, which is replaced by synthetic states here)
@@ -423,6 +453,7 @@ def run_reference(args):
             return z
 
         out["sampling"] = measure_sampling(ref_sample, args, world, local)
+        profile_sampling(ref_sample, args, rank)
     emit(rank, out)
     if world > 1:
         dist.destroy_process_group()

@@ -1,21 +1,20 @@
 // Flash attention forward on the 5th-generation tensor cores (tcgen05 + TMEM), head dims 64 and 128.
 //
-// CTA = two tiles of 128 query rows of one (batch, head); 320 threads, one CTA per SM:
-//   warp 0        TMA loads: both Q tiles once, then K and V tiles of 64 keys into 4-stage rings with their own
-//                 barriers (K_{j+1} is requested before V_j: a K tile is free once S of both Q tiles is computed,
-//                 a V tile only after both P V products)
+// Persistent CTA (one per SM, 320 threads) walking work items = two tiles of 128 query rows of one (batch, head):
+//   warp 0        TMA loads: both Q tiles of an item, then K and V tiles of 128 keys; K into a 3-stage ring one
+//                 tile ahead of V (2-stage ring): a K tile is free once S of both Q tiles is computed, a V tile
+//                 only after both P V products
 //   warp 1        TMEM allocation (512 columns) and the single MMA-issuing thread, per K / V tile j:
-//                   S_g(j+1) = Q_g K_{j+1}^T  (M 128, N 64, K hd) -> TMEM, two buffers per Q tile (g * 128 + 0 / 64)
-//                   O_g += P_g(j) V_j          (M 128, N hd, K 64) -> TMEM 256 + g * hd, P read from TMEM
+//                   S_g(j+1) = Q_g K_{j+1}^T  (M 128, N 128, K hd) -> TMEM columns g * 128
+//                   O_g += P_g(j) V_j          (M 128, N hd, K 128) -> TMEM 256 + g * hd, P read from TMEM
 //   warps 2-5/6-9 softmax of Q tile 0 / 1: thread = query row = TMEM lane; reads its S row (tcgen05.ld), online
-//                 softmax in exp2 form, writes P (bf16 pairs) back over the first 32 columns of its S buffer
-//                 (tcgen05.st), where the P V MMA reads it as its A operand; rescales its O row in TMEM only when
-//                 its running max grew by more than 2^8 (the stale max is used consistently, so the result is
-//                 exact); before writing P it waits for the previous P V of its tile (see the note at the store);
+//                 softmax in exp2 form with packed f32x2 arithmetic and 3-input max, a fraction of the
+//                 exponentials as FMA-pipe polynomials (the MUFU unit alone cannot keep up with the tensor core at
+//                 head dim 128), writes P (bf16 pairs) back over the first 64 columns of its S buffer (tcgen05.st),
+//                 where the P V MMA reads it as its A operand; rescales its O row in TMEM only when its running
+//                 max grew by more than 2^8 (the stale max is used consistently, so the result is exact); before
+//                 writing P it waits for the previous P V of the other tile (see the note at the store);
 //                 final O / l and log-sum-exp.
-// S(j+1) is issued before P(j) V_j, so the tensor core works on the next tile while the softmax warps work on this
-// one; the two Q tiles share every K / V tile (half the L2 traffic per FLOP of one tile per CTA) and the 4-stage
-// rings keep three tiles of loads in flight.
 // Key masking by per-sample valid length; grouped-query attention by head mapping. Output and LSE layout match
 // the mma.sync kernel in attention.cu, so the backward there consumes them unchanged.
 // Packed variable-length sequences (cu_seqlens) and causal masking serve the frozen caption LM (inference): a CTA
@@ -33,11 +32,13 @@ namespace {
 constexpr int TQ = 128;      // query rows per Q tile (one softmax warpgroup)
 constexpr int NQ = 2;        // Q tiles per CTA
 constexpr int TK = 128;      // keys per K / V tile
-constexpr int KV_STAGES = 2; // K and V rings
+constexpr int K_STAGES = 3;  // K ring (loaded one tile ahead of V)
+constexpr int V_STAGES = 2;  // V ring
 constexpr int THREADS = 320; // warp 0 TMA, warp 1 MMA, warps 2-5 softmax of Q tile 0, warps 6-9 of Q tile 1
 constexpr int TMEM_COLS = 512;
 constexpr int O_COL = 256;   // Q tile g: S / P at g * 128 (P: bf16 pairs in the first 64 columns); O at 256 + g * hd
 constexpr float kRescaleThreshold = 8.f;  // log2 units
+constexpr int kDefaultFwdEmu = 2;         // key pairs (in eighths) whose exponentials use the FMA pipe
 
 // Optional per-phase timeline of one CTA (clock64 per event and iteration), for profiling the pipelines: off
 // unless attention_set_trace() installed a buffer. Slot = event * 64 + (iteration & 63).
@@ -65,23 +66,76 @@ __device__ __forceinline__ float ex2(float x) {  // hardware 2^x (MUFU)
   return y;
 }
 
+// Packed fp32 pairs (sm_100 f32x2 instructions: one issue slot for two lanes of work) and the 3-input max.
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x of two values on the FMA pipe (relieves the MUFU unit, whose exponential rate equals the tensor core's
+// consumption of probabilities at head dim 128). x = j + f with j = round(x), taken from the low mantissa bits of
+// x + 1.5 * 2^23; 2^f on [-0.5, 0.5] by a degree-3 polynomial fitted here for minimum maximum relative error
+// (Lawson's iteratively reweighted least squares; max relative error 7.5e-5, far below the bf16 rounding of P);
+// 2^j enters as an integer add to the exponent field. Inputs are clamped to -126 (2^f >= 0.707 keeps the
+// exponent field non-negative there; the result is then a denormal of at most 2^-126, where ex2.ftz gives 0).
+__device__ __forceinline__ void ex2_fma2(uint64_t x2, float& ya, float& yb) {
+  float xa, xb;
+  f2_split(x2, xa, xb);
+  const uint64_t x = f2(fmaxf(xa, -126.f), fmaxf(xb, -126.f));
+  const uint64_t shifter = f2(12582912.f, 12582912.f);
+  const uint64_t t = f2_add(x, shifter);
+  const uint64_t f = f2_sub(x, f2_sub(t, shifter));
+  uint64_t q = f2_fma(f2(0.05517143f, 0.05517143f), f, f2(0.24261081f, 0.24261081f));
+  q = f2_fma(q, f, f2(0.69326097f, 0.69326097f));
+  q = f2_fma(q, f, f2(0.9999281f, 0.9999281f));
+  float qa, qb, ta, tb;
+  f2_split(q, qa, qb);
+  f2_split(t, ta, tb);
+  ya = __int_as_float(__float_as_int(qa) + (__float_as_int(ta) << 23));
+  yb = __int_as_float(__float_as_int(qb) + (__float_as_int(tb) << 23));
+}
+
 template <int HD>
 struct FwdSmem {
   static constexpr int Q_BYTES = TQ * HD * 2;          // per Q tile: HD / 64 blocks of 128 rows x 128 B
   static constexpr int KV_BYTES = TK * HD * 2;         // HD / 64 blocks of 128 rows x 128 B
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + NQ * Q_BYTES;
-  static constexpr int V_OFF = K_OFF + KV_STAGES * KV_BYTES;
-  static constexpr int BAR_OFF = V_OFF + KV_STAGES * KV_BYTES;
+  static constexpr int V_OFF = K_OFF + K_STAGES * KV_BYTES;
+  static constexpr int BAR_OFF = V_OFF + V_STAGES * KV_BYTES;
   static constexpr int TOTAL = BAR_OFF + 512;
 };
 
 struct FwdBars {
   uint64_t q_full, q_empty;                        // Q tiles of the current item loaded / read by its last S
-  uint64_t k_full[KV_STAGES], k_empty[KV_STAGES];  // K tile free once S of both Q tiles is computed
-  uint64_t v_full[KV_STAGES], v_empty[KV_STAGES];  // V tile free once P V of both Q tiles is computed
+  uint64_t k_full[K_STAGES], k_empty[K_STAGES];    // K tile free once S of both Q tiles is computed
+  uint64_t v_full[V_STAGES], v_empty[V_STAGES];    // V tile free once P V of both Q tiles is computed
   uint64_t s_full[NQ];                             // S_g(j) in TMEM (and, by issue order, P_g(j-1) V done)
-  uint64_t p_full[NQ];                             // softmax wrote P_g(j) over S_g(j): 128 arrivals
+  uint64_t p_full[NQ];                             // softmax wrote P_g(j) over S_g(j): one arrival per warp
   uint64_t pv_done[NQ];                            // one phase per P_g(j) V_j
   uint64_t o_free[NQ];                             // the epilogue read O_g of the item: 128 arrivals
   uint32_t tmem_base;
@@ -129,7 +183,7 @@ __device__ __forceinline__ FwdItem fwd_item(const AttnParams& p, int item, int n
 // P V and next S. Before a tcgen05.st into TMEM the softmax waits for the other tile's P V that may still be
 // reading its A operand from TMEM (a tcgen05.st into TMEM lanes under an in-flight TS-MMA gave wrong products on
 // B200); in the steady state that P V finished long before the exponentials do.
-template <int HD>
+template <int HD, int EMU>
 __global__ void __launch_bounds__(THREADS, 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, AttnParams p, int* err) {
@@ -148,15 +202,17 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
     mbar_init(&bars->q_empty, 1);
-    for (int i = 0; i < KV_STAGES; ++i) {
+    for (int i = 0; i < K_STAGES; ++i) {
       mbar_init(&bars->k_full[i], 1);
       mbar_init(&bars->k_empty[i], 1);
+    }
+    for (int i = 0; i < V_STAGES; ++i) {
       mbar_init(&bars->v_full[i], 1);
       mbar_init(&bars->v_empty[i], 1);
     }
     for (int g = 0; g < NQ; ++g) {
       mbar_init(&bars->s_full[g], 1);
-      mbar_init(&bars->p_full[g], 128);
+      mbar_init(&bars->p_full[g], 4);
       mbar_init(&bars->pv_done[g], 1);
       mbar_init(&bars->o_free[g], 128);
     }
@@ -197,17 +253,27 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int blk = 0; blk < HD / 64; ++blk)
             tma_load_4d(smem + L::Q_OFF + g * L::Q_BYTES + blk * TQ * 128, &tmQ, &bars->q_full, blk * 64,
                         w.seq0 + w.q0 + g * TQ, w.h, w.tb);
-        for (int j = 0; j < w.n_tiles && ok; ++j, ++gt) {
-          const int st = gt % KV_STAGES, ph = (gt / KV_STAGES) & 1;
-          if (!mbar_wait(&bars->k_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
-            ok = false;
-            break;
-          }
+        // K_j of global tile t goes to ring slot t % K_STAGES; within an item K runs one tile ahead of V
+        auto load_k = [&](int t, int jj) -> bool {
+          const int st = t % K_STAGES, ph = (t / K_STAGES) & 1;
+          if (!mbar_wait(&bars->k_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) return false;
           mbar_expect_tx(&bars->k_full[st], L::KV_BYTES);
 #pragma unroll
           for (int blk = 0; blk < HD / 64; ++blk)
             tma_load_4d(smem + L::K_OFF + st * L::KV_BYTES + blk * TK * 128, &tmK, &bars->k_full[st], blk * 64,
-                        w.seq0 + j * TK, w.hk, w.tb);
+                        w.seq0 + jj * TK, w.hk, w.tb);
+          return true;
+        };
+        if (!load_k(gt, 0)) {
+          ok = false;
+          break;
+        }
+        for (int j = 0; j < w.n_tiles && ok; ++j, ++gt) {
+          if (j + 1 < w.n_tiles && !load_k(gt + 1, j + 1)) {
+            ok = false;
+            break;
+          }
+          const int st = gt % V_STAGES, ph = (gt / V_STAGES) & 1;
           if (!mbar_wait(&bars->v_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
@@ -232,7 +298,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint64_t k_desc0 = sdesc_sw128(smem_u32(smem + L::K_OFF), 16, 1024);
       const uint64_t v_desc0 = sdesc_sw128(smem_u32(smem + L::V_OFF), TK * 128, 1024);
       auto issue_s = [&](int g, int gtile, bool last_s) {  // S_g = Q_g K^T into TMEM columns g * 128
-        const int ks = gtile % KV_STAGES;
+        const int ks = gtile % K_STAGES;
         const uint64_t kd = sdesc_add(k_desc0, ks * L::KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
@@ -253,7 +319,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int n = w.n_tiles;
         if (n == 0) continue;
         ok = mbar_wait(&bars->q_full, items & 1, err, ERR_MBAR_TIMEOUT_MMA) &&
-             mbar_wait(&bars->k_full[gt % KV_STAGES], (gt / KV_STAGES) & 1, err, ERR_MBAR_TIMEOUT_MMA);
+             mbar_wait(&bars->k_full[gt % K_STAGES], (gt / K_STAGES) & 1, err, ERR_MBAR_TIMEOUT_MMA);
         if (!ok) break;
         tc_fence_after();
         issue_s(0, gt, false);  // after the previous item's last P_0 V in tensor-pipe order (same TMEM columns)
@@ -261,8 +327,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         ATTN_TRACE(tr, 20, gt);
         for (int j = 0; j < n && ok; ++j) {
           const int gj = gt + j;
-          const int vs = gj % KV_STAGES, vph = (gj / KV_STAGES) & 1;
-          const int kn = (gj + 1) % KV_STAGES, knph = ((gj + 1) / KV_STAGES) & 1;
+          const int vs = gj % V_STAGES, vph = (gj / V_STAGES) & 1;
+          const int kn = (gj + 1) % K_STAGES, knph = ((gj + 1) / K_STAGES) & 1;
           if (!mbar_wait(&bars->v_full[vs], vph, err, ERR_MBAR_TIMEOUT_MMA)) {
             ok = false;
             break;
@@ -374,33 +440,47 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int i = 0; i < 32; ++i)
               if (kbase + c * 32 + i >= key_lim) sr[c][i] = __float_as_uint(-INFINITY);
         }
-        float mx[8];  // short dependency chains: 8 partial maxima, then a tree
+        float mx[4];  // 3-input max, 4 partial maxima (short dependency chains), then a tree
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+        for (int k = 0; k < 4; ++k) mx[k] = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sr[c][i]));
-        const float smax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
+          for (int i = 0; i < 32; i += 2)
+            mx[(i >> 1) & 3] = max3(mx[(i >> 1) & 3], __uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]));
+        const float smax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
         const float m_new = fmaxf(m, smax);
         const bool rescale = (j > 0) && (m_new > m + kRescaleThreshold);
         const float corr = rescale ? ((m == -INFINITY) ? 0.f : ex2(m - m_new)) : 1.f;
         if (rescale || j == 0) m = m_new;
         const float mu = (m == -INFINITY) ? 0.f : m;
-        float rs[4] = {0.f, 0.f, 0.f, 0.f};
+        // per key pair: one packed FMA (scale, subtract the max), two exponentials (MUFU, or the FMA-pipe
+        // polynomial for EMU of every 8 pairs), one packed add into the row sum, one bf16x2 pack
+        const uint64_t sl2x2 = f2(sl2, sl2), nmu2 = f2(-mu, -mu);
+        uint64_t rs2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const float a = ex2(fmaf(__uint_as_float(sr[c][2 * e]), sl2, -mu));
-            const float bq = ex2(fmaf(__uint_as_float(sr[c][2 * e + 1]), sl2, -mu));
-            rs[(e & 1) * 2] += a;
-            rs[(e & 1) * 2 + 1] += bq;
+            const uint64_t x2 = f2_fma(f2(__uint_as_float(sr[c][2 * e]), __uint_as_float(sr[c][2 * e + 1])),
+                                       sl2x2, nmu2);
+            float a, bq;
+            if ((e & 7) >= 8 - EMU) {
+              ex2_fma2(x2, a, bq);
+            } else {
+              float xa, xb;
+              f2_split(x2, xa, xb);
+              a = ex2(xa);
+              bq = ex2(xb);
+            }
+            rs2[e & 1] = f2_add(rs2[e & 1], f2(a, bq));
             sr[c][e] = pack_bf16x2(a, bq);  // e <= 2e: the pair was read above
           }
         }
-        l = l * corr + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+        float r0, r1, r2, r3;
+        f2_split(rs2[0], r0, r1);
+        f2_split(rs2[1], r2, r3);
+        l = l * corr + ((r0 + r1) + (r2 + r3));
         ATTN_TRACE(tw, 25 + 4 * g, gj);
         // the other Q tile's P V may still read its A operand from TMEM: let it finish before any tcgen05.st here
         // (tile 0 waits for the P_1 V of the previous KV tile, tile 1 for the P_0 V of this one; the later P V of
@@ -428,8 +508,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_st_32x32b_x16(s_base + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&sr[c][0]));
         tmem_st_wait();
         tc_fence_before();
+        __syncwarp();
         ATTN_TRACE(tw, 26 + 4 * g, gj);
-        mbar_arrive(&bars->p_full[g]);
+        if (lane == 0) mbar_arrive(&bars->p_full[g]);  // one arrival per warp, after its stores completed
       }
       if (!ok) break;
       // epilogue: O / l -> bf16, log-sum-exp; then O_g is released to the next item's first P V
@@ -475,29 +556,51 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-template <int HD>
+template <int HD, int EMU>
 static cudaError_t fwd_tc_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                const AttnParams& p, int* err, cudaStream_t s) {
   using L = FwdSmem<HD>;
+  static_assert(L::TOTAL <= 232448, "shared memory");
   static bool set = false;
   if (!set) {
-    cudaFuncSetAttribute(flash_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+    cudaFuncSetAttribute(flash_fwd_tc_kernel<HD, EMU>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
     set = true;
   }
   const long long items = (long long)((p.Tq + NQ * TQ - 1) / (NQ * TQ)) * p.Hq * p.B;
   if (items <= 0) return cudaSuccess;
   if (items >= (1ll << 31)) return cudaErrorInvalidValue;
   const int grid = (int)std::min<long long>(items, num_sms());
-  flash_fwd_tc_kernel<HD><<<grid, THREADS, L::TOTAL, s>>>(tq, tk, tv, p, err);
+  flash_fwd_tc_kernel<HD, EMU><<<grid, THREADS, L::TOTAL, s>>>(tq, tk, tv, p, err);
   return cudaGetLastError();
 }
 
+// Exponentials computed on the FMA pipe, in eighths of the key pairs (0: all on the MUFU unit).
+static int g_fwd_emu = kDefaultFwdEmu;
+
 cudaError_t attention_set_fwd_split(int wpq) { return wpq == 1 ? cudaSuccess : cudaErrorInvalidValue; }
+
+cudaError_t attention_set_fwd_emu(int eighths) {  // -1: the built-in default
+  if (eighths == -1) eighths = kDefaultFwdEmu;
+  if (eighths != 0 && eighths != 2 && eighths != 3 && eighths != 4) return cudaErrorInvalidValue;
+  g_fwd_emu = eighths;
+  return cudaSuccess;
+}
+
+template <int HD>
+static cudaError_t fwd_tc_dispatch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                                   const AttnParams& p, int* err, cudaStream_t s) {
+  switch (g_fwd_emu) {
+    case 2: return fwd_tc_impl<HD, 2>(tq, tk, tv, p, err, s);
+    case 3: return fwd_tc_impl<HD, 3>(tq, tk, tv, p, err, s);
+    case 4: return fwd_tc_impl<HD, 4>(tq, tk, tv, p, err, s);
+    default: return fwd_tc_impl<HD, 0>(tq, tk, tv, p, err, s);
+  }
+}
 
 cudaError_t attention_fwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                     const AttnParams& p, int* err, cudaStream_t s) {
-  if (p.hd == 128) return fwd_tc_impl<128>(tq, tk, tv, p, err, s);
-  if (p.hd == 64) return fwd_tc_impl<64>(tq, tk, tv, p, err, s);
+  if (p.hd == 128) return fwd_tc_dispatch<128>(tq, tk, tv, p, err, s);
+  if (p.hd == 64) return fwd_tc_dispatch<64>(tq, tk, tv, p, err, s);
   return cudaErrorInvalidValue;
 }
 

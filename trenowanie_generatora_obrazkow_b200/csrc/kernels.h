@@ -264,6 +264,7 @@ cudaError_t moe_release_launch(uint32_t* const* free_peer, int rank, int world, 
 
 cudaError_t attention_set_trace(long long* buf, int cta);  // profiling timeline (null: off)
 cudaError_t attention_set_fwd_split(int wpq);  // softmax warps per TMEM lane quarter in the forward (1 or 2)
+cudaError_t attention_set_fwd_emu(int eighths);  // forward exponentials on the FMA pipe: 0, 2, 3 or 4 eighths
 cudaError_t muon_rs_launch(const MuonRSParams& p, int blocks, cudaStream_t s);
 cudaError_t muon_momentum_launch(const MuonMomentumParams& p, cudaStream_t s);
 cudaError_t muon_ag_apply_launch(const MuonAGParams& p, int blocks, cudaStream_t s);

@@ -93,6 +93,9 @@ void set_attention_tc(bool on) { g_attention_tc = on; }
 void set_attention_fwd_split(int64_t wpq) {
   TORCH_CHECK(attention_set_fwd_split((int)wpq) == cudaSuccess, "attention forward split: 1 or 2");
 }
+void set_attention_fwd_emu(int64_t eighths) {
+  TORCH_CHECK(attention_set_fwd_emu((int)eighths) == cudaSuccess, "attention forward FMA exponentials: 0, 2, 3, 4 (-1: default)");
+}
 
 static bool g_gemm_pair_enabled = true;  // 256 x 256 CTA-pair tiles: 3-6 % faster on the training shapes
 void set_gemm_pair(bool on) { g_gemm_pair_enabled = on; }
@@ -935,6 +938,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("muon_rs", &tgo::muon_rs, "sharded Muon: gradient bucket reduce-scatter to the matrix owners (NVLink)");
   m.def("muon_momentum", &tgo::muon_momentum, "sharded Muon: owner momentum + Nesterov -> bf16 NS input");
   m.def("muon_ag_apply", &tgo::muon_ag_apply, "sharded Muon: update all-gather fused with the parameter update");
+  m.def("set_attention_fwd_emu", &tgo::set_attention_fwd_emu,
+        "eighths of the key pairs whose forward exponentials run as FMA-pipe polynomials (0, 2, 3, 4)");
   m.def("set_attention_fwd_split", &tgo::set_attention_fwd_split,
         "softmax warps per TMEM lane quarter in the tcgen05 attention forward (1 or 2)");
   m.def("set_attention_tc", &tgo::set_attention_tc, "use the tcgen05 attention forward (default) or mma.sync");

@@ -301,6 +301,8 @@ def main(argv=None):
     p.add_argument("--small", action="store_true")
     p.add_argument("--no-library", action="store_true", help="time only our kernels (profiler captures)")
     p.add_argument("--gemm-pair", type=int, default=-1, help="1 / 0: force the 2-CTA GEMM on / off")
+    p.add_argument("--attn-emu", default="", help="comma-separated settings of the attention forward's FMA-pipe "
+                   "exponentials (eighths of the key pairs: 0, 2, 3, 4); every op runs once per setting")
     a = p.parse_args(argv)
     torch.manual_seed(0)
     if a.gemm_pair >= 0:
@@ -309,14 +311,20 @@ def main(argv=None):
     table = cases(a.small)
     names = list(table) if a.op == "all" else a.op.split(",")
     rows = []
-    for n in names:
-        ours, lib, flops, nbytes = table[n]()
-        row = report(n, ours, lib, flops, nbytes, a.iters, a.warmup, peaks, not a.no_library)
-        from ._ext import check_errors
-        check_errors()
-        print(json.dumps(row), flush=True)
-        rows.append(row)
-        torch.cuda.empty_cache()
+    settings = [int(v) for v in a.attn_emu.split(",")] if a.attn_emu else [None]
+    for emu in settings:
+        if emu is not None:
+            ext().set_attention_fwd_emu(emu)
+        for n in names:
+            ours, lib, flops, nbytes = table[n]()
+            row = report(n, ours, lib, flops, nbytes, a.iters, a.warmup, peaks, not a.no_library)
+            if emu is not None:
+                row["attn_emu"] = emu
+            from ._ext import check_errors
+            check_errors()
+            print(json.dumps(row), flush=True)
+            rows.append(row)
+            torch.cuda.empty_cache()
     return rows
 
 
