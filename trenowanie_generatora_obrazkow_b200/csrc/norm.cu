@@ -134,6 +134,91 @@ __global__ void __launch_bounds__(1024) adanorm_fwd_kernel(AdaNormFwdParams p) {
   }
 }
 
+// Warp-per-row variant for D = 256 NC: lane l owns columns k * 256 + 8 l (k < NC), 16-byte accesses. All NC x / y
+// (and gate) loads of a row are issued before any use, the row sum of squares is a shuffle reduction (no block
+// barrier), and x_new stays packed bf16 between the two passes, so 2 blocks of 8 warps fit per SM with every
+// warp's loads in flight. The bf16-rounded steps run as packed bf16x2 arithmetic on the FMA pipe: x + bf16(g y)
+// (two roundings, as the autocast ops) and bf16(x_new rstd_bf16) (the product of two bf16 values is exact in fp32,
+// so one bf16x2 multiply rounds it identically); fp32 <-> bf16 conversions per element otherwise saturate the
+// conversion unit (XU) before HBM.
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(f[0], f[1]);
+  u.y = pack_bf16x2(f[2], f[3]);
+  u.z = pack_bf16x2(f[4], f[5]);
+  u.w = pack_bf16x2(f[6], f[7]);
+  return u;
+}
+__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 b) { return *reinterpret_cast<uint32_t*>(&b); }
+
+template <int NC>
+__global__ void __launch_bounds__(256, 2) adanorm_fwd_warp_kernel(AdaNormFwdParams p) {
+  const int row = blockIdx.x * 8 + warp_id();
+  if (row >= p.M) return;
+  const int c_lane = lane_id() * 8;
+  const int b = row / p.T;
+  const long long off = (long long)row * p.D + c_lane;
+  const bool res = p.y != nullptr, gated = res && p.gate != nullptr;
+  uint4 ux[NC], uy[NC], ug[NC];
+#pragma unroll
+  for (int k = 0; k < NC; ++k) ux[k] = *reinterpret_cast<const uint4*>(p.x + off + k * 256);
+  if (res) {
+#pragma unroll
+    for (int k = 0; k < NC; ++k) uy[k] = *reinterpret_cast<const uint4*>(p.y + off + k * 256);
+  }
+  if (gated) {
+#pragma unroll
+    for (int k = 0; k < NC; ++k)
+      ug[k] = *reinterpret_cast<const uint4*>(p.gate + (long long)b * p.gate_bs + k * 256 + c_lane);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    uint32_t* xw = reinterpret_cast<uint32_t*>(&ux[k]);
+    if (res) {
+      const uint32_t* yw = reinterpret_cast<const uint32_t*>(&uy[k]);
+      const uint32_t* gw = reinterpret_cast<const uint32_t*>(&ug[k]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        xw[i] = bf2_bits(gated ? __hadd2(as_bf2(xw[i]), __hmul2(as_bf2(gw[i]), as_bf2(yw[i])))
+                               : __hadd2(as_bf2(xw[i]), as_bf2(yw[i])));
+      *reinterpret_cast<uint4*>(p.x_out + off + k * 256) = ux[k];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(as_bf2(xw[i]));
+      ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / p.D + p.eps);
+  if (lane_id() == 0) p.rstd[row] = r;
+  const __nv_bfloat162 rb2 = __float2bfloat162_rn(r);
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    const int c = k * 256 + c_lane;
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(&ux[k]);
+    const float4 w0 = *reinterpret_cast<const float4*>(p.w + c), w1 = *reinterpret_cast<const float4*>(p.w + c + 4);
+    const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    float h[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 n = __bfloat1622float2(__hmul2(as_bf2(xw[i]), rb2));
+      h[2 * i] = n.x * w[2 * i];
+      h[2 * i + 1] = n.y * w[2 * i + 1];
+    }
+    if (p.scale != nullptr) {
+      float sc[8], sh[8];
+      load8(p.scale + (long long)b * p.mod_bs + c, sc);
+      load8(p.shift + (long long)b * p.mod_bs + c, sh);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = fmaf(h[i], 1.f + sc[i], sh[i]);
+    }
+    *reinterpret_cast<uint4*>(p.h + off + k * 256) = pack8(h);
+  }
+}
+
 // ------------------------------------------------------------------------------------------------------------------
 // adanorm backward: row pass (dx, dy, per-CTA partial column sums)
 // partial layout: [B][chunks][4][D] = dshift, dscale, dgate, dw
@@ -289,6 +374,14 @@ __global__ void adanorm_bwd_reduce_kernel(const float* __restrict__ partial, flo
 }
 
 cudaError_t adanorm_fwd_launch(const AdaNormFwdParams& p, cudaStream_t s) {
+  if (p.D % 256 == 0 && p.D <= 2048) {  // warp per row (wider rows would spill the held row)
+    const unsigned grid = (unsigned)((p.M + 7) / 8);
+    switch (p.D / 256) {
+      case 4: adanorm_fwd_warp_kernel<4><<<grid, 256, 0, s>>>(p); return cudaGetLastError();
+      case 8: adanorm_fwd_warp_kernel<8><<<grid, 256, 0, s>>>(p); return cudaGetLastError();
+      default: break;
+    }
+  }
   const int threads = ((p.D / 8 + 31) / 32) * 32;
   const int grid = (p.M + p.rows_per_cta - 1) / p.rows_per_cta;
   adanorm_fwd_kernel<<<grid, threads, 0, s>>>(p);
@@ -322,52 +415,76 @@ __device__ __forceinline__ void load8f(const float* p, float (&f)[8]) {
   f[0] = a.x, f[1] = a.y, f[2] = a.z, f[3] = a.w, f[4] = b.x, f[5] = b.y, f[6] = b.z, f[7] = b.w;
 }
 
+// One warp per token row walks that row's q and k heads, HD / 8 lanes per head (8 elements per lane), several heads
+// per load batch: the row's RoPE table entries and the norm weights are read once per warp and reused for every head
+// (per-head table reads made the table traffic twice the activation traffic), and each lane keeps UNROLL 16-byte
+// loads in flight.
 template <int HD>
 __global__ void __launch_bounds__(256) qknorm_rope_fwd_kernel(QKNormRopeParams p) {
-  constexpr int LPH = HD / 8, IPW = 32 / LPH;
+  constexpr int LPH = HD / 8, HPI = 32 / LPH, UNROLL = 4;  // lanes per head, heads per pass, passes per batch
   const int heads = p.hq + p.hkv;
-  const long long total = (long long)p.M * heads;
-  const long long item = ((long long)blockIdx.x * (blockDim.x >> 5) + warp_id()) * IPW + lane_id() / LPH;
-  const bool valid = item < total;  // invalid lanes still take part in the shuffles
-  const int row = valid ? (int)(item / heads) : 0, hh = valid ? (int)(item % heads) : 0;
-  const bool is_q = hh < p.hq;
+  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + warp_id();
+  if (row >= p.M) return;  // whole warps leave together: the shuffles below stay warp-uniform
+  const int sub = lane_id() / LPH;
   const int e0 = (lane_id() % LPH) * 8;
-  float x[8];
-  if (valid) load8(p.qkv + (long long)row * p.ld_qkv + (long long)hh * HD + e0, x);
-  else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = 0.f;
+  float cs[8], sn[8], wq[8], wk[8];
+  if (p.cos != nullptr) {
+    const long long b = row / p.T, t = row % p.T;
+    load8f(p.cos + b * p.rope_bs + t * HD + e0, cs);
+    load8f(p.sin + b * p.rope_bs + t * HD + e0, sn);
   }
-  const float* nw = is_q ? p.q_w : p.k_w;
-  if (nw != nullptr) {
-    float ss = 0.f;
+  if (p.q_w != nullptr) load8f(p.q_w + e0, wq);
+  if (p.k_w != nullptr) load8f(p.k_w + e0, wk);
+  const bf16* src = p.qkv + row * p.ld_qkv;
+  for (int h0 = 0; h0 < heads; h0 += UNROLL * HPI) {
+    uint4 ux[UNROLL];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
-    ss = group_sum<LPH>(ss);
-    const float r = rsqrtf(ss / HD + p.eps);
-    const float rb = bf16_round(r);
-    float w8[8];
-    load8f(nw + e0, w8);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = bf16_round(x[i] * rb) * w8[i];
-    if (valid && e0 == 0) (is_q ? p.rstd_q : p.rstd_k)[(long long)row * (is_q ? p.hq : p.hkv) + (is_q ? hh : hh - p.hq)] = r;
-  }
-  if (p.cos != nullptr && valid) {
-    const int b = row / p.T, t = row % p.T;
-    float cs[8], sn[8];
-    load8f(p.cos + (long long)b * p.rope_bs + (long long)t * HD + e0, cs);
-    load8f(p.sin + (long long)b * p.rope_bs + (long long)t * HD + e0, sn);
-#pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-      const float a = x[i], c = x[i + 1];
-      x[i] = a * cs[i] - c * sn[i];
-      x[i + 1] = c * cs[i + 1] + a * sn[i + 1];
+    for (int u = 0; u < UNROLL; ++u) {
+      const int hh = h0 + u * HPI + sub;
+      ux[u] = hh < heads ? *reinterpret_cast<const uint4*>(src + (long long)hh * HD + e0) : make_uint4(0u, 0u, 0u, 0u);
     }
-  }
-  if (valid) {
-    bf16* dst = is_q ? p.q_out + (long long)row * p.ld_q + (long long)hh * HD + e0
-                     : p.k_out + (long long)row * p.ld_k + (long long)(hh - p.hq) * HD + e0;
-    store8(dst, x);
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int hh = h0 + u * HPI + sub;
+      const bool valid = hh < heads, is_q = hh < p.hq;
+      const float* nw = is_q ? p.q_w : p.k_w;
+      const uint32_t* xw = reinterpret_cast<const uint32_t*>(&ux[u]);
+      float x[8];
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(as_bf2(xw[i]));
+        x[2 * i] = f.x;
+        x[2 * i + 1] = f.y;
+        ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+      }
+      ss = group_sum<LPH>(ss);  // every lane takes part (q_w / k_w presence is uniform per head group only)
+      if (nw != nullptr) {
+        const float r = rsqrtf(ss / HD + p.eps);
+        const __nv_bfloat162 rb2 = __float2bfloat162_rn(r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // bf16(x rstd_bf16): one packed multiply, then the fp32 weight
+          const float2 n = __bfloat1622float2(__hmul2(as_bf2(xw[i]), rb2));
+          x[2 * i] = n.x * (is_q ? wq[2 * i] : wk[2 * i]);
+          x[2 * i + 1] = n.y * (is_q ? wq[2 * i + 1] : wk[2 * i + 1]);
+        }
+        if (valid && e0 == 0)
+          (is_q ? p.rstd_q : p.rstd_k)[row * (is_q ? p.hq : p.hkv) + (is_q ? hh : hh - p.hq)] = r;
+      }
+      if (p.cos != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          const float a = x[i], c = x[i + 1];
+          x[i] = a * cs[i] - c * sn[i];
+          x[i + 1] = c * cs[i + 1] + a * sn[i + 1];
+        }
+      }
+      if (valid) {
+        bf16* dst = is_q ? p.q_out + row * p.ld_q + (long long)hh * HD + e0
+                         : p.k_out + row * p.ld_k + (long long)(hh - p.hq) * HD + e0;
+        *reinterpret_cast<uint4*>(dst) = pack8(x);
+      }
+    }
   }
 }
 
@@ -461,9 +578,7 @@ __global__ void __launch_bounds__(512) qknorm_rope_bwd_kernel(QKNormRopeParams p
 }
 
 cudaError_t qknorm_rope_fwd_launch(const QKNormRopeParams& p, cudaStream_t s) {
-  const long long items = (long long)p.M * (p.hq + p.hkv);
-  const int per_block = 8 * (32 / (p.hd / 8));  // 8 warps
-  const unsigned grid = (unsigned)((items + per_block - 1) / per_block);
+  const unsigned grid = (unsigned)(((long long)p.M + 7) / 8);  // one warp per token row, 8 warps per block
   if (p.hd == 128) qknorm_rope_fwd_kernel<128><<<grid, 256, 0, s>>>(p);
   else if (p.hd == 64) qknorm_rope_fwd_kernel<64><<<grid, 256, 0, s>>>(p);
   else return cudaErrorInvalidValue;
