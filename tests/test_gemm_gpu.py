@@ -56,6 +56,37 @@ def test_gemm_batched_strided():
     assert _rel(c, a.float() @ b.float()) < 1e-2
 
 
+@pytest.mark.parametrize("M,N,K,batch", [(4000, 2312, 512, 1), (1024, 2048, 256, 3)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, True)])
+def test_gemm_pair_tma_epilogue(M, N, K, batch, a_mn, b_mn):
+    """2-CTA GEMM whose epilogue writes C by TMA stores (clipped at ragged M / N edges, batched C) and fp32 TMA
+    reduce-adds, against the per-row store epilogue (bitwise) and the fp32 oracle."""
+    from trenowanie_generatora_obrazkow_b200.ops.gemm import gemm
+    from trenowanie_generatora_obrazkow_b200.ops._ext import check_errors, ext
+    torch.manual_seed(3)
+    lead = (batch,) if batch > 1 else ()
+    a = torch.randn(*lead, *((K, M) if a_mn else (M, K)), device="cuda").bfloat16()
+    b = torch.randn(*lead, *((K, N) if b_mn else (N, K)), device="cuda").bfloat16()
+    c_tma = gemm(a, b, a_mn=a_mn, b_mn=b_mn)
+    acc_tma = torch.randn(*lead, M, N, device="cuda")
+    acc_rows = acc_tma.clone()
+    gemm(a, b, out=acc_tma, a_mn=a_mn, b_mn=b_mn, alpha=0.5, accumulate=True)
+    ext().set_gemm_tma_epilogue(False)
+    try:
+        c_rows = gemm(a, b, a_mn=a_mn, b_mn=b_mn)
+        gemm(a, b, out=acc_rows, a_mn=a_mn, b_mn=b_mn, alpha=0.5, accumulate=True)
+    finally:
+        ext().set_gemm_tma_epilogue(True)
+    torch.cuda.synchronize()
+    check_errors()
+    A = a.float().mT if a_mn else a.float()
+    B = b.float() if b_mn else b.float().mT
+    ref = A @ B
+    assert torch.equal(c_tma, c_rows)
+    assert _rel(c_tma, ref) < 1e-2
+    assert _rel(acc_tma, acc_rows) < 1e-6
+
+
 @pytest.mark.parametrize("b_mn", [False, True])
 def test_gemm_grouped_device_schedule(b_mn):
     """Grouped GEMM with the tile schedule built on the device: uneven, empty and sub-tile groups, routing-weight row

@@ -392,6 +392,57 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 }
 
 
+// TMA epilogue of the 2-CTA kernel: a warp stages its 32 rows x 32 columns in shared memory in the tensor map's
+// swizzled layout (bf16: 64-byte rows, 64-byte swizzle; fp32: 128-byte rows, 128-byte swizzle; both conflict-free for
+// one 16-byte store per lane and phase), then one lane issues the TMA store (or, for the fp32 accumulate epilogue,
+// the TMA reduce-add, so the fp32 gradient bucket is never read by the SM). Per-row global stores from the epilogue
+// cost 32 L1 wavefronts per warp instruction on the same data path as the tensor core's shared-memory operand reads.
+template <int EPI>
+__device__ __forceinline__ void gemm_stage_chunk(const GemmParams& p, int row, uint8_t* buf, int lane,
+                                                 const uint32_t (&r)[32]) {
+  const float a = (p.row_scale != nullptr && row < p.M) ? p.alpha * p.row_scale[row] : p.alpha;
+  if constexpr (EPI == EPI_BF16) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 u;
+      u.x = pack_bf16x2(__uint_as_float(r[j * 8 + 0]) * a, __uint_as_float(r[j * 8 + 1]) * a);
+      u.y = pack_bf16x2(__uint_as_float(r[j * 8 + 2]) * a, __uint_as_float(r[j * 8 + 3]) * a);
+      u.z = pack_bf16x2(__uint_as_float(r[j * 8 + 4]) * a, __uint_as_float(r[j * 8 + 5]) * a);
+      u.w = pack_bf16x2(__uint_as_float(r[j * 8 + 6]) * a, __uint_as_float(r[j * 8 + 7]) * a);
+      *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = u;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 f;
+      f.x = __uint_as_float(r[j * 4 + 0]) * a;
+      f.y = __uint_as_float(r[j * 4 + 1]) * a;
+      f.z = __uint_as_float(r[j * 4 + 2]) * a;
+      f.w = __uint_as_float(r[j * 4 + 3]) * a;
+      *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = f;
+    }
+  }
+}
+__device__ __forceinline__ void gemm_stage_swiglu(uint8_t* buf, int lane, const uint32_t (&gt)[32],
+                                                  const uint32_t (&ut)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float a = __bfloat162float(__float2bfloat16(__uint_as_float(gt[j * 8 + e])));
+      const float u = __bfloat162float(__float2bfloat16(__uint_as_float(ut[j * 8 + e])));
+      o[e] = __bfloat162float(__float2bfloat16(a / (1.f + __expf(-a)))) * u;
+    }
+    uint4 w;
+    w.x = pack_bf16x2(o[0], o[1]);
+    w.y = pack_bf16x2(o[2], o[3]);
+    w.z = pack_bf16x2(o[4], o[5]);
+    w.w = pack_bf16x2(o[6], o[7]);
+    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = w;
+  }
+}
+
 // ----------------------------------------------------------------------------------------------------------------
 // 2-CTA variant: a cluster of two CTAs (one TPC) computes a 256 x 256 tile with tcgen05.mma.cta_group::2.
 // CTA r of the pair loads rows [m0 + 128 r, +128) of A and rows [n0 + 128 r, +128) of B into its own shared memory
@@ -405,13 +456,14 @@ constexpr int G2_A_BYTES = 128 * 64 * 2; // 16 KB
 constexpr int G2_B_BYTES = 128 * 64 * 2; // 16 KB
 constexpr int G2_STAGE_BYTES = G2_A_BYTES + G2_B_BYTES;
 constexpr int G2_STAGES = 6;
-constexpr int G2_SMEM = G2_STAGES * G2_STAGE_BYTES + 1024;
+constexpr int G2_C_STAGE = 8192;         // TMA epilogue: per epilogue warp two 32 x 32 staging tiles (<= 4 KB each)
+constexpr int G2_SMEM = G2_STAGES * G2_STAGE_BYTES + 4 * G2_C_STAGE + 1024;
 constexpr int G2_TMEM_COLS = 512;        // two 256-column accumulators
 
 template <bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                             GemmParams p) {
+                             const __grid_constant__ CUtensorMap tmC, GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[G2_STAGES];
@@ -540,6 +592,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   } else {
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
     const int q = warp & 3;
+    const bool tma_c = p.c_tma != 0;
+    uint8_t* const cstage = smem + G2_STAGES * G2_STAGE_BYTES + q * G2_C_STAGE;
+    int cbuf = 0;
+    // stage one 32 x 32 chunk and hand it to the TMA unit (the buffer's previous store must have read it)
+    auto tma_chunk = [&](auto&& fill, int x, int y, int z) {
+      uint8_t* buf = cstage + (cbuf & 1) * (G2_C_STAGE / 2);
+      if (lane == 0) bulk_wait_group_read<1>();
+      __syncwarp();
+      fill(buf);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (EPI == EPI_F32_ACC) tma_reduce_add_3d(&tmC, buf, x, y, z);
+        else tma_store_3d(&tmC, buf, x, y, z);
+        bulk_commit_group();
+      }
+      ++cbuf;
+    };
     int local = 0;
     for (int tile = cluster; tile < num_tiles; tile += n_clusters, ++local) {
       const int acc = local & 1;
@@ -564,7 +634,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
           tmem_ld_32x32b_x32(tbase + c * 32, gv);
           tmem_ld_32x32b_x32(tbase + G2_BN / 2 + c * 32, uv);
           tmem_ld_wait();
-          gemm_store_swiglu(p, b, row, n0 / 2 + c * 32, gv, uv);
+          if (tma_c)
+            tma_chunk([&](uint8_t* buf) { gemm_stage_swiglu(buf, lane, gv, uv); }, n0 / 2 + c * 32, m0 + q * 32, b);
+          else
+            gemm_store_swiglu(p, b, row, n0 / 2 + c * 32, gv, uv);
         }
       } else {
 #pragma unroll 1
@@ -572,13 +645,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
           uint32_t v[32];
           tmem_ld_32x32b_x32(tbase + c * 32, v);
           tmem_ld_wait();
-          gemm_store_chunk<EPI>(p, b, row, n0 + c * 32, v);
+          if (tma_c)
+            tma_chunk([&](uint8_t* buf) { gemm_stage_chunk<EPI>(p, row, buf, lane, v); }, n0 + c * 32, m0 + q * 32, b);
+          else
+            gemm_store_chunk<EPI>(p, b, row, n0 + c * 32, v);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
     }
+    if (tma_c && lane == 0) bulk_wait_group_all();  // C written before the CTA retires
   }
   tc_fence_before();
   __syncthreads();
@@ -628,7 +705,8 @@ static cudaError_t dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, c
 
 template <bool A_MN, bool B_MN, int EPI>
 static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-                                    cudaStream_t stream) {
+                                    cudaStream_t stream, const CUtensorMap* tc) {
+  static_assert(G2_SMEM + 1024 <= 232448, "2-CTA GEMM: dynamic + static shared memory");
   auto kern = gemm_tcgen05_pair_kernel<A_MN, B_MN, EPI>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -637,17 +715,18 @@ static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb
   }
   const int num_tiles = ((p.M + 255) / 256) * ((p.N + G2_BN - 1) / G2_BN) * p.batch;
   const int grid = std::max(2, std::min(2 * num_tiles, (num_sms() / 2) * 2));
-  kern<<<grid, GEMM_THREADS, G2_SMEM, stream>>>(ta, tb, p);
+  kern<<<grid, GEMM_THREADS, G2_SMEM, stream>>>(ta, tb, tc != nullptr ? *tc : ta, p);
   return cudaGetLastError();
 }
 
 template <int EPI>
 static cudaError_t dispatch_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                                 const GemmParams& p, cudaStream_t s) {
-  if (!a_mn && !b_mn) return launch_gemm_pair<false, false, EPI>(ta, tb, p, s);
-  if (!a_mn && b_mn) return launch_gemm_pair<false, true, EPI>(ta, tb, p, s);
-  if (a_mn && !b_mn) return launch_gemm_pair<true, false, EPI>(ta, tb, p, s);
-  return launch_gemm_pair<true, true, EPI>(ta, tb, p, s);
+                                 const GemmParams& p, cudaStream_t s,
+                                  const CUtensorMap* tc) {
+  if (!a_mn && !b_mn) return launch_gemm_pair<false, false, EPI>(ta, tb, p, s, tc);
+  if (!a_mn && b_mn) return launch_gemm_pair<false, true, EPI>(ta, tb, p, s, tc);
+  if (a_mn && !b_mn) return launch_gemm_pair<true, false, EPI>(ta, tb, p, s, tc);
+  return launch_gemm_pair<true, true, EPI>(ta, tb, p, s, tc);
 }
 
 template <bool B_MN, int PEER>
@@ -705,16 +784,17 @@ cudaError_t gemm_peer_launch(const CUtensorMap& ta, const CUtensorMap& tb, const
 }
 
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int bn, bool a_mn,
-                        bool b_mn, int epi, cudaStream_t s) {
+                        bool b_mn, int epi, cudaStream_t s, const CUtensorMap* tc) {
+  if (p.c_tma != 0 && (bn != 0 || tc == nullptr)) return cudaErrorInvalidValue;  // TMA epilogue: 2-CTA kernel only
   if (epi == EPI_SWIGLU) {  // forward only (A and B K-major), 256-column tiles
     if (a_mn || b_mn || (bn != 0 && bn != 256) || p.N % 256 != 0) return cudaErrorInvalidValue;
-    return bn == 0 ? launch_gemm_pair<false, false, EPI_SWIGLU>(ta, tb, p, s)
+    return bn == 0 ? launch_gemm_pair<false, false, EPI_SWIGLU>(ta, tb, p, s, tc)
                    : launch_gemm<256, false, false, EPI_SWIGLU>(ta, tb, p, s);
   }
   if (bn == 0) {  // 2-CTA kernel (tensor maps built with 128-row / 64-row boxes per CTA)
-    if (epi == EPI_BF16) return dispatch_pair<EPI_BF16>(a_mn, b_mn, ta, tb, p, s);
-    if (epi == EPI_F32) return dispatch_pair<EPI_F32>(a_mn, b_mn, ta, tb, p, s);
-    return dispatch_pair<EPI_F32_ACC>(a_mn, b_mn, ta, tb, p, s);
+    if (epi == EPI_BF16) return dispatch_pair<EPI_BF16>(a_mn, b_mn, ta, tb, p, s, tc);
+    if (epi == EPI_F32) return dispatch_pair<EPI_F32>(a_mn, b_mn, ta, tb, p, s, tc);
+    return dispatch_pair<EPI_F32_ACC>(a_mn, b_mn, ta, tb, p, s, tc);
   }
   if (bn == 128) {
     if (epi == EPI_BF16) return dispatch_major<128, EPI_BF16>(a_mn, b_mn, ta, tb, p, s);

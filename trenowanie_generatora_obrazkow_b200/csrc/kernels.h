@@ -40,14 +40,17 @@ struct GemmParams {
   float alpha, beta;
   int* err;
   GemmPeer peer;
+  int c_tma;  // 1: the 2-CTA kernel writes C through the tensor map it is given (TMA store / reduce-add)
   // grouped mode (gemm_grouped_launch): A rows [offsets[g], offsets[g + 1]) use B batch g; C rows as A's
   const int* group_offsets;            // device [batch + 1], batch = groups (<= kMaxGroups)
   const float* row_scale;              // optional [M]: output row r scaled by row_scale[r]
 };
 constexpr int kMaxGroups = 256;
 // epi: 0 = bf16 store, 1 = fp32 store, 2 = fp32 accumulate (C += alpha * A B^T)
+// tc: tensor map of C ({N, M, batch}, box {32, 32, 1}; bf16 with 64-byte or fp32 with 128-byte swizzle) for the
+// 2-CTA kernel's TMA epilogue when p.c_tma is set.
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int bn, bool a_mn,
-                        bool b_mn, int epi, cudaStream_t s);
+                        bool b_mn, int epi, cudaStream_t s, const CUtensorMap* tc = nullptr);
 // Grouped GEMM with a device-side tile schedule (no host synchronisation on the group sizes): bf16 output,
 // A [M, K] K-major with the rows of group g at [offsets[g], offsets[g + 1]), B [groups, N, K] (or, b_mn, [groups, K, N]).
 cudaError_t gemm_grouped_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, bool b_mn,

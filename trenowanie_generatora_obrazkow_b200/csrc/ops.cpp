@@ -55,6 +55,28 @@ static CUtensorMap make_tmap_bf16_sw128(const void* base, uint64_t inner, uint64
   return m;
 }
 
+// 3-D map of a GEMM output C {N, M, batch} for the 2-CTA kernel's TMA epilogue: box {32, 32, 1}; bf16 rows of the
+// box are 64 bytes (64-byte swizzle), fp32 rows 128 bytes (128-byte swizzle). Returns false (no map) when C's base
+// or strides are not 16-byte aligned, in which case the kernel stores rows directly.
+static bool make_tmap_c(CUtensorMap* m, void* base, bool f32, uint64_t N, uint64_t M, uint64_t batch,
+                        uint64_t ldc, uint64_t bsc) {
+  const uint64_t es = f32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ldc * es) % 16 != 0) return false;
+  if (batch <= 1) bsc = ldc * M;
+  if ((bsc * es) % 16 != 0) return false;
+  cuuint64_t dims[3] = {N, M, batch};
+  cuuint64_t strides[2] = {ldc * es, bsc * es};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = tmap_encoder()(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base,
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+static bool g_gemm_tma_c = true;  // 2-CTA GEMM epilogue through TMA stores / reduce-adds
+void set_gemm_tma_epilogue(bool on) { g_gemm_tma_c = on; }
+
 // 4-D fp32 map of the dQ accumulator [B][Tq][Hq][hd] as {hd, Hq, Tq, B}, box {hd, 1, 32, 1}, no swizzle: the
 // backward kernel reduce-adds 32-query x hd tiles into it.
 static CUtensorMap make_tmap_dq(const float* base, uint64_t hd, uint64_t H, uint64_t T, uint64_t B) {
@@ -168,7 +190,11 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor C, bool a_mn, bool b_mn, c10::o
   p.beta = (float)beta;
   p.err = err_ptr(err);
   const int epi = out_f32 ? (accumulate ? 2 : 1) : 0;
-  TGO_CHECK_LAUNCH(gemm_launch(ta, tb, p, bn, a_mn, b_mn, epi, at::cuda::getCurrentCUDAStream()));
+  CUtensorMap tc;
+  p.c_tma = (use_pair && g_gemm_tma_c && p.D == nullptr &&
+             make_tmap_c(&tc, C.data_ptr(), out_f32, N, M, batch, p.ldc, p.bsc)) ? 1 : 0;
+  TGO_CHECK_LAUNCH(gemm_launch(ta, tb, p, bn, a_mn, b_mn, epi, at::cuda::getCurrentCUDAStream(),
+                               p.c_tma ? &tc : nullptr));
 }
 
 
@@ -219,7 +245,10 @@ void gemm_swiglu(at::Tensor A, at::Tensor B, at::Tensor C, at::Tensor err) {
   p.alpha = 1.f;
   p.err = err_ptr(err);
   TORCH_CHECK(reinterpret_cast<uintptr_t>(p.C) % 16 == 0, "gemm_swiglu: C alignment");
-  TGO_CHECK_LAUNCH(gemm_launch(ta, tb, p, use_pair ? 0 : 256, false, false, 3, at::cuda::getCurrentCUDAStream()));
+  CUtensorMap tc;
+  p.c_tma = (use_pair && g_gemm_tma_c && make_tmap_c(&tc, p.C, false, N / 2, M, 1, p.ldc, 0)) ? 1 : 0;
+  TGO_CHECK_LAUNCH(gemm_launch(ta, tb, p, use_pair ? 0 : 256, false, false, 3, at::cuda::getCurrentCUDAStream(),
+                               p.c_tma ? &tc : nullptr));
 }
 
 // Expert GEMM of the peer-memory MoE exchange (A [batch, M, K] K-major bf16 = the local receive buffer or local
@@ -943,6 +972,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_attention_fwd_split", &tgo::set_attention_fwd_split,
         "softmax warps per TMEM lane quarter in the tcgen05 attention forward (1 or 2)");
   m.def("set_attention_tc", &tgo::set_attention_tc, "use the tcgen05 attention forward (default) or mma.sync");
+  m.def("set_gemm_tma_epilogue", &tgo::set_gemm_tma_epilogue,
+        "2-CTA GEMM epilogue through TMA stores / reduce-adds (default) or per-row global stores");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");
   m.def("launch_count", &tgo::launch_count, "kernels launched by this extension so far");
   m.def("adanorm_fwd", &tgo::adanorm_fwd, "x_new = x + gate*y; h = rmsnorm(x_new)*w*(1+scale)+shift");

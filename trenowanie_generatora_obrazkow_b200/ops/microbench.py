@@ -301,12 +301,16 @@ def main(argv=None):
     p.add_argument("--small", action="store_true")
     p.add_argument("--no-library", action="store_true", help="time only our kernels (profiler captures)")
     p.add_argument("--gemm-pair", type=int, default=-1, help="1 / 0: force the 2-CTA GEMM on / off")
+    p.add_argument("--gemm-tma-epilogue", type=int, default=-1, help="1 / 0: force the 2-CTA GEMM's TMA epilogue "
+                   "on / off (per-row global stores)")
     p.add_argument("--attn-emu", default="", help="comma-separated settings of the attention forward's FMA-pipe "
                    "exponentials (eighths of the key pairs: 0, 2, 3, 4); every op runs once per setting")
     a = p.parse_args(argv)
     torch.manual_seed(0)
     if a.gemm_pair >= 0:
         ext().set_gemm_pair(bool(a.gemm_pair))
+    if a.gemm_tma_epilogue >= 0:
+        ext().set_gemm_tma_epilogue(bool(a.gemm_tma_epilogue))
     peaks = measured_peaks()
     table = cases(a.small)
     names = list(table) if a.op == "all" else a.op.split(",")
