@@ -56,11 +56,13 @@ def test_gemm_batched_strided():
     assert _rel(c, a.float() @ b.float()) < 1e-2
 
 
-@pytest.mark.parametrize("M,N,K,batch", [(4000, 2312, 512, 1), (1024, 2048, 256, 3)])
+@pytest.mark.parametrize("M,N,K,batch", [(4000, 2312, 512, 1), (1024, 2048, 256, 3), (200, 136, 72, 1),
+                                         (192, 264, 128, 2), (296, 88, 64, 1)])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, True)])
-def test_gemm_pair_tma_epilogue(M, N, K, batch, a_mn, b_mn):
-    """2-CTA GEMM whose epilogue writes C by TMA stores (clipped at ragged M / N edges, batched C) and fp32 TMA
-    reduce-adds, against the per-row store epilogue (bitwise) and the fp32 oracle."""
+def test_gemm_tma_epilogue(M, N, K, batch, a_mn, b_mn):
+    """GEMM whose epilogue writes C by TMA stores (clipped at ragged M / N edges, batched C) and fp32 TMA
+    reduce-adds, against the per-row store epilogue (bitwise) and the fp32 oracle; the first two shapes run the
+    2-CTA kernel, the others the 1-CTA kernel (128- and 256-column tiles)."""
     from trenowanie_generatora_obrazkow_b200.ops.gemm import gemm
     from trenowanie_generatora_obrazkow_b200.ops._ext import check_errors, ext
     torch.manual_seed(3)

@@ -189,11 +189,12 @@ def test_up_swiglu_fused_matches_separate_ops(M, D, H):
     assert fused.shape == (M, H) and err < 1e-2, err
 
 
-@pytest.mark.parametrize("emu", [0, 2, 3, 4])
+@pytest.mark.parametrize("emu,pingpong", [(0, False), (2, False), (3, False), (4, False), (0, True), (3, True)])
 @pytest.mark.parametrize("hd,T,logit_scale", [(128, 640, 1.0), (128, 300, 6.0), (64, 520, 3.0)])
-def test_attention_fwd_fma_exponentials(emu, hd, T, logit_scale):
-    """tcgen05 forward with `emu` eighths of its exponentials as FMA-pipe polynomials, against the fp32 oracle:
-    masked keys (-inf logits), wide logit ranges (running-max rescales, probabilities that underflow)."""
+def test_attention_fwd_fma_exponentials(emu, pingpong, hd, T, logit_scale):
+    """tcgen05 forward with `emu` eighths of its exponentials as FMA-pipe polynomials (and optionally the two
+    softmax groups taking turns), against the fp32 oracle: masked keys (-inf logits), wide logit ranges
+    (running-max rescales, probabilities that underflow)."""
     from trenowanie_generatora_obrazkow_b200.ops._ext import check_errors, err_buf, ext
     torch.manual_seed(5)
     B, H = 2, 3
@@ -203,12 +204,14 @@ def test_attention_fwd_fma_exponentials(emu, hd, T, logit_scale):
     kv_len = torch.tensor([T, T // 2 + 7], device="cuda", dtype=torch.int32)
     scale = hd ** -0.5
     ext().set_attention_fwd_emu(emu)
+    ext().set_attention_fwd_pingpong(pingpong)
     try:
         o, lse = ext().attention_fwd(q, k, v, kv_len, scale, None, err_buf(q.device))
         torch.cuda.synchronize()
         check_errors()
     finally:
-        ext().set_attention_fwd_emu(-1)  # back to the default
+        ext().set_attention_fwd_emu(-1)  # back to the defaults
+        ext().set_attention_fwd_pingpong(False)
     ref = R.attention(q.float().cpu(), k.float().cpu(), v.float().cpu(), kv_len.cpu(), scale)
     assert torch.isfinite(o).all()
     assert rel(o.cpu(), ref) < 1.5e-2

@@ -138,6 +138,7 @@ struct FwdBars {
   uint64_t p_full[NQ];                             // softmax wrote P_g(j) over S_g(j): one arrival per warp
   uint64_t pv_done[NQ];                            // one phase per P_g(j) V_j
   uint64_t o_free[NQ];                             // the epilogue read O_g of the item: 128 arrivals
+  uint64_t turn[NQ];                               // ping-pong: softmax group g may run its exponentials
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -186,7 +187,7 @@ __device__ __forceinline__ FwdItem fwd_item(const AttnParams& p, int item, int n
 template <int HD, int EMU>
 __global__ void __launch_bounds__(THREADS, 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, AttnParams p, int* err) {
+                        const __grid_constant__ CUtensorMap tmV, AttnParams p, int* err, int pingpong) {
   using L = FwdSmem<HD>;
   static_assert(sizeof(FwdBars) <= 512, "barrier block");
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -215,6 +216,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&bars->p_full[g], 4);
       mbar_init(&bars->pv_done[g], 1);
       mbar_init(&bars->o_free[g], 128);
+      mbar_init(&bars->turn[g], 4);
     }
     bars->abort_flag = 0;
     fence_barrier_init();
@@ -396,6 +398,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                                      : ((long long)w.b * p.Hq + w.h) * p.Tq + qpos;
     };
     int gt = 0;
+    // Ping-pong (optional): the two softmax groups take turns for their exponential phases (turn[g] completes when
+    // the other group finished its phase; group 1 hands group 0 the first turn), so each phase runs with the MUFU
+    // and issue slots of its SM sub-partitions to itself instead of interleaved with the other group's.
+    int turns = 0;
+    if (pingpong && g == 1 && lane == 0) mbar_arrive(&bars->turn[0]);
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       int n, key_lim;
       {
@@ -456,6 +463,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         const float mu = (m == -INFINITY) ? 0.f : m;
         // per key pair: one packed FMA (scale, subtract the max), two exponentials (MUFU, or the FMA-pipe
         // polynomial for EMU of every 8 pairs), one packed add into the row sum, one bf16x2 pack
+        if (pingpong) {
+          if (!warp_wait(&bars->turn[g], turns & 1)) {
+            ok = false;
+            break;
+          }
+          ++turns;
+        }
         const uint64_t sl2x2 = f2(sl2, sl2), nmu2 = f2(-mu, -mu);
         uint64_t rs2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
 #pragma unroll
@@ -481,6 +495,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         f2_split(rs2[0], r0, r1);
         f2_split(rs2[1], r2, r3);
         l = l * corr + ((r0 + r1) + (r2 + r3));
+        if (pingpong) {  // hand the exponential unit to the other group
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->turn[1 - g]);
+        }
         ATTN_TRACE(tw, 25 + 4 * g, gj);
         // the other Q tile's P V may still read its A operand from TMEM: let it finish before any tcgen05.st here
         // (tile 0 waits for the P_1 V of the previous KV tile, tile 1 for the P_0 V of this one; the later P V of
@@ -556,6 +574,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+static int g_fwd_pingpong = 0;  // softmax groups alternate their exponential phases
+
 template <int HD, int EMU>
 static cudaError_t fwd_tc_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                const AttnParams& p, int* err, cudaStream_t s) {
@@ -570,7 +590,7 @@ static cudaError_t fwd_tc_impl(const CUtensorMap& tq, const CUtensorMap& tk, con
   if (items <= 0) return cudaSuccess;
   if (items >= (1ll << 31)) return cudaErrorInvalidValue;
   const int grid = (int)std::min<long long>(items, num_sms());
-  flash_fwd_tc_kernel<HD, EMU><<<grid, THREADS, L::TOTAL, s>>>(tq, tk, tv, p, err);
+  flash_fwd_tc_kernel<HD, EMU><<<grid, THREADS, L::TOTAL, s>>>(tq, tk, tv, p, err, g_fwd_pingpong);
   return cudaGetLastError();
 }
 
@@ -578,6 +598,11 @@ static cudaError_t fwd_tc_impl(const CUtensorMap& tq, const CUtensorMap& tk, con
 static int g_fwd_emu = kDefaultFwdEmu;
 
 cudaError_t attention_set_fwd_split(int wpq) { return wpq == 1 ? cudaSuccess : cudaErrorInvalidValue; }
+
+cudaError_t attention_set_fwd_pingpong(int on) {
+  g_fwd_pingpong = on ? 1 : 0;
+  return cudaSuccess;
+}
 
 cudaError_t attention_set_fwd_emu(int eighths) {  // -1: the built-in default
   if (eighths == -1) eighths = kDefaultFwdEmu;

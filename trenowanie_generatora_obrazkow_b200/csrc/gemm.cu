@@ -35,7 +35,8 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * GEMM_BK * 2;       // 16 or 32 KB
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = BN == 256 ? 4 : 6;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static constexpr int C_STAGE = 4096;  // TMA epilogue: one 32 x 32 staging tile per epilogue warp
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 4 * C_STAGE + 1024;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (256 or 512 columns)
 };
 
@@ -144,10 +145,61 @@ __device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int b, int
   }
 }
 
+// TMA epilogue of the GEMM kernels: a warp stages its 32 rows x 32 columns in shared memory in the tensor map's
+// swizzled layout (bf16: 64-byte rows, 64-byte swizzle; fp32: 128-byte rows, 128-byte swizzle; both conflict-free for
+// one 16-byte store per lane and phase), then one lane issues the TMA store (or, for the fp32 accumulate epilogue,
+// the TMA reduce-add, so the fp32 gradient bucket is never read by the SM). Per-row global stores from the epilogue
+// cost 32 L1 wavefronts per warp instruction on the same data path as the tensor core's shared-memory operand reads.
+template <int EPI>
+__device__ __forceinline__ void gemm_stage_chunk(const GemmParams& p, int row, uint8_t* buf, int lane,
+                                                 const uint32_t (&r)[32]) {
+  const float a = (p.row_scale != nullptr && row < p.M) ? p.alpha * p.row_scale[row] : p.alpha;
+  if constexpr (EPI == EPI_BF16) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 u;
+      u.x = pack_bf16x2(__uint_as_float(r[j * 8 + 0]) * a, __uint_as_float(r[j * 8 + 1]) * a);
+      u.y = pack_bf16x2(__uint_as_float(r[j * 8 + 2]) * a, __uint_as_float(r[j * 8 + 3]) * a);
+      u.z = pack_bf16x2(__uint_as_float(r[j * 8 + 4]) * a, __uint_as_float(r[j * 8 + 5]) * a);
+      u.w = pack_bf16x2(__uint_as_float(r[j * 8 + 6]) * a, __uint_as_float(r[j * 8 + 7]) * a);
+      *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = u;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 f;
+      f.x = __uint_as_float(r[j * 4 + 0]) * a;
+      f.y = __uint_as_float(r[j * 4 + 1]) * a;
+      f.z = __uint_as_float(r[j * 4 + 2]) * a;
+      f.w = __uint_as_float(r[j * 4 + 3]) * a;
+      *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = f;
+    }
+  }
+}
+__device__ __forceinline__ void gemm_stage_swiglu(uint8_t* buf, int lane, const uint32_t (&gt)[32],
+                                                  const uint32_t (&ut)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float a = __bfloat162float(__float2bfloat16(__uint_as_float(gt[j * 8 + e])));
+      const float u = __bfloat162float(__float2bfloat16(__uint_as_float(ut[j * 8 + e])));
+      o[e] = __bfloat162float(__float2bfloat16(a / (1.f + __expf(-a)))) * u;
+    }
+    uint4 w;
+    w.x = pack_bf16x2(o[0], o[1]);
+    w.y = pack_bf16x2(o[2], o[3]);
+    w.z = pack_bf16x2(o[4], o[5]);
+    w.w = pack_bf16x2(o[6], o[7]);
+    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = w;
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI, int PEER = PEER_NONE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        GemmParams p) {
+                        const __grid_constant__ CUtensorMap tmC, GemmParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -366,7 +418,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         } else if constexpr (PEER == GROUPED) {
           if (row < rows) gemm_store_chunk<EPI>(p, 0, row_base + row, n0 + c * 32, v);
         } else {
-          gemm_store_chunk<EPI>(p, b, row, n0 + c * 32, v);
+          if (p.c_tma != 0) {  // TMA epilogue (see gemm_stage_chunk), one staging tile per warp
+            uint8_t* buf = smem + STAGES * Cfg::STAGE_BYTES + q * Cfg::C_STAGE;
+            if (lane == 0) bulk_wait_group_read<0>();
+            __syncwarp();
+            gemm_stage_chunk<EPI>(p, row, buf, lane, v);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if constexpr (EPI == EPI_F32_ACC) tma_reduce_add_3d(&tmC, buf, n0 + c * 32, m0 + q * 32, b);
+              else tma_store_3d(&tmC, buf, n0 + c * 32, m0 + q * 32, b);
+              bulk_commit_group();
+            }
+          } else {
+            gemm_store_chunk<EPI>(p, b, row, n0 + c * 32, v);
+          }
         }
       }
       tc_fence_before();
@@ -382,6 +448,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       }
     }
+    if (PEER == PEER_NONE && p.c_tma != 0 && lane == 0) bulk_wait_group_all();  // C written before the CTA retires
   }
   tc_fence_before();
   __syncthreads();
@@ -391,57 +458,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 }
 
-
-// TMA epilogue of the 2-CTA kernel: a warp stages its 32 rows x 32 columns in shared memory in the tensor map's
-// swizzled layout (bf16: 64-byte rows, 64-byte swizzle; fp32: 128-byte rows, 128-byte swizzle; both conflict-free for
-// one 16-byte store per lane and phase), then one lane issues the TMA store (or, for the fp32 accumulate epilogue,
-// the TMA reduce-add, so the fp32 gradient bucket is never read by the SM). Per-row global stores from the epilogue
-// cost 32 L1 wavefronts per warp instruction on the same data path as the tensor core's shared-memory operand reads.
-template <int EPI>
-__device__ __forceinline__ void gemm_stage_chunk(const GemmParams& p, int row, uint8_t* buf, int lane,
-                                                 const uint32_t (&r)[32]) {
-  const float a = (p.row_scale != nullptr && row < p.M) ? p.alpha * p.row_scale[row] : p.alpha;
-  if constexpr (EPI == EPI_BF16) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 u;
-      u.x = pack_bf16x2(__uint_as_float(r[j * 8 + 0]) * a, __uint_as_float(r[j * 8 + 1]) * a);
-      u.y = pack_bf16x2(__uint_as_float(r[j * 8 + 2]) * a, __uint_as_float(r[j * 8 + 3]) * a);
-      u.z = pack_bf16x2(__uint_as_float(r[j * 8 + 4]) * a, __uint_as_float(r[j * 8 + 5]) * a);
-      u.w = pack_bf16x2(__uint_as_float(r[j * 8 + 6]) * a, __uint_as_float(r[j * 8 + 7]) * a);
-      *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = u;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float4 f;
-      f.x = __uint_as_float(r[j * 4 + 0]) * a;
-      f.y = __uint_as_float(r[j * 4 + 1]) * a;
-      f.z = __uint_as_float(r[j * 4 + 2]) * a;
-      f.w = __uint_as_float(r[j * 4 + 3]) * a;
-      *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = f;
-    }
-  }
-}
-__device__ __forceinline__ void gemm_stage_swiglu(uint8_t* buf, int lane, const uint32_t (&gt)[32],
-                                                  const uint32_t (&ut)[32]) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float o[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float a = __bfloat162float(__float2bfloat16(__uint_as_float(gt[j * 8 + e])));
-      const float u = __bfloat162float(__float2bfloat16(__uint_as_float(ut[j * 8 + e])));
-      o[e] = __bfloat162float(__float2bfloat16(a / (1.f + __expf(-a)))) * u;
-    }
-    uint4 w;
-    w.x = pack_bf16x2(o[0], o[1]);
-    w.y = pack_bf16x2(o[2], o[3]);
-    w.z = pack_bf16x2(o[4], o[5]);
-    w.w = pack_bf16x2(o[6], o[7]);
-    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = w;
-  }
-}
 
 // ----------------------------------------------------------------------------------------------------------------
 // 2-CTA variant: a cluster of two CTAs (one TPC) computes a 256 x 256 tile with tcgen05.mma.cta_group::2.
@@ -680,8 +696,10 @@ int num_sms() {
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
+static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream,
+                               const CUtensorMap* tc = nullptr) {
   using Cfg = GemmCfg<BN>;
+  static_assert(Cfg::SMEM + 1024 <= 232448, "GEMM: dynamic + static shared memory");
   auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, EPI>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -690,17 +708,18 @@ static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, con
   }
   const int num_tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * ((p.N + BN - 1) / BN) * p.batch;
   const int grid = std::max(1, std::min(num_tiles, num_sms()));
-  kern<<<grid, GEMM_THREADS, Cfg::SMEM, stream>>>(ta, tb, p);
+  kern<<<grid, GEMM_THREADS, Cfg::SMEM, stream>>>(ta, tb, tc != nullptr ? *tc : ta, p);
   return cudaGetLastError();
 }
 
 template <int BN, int EPI>
 static cudaError_t dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                                  const GemmParams& p, cudaStream_t s) {
-  if (!a_mn && !b_mn) return launch_gemm<BN, false, false, EPI>(ta, tb, p, s);
-  if (!a_mn && b_mn) return launch_gemm<BN, false, true, EPI>(ta, tb, p, s);
-  if (a_mn && !b_mn) return launch_gemm<BN, true, false, EPI>(ta, tb, p, s);
-  return launch_gemm<BN, true, true, EPI>(ta, tb, p, s);
+                                  const GemmParams& p, cudaStream_t s,
+                                   const CUtensorMap* tc) {
+  if (!a_mn && !b_mn) return launch_gemm<BN, false, false, EPI>(ta, tb, p, s, tc);
+  if (!a_mn && b_mn) return launch_gemm<BN, false, true, EPI>(ta, tb, p, s, tc);
+  if (a_mn && !b_mn) return launch_gemm<BN, true, false, EPI>(ta, tb, p, s, tc);
+  return launch_gemm<BN, true, true, EPI>(ta, tb, p, s, tc);
 }
 
 template <bool A_MN, bool B_MN, int EPI>
@@ -741,7 +760,7 @@ static cudaError_t launch_gemm_peer(const CUtensorMap& ta, const CUtensorMap& tb
     set = true;
   }
   const int tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * ((p.N + 255) / 256) * p.batch;
-  kern<<<std::min(tiles, num_sms()), GEMM_THREADS, Cfg::SMEM, s>>>(ta, tb, p);
+  kern<<<std::min(tiles, num_sms()), GEMM_THREADS, Cfg::SMEM, s>>>(ta, tb, ta, p);
   return cudaGetLastError();
 }
 
@@ -760,7 +779,7 @@ cudaError_t gemm_grouped_launch(const CUtensorMap& ta, const CUtensorMap& tb, co
   // the tile count is known on the device only: a persistent grid, bounded by the worst case
   const long long worst = ((long long)(p.M + GEMM_BM - 1) / GEMM_BM + p.batch) * ((p.N + 255) / 256);
   const int grid = (int)std::max(1LL, std::min<long long>(worst, num_sms()));
-  kern<<<grid, GEMM_THREADS, Cfg::SMEM, s>>>(ta, tb, p);
+  kern<<<grid, GEMM_THREADS, Cfg::SMEM, s>>>(ta, tb, ta, p);
   return cudaGetLastError();
 }
 
@@ -785,11 +804,11 @@ cudaError_t gemm_peer_launch(const CUtensorMap& ta, const CUtensorMap& tb, const
 
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int bn, bool a_mn,
                         bool b_mn, int epi, cudaStream_t s, const CUtensorMap* tc) {
-  if (p.c_tma != 0 && (bn != 0 || tc == nullptr)) return cudaErrorInvalidValue;  // TMA epilogue: 2-CTA kernel only
+  if (p.c_tma != 0 && tc == nullptr) return cudaErrorInvalidValue;  // TMA epilogue needs C's tensor map
   if (epi == EPI_SWIGLU) {  // forward only (A and B K-major), 256-column tiles
     if (a_mn || b_mn || (bn != 0 && bn != 256) || p.N % 256 != 0) return cudaErrorInvalidValue;
     return bn == 0 ? launch_gemm_pair<false, false, EPI_SWIGLU>(ta, tb, p, s, tc)
-                   : launch_gemm<256, false, false, EPI_SWIGLU>(ta, tb, p, s);
+                   : launch_gemm<256, false, false, EPI_SWIGLU>(ta, tb, p, s);  // row stores (c_tma unused)
   }
   if (bn == 0) {  // 2-CTA kernel (tensor maps built with 128-row / 64-row boxes per CTA)
     if (epi == EPI_BF16) return dispatch_pair<EPI_BF16>(a_mn, b_mn, ta, tb, p, s, tc);
@@ -797,13 +816,13 @@ cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
     return dispatch_pair<EPI_F32_ACC>(a_mn, b_mn, ta, tb, p, s, tc);
   }
   if (bn == 128) {
-    if (epi == EPI_BF16) return dispatch_major<128, EPI_BF16>(a_mn, b_mn, ta, tb, p, s);
-    if (epi == EPI_F32) return dispatch_major<128, EPI_F32>(a_mn, b_mn, ta, tb, p, s);
-    return dispatch_major<128, EPI_F32_ACC>(a_mn, b_mn, ta, tb, p, s);
+    if (epi == EPI_BF16) return dispatch_major<128, EPI_BF16>(a_mn, b_mn, ta, tb, p, s, tc);
+    if (epi == EPI_F32) return dispatch_major<128, EPI_F32>(a_mn, b_mn, ta, tb, p, s, tc);
+    return dispatch_major<128, EPI_F32_ACC>(a_mn, b_mn, ta, tb, p, s, tc);
   }
-  if (epi == EPI_BF16) return dispatch_major<256, EPI_BF16>(a_mn, b_mn, ta, tb, p, s);
-  if (epi == EPI_F32) return dispatch_major<256, EPI_F32>(a_mn, b_mn, ta, tb, p, s);
-  return dispatch_major<256, EPI_F32_ACC>(a_mn, b_mn, ta, tb, p, s);
+  if (epi == EPI_BF16) return dispatch_major<256, EPI_BF16>(a_mn, b_mn, ta, tb, p, s, tc);
+  if (epi == EPI_F32) return dispatch_major<256, EPI_F32>(a_mn, b_mn, ta, tb, p, s, tc);
+  return dispatch_major<256, EPI_F32_ACC>(a_mn, b_mn, ta, tb, p, s, tc);
 }
 
 }  // namespace tgo

@@ -40,7 +40,7 @@ struct GemmParams {
   float alpha, beta;
   int* err;
   GemmPeer peer;
-  int c_tma;  // 1: the 2-CTA kernel writes C through the tensor map it is given (TMA store / reduce-add)
+  int c_tma;  // 1: the kernel writes C through the tensor map it is given (TMA store / reduce-add)
   // grouped mode (gemm_grouped_launch): A rows [offsets[g], offsets[g + 1]) use B batch g; C rows as A's
   const int* group_offsets;            // device [batch + 1], batch = groups (<= kMaxGroups)
   const float* row_scale;              // optional [M]: output row r scaled by row_scale[r]
@@ -48,7 +48,7 @@ struct GemmParams {
 constexpr int kMaxGroups = 256;
 // epi: 0 = bf16 store, 1 = fp32 store, 2 = fp32 accumulate (C += alpha * A B^T)
 // tc: tensor map of C ({N, M, batch}, box {32, 32, 1}; bf16 with 64-byte or fp32 with 128-byte swizzle) for the
-// 2-CTA kernel's TMA epilogue when p.c_tma is set.
+// TMA epilogue when p.c_tma is set (not for the SwiGLU epilogue of the 1-CTA kernel).
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int bn, bool a_mn,
                         bool b_mn, int epi, cudaStream_t s, const CUtensorMap* tc = nullptr);
 // Grouped GEMM with a device-side tile schedule (no host synchronisation on the group sizes): bf16 output,
@@ -267,7 +267,8 @@ cudaError_t moe_release_launch(uint32_t* const* free_peer, int rank, int world, 
 
 cudaError_t attention_set_trace(long long* buf, int cta);  // profiling timeline (null: off)
 cudaError_t attention_set_fwd_split(int wpq);  // softmax warps per TMEM lane quarter in the forward (1 or 2)
-cudaError_t attention_set_fwd_emu(int eighths);  // forward exponentials on the FMA pipe: 0, 2, 3 or 4 eighths
+cudaError_t attention_set_fwd_emu(int eighths);
+cudaError_t attention_set_fwd_pingpong(int on);  // forward softmax groups alternate their exponential phases  // forward exponentials on the FMA pipe: 0, 2, 3 or 4 eighths
 cudaError_t muon_rs_launch(const MuonRSParams& p, int blocks, cudaStream_t s);
 cudaError_t muon_momentum_launch(const MuonMomentumParams& p, cudaStream_t s);
 cudaError_t muon_ag_apply_launch(const MuonAGParams& p, int blocks, cudaStream_t s);

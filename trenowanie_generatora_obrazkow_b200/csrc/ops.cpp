@@ -55,7 +55,7 @@ static CUtensorMap make_tmap_bf16_sw128(const void* base, uint64_t inner, uint64
   return m;
 }
 
-// 3-D map of a GEMM output C {N, M, batch} for the 2-CTA kernel's TMA epilogue: box {32, 32, 1}; bf16 rows of the
+// 3-D map of a GEMM output C {N, M, batch} for the GEMM kernels' TMA epilogue: box {32, 32, 1}; bf16 rows of the
 // box are 64 bytes (64-byte swizzle), fp32 rows 128 bytes (128-byte swizzle). Returns false (no map) when C's base
 // or strides are not 16-byte aligned, in which case the kernel stores rows directly.
 static bool make_tmap_c(CUtensorMap* m, void* base, bool f32, uint64_t N, uint64_t M, uint64_t batch,
@@ -74,7 +74,7 @@ static bool make_tmap_c(CUtensorMap* m, void* base, bool f32, uint64_t N, uint64
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
-static bool g_gemm_tma_c = true;  // 2-CTA GEMM epilogue through TMA stores / reduce-adds
+static bool g_gemm_tma_c = true;  // GEMM epilogue through TMA stores / reduce-adds
 void set_gemm_tma_epilogue(bool on) { g_gemm_tma_c = on; }
 
 // 4-D fp32 map of the dQ accumulator [B][Tq][Hq][hd] as {hd, Hq, Tq, B}, box {hd, 1, 32, 1}, no swizzle: the
@@ -115,6 +115,7 @@ void set_attention_tc(bool on) { g_attention_tc = on; }
 void set_attention_fwd_split(int64_t wpq) {
   TORCH_CHECK(attention_set_fwd_split((int)wpq) == cudaSuccess, "attention forward split: 1 or 2");
 }
+void set_attention_fwd_pingpong(bool on) { attention_set_fwd_pingpong(on ? 1 : 0); }
 void set_attention_fwd_emu(int64_t eighths) {
   TORCH_CHECK(attention_set_fwd_emu((int)eighths) == cudaSuccess, "attention forward FMA exponentials: 0, 2, 3, 4 (-1: default)");
 }
@@ -191,7 +192,7 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor C, bool a_mn, bool b_mn, c10::o
   p.err = err_ptr(err);
   const int epi = out_f32 ? (accumulate ? 2 : 1) : 0;
   CUtensorMap tc;
-  p.c_tma = (use_pair && g_gemm_tma_c && p.D == nullptr &&
+  p.c_tma = (g_gemm_tma_c && p.D == nullptr &&
              make_tmap_c(&tc, C.data_ptr(), out_f32, N, M, batch, p.ldc, p.bsc)) ? 1 : 0;
   TGO_CHECK_LAUNCH(gemm_launch(ta, tb, p, bn, a_mn, b_mn, epi, at::cuda::getCurrentCUDAStream(),
                                p.c_tma ? &tc : nullptr));
@@ -967,13 +968,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("muon_rs", &tgo::muon_rs, "sharded Muon: gradient bucket reduce-scatter to the matrix owners (NVLink)");
   m.def("muon_momentum", &tgo::muon_momentum, "sharded Muon: owner momentum + Nesterov -> bf16 NS input");
   m.def("muon_ag_apply", &tgo::muon_ag_apply, "sharded Muon: update all-gather fused with the parameter update");
+  m.def("set_attention_fwd_pingpong", &tgo::set_attention_fwd_pingpong,
+        "attention forward: the two softmax groups take turns for their exponential phases");
   m.def("set_attention_fwd_emu", &tgo::set_attention_fwd_emu,
         "eighths of the key pairs whose forward exponentials run as FMA-pipe polynomials (0, 2, 3, 4)");
   m.def("set_attention_fwd_split", &tgo::set_attention_fwd_split,
         "softmax warps per TMEM lane quarter in the tcgen05 attention forward (1 or 2)");
   m.def("set_attention_tc", &tgo::set_attention_tc, "use the tcgen05 attention forward (default) or mma.sync");
   m.def("set_gemm_tma_epilogue", &tgo::set_gemm_tma_epilogue,
-        "2-CTA GEMM epilogue through TMA stores / reduce-adds (default) or per-row global stores");
+        "GEMM epilogue through TMA stores / reduce-adds (default) or per-row global stores");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");
   m.def("launch_count", &tgo::launch_count, "kernels launched by this extension so far");
   m.def("adanorm_fwd", &tgo::adanorm_fwd, "x_new = x + gate*y; h = rmsnorm(x_new)*w*(1+scale)+shift");

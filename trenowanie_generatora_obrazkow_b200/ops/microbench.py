@@ -303,6 +303,8 @@ def main(argv=None):
     p.add_argument("--gemm-pair", type=int, default=-1, help="1 / 0: force the 2-CTA GEMM on / off")
     p.add_argument("--gemm-tma-epilogue", type=int, default=-1, help="1 / 0: force the 2-CTA GEMM's TMA epilogue "
                    "on / off (per-row global stores)")
+    p.add_argument("--attn-pingpong", default="", help="comma-separated 0 / 1: attention forward softmax groups "
+                   "alternate their exponential phases; every op runs once per setting (and per --attn-emu)")
     p.add_argument("--attn-emu", default="", help="comma-separated settings of the attention forward's FMA-pipe "
                    "exponentials (eighths of the key pairs: 0, 2, 3, 4); every op runs once per setting")
     a = p.parse_args(argv)
@@ -316,14 +318,19 @@ def main(argv=None):
     names = list(table) if a.op == "all" else a.op.split(",")
     rows = []
     settings = [int(v) for v in a.attn_emu.split(",")] if a.attn_emu else [None]
-    for emu in settings:
+    pps = [int(v) for v in a.attn_pingpong.split(",")] if a.attn_pingpong else [None]
+    for emu, pp in [(e, q) for q in pps for e in settings]:
         if emu is not None:
             ext().set_attention_fwd_emu(emu)
+        if pp is not None:
+            ext().set_attention_fwd_pingpong(bool(pp))
         for n in names:
             ours, lib, flops, nbytes = table[n]()
             row = report(n, ours, lib, flops, nbytes, a.iters, a.warmup, peaks, not a.no_library)
             if emu is not None:
                 row["attn_emu"] = emu
+            if pp is not None:
+                row["attn_pingpong"] = pp
             from ._ext import check_errors
             check_errors()
             print(json.dumps(row), flush=True)
