@@ -61,3 +61,65 @@ def test_opd_with_lm_server_text_lookahead(tmp_path):
                     "--opd-rollout-steps", "2", "--teacher-size", "nano", "--random-lm", "--lm-layers", "2",
                     "--lm-rank", "1", "--opd-text-ahead", "2")
     assert "step 3/3" in out and "[lm server 2] served" in out
+
+
+def _torchrun_rc(n, *args):
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", str(n),
+           "--master-addr", "127.0.0.1", "--master-port", str(_port()), os.path.join(ROOT, "train_pp.py"), *args]
+    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=600,
+                       env=dict(os.environ, CUDA_VISIBLE_DEVICES="", DIST_BACKEND="gloo"))
+    return r.returncode, r.stdout + r.stderr
+
+
+def test_pipeline_shards_checkpoint_and_resume(tmp_path):
+    """--data shards (latents + caption rows through a frozen LM), latest.pt in the single-model layout (loads into
+    the unsplit modules), per-rank optimizer files, resume at the same pipeline layout and, only with
+    --resume-opt-mismatch, at another one."""
+    import torch
+
+    from trenowanie_generatora_obrazkow_b200.data.shards import write_synthetic_shards
+    from trenowanie_generatora_obrazkow_b200.models import DenoiserConfig, build_models
+    from trenowanie_generatora_obrazkow_b200.models.config import te_config_from_dict
+    from trenowanie_generatora_obrazkow_b200.utils.checkpoint import load_weights
+    import glob
+    data = str(tmp_path / "shards")
+    write_synthetic_shards(data, n_shards=3, per_shard=8, side=8)
+    import shutil
+    for f in glob.glob(os.path.join(data, "*.lat.npy")):  # 8 x 8 latents serve as the 128 px grids (.lat128.npy)
+        shutil.copy(f, f[: -len(".lat.npy")] + ".lat128.npy")
+    out = str(tmp_path / "run")
+    common = ["--out", out, "--data", data, "--fraction", "1", "--size", "nano", "--te-size", "states-nano",
+              "--microbatches", "2", "--micro-batch", "2", "--res", "128", "--log-every", "1", "--random-lm",
+              "--lm-layers", "2", "--ckpt-every", "2", "--workers", "0", "--keep-ckpt-steps", "2"]
+    log = _torchrun(2, *common, "--pp", "2", "--steps", "2")
+    assert "step 2/2" in log
+    ck = torch.load(os.path.join(out, "latest.pt"), weights_only=False)
+    assert ck["step"] == 2 and ck["samples"] == 8 and len(ck["ema"]) == len(ck["te"]) + len(ck["den"])
+    te, den = build_models(DenoiserConfig(**ck["den_config"]), te_config_from_dict(ck["te_config"]))
+    load_weights(ck, te, den)  # strict: every parameter of the unsplit model, under its own name
+    assert all(os.path.exists(os.path.join(out, f)) for f in ("opt_stage0_rep0.pt", "opt_stage1_rep0.pt",
+                                                              "step_0000002.pt"))
+    log = _torchrun(2, *common, "--pp", "2", "--steps", "4")
+    assert "resumed" in log and "step 4/4" in log
+    rc, msg = _torchrun_rc(1, *common, "--pp", "1", "--steps", "5")
+    assert rc != 0 and "resume-opt-mismatch" in msg
+    log = _torchrun(1, *common, "--pp", "1", "--steps", "5", "--resume-opt-mismatch")
+    assert "fresh" in log and "step 5/5" in log
+
+
+def test_pipeline_flags_stage0_lm_profile_and_unsupported(tmp_path):
+    """--lm-stage0, --te-checkpoint, --bench, --mem-debug and the profiler window; flags the pipeline trainer does
+    not run stop it with a pointer to train.py."""
+    prof = str(tmp_path / "prof")
+    log = _torchrun(2, "--out", str(tmp_path / "a"), "--size", "nano", "--te-size", "states-nano", "--pp", "2",
+                    "--microbatches", "2", "--micro-batch", "2", "--res", "128", "--steps", "3", "--log-every", "3",
+                    "--random-lm", "--lm-layers", "2", "--lm-stage0", "--te-checkpoint", "--bench", "--mem-debug",
+                    "--profile-dir", prof, "--profile-start", "1", "--profile-steps", "1", "--synthetic", "64")
+    assert "step 3/3" in log and "[bench]" in log and "memory:" in log
+    assert os.path.exists(os.path.join(prof, "kernels_rank0.json"))
+    rc, msg = _torchrun_rc(1, "--out", str(tmp_path / "b"), "--size", "nano", "--te-size", "states-nano",
+                           "--steps", "1", "--diloco", "4")
+    assert rc != 0 and "use train.py" in msg
+    rc, msg = _torchrun_rc(1, "--out", str(tmp_path / "c"), "--size", "nano", "--te-size", "states-nano",
+                           "--steps", "1", "--klein")
+    assert rc != 0 and "unavailable on this box" in msg

@@ -29,10 +29,16 @@ from trenowanie_generatora_obrazkow_b200.utils import checkpoint as ckpt
 
 
 def build_parser():
-    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    """train.py's flags (the reference's train_pp.py takes train.py's parser and adds its own, train_pp.py:79-268),
+    then the pipeline / OPD / service-rank flags; where both define a flag, this file's definition wins."""
+    import train as train_cli
+    p = train_cli.build_parser()
+    p.description = __doc__
+    for container in [p] + list(p._action_groups):  # a definition below replaces train.py's of the same flag
+        container.conflict_handler = "resolve"
     a = p.add_argument
     a("--out", required=True)
-    a("--data", default="data/aurora")
+    a("--data", default="data/aurora", help="shard directory (latents + LM caption rows); --synthetic N skips it")
     a("--synthetic", type=int, default=0)
     a("--size", default="1.5b", choices=sorted(SIZES))
     a("--depth", type=int, default=None)
@@ -44,6 +50,8 @@ def build_parser():
     a("--micro-batch", type=int, default=4)
     a("--te-cost", type=float, default=1.0, help="text encoder + stem cost in blocks (stage balancing)")
     a("--act-checkpoint", action="store_true")
+    a("--te-checkpoint", action="store_true", help="recompute the text encoder in the backward (with --act-checkpoint "
+      "the whole first stage is recomputed already)")
     a("--steps", type=int, default=100)
     a("--lr-muon", type=float, default=1e-2)
     a("--lr-adam", type=float, default=3e-4)
@@ -53,8 +61,25 @@ def build_parser():
     a("--clip", type=float, default=1.0)
     a("--seed", type=int, default=0)
     a("--log-every", type=int, default=10)
-    a("--ckpt-every", type=int, default=0)
+    a("--ckpt-every", type=int, default=0, help="write latest.pt (+ per-rank optimizer files) every N steps")
+    a("--keep-ckpt-steps", type=int, nargs="*", default=[], help="keep latest.pt of these steps as step_<n>.pt")
+    a("--resume-opt-mismatch", action="store_true",
+      help="resume weights / EMA from latest.pt with fresh optimizer state when the pipeline layout changed")
+    a("--lat-dir", default="", help="latents from this directory (shard names as in --data)")
+    a("--val-per-shard", action="store_true", help="(train.py's per-shard validation; not run by the pipeline trainer)")
+    a("--lm-stage0", action="store_true", help="the frozen LM runs on stage 0 only (default: micro-batch k on stage "
+      "k %% pp, gathered to stage 0)")
+    a("--masked-attention-backend", default="tcgen05", choices=["tcgen05", "sdpa", "flex", "cudnn"],
+      help="accepted for the reference's launch lines; the masked (caption) attention is always this framework's "
+           "tcgen05 kernel")
+    a("--bench", action="store_true", help="print per-step wall time and latent tokens / s")
     a("--dist-timeout", type=float, default=120.0, help="minutes")
+    a("--mem-debug", action="store_true", help="print the memory breakdown after the first step")
+    a("--mem-snapshot", default="", help="on an out-of-memory error, dump the CUDA allocator snapshot here")
+    a("--profile-dir", default="", help="torch.profiler traces and kernel tables of --profile-steps steps")
+    a("--profile-start", type=int, default=2)
+    a("--profile-steps", type=int, default=2)
+    a("--profile-ranks", type=int, nargs="*", default=[0])
     # OPD
     a("--dance-opd", action="store_true")
     a("--diffusion-opd", action="store_true")
@@ -66,15 +91,30 @@ def build_parser():
     a("--opd-state-weighting", action="store_true")
     a("--opd-resolutions", type=int, nargs="*", default=())
     a("--opd-res-weights", type=float, nargs="*", default=())
+    a("--opd-res-shifts", type=float, nargs="*", default=(), help="time shift per --opd-resolutions entry")
+    a("--opd-res-batches", type=int, nargs="*", default=(), help="images per learner per --opd-resolutions entry")
+    a("--opd-res-mb", type=int, nargs="*", default=(), help="micro-batch per --opd-resolutions entry")
     a("--opd-token-batch", action="store_true")
     a("--opd-actor", action="store_true", help="dedicated rollout-actor rank(s) (one per --opd-actor-gpus entry)")
     a("--opd-actor-gpus", type=int, nargs="*", default=[], help="GPUs of the rollout actors (nvidia-smi numbers)")
+    a("--opd-actor-gpu", type=int, default=-1, help="a single rollout actor's GPU (same as --opd-actor-gpus N)")
     a("--opd-text-ahead", type=int, default=0,
       help="OPD: encode this many future caption batches per learner on the LM server (CPU queue, needs --lm-rank)")
+    a("--opd-learner-profile", action="store_true", help="print the learner's per-phase times every log step")
+    a("--opd-actor-profile", action="store_true", help="print the actor's per-job times")
+    a("--opd-captions-only", action="store_true", help="OPD reads only captions from the shards (no latents)")
+    a("--opd-balance-rollouts", action="store_true", help="round-robin the learners' rollout jobs over the actors")
+    a("--opd-sort-rollouts", action="store_true", help="caption-length-sorted rollout batches")
+    a("--opd-prefetch", action="store_true", help="(rollout prefetch; not run here: rollouts are requested when the "
+      "replay budget of the cached ones is spent)")
+    a("--opd-parts", type=int, default=1, help="split each rollout batch into this many teacher requests")
     a("--teacher-ranks", type=int, default=0)
     a("--teacher-size", default="teacher-4b", choices=sorted(SIZES))
     a("--teacher-ckpt", default="")
     a("--teacher-gpu", type=int, default=-1)
+    a("--klein", action="store_true", help="FLUX.2-klein teacher (diffusers + weights; unavailable offline)")
+    a("--klein-quant", default="", help="klein teacher weight quantization (with --klein)")
+    a("--teacher-on-lm", action="store_true", help="the klein teacher shares the LM server's GPU (with --klein)")
     # frozen LM / VAE placement
     a("--lm-rank", type=int, default=0, help="dedicated LM server ranks (after the learners, actors and teachers)")
     a("--lm-gpu", type=int, default=-1, help="GPU of the (last) LM server")
@@ -83,11 +123,48 @@ def build_parser():
     a("--vae-gpu", type=int, default=-1)
     a("--vae-on-lm", action="store_true", help="the LM server also encodes the learners' images")
     a("--vae", default="", help="FLUX.2 VAE directory (default: the PatchEncoder stand-in)")
+    a("--enc-vae", default="", help="encode --img-dir images with this VAE directory (same as --vae)")
+    a("--enc-chunk", type=int, default=64, help="images per VAE encode call")
+    a("--img-dir", default="", help="train on packed images (<shard>.img.bin) from this directory, VAE-encoded "
+      "in the loop (on the VAE / LM server with --vae-rank / --vae-on-lm, else locally)")
+    a("--img-extra", default="", help="(a second image directory; not run by the pipeline trainer)")
+    a("--img-extra-val", action="store_true", help="(validation on --img-extra; not run by the pipeline trainer)")
+    a("--vae-remote-frac", type=float, default=1.0,
+      help="fraction of the images encoded on the VAE server (the rest locally on stage 0)")
     a("--skip-gpus", type=int, nargs="*", default=[])
     a("--random-lm", action="store_true",
       help="caption ids through a random-init Slayer-shaped LM of the encoder's width (no pretrained weights)")
     a("--lm-layers", type=int, default=4, help="--random-lm: LM depth")
     return p
+
+
+# train.py flags the pipeline trainer does not run; they stop the run when set away from their defaults
+UNSUPPORTED = dict(diloco=(0, "DiLoCo / MuLoCo outer steps"), repa_weight=(0.0, "REPA"), offload=(False, "offload"),
+                   multi_res=([], "mixed-resolution steps (the reference needs --pp 1 for them too)"),
+                   eval_only=(False, "--eval-only"), freeze_den=(False, "--freeze-den"), te_experts=(None, "MoE text "
+                   "encoder"), te_quant=(None, "quantized text encoder"), pl_prob=(0.0, "Polish captions"),
+                   rope_random=(False, "RPE-2D random positions"), length_sort=(False, "--length-sort"),
+                   val_per_shard=(False, "validation per shard group (train.py --eval-every)"),
+                   img_extra=("", "a second image directory"), img_extra_val=(False, "validation on --img-extra"),
+                   opd_prefetch=(False, "rollout prefetch"))
+
+
+def check_flags(args):
+    for dest, (default, what) in UNSUPPORTED.items():
+        if hasattr(args, dest) and getattr(args, dest) != default:
+            raise SystemExit(f"train_pp.py: {what} is not run by the pipeline trainer here; use train.py")
+    if args.grad_comm == "powersgd":
+        raise SystemExit("train_pp.py: PowerSGD gradient compression is not run by the pipeline trainer; use train.py")
+    if args.klein or args.klein_quant or args.teacher_on_lm:
+        raise SystemExit("train_pp.py: the FLUX.2-klein teacher is unavailable on this box (no diffusers, no "
+                         "weights); use a DiT teacher (--teacher-size / --teacher-ckpt)")
+    if args.opd_actor_gpu >= 0:
+        args.opd_actor = True
+        args.opd_actor_gpus = list(args.opd_actor_gpus) or [args.opd_actor_gpu]
+    if args.enc_vae and not args.vae:
+        args.vae = args.enc_vae
+    assert not args.crop_res or args.micro_cond, "--crop-res needs --micro-cond"
+    return args
 
 
 def actor_count(args):
@@ -144,7 +221,7 @@ def serve(args, role, lay, te_cfg, device, ctl, text_group, pp):
 
 
 def main():
-    args = build_parser().parse_args()
+    args = check_flags(build_parser().parse_args())
     from datetime import timedelta
 
     from trenowanie_generatora_obrazkow_b200.parallel.placement import RankLayout, local_device
@@ -167,7 +244,15 @@ def main():
         print(f"rank {rank} ({role}): GPU {device.index}, PCI bus {bus:02X}", flush=True)
     den_cfg, te_cfg = make_configs(args.size, args.te_size, depth=args.depth)
     side = args.res // 16
-    den_cfg = replace(den_cfg, latent_size=side)
+    den_cfg = replace(den_cfg, latent_size=side, rope_ref=args.rope_ref, micro_cond=args.micro_cond)
+    latest = os.path.join(args.out, "latest.pt")
+    if os.path.exists(latest):  # the checkpoint's architecture wins (reference train_pp.py:1453-1460)
+        from trenowanie_generatora_obrazkow_b200.models import DenoiserConfig as _DC
+        from trenowanie_generatora_obrazkow_b200.models.config import te_config_from_dict
+        ck = ckpt.load(latest)
+        den_cfg = replace(_DC(**ck["den_config"]), latent_size=side)
+        te_cfg = te_config_from_dict(ck["te_config"])
+        del ck
     # control planes (Gloo, any-source headers; CPU text jobs): every rank creates them, in the same order
     ctl = dist.new_group(backend="gloo")
     text_group = dist.new_group(backend="gloo")
@@ -191,6 +276,10 @@ def fm_text(args, tr, lm, lm_client, ids_all, M, mb, width):
     base, s, pp = tr.replica * tr.pp, tr.stage, tr.pp
     if args.lm_rank:  # stage 0 holds the client
         return lm_client.collect(lm_client.request(ids_all)) if tr.first else None
+    if args.lm_stage0:  # the whole LM on stage 0
+        if not tr.first:
+            return None
+        return torch.cat([lm.states(c.to(tr.device)).to(torch.bfloat16) for c in ids_all.split(mb)]).contiguous()
     chunks = list(ids_all.split(mb))
     if args.lm_split:
         nb = len(lm.model.blocks)
@@ -204,32 +293,92 @@ def fm_text(args, tr, lm, lm_client, ids_all, M, mb, width):
     return torch.cat(outs) if outs is not None else None
 
 
+def shard_loader(args, te_cfg, den_cfg, mb, replica, dp, start_micro, with_data):
+    """Micro-batches of --data (or --img-dir) for one replica: every stage of the replica walks the same sample and
+    caption choices (TrainStream seeded by (seed, replica)); stage 0 also reads latents (or images) and
+    micro-conditions, the others only caption rows."""
+    from trenowanie_generatora_obrazkow_b200.data.shards import ShardStore, TrainStream, select_shards
+    from trenowanie_generatora_obrazkow_b200.models.text import build_text_encoder
+    root = args.img_dir or args.data
+    tok_suffix = getattr(te_cfg, "tok_suffix", "")
+    with torch.device("meta"):
+        null_row = build_text_encoder(te_cfg).null_ids()
+    names, _ = select_shards(root, args.fraction, tok_suffix)
+    side = args.res // 16
+    kw = dict(lat_kind="lat" if side == 16 else f"lat{args.res}", lat_root=args.lat_dir)
+    if with_data:
+        kw.update(crops=[("lat" if r == 256 else f"lat{r}", "") for r in args.crop_res], crop_prob=args.crop_prob,
+                  cond_base=den_cfg.micro_cond, img_res=args.res if args.img_dir else 0)
+        if args.img_dir:
+            kw.pop("crops"), kw.pop("crop_prob")
+    store = ShardStore(root, names, tok_suffix, null_row, **kw)
+    stream = TrainStream(store, mb, replica, dp, args.seed, start_micro=start_micro, captions_only=not with_data)
+    return iter(torch.utils.data.DataLoader(stream, batch_size=None, num_workers=min(args.workers, 2) if with_data
+                                            else 0, persistent_workers=False))
+
+
+def fit_ids(ids, L):
+    """Caption rows trimmed / padded (LM PAD) to the text encoder's max_tokens."""
+    from trenowanie_generatora_obrazkow_b200.models.frozen_lm import LM_PAD
+    if ids.shape[1] >= L:
+        return ids[:, :L]
+    return torch.cat([ids, torch.full((ids.shape[0], L - ids.shape[1]), LM_PAD, dtype=ids.dtype)], 1)
+
+
 def run_fm(args, den_cfg, te_cfg, lay, device, ctl, text_group):
     from trenowanie_generatora_obrazkow_b200.models.frozen_lm import LM_PAD
     from trenowanie_generatora_obrazkow_b200.parallel.lm_service import LMClient
+    from trenowanie_generatora_obrazkow_b200.train import pp_checkpoint
     from trenowanie_generatora_obrazkow_b200.train.pp_trainer import PPTrainer, pp_groups
+    from trenowanie_generatora_obrazkow_b200.utils import memory
+    from trenowanie_generatora_obrazkow_b200.utils.profiling import TrainingProfile
     M = args.microbatches or 4 * args.pp
     world = lay.n_learners
     dp = world // args.pp
     groups = pp_groups(world, args.pp)  # collective: service ranks take part
+    # Gloo groups for checkpoints (replica 0's stages; all learners), created by every rank in the same order
+    save_group = dist.new_group(list(range(args.pp)), backend="gloo")
+    learner_group = dist.new_group(list(range(world)), backend="gloo")
     role = lay.role(dist.get_rank())
     if role != "learner":
         serve(args, role, lay, te_cfg, device, ctl, text_group, args.pp)
         return
+    cuda = device.type == "cuda"
+    transport = args.grad_transport if args.grad_transport != "auto" else ("p2p" if cuda else "nccl")
+    grad_comm = "nccl_fp32" if (args.grad_comm == "fp32" or not cuda) else ("p2p" if transport == "p2p" else
+                                                                           "nccl_bf16")
     cfg = TrainConfig(global_batch=M * args.micro_batch * dp, micro_batch=args.micro_batch, steps=args.steps,
-                      lr_muon=args.lr_muon, lr_adam=args.lr_adam, wd=args.wd, clip=args.clip, seed=args.seed,
-                      t_shift=args.t_shift, grad_comm="p2p" if device.type == "cuda" else "nccl_fp32")
+                      warmup=int(args.warmup_frac * args.steps), schedule=args.schedule, optimizer=args.optimizer,
+                      lr_muon=args.lr_muon, lr_emb=args.lr_emb, lr_adam=args.lr_adam, lr_hidden=args.lr_hidden,
+                      no_lr_batch_scaling=args.no_lr_batch_scaling, wd=args.wd, beta2=args.beta2,
+                      momentum=args.momentum, ns_steps=args.ns_steps, cmuon=args.cmuon, muon_period=args.muon_period,
+                      muon_gamma=args.muon_gamma, clip=args.clip, ema=args.ema, cfg_drop=args.cfg_drop,
+                      seed=args.seed, t_shift=args.t_shift, grad_comm=grad_comm)
     tr = PPTrainer(den_cfg, te_cfg, cfg, device, args.pp, M, args.te_cost, world=world, groups=groups)
+    if tr.first and args.te_checkpoint:
+        tr.model.te_checkpoint = True
+    step, samples = pp_checkpoint.resume(tr, args.out, args.resume_opt_mismatch)
+    if step and tr.first and tr.replica == 0:
+        print(f"[stage 0] resumed from {os.path.join(args.out, 'latest.pt')} at step {step}", flush=True)
     side, L = den_cfg.latent_size, te_cfg.max_tokens
     n = M * args.micro_batch
-    use_ids = args.random_lm or te_cfg.backend != "states" or args.lm_rank > 0 or args.lm_split
+    real = not args.synthetic and os.path.isdir(args.data)
+    if not args.synthetic and not real and tr.first and tr.replica == 0:
+        print(f"[stage 0] no data directory {args.data}: synthetic latents and captions", flush=True)
+    use_ids = real or args.random_lm or te_cfg.backend != "states" or args.lm_rank > 0 or args.lm_split
+    if real:
+        assert te_cfg.backend != "states" or args.random_lm or args.lm_rank, \
+            "shard data holds caption ids: use an LM text encoder (--te-size), --random-lm or an LM server"
+        assert not (args.crop_res and args.lm_split), "--crop-res: the LM runs on stage 0 or an LM server"
+        if args.crop_res and not args.lm_rank:
+            args.lm_stage0 = True  # crop draws advance stage 0's generator: only stage 0's caption choice counts
     lm = lm_client = None
     width = te_cfg.lm_dim
     if use_ids:
         if args.lm_rank:
             if tr.first:
                 lm_client = LMClient(lay.lm_server_of(tr.replica), width, device, ctl)
-        else:
+        elif tr.first or not args.lm_stage0:
             lm, width = build_lm(args, te_cfg, device)
             if args.lm_split:  # keep only this stage's slice of the LM (and the embedding on stage 0)
                 nb = len(lm.model.blocks)
@@ -237,41 +386,89 @@ def run_fm(args, den_cfg, te_cfg, lay, device, ctl, text_group):
                 for i in range(nb):
                     if not lo <= i < hi:
                         lm.model.blocks[i] = torch.nn.Identity()
-    vae_client = None
-    if tr.first and (args.vae_rank or args.vae_on_lm):
-        vae_srv = lay.lm_server_of(tr.replica) if args.vae_on_lm else \
-            lay.vae_servers[tr.replica % len(lay.vae_servers)]
-        vae_client = lm_client if (args.vae_on_lm and lm_client is not None) else LMClient(vae_srv, 0, device, ctl)
+    vae_client = vae_local = None
+    images = bool(args.img_dir) or (not real and (args.vae_rank or args.vae_on_lm))
+    if tr.first and images:
+        if args.vae_rank or args.vae_on_lm:
+            vae_srv = lay.lm_server_of(tr.replica) if args.vae_on_lm else \
+                lay.vae_servers[tr.replica % len(lay.vae_servers)]
+            vae_client = lm_client if (args.vae_on_lm and lm_client is not None) else LMClient(vae_srv, 0, device,
+                                                                                             ctl)
+        if vae_client is None or args.vae_remote_frac < 1.0:
+            vae_local = build_vae(args, device)
+    # caption ids are needed on every stage that runs LM work (all of them, unless the LM is on stage 0 / a server)
+    reads_ids = real and (tr.first or (not args.lm_rank and not args.lm_stage0))
+    loader = shard_loader(args, te_cfg, den_cfg, args.micro_batch, tr.replica, dp, step * M, tr.first) \
+        if reads_ids else None
     g = torch.Generator().manual_seed(args.seed * 1000 + tr.replica)
+
+    def encode(u8):
+        """uint8 images -> latents: the first --vae-remote-frac on the VAE / LM server, the rest locally."""
+        k = len(u8) if vae_local is None else int(round(args.vae_remote_frac * len(u8))) if vae_client else 0
+        shape = lambda m: (m, den_cfg.latent_channels, side, side)
+        h = vae_client.request_vae(u8[:k], shape(k)) if k else None
+        parts = []
+        for i in range(k, len(u8), args.enc_chunk):
+            parts.append(vae_local.encode(u8[i:i + args.enc_chunk].to(device)).float().cpu())
+        remote = [LMClient.vae_collect(h).float().cpu()] if k else []
+        return torch.cat(remote + parts)
+
+    prof = TrainingProfile(args.profile_dir, args.profile_start, args.profile_steps, args.profile_ranks,
+                           dist.get_rank()) if args.profile_dir else None
     t0 = time.time()
-    for step in range(args.steps):
+    while step < args.steps:
+        ts = time.time()
+        if prof is not None:
+            prof.step_begin(step)
         batch = dict(n=n, side=side, text_len=L)
-        x0 = None
-        if tr.first:
-            if vae_client is not None:  # images -> latents on the VAE / LM server rank
-                u8 = torch.randint(0, 256, (n, 3, args.res, args.res), generator=g, dtype=torch.uint8)
-                h = vae_client.request_vae(u8, (n, den_cfg.latent_channels, side, side))
-                x0 = LMClient.vae_collect(h)
+        x0 = ids = cond = None
+        if loader is not None:
+            micros = [next(loader) for _ in range(M)]
+            ids = fit_ids(torch.cat([m[1] for m in micros]), L)
+            if tr.first:
+                data = torch.cat([m[0] for m in micros])
+                x0 = encode(data) if args.img_dir else data.float()
+                if den_cfg.micro_cond and len(micros[0]) > 2:
+                    cond = torch.cat([m[-1] for m in micros])
+        elif tr.first:
+            if images:  # synthetic images -> latents on the VAE / LM server rank
+                x0 = encode(torch.randint(0, 256, (n, 3, args.res, args.res), generator=g, dtype=torch.uint8))
             else:
                 x0 = torch.randn(n, den_cfg.latent_channels, side, side, generator=g)
         if use_ids:
-            # identical on every stage of the replica: a generator of its own, seeded by (replica, step)
-            ids = synthetic_ids(torch.Generator().manual_seed(args.seed * 7919 + 104729 * tr.replica + step), n, L)
+            if ids is None:  # synthetic captions, identical on every stage of the replica
+                ids = synthetic_ids(torch.Generator().manual_seed(args.seed * 7919 + 104729 * tr.replica + step),
+                                    n, L)
             batch["lm_states"] = fm_text(args, tr, lm, lm_client, ids, M, args.micro_batch, width)
             batch["valid"] = ids.ne(LM_PAD)
         else:
             batch["lm_states"] = torch.randn(n, L, te_cfg.lm_dim, generator=g) if tr.first else None
         batch["x0"] = x0
-        loss = tr.step(batch)
-        if tr.last and tr.replica == 0 and ((step + 1) % args.log_every == 0 or step + 1 == args.steps):
+        batch["cond"] = cond
+        with memory.oom_guard(lambda: memory.report(dist.get_rank(), params=tr.params, opts=tr.opts),
+                              args.mem_snapshot or None):
+            loss = tr.step(batch)
+        step += 1
+        samples += n * dp
+        if prof is not None:
+            prof.step_end(step - 1)
+        if args.mem_debug and step == 1:
+            print(memory.report(dist.get_rank(), params=tr.params, opts=tr.opts,
+                                ema=tr.ema.shadow if tr.ema is not None else None), flush=True)
+        if args.bench and tr.last and tr.replica == 0:
+            if cuda:
+                torch.cuda.synchronize()
+            dt = time.time() - ts
+            print(f"[bench] step {step} {dt * 1e3:.1f} ms {n * dp * side * side / dt:.0f} latent-tokens/s",
+                  flush=True)
+        if tr.last and tr.replica == 0 and (step % args.log_every == 0 or step == args.steps):
             dt = time.time() - t0
-            print(f"[stage {tr.stage}] step {step + 1}/{args.steps} loss {loss.item():.4f} "
+            print(f"[stage {tr.stage}] step {step}/{args.steps} loss {loss.item():.4f} "
                   f"{args.log_every * n * dp / dt:.1f} img/s", flush=True)
             t0 = time.time()
-        if args.ckpt_every and (step + 1) % args.ckpt_every == 0 and tr.replica == 0:
-            os.makedirs(args.out, exist_ok=True)
-            ckpt.atomic_save({f"{pre}.{nm}": p.detach().cpu() for pre, nm, p in tr.named},
-                             os.path.join(args.out, f"stage{tr.stage}.pt"))
+        if args.ckpt_every and (step % args.ckpt_every == 0 or step == args.steps):
+            pp_checkpoint.save(tr, args.out, step, samples, vars(args), save_group, learner_group,
+                               keep=step in args.keep_ckpt_steps)
     for c in {id(c): c for c in (lm_client, vae_client) if c is not None}.values():
         c.stop()
 
@@ -337,7 +534,8 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         tte, tden = build_models(tcfg, te_cfg, device=device)
         randomize_teacher(tden)
         teacher = DiTTeacher(tte, tden, args.opd_cfg)
-    actor = ActorClient(lay.actors[lrank % len(lay.actors)], ctl, args.opd_states) if lay.actors else None
+    actors = [ActorClient(a, ctl, args.opd_states) for a in lay.actors]
+    actor = actors[lrank % len(actors)] if actors else None
     sender = SnapshotSender(params, lay.actors, ctl) if (lay.actors and lrank == 0) else None
     learner = OPDLearner(te, den, teacher, args.opd_rollout_steps, args.opd_states, method, tuple(args.dance_beta),
                          args.t_shift, args.micro_batch, args.opd_reuse, args.opd_state_weighting, args.seed, lrank)
@@ -348,12 +546,29 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
 
     def batch_shape(step):
         res = batch_resolution(args.seed, step, args.opd_resolutions, args.opd_res_weights or None, args.res)
+        k = list(args.opd_resolutions).index(res) if args.opd_resolutions else 0
+        if args.opd_res_batches:  # images per learner at this resolution
+            return res, args.opd_res_batches[k]
         mult = token_batch_multiplier(res, args.res) if args.opd_token_batch else 1
         return res, per * mult
 
-    def caption_ids(step):  # the captions of a step (synthetic, seeded by step so the lookahead can prepare them)
-        return synthetic_ids(torch.Generator().manual_seed(args.seed * 7919 + 104729 * rank + step),
-                             batch_shape(step)[1], L)
+    cap_loader = local_lm = None
+    if not args.synthetic and os.path.isdir(args.data):  # shard captions (OPD needs no latents); LM server or here
+        cap_loader = shard_loader(args, te_cfg, den_cfg, args.micro_batch, lrank, n_learn, 0, False)
+        if not args.lm_rank:
+            local_lm, _ = build_lm(args, te_cfg, device)
+    cap_cache = {}
+
+    def caption_ids(step):  # the captions of a step (seeded by step so the lookahead can prepare them)
+        B = batch_shape(step)[1]
+        if cap_loader is None:
+            return synthetic_ids(torch.Generator().manual_seed(args.seed * 7919 + 104729 * rank + step), B, L)
+        if step not in cap_cache:  # shard captions in step order (the lookahead asks ahead, the loop later)
+            rows = []
+            while sum(len(r) for r in rows) < B:
+                rows.append(fit_ids(next(cap_loader)[1], L))
+            cap_cache[step] = torch.cat(rows)[:B]
+        return cap_cache[step]
 
     lookahead = None
     if args.opd_text_ahead:
@@ -365,7 +580,11 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
     for step in range(args.steps):
         res, B = batch_shape(step)
         side = res // 16
-        shift = resolution_shift(res, args.opd_resolutions, (), args.t_shift_ref, args.t_shift, args.res)
+        shift = resolution_shift(res, args.opd_resolutions, args.opd_res_shifts, args.t_shift_ref, args.t_shift,
+                                 args.res)
+        if args.opd_res_mb and args.opd_resolutions:
+            learner.mb = args.opd_res_mb[list(args.opd_resolutions).index(res)]
+        tp = time.time()
         noise = torch.randn(B, den_cfg.latent_channels, side, side, generator=g).to(device)
         if lookahead is not None:
             job = lookahead.take(step)
@@ -373,21 +592,43 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         elif lm_client is not None:
             ids = caption_ids(step)
             st, valid = lm_client.collect(lm_client.request(ids)), ids.ne(LM_PAD).to(device)
+        elif local_lm is not None:
+            ids = caption_ids(step)
+            st = torch.cat([local_lm.states(c.to(device)).to(torch.bfloat16) for c in ids.split(args.micro_batch)])
+            valid = ids.ne(LM_PAD).to(device)
         else:
             st = torch.randn(B, L, te_cfg.lm_dim, generator=g).to(device)
             valid = torch.ones(B, L, dtype=torch.bool, device=device)
+        cap_cache.pop(step, None)
+        if args.opd_sort_rollouts:  # caption-length-sorted batch (similar lengths share rollout micro-batches)
+            order = valid.sum(1).argsort(stable=True)
+            st, valid, noise = st[order], valid[order], noise[order]
+        if args.opd_balance_rollouts and actors:
+            actor = actors[(lrank + step) % len(actors)]
+        t_data = time.time() - tp
+        t_roll = t_teach = 0.0
         for p in params:
             p.grad = None
         if actor is not None and (learner.cache is None or learner.uses >= learner.reuse):
             if sender is not None:
                 version = sender.send()
+            tr0 = time.time()
             states, t = actor.rollouts(noise, st, valid, step, version)
+            t_roll = time.time() - tr0
             rep = lambda a: a.repeat_interleave(args.opd_states, dim=0)
-            target = teacher.velocity(states, t, dict(lm_states=rep(st), valid=rep(valid)))
+            kw_all = dict(lm_states=rep(st), valid=rep(valid))
+            tt0 = time.time()
+            bounds = [(i * len(states) // args.opd_parts, (i + 1) * len(states) // args.opd_parts)
+                      for i in range(args.opd_parts)]
+            target = torch.cat([teacher.velocity(states[a:b], t[a:b], {k: v[a:b] for k, v in kw_all.items()})
+                                for a, b in bounds if b > a])
+            t_teach = time.time() - tt0
             learner.cache = dict(x=states, t=t, target=target, text_kw=dict(lm_states=rep(st), valid=rep(valid)),
                                  errors=None)
             learner.uses = 0
+        tl0 = time.time()
         loss = learner.step_grads(step, st, valid, noise, shift)
+        t_learn = time.time() - tl0
         if n_learn > 1:
             for p in params:
                 if p.grad is not None:
@@ -400,7 +641,13 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         if lrank == 0 and ((step + 1) % args.log_every == 0 or step + 1 == args.steps):
             print(f"[learner] step {step + 1}/{args.steps} opd loss {float(loss):.4f} res {res} "
                   f"{(time.time() - t0) / args.log_every:.2f} s/step", flush=True)
+            if args.opd_learner_profile:
+                print(f"[learner profile] captions {t_data * 1e3:.0f} ms, rollouts {t_roll * 1e3:.0f} ms, teacher "
+                      f"{t_teach * 1e3:.0f} ms ({args.opd_parts} parts), student {t_learn * 1e3:.0f} ms", flush=True)
             t0 = time.time()
+        if args.opd_actor_profile and actor is not None and t_roll:
+            print(f"[actor profile] learner {lrank} step {step + 1}: {len(noise)} rollouts of "
+                  f"{args.opd_rollout_steps} steps in {t_roll * 1e3:.0f} ms (request to reply)", flush=True)
     if lookahead is not None:
         lookahead.close()
     if lm_client is not None:
@@ -409,8 +656,8 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         if isinstance(teacher, TeacherClient):
             teacher.stop()
     dist.barrier(group=learner_group)
-    if actor is not None and lrank < len(lay.actors):
-        actor.stop()
+    if actors and lrank < len(actors):
+        actors[lrank].stop()
 
 
 if __name__ == "__main__":

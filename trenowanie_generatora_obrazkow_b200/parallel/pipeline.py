@@ -122,7 +122,12 @@ class StageModel(nn.Module):
         from ..train.flow import LMTextEncoder
         b, c, h, w = z_t.shape
         if isinstance(self.te, LMTextEncoder):
-            text, valid = self.te(**text_kw)
+            if getattr(self, "te_checkpoint", False) and torch.is_grad_enabled():  # recomputed in the backward
+                text, valid = torch.utils.checkpoint.checkpoint(
+                    lambda st, v, nl: self.te(lm_states=st, valid=v, is_null=nl), text_kw["lm_states"],
+                    text_kw["valid"], text_kw.get("is_null"), use_reentrant=False)
+            else:
+                text, valid = self.te(**text_kw)
         else:
             text, valid = self.te(text_kw["ids"])
         tok = z_t.flatten(2).transpose(1, 2)
@@ -198,7 +203,7 @@ class OneFOneB:
         def forward(i, acts):
             if first:
                 z, t, kw = first_inputs(i)
-                x, t6, text, tl = self.m.stem(z, t, kw)
+                x, t6, text, tl = self.m.stem(z, t, {k: v for k, v in kw.items() if k != "cond"}, kw.get("cond"))
                 ins = None
             else:
                 x, t6, text, tl = acts

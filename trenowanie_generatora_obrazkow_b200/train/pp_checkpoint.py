@@ -1,0 +1,100 @@
+"""Checkpoints of a PP x DP flow-matching run in the single-model layout.
+
+Save (reference train_pp.py:1749-1785): replica 0's stages send their parameters and EMA (under the unsplit model's
+names) to global rank 0 over a Gloo group; rank 0 writes ``latest.pt`` in the layout train.py, sample_ckpt.py,
+export.py and merge.py read (te / den state dicts, the flat EMA list in the unsplit model's ``parameters()``
+order). Every learner rank writes its optimizer state to ``opt_stage{s}_rep{r}.pt`` together with the pipeline
+layout it belongs to. The commit is two-phase (every ``.tmp`` first, then the renames), so a crash mid-save leaves
+the previous checkpoint intact.
+
+Resume (reference train_pp.py:1453-1500): any pipeline layout loads the weights and the EMA of ``latest.pt`` by
+name; the optimizer state only when the rank's file exists and its layout matches (pp, dp, the stage's block
+range); otherwise the run stops, unless ``resume_opt_mismatch`` asks for fresh optimizer state.
+"""
+import os
+from dataclasses import asdict
+
+import torch
+import torch.distributed as dist
+
+from ..models import build_models
+from ..parallel.pipeline import stage_ranges
+from ..utils import checkpoint as ckpt
+
+
+def layout(tr):
+    return dict(pp=tr.pp, dp=tr.dp, stage=tr.stage, blocks=list(stage_ranges(tr.den_cfg.depth, tr.pp,
+                                                                             tr.te_cost)[tr.stage]))
+
+
+def opt_path(out, tr):
+    return os.path.join(out, f"opt_stage{tr.stage}_rep{tr.replica}.pt")
+
+
+def _unsplit_order(den_cfg, te_cfg):
+    """[(prefix, name)] of the unsplit model in parameters() order (text encoder first), built on the meta device."""
+    with torch.device("meta"):
+        te, den = build_models(den_cfg, te_cfg)
+    return [("te", n) for n, _ in te.named_parameters()] + [("den", n) for n, _ in den.named_parameters()]
+
+
+def save(tr, out, step, samples, args, save_group, learner_group, keep=False):
+    """Collective over the learner ranks. save_group: Gloo group of replica 0's stages (ranks 0 .. pp - 1)."""
+    os.makedirs(out, exist_ok=True)
+    writes = [(dict(layout=layout(tr), step=step, opts=[o.state_dict() for o in tr.opts]), opt_path(out, tr))]
+    latest = os.path.join(out, "latest.pt")
+    if tr.replica == 0:
+        trainable = [(pre, n) for pre, n, p in tr.named if p.requires_grad]
+        payload = dict(params={(pre, n): p.detach().float().cpu() for pre, n, p in tr.named},
+                       ema={k: s.detach().float().cpu() for k, s in zip(trainable, tr.ema.shadow)})
+        got = [None] * tr.pp if dist.get_rank() == 0 else None
+        dist.gather_object(payload, got, dst=0, group=save_group)
+        if dist.get_rank() == 0:
+            params, ema = {}, {}
+            for part in got:
+                params.update(part["params"])
+                ema.update(part["ema"])
+            order = _unsplit_order(tr.den_cfg, tr.te_cfg)
+            missing = [k for k in order if k not in params]
+            assert not missing, f"pipeline checkpoint: parameters owned by no stage: {missing[:4]}"
+            ck = dict(step=step, samples=samples, den_config=asdict(tr.den_cfg), te_config=asdict(tr.te_cfg),
+                      te={n: params[(pre, n)] for pre, n in order if pre == "te"},
+                      den={n: params[(pre, n)] for pre, n in order if pre == "den"},
+                      opts=None, ema=[ema.get(k, params[k]) for k in order], args=dict(args or {}),
+                      outer=None, repa_proj=None, pp_layout=dict(pp=tr.pp, dp=tr.dp))
+            writes.append((ck, latest))
+    ckpt.two_phase_commit(writes, barrier=lambda: dist.barrier(group=learner_group))
+    if keep and dist.get_rank() == 0:
+        ckpt.keep_hardlink(latest, step, out)
+    dist.barrier(group=learner_group)
+
+
+@torch.no_grad()
+def resume(tr, out, resume_opt_mismatch=False, log=print):
+    """Load latest.pt (if any) into this rank's stage. Returns (step, samples) or (0, 0) without a checkpoint."""
+    latest = os.path.join(out, "latest.pt")
+    if not os.path.exists(latest):
+        return 0, 0
+    ck = ckpt.load(latest)
+    order = _unsplit_order(tr.den_cfg, tr.te_cfg)
+    ema_by_name = dict(zip(order, ck["ema"])) if ck.get("ema") and len(ck["ema"]) == len(order) else {}
+    for pre, n, p in tr.named:
+        p.copy_(ck[pre][n].to(p.device, p.dtype))
+    if tr.ema is not None:
+        trainable = [(pre, n) for pre, n, p in tr.named if p.requires_grad]
+        for k, s in zip(trainable, tr.ema.shadow):
+            s.copy_(ema_by_name.get(k, ck[k[0]][k[1]]).to(s.device, s.dtype))
+    path = opt_path(out, tr)
+    opt = ckpt.load(path) if os.path.exists(path) else None
+    if opt is not None and opt.get("layout") == layout(tr) and len(opt["opts"]) == len(tr.opts):
+        for o, st in zip(tr.opts, opt["opts"]):
+            ckpt.load_opt_state(o, st)
+    elif resume_opt_mismatch:
+        log(f"[stage {tr.stage} replica {tr.replica}] optimizer state of {path} does not match this pipeline "
+            "layout: starting it fresh (--resume-opt-mismatch)")
+    else:
+        raise RuntimeError(f"{path}: optimizer state missing or written by another pipeline layout; pass "
+                           "--resume-opt-mismatch to resume the weights with fresh optimizer state")
+    step = int(ck.get("step", 0))
+    tr.step_idx = step
+    return step, int(ck.get("samples", 0))

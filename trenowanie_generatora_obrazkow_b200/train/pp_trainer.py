@@ -37,7 +37,7 @@ class PPTrainer:
         self.cfg, self.device = cfg, torch.device(device)
         self.rank = dist.get_rank()
         self.world = world or dist.get_world_size()
-        self.pp, self.M = pp, microbatches
+        self.pp, self.M, self.te_cost = pp, microbatches, te_cost
         self.dp, pipes, stages = grid_layout(self.world, pp)
         self.stage, self.replica = self.rank % pp, self.rank // pp
         self.pipe = pipes[self.replica]
@@ -74,7 +74,8 @@ class PPTrainer:
         return OneFOneB(self.model, self.pipe, self.stage, shapes, self.device)
 
     def step(self, batch):
-        """batch (stage 0 of every replica): x0 (M * mb, C, h, w) and lm_states (M * mb, L, D) [+ valid, is_null].
+        """batch (stage 0 of every replica): x0 (M * mb, C, h, w) and lm_states (M * mb, L, D) [+ valid, is_null,
+        cond (M * mb, 8) micro-conditions].
         Other stages pass the same keys with shapes only used for sizing (or None). Returns the loss on the last
         stage (device scalar), else None."""
         cfg, M = self.cfg, self.M
@@ -101,8 +102,10 @@ class PPTrainer:
                 is_null = batch["is_null"][sl].to(self.device) if batch.get("is_null") is not None else None
                 is_null, valid = drop_captions(is_null, valid, cfg.cfg_drop, self.gen)
                 tt = t.view(-1, 1, 1, 1)
-                inputs.append(((1 - tt) * x0 + tt * eps, t, dict(lm_states=st_all[sl], valid=valid,
-                                                                  is_null=is_null)))
+                kw = dict(lm_states=st_all[sl], valid=valid, is_null=is_null)
+                if batch.get("cond") is not None:  # micro-conditions (crop windows) of the micro-batch
+                    kw["cond"] = batch["cond"][sl].to(self.device)
+                inputs.append(((1 - tt) * x0 + tt * eps, t, kw))
                 targets.append((eps - x0).flatten(2).transpose(1, 2).contiguous())
             if self.pp > 1:
                 send_targets(targets, self.pipe)
