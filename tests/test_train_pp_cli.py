@@ -92,7 +92,7 @@ def test_pipeline_shards_checkpoint_and_resume(tmp_path):
               "--microbatches", "2", "--micro-batch", "2", "--res", "128", "--log-every", "1", "--random-lm",
               "--lm-layers", "2", "--ckpt-every", "2", "--workers", "0", "--keep-ckpt-steps", "2"]
     log = _torchrun(2, *common, "--pp", "2", "--steps", "2")
-    assert "step 2/2" in log
+    assert "step 2/2" in log and "data: latents from" in log
     ck = torch.load(os.path.join(out, "latest.pt"), weights_only=False)
     assert ck["step"] == 2 and ck["samples"] == 8 and len(ck["ema"]) == len(ck["te"]) + len(ck["den"])
     te, den = build_models(DenoiserConfig(**ck["den_config"]), te_config_from_dict(ck["te_config"]))
@@ -123,3 +123,30 @@ def test_pipeline_flags_stage0_lm_profile_and_unsupported(tmp_path):
     rc, msg = _torchrun_rc(1, "--out", str(tmp_path / "c"), "--size", "nano", "--te-size", "states-nano",
                            "--steps", "1", "--klein")
     assert rc != 0 and "unavailable on this box" in msg
+
+
+def test_pipeline_packed_images_local_encode(tmp_path):
+    """--img-dir: packed JPEG shards decoded by the loader and encoded on stage 0 (the VAE stand-in here)."""
+    import io
+
+    import numpy as np
+    import pytest
+    PIL = pytest.importorskip("PIL.Image")
+    from trenowanie_generatora_obrazkow_b200.data.shards import write_synthetic_shards
+    data = str(tmp_path / "imgs")
+    names = write_synthetic_shards(data, n_shards=3, per_shard=6, side=8)
+    rng = np.random.default_rng(0)
+    for name in names:
+        blobs = []
+        for _ in range(6):
+            buf = io.BytesIO()
+            PIL.fromarray(rng.integers(0, 256, (128, 128, 3), dtype=np.uint8)).save(buf, format="JPEG")
+            blobs.append(buf.getvalue())
+        with open(os.path.join(data, f"{name}.img.bin"), "wb") as f:
+            f.write(b"".join(blobs))
+        np.save(os.path.join(data, f"{name}.img.off.npy"), np.cumsum([0] + [len(b) for b in blobs]).astype(np.int64))
+    log = _torchrun(2, "--out", str(tmp_path / "run"), "--img-dir", data, "--fraction", "1", "--size", "nano",
+                    "--te-size", "states-nano", "--pp", "2", "--microbatches", "2", "--micro-batch", "2", "--res",
+                    "128", "--steps", "2", "--log-every", "2", "--random-lm", "--lm-layers", "2", "--workers", "0",
+                    "--enc-chunk", "2")
+    assert "step 2/2" in log and "data: images from" in log

@@ -362,9 +362,11 @@ def run_fm(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         print(f"[stage 0] resumed from {os.path.join(args.out, 'latest.pt')} at step {step}", flush=True)
     side, L = den_cfg.latent_size, te_cfg.max_tokens
     n = M * args.micro_batch
-    real = not args.synthetic and os.path.isdir(args.data)
-    if not args.synthetic and not real and tr.first and tr.replica == 0:
-        print(f"[stage 0] no data directory {args.data}: synthetic latents and captions", flush=True)
+    root = args.img_dir or args.data
+    real = not args.synthetic and os.path.isdir(root)
+    if not args.synthetic and tr.first and tr.replica == 0:
+        print(f"[stage 0] data: {'images' if args.img_dir else 'latents'} from {root}" if real else
+              f"[stage 0] no data directory {root}: synthetic latents and captions", flush=True)
     use_ids = real or args.random_lm or te_cfg.backend != "states" or args.lm_rank > 0 or args.lm_split
     if real:
         assert te_cfg.backend != "states" or args.random_lm or args.lm_rank, \
@@ -409,7 +411,7 @@ def run_fm(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         h = vae_client.request_vae(u8[:k], shape(k)) if k else None
         parts = []
         for i in range(k, len(u8), args.enc_chunk):
-            parts.append(vae_local.encode(u8[i:i + args.enc_chunk].to(device)).float().cpu())
+            parts.append(vae_local(u8[i:i + args.enc_chunk].to(device)).float().cpu())
         remote = [LMClient.vae_collect(h).float().cpu()] if k else []
         return torch.cat(remote + parts)
 
