@@ -215,3 +215,36 @@ def test_attention_fwd_fma_exponentials(emu, pingpong, hd, T, logit_scale):
     ref = R.attention(q.float().cpu(), k.float().cpu(), v.float().cpu(), kv_len.cpu(), scale)
     assert torch.isfinite(o).all()
     assert rel(o.cpu(), ref) < 1.5e-2
+
+
+def test_fm_inputs_and_forward_tokens():
+    """Fused flow-matching input / target kernel against the eager formulas, and the denoiser fed the token-major
+    input against the latent-layout forward."""
+    from trenowanie_generatora_obrazkow_b200.models import DenoiserConfig
+    from trenowanie_generatora_obrazkow_b200.models.dit import Denoiser
+    from trenowanie_generatora_obrazkow_b200.ops._ext import check_errors
+    torch.manual_seed(7)
+    x0 = torch.randn(3, 128, 12, 10, device="cuda")
+    eps = torch.randn_like(x0)
+    t = torch.rand(3, device="cuda")
+    z_tok, target = Fz.fm_inputs(x0, eps, t)
+    torch.cuda.synchronize()
+    check_errors()
+    tt = t.view(-1, 1, 1, 1)
+    tok = lambda a: a.flatten(2).transpose(1, 2)
+    z_ref = tok((1 - tt) * x0 + tt * eps)
+    assert z_tok.dtype == torch.bfloat16 and z_tok.shape == (3, 120, 128)
+    assert rel(z_tok, z_ref) < 5e-3
+    assert torch.allclose(target, tok(eps - x0), atol=1e-6)
+    den = Denoiser(DenoiserConfig(dim=256, depth=2, heads=2, mlp_hidden=704, text_dim=256, latent_size=12)).cuda()
+    den.init_weights()
+    with torch.no_grad():
+        for p in den.parameters():  # non-zero output layers, so the comparison is not trivially exact
+            p.add_(0.02 * torch.randn_like(p))
+    text = torch.randn(3, 16, 256, device="cuda")
+    valid = torch.ones(3, 16, dtype=torch.bool, device="cuda")
+    with torch.no_grad():
+        v_tok = den.forward_tokens(z_tok, (12, 10), t, text, valid)
+        v_ref = den((1 - tt) * x0 + tt * eps, t, text, valid, tokens_out=True)
+    assert v_tok.shape == v_ref.shape
+    assert rel(v_tok, v_ref) < 1e-2

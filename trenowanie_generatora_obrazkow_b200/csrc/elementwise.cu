@@ -1,4 +1,4 @@
-// Elementwise kernels of the sampler.
+// Elementwise kernels of the sampler and of the flow-matching step.
 //
 // euler_cfg: one Euler step with classifier-free guidance (reference aurora/fid.py:35-37,
 //   aurora/hf_pipeline.py:753-759), reading the denoiser's token-major output directly:
@@ -39,6 +39,48 @@ cudaError_t euler_cfg_launch(const __nv_bfloat16* out, float* z, int B, int T, i
                              cudaStream_t s) {
   dim3 grid((T + 31) / 32, (C + 31) / 32, B), block(32, 8);
   euler_cfg_kernel<<<grid, block, 0, s>>>(out, z, B, T, C, dt, w);
+  return cudaGetLastError();
+}
+
+// fm_inputs: the flow-matching input and target of a training micro-batch (reference aurora/model.py FlowModel,
+// train.py:662-668), in the layouts their consumers read:
+//     z_t    = (1 - t) x0 + t eps   -> bf16 token-major [B, T, C] (the patch-in GEMM's A operand)
+//     target = eps - x0             -> fp32 token-major [B, T, C] (compared with the token-major velocity)
+// from x0 / eps fp32 [B, C, T] (latent layout), one pass through a shared 32 x 32 transpose tile.
+__global__ void fm_inputs_kernel(const float* __restrict__ x0, const float* __restrict__ eps,
+                                 const float* __restrict__ t, __nv_bfloat16* __restrict__ z_tok,
+                                 float* __restrict__ target, int T, int C) {
+  __shared__ float tz[32][33], tg[32][33];
+  const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32, b = blockIdx.z;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const float tb = t[b];
+  for (int i = ty; i < 32; i += 8) {  // read along tokens (contiguous in the latent layout)
+    const int c = c0 + i, tt = t0 + tx;
+    float z = 0.f, g = 0.f;
+    if (tt < T && c < C) {
+      const long long off = ((long long)b * C + c) * T + tt;
+      const float x = x0[off], e = eps[off];
+      z = (1.f - tb) * x + tb * e;
+      g = e - x;
+    }
+    tz[i][tx] = z;
+    tg[i][tx] = g;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {  // write along channels (contiguous in the token-major layout)
+    const int tt = t0 + i, c = c0 + tx;
+    if (tt < T && c < C) {
+      const long long off = ((long long)b * T + tt) * C + c;
+      z_tok[off] = __float2bfloat16(tz[tx][i]);
+      target[off] = tg[tx][i];
+    }
+  }
+}
+
+cudaError_t fm_inputs_launch(const float* x0, const float* eps, const float* t, __nv_bfloat16* z_tok, float* target,
+                             int B, int T, int C, cudaStream_t s) {
+  dim3 grid((T + 31) / 32, (C + 31) / 32, B), block(32, 8);
+  fm_inputs_kernel<<<grid, block, 0, s>>>(x0, eps, t, z_tok, target, T, C);
   return cudaGetLastError();
 }
 

@@ -170,6 +170,9 @@ cudaError_t attention_fwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk
 // ---------------------------------------------------------------- elementwise (elementwise.cu)
 cudaError_t euler_cfg_launch(const __nv_bfloat16* out, float* z, int B, int T, int C, float dt, float w,
                              cudaStream_t s);
+// flow-matching input (bf16) and target (fp32), token-major [B, T, C], from fp32 x0 / eps [B, C, T] and t [B]
+cudaError_t fm_inputs_launch(const float* x0, const float* eps, const float* t, __nv_bfloat16* z_tok, float* target,
+                             int B, int T, int C, cudaStream_t s);
 
 // ---------------------------------------------------------------- peer-memory collectives (comm.cu)
 struct PeerAllReduceParams {

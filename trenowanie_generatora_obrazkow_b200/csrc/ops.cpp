@@ -768,6 +768,21 @@ void euler_cfg(at::Tensor out, at::Tensor z, double dt, double w) {
                                     at::cuda::getCurrentCUDAStream()));
 }
 
+std::vector<at::Tensor> fm_inputs(at::Tensor x0, at::Tensor eps, at::Tensor t) {
+  TORCH_CHECK(x0.is_cuda() && x0.scalar_type() == at::kFloat && x0.is_contiguous() && x0.dim() == 4,
+              "fm_inputs: x0 fp32 [B, C, H, W] contiguous");
+  TORCH_CHECK(eps.sizes() == x0.sizes() && eps.scalar_type() == at::kFloat && eps.is_contiguous(), "fm_inputs: eps");
+  TORCH_CHECK(t.scalar_type() == at::kFloat && t.is_contiguous() && t.numel() == x0.size(0), "fm_inputs: t fp32 [B]");
+  const int64_t B = x0.size(0), C = x0.size(1), T = x0.size(2) * x0.size(3);
+  const c10::cuda::CUDAGuard guard(x0.device());
+  auto z_tok = at::empty({B, T, C}, x0.options().dtype(at::kBFloat16));
+  auto target = at::empty({B, T, C}, x0.options());
+  TGO_CHECK_LAUNCH(fm_inputs_launch(x0.data_ptr<float>(), eps.data_ptr<float>(), t.data_ptr<float>(), bfp(z_tok),
+                                    target.data_ptr<float>(), (int)B, (int)T, (int)C,
+                                    at::cuda::getCurrentCUDAStream()));
+  return {z_tok, target};
+}
+
 // ------------------------------------------------------------------------------------------------ peer memory
 // Device buffers shared between the ranks of one node: allocated with cudaMalloc (zeroed), exported as a CUDA IPC
 // handle, opened by the peers.  Pointers travel as integers.
@@ -956,6 +971,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &tgo::gemm, "tcgen05 bf16 GEMM: C = alpha * op(A) op(B)^T (+ beta D)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("a_mn"), py::arg("b_mn"), py::arg("D") = c10::nullopt, py::arg("alpha") = 1.0,
         py::arg("beta") = 0.0, py::arg("accumulate") = false, py::arg("err"));
+  m.def("fm_inputs", &tgo::fm_inputs, "flow-matching input (bf16) and target (fp32), token-major, in one pass");
   m.def("euler_cfg", &tgo::euler_cfg, "fused classifier-free-guidance Euler step from token-major velocities");
   m.def("symm_alloc", &tgo::symm_alloc, "zeroed device buffer + its CUDA IPC handle");
   m.def("symm_free", &tgo::symm_free);

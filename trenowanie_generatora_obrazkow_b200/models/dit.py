@@ -192,18 +192,29 @@ class Denoiser(nn.Module):
         hidden_at > 0: also return the token states after that many blocks (REPA).
         rope: optional (cos, sin) [B, T, d] per-sample tables (RPE-2D random positions).
         tokens_out: return the velocity token-major (B, H*W, C) as computed (the sampler's fused update reads it)."""
-        b, c, h, w = z_t.shape
+        return self._forward(self.embed(z_t), z_t.shape, t, text, text_valid, hidden_at, cond, text_len, rope,
+                             tokens_out)
+
+    def forward_tokens(self, z_tok, hw, t, text, text_valid=None, hidden_at=0, cond=None, text_len=None, rope=None):
+        """z_tok [B, H*W, C] token-major latents (bf16 on CUDA, as the fused flow-matching input kernel writes them):
+        the patch-in GEMM reads them directly. Returns the token-major velocity [B, H*W, C] (and the hidden state
+        with hidden_at)."""
+        b, _, c = z_tok.shape
+        return self._forward(Fz.linear(z_tok, self.patch_in), (b, c) + tuple(hw), t, text, text_valid, hidden_at,
+                             cond, text_len, rope, True)
+
+    def _forward(self, x, shape, t, text, text_valid, hidden_at, cond, text_len, rope, tokens_out):
+        b, c, h, w = shape
         if text_len is None:
             text_len = R.valid_to_len(text_valid) if text_valid is not None else None
-        if z_t.is_cuda:
+        if x.is_cuda:
             text = text.to(torch.bfloat16)
             if text_len is not None:
-                text_len = text_len.to(device=z_t.device, dtype=torch.int32)
-        x = self.embed(z_t)
+                text_len = text_len.to(device=x.device, dtype=torch.int32)
         t6 = self.modulation(t, cond, 16 * h)
-        cos, sin = rope if rope is not None else self.rope(h, w, z_t.device)
+        cos, sin = rope if rope is not None else self.rope(h, w, x.device)
         x, pending, hidden = self.run_blocks(x, None, t6, text, text_len, cos, sin, hidden_at=hidden_at)
-        out = self.head(x, pending, z_t.shape, tokens_out)
+        out = self.head(x, pending, shape, tokens_out)
         return out if not hidden_at else (out, hidden)
 
     # ---------------------------------------------------------------------------------------------- init

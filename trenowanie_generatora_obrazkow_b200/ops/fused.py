@@ -356,6 +356,17 @@ class _SwiGLUFn(torch.autograd.Function):
         return ext().swiglu_bwd(ab, dg.contiguous())
 
 
+def fm_inputs(x0, eps, t):
+    """Flow-matching input and target, token-major [B, H*W, C]: z_t = (1 - t) x0 + t eps (bf16 on CUDA, the
+    patch-in GEMM's input) and eps - x0 (fp32), from fp32 [B, C, H, W] latents; one kernel on CUDA."""
+    if x0.is_cuda:
+        z_tok, target = ext().fm_inputs(x0.float().contiguous(), eps.float().contiguous(), t.float().contiguous())
+        return z_tok, target
+    tt = t.view(-1, 1, 1, 1)
+    tok = lambda a: a.flatten(2).transpose(1, 2)
+    return tok((1 - tt) * x0 + tt * eps), tok(eps - x0)
+
+
 def swiglu(ab):
     if not ab.is_cuda:
         return R.swiglu(ab)

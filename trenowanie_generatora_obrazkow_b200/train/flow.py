@@ -11,6 +11,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from ..ops import fused as Fz
+
 from ..models.text import MASK_ID, LMTextEncoder
 
 
@@ -48,16 +50,25 @@ class FlowModel(nn.Module):
                 repa_target=None, cond=None, rope=None):
         """Returns (loss, fm, mlm or None, repa or None); x0 / eps (B, C, H, W) fp32, t (B,)."""
         text, text_valid = self.encode_text(ids, lm_states, valid, is_null)
-        tt = t.view(-1, 1, 1, 1)
-        z_t = (1 - tt) * x0 + tt * eps
-        target = eps - x0
         loss_repa = None
-        if repa_target is not None and self.repa_proj is not None:
-            v, h = self.den(z_t, t, text, text_valid, hidden_at=self.repa_layer, cond=cond, rope=rope)
+        repa = repa_target is not None and self.repa_proj is not None
+        if x0.is_cuda and hasattr(self.den, "forward_tokens"):
+            # one kernel writes the token-major input the patch-in GEMM reads and the token-major target the
+            # token-major velocity is compared with (no latent-layout transposes on either side)
+            z_tok, target = Fz.fm_inputs(x0, eps, t)
+            out = self.den.forward_tokens(z_tok, x0.shape[2:], t, text, text_valid, cond=cond, rope=rope,
+                                          hidden_at=self.repa_layer if repa else 0)
+        else:
+            tt = t.view(-1, 1, 1, 1)
+            z_t = (1 - tt) * x0 + tt * eps
+            target = eps - x0
+            out = self.den(z_t, t, text, text_valid, cond=cond, rope=rope, hidden_at=self.repa_layer if repa else 0)
+        if repa:
+            v, h = out
             pred = self.repa_proj(h[: repa_target.shape[0]].float())
             loss_repa = -F.cosine_similarity(pred.float(), repa_target, dim=-1).mean()
         else:
-            v = self.den(z_t, t, text, text_valid, cond=cond, rope=rope)
+            v = out
         loss_fm = F.mse_loss(v.float(), target)
         loss = loss_fm
         if self.moe_aux_weight > 0:
