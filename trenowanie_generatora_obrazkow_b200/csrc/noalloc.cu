@@ -1,4 +1,4 @@
-// Allocation-free entry point for the fused RMSNorm / adaLN backward.
+// Allocation-free entry point for the fused RMSNorm / adaLN backward (C interface declared in noalloc.h).
 //
 // This entry point has no counterpart in the reference; it exists for callers of this library that cannot
 // allocate device memory at the moment they run the op: for example a plugin executed inside a host framework
@@ -7,25 +7,28 @@
 // (`adanorm_bwd` in ops.cpp) asks torch's allocator for a per-call partial-sum buffer; this one uses a fixed
 // scratch array that lives in the library image instead.
 //
-//   int tgo_adanorm_bwd_noalloc(...)   (extern "C", raw device pointers, see below)
-//
 // Scratch: `g_noalloc_scratch`, a file-scope __device__ array of kNoAllocScratchFloats floats (16 MiB).  Every
 // GPU on which the library is loaded holds it until the process exits.  The caller still passes all inputs and
 // outputs.  Limits and rules:
 //   * the partial sums need B * ceil(T / rows) * 4 * D floats; the entry point picks the smallest row chunk
 //     (a multiple of 32) that fits and returns TGO_NOALLOC_TOO_LARGE when even one chunk per sample
-//     (B * 4 * D floats) does not fit;
+//     (B * 4 * D floats) does not fit, or when B exceeds 65535 (the kernels put one grid row per sample);
 //   * every call shares the one array and the row pass overwrites every element it later reads, so nothing needs
 //     clearing between calls; two calls that overlap on the GPU (different streams without ordering, or two
 //     host threads) race on the array and give wrong results;
 //   * the first call on each device looks up the array's device address with cudaGetSymbolAddress (with that
 //     device current) and caches it; make that first call before any stream capture begins;
+//   * pointers and strides are checked on the host before anything is launched: the kernels move bf16 rows and
+//     the scale / gate vectors in 16-byte loads and stores, so bf16 pointers must be 16-byte aligned and the batch
+//     strides multiples of 8 elements; fp32 pointers must be 4-byte aligned;
 //   * no cudaMalloc, cudaFree or allocating library routine is called.
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <mutex>
 
 #include "kernels.h"
+#include "noalloc.h"
 
 namespace {
 
@@ -59,26 +62,37 @@ cudaError_t scratch_for_current_device(float** out) {
 
 extern "C" {
 
-enum {
-  TGO_NOALLOC_OK = 0,
-  TGO_NOALLOC_BAD_ARGS = 1,
-  TGO_NOALLOC_TOO_LARGE = 2,
-  TGO_NOALLOC_CUDA_ERROR = 3,
-};
-
 // Capacity of the scratch array in floats.
 long long tgo_noalloc_scratch_floats() { return kNoAllocScratchFloats; }
 
 const char* tgo_noalloc_error_string(int code) {
   switch (code) {
     case TGO_NOALLOC_OK: return "ok";
-    case TGO_NOALLOC_BAD_ARGS: return "invalid arguments (null pointer, D % 8 != 0, D > 4096, or M % T != 0)";
+    case TGO_NOALLOC_BAD_ARGS:
+      return "invalid arguments (null pointer, bf16 pointer not 16-byte aligned, fp32 pointer not 4-byte aligned, "
+             "scale / gate batch stride negative or not a multiple of 8, D % 8 != 0, D > 4096, or M % T != 0)";
     case TGO_NOALLOC_TOO_LARGE:
       return "problem too large for the fixed scratch array (needs B * 4 * D floats at least; capacity "
-             "4194304 floats)";
+             "4194304 floats) or more than 65535 samples (B = M / T)";
     case TGO_NOALLOC_CUDA_ERROR: return "CUDA error (see cudaGetLastError)";
     default: return "unknown";
   }
+}
+
+// Smallest row chunk (a multiple of 32) whose partial sums fit the scratch array, or -1 if none does.
+static int noalloc_rows(long long M, long long D, long long T) {
+  if (M <= 0 || D <= 0 || T <= 0 || M % T != 0) return -1;
+  const long long B = M / T;
+  if (B > 65535 || B * 4ll * D > kNoAllocScratchFloats) return -1;
+  long long rows = 32;
+  while (B * ((T + rows - 1) / rows) * 4ll * D > kNoAllocScratchFloats) rows += 32;
+  return static_cast<int>(rows);
+}
+
+int tgo_noalloc_adanorm_rows(int M, int D, int T) { return noalloc_rows(M, D, T); }
+
+static bool misaligned(const void* p, unsigned bytes) {
+  return p != nullptr && (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) != 0;
 }
 
 // Backward of  x_new = x + gate * y ;  h = rmsnorm(x_new) * w * (1 + scale) + shift   over M = B * T rows of D.
@@ -86,7 +100,8 @@ const char* tgo_noalloc_error_string(int code) {
 // xn [M, D] (x_new of the forward); rstd [M] fp32; w [D] fp32; scale [B, D] or null (batch stride mod_bs);
 // y [M, D] or null; gate [B, D] or null (batch stride gate_bs).
 // Outputs: dx [M, D]; dy [M, D] (only with y and gate); dshift, dscale [B, D] fp32 (only with scale);
-// dgate [B, D] fp32 (only with gate); dw [D] fp32 is accumulated (+=), so clear it first for a plain gradient.
+// dgate [B, D] fp32 (only with y and gate); dw [D] fp32 is accumulated (+=), so clear it first for a plain
+// gradient.
 // Same results as the allocating entry point, on the given stream.
 int tgo_adanorm_bwd_noalloc(const void* dh, const void* dxe, const void* xn, const float* rstd, const float* w,
                             const void* scale, long long mod_bs, const void* y, const void* gate, long long gate_bs,
@@ -97,10 +112,17 @@ int tgo_adanorm_bwd_noalloc(const void* dh, const void* dxe, const void* xn, con
     return TGO_NOALLOC_BAD_ARGS;
   if (scale != nullptr && (dshift == nullptr || dscale == nullptr)) return TGO_NOALLOC_BAD_ARGS;
   if (gate != nullptr && y != nullptr && (dy == nullptr || dgate == nullptr)) return TGO_NOALLOC_BAD_ARGS;
-  const long long B = M / T;
-  if (B * 4ll * D > kNoAllocScratchFloats) return TGO_NOALLOC_TOO_LARGE;
-  int rows = 32;
-  while (B * ((T + rows - 1) / rows) * 4ll * D > kNoAllocScratchFloats) rows += 32;
+  // 16-byte vector loads / stores of bf16 rows and of the scale / gate vectors; scalar fp32 accesses.
+  for (const void* p : {dh, dxe, xn, scale, y, gate, static_cast<const void*>(dx), static_cast<const void*>(dy)})
+    if (misaligned(p, 16)) return TGO_NOALLOC_BAD_ARGS;
+  for (const void* p : {static_cast<const void*>(rstd), static_cast<const void*>(w), static_cast<const void*>(dshift),
+                        static_cast<const void*>(dscale), static_cast<const void*>(dgate),
+                        static_cast<const void*>(dw)})
+    if (misaligned(p, 4)) return TGO_NOALLOC_BAD_ARGS;
+  if (scale != nullptr && (mod_bs < 0 || mod_bs % 8 != 0)) return TGO_NOALLOC_BAD_ARGS;
+  if (gate != nullptr && (gate_bs < 0 || gate_bs % 8 != 0)) return TGO_NOALLOC_BAD_ARGS;
+  const int rows = noalloc_rows(M, D, T);
+  if (rows < 0) return TGO_NOALLOC_TOO_LARGE;
   float* scratch = nullptr;
   if (scratch_for_current_device(&scratch) != cudaSuccess) return TGO_NOALLOC_CUDA_ERROR;
 
