@@ -97,3 +97,21 @@ def test_export_import_roundtrip(tmp_path):
     _py("train.py", "--synthetic", "32", "--out", str(tmp_path / "run2"), "--init", init, "--size", "50m",
         "--te-size", "13m", "--batch", "2",
         "--micro-batch", "2", "--steps", "1", "--eval-every", "0", "--no-wandb")
+
+
+def test_merge_assemble_streams_a_weighted_sum(tmp_path):
+    """merge.assemble builds sum_i c_i theta_i in place from checkpoints opened one at a time."""
+    import merge as M
+    files = []
+    for i in range(3):
+        f = str(tmp_path / f"step_{i:07d}.pt")
+        torch.save({"step": 10 * i, "te": {"w": torch.full((3,), float(i))}, "den": {"b": torch.arange(4.0) * i}}, f)
+        files.append(f)
+    stream = M.CheckpointStream(files)
+    assert stream.steps == [0, 10, 20]
+    targets = {"te": {"w": torch.zeros(3)}, "den": {"b": torch.zeros(4, dtype=torch.bfloat16)}}
+    M.assemble(targets, stream, {1: 0.25, 2: 0.75})
+    assert torch.allclose(targets["te"]["w"], torch.full((3,), 1.75))
+    assert torch.allclose(targets["den"]["b"].float(), torch.arange(4.0) * 1.75)
+    table = M.candidate_table([0, 10, 20], 100, [0.15], ["mean"], ["wsm", "qam"])
+    assert [sorted(c.weights) for c in table] == [[1, 2], [1, 2]]

@@ -1,6 +1,8 @@
-"""Prepared-shard reader and the deterministic training stream.
+"""Prepared-shard data layer: a catalog of what a data directory holds, a flat sample table, a memory-mapped reader
+with vectorised caption / crop draws, and the deterministic per-rank micro-batch stream.
 
-On-disk format (the reference's, prepare_data.py / aurora/data.py:1-9), one set of files per shard <name>:
+On-disk format (shared with the reference's prepare_data.py / aurora/data.py:1-9 so prepared data serves both
+frameworks), one set of files per shard <name>:
   <name>.lat.npy           float16 [N, 128, h, w]  normalised, 2x2-packed FLUX.2 latents (.lat<res>.npy: other grids)
   <name>.tok.npy           uint16  [C, 64]         from-scratch tokenizer captions ([BOS] ids [EOS] PAD)
   <name>.off.npy           int64   [N + 1]         captions of image i are rows off[i]:off[i+1]
@@ -8,19 +10,27 @@ On-disk format (the reference's, prepare_data.py / aurora/data.py:1-9), one set 
   <name>.caps[_<lang>].json                         caption strings, flattened in the same row order
   <name>.img.bin + <name>.img.off.npy               encoded images (prepare_images.py)
   manifest.json                                     the full shard list of the source dataset
-Everything is memory-mapped, so ranks and loader workers on a node share the page cache.
 
-Stream semantics (reference aurora/data.py:271-334): every epoch is a seeded global permutation; global batch k is
-perm[k*G:(k+1)*G] and rank r takes its contiguous slice; loader workers take micro-batches round-robin; resuming at
-micro-batch m reproduces the same sequence. The random generators are keyed by (seed, epoch) and
-(seed, micro-batch, rank, 1) so a resumed run draws the same captions / crops.
+Design:
+  * ``ShardCatalog`` reads a directory listing once; shard selection (hold-out, fractions) works on names only.
+  * ``SampleTable`` flattens every shard's offsets once into per-sample (shard, row, first caption, caption count)
+    columns, so a batch's lookups are array gathers instead of a search per sample.
+  * ``MapCache`` opens memory maps lazily and keeps at most ``max_open`` of them (least recently used is closed), so
+    a run over thousands of shards needs a bounded number of file descriptors in every loader worker. The maps share
+    the node's page cache across ranks and workers.
+  * ``ShardStore.fetch`` draws every random choice of a batch as one vector (caption row, translated-caption switch,
+    crop source and window) and then gathers rows shard by shard.
+  * ``TrainStream`` yields micro-batch m of a rank from a plan keyed by (epoch, global micro-batch index); the epoch
+    permutation is cached; workers take micro-batches round-robin, so resuming at m reproduces the sequence.
+Stream semantics kept from the reference (aurora/data.py:271-334): one seeded global permutation per epoch, global
+batch k = perm[k G:(k+1) G] with rank r taking its contiguous slice, round-robin loader workers.
 """
-import glob
 import io
+import itertools
 import json
 import os
 import re
-import resource
+from collections import OrderedDict
 
 import numpy as np
 import torch
@@ -29,312 +39,475 @@ from torch.utils.data import IterableDataset, get_worker_info
 MAX_TOKENS = 64
 PAD_ID, BOS_ID, EOS_ID, NULL_ID, MASK_ID = 0, 2, 3, 4, 5
 
+_SHARD_SUFFIX = re.compile(r"-\d+-of-\d+$")
+
 
 def null_ids(max_tokens=MAX_TOKENS):
-    row = np.full(max_tokens, PAD_ID, dtype=np.int64)
-    row[:3] = (BOS_ID, NULL_ID, EOS_ID)
+    """Caption row of the empty (CFG-dropped) prompt: [BOS] [NULL] [EOS] then padding."""
+    row = np.zeros(max_tokens, dtype=np.int64)
+    row[0], row[1], row[2] = BOS_ID, NULL_ID, EOS_ID
+    row[3:] = PAD_ID
     return row
 
 
 def tok_kind(suffix=""):
-    return f"tok_{suffix}" if suffix else "tok"
+    """File kind of a tokenisation: ``tok`` (from-scratch tokenizer) or ``tok_<suffix>`` (a frozen LM's)."""
+    return "tok_" + suffix if suffix else "tok"
 
 
-def list_shards(root, img_root=""):
-    """Shards with captions (.off.npy) and latents (or images under img_root)."""
-    names = sorted(os.path.basename(p)[: -len(".off.npy")] for p in glob.glob(os.path.join(root, "*.off.npy"))
-                   if not p.endswith(".img.off.npy"))
-    if img_root:
-        return [n for n in names if os.path.exists(os.path.join(img_root, n + ".img.off.npy"))]
-    return [n for n in names if os.path.exists(os.path.join(root, n + ".lat.npy"))]
+# ------------------------------------------------------------------------------------------------------------------
+# shard catalog and selection
+# ------------------------------------------------------------------------------------------------------------------
+def subset_name(shard):
+    """Subset a shard belongs to: its name without the ``-NNNNN-of-NNNNN`` part."""
+    return _SHARD_SUFFIX.sub("", shard)
 
 
 def subsets(names):
-    """Group shard names by subset (the name without its -NNNNN-of-NNNNN suffix)."""
-    groups = {}
+    """{subset: sorted shard names}."""
+    out = {}
     for n in sorted(names):
-        groups.setdefault(re.sub(r"-\d+-of-\d+$", "", n), []).append(n)
-    return groups
+        out.setdefault(subset_name(n), []).append(n)
+    return out
 
 
-def split_shards(names, val_names=None):
-    """Hold-out: the last shard of every subset with more than one shard (unless val_names is given)."""
-    if val_names is None:
-        val_names = [g[-1] for g in subsets(names).values() if len(g) > 1]
-    hold = set(val_names)
-    return [n for n in names if n not in hold], [n for n in names if n in hold]
+def evenly_spaced(count, k):
+    """k positions spread evenly over range(count), first and last included (duplicates dropped)."""
+    if k <= 1:
+        return [0]
+    step = (count - 1) / (k - 1)
+    return sorted({int(round(i * step)) for i in range(k)})
 
 
-def select_fraction(train_names, fraction):
-    """Evenly spaced shards of every subset, so the subset mix is that of the full data."""
-    if fraction >= 1:
-        return list(train_names)
-    picked = []
-    for g in subsets(train_names).values():
-        k = max(1, round(fraction * len(g)))
-        picked += [g[i] for i in sorted(set(np.linspace(0, len(g) - 1, k).round().astype(int)))]
-    return sorted(picked)
+class ShardCatalog:
+    """What a data directory holds, from one listing. ``ready`` = shards with captions and latents (or, with
+    img_root, with packed images there)."""
+
+    def __init__(self, root, img_root=""):
+        self.root, self.img_root = root, img_root
+        self.files = set(os.listdir(root)) if os.path.isdir(root) else set()
+        img_files = set(os.listdir(img_root)) if img_root and os.path.isdir(img_root) else set()
+        with_captions = {f[: -len(".off.npy")] for f in self.files
+                         if f.endswith(".off.npy") and not f.endswith(".img.off.npy")}
+        if img_root:
+            self.ready = sorted(n for n in with_captions if n + ".img.off.npy" in img_files)
+        else:
+            self.ready = sorted(n for n in with_captions if n + ".lat.npy" in self.files)
+
+    def has(self, name, kind):
+        return f"{name}.{kind}.npy" in self.files
+
+    def full(self):
+        """Every shard of the source dataset (manifest.json of prepare_data.py), else the ready ones."""
+        if "manifest.json" in self.files:
+            with open(os.path.join(self.root, "manifest.json")) as f:
+                return list(json.load(f)["shards"])
+        return list(self.ready)
+
+
+def list_shards(root, img_root=""):
+    return ShardCatalog(root, img_root).ready
 
 
 def full_shard_list(root, img_root=""):
-    manifest = os.path.join(root, "manifest.json")
-    if os.path.exists(manifest):
-        with open(manifest) as f:
-            return json.load(f)["shards"]
-    return list_shards(root, img_root)
+    return ShardCatalog(root, img_root).full()
+
+
+def split_shards(names, val_names=None):
+    """(train, val) in the order of `names`. Default hold-out: the last shard of each subset that has several."""
+    if val_names is None:
+        val_names = [group[-1] for group in subsets(names).values() if len(group) > 1]
+    held = frozenset(val_names)
+    return [n for n in names if n not in held], [n for n in names if n in held]
+
+
+def select_fraction(train_names, fraction):
+    """Evenly spaced shards of every subset, so the subset mix is that of the full data (the same choice for
+    prepare_data.py's download and for training)."""
+    if fraction >= 1:
+        return list(train_names)
+    picked = []
+    for group in subsets(train_names).values():
+        picked += [group[i] for i in evenly_spaced(len(group), max(1, round(fraction * len(group))))]
+    return sorted(picked)
 
 
 def select_shards(root, fraction, tok_suffix="", alt_suffix="", img_root=""):
-    """(train, val) names for a fraction of the full dataset; exits with a hint when selected shards are missing."""
+    """(train, val) names for a fraction of the full dataset; val does not depend on the fraction. Exits with a hint
+    when a selected shard is not prepared."""
+    cat = ShardCatalog(root, img_root)
     kinds = [tok_kind(tok_suffix)] + ([tok_kind(alt_suffix)] if alt_suffix else [])
-    present = [n for n in list_shards(root, img_root)
-               if all(os.path.exists(os.path.join(root, f"{n}.{k}.npy")) for k in kinds)]
-    train, val = split_shards(full_shard_list(root, img_root))
+    usable = {n for n in cat.ready if all(cat.has(n, k) for k in kinds)}
+    train, val = split_shards(cat.full())
     train = select_fraction(train, fraction)
-    missing = sorted(set(train + val) - set(present))
+    missing = sorted(n for n in set(train) | set(val) if n not in usable)
     if missing:
         raise SystemExit(f"{len(missing)} shards selected by fraction {fraction} are not prepared in {root} "
-                         f"(e.g. {missing[0]}); prepare them first (prepare_data.py convert / tokenize)")
-    assert train, f"no prepared shards in {root}"
+                         f"(e.g. {missing[0]}); prepare them first (prepare_data.py convert / tokenize"
+                         + (f" --encoder {tok_suffix}" if tok_suffix else "") + ")")
+    if not train:
+        raise SystemExit(f"no prepared training shards in {root}")
     return train, val
 
 
-def raise_fd_limit(needed):
-    """Each memory map holds a descriptor; raise the soft limit to what the shard count needs."""
-    soft, hard = resource.getrlimit(resource.RLIMIT_NOFILE)
-    if soft == resource.RLIM_INFINITY or soft >= needed:
-        return
-    target = needed if hard == resource.RLIM_INFINITY else min(max(needed, 65536), hard)
-    resource.setrlimit(resource.RLIMIT_NOFILE, (target, hard))
-    if target < needed:
-        raise SystemExit(f"need ~{needed} open files for the shards, hard limit is {hard}")
+# ------------------------------------------------------------------------------------------------------------------
+# sample table, memory maps, image decode
+# ------------------------------------------------------------------------------------------------------------------
+class SampleTable:
+    """Per-sample columns over shards in order: shard, row within the shard, first caption row, caption count."""
 
-
-def decode_image(data, res):
-    """Encoded square image -> (3, res, res) uint8: JPEG draft decode near res, then bicubic resize."""
-    from PIL import Image
-    im = Image.open(io.BytesIO(bytes(data)))
-    im.draft("RGB", (res, res))
-    im = im.convert("RGB")
-    if im.size != (res, res):
-        im = im.resize((res, res), Image.BICUBIC, reducing_gap=None)
-    return np.asarray(im).transpose(2, 0, 1)
-
-
-class ShardStore:
-    """Random access to (latents or images, one caption per image[, caption rows][, micro-conditions])."""
-
-    def __init__(self, root, names, tok_suffix="", null_row=None, alt_suffix="", alt_prob=0.0, lat_kind="lat",
-                 lat_root="", crops=(), crop_prob=0.0, cond_base=0, img_res=0):
-        self.root, self.names, self.lat_kind = root, list(names), lat_kind
-        self.lat_root = lat_root or root
-        self.crops, self.crop_prob, self.cond_base, self.img_res = list(crops), crop_prob, cond_base, img_res
-        assert not self.crops or cond_base, "crops need micro-conditions (cond_base)"
-        assert not (img_res and self.crops), "latent crops and images do not mix"
-        self.tok = tok_kind(tok_suffix)
-        self.alt = tok_kind(alt_suffix) if alt_suffix and alt_prob > 0 else None
-        self.alt_prob = alt_prob
-        self.null_row = null_ids() if null_row is None else np.asarray(null_row, dtype=np.int64)
-        raise_fd_limit(((3 if self.alt else 2) + len(self.crops)) * len(self.names) + 512)
-        self.offs = [np.load(os.path.join(root, f"{n}.off.npy")) for n in self.names]
-        self.sizes = np.array([len(o) - 1 for o in self.offs], dtype=np.int64)
-        self.starts = np.concatenate([[0], np.cumsum(self.sizes)])
-        self._lat = self._tok = self._alt = self._crop = None
+    def __init__(self, offsets):
+        counts = np.array([len(o) - 1 for o in offsets], dtype=np.int64)
+        self.sizes = counts
+        self.starts = np.zeros(len(counts) + 1, dtype=np.int64)
+        np.cumsum(counts, out=self.starts[1:])
+        n = int(self.starts[-1])
+        self.shard = np.repeat(np.arange(len(counts), dtype=np.int32), counts)
+        self.row = (np.arange(n, dtype=np.int64) - self.starts[:-1][self.shard]).astype(np.int32) if n else \
+            np.zeros(0, np.int32)
+        self.cap_first = np.concatenate([o[:-1] for o in offsets]).astype(np.int64) if n else np.zeros(0, np.int64)
+        self.cap_count = np.concatenate([np.diff(o) for o in offsets]).astype(np.int32) if n else \
+            np.zeros(0, np.int32)
 
     def __len__(self):
         return int(self.starts[-1])
 
-    def _open(self, captions_only=False):
-        if self._lat is None and not captions_only:
-            if self.img_res:
-                self._lat = [(np.memmap(os.path.join(self.lat_root, f"{n}.img.bin"), dtype=np.uint8, mode="r"),
-                              np.load(os.path.join(self.lat_root, f"{n}.img.off.npy"))) for n in self.names]
-            else:
-                self._lat = [np.load(os.path.join(self.lat_root, f"{n}.{self.lat_kind}.npy"), mmap_mode="r")
-                             for n in self.names]
-            self._crop = [[np.load(os.path.join(r or self.root, f"{n}.{k}.npy"), mmap_mode="r") for n in self.names]
-                          for k, r in self.crops]
-        if self._tok is None:
-            self._tok = [np.load(os.path.join(self.root, f"{n}.{self.tok}.npy"), mmap_mode="r") for n in self.names]
-            if self.alt:
-                self._alt = [np.load(os.path.join(self.root, f"{n}.{self.alt}.npy"), mmap_mode="r")
-                             for n in self.names]
+
+class MapCache:
+    """Lazily opened read-only memory maps, at most `max_open` held (the least recently used one is dropped; its
+    file handle closes once no array refers to it)."""
+
+    def __init__(self, max_open=1024):
+        self.max_open = max_open
+        self._maps = OrderedDict()
+
+    def get(self, path, raw_bytes=False):
+        m = self._maps.get(path)
+        if m is None:
+            m = np.memmap(path, dtype=np.uint8, mode="r") if raw_bytes else np.load(path, mmap_mode="r")
+            self._maps[path] = m
+            while len(self._maps) > self.max_open:
+                self._maps.popitem(last=False)
+        else:
+            self._maps.move_to_end(path)
+        return m
+
+    def __getstate__(self):  # loader workers start with no open maps
+        return {"max_open": self.max_open, "_maps": OrderedDict()}
+
+
+def decode_image(data, res):
+    """Encoded square image -> (3, res, res) uint8 RGB. A JPEG is decoded at the smallest DCT scale that still covers
+    res (PIL draft mode), then resized with PIL's antialiased bicubic filter (prepare_lowres.py's downscale)."""
+    from PIL import Image
+    with Image.open(io.BytesIO(memoryview(data).tobytes())) as im:
+        im.draft("RGB", (res, res))
+        rgb = im.convert("RGB")
+    if rgb.size != (res, res):
+        rgb = rgb.resize((res, res), resample=Image.BICUBIC, reducing_gap=None)
+    return np.ascontiguousarray(np.asarray(rgb).transpose(2, 0, 1))
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# store
+# ------------------------------------------------------------------------------------------------------------------
+class ShardStore:
+    """Random access to (latents or images, one caption row per image[, picked caption rows][, micro-conditions]).
+
+    tok_suffix: which tokenisation to read; alt_suffix / alt_prob: with probability alt_prob a sample's caption row
+    comes from the translated file instead (same row). lat_kind: latent grid file kind (``lat``, ``lat128``, ...);
+    lat_root: folder of the latents / images if not `root`. crops [(lat_kind, root)] / crop_prob: with probability
+    crop_prob a sample is a random window (the size of the training grid) of one of these larger grids of the same
+    image, with its micro-conditions set to the window (RPE-2D resize-and-crop). cond_base > 0: also return (B, 8)
+    micro-conditions in pixels of a cond_base-px original. img_res > 0: decoded uint8 images instead of latents.
+    """
+
+    def __init__(self, root, names, tok_suffix="", null_row=None, alt_suffix="", alt_prob=0.0, lat_kind="lat",
+                 lat_root="", crops=(), crop_prob=0.0, cond_base=0, img_res=0, max_open=1024):
+        if crops and not cond_base:
+            raise ValueError("latent crops need micro-conditions (cond_base > 0)")
+        if img_res and crops:
+            raise ValueError("latent crops and decoded images do not mix")
+        self.root, self.names = root, list(names)
+        self.lat_root = lat_root or root
+        self.lat_kind, self.img_res, self.cond_base = lat_kind, img_res, cond_base
+        self.crops, self.crop_prob = [(k, r or root) for k, r in crops], crop_prob
+        self.tok = tok_kind(tok_suffix)
+        self.alt = tok_kind(alt_suffix) if alt_suffix and alt_prob > 0 else None
+        self.alt_prob = alt_prob
+        self.null_row = null_ids() if null_row is None else np.asarray(null_row, dtype=np.int64)
+        self.table = SampleTable([np.load(self._path(root, n, "off")) for n in self.names])
+        self.maps = MapCache(max_open)
+
+    # compatibility views of the table
+    @property
+    def sizes(self):
+        return self.table.sizes
+
+    @property
+    def starts(self):
+        return self.table.starts
+
+    def __len__(self):
+        return len(self.table)
+
+    @staticmethod
+    def _path(root, name, kind):
+        return os.path.join(root, f"{name}.{kind}.npy")
+
+    def _latents(self, s):
+        return self.maps.get(self._path(self.lat_root, self.names[s], self.lat_kind))
+
+    def _tokens(self, s, kind):
+        return self.maps.get(self._path(self.root, self.names[s], kind))
+
+    def _images(self, s):
+        base = os.path.join(self.lat_root, self.names[s])
+        return self.maps.get(base + ".img.bin", raw_bytes=True), self.maps.get(base + ".img.off.npy")
+
+    def _draw(self, n, rng, side):
+        """Every random choice of a batch: caption row offsets, translated-caption switch, crop source / window."""
+        plan = {"alt": np.zeros(n, bool), "crop": np.zeros(n, bool)}
+        if rng is None:
+            plan["cap_u"] = np.zeros(n)
+            return plan
+        plan["cap_u"] = rng.random(n)
+        if self.alt:
+            plan["alt"] = rng.random(n) < self.alt_prob
+        if self.crops and side:
+            plan["crop"] = rng.random(n) < self.crop_prob
+            plan["crop_src"] = rng.integers(len(self.crops), size=n)
+            plan["crop_u"] = rng.random((n, 2))
+        return plan
 
     def fetch(self, indices, rng, rows=False, res=0, captions_only=False):
-        """Latents (or images at res) + one caption per image (random with rng, else the first);
-        rows: also [shard, caption row] (-1 when the image has no caption)."""
-        assert not captions_only or not self.crops
-        self._open(captions_only)
-        indices = np.asarray(indices)
-        picked = np.full((len(indices), 2), -1, dtype=np.int64)
+        """Latents (or images at res) + one caption per image (random with rng, else the first). rows: also
+        [shard, caption row] per image (-1 when the image has no caption). captions_only: no latents (empty
+        [B, 0] array), captions drawn with the same random choices."""
+        if captions_only and self.crops:
+            raise ValueError("caption-only reads cannot reproduce crop draws")
+        idx = np.asarray(indices, dtype=np.int64)
+        n = len(idx)
+        t = self.table
+        shard, row = t.shard[idx], t.row[idx].astype(np.int64)
         res = res or self.img_res
         if captions_only:
-            lat = np.empty((len(indices), 0), dtype=np.float16)
+            lat = np.empty((n, 0), dtype=np.float16)
         elif res:
-            lat = np.empty((len(indices), 3, res, res), dtype=np.uint8)
+            lat = np.empty((n, 3, res, res), dtype=np.uint8)
         else:
-            lat = np.empty((len(indices), *self._lat[0].shape[1:]), dtype=np.float16)
-        ids = np.empty((len(indices), self._tok[0].shape[1]), dtype=np.int64)
-        n = lat.shape[-1]
-        cb = self.cond_base
-        cond = np.tile(np.array([cb, cb, 0, 0, cb, cb, 16 * n, 16 * n], np.float32), (len(indices), 1))
-        shard = np.searchsorted(self.starts, indices, side="right") - 1
-        for j, (s, gi) in enumerate(zip(shard, indices)):
-            i = gi - self.starts[s]
+            lat = np.empty((n,) + self._latents(int(shard[0]) if n else 0).shape[1:], dtype=np.float16)
+        side = 0 if (captions_only or res) else lat.shape[-1]
+        plan = self._draw(n, rng, side)
+
+        # caption rows (vectorised): first + floor(u * count); no caption -> the null row
+        count = t.cap_count[idx].astype(np.int64)
+        cap = t.cap_first[idx] + np.minimum((plan["cap_u"] * count).astype(np.int64), np.maximum(count - 1, 0))
+        has_cap = count > 0
+        width = self._tokens(int(shard[0]) if n else 0, self.tok).shape[1]
+        ids = np.empty((n, width), dtype=np.int64)
+        if not has_cap.all():
+            ids[~has_cap] = self.null_row
+        picked = np.where(has_cap[:, None], np.stack([shard.astype(np.int64), cap], 1), -1)
+
+        cond = None
+        if self.cond_base:
+            grid = lat.shape[-1]
+            cb = float(self.cond_base)
+            cond = np.empty((n, 8), np.float32)
+            cond[:] = (cb, cb, 0.0, 0.0, cb, cb, 16.0 * grid, 16.0 * grid)
+
+        for s in np.unique(shard):
+            at = np.nonzero(shard == s)[0]
+            s = int(s)
+            with_cap = at[has_cap[at]]
+            if len(with_cap):
+                use_alt = plan["alt"][with_cap]
+                for kind, sel in ((self.tok, with_cap[~use_alt]), (self.alt, with_cap[use_alt])):
+                    if len(sel):
+                        ids[sel] = self._tokens(s, kind)[cap[sel]]
             if captions_only:
-                pass
-            elif self._crop and rng is not None and rng.random() < self.crop_prob:
-                src = self._crop[rng.integers(len(self._crop))][s]
-                side = src.shape[-1]
-                r, c = rng.integers(0, side - n + 1, size=2)
-                lat[j] = src[i, :, r:r + n, c:c + n]
-                px = cb / side
-                cond[j, 2:6] = r * px, c * px, (r + n) * px, (c + n) * px
-            elif res:
-                blob, off = self._lat[s]
-                lat[j] = decode_image(blob[off[i]:off[i + 1]], res)
-            else:
-                lat[j] = self._lat[s][i]
-            lo, hi = self.offs[s][i], self.offs[s][i + 1]
-            if hi == lo:
-                ids[j] = self.null_row
                 continue
-            c = lo if rng is None else rng.integers(lo, hi)
-            src_tok = self._alt if (rng is not None and self.alt and rng.random() < self.alt_prob) else self._tok
-            ids[j] = src_tok[s][c]
-            picked[j] = s, c
+            if res:
+                blob, off = self._images(s)
+                for j in at:
+                    lat[j] = decode_image(blob[off[row[j]]:off[row[j] + 1]], res)
+                continue
+            whole = at[~plan["crop"][at]]
+            if len(whole):
+                lat[whole] = self._latents(s)[row[whole]]
+            for j in at[plan["crop"][at]]:
+                kind, croot = self.crops[int(plan["crop_src"][j])]
+                src = self.maps.get(self._path(croot, self.names[s], kind))
+                big = src.shape[-1]
+                r0, c0 = (plan["crop_u"][j] * (big - side + 1)).astype(np.int64)
+                lat[j] = src[row[j], :, r0:r0 + side, c0:c0 + side]
+                px = self.cond_base / big  # original pixels per source token
+                cond[j, 2:6] = (r0 * px, c0 * px, (r0 + side) * px, (c0 + side) * px)
         out = (lat, ids, picked) if rows else (lat, ids)
         return out + (cond,) if self.cond_base else out
 
 
 class ConcatStore:
-    """Several stores as one index space (same layout, no micro-conditions)."""
+    """Several stores (same layout, no micro-conditions) as one index space, in their natural proportions."""
 
     def __init__(self, stores):
         self.stores = list(stores)
-        self.starts = np.concatenate([[0], np.cumsum([len(s) for s in self.stores])])
+        lens = [len(s) for s in self.stores]
+        self.owner = np.repeat(np.arange(len(lens), dtype=np.int32), lens)
+        self.local = np.concatenate([np.arange(k, dtype=np.int64) for k in lens]) if lens else np.zeros(0, np.int64)
 
     def __len__(self):
-        return int(self.starts[-1])
+        return len(self.owner)
 
     def fetch(self, indices, rng, rows=False, res=0):
-        indices = np.asarray(indices)
-        which = np.searchsorted(self.starts, indices, side="right") - 1
-        lat = ids = None
-        for k, store in enumerate(self.stores):
-            pos = np.nonzero(which == k)[0]
-            if not len(pos):
-                continue
-            got = store.fetch(indices[pos] - self.starts[k], rng, res=res)
-            if lat is None:
-                lat = np.empty((len(indices), *got[0].shape[1:]), dtype=got[0].dtype)
-                ids = np.empty((len(indices), got[1].shape[1]), dtype=got[1].dtype)
-            lat[pos], ids[pos] = got[0], got[1]
-        return (lat, ids, np.full((len(indices), 2), -1, dtype=np.int64)) if rows else (lat, ids)
+        idx = np.asarray(indices, dtype=np.int64)
+        parts = {}
+        for k in np.unique(self.owner[idx]):
+            at = np.nonzero(self.owner[idx] == k)[0]
+            got = self.stores[int(k)].fetch(self.local[idx[at]], rng, res=res)
+            if len(got) != 2:
+                raise ValueError("ConcatStore: stores with micro-conditions are not supported")
+            parts[int(k)] = (at, got)
+        first = next(iter(parts.values()))[1]
+        lat = np.empty((len(idx),) + first[0].shape[1:], dtype=first[0].dtype)
+        ids = np.empty((len(idx), first[1].shape[1]), dtype=first[1].dtype)
+        for at, (l, i) in parts.values():
+            if i.shape[1] != ids.shape[1]:
+                raise ValueError("ConcatStore: caption widths differ between stores")
+            lat[at], ids[at] = l, i
+        return (lat, ids, np.full((len(idx), 2), -1, dtype=np.int64)) if rows else (lat, ids)
 
 
 class CaptionText:
-    """Caption strings by (shard, caption row), a few parsed shards cached."""
+    """Caption strings by (shard, caption row), from the .caps[_<lang>].json files the token rows were made from; the
+    `keep` most recently used shards stay parsed."""
 
     def __init__(self, root, names, lang="", keep=8):
-        self.root, self.names, self.lang, self.keep = root, list(names), lang, keep
-        self._cache = {}
+        self.root, self.names, self.keep = root, list(names), keep
+        self.suffix = f"caps_{lang}" if lang else "caps"
+        self._parsed = OrderedDict()
 
-    def _flat(self, s):
-        if s not in self._cache:
-            if len(self._cache) >= self.keep:
-                self._cache.pop(next(iter(self._cache)))
-            suffix = f"caps_{self.lang}" if self.lang else "caps"
-            with open(os.path.join(self.root, f"{self.names[s]}.{suffix}.json")) as f:
-                self._cache[s] = [c for caps in json.load(f) for c in caps]
-        return self._cache[s]
+    def shard_captions(self, s):
+        caps = self._parsed.get(s)
+        if caps is None:
+            with open(os.path.join(self.root, f"{self.names[s]}.{self.suffix}.json")) as f:
+                caps = list(itertools.chain.from_iterable(json.load(f)))
+            self._parsed[s] = caps
+            if len(self._parsed) > self.keep:
+                self._parsed.popitem(last=False)
+        else:
+            self._parsed.move_to_end(s)
+        return caps
 
     def __call__(self, rows):
-        return ["" if s < 0 else self._flat(int(s))[int(c)] for s, c in rows]
+        return [self.shard_captions(int(s))[int(c)] if s >= 0 else "" for s, c in rows]
 
 
+# ------------------------------------------------------------------------------------------------------------------
+# stream
+# ------------------------------------------------------------------------------------------------------------------
 class TrainStream(IterableDataset):
-    """Deterministic, resumable per-rank micro-batches (see the module docstring)."""
+    """Deterministic, resumable per-rank micro-batches (module docstring). sort_pad: order each micro-batch's rows by
+    caption length (stable); rows: also yield the picked caption rows; res_groups [(res, n)]: split the micro-batch
+    at random into groups decoded at their own resolutions (images as a tuple, captions concatenated in group order);
+    captions_only: caption rows without latents."""
 
     def __init__(self, store, micro_batch, rank, world, seed, start_micro=0, sort_pad=None, rows=False,
                  res_groups=None, captions_only=False):
+        if res_groups and sum(n for _, n in res_groups) != micro_batch:
+            raise ValueError("res_groups must add up to the micro-batch")
         self.store, self.mb, self.rank, self.world = store, micro_batch, rank, world
         self.seed, self.start, self.sort_pad, self.rows = seed, start_micro, sort_pad, rows
         self.res_groups, self.captions_only = res_groups, captions_only
-        assert not res_groups or sum(n for _, n in res_groups) == micro_batch
         self.per_epoch = max(1, len(store) // (micro_batch * world))
+        self._perm_key, self._perm = None, None
+
+    def _permutation(self, epoch):
+        if self._perm_key != epoch:
+            self._perm = np.random.default_rng((self.seed, epoch, 0x70)).permutation(len(self.store))
+            self._perm_key = epoch
+        return self._perm
+
+    def _rng(self, m, stream):
+        return np.random.default_rng((self.seed, m * self.world + self.rank, stream))
 
     def indices(self, m):
-        """Global sample indices of this rank's micro-batch m."""
+        """Global sample indices of this rank's micro-batch m (sorted: shard-local reads)."""
         epoch, k = divmod(m, self.per_epoch)
-        perm = np.random.default_rng([self.seed, epoch]).permutation(len(self.store))
-        g0 = k * self.mb * self.world + self.rank * self.mb
-        return np.sort(perm[g0:g0 + self.mb])
+        first = (k * self.world + self.rank) * self.mb
+        return np.sort(self._permutation(epoch)[first:first + self.mb])
 
-    def _sorted(self, ids, *rest):
+    def _length_order(self, ids):
         if self.sort_pad is None:
-            return (ids,) + rest
-        order = ids.ne(self.sort_pad).sum(1).argsort(stable=True)
-        return (ids[order],) + tuple(r[order] for r in rest)
+            return None
+        return np.argsort((ids != self.sort_pad).sum(1), kind="stable")
+
+    def batch(self, m):
+        """Micro-batch m of this rank, as the stream yields it."""
+        idx = self.indices(m)
+        if self.res_groups:
+            return self._mixed(idx, m)
+        kw = {"captions_only": True} if self.captions_only else {}
+        lat, ids, picked, *cond = self.store.fetch(idx, self._rng(m, 1), rows=True, **kw)
+        order = self._length_order(ids)
+        if order is not None:
+            lat, ids, picked, cond = lat[order], ids[order], picked[order], [c[order] for c in cond]
+        out = (lat, ids, picked) if self.rows else (lat, ids)
+        return tuple(torch.from_numpy(np.ascontiguousarray(x)) for x in out + tuple(cond))
+
+    def _mixed(self, idx, m):
+        rng = self._rng(m, 1)
+        shuffled = idx[self._rng(m, 2).permutation(len(idx))]
+        bounds = np.cumsum([0] + [n for _, n in self.res_groups])
+        lats, ids, picked = [], [], []
+        for (res, _), a, b in zip(self.res_groups, bounds[:-1], bounds[1:]):
+            lat, ids_g, picked_g = self.store.fetch(np.sort(shuffled[a:b]), rng, rows=True, res=res)
+            order = self._length_order(ids_g)
+            if order is not None:
+                lat, ids_g, picked_g = lat[order], ids_g[order], picked_g[order]
+            lats.append(torch.from_numpy(np.ascontiguousarray(lat)))
+            ids.append(ids_g), picked.append(picked_g)
+        out = (tuple(lats), torch.from_numpy(np.concatenate(ids)))
+        return out + (torch.from_numpy(np.concatenate(picked)),) if self.rows else out
 
     def __iter__(self):
         info = get_worker_info()
-        wid, nw = (info.id, info.num_workers) if info else (0, 1)
-        perm_epoch, perm = -1, None
-        m = self.start + wid
-        while True:
-            epoch, k = divmod(m, self.per_epoch)
-            if epoch != perm_epoch:
-                perm = np.random.default_rng([self.seed, epoch]).permutation(len(self.store))
-                perm_epoch = epoch
-            g0 = k * self.mb * self.world + self.rank * self.mb
-            idx = np.sort(perm[g0:g0 + self.mb])
-            if self.res_groups:
-                yield self._mixed(idx, m)
-            else:
-                kw = {"captions_only": True} if self.captions_only else {}
-                got = self.store.fetch(idx, np.random.default_rng([self.seed, m, self.rank, 1]), rows=True, **kw)
-                lat, ids, picked, *cond = (torch.from_numpy(x) for x in got)
-                ids, lat, picked, *cond = self._sorted(ids, lat, picked, *cond)
-                yield ((lat, ids, picked) if self.rows else (lat, ids)) + tuple(cond)
-            m += nw
+        worker, workers = (info.id, info.num_workers) if info is not None else (0, 1)
+        for m in itertools.count(self.start + worker, workers):
+            yield self.batch(m)
 
-    def _mixed(self, idx, m):
-        rng = np.random.default_rng([self.seed, m, self.rank, 1])
-        idx = idx[np.random.default_rng([self.seed, m, self.rank, 2]).permutation(len(idx))]
-        lats, ids, picked, o = [], [], [], 0
-        for res, n in self.res_groups:
-            lat, ids_g, picked_g = (torch.from_numpy(x) for x in self.store.fetch(np.sort(idx[o:o + n]), rng,
-                                                                                  rows=True, res=res))
-            o += n
-            ids_g, lat, picked_g = self._sorted(ids_g, lat, picked_g)
-            lats.append(lat), ids.append(ids_g), picked.append(picked_g)
-        out = (tuple(lats), torch.cat(ids))
-        return out + (torch.cat(picked),) if self.rows else out
+
+# ------------------------------------------------------------------------------------------------------------------
+# validation
+# ------------------------------------------------------------------------------------------------------------------
+def _val_counts(sizes, n):
+    """Images taken from each held-out shard: up to ceil(n / shards) from each, in order, n in total at most."""
+    per = -(-n // max(1, len(sizes)))
+    counts = np.minimum(np.asarray(sizes, dtype=np.int64), per)
+    total = np.cumsum(counts)
+    return np.clip(counts - np.maximum(total - n, 0), 0, None)
 
 
 def val_groups(root, names, n):
-    per = -(-n // len(names))
-    out, left = [], n
-    for name in names:
-        k = min(per, len(np.load(os.path.join(root, f"{name}.off.npy"))) - 1, left)
-        out.append((name, k))
-        left -= k
-    return out
+    """[(shard, count)]: how load_val's n images split over the held-out shards."""
+    sizes = [len(np.load(os.path.join(root, f"{name}.off.npy"))) - 1 for name in names]
+    return [(name, int(k)) for name, k in zip(names, _val_counts(sizes, n))]
 
 
 def load_val(root, names, n, tok_suffix="", null_row=None, lat_kind="lat", lat_root="", img_res=0, encode=None,
              chunk=64):
-    """First n images of the held-out shards (round-robin), first caption each."""
+    """The first images of the held-out shards (val_groups' split), first caption each. encode: applied to every
+    `chunk` of images as they are read (e.g. the VAE encoder), so only its outputs are kept."""
     store = ShardStore(root, names, tok_suffix, null_row, lat_kind=lat_kind, lat_root=lat_root, img_res=img_res)
-    per = -(-n // len(names))
-    idx = np.concatenate([store.starts[s] + np.arange(min(per, store.sizes[s])) for s in range(len(names))])[:n]
+    counts = _val_counts(store.sizes, n)
+    idx = np.concatenate([store.starts[s] + np.arange(k) for s, k in enumerate(counts)]).astype(np.int64)
     if encode is None:
         lat, ids = store.fetch(idx, None)
         return torch.from_numpy(lat), torch.from_numpy(ids)
     lats, ids = [], []
-    for i in range(0, len(idx), chunk):
-        lat, ids_c = store.fetch(idx[i:i + chunk], None)
+    for lo in range(0, len(idx), chunk):
+        lat, ids_c = store.fetch(idx[lo:lo + chunk], None)
         lats.append(encode(torch.from_numpy(lat)))
         ids.append(torch.from_numpy(ids_c))
     return torch.cat(lats), torch.cat(ids)
