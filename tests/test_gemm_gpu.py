@@ -120,3 +120,36 @@ def test_fused_moe_inference_gpu():
     got = FusedMoE(router, gu, dn, 4).to("cuda")(x.cuda().bfloat16())
     err = ((got.float().cpu() - ref).norm() / ref.norm()).item()
     assert err < 3e-2, err  # bf16 inputs and weights against the fp32 products
+
+
+@pytest.mark.parametrize("batch,M,K,with_d", [(8, 2048, 2048, False), (8, 2048, 2048, True), (40, 1000, 512, True),
+                                              (16, 1024, 2048, False), (2, 256, 128, True)])
+def test_gemm_syrk_matches_full_product(batch, M, K, with_d):
+    """Symmetric mode: lower-triangle tiles plus mirrored stores equal the full alpha A A^T + beta D (D symmetric);
+    the last case is too small for the 2-CTA kernel and takes the full-product fallback."""
+    from trenowanie_generatora_obrazkow_b200.ops._ext import check_errors, err_buf, ext
+    torch.manual_seed(2)
+    a = (torch.randn(batch, M, K, device="cuda") / K ** 0.5).bfloat16()
+    d = None
+    if with_d:
+        s = torch.randn(batch, M, M, device="cuda")
+        d = (s + s.mT).bfloat16()
+    c = torch.full((batch, M, M), float("nan"), device="cuda").bfloat16()  # every element must be written
+    ext().gemm_syrk(a, c, d, 0.75, -0.5 if with_d else 0.0, err_buf(a.device))
+    torch.cuda.synchronize()
+    check_errors()
+    ref = 0.75 * a.float() @ a.float().mT
+    if with_d:
+        ref = ref - 0.5 * d.float()
+    assert not torch.isnan(c.float()).any()
+    assert _rel(c, ref) < 1e-2
+    assert torch.equal(c, c.mT)  # exactly symmetric: the upper half is the mirrored lower half
+
+
+def test_newton_schulz_syrk_matches_reference():
+    from trenowanie_generatora_obrazkow_b200.optim.newton_schulz import zeropower, zeropower_reference
+    torch.manual_seed(3)
+    g = torch.randn(12, 1024, 2560, device="cuda")
+    x = zeropower(g)
+    ref = zeropower_reference(g.float())
+    assert _rel(x, ref) < 3e-2

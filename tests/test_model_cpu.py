@@ -15,8 +15,8 @@ REF = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), 
 def _ref_model():
     if not os.path.isdir(os.path.join(REF, "aurora")):
         pytest.skip("reference not installed in baseline/_ref")
-    if REF not in sys.path:
-        sys.path.insert(0, REF)
+    if REF not in sys.path:  # appended: the repository's own same-named scripts keep priority
+        sys.path.append(REF)
     import aurora.model as am
     return am
 

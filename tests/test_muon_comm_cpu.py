@@ -64,8 +64,8 @@ def _worker(rank, world, port, out_dir, momentum_dtype):
         norms.append((float(na), float(nb)))
     comm.export_momentum()
     torch.save(dict(a=[p.detach() for p in pa], b=[p.detach() for p in pb], norms=norms,
-                    ma=[opt_a.state[p]["momentum_buffer"].float() for p in pa],
-                    mb=[opt_b.state[p]["momentum_buffer"].float() for p in pb]),
+                    ma=[opt_a.momentum_buffer(p).float() for p in pa],
+                    mb=[opt_b.momentum_buffer(p).float() for p in pb]),
                os.path.join(out_dir, f"r{rank}.pt"))
     dist.destroy_process_group()
 

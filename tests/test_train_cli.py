@@ -65,7 +65,8 @@ def test_checkpoint_loads_into_reference_modules(tmp_path, shards):
     _run(["--synthetic", "64", "--out", out, "--size", "50m", "--te-size", "13m", "--batch", "2", "--micro-batch",
           "2", "--steps", "1", "--eval-every", "0", "--no-wandb"])
     ck = torch.load(os.path.join(out, "latest.pt"), weights_only=False)
-    sys.path.insert(0, ref)
+    if ref not in sys.path:  # appended: the repository's own same-named scripts keep priority
+        sys.path.append(ref)
     import aurora.model as am
     den = am.Denoiser(am.DenoiserConfig(**ck["den_config"]))
     te = am.TextEncoder(am.TextEncoderConfig(**ck["te_config"]))

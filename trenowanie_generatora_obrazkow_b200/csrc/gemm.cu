@@ -196,6 +196,55 @@ __device__ __forceinline__ void gemm_stage_swiglu(uint8_t* buf, int lane, const 
   }
 }
 
+// Symmetric-product epilogue helpers (2-CTA kernel, bf16 C): the tile's fp32 values with the beta D term, staged
+// as itself or transposed in the 64-byte-swizzled 32 x 32 layout of C's tensor map.
+__device__ __forceinline__ void syrk_values(const GemmParams& p, int b, int row, int col0, const uint32_t (&r)[32],
+                                            float (&f)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(r[i]) * p.alpha;
+  if (p.D != nullptr && row < p.M) {
+    const __nv_bfloat16* d = p.D + (long long)b * p.bsd + (long long)row * p.ldd + col0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (col0 + j * 8 < p.N) {
+        uint4 u = *reinterpret_cast<const uint4*>(d + j * 8);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 v = __bfloat1622float2(h[e]);
+          f[j * 8 + 2 * e] += p.beta * v.x;
+          f[j * 8 + 2 * e + 1] += p.beta * v.y;
+        }
+      }
+    }
+  }
+}
+__device__ __forceinline__ void syrk_stage(uint8_t* buf, int lane, const float (&f)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 u;
+    u.x = pack_bf16x2(f[j * 8 + 0], f[j * 8 + 1]);
+    u.y = pack_bf16x2(f[j * 8 + 2], f[j * 8 + 3]);
+    u.z = pack_bf16x2(f[j * 8 + 4], f[j * 8 + 5]);
+    u.w = pack_bf16x2(f[j * 8 + 6], f[j * 8 + 7]);
+    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = u;
+  }
+}
+// transposed: staged row k = column k of the chunk. Lane pairs exchange one value per two rows, so every lane
+// stores 32-bit words: even lanes (T[k][l], T[k][l+1]), odd lanes (T[k+1][l-1], T[k+1][l]); the two rows a store
+// instruction covers fill all 32 banks.
+__device__ __forceinline__ void syrk_stage_t(uint8_t* buf, int lane, const float (&f)[32]) {
+  const bool odd = lane & 1;
+  const int col = lane & ~1;
+#pragma unroll
+  for (int k = 0; k < 32; k += 2) {
+    const float recv = __shfl_xor_sync(0xffffffffu, odd ? f[k] : f[k + 1], 1);
+    const uint32_t word = odd ? pack_bf16x2(recv, f[k + 1]) : pack_bf16x2(f[k], recv);
+    const int trow = odd ? k + 1 : k;
+    *reinterpret_cast<uint32_t*>(buf + trow * 64 + (((col >> 3) ^ ((trow >> 1) & 3)) << 4) + ((col * 2) & 15)) = word;
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI, int PEER = PEER_NONE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -495,9 +544,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   const int cluster = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
   const int num_m = (p.M + 255) / 256;
   const int num_n = (p.N + G2_BN - 1) / G2_BN;
-  const int tiles_per_batch = num_m * num_n;
+  const bool syrk = p.syrk != 0;
+  const int tiles_per_batch = syrk ? num_m * (num_m + 1) / 2 : num_m * num_n;
   const int num_tiles = tiles_per_batch * p.batch;
   const int num_kb = (p.K + GEMM_BK - 1) / GEMM_BK;
+  // tile index within a batch -> (row block, column block); symmetric mode: the lower triangle, row by row
+  auto tile_mn = [&](int r, int& mt, int& nt) {
+    if (syrk) {
+      int i = (int)((sqrtf(8.f * (float)r + 1.f) - 1.f) * 0.5f);
+      while ((i + 1) * (i + 2) / 2 <= r) ++i;
+      while (i * (i + 1) / 2 > r) --i;
+      mt = i;
+      nt = r - i * (i + 1) / 2;
+    } else {
+      mt = r / num_n;
+      nt = r % num_n;
+    }
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < G2_STAGES; ++s) {
@@ -530,8 +593,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = cluster; tile < num_tiles && !abort_sh; tile += n_clusters) {
-        const int b = tile / tiles_per_batch, r = tile % tiles_per_batch;
-        const int m0 = (r / num_n) * 256 + rank * 128, n0 = (r % num_n) * G2_BN + rank * 128;
+        const int b = tile / tiles_per_batch;
+        int mt, nt;
+        tile_mn(tile % tiles_per_batch, mt, nt);
+        const int m0 = mt * 256 + rank * 128, n0 = nt * G2_BN + rank * 128;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.err, ERR_MBAR_TIMEOUT_PRODUCER)) {
             abort_sh = 1;
@@ -639,10 +704,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       }
       __syncwarp();
       tc_fence_after();
-      const int b = tile / tiles_per_batch, r = tile % tiles_per_batch;
-      const int m0 = (r / num_n) * 256 + rank * 128, n0 = (r % num_n) * G2_BN;
+      const int b = tile / tiles_per_batch;
+      int mt, nt;
+      tile_mn(tile % tiles_per_batch, mt, nt);
+      const int m0 = mt * 256 + rank * 128, n0 = nt * G2_BN;
       const int row = m0 + q * 32 + lane;
       const uint32_t tbase = tmem_base + acc * G2_BN + ((uint32_t)(q * 32) << 16);
+      if constexpr (EPI == EPI_BF16) {
+        if (syrk) {  // the tile, and its mirror image above the diagonal
+#pragma unroll 1
+          for (int c = 0; c < G2_BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tbase + c * 32, v);
+            tmem_ld_wait();
+            float f[32];
+            syrk_values(p, b, row, n0 + c * 32, v, f);
+            tma_chunk([&](uint8_t* buf) { syrk_stage(buf, lane, f); }, n0 + c * 32, m0 + q * 32, b);
+            if (mt != nt) tma_chunk([&](uint8_t* buf) { syrk_stage_t(buf, lane, f); }, m0 + q * 32, n0 + c * 32, b);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+          continue;
+        }
+      }
       if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll 1
         for (int c = 0; c < G2_BN / 64; ++c) {
@@ -732,7 +817,8 @@ static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G2_SMEM);
     attr_set = true;
   }
-  const int num_tiles = ((p.M + 255) / 256) * ((p.N + G2_BN - 1) / G2_BN) * p.batch;
+  const int nm = (p.M + 255) / 256;
+  const int num_tiles = (p.syrk ? nm * (nm + 1) / 2 : nm * ((p.N + G2_BN - 1) / G2_BN)) * p.batch;
   const int grid = std::max(2, std::min(2 * num_tiles, (num_sms() / 2) * 2));
   kern<<<grid, GEMM_THREADS, G2_SMEM, stream>>>(ta, tb, tc != nullptr ? *tc : ta, p);
   return cudaGetLastError();
@@ -805,6 +891,7 @@ cudaError_t gemm_peer_launch(const CUtensorMap& ta, const CUtensorMap& tb, const
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int bn, bool a_mn,
                         bool b_mn, int epi, cudaStream_t s, const CUtensorMap* tc) {
   if (p.c_tma != 0 && tc == nullptr) return cudaErrorInvalidValue;  // TMA epilogue needs C's tensor map
+  if (p.syrk != 0 && (bn != 0 || epi != EPI_BF16 || p.c_tma == 0 || p.M != p.N)) return cudaErrorInvalidValue;
   if (epi == EPI_SWIGLU) {  // forward only (A and B K-major), 256-column tiles
     if (a_mn || b_mn || (bn != 0 && bn != 256) || p.N % 256 != 0) return cudaErrorInvalidValue;
     return bn == 0 ? launch_gemm_pair<false, false, EPI_SWIGLU>(ta, tb, p, s, tc)

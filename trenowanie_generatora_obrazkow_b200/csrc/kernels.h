@@ -44,6 +44,10 @@ struct GemmParams {
   // grouped mode (gemm_grouped_launch): A rows [offsets[g], offsets[g + 1]) use B batch g; C rows as A's
   const int* group_offsets;            // device [batch + 1], batch = groups (<= kMaxGroups)
   const float* row_scale;              // optional [M]: output row r scaled by row_scale[r]
+  // symmetric product (2-CTA kernel, bf16 C through its tensor map, M == N, A and B the same operand): only the
+  // 256-row tile blocks on or below the diagonal are computed; each off-diagonal tile is stored twice (as itself
+  // and transposed). Valid when alpha A B^T + beta D is symmetric (D symmetric or absent).
+  int syrk;
 };
 constexpr int kMaxGroups = 256;
 // epi: 0 = bf16 store, 1 = fp32 store, 2 = fp32 accumulate (C += alpha * A B^T)
@@ -222,15 +226,37 @@ struct MuonMomentumParams {
   int nesterov;
   unsigned long long seed;
 };
+// Single-owner Muon step (the optimizer's local path; same flat, bucket-major Muon space as the sharded path).
+struct MuonSegMomentumParams {
+  const long long* segs;               // [nsegs][3]: (fp32 gradient ptr, offset in the Muon space, length)
+  int nsegs;
+  float* buf_f32;                      // flat momentum, fp32 ...
+  __nv_bfloat16* buf_bf16;             // ... or bf16 with stochastic rounding (exactly one is non-null)
+  __nv_bfloat16* x_out;                // flat Newton-Schulz input
+  const float* coef;                   // gradient-clip coefficient (device scalar)
+  float mu;
+  int nesterov;
+  unsigned long long seed;
+};
+struct MuonApplyParams {
+  const __nv_bfloat16* upd;            // flat orthogonalised updates (the whole Muon space)
+  const long long* segs;               // [nsegs][5]: (fp32 param ptr, bf16 shadow ptr or 0, offset, length,
+                                       //              fp32 EMA ptr or 0)
+  const float* coefs;                  // [nsegs][2]: (alpha, decay): p = p * decay + alpha * U
+  int nsegs;
+  float ema_rate;                      // EMA: e += ema_rate * (p - e) after the update
+};
 struct MuonAGParams {
   __nv_bfloat16* upd[kMaxPeers];       // every rank's update buffer (the whole Muon space)
   uint32_t* flags[kMaxPeers];          // every rank's AG flag array
   const long long* own;                // [nown][2]: (offset, length) of my owned ranges in the Muon space
   int nown;
   long long owned;
-  const long long* segs;               // [nsegs][4]: (fp32 param ptr, bf16 shadow ptr or 0, offset, length)
+  const long long* segs;               // [nsegs][5]: (fp32 param ptr, bf16 shadow ptr or 0, offset, length,
+                                       //              fp32 EMA ptr or 0)
   const float* coefs;                  // [nsegs][2]: (alpha, decay): p = p * decay + alpha * U
   int nsegs;
+  float ema_rate;
   int rank, world;
   uint32_t epoch;
   unsigned long long timeout_ns;
@@ -273,6 +299,32 @@ cudaError_t attention_set_fwd_split(int wpq);  // softmax warps per TMEM lane qu
 cudaError_t attention_set_fwd_emu(int eighths);
 cudaError_t attention_set_fwd_pingpong(int on);  // forward softmax groups alternate their exponential phases  // forward exponentials on the FMA pipe: 0, 2, 3 or 4 eighths
 cudaError_t muon_rs_launch(const MuonRSParams& p, int blocks, cudaStream_t s);
+cudaError_t muon_seg_momentum_launch(const MuonSegMomentumParams& p, int blocks, cudaStream_t s);
+cudaError_t muon_apply_launch(const MuonApplyParams& p, int blocks, cudaStream_t s);
+
+// Optimizer tail (optim.cu): global gradient norm + clip coefficient in one launch, multi-tensor AdamW with the
+// clip coefficient, the bf16 shadow refresh and the EMA update fused in.
+struct GradNormParams {
+  const long long* segs;               // [nsegs][2]: (fp32 gradient ptr, length)
+  int nsegs;
+  float* acc;                          // [1] running sum of squares (zero between launches; the last CTA resets it)
+  unsigned int* counter;               // [1] finished-CTA counter (zero between launches)
+  const float* extra_sumsq;            // optional [1]: squares of gradients counted elsewhere (added to the total)
+  float clip;                          // max norm (<= 0: no clipping, coef = 1)
+  float* gnorm;                        // [1] out: the global norm
+  float* coef;                         // [1] out: min(1, clip / (norm + 1e-6))
+};
+struct AdamWParams {
+  const long long* segs;               // [nsegs][8]: (param, grad, exp_avg, exp_avg_sq fp32 ptrs, bf16 shadow ptr or 0,
+                                       //              fp32 EMA ptr or 0, length, group)
+  int nsegs;
+  const float* hyper;                  // [groups][6]: decay (1 - lr wd), step size (lr / bc1), 1 / sqrt(bc2), eps,
+                                       //              beta1, beta2
+  const float* coef;                   // gradient scale (clip coefficient, device scalar) or null
+  float ema_rate;
+};
+cudaError_t grad_norm_launch(const GradNormParams& p, int blocks, cudaStream_t s);
+cudaError_t adamw_launch(const AdamWParams& p, int blocks, cudaStream_t s);
 cudaError_t muon_momentum_launch(const MuonMomentumParams& p, cudaStream_t s);
 cudaError_t muon_ag_apply_launch(const MuonAGParams& p, int blocks, cudaStream_t s);
 

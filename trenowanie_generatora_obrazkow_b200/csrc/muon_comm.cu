@@ -192,6 +192,77 @@ __global__ void muon_momentum_kernel(MuonMomentumParams p) {
 // ------------------------------------------------------------------------------------------------------------------
 // all-gather of the updates fused with the parameter update
 // ------------------------------------------------------------------------------------------------------------------
+// Chunk c (of C) of every matrix segment: p = p * decay + alpha * U, the bf16 shadow := bf16(p), and the EMA
+// e += ema_rate (p - e) where the segment has one.
+__device__ void apply_segments(const __nv_bfloat16* U, const long long* segs, const float* coefs, int nsegs, int c,
+                               int C, float ema_rate) {
+  for (int s = 0; s < nsegs; ++s) {
+    float* w = reinterpret_cast<float*>(segs[5 * s]);
+    __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(segs[5 * s + 1]);
+    const long long off = segs[5 * s + 2], n = segs[5 * s + 3];
+    float* ema = reinterpret_cast<float*>(segs[5 * s + 4]);
+    const float alpha = coefs[2 * s], decay = coefs[2 * s + 1];
+    const long long chunk = ((n + C - 1) / C + 7) / 8 * 8;
+    const long long a = (long long)c * chunk, b = min(n, a + chunk);
+    const bool vec = (off % 8 == 0) && (reinterpret_cast<uintptr_t>(w) % 16 == 0) &&
+                     (sh == nullptr || reinterpret_cast<uintptr_t>(sh) % 16 == 0) &&
+                     (ema == nullptr || reinterpret_cast<uintptr_t>(ema) % 16 == 0);
+    long long i = a + threadIdx.x * 8;
+    if (vec) {
+      for (; i + 8 <= b; i += (long long)blockDim.x * 8) {
+        const uint4 uu = ld_v4_volatile(U + off + i);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&uu);
+        float4* wp = reinterpret_cast<float4*>(w + i);
+        float4 w0 = wp[0], w1 = wp[1];
+        float2 u0 = __bfloat1622float2(h[0]), u1 = __bfloat1622float2(h[1]);
+        float2 u2 = __bfloat1622float2(h[2]), u3 = __bfloat1622float2(h[3]);
+        w0.x = w0.x * decay + alpha * u0.x;
+        w0.y = w0.y * decay + alpha * u0.y;
+        w0.z = w0.z * decay + alpha * u1.x;
+        w0.w = w0.w * decay + alpha * u1.y;
+        w1.x = w1.x * decay + alpha * u2.x;
+        w1.y = w1.y * decay + alpha * u2.y;
+        w1.z = w1.z * decay + alpha * u3.x;
+        w1.w = w1.w * decay + alpha * u3.y;
+        wp[0] = w0;
+        wp[1] = w1;
+        if (sh != nullptr) {
+          uint4 o;
+          o.x = pack_bf16x2(w0.x, w0.y);
+          o.y = pack_bf16x2(w0.z, w0.w);
+          o.z = pack_bf16x2(w1.x, w1.y);
+          o.w = pack_bf16x2(w1.z, w1.w);
+          *reinterpret_cast<uint4*>(sh + i) = o;
+        }
+        if (ema != nullptr) {
+          float4* ep = reinterpret_cast<float4*>(ema + i);
+          float4 e0 = ep[0], e1 = ep[1];
+          e0.x += ema_rate * (w0.x - e0.x);
+          e0.y += ema_rate * (w0.y - e0.y);
+          e0.z += ema_rate * (w0.z - e0.z);
+          e0.w += ema_rate * (w0.w - e0.w);
+          e1.x += ema_rate * (w1.x - e1.x);
+          e1.y += ema_rate * (w1.y - e1.y);
+          e1.z += ema_rate * (w1.z - e1.z);
+          e1.w += ema_rate * (w1.w - e1.w);
+          ep[0] = e0;
+          ep[1] = e1;
+        }
+      }
+    }
+    // scalar path: misaligned segments, and the < 8-element tail of an aligned one (one thread holds it)
+    long long j = vec ? i : a + threadIdx.x;
+    const long long jstep = vec ? 1 : blockDim.x;
+    for (; j < b; j += jstep) {
+      const float u = __bfloat162float(ld_bf16_volatile(U + off + j));
+      const float v = w[j] * decay + alpha * u;
+      w[j] = v;
+      if (sh != nullptr) sh[j] = __float2bfloat16_rn(v);
+      if (ema != nullptr) ema[j] += ema_rate * (v - ema[j]);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(512) muon_ag_apply_kernel(MuonAGParams p) {
   const int c = blockIdx.x, C = gridDim.x;
   __shared__ int ok_sh;
@@ -224,55 +295,86 @@ __global__ void __launch_bounds__(512) muon_ag_apply_kernel(MuonAGParams p) {
   signal_all_peers(p.flags, p.world, (long long)p.rank * C + c, p.epoch);
   // ---- phase 1: every update has landed; apply chunk c of every matrix ----
   if (!wait_all_flags(p.flags[p.rank], p.world * C, p.epoch, deadline, p.err, &ok_sh)) return;
-  const __nv_bfloat16* U = p.upd[p.rank];
+  apply_segments(p.upd[p.rank], p.segs, p.coefs, p.nsegs, c, C, p.ema_rate);
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// single-owner step: momentum read straight from the gradients (segment table), and the local apply
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float momentum_elem(const MuonSegMomentumParams& p, float g, long long i, float* mq) {
+  float m = p.buf_f32 != nullptr ? p.buf_f32[i] : __bfloat162float(p.buf_bf16[i]);
+  m = m + (1.f - p.mu) * (g - m);
+  if (p.buf_f32 != nullptr) {
+    p.buf_f32[i] = m;
+    *mq = m;
+  } else {
+    const __nv_bfloat16 r = round_stochastic(m, p.seed, i);
+    p.buf_bf16[i] = r;
+    *mq = __bfloat162float(r);
+  }
+  return p.nesterov ? g + p.mu * (*mq - g) : *mq;
+}
+
+__global__ void __launch_bounds__(256) muon_seg_momentum_kernel(MuonSegMomentumParams p) {
+  const int c = blockIdx.x, C = gridDim.x;
+  const float coef = *p.coef;
   for (int s = 0; s < p.nsegs; ++s) {
-    float* w = reinterpret_cast<float*>(p.segs[4 * s]);
-    __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(p.segs[4 * s + 1]);
-    const long long off = p.segs[4 * s + 2], n = p.segs[4 * s + 3];
-    const float alpha = p.coefs[2 * s], decay = p.coefs[2 * s + 1];
+    const float* g = reinterpret_cast<const float*>(p.segs[3 * s]);
+    const long long off = p.segs[3 * s + 1], n = p.segs[3 * s + 2];
     const long long chunk = ((n + C - 1) / C + 7) / 8 * 8;
     const long long a = (long long)c * chunk, b = min(n, a + chunk);
-    const bool vec = (off % 8 == 0) && (reinterpret_cast<uintptr_t>(w) % 16 == 0) &&
-                     (sh == nullptr || reinterpret_cast<uintptr_t>(sh) % 16 == 0);
+    const bool vec = (off % 8 == 0) && (reinterpret_cast<uintptr_t>(g) % 16 == 0);
     long long i = a + threadIdx.x * 8;
     if (vec) {
       for (; i + 8 <= b; i += (long long)blockDim.x * 8) {
-        const uint4 uu = ld_v4_volatile(U + off + i);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&uu);
-        float4* wp = reinterpret_cast<float4*>(w + i);
-        float4 w0 = wp[0], w1 = wp[1];
-        float2 u0 = __bfloat1622float2(h[0]), u1 = __bfloat1622float2(h[1]);
-        float2 u2 = __bfloat1622float2(h[2]), u3 = __bfloat1622float2(h[3]);
-        w0.x = w0.x * decay + alpha * u0.x;
-        w0.y = w0.y * decay + alpha * u0.y;
-        w0.z = w0.z * decay + alpha * u1.x;
-        w0.w = w0.w * decay + alpha * u1.y;
-        w1.x = w1.x * decay + alpha * u2.x;
-        w1.y = w1.y * decay + alpha * u2.y;
-        w1.z = w1.z * decay + alpha * u3.x;
-        w1.w = w1.w * decay + alpha * u3.y;
-        wp[0] = w0;
-        wp[1] = w1;
-        if (sh != nullptr) {
-          uint4 o;
-          o.x = pack_bf16x2(w0.x, w0.y);
-          o.y = pack_bf16x2(w0.z, w0.w);
-          o.z = pack_bf16x2(w1.x, w1.y);
-          o.w = pack_bf16x2(w1.z, w1.w);
-          *reinterpret_cast<uint4*>(sh + i) = o;
+        const long long f = off + i;  // flat index of the first of 8 elements
+        const float4 g0 = *reinterpret_cast<const float4*>(g + i);
+        const float4 g1 = *reinterpret_cast<const float4*>(g + i + 4);
+        const float gv[8] = {g0.x * coef, g0.y * coef, g0.z * coef, g0.w * coef,
+                             g1.x * coef, g1.y * coef, g1.z * coef, g1.w * coef};
+        float m[8], d[8];
+        if (p.buf_f32 != nullptr) {
+          float4* mp = reinterpret_cast<float4*>(p.buf_f32 + f);
+          const float4 m0 = mp[0], m1 = mp[1];
+          m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w;
+          m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) m[k] = m[k] + (1.f - p.mu) * (gv[k] - m[k]);
+          mp[0] = make_float4(m[0], m[1], m[2], m[3]);
+          mp[1] = make_float4(m[4], m[5], m[6], m[7]);
+        } else {
+          uint4* mp = reinterpret_cast<uint4*>(p.buf_bf16 + f);
+          uint4 mu4 = *mp;
+          __nv_bfloat16* mb = reinterpret_cast<__nv_bfloat16*>(&mu4);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float mk = __bfloat162float(mb[k]);
+            mb[k] = round_stochastic(mk + (1.f - p.mu) * (gv[k] - mk), p.seed, f + k);
+            m[k] = __bfloat162float(mb[k]);
+          }
+          *mp = mu4;
         }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) d[k] = p.nesterov ? gv[k] + p.mu * (m[k] - gv[k]) : m[k];
+        uint4 u;
+        u.x = pack_bf16x2(d[0], d[1]);
+        u.y = pack_bf16x2(d[2], d[3]);
+        u.z = pack_bf16x2(d[4], d[5]);
+        u.w = pack_bf16x2(d[6], d[7]);
+        *reinterpret_cast<uint4*>(p.x_out + f) = u;
       }
     }
-    // scalar path: misaligned segments, and the < 8-element tail of an aligned one (one thread holds it)
     long long j = vec ? i : a + threadIdx.x;
     const long long jstep = vec ? 1 : blockDim.x;
     for (; j < b; j += jstep) {
-      const float u = __bfloat162float(ld_bf16_volatile(U + off + j));
-      const float v = w[j] * decay + alpha * u;
-      w[j] = v;
-      if (sh != nullptr) sh[j] = __float2bfloat16_rn(v);
+      float mq;
+      p.x_out[off + j] = __float2bfloat16_rn(momentum_elem(p, g[j] * coef, off + j, &mq));
     }
   }
+}
+
+__global__ void __launch_bounds__(512) muon_apply_kernel(MuonApplyParams p) {
+  apply_segments(p.upd, p.segs, p.coefs, p.nsegs, blockIdx.x, gridDim.x, p.ema_rate);
 }
 
 cudaError_t muon_rs_launch(const MuonRSParams& p, int blocks, cudaStream_t s) {
@@ -292,6 +394,18 @@ cudaError_t muon_momentum_launch(const MuonMomentumParams& p, cudaStream_t s) {
 cudaError_t muon_ag_apply_launch(const MuonAGParams& p, int blocks, cudaStream_t s) {
   if (p.world < 1 || p.world > kMaxPeers || blocks * p.world > kMuonMaxFlags) return cudaErrorInvalidValue;
   muon_ag_apply_kernel<<<blocks, 512, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t muon_seg_momentum_launch(const MuonSegMomentumParams& p, int blocks, cudaStream_t s) {
+  if (p.nsegs == 0) return cudaSuccess;
+  muon_seg_momentum_kernel<<<blocks, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t muon_apply_launch(const MuonApplyParams& p, int blocks, cudaStream_t s) {
+  if (p.nsegs == 0) return cudaSuccess;
+  muon_apply_kernel<<<blocks, 512, 0, s>>>(p);
   return cudaGetLastError();
 }
 

@@ -199,6 +199,59 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor C, bool a_mn, bool b_mn, c10::o
 }
 
 
+// Symmetric product C = alpha A A^T + beta D (D symmetric or absent), A [batch,] M x K K-major, C / D [batch,] M x M
+// bf16: the 2-CTA kernel computes only the tile blocks on and below the diagonal and stores each off-diagonal block
+// twice (csrc/gemm.cu, GemmParams::syrk); shapes too small for the 2-CTA kernel run the full product.
+void gemm_syrk(at::Tensor A, at::Tensor C, c10::optional<at::Tensor> D, double alpha, double beta, at::Tensor err) {
+  TORCH_CHECK(A.is_cuda() && C.is_cuda() && A.scalar_type() == at::kBFloat16 && C.scalar_type() == at::kBFloat16,
+              "gemm_syrk: bf16 CUDA tensors");
+  TORCH_CHECK(A.dim() == C.dim() && (A.dim() == 2 || A.dim() == 3), "gemm_syrk: rank mismatch");
+  TORCH_CHECK(A.stride(-1) == 1 && C.stride(-1) == 1, "gemm_syrk: inner dim must be contiguous");
+  const c10::cuda::CUDAGuard guard(A.device());
+  const bool batched = A.dim() == 3;
+  const int64_t batch = batched ? A.size(0) : 1;
+  const int64_t M = A.size(-2), K = A.size(-1);
+  TORCH_CHECK(C.size(-2) == M && C.size(-1) == M && (!batched || C.size(0) == batch), "gemm_syrk: C shape");
+  TORCH_CHECK(K % 8 == 0 && M % 8 == 0, "gemm_syrk: dims must be multiples of 8");
+  const int64_t tri = ((M + 255) / 256) * ((M + 255) / 256 + 1) / 2 * batch;
+  const bool use_pair = g_gemm_pair_enabled && g_gemm_tma_c && M >= 256 && tri >= num_sms() / 2;
+  if (!use_pair) {
+    gemm(A, A, C, false, false, D, alpha, beta, false, err);
+    return;
+  }
+  const uint64_t bsA = batched ? A.stride(0) : 0;
+  CUtensorMap ta = make_tmap_bf16_sw128(A.data_ptr(), K, M, batch, A.stride(-2), bsA, 128);
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)M;
+  p.K = (int)K;
+  p.batch = (int)batch;
+  p.C = C.data_ptr();
+  p.ldc = C.stride(-2);
+  p.bsc = batched ? C.stride(0) : 0;
+  if (D.has_value() && D->defined()) {
+    TORCH_CHECK(D->scalar_type() == at::kBFloat16 && D->stride(-1) == 1 && D->dim() == C.dim() &&
+                D->size(-2) == M && D->size(-1) == M, "gemm_syrk: D must be bf16 like C");
+    TORCH_CHECK(D->stride(-2) % 8 == 0 && reinterpret_cast<uintptr_t>(D->data_ptr()) % 16 == 0, "gemm_syrk: D align");
+    p.D = reinterpret_cast<const __nv_bfloat16*>(D->data_ptr());
+    p.ldd = D->stride(-2);
+    p.bsd = batched ? D->stride(0) : 0;
+  }
+  TORCH_CHECK(p.ldc % 8 == 0 && reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0, "gemm_syrk: C alignment");
+  p.alpha = (float)alpha;
+  p.beta = (float)beta;
+  p.err = err_ptr(err);
+  p.syrk = 1;
+  CUtensorMap tc;
+  if (!make_tmap_c(&tc, C.data_ptr(), false, M, M, batch, p.ldc, p.bsc)) {
+    gemm(A, A, C, false, false, D, alpha, beta, false, err);
+    return;
+  }
+  p.c_tma = 1;
+  TGO_CHECK_LAUNCH(gemm_launch(ta, ta, p, 0, false, false, 0, at::cuda::getCurrentCUDAStream(), &tc));
+}
+
+
 // ------------------------------------------------------------------------------------------------ helpers
 static const __nv_bfloat16* bf16_ptr_or_null(const c10::optional<at::Tensor>& t) {
   if (!t.has_value() || !t->defined()) return nullptr;
@@ -923,12 +976,12 @@ void muon_momentum(at::Tensor g, at::Tensor buf, at::Tensor x_out, at::Tensor co
 }
 
 void muon_ag_apply(std::vector<int64_t> upd, std::vector<int64_t> flags, at::Tensor own, int64_t owned,
-                   at::Tensor segs, at::Tensor coefs, int64_t rank, int64_t world,
+                   at::Tensor segs, at::Tensor coefs, double ema_rate, int64_t rank, int64_t world,
                    int64_t epoch, int64_t blocks, int64_t timeout_ns, at::Tensor err) {
   TORCH_CHECK(own.is_cuda() && own.scalar_type() == at::kLong && own.dim() == 2 && own.size(1) == 2 &&
               own.is_contiguous(), "muon_ag_apply: own int64 [n, 2] on the device");
-  TORCH_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 4 &&
-              segs.is_contiguous(), "muon_ag_apply: segs int64 [n, 4] on the device");
+  TORCH_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 5 &&
+              segs.is_contiguous(), "muon_ag_apply: segs int64 [n, 5] on the device");
   TORCH_CHECK(coefs.is_cuda() && coefs.scalar_type() == at::kFloat && coefs.is_contiguous() &&
               coefs.numel() == 2 * segs.size(0), "muon_ag_apply: coefs fp32 [n, 2] on the device");
   peer_list(upd, world, "muon_ag_apply upd");
@@ -946,12 +999,101 @@ void muon_ag_apply(std::vector<int64_t> upd, std::vector<int64_t> flags, at::Ten
   p.segs = reinterpret_cast<const long long*>(segs.data_ptr<int64_t>());
   p.coefs = coefs.data_ptr<float>();
   p.nsegs = (int)segs.size(0);
+  p.ema_rate = (float)ema_rate;
   p.rank = (int)rank;
   p.world = (int)world;
   p.epoch = (uint32_t)epoch;
   p.timeout_ns = (unsigned long long)timeout_ns;
   p.err = err_ptr(err);
   TGO_CHECK_LAUNCH(muon_ag_apply_launch(p, (int)blocks, at::cuda::getCurrentCUDAStream()));
+}
+
+// Single-owner Muon step: momentum + Nesterov direction read from the gradients in place (segment table
+// (grad ptr, flat offset, length)), and the parameter update + bf16 shadow refresh from the flat updates.
+void muon_seg_momentum(at::Tensor segs, at::Tensor buf, at::Tensor x_out, at::Tensor coef, double mu, bool nesterov,
+                       int64_t seed, int64_t blocks) {
+  TORCH_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 3 &&
+              segs.is_contiguous(), "muon_seg_momentum: segs int64 [n, 3] on the device");
+  TORCH_CHECK(coef.is_cuda() && coef.scalar_type() == at::kFloat && coef.numel() == 1, "muon_seg_momentum: coef");
+  TORCH_CHECK(buf.is_cuda() && buf.is_contiguous() &&
+              (buf.scalar_type() == at::kFloat || buf.scalar_type() == at::kBFloat16), "muon_seg_momentum: buf");
+  TORCH_CHECK(x_out.is_cuda() && x_out.is_contiguous() && x_out.scalar_type() == at::kBFloat16 &&
+              x_out.numel() == buf.numel(), "muon_seg_momentum: x_out");
+  TORCH_CHECK(blocks >= 1 && blocks <= 65535, "muon_seg_momentum: blocks");
+  const c10::cuda::CUDAGuard guard(buf.device());
+  MuonSegMomentumParams p{};
+  p.segs = reinterpret_cast<const long long*>(segs.data_ptr<int64_t>());
+  p.nsegs = (int)segs.size(0);
+  if (buf.scalar_type() == at::kFloat) p.buf_f32 = buf.data_ptr<float>();
+  else p.buf_bf16 = bfp(buf);
+  p.x_out = bfp(x_out);
+  p.coef = coef.data_ptr<float>();
+  p.mu = (float)mu;
+  p.nesterov = nesterov ? 1 : 0;
+  p.seed = (unsigned long long)seed;
+  TGO_CHECK_LAUNCH(muon_seg_momentum_launch(p, (int)blocks, at::cuda::getCurrentCUDAStream()));
+}
+
+void muon_apply(at::Tensor upd, at::Tensor segs, at::Tensor coefs, double ema_rate, int64_t blocks) {
+  TORCH_CHECK(upd.is_cuda() && upd.is_contiguous() && upd.scalar_type() == at::kBFloat16, "muon_apply: upd");
+  TORCH_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 5 &&
+              segs.is_contiguous(), "muon_apply: segs int64 [n, 5] on the device");
+  TORCH_CHECK(coefs.is_cuda() && coefs.scalar_type() == at::kFloat && coefs.is_contiguous() &&
+              coefs.numel() == 2 * segs.size(0), "muon_apply: coefs fp32 [n, 2] on the device");
+  TORCH_CHECK(blocks >= 1 && blocks <= 65535, "muon_apply: blocks");
+  const c10::cuda::CUDAGuard guard(upd.device());
+  MuonApplyParams p{};
+  p.upd = bfp(upd);
+  p.segs = reinterpret_cast<const long long*>(segs.data_ptr<int64_t>());
+  p.coefs = coefs.data_ptr<float>();
+  p.nsegs = (int)segs.size(0);
+  p.ema_rate = (float)ema_rate;
+  TGO_CHECK_LAUNCH(muon_apply_launch(p, (int)blocks, at::cuda::getCurrentCUDAStream()));
+}
+
+// Global gradient norm and clip coefficient on the device (one launch; see optim.cu).
+void grad_norm(at::Tensor segs, at::Tensor acc, at::Tensor counter, c10::optional<at::Tensor> extra, double clip,
+               at::Tensor gnorm, at::Tensor coef, int64_t blocks) {
+  TORCH_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 2 &&
+              segs.is_contiguous(), "grad_norm: segs int64 [n, 2] on the device");
+  for (const at::Tensor* t : {&acc, &gnorm, &coef})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->numel() >= 1, "grad_norm: fp32 scalars");
+  TORCH_CHECK(counter.is_cuda() && counter.scalar_type() == at::kInt && counter.numel() >= 1, "grad_norm: counter");
+  TORCH_CHECK(blocks >= 1 && blocks <= 65535, "grad_norm: blocks");
+  const c10::cuda::CUDAGuard guard(acc.device());
+  GradNormParams p{};
+  p.segs = reinterpret_cast<const long long*>(segs.data_ptr<int64_t>());
+  p.nsegs = (int)segs.size(0);
+  p.acc = acc.data_ptr<float>();
+  p.counter = reinterpret_cast<unsigned int*>(counter.data_ptr<int>());
+  if (extra.has_value() && extra->defined()) {
+    TORCH_CHECK(extra->is_cuda() && extra->scalar_type() == at::kFloat, "grad_norm: extra");
+    p.extra_sumsq = extra->data_ptr<float>();
+  }
+  p.clip = (float)clip;
+  p.gnorm = gnorm.data_ptr<float>();
+  p.coef = coef.data_ptr<float>();
+  TGO_CHECK_LAUNCH(grad_norm_launch(p, (int)blocks, at::cuda::getCurrentCUDAStream()));
+}
+
+// Multi-tensor AdamW with the clip coefficient, bf16 shadow refresh and EMA fused in (see optim.cu).
+void adamw(at::Tensor segs, at::Tensor hyper, c10::optional<at::Tensor> coef, double ema_rate, int64_t blocks) {
+  TORCH_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 8 &&
+              segs.is_contiguous(), "adamw: segs int64 [n, 8] on the device");
+  TORCH_CHECK(hyper.is_cuda() && hyper.scalar_type() == at::kFloat && hyper.dim() == 2 && hyper.size(1) == 6 &&
+              hyper.is_contiguous(), "adamw: hyper fp32 [groups, 6] on the device");
+  TORCH_CHECK(blocks >= 1 && blocks <= 65535, "adamw: blocks");
+  const c10::cuda::CUDAGuard guard(segs.device());
+  AdamWParams p{};
+  p.segs = reinterpret_cast<const long long*>(segs.data_ptr<int64_t>());
+  p.nsegs = (int)segs.size(0);
+  p.hyper = hyper.data_ptr<float>();
+  if (coef.has_value() && coef->defined()) {
+    TORCH_CHECK(coef->is_cuda() && coef->scalar_type() == at::kFloat, "adamw: coef");
+    p.coef = coef->data_ptr<float>();
+  }
+  p.ema_rate = (float)ema_rate;
+  TGO_CHECK_LAUNCH(adamw_launch(p, (int)blocks, at::cuda::getCurrentCUDAStream()));
 }
 
 // src (contiguous CUDA tensor) -> dst (a peer's mapped buffer), then dst_version := version (see comm.cu)
@@ -984,6 +1126,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("muon_rs", &tgo::muon_rs, "sharded Muon: gradient bucket reduce-scatter to the matrix owners (NVLink)");
   m.def("muon_momentum", &tgo::muon_momentum, "sharded Muon: owner momentum + Nesterov -> bf16 NS input");
   m.def("muon_ag_apply", &tgo::muon_ag_apply, "sharded Muon: update all-gather fused with the parameter update");
+  m.def("muon_seg_momentum", &tgo::muon_seg_momentum, "Muon: momentum + Nesterov from the gradients in place");
+  m.def("muon_apply", &tgo::muon_apply, "Muon: parameter update + bf16 shadow refresh from the flat updates");
+  m.def("grad_norm", &tgo::grad_norm, "global gradient norm and clip coefficient on the device (one launch)");
+  m.def("adamw", &tgo::adamw, "multi-tensor AdamW with clip coefficient, bf16 shadow refresh and EMA fused in");
   m.def("set_attention_fwd_pingpong", &tgo::set_attention_fwd_pingpong,
         "attention forward: the two softmax groups take turns for their exponential phases");
   m.def("set_attention_fwd_emu", &tgo::set_attention_fwd_emu,
@@ -993,6 +1139,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_attention_tc", &tgo::set_attention_tc, "use the tcgen05 attention forward (default) or mma.sync");
   m.def("set_gemm_tma_epilogue", &tgo::set_gemm_tma_epilogue,
         "GEMM epilogue through TMA stores / reduce-adds (default) or per-row global stores");
+  m.def("gemm_syrk", &tgo::gemm_syrk, "symmetric C = alpha A A^T + beta D: lower-triangle tiles, mirrored stores");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");
   m.def("launch_count", &tgo::launch_count, "kernels launched by this extension so far");
   m.def("adanorm_fwd", &tgo::adanorm_fwd, "x_new = x + gate*y; h = rmsnorm(x_new)*w*(1+scale)+shift");

@@ -11,6 +11,7 @@ import math
 
 import torch
 
+from .adamw import FusedAdamW
 from .muon import Muon, muon_splits
 
 
@@ -56,7 +57,10 @@ def build_optimizers(named, optimizer="muon", lr_muon=1e-2, lr_emb=5e-4, lr_adam
     b2 = beta2 if beta2 is not None else (0.99 if optimizer == "adamw" else 0.95)
     if fused_adam is None:
         fused_adam = all(p.is_cuda for g in adam_groups for p in g["params"]) and bool(adam_groups)
-    opts.append(torch.optim.AdamW(adam_groups, betas=(0.9, b2), eps=1e-8, fused=fused_adam))
+    if fused_adam:  # one launch with the clip coefficient, bf16 shadows and the EMA (csrc/optim.cu)
+        opts.append(FusedAdamW(adam_groups, betas=(0.9, b2), eps=1e-8))
+    else:
+        opts.append(torch.optim.AdamW(adam_groups, betas=(0.9, b2), eps=1e-8))
     counts = {k: sum(p.numel() for p in v) for k, v in parts.items()}
     return opts, counts
 
@@ -76,7 +80,10 @@ def set_lr(opts, mult):
 
 
 class EMA:
-    """fp32 exponential moving average of a list of parameters (optionally on the CPU, pinned)."""
+    """fp32 exponential moving average of a list of parameters (optionally on the CPU, pinned).
+
+    Fused optimizers may update the EMA of their own parameters inside their parameter-update launch: they call
+    ``lookup(p)`` for the EMA tensor and ``mark_fused(p)``; ``update`` then skips those parameters for that step."""
 
     def __init__(self, params, decay, device=None):
         self.params = list(params)
@@ -84,14 +91,34 @@ class EMA:
         self.shadow = [p.detach().float().clone().to(device or p.device) for p in self.params]
         if device is not None and str(device) == "cpu" and torch.cuda.is_available():
             self.shadow = [s.pin_memory() for s in self.shadow]
+        self._index = {id(p): i for i, p in enumerate(self.params)}
+        self._fused = set()
+
+    def decay_at(self, step):
+        return min(self.decay, step / (9 + step))
+
+    def lookup(self, p):
+        """The EMA tensor of p when it can be updated in place next to p (same device), else None."""
+        i = self._index.get(id(p))
+        if i is None or self.shadow[i].device != p.device:
+            return None
+        return self.shadow[i]
+
+    def mark_fused(self, p):
+        self._fused.add(id(p))
 
     @torch.no_grad()
     def update(self, step, decay=None):
-        """Per-step update with decay min(ema, step / (9 + step)), or with an explicit ``decay`` (DiLoCo syncs)."""
-        d = decay if decay is not None else min(self.decay, step / (9 + step))
+        """Per-step update with decay min(ema, step / (9 + step)), or with an explicit ``decay`` (DiLoCo syncs).
+        Parameters whose EMA a fused optimizer already updated this step are skipped."""
+        d = decay if decay is not None else self.decay_at(step)
+        todo = [(p, s) for p, s in zip(self.params, self.shadow) if id(p) not in self._fused]
+        self._fused.clear()
+        if not todo:
+            return
         src = [p.detach().float() if p.device == s.device else p.detach().float().to(s.device, non_blocking=True)
-               for p, s in zip(self.params, self.shadow)]
-        torch._foreach_lerp_(self.shadow, src, 1 - d)
+               for p, s in todo]
+        torch._foreach_lerp_([s for _, s in todo], src, 1 - d)
 
     def state_list(self):
         return [s.clone().cpu() for s in self.shadow]

@@ -6,7 +6,10 @@ Iteration (Keller Jordan's Muon; reference aurora/muon.py:25-39 and aurora/ns_tr
 
 On CUDA every product is one launch of the tcgen05 GEMM (csrc/gemm.cu) with the affine terms fused into its
 epilogue (``alpha * acc + beta * D``): A A is formed as A A^T (A is symmetric), and B X reads X MN-major, so no
-transposes are materialised inside the loop.
+transposes are materialised inside the loop. The two symmetric products (X X^T and c A A^T + b A) run in the
+GEMM's symmetric mode (``gemm_syrk``): only the 256-row tile blocks on and below the diagonal are computed and
+each off-diagonal block is stored twice, which halves their tensor work (reference aurora/ns_triton.py:20-48
+computes the lower triangle the same way).
 """
 import torch
 
@@ -48,9 +51,11 @@ def zeropower(G, steps=5):
     A = torch.empty(n, m, m, device=X.device, dtype=torch.bfloat16)
     Bm = torch.empty_like(A)
     Y = torch.empty_like(X)
+    from ..ops._ext import err_buf, ext
+    err = err_buf(X.device)
     for _ in range(steps):
-        gemm(X, X, out=A)                              # A = X X^T
-        gemm(A, A, out=Bm, d=A, alpha=c, beta=b)       # B = c A A^T + b A
+        ext().gemm_syrk(X, A, None, 1.0, 0.0, err)     # A = X X^T            (symmetric)
+        ext().gemm_syrk(A, Bm, A, c, b, err)           # B = c A A^T + b A    (symmetric)
         gemm(Bm, X, out=Y, b_mn=True, d=X, alpha=1.0, beta=a)  # X = B X + a X
         X, Y = Y, X
     if transposed:

@@ -44,29 +44,26 @@ class MuonShardedComm:
         self.device = torch.device(device) if device is not None else first.device
         self.transport = transport if self.device.type == "cuda" else "torch"
         self.blocks, self.timeout_ns = blocks, int(timeout_s * 1e9)
-        # ---- the Muon space: every entry (row block of a matrix), bucket by bucket ----
+        # ---- the Muon space: the optimizer's layout without padding (same entries, order and owners) ----
+        from ..optim.muon import MuonLayout
+        self.layout = MuonLayout(muon.param_groups, muon.splits, self.world, self.rank, pad=False)
         self.entries = []       # dict(p, r0, r1, scale, gi, off, n, owner, oown)
         self.bucket_views = []  # (gi, rows, cols, lo, hi, off_lo, own_lo): owned slice of each shape bucket
-        off = own = 0
-        for gi, buckets in enumerate(muon._buckets):
-            for entries in buckets:
-                per = math.ceil(len(entries) / self.world)
-                rows, cols = entries[0][2] - entries[0][1], entries[0][0].shape[1]
-                lo, hi = min(len(entries), self.rank * per), min(len(entries), (self.rank + 1) * per)
-                own_lo, off_lo = own, None
-                for i, (p, r0, r1, s) in enumerate(entries):
-                    n = (r1 - r0) * cols
-                    owner = i // per
-                    e = dict(p=p, r0=r0, r1=r1, scale=s, gi=gi, off=off, n=n, owner=owner, oown=None)
-                    if owner == self.rank:
-                        if off_lo is None:
-                            off_lo = off
-                        e["oown"] = own
-                        own += n
-                    self.entries.append(e)
-                    off += n
-                if hi > lo:
-                    self.bucket_views.append((gi, rows, cols, lo, hi, off_lo, own_lo))
+        own = 0
+        for b in self.layout.buckets:
+            lo, hi = b.owned_slots(self.rank)
+            own_lo = own
+            for k in b.entries:
+                le = self.layout.entries[k]
+                e = dict(p=le.p, r0=le.r0, r1=le.r1, scale=le.scale, gi=le.group, off=le.off, n=le.n,
+                         owner=le.owner, oown=None)
+                if le.owner == self.rank:
+                    e["oown"] = own
+                    own += le.n
+                self.entries.append(e)
+            if hi > lo:
+                self.bucket_views.append((b.group, b.rows, b.cols, lo, hi, b.off + lo * b.rows * b.cols, own_lo))
+        off = self.layout.total
         self.total, self.owned = off, own
         self.own_ranges = [(v[5], (v[4] - v[3]) * v[1] * v[2]) for v in self.bucket_views]
         # owned elements per param group (contiguous: buckets are laid out group by group)
@@ -129,18 +126,21 @@ class MuonShardedComm:
             self._build_apply_tables()
         return self
 
-    def _shadow_ptrs(self):
-        """(fp32 master, bf16 shadow) addresses of every matrix; ``bf16_weight`` re-creates a shadow whose master
-        was changed by torch in place (load_state_dict, DiLoCo outer step), so the table is checked every step."""
-        return [(e["p"].data_ptr(), Fz.bf16_weight(e["p"]).data_ptr()) for e in self.entries]
-
-    def _build_apply_tables(self):
+    def _apply_rows(self, ema=None):
+        """(fp32 master, bf16 shadow, offset, length, EMA) rows of every entry. ``bf16_weight`` re-creates a shadow
+        whose master was changed by torch in place (load_state_dict, DiLoCo outer step), so the rows are rebuilt
+        and compared every step."""
         rows = []
-        self._ptrs = self._shadow_ptrs()
-        for e, (pp, sp) in zip(self.entries, self._ptrs):
+        for e in self.entries:
             cols = e["p"].shape[1]
-            rows.append([pp + e["r0"] * cols * 4, sp + e["r0"] * cols * 2, e["off"], e["n"]])
-        self.apply_segs = torch.tensor(rows, dtype=torch.int64, device=self.device)
+            ev = ema.lookup(e["p"]) if ema is not None else None
+            rows.append((e["p"].data_ptr() + e["r0"] * cols * 4, Fz.bf16_weight(e["p"]).data_ptr() + e["r0"] * cols * 2,
+                         e["off"], e["n"], 0 if ev is None else ev.data_ptr() + e["r0"] * cols * 4))
+        return rows
+
+    def _build_apply_tables(self, ema=None):
+        self._rows = self._apply_rows(ema)
+        self.apply_segs = torch.tensor(self._rows, dtype=torch.int64, device=self.device).reshape(-1, 5)
         self.own_t = torch.tensor(self.own_ranges if self.own_ranges else [[0, 0]], dtype=torch.int64,
                                   device=self.device).reshape(-1, 2)
         if not self.own_ranges:
@@ -186,9 +186,9 @@ class MuonShardedComm:
     # optimizer step
     # ------------------------------------------------------------------------------------------------------------
     @torch.no_grad()
-    def step(self, coef=1.0):
+    def step(self, coef=1.0, ema=None, ema_rate=0.0):
         """One Muon step from the owned reduced gradients; ``coef`` is the gradient-clip coefficient (float or
-        device scalar)."""
+        device scalar); ``ema`` (optim.groups.EMA, where this rank keeps one): updated inside the apply launch."""
         m = self.muon
         refresh = m._t % m.period == 0
         m._t += 1
@@ -207,7 +207,7 @@ class MuonShardedComm:
             steps = m.param_groups[gi]["ns_steps"]
             Y = zeropower(X, steps) if refresh else rownorm(X) * m.gamma
             upd_local[off_lo:off_lo + n].copy_(Y.reshape(-1))
-        self._gather_apply()
+        self._gather_apply(ema, ema_rate)
 
     def _momentum(self, g, buf, x, coef, mu, nesterov):
         if self.transport == "p2p":
@@ -231,7 +231,7 @@ class MuonShardedComm:
         self.update.zero_()
         return self.update
 
-    def _gather_apply(self):
+    def _gather_apply(self, ema=None, ema_rate=0.0):
         m = self.muon
         coefs = []
         for e in self.entries:
@@ -239,48 +239,59 @@ class MuonShardedComm:
             coefs.append([-g["lr"] * e["scale"], 1 - g["lr"] * g["weight_decay"]])
         if self.transport == "p2p":
             from ..ops._ext import err_buf, ext
-            if self._shadow_ptrs() != self._ptrs:
-                self._build_apply_tables()
+            if self._apply_rows(ema) != self._rows:
+                self._build_apply_tables(ema)
             self.coefs.copy_(torch.tensor(coefs, dtype=torch.float32), non_blocking=False)
             self.ag_epoch = (self.ag_epoch + 1) & 0xFFFFFFFF or 1
             pp = self._peer.ptrs
             ext().muon_ag_apply(pp["update"], pp["ag_flags"], self.own_t, self.owned, self.apply_segs, self.coefs,
-                                self.rank, self.world, self.ag_epoch, self.blocks, self.timeout_ns,
+                                float(ema_rate), self.rank, self.world, self.ag_epoch, self.blocks, self.timeout_ns,
                                 err_buf(self.device))
+            from ..optim.adamw import after_raw_update
+            after_raw_update(e["p"] for e in self.entries)
+            self._mark_ema(ema)
             return
         dist.all_reduce(self.update, group=self.group)  # every owner contributed its ranges, zeros elsewhere
         U = self.update.float()
         for e, (alpha, decay) in zip(self.entries, coefs):
             blk = e["p"][e["r0"]:e["r1"]]  # a view: the in-place update bumps the parameter's version
             blk.mul_(decay).add_(U[e["off"]:e["off"] + e["n"]].view_as(blk), alpha=alpha)
+        if ema is not None:
+            for p in {id(e["p"]): e["p"] for e in self.entries}.values():
+                ev = ema.lookup(p)
+                if ev is not None:
+                    ev.lerp_(p.detach().float(), ema_rate)
+        self._mark_ema(ema)
+
+    def _mark_ema(self, ema):
+        if ema is not None:
+            for e in self.entries:
+                if ema.lookup(e["p"]) is not None:
+                    ema.mark_fused(e["p"])
 
     # ------------------------------------------------------------------------------------------------------------
     # checkpoints: the optimizer's per-parameter momentum buffers <-> the owners' shards
     # ------------------------------------------------------------------------------------------------------------
     @torch.no_grad()
     def export_momentum(self):
-        """Assemble full momentum buffers (all ranks take part) into ``muon.state[p]['momentum_buffer']``."""
+        """Assemble the full momentum (all ranks take part) into the optimizer's flat momentum, from which its
+        ``state_dict`` materialises per-parameter buffers."""
         full = torch.zeros(self.total, dtype=torch.float32, device=self.device)
         for e in self.entries:
             if e["owner"] == self.rank:
                 full[e["off"]:e["off"] + e["n"]] = self.momentum[e["oown"]:e["oown"] + e["n"]].float()
         dist.all_reduce(full, group=self.group)
-        mdt = self.muon.momentum_dtype or torch.float32
-        for e in self.entries:
-            p = e["p"]
-            st = self.muon.state[p]
-            if "momentum_buffer" not in st:
-                st["momentum_buffer"] = torch.zeros_like(p, dtype=mdt)
-            st["momentum_buffer"][e["r0"]:e["r1"]] = full[e["off"]:e["off"] + e["n"]].view(e["r1"] - e["r0"], -1)
+        flat = self.muon.momentum
+        for e, me in zip(self.entries, self.muon.layout.entries):
+            flat[me.off:me.off + me.n] = full[e["off"]:e["off"] + e["n"]].to(flat.dtype)
 
     @torch.no_grad()
     def import_momentum(self):
-        """Take this rank's shards from ``muon.state[p]['momentum_buffer']`` (after ``load_state_dict``)."""
-        for e in self.entries:
-            st = self.muon.state.get(e["p"], {})
-            if e["owner"] == self.rank and "momentum_buffer" in st:
-                src = st["momentum_buffer"][e["r0"]:e["r1"]].reshape(-1)
-                self.momentum[e["oown"]:e["oown"] + e["n"]] = src.to(self.momentum.dtype)
+        """Take this rank's shards from the optimizer's flat momentum (after its ``load_state_dict``)."""
+        flat = self.muon.momentum
+        for e, me in zip(self.entries, self.muon.layout.entries):
+            if e["owner"] == self.rank:
+                self.momentum[e["oown"]:e["oown"] + e["n"]] = flat[me.off:me.off + me.n].to(self.momentum.dtype)
 
 
 def _wrap_bf16(ptr, n, device):

@@ -19,6 +19,7 @@ from ..models import build_models
 from ..models.frozen_lm import LM_NULL, LM_PAD, build_frozen_lm
 from ..models.text import LMTextEncoder
 from ..optim import EMA, build_optimizers, lr_mult, set_lr
+from ..optim.adamw import FusedAdamW, GradNorm
 from ..optim.muon import Muon
 from ..parallel.ddp import GradBuckets
 from . import diloco as D
@@ -193,6 +194,7 @@ class Trainer:
             else:
                 self.buckets = GradBuckets(dense, group=group, comm=cfg.grad_comm if reduce_grads else "none")
         self.ema_decay = ema
+        self.grad_norm = GradNorm(self.device) if self.device.type == "cuda" else None
         self.global_params = self.outer_opt = None
         if cfg.diloco:
             if self.distributed and self.world > 1:
@@ -229,6 +231,11 @@ class Trainer:
         if self.global_params is not None:
             extra["diloco_global"] = list(self.global_params)
         return report(self.rank, params=self.params, grads=grads, opts=self.opts, ema=self.ema, extra=extra)
+
+    def _fused_tail(self):
+        """On-device norm + coefficient: CUDA, gradients in the flat buckets, every optimizer takes a coefficient."""
+        return (self.device.type == "cuda" and self.buckets is not None and self.powersgd is None
+                and all(isinstance(o, (Muon, FusedAdamW)) for o in self.opts))
 
     def before_save(self):
         """All ranks: bring sharded optimizer state into the optimizers' state dicts (collective)."""
@@ -369,7 +376,11 @@ class Trainer:
             torch._foreach_mul_([p.grad for p in self.expert_params if p.grad is not None], 1.0 / self.world)
         coef = None
         if self.muon_comm is None:
-            self.last_gnorm = torch.nn.utils.clip_grad_norm_(self.params, cfg.clip, foreach=True)
+            if self._fused_tail():  # norm + clip coefficient on the device; the optimizers take the coefficient
+                grads = list(self.buckets.flat) + [p.grad for p in self.expert_params if p.grad is not None]
+                self.last_gnorm, coef = self.grad_norm(grads, cfg.clip)
+            else:
+                self.last_gnorm = torch.nn.utils.clip_grad_norm_(self.params, cfg.clip, foreach=True)
         else:  # Muon gradients exist reduced only on their owners: norm = other grads + all-reduced owned squares
             others = [p.grad for p in self.buckets.params if p.grad is not None] + \
                 [p.grad for p in self.expert_params if p.grad is not None]
@@ -377,14 +388,21 @@ class Trainer:
             if others:
                 sq = sq + torch.stack(torch._foreach_norm(others)).square().sum()
             self.last_gnorm = sq.sqrt()
-            coef = (cfg.clip / (self.last_gnorm + 1e-6)).clamp(max=1.0)
-            if others:
-                torch._foreach_mul_(others, coef)
+            coef = (cfg.clip / (self.last_gnorm + 1e-6)).clamp(max=1.0)  # applied by the optimizers
         set_lr(self.opts, lr_mult(self.step_idx, cfg.steps, cfg.warmup, cfg.schedule))
+        # the per-step EMA is updated inside the fused optimizers' parameter-update launches where they can
+        ema = self.ema if (self.ema is not None and not cfg.diloco) else None
+        rate = 1.0 - self.ema.decay_at(self.step_idx + 1) if ema is not None else 0.0
         for o in self.opts:
             if o is self.muon and self.muon_comm is not None:
-                self.muon_comm.step(coef)
+                self.muon_comm.step(coef, ema=ema, ema_rate=rate)
+            elif isinstance(o, (Muon, FusedAdamW)):
+                o.step(coef=coef, ema=ema, ema_rate=rate)
             else:
+                if coef is not None:
+                    grads = [p.grad for g in o.param_groups for p in g["params"] if p.grad is not None]
+                    if grads:
+                        torch._foreach_mul_(grads, coef)
                 o.step()
         self.step_idx += 1
         if cfg.diloco:
@@ -395,6 +413,6 @@ class Trainer:
                     n = self.step_idx // cfg.diloco
                     self.ema.update(self.step_idx, D.ema_decay_at_sync(self.ema_decay, cfg.diloco, n))
         elif self.ema is not None:
-            self.ema.update(self.step_idx)
+            self.ema.update(self.step_idx)  # what the fused launches did not cover
         self.last = dict(mlm=acc_mlm, gnorm=self.last_gnorm, repa=acc_repa)
         return acc
