@@ -200,6 +200,23 @@ def profile_sampling(run_batch, args, rank, steps=2):
               flush=True)
 
 
+def phase_breakdown(tr, batch, world, device, steps=2):
+    """Per-phase device time of a step (ms, mean of `steps` extra steps after the timed region, max over ranks):
+    forward_backward, grad_sync_exposed (gradient reductions still running after the last backward kernel),
+    grad_norm, muon_momentum, muon_newton_schulz, muon_apply / muon_allgather_apply, adamw, ema_and_rest."""
+    from trenowanie_generatora_obrazkow_b200.utils.profiling import PhaseTimer
+    tr.timer = PhaseTimer(device)
+    for _ in range(steps):
+        tr.step(batch)
+    got = tr.timer.collect()
+    tr.timer = None
+    names = list(got)
+    vals = torch.tensor([got[k] / steps for k in names], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    return {k: round(v, 2) for k, v in zip(names, vals.tolist())}
+
+
 def emit(rank, out):
     if rank == 0:
         print(json.dumps(out), flush=True)
@@ -260,6 +277,7 @@ def run_ours(args):
                               "exchange") if args.moe else None,
                       "l2": "inputs larger than L2 (no flush needed)"},
            "clocks": clocks, "gpu_launches": int(launches), "impl": "ours"}
+    out["phases_ms"] = phase_breakdown(tr, devb, world, device)
     if not args.no_e2e:
         loss_host = []
 

@@ -56,8 +56,8 @@ def _worker(rank, world, port, d):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_moe_peer_exchange_two_gpus():
-    world = 2
+def test_moe_peer_exchange_multi_gpu():
+    world = min(8, torch.cuda.device_count())  # every visible GPU (experts = 2 per rank)
     with tempfile.TemporaryDirectory() as d:
         mp.spawn(_worker, args=(world, _port(), d), nprocs=world, join=True)
         for r in range(world):

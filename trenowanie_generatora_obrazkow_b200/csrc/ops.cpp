@@ -122,6 +122,8 @@ void set_attention_fwd_emu(int64_t eighths) {
 
 static bool g_gemm_pair_enabled = true;  // 256 x 256 CTA-pair tiles: 3-6 % faster on the training shapes
 void set_gemm_pair(bool on) { g_gemm_pair_enabled = on; }
+static bool g_gemm_syrk = true;  // symmetric mode of gemm_syrk (off: the full product, for A/B runs)
+void set_gemm_syrk(bool on) { g_gemm_syrk = on; }
 
 static int* err_ptr(const at::Tensor& err) {
   TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt && err.numel() >= 1, "err must be a CUDA int32 tensor");
@@ -214,7 +216,7 @@ void gemm_syrk(at::Tensor A, at::Tensor C, c10::optional<at::Tensor> D, double a
   TORCH_CHECK(C.size(-2) == M && C.size(-1) == M && (!batched || C.size(0) == batch), "gemm_syrk: C shape");
   TORCH_CHECK(K % 8 == 0 && M % 8 == 0, "gemm_syrk: dims must be multiples of 8");
   const int64_t tri = ((M + 255) / 256) * ((M + 255) / 256 + 1) / 2 * batch;
-  const bool use_pair = g_gemm_pair_enabled && g_gemm_tma_c && M >= 256 && tri >= num_sms() / 2;
+  const bool use_pair = g_gemm_syrk && g_gemm_pair_enabled && g_gemm_tma_c && M >= 256 && tri >= num_sms() / 2;
   if (!use_pair) {
     gemm(A, A, C, false, false, D, alpha, beta, false, err);
     return;
@@ -1139,6 +1141,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_attention_tc", &tgo::set_attention_tc, "use the tcgen05 attention forward (default) or mma.sync");
   m.def("set_gemm_tma_epilogue", &tgo::set_gemm_tma_epilogue,
         "GEMM epilogue through TMA stores / reduce-adds (default) or per-row global stores");
+  m.def("set_gemm_syrk", &tgo::set_gemm_syrk, "enable / disable the symmetric (lower-triangle) GEMM mode (A/B runs)");
   m.def("gemm_syrk", &tgo::gemm_syrk, "symmetric C = alpha A A^T + beta D: lower-triangle tiles, mirrored stores");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");
   m.def("launch_count", &tgo::launch_count, "kernels launched by this extension so far");

@@ -244,6 +244,26 @@ def euler_case(B, side, C):
     return ours, lib, 0.0, 4 * 2 * B * C * T + 2 * 2 * B * T * C
 
 
+def ns_case(batch, m, n, steps=5):
+    """Muon's quintic Newton-Schulz on a shape bucket: ours with the symmetric GEMM mode for X X^T and A A^T, the
+    'library' column the same loop with full products (the symmetric mode switched off). FLOPs: the full math,
+    2 m^2 n + 2 m^3 + 2 m^2 n per iteration, so the symmetric saving shows as higher TFLOP/s."""
+    from ..optim.newton_schulz import zeropower
+    g = torch.randn(batch, m, n, device="cuda")
+
+    def ours():
+        zeropower(g, steps)
+
+    def lib():
+        ext().set_gemm_syrk(False)
+        try:
+            zeropower(g, steps)
+        finally:
+            ext().set_gemm_syrk(True)
+
+    return ours, lib, steps * batch * (4 * m * m * n + 2 * m ** 3), 0
+
+
 def cases(small):
     B = 8 if small else 32
     T, D, H, hd, MLP = 1024, 2048, 16, 128, 5504
@@ -269,6 +289,10 @@ def cases(small):
         "euler_cfg": lambda: euler_case(8, 64, 128),
         "gemm_swiglu": lambda: swiglu_gemm_case(M, D, MLP),
         "gemm_grouped": lambda: grouped_gemm_case(M, 8192, D, 8),  # MoE experts: up projection of hidden 4096
+        # Newton-Schulz buckets of the 1.24B model on one GPU: 2048 x 2048 (q, k, v, out, cross q / out of 24
+        # blocks) and 2048 x 5504 (SwiGLU gate / up / down)
+        "ns_2048": lambda: ns_case(24 if small else 144, D, D),
+        "ns_2048x5504": lambda: ns_case(12 if small else 72, D, MLP),
     }
 
 

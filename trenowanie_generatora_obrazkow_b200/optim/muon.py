@@ -132,7 +132,7 @@ class Muon(torch.optim.Optimizer):
         self.world = dist.get_world_size(group) if distributed else 1
         self.momentum_dtype = momentum_dtype
         self.gather = gather or default_gather
-        self.chunk_elems = chunk_elems or 64 * 2 ** 20
+        self.chunk_elems = chunk_elems or 512 * 2 ** 20
         self.period, self.gamma, self._t = period, gamma, 0
         self.splits = splits or {}
         self.layout = MuonLayout(self.param_groups, self.splits, self.world, self.rank, pad=self.world > 1)
@@ -236,7 +236,7 @@ class Muon(torch.optim.Optimizer):
             self._x[e.off:e.off + e.n] = (grad.lerp(mq, mu) if nesterov else mq).to(torch.bfloat16)
 
     @torch.no_grad()
-    def step(self, closure=None, coef=None, ema=None, ema_rate=0.0):
+    def step(self, closure=None, coef=None, ema=None, ema_rate=0.0, timer=None):
         """One Muon step. ``coef`` (float or device scalar) scales the gradients first (the clip coefficient);
         ``ema`` (optim.groups.EMA): its tensors of these matrices get e += ema_rate (p - e) after the update, in the
         same launch on the device (and are marked done for this step)."""
@@ -270,6 +270,8 @@ class Muon(torch.optim.Optimizer):
             for gi, g in enumerate(self.param_groups):
                 self._momentum_torch(gi, g, 1.0 if coef is None else coef)
 
+        if timer is not None:
+            timer.mark("muon_momentum")
         # Newton-Schulz (or the row-wise step) of the owned entries of every bucket, into the update buffer
         for b in L.buckets:
             lo, hi = b.owned_slots(self.rank)
@@ -280,13 +282,17 @@ class Muon(torch.optim.Optimizer):
                 s1 = min(hi, s0 + per_launch)
                 a, z = b.off + s0 * size, b.off + s1 * size
                 X = self._x[a:z].view(s1 - s0, b.rows, b.cols)
-                Y = zeropower(X, steps) if refresh else rownorm(X) * self.gamma
-                self._upd[a:z].copy_(Y.reshape(-1))
+                if refresh:  # the flat input is scratch: normalised in place, result straight into the updates
+                    zeropower(X, steps, out=self._upd[a:z].view(s1 - s0, b.rows, b.cols), scratch_ok=True)
+                else:
+                    self._upd[a:z].copy_((rownorm(X) * self.gamma).reshape(-1))
             if self.world > 1:  # in place: rank r's owned slots are chunk r of the bucket's padded span
                 span = self._upd[b.off:b.off + b.span]
                 chunk = b.per * size
                 self.gather(span, span[self.rank * chunk:(self.rank + 1) * chunk], self.group)
 
+        if timer is not None:
+            timer.mark("muon_newton_schulz")  # with W > 1: and the update all-gather
         # p <- p (1 - lr wd) - lr s U, and the bf16 shadow
         coefs = [(-self.param_groups[e.group]["lr"] * e.scale,
                   1 - self.param_groups[e.group]["lr"] * self.param_groups[e.group]["weight_decay"])
@@ -301,6 +307,8 @@ class Muon(torch.optim.Optimizer):
             for e, (alpha, decay) in zip(L.entries, coefs):
                 blk = e.p[e.r0:e.r1]  # a view: the in-place update bumps the parameter's version
                 blk.mul_(decay).add_(self._upd[e.off:e.off + e.n].view_as(blk).float(), alpha=alpha)
+        if timer is not None:
+            timer.mark("muon_apply")
         if ema is not None:
             done = set()
             for e in L.entries:

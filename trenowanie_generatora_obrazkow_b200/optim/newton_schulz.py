@@ -35,31 +35,48 @@ def zeropower_reference(G, steps=5):
     return X
 
 
-def zeropower(G, steps=5):
-    """Orthogonalise the last two dims of G (B, m, n) or (m, n); returns bf16."""
+def zeropower(G, steps=5, out=None, scratch_ok=False):
+    """Orthogonalise the last two dims of G (B, m, n) or (m, n); returns bf16 (written into `out` when given).
+    scratch_ok: G is a contiguous bf16 buffer the caller does not need afterwards, so the Frobenius normalisation
+    happens in place (one fp32-accumulated norm pass and one scaling pass over the bf16 data)."""
     if not G.is_cuda:
-        return zeropower_reference(G, steps)
+        X = zeropower_reference(G, steps)
+        return out.copy_(X) if out is not None else X
     a, b, c = NS_COEFFS
     squeeze = G.dim() == 2
     X = G.unsqueeze(0) if squeeze else G
     transposed = X.size(-2) > X.size(-1)
-    if transposed:
-        X = X.mT
-    norm = X.float().norm(dim=(-2, -1), keepdim=True)
-    X = (X.float() / (norm + 1e-7)).to(torch.bfloat16).contiguous()
+    if scratch_ok and X.dtype == torch.bfloat16 and X.is_contiguous():
+        norm = torch.linalg.vector_norm(X, dim=(-2, -1), keepdim=True, dtype=torch.float32)
+        X.mul_(1.0 / (norm + 1e-7))  # fp32 math, one rounding to bf16 (the transpose comes free below)
+        if transposed:
+            X = X.mT.contiguous()
+    else:
+        if transposed:
+            X = X.mT
+        norm = X.float().norm(dim=(-2, -1), keepdim=True)
+        X = (X.float() / (norm + 1e-7)).to(torch.bfloat16).contiguous()
     n, m, k = X.shape
     A = torch.empty(n, m, m, device=X.device, dtype=torch.bfloat16)
     Bm = torch.empty_like(A)
+    final = None
+    if out is not None and not transposed:
+        final = out.view(n, m, k)
     Y = torch.empty_like(X)
     from ..ops._ext import err_buf, ext
     err = err_buf(X.device)
-    for _ in range(steps):
+    for i in range(steps):
         ext().gemm_syrk(X, A, None, 1.0, 0.0, err)     # A = X X^T            (symmetric)
         ext().gemm_syrk(A, Bm, A, c, b, err)           # B = c A A^T + b A    (symmetric)
-        gemm(Bm, X, out=Y, b_mn=True, d=X, alpha=1.0, beta=a)  # X = B X + a X
-        X, Y = Y, X
+        dst = final if (final is not None and i == steps - 1) else Y
+        gemm(Bm, X, out=dst, b_mn=True, d=X, alpha=1.0, beta=a)  # X = B X + a X
+        X, Y = dst, X
     if transposed:
         X = X.mT
+    if out is not None:
+        if final is None:
+            out.view(X.shape).copy_(X)
+        return out
     return X.squeeze(0) if squeeze else X
 
 

@@ -186,7 +186,7 @@ class MuonShardedComm:
     # optimizer step
     # ------------------------------------------------------------------------------------------------------------
     @torch.no_grad()
-    def step(self, coef=1.0, ema=None, ema_rate=0.0):
+    def step(self, coef=1.0, ema=None, ema_rate=0.0, timer=None):
         """One Muon step from the owned reduced gradients; ``coef`` is the gradient-clip coefficient (float or
         device scalar); ``ema`` (optim.groups.EMA, where this rank keeps one): updated inside the apply launch."""
         m = self.muon
@@ -200,14 +200,23 @@ class MuonShardedComm:
                 continue
             self._momentum(self.g_owned[a:b], self.momentum[a:b], self.x_in[a:b], coef_t, g["momentum"],
                            g["nesterov"])
+        if timer is not None:
+            timer.mark("muon_momentum")
         upd_local = self._local_update_view()
         for gi, rows, cols, lo, hi, off_lo, own_lo in self.bucket_views:
             n = (hi - lo) * rows * cols
             X = self.x_in[own_lo:own_lo + n].view(hi - lo, rows, cols)
             steps = m.param_groups[gi]["ns_steps"]
-            Y = zeropower(X, steps) if refresh else rownorm(X) * m.gamma
-            upd_local[off_lo:off_lo + n].copy_(Y.reshape(-1))
+            dst = upd_local[off_lo:off_lo + n].view(hi - lo, rows, cols)
+            if refresh:  # x_in is scratch: normalised in place, the result lands in the peer-visible update buffer
+                zeropower(X, steps, out=dst, scratch_ok=True)
+            else:
+                dst.copy_(rownorm(X) * m.gamma)
+        if timer is not None:
+            timer.mark("muon_newton_schulz")
         self._gather_apply(ema, ema_rate)
+        if timer is not None:
+            timer.mark("muon_allgather_apply")
 
     def _momentum(self, g, buf, x, coef, mu, nesterov):
         if self.transport == "p2p":

@@ -195,6 +195,7 @@ class Trainer:
                 self.buckets = GradBuckets(dense, group=group, comm=cfg.grad_comm if reduce_grads else "none")
         self.ema_decay = ema
         self.grad_norm = GradNorm(self.device) if self.device.type == "cuda" else None
+        self.timer = None  # utils.profiling.PhaseTimer: per-phase device times of each step when set
         self.global_params = self.outer_opt = None
         if cfg.diloco:
             if self.distributed and self.world > 1:
@@ -321,6 +322,9 @@ class Trainer:
         """One optimizer step over this rank's share of the global batch. Returns the mean flow-matching loss
         (device scalar); ``self.last`` holds the MLM loss and the gradient norm."""
         cfg = self.cfg
+        timer = self.timer
+        if timer is not None:
+            timer.begin()
         items = list(self._micro_items(batch))
         total = sum(x0.shape[0] for x0, _, _ in items)
         if self.muon_buckets is not None:
@@ -366,6 +370,8 @@ class Trainer:
             acc += l_fm * w
             if l_mlm is not None:
                 acc_mlm += l_mlm * w
+        if timer is not None:
+            timer.mark("forward_backward")
         if self.buckets is not None:
             self.buckets.finish()
             if getattr(self, "powersgd", None) is not None:
@@ -374,6 +380,8 @@ class Trainer:
             self.muon_buckets.finish()
         if self.expert_params and self.world > 1:  # their gradients summed every rank's loss: make it the mean
             torch._foreach_mul_([p.grad for p in self.expert_params if p.grad is not None], 1.0 / self.world)
+        if timer is not None:
+            timer.mark("grad_sync_exposed")  # reductions still running after the last backward kernel
         coef = None
         if self.muon_comm is None:
             if self._fused_tail():  # norm + clip coefficient on the device; the optimizers take the coefficient
@@ -389,21 +397,29 @@ class Trainer:
                 sq = sq + torch.stack(torch._foreach_norm(others)).square().sum()
             self.last_gnorm = sq.sqrt()
             coef = (cfg.clip / (self.last_gnorm + 1e-6)).clamp(max=1.0)  # applied by the optimizers
+        if timer is not None:
+            timer.mark("grad_norm")
         set_lr(self.opts, lr_mult(self.step_idx, cfg.steps, cfg.warmup, cfg.schedule))
         # the per-step EMA is updated inside the fused optimizers' parameter-update launches where they can
         ema = self.ema if (self.ema is not None and not cfg.diloco) else None
         rate = 1.0 - self.ema.decay_at(self.step_idx + 1) if ema is not None else 0.0
         for o in self.opts:
             if o is self.muon and self.muon_comm is not None:
-                self.muon_comm.step(coef, ema=ema, ema_rate=rate)
-            elif isinstance(o, (Muon, FusedAdamW)):
+                self.muon_comm.step(coef, ema=ema, ema_rate=rate, timer=timer)
+            elif isinstance(o, Muon):
+                o.step(coef=coef, ema=ema, ema_rate=rate, timer=timer)
+            elif isinstance(o, FusedAdamW):
                 o.step(coef=coef, ema=ema, ema_rate=rate)
+                if timer is not None:
+                    timer.mark("adamw")
             else:
                 if coef is not None:
                     grads = [p.grad for g in o.param_groups for p in g["params"] if p.grad is not None]
                     if grads:
                         torch._foreach_mul_(grads, coef)
                 o.step()
+                if timer is not None:
+                    timer.mark(type(o).__name__.lower())
         self.step_idx += 1
         if cfg.diloco:
             if self.step_idx % cfg.diloco == 0 or self.step_idx == cfg.steps:
@@ -414,5 +430,7 @@ class Trainer:
                     self.ema.update(self.step_idx, D.ema_decay_at_sync(self.ema_decay, cfg.diloco, n))
         elif self.ema is not None:
             self.ema.update(self.step_idx)  # what the fused launches did not cover
+        if timer is not None:
+            timer.mark("ema_and_rest")
         self.last = dict(mlm=acc_mlm, gnorm=self.last_gnorm, repa=acc_repa)
         return acc

@@ -78,3 +78,42 @@ def summarize_kernels(table, total, width=90):
         lines.append(f"{n[:width]:{width}s} {ms:9.2f} {c:6d} {100 * s:5.1f}%")
     lines.append(f"{'total':{width}s} {total:9.2f}")
     return "\n".join(lines)
+
+
+class PhaseTimer:
+    """Device-time breakdown of a training step: ``mark(name)`` records a CUDA event on the current stream; the
+    phase called `name` is the device time from the previous mark to this one. Marks are cheap (no
+    synchronisation); ``collect()`` synchronises once and returns {phase: ms} summed over the recorded steps.
+    On CPU tensors it does nothing."""
+
+    def __init__(self, device):
+        self.enabled = torch.device(device).type == "cuda"
+        self.steps = []   # per step: [(name, event)]
+        self._cur = None
+
+    def begin(self):
+        if not self.enabled:
+            return
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self._cur = [("begin", e)]
+        self.steps.append(self._cur)
+
+    def mark(self, name):
+        if not self.enabled or self._cur is None:
+            return
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self._cur.append((name, e))
+
+    def collect(self):
+        """{phase: total ms over the recorded steps} (then cleared); the phases keep their first-seen order."""
+        if not self.enabled:
+            return {}
+        torch.cuda.synchronize()
+        out = {}
+        for marks in self.steps:
+            for (_, a), (name, b) in zip(marks[:-1], marks[1:]):
+                out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        self.steps, self._cur = [], None
+        return out
