@@ -640,6 +640,16 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         set_lr(opts, 1.0)
         for o in opts:
             o.step()
+        if args.bench and lrank == 0:  # learner throughput: student latent tokens trained per second
+            torch.cuda.synchronize(device) if device.type == "cuda" else None
+            dt = time.time() - tp
+            toks = n_learn * B * args.opd_states * side * side
+            line = (f"[bench] step {step} {dt * 1e3:.1f} ms {toks / dt:.0f} learner-latent-tokens/s res {res} "
+                    f"(rollouts {t_roll * 1e3:.0f} ms, teacher {t_teach * 1e3:.0f} ms, student {t_learn * 1e3:.0f} ms)")
+            if sender is not None and sender.last_copy is not None and t_roll:
+                nb, ms = sender.last_copy
+                line += f"; snapshot {nb / 1e9:.2f} GB in {ms:.2f} ms = {nb / ms / 1e6:.0f} GB/s"
+            print(line, flush=True)
         if lrank == 0 and ((step + 1) % args.log_every == 0 or step + 1 == args.steps):
             print(f"[learner] step {step + 1}/{args.steps} opd loss {float(loss):.4f} res {res} "
                   f"{(time.time() - t0) / args.log_every:.2f} s/step", flush=True)

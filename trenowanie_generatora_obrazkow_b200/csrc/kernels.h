@@ -119,10 +119,11 @@ struct QKNormRopeParams {
   float eps;
 };
 cudaError_t qknorm_rope_fwd_launch(const QKNormRopeParams& p, cudaStream_t s);
-cudaError_t qknorm_rope_bwd_launch(const QKNormRopeParams& p, const __nv_bfloat16* dq, long long ld_dq,
+cudaError_t qknorm_rope_bwd_launch(const QKNormRopeParams& p, const void* dq, long long ld_dq, bool dq_f32,
                                    const __nv_bfloat16* dk, long long ld_dk, __nv_bfloat16* dqkv, long long ld_dqkv,
                                    float* dwq, float* dwk, cudaStream_t s);
 
+cudaError_t qknorm_set_bwd_unroll(int u);     // 2 or 4 heads in flight per lane group (A/B runs)
 cudaError_t swiglu_fwd_launch(const __nv_bfloat16* ab, __nv_bfloat16* g, long long M, int H, cudaStream_t s);
 cudaError_t swiglu_bwd_launch(const __nv_bfloat16* ab, const __nv_bfloat16* dg, __nv_bfloat16* dab, long long M,
                               int H, cudaStream_t s);

@@ -388,6 +388,13 @@ cudaError_t adanorm_fwd_launch(const AdaNormFwdParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+static int g_qknorm_bwd_unroll = 4;  // heads per lane group with loads in flight (2 or 4)
+cudaError_t qknorm_set_bwd_unroll(int u) {
+  if (u != 2 && u != 4) return cudaErrorInvalidValue;
+  g_qknorm_bwd_unroll = u;
+  return cudaSuccess;
+}
+
 cudaError_t adanorm_bwd_launch(const AdaNormBwdParams& p, float* dshift, float* dscale, float* dgate, float* dw,
                                cudaStream_t s) {
   const int threads = ((p.D / 8 + 31) / 32) * 32;
@@ -489,81 +496,107 @@ __global__ void __launch_bounds__(256) qknorm_rope_fwd_kernel(QKNormRopeParams p
 }
 
 // Backward: dq / dk (post-RoPE) -> d(pre-norm q / k) written into dqkv; dw_q, dw_k accumulated (+=).
-// Persistent grid: each lane group walks (row, head) items with a grid stride and keeps its dw partials in registers;
-// one shared-memory reduction and one global atomic per element and CTA at the end.
+// Mirror of the forward's layout: one warp per token row walks all of the row's q and k heads, HD / 8 lanes per head,
+// so the row's RoPE table entries and the norm weights are loaded once per row, and each lane keeps UNROLL heads'
+// loads (incoming gradient, pre-norm input) in flight. dq may be the attention backward's fp32 accumulator (then no
+// separate fp32 -> bf16 conversion pass runs before this one). Persistent grid: a warp walks rows with a grid stride,
+// keeps its dw partials in registers (a lane's channel slice e0 is the same for every head), then one shared-memory
+// reduction and one global atomic per element and CTA.
 template <int HD>
-__global__ void __launch_bounds__(512) qknorm_rope_bwd_kernel(QKNormRopeParams p, const bf16* __restrict__ dq,
-                                                              long long ld_dq, const bf16* __restrict__ dk,
-                                                              long long ld_dk, bf16* __restrict__ dqkv,
-                                                              long long ld_dqkv, float* __restrict__ dwq,
-                                                              float* __restrict__ dwk) {
-  constexpr int LPH = HD / 8, IPW = 32 / LPH;
+__device__ __forceinline__ void load8_any(const void* base, long long off, bool f32, float (&g)[8]) {
+  if (f32) {
+    load8f(reinterpret_cast<const float*>(base) + off, g);
+  } else {
+    load8(reinterpret_cast<const bf16*>(base) + off, g);
+  }
+}
+
+template <int HD, int UNROLL>
+__global__ void __launch_bounds__(256, 2) qknorm_rope_bwd_kernel(QKNormRopeParams p, const void* __restrict__ dq,
+                                                              long long ld_dq, int dq_f32,
+                                                              const bf16* __restrict__ dk, long long ld_dk,
+                                                              bf16* __restrict__ dqkv, long long ld_dqkv,
+                                                              float* __restrict__ dwq, float* __restrict__ dwk) {
+  constexpr int LPH = HD / 8, HPI = 32 / LPH;
   __shared__ float s_dw[2][HD];
   for (int i = threadIdx.x; i < 2 * HD; i += blockDim.x) (&s_dw[0][0])[i] = 0.f;
   __syncthreads();
   const int heads = p.hq + p.hkv;
-  const long long total = (long long)p.M * heads;
+  const int sub = lane_id() / LPH;
   const int e0 = (lane_id() % LPH) * 8;
-  float acc_q[8], acc_k[8];
+  const bool norm = p.q_w != nullptr;  // q_w and k_w are both given or both absent
+  float wq[8], wk[8], acc_q[8], acc_k[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc_q[i] = acc_k[i] = 0.f;
-  const long long stride = (long long)gridDim.x * (blockDim.x >> 5) * IPW;
-  const long long first = ((long long)blockIdx.x * (blockDim.x >> 5) + warp_id()) * IPW + lane_id() / LPH;
-  // every lane of a warp runs the same number of iterations (shuffles inside); items past the end are masked
-  const long long warp_first = first - lane_id() / LPH;
-  for (long long wbase = warp_first; wbase < total; wbase += stride) {
-    const long long item = wbase + lane_id() / LPH;
-    const bool valid = item < total;
-    const int row = valid ? (int)(item / heads) : 0, hh = valid ? (int)(item % heads) : 0;
-    const bool is_q = hh < p.hq;
-    float g[8];
-    if (valid) {
-      const bf16* gsrc = is_q ? dq + (long long)row * ld_dq + (long long)hh * HD + e0
-                              : dk + (long long)row * ld_dk + (long long)(hh - p.hq) * HD + e0;
-      load8(gsrc, g);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) g[i] = 0.f;
+  for (int i = 0; i < 8; ++i) acc_q[i] = acc_k[i] = wq[i] = wk[i] = 0.f;
+  if (norm) {
+    load8f(p.q_w + e0, wq);
+    load8f(p.k_w + e0, wk);
+  }
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + warp_id(); row < p.M; row += warps) {
+    float cs[8], sn[8];
+    if (p.cos != nullptr) {
+      const long long b = row / p.T, t = row % p.T;
+      load8f(p.cos + b * p.rope_bs + t * HD + e0, cs);
+      load8f(p.sin + b * p.rope_bs + t * HD + e0, sn);
     }
-    if (p.cos != nullptr && valid) {  // transpose of the rotation
-      const int b = row / p.T, t = row % p.T;
-      float cs[8], sn[8];
-      load8f(p.cos + (long long)b * p.rope_bs + (long long)t * HD + e0, cs);
-      load8f(p.sin + (long long)b * p.rope_bs + (long long)t * HD + e0, sn);
+    for (int h0 = 0; h0 < heads; h0 += UNROLL * HPI) {
+      float g[UNROLL][8];
+      uint4 ux[UNROLL];
+      float r[UNROLL];
 #pragma unroll
-      for (int i = 0; i < 8; i += 2) {
-        const float a = g[i], c = g[i + 1];
-        g[i] = a * cs[i] + c * sn[i + 1];
-        g[i + 1] = c * cs[i + 1] - a * sn[i];
+      for (int u = 0; u < UNROLL; ++u) {  // every load of the batch first
+        const int hh = h0 + u * HPI + sub;
+        const bool valid = hh < heads, is_q = hh < p.hq;
+        if (valid) {
+          if (is_q) load8_any<HD>(dq, row * ld_dq + (long long)hh * HD + e0, dq_f32 != 0, g[u]);
+          else load8(dk + row * ld_dk + (long long)(hh - p.hq) * HD + e0, g[u]);
+          ux[u] = norm ? *reinterpret_cast<const uint4*>(p.qkv + row * p.ld_qkv + (long long)hh * HD + e0)
+                       : make_uint4(0u, 0u, 0u, 0u);
+          r[u] = norm ? (is_q ? p.rstd_q[row * p.hq + hh] : p.rstd_k[row * p.hkv + (hh - p.hq)]) : 0.f;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) g[u][i] = 0.f;
+          ux[u] = make_uint4(0u, 0u, 0u, 0u);
+          r[u] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const int hh = h0 + u * HPI + sub;
+        const bool valid = hh < heads, is_q = hh < p.hq;
+        if (p.cos != nullptr) {  // transpose of the rotation
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) {
+            const float a = g[u][i], c = g[u][i + 1];
+            g[u][i] = a * cs[i] + c * sn[i + 1];
+            g[u][i + 1] = c * cs[i + 1] - a * sn[i];
+          }
+        }
+        if (norm) {
+          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&ux[u]);
+          float n[8];
+          float dot = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(as_bf2(xw[i]));
+            n[2 * i] = f.x * r[u];
+            n[2 * i + 1] = f.y * r[u];
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (is_q) acc_q[i] += g[u][i] * n[i];
+            else acc_k[i] += g[u][i] * n[i];
+            g[u][i] *= is_q ? wq[i] : wk[i];  // d(normalised x)
+            dot += g[u][i] * n[i];
+          }
+          dot = group_sum<LPH>(dot) / HD;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) g[u][i] = r[u] * (g[u][i] - n[i] * dot);
+        }
+        if (valid) store8(dqkv + row * ld_dqkv + (long long)hh * HD + e0, g[u]);
       }
     }
-    const float* nw = is_q ? p.q_w : p.k_w;
-    if (nw != nullptr) {  // uniform per warp: q_w and k_w are both given or both absent
-      float x[8], w8[8];
-      if (valid) load8(p.qkv + (long long)row * p.ld_qkv + (long long)hh * HD + e0, x);
-      else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] = 0.f;
-      }
-      load8f(nw + e0, w8);
-      const float r = valid ? (is_q ? p.rstd_q : p.rstd_k)[(long long)row * (is_q ? p.hq : p.hkv) +
-                                                           (is_q ? hh : hh - p.hq)]
-                            : 0.f;
-      float dot = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float n = x[i] * r;
-        if (is_q) acc_q[i] += g[i] * n;
-        else acc_k[i] += g[i] * n;
-        g[i] *= w8[i];  // dn
-        dot += g[i] * n;
-        x[i] = n;
-      }
-      dot = group_sum<LPH>(dot) / HD;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) g[i] = r * (g[i] - x[i] * dot);
-    }
-    if (valid) store8(dqkv + (long long)row * ld_dqkv + (long long)hh * HD + e0, g);
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -571,9 +604,9 @@ __global__ void __launch_bounds__(512) qknorm_rope_bwd_kernel(QKNormRopeParams p
     atomicAdd(&s_dw[1][e0 + i], acc_k[i]);
   }
   __syncthreads();
-  if (p.q_w != nullptr && dwq != nullptr)
+  if (norm && dwq != nullptr)
     for (int i = threadIdx.x; i < HD; i += blockDim.x) atomicAdd(&dwq[i], s_dw[0][i]);
-  if (p.k_w != nullptr && dwk != nullptr)
+  if (norm && dwk != nullptr)
     for (int i = threadIdx.x; i < HD; i += blockDim.x) atomicAdd(&dwk[i], s_dw[1][i]);
 }
 
@@ -585,17 +618,22 @@ cudaError_t qknorm_rope_fwd_launch(const QKNormRopeParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-cudaError_t qknorm_rope_bwd_launch(const QKNormRopeParams& p, const bf16* dq, long long ld_dq, const bf16* dk,
-                                   long long ld_dk, bf16* dqkv, long long ld_dqkv, float* dwq, float* dwk,
-                                   cudaStream_t s) {
-  const long long items = (long long)p.M * (p.hq + p.hkv);
-  const int per_block = 16 * (32 / (p.hd / 8));  // 16 warps
-  const unsigned grid = (unsigned)std::min<long long>((items + per_block - 1) / per_block, (long long)num_sms() * 4);
-  if (p.hd == 128)
-    qknorm_rope_bwd_kernel<128><<<grid, 512, 0, s>>>(p, dq, ld_dq, dk, ld_dk, dqkv, ld_dqkv, dwq, dwk);
-  else if (p.hd == 64)
-    qknorm_rope_bwd_kernel<64><<<grid, 512, 0, s>>>(p, dq, ld_dq, dk, ld_dk, dqkv, ld_dqkv, dwq, dwk);
-  else return cudaErrorInvalidValue;
+cudaError_t qknorm_rope_bwd_launch(const QKNormRopeParams& p, const void* dq, long long ld_dq, bool dq_f32,
+                                   const bf16* dk, long long ld_dk, bf16* dqkv, long long ld_dqkv, float* dwq,
+                                   float* dwk, cudaStream_t s) {
+  const long long rows = p.M;  // one warp per row, 8 warps per block, at most 4 blocks per SM (grid stride)
+  const unsigned grid = (unsigned)std::min<long long>((rows + 7) / 8, (long long)num_sms() * 4);
+  const int f32 = dq_f32 ? 1 : 0;
+#define TGO_QKB(HD, U) qknorm_rope_bwd_kernel<HD, U><<<grid, 256, 0, s>>>(p, dq, ld_dq, f32, dk, ld_dk, dqkv, \
+                                                                          ld_dqkv, dwq, dwk)
+  if (p.hd == 128) {
+    if (g_qknorm_bwd_unroll == 4) TGO_QKB(128, 4); else TGO_QKB(128, 2);
+  } else if (p.hd == 64) {
+    if (g_qknorm_bwd_unroll == 4) TGO_QKB(64, 4); else TGO_QKB(64, 2);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+#undef TGO_QKB
   return cudaGetLastError();
 }
 
@@ -604,53 +642,81 @@ cudaError_t qknorm_rope_bwd_launch(const QKNormRopeParams& p, const bf16* dq, lo
 // ------------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ float silu_f(float a) { return a / (1.f + __expf(-a)); }
 
-__global__ void swiglu_fwd_kernel(const bf16* __restrict__ ab, bf16* __restrict__ g, long long M, int H) {
-  const long long n8 = M * (H / 8);
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
-    const long long row = i / (H / 8);
-    const int c = (int)(i % (H / 8)) * 8;
-    float a[8], b[8], o[8];
-    load8(ab + row * 2 * H + c, a);
-    load8(ab + row * 2 * H + H + c, b);
+// Flat index over 8-element groups (n8 < 2^31, checked by the launchers): 32-bit index arithmetic (a 64-bit division
+// per group dominated the instruction count), two groups per thread per step with all their loads issued first.
+__global__ void swiglu_fwd_kernel(const bf16* __restrict__ ab, bf16* __restrict__ g, int n8, int H) {
+  const unsigned H8 = (unsigned)(H / 8);
+  const unsigned stride = gridDim.x * blockDim.x;
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < (unsigned)n8; i += 2 * stride) {
+    const bool two = i + stride < (unsigned)n8;
+    float a[2][8], b[2][8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) o[k] = bf16_round(silu_f(a[k])) * b[k];
-    store8(g + row * H + c, o);
+    for (int k = 0; k < 2; ++k) {
+      const unsigned ii = k == 0 ? i : (two ? i + stride : i);
+      const unsigned row = ii / H8, c = (ii - row * H8) * 8;
+      load8(ab + (long long)row * 2 * H + c, a[k]);
+      load8(ab + (long long)row * 2 * H + H + c, b[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (k == 1 && !two) break;
+      const unsigned ii = i + k * stride;
+      const unsigned row = ii / H8, c = (ii - row * H8) * 8;
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = bf16_round(silu_f(a[k][e])) * b[k][e];
+      store8(g + (long long)row * H + c, o);
+    }
   }
 }
 
 __global__ void swiglu_bwd_kernel(const bf16* __restrict__ ab, const bf16* __restrict__ dg, bf16* __restrict__ dab,
-                                  long long M, int H) {
-  const long long n8 = M * (H / 8);
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
-    const long long row = i / (H / 8);
-    const int c = (int)(i % (H / 8)) * 8;
-    float a[8], b[8], d[8], da[8], db[8];
-    load8(ab + row * 2 * H + c, a);
-    load8(ab + row * 2 * H + H + c, b);
-    load8(dg + row * H + c, d);
+                                  int n8, int H) {
+  const unsigned H8 = (unsigned)(H / 8);
+  const unsigned stride = gridDim.x * blockDim.x;
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < (unsigned)n8; i += 2 * stride) {
+    const bool two = i + stride < (unsigned)n8;
+    float a[2][8], b[2][8], d[2][8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float sg = 1.f / (1.f + __expf(-a[k]));
-      const float s = a[k] * sg;
-      db[k] = d[k] * s;
-      da[k] = d[k] * b[k] * sg * (1.f + a[k] * (1.f - sg));
+    for (int k = 0; k < 2; ++k) {
+      const unsigned ii = k == 0 ? i : (two ? i + stride : i);
+      const unsigned row = ii / H8, c = (ii - row * H8) * 8;
+      load8(ab + (long long)row * 2 * H + c, a[k]);
+      load8(ab + (long long)row * 2 * H + H + c, b[k]);
+      load8(dg + (long long)row * H + c, d[k]);
     }
-    store8(dab + row * 2 * H + c, da);
-    store8(dab + row * 2 * H + H + c, db);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (k == 1 && !two) break;
+      const unsigned ii = i + k * stride;
+      const unsigned row = ii / H8, c = (ii - row * H8) * 8;
+      float da[8], db[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float sg = 1.f / (1.f + __expf(-a[k][e]));
+        const float sv = a[k][e] * sg;
+        db[e] = d[k][e] * sv;
+        da[e] = d[k][e] * b[k][e] * sg * (1.f + a[k][e] * (1.f - sg));
+      }
+      store8(dab + (long long)row * 2 * H + c, da);
+      store8(dab + (long long)row * 2 * H + H + c, db);
+    }
   }
 }
 
 cudaError_t swiglu_fwd_launch(const bf16* ab, bf16* g, long long M, int H, cudaStream_t s) {
   const long long n8 = M * (H / 8);
-  const int grid = (int)std::min<long long>((n8 + 255) / 256, (long long)num_sms() * 16);
-  swiglu_fwd_kernel<<<grid, 256, 0, s>>>(ab, g, M, H);
+  if (n8 >= (1ll << 31) || H % 8 != 0) return cudaErrorInvalidValue;
+  const int grid = (int)std::min<long long>((n8 + 511) / 512, (long long)num_sms() * 8);
+  swiglu_fwd_kernel<<<grid, 256, 0, s>>>(ab, g, (int)n8, H);
   return cudaGetLastError();
 }
 
 cudaError_t swiglu_bwd_launch(const bf16* ab, const bf16* dg, bf16* dab, long long M, int H, cudaStream_t s) {
   const long long n8 = M * (H / 8);
-  const int grid = (int)std::min<long long>((n8 + 255) / 256, (long long)num_sms() * 16);
-  swiglu_bwd_kernel<<<grid, 256, 0, s>>>(ab, dg, dab, M, H);
+  if (n8 >= (1ll << 31) || H % 8 != 0) return cudaErrorInvalidValue;
+  const int grid = (int)std::min<long long>((n8 + 511) / 512, (long long)num_sms() * 8);
+  swiglu_bwd_kernel<<<grid, 256, 0, s>>>(ab, dg, dab, (int)n8, H);
   return cudaGetLastError();
 }
 

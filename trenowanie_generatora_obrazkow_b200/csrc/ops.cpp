@@ -625,9 +625,14 @@ void qknorm_rope_bwd(at::Tensor qkv, int64_t hq, int64_t hkv, int64_t hd, c10::o
   QKNormRopeParams p = qk_params(qkv, hq, hkv, hd, q_w, k_w, cos, sin, T, 1e-6);
   p.rstd_q = rstd_q.has_value() && rstd_q->defined() ? rstd_q->data_ptr<float>() : nullptr;
   p.rstd_k = rstd_k.has_value() && rstd_k->defined() ? rstd_k->data_ptr<float>() : nullptr;
+  // dq: bf16 [M, >= hq hd], or the attention backward's fp32 accumulator [M, hq hd] (read directly)
   TORCH_CHECK(dq.stride(-1) == 1 && dk.stride(-1) == 1 && dqkv.stride(-1) == 1 && dq.stride(0) % 8 == 0 &&
                   dk.stride(0) % 8 == 0 && dqkv.stride(0) % 8 == 0, "qknorm_rope_bwd: layouts (16-byte rows)");
-  TGO_CHECK_LAUNCH(qknorm_rope_bwd_launch(p, bfp(dq), dq.stride(0), bfp(dk), dk.stride(0), bfp(dqkv), dqkv.stride(0),
+  const bool dq_f32 = dq.scalar_type() == at::kFloat;
+  TORCH_CHECK(dq_f32 || dq.scalar_type() == at::kBFloat16, "qknorm_rope_bwd: dq bf16 or fp32");
+  TORCH_CHECK(dk.scalar_type() == at::kBFloat16 && dqkv.scalar_type() == at::kBFloat16, "qknorm_rope_bwd: dk / dqkv bf16");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(dq.data_ptr()) % 16 == 0, "qknorm_rope_bwd: dq alignment");
+  TGO_CHECK_LAUNCH(qknorm_rope_bwd_launch(p, dq.data_ptr(), dq.stride(0), dq_f32, bfp(dk), dk.stride(0), bfp(dqkv), dqkv.stride(0),
                                           const_cast<float*>(f32_ptr_or_null(dwq)),
                                           const_cast<float*>(f32_ptr_or_null(dwk)), at::cuda::getCurrentCUDAStream()));
 }
@@ -777,7 +782,22 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::T
   AttnParams p = attn_params(q, k, v, kv_len, scale);
   attn_check4(o, "o");
   attn_check4(dO, "dO");
-  attn_check4(dq, "dq");
+  // dq: bf16 [B, T, Hq, hd], or (tcgen05 path) a contiguous fp32 [B, T, Hq, hd] that receives the accumulator
+  // itself, so no conversion pass runs (the q/k-norm backward reads the fp32 values)
+  const bool dq_f32 = dq.scalar_type() == at::kFloat;
+  if (dq_f32) {
+    TORCH_CHECK(dq.is_contiguous() && dq.dim() == 4 && dq.size(0) == q.size(0) && dq.size(1) == q.size(1) &&
+                    dq.size(2) == q.size(2) && dq.size(3) == q.size(3), "attention_bwd: fp32 dq must be contiguous "
+                "[B, T, Hq, hd]");
+    if (!(g_attention_tc && q.size(3) == 128)) {  // the mma.sync path converts itself: through a bf16 temporary
+      at::Tensor tmp = at::empty(dq.sizes(), dq.options().dtype(at::kBFloat16));
+      attention_bwd(q, k, v, o, lse, dO, kv_len, scale, tmp, dk, dv, err);
+      dq.copy_(tmp);
+      return;
+    }
+  } else {
+    attn_check4(dq, "dq");
+  }
   attn_check4(dk, "dk");
   attn_check4(dv, "dv");
   TORCH_CHECK(dO.strides() == o.strides(), "attention_bwd: dO must have o's strides");
@@ -788,7 +808,7 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::T
   p.lse = lse.data_ptr<float>();
   at::Tensor delta = at::empty({2, p.B, p.Hq, p.Tq}, q.options().dtype(at::kFloat));  // delta, lse * log2(e)
   float* lse2 = delta.data_ptr<float>() + (long long)p.B * p.Hq * p.Tq;
-  at::Tensor dq_acc = at::empty({p.B, p.Tq, p.Hq, p.hd}, q.options().dtype(at::kFloat));
+  at::Tensor dq_acc = dq_f32 ? dq : at::empty({p.B, p.Tq, p.Hq, p.hd}, q.options().dtype(at::kFloat));
   if (g_attention_tc && p.hd == 128) {
     cudaStream_t st = at::cuda::getCurrentCUDAStream();
     CUtensorMap tq = make_tmap_bhtd(p.q, p.hd, p.Tq, p.Hq, p.B, p.q_ts, p.q_hs, p.q_bs, 64);
@@ -801,8 +821,9 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::T
     TGO_CHECK_LAUNCH(attention_bwd_tc_launch(tq, tk, tv, tdo, tdq, p, delta.data_ptr<float>(), lse2, bfp(dk), dk.stride(0),
                                              dk.stride(1), dk.stride(2), bfp(dv), dv.stride(0), dv.stride(1),
                                              dv.stride(2), err_ptr(err), st));
-    TGO_CHECK_LAUNCH(attention_dq_convert_launch(p, dq_acc.data_ptr<float>(), bfp(dq), dq.stride(0), dq.stride(1),
-                                                 dq.stride(2), st));
+    if (!dq_f32)
+      TGO_CHECK_LAUNCH(attention_dq_convert_launch(p, dq_acc.data_ptr<float>(), bfp(dq), dq.stride(0), dq.stride(1),
+                                                   dq.stride(2), st));
   } else {
     TGO_CHECK_LAUNCH_N(attention_bwd_launch(p, bfp(dO), delta.data_ptr<float>(), dq_acc.data_ptr<float>(), bfp(dq),
                                           dq.stride(0), dq.stride(1), dq.stride(2), bfp(dk), dk.stride(0), dk.stride(1),
@@ -1141,6 +1162,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_attention_tc", &tgo::set_attention_tc, "use the tcgen05 attention forward (default) or mma.sync");
   m.def("set_gemm_tma_epilogue", &tgo::set_gemm_tma_epilogue,
         "GEMM epilogue through TMA stores / reduce-adds (default) or per-row global stores");
+  m.def("set_qknorm_bwd_unroll", [](int64_t u) { TORCH_CHECK(tgo::qknorm_set_bwd_unroll((int)u) == cudaSuccess, "2 or 4"); },
+        "q/k-norm + RoPE backward: heads in flight per lane group (A/B runs)");
   m.def("set_gemm_syrk", &tgo::set_gemm_syrk, "enable / disable the symmetric (lower-triangle) GEMM mode (A/B runs)");
   m.def("gemm_syrk", &tgo::gemm_syrk, "symmetric C = alpha A A^T + beta D: lower-triangle tiles, mirrored stores");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");

@@ -245,7 +245,9 @@ class _SelfAttnFn(torch.autograd.Function):
         B, T, C = qkv.shape
         do = do.contiguous().view(B, T, hq, hd)
         dqkv = torch.empty_like(qkv)
-        dq = torch.empty_like(q)
+        # fp32 dq: the attention backward hands over its accumulator and the q/k-norm backward reads it, so no
+        # separate fp32 -> bf16 pass runs in between
+        dq = torch.empty(q.shape, device=q.device, dtype=torch.float32)
         dk = torch.empty_like(k)
         dv4 = dqkv[:, :, (hq + hkv) * hd:(hq + 2 * hkv) * hd].unflatten(-1, (hkv, hd))
         q4, k4 = q.view(B, T, hq, hd), k.view(B, T, hkv, hd)

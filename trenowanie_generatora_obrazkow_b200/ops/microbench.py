@@ -200,13 +200,15 @@ def swiglu_case(M, H, backward):
             2 * 5 * M * H)
 
 
-def qknorm_case(B, T, H, hd, backward):
+def qknorm_case(B, T, H, hd, backward, dq_f32=False):
     C = 3 * H * hd
     qkv = _bf16(B * T, C)
     qw, kw = torch.ones(hd, device="cuda"), torch.ones(hd, device="cuda")
     cos, sin = R.rope_1d_table(T, hd, device="cuda")
     q, k, rq, rk = ext().qknorm_rope_fwd(qkv, H, H, hd, qw, kw, cos, sin, T, R.EPS)
     dq, dk = torch.randn_like(q), torch.randn_like(k)
+    if dq_f32:  # the training path: the attention backward's fp32 dq accumulator read directly
+        dq = dq.float()
     dqkv = torch.empty_like(qkv)
     dwq, dwk = torch.zeros_like(qw), torch.zeros_like(kw)
     qv = qkv[:, :2 * H * hd].view(B, T, 2 * H, hd)
@@ -226,7 +228,7 @@ def qknorm_case(B, T, H, hd, backward):
     def lib():
         torch.autograd.grad(nr, xr, torch.cat([dq.view(B, T, H, hd), dk.view(B, T, H, hd)], 2).float(), retain_graph=True)
 
-    return ours, lib, 0.0, 2 * 9 * B * T * H * hd
+    return ours, lib, 0.0, (2 * 9 + (4 if dq_f32 else 0)) * B * T * H * hd
 
 
 def euler_case(B, side, C):
@@ -284,6 +286,7 @@ def cases(small):
         "adanorm_bwd": lambda: adanorm_case(B, T, D, True),
         "qknorm_rope_fwd": lambda: qknorm_case(B, T, H, hd, False),
         "qknorm_rope_bwd": lambda: qknorm_case(B, T, H, hd, True),
+        "qknorm_rope_bwd_f32dq": lambda: qknorm_case(B, T, H, hd, True, dq_f32=True),
         "swiglu_fwd": lambda: swiglu_case(M, MLP, False),
         "swiglu_bwd": lambda: swiglu_case(M, MLP, True),
         "euler_cfg": lambda: euler_case(8, 64, 128),
@@ -327,6 +330,7 @@ def main(argv=None):
     p.add_argument("--gemm-pair", type=int, default=-1, help="1 / 0: force the 2-CTA GEMM on / off")
     p.add_argument("--gemm-tma-epilogue", type=int, default=-1, help="1 / 0: force the 2-CTA GEMM's TMA epilogue "
                    "on / off (per-row global stores)")
+    p.add_argument("--qknorm-bwd-unroll", type=int, default=0, help="2 / 4: q/k-norm backward heads in flight")
     p.add_argument("--attn-pingpong", default="", help="comma-separated 0 / 1: attention forward softmax groups "
                    "alternate their exponential phases; every op runs once per setting (and per --attn-emu)")
     p.add_argument("--attn-emu", default="", help="comma-separated settings of the attention forward's FMA-pipe "
@@ -337,6 +341,8 @@ def main(argv=None):
         ext().set_gemm_pair(bool(a.gemm_pair))
     if a.gemm_tma_epilogue >= 0:
         ext().set_gemm_tma_epilogue(bool(a.gemm_tma_epilogue))
+    if a.qknorm_bwd_unroll:
+        ext().set_qknorm_bwd_unroll(a.qknorm_bwd_unroll)
     peaks = measured_peaks()
     table = cases(a.small)
     names = list(table) if a.op == "all" else a.op.split(",")

@@ -35,7 +35,7 @@ from ..optim.newton_schulz import rownorm, zeropower
 
 
 class MuonShardedComm:
-    def __init__(self, muon, group=None, device=None, transport="p2p", blocks=32, timeout_s=60.0):
+    def __init__(self, muon, group=None, device=None, transport="p2p", blocks=32, timeout_s=60.0, ag_blocks=None):
         self.muon, self.group = muon, group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -43,7 +43,10 @@ class MuonShardedComm:
         first = muon.param_groups[0]["params"][0]
         self.device = torch.device(device) if device is not None else first.device
         self.transport = transport if self.device.type == "cuda" else "torch"
+        # reduce-scatter: few CTAs (it runs beside the backward's kernels); all-gather + apply: enough CTAs to keep
+        # HBM and NVLink busy (it streams every master weight), within the flag array's limit
         self.blocks, self.timeout_ns = blocks, int(timeout_s * 1e9)
+        self.ag_blocks = ag_blocks or max(1, min(296, 1024 // max(1, self.world)))
         # ---- the Muon space: the optimizer's layout without padding (same entries, order and owners) ----
         from ..optim.muon import MuonLayout
         self.layout = MuonLayout(muon.param_groups, muon.splits, self.world, self.rank, pad=False)
@@ -91,7 +94,7 @@ class MuonShardedComm:
     # ------------------------------------------------------------------------------------------------------------
     def _init_peer(self):
         self._peer_sizes = dict(update=self.total * 2,
-                                rs_flags=2 * self.world * self.blocks * 4, ag_flags=self.world * self.blocks * 4)
+                                rs_flags=2 * self.world * self.blocks * 4, ag_flags=self.world * self.ag_blocks * 4)
 
     def attach_buckets(self, buckets):
         """Build the per-bucket segment tables from the gradient buckets of the Muon matrices (``GradBuckets``):
@@ -254,7 +257,7 @@ class MuonShardedComm:
             self.ag_epoch = (self.ag_epoch + 1) & 0xFFFFFFFF or 1
             pp = self._peer.ptrs
             ext().muon_ag_apply(pp["update"], pp["ag_flags"], self.own_t, self.owned, self.apply_segs, self.coefs,
-                                float(ema_rate), self.rank, self.world, self.ag_epoch, self.blocks, self.timeout_ns,
+                                float(ema_rate), self.rank, self.world, self.ag_epoch, self.ag_blocks, self.timeout_ns,
                                 err_buf(self.device))
             from ..optim.adamw import after_raw_update
             after_raw_update(e["p"] for e in self.entries)

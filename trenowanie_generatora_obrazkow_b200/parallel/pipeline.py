@@ -8,9 +8,14 @@ gradients backward; M micro-batches per step run in one-forward-one-backward ord
 * ``stage_ranges`` balances blocks the same way; ``StageModel`` materialises only the parameters a stage owns
   (the full model is built on the meta device first), with the full model's parameter names, so stage files merge
   into an ordinary checkpoint.
-* ``OneFOneB`` is this framework's own scheduler: warm-up forwards (pp - s - 1), steady 1F1B with the send of one
-  micro-batch's activations batched with the receive of another's gradient (``batch_isend_irecv``, so the pairs can
-  not deadlock), cool-down backwards. Per stage boundary and micro-batch: x (bf16), t6, text (bf16), text lengths.
+* ``OneFOneB`` is this framework's own scheduler: warm-up forwards (pp - s - 1), steady 1F1B, cool-down backwards.
+  Per stage boundary and micro-batch: x (bf16), t6, text (bf16), text lengths forward; their gradients backward.
+  Every adjacent stage pair has two process groups, one per direction (``direction_groups``), so a communicator
+  stream only ever carries activations s -> s + 1 or gradients s + 1 -> s, in the same order on both ends: no
+  send can wait behind a receive, and transfers are posted individually. A receive is posted one micro-batch
+  before its data is used and the compute stream waits for it only right before that use; sends never hold the
+  compute stream (their completion is awaited once, at the end of the step), so a stage runs on while its
+  neighbour is still busy.
 * The last stage needs the flow-matching target eps - x0 for every micro-batch; stage 0 (which has the data)
   sends all of them before the schedule starts.
 * PP x DP: rank = replica * pp + stage; gradient reduction and sharded Muon run over the stage group (the same
@@ -116,11 +121,15 @@ class StageModel(nn.Module):
                                               device)
         return self._rope[key]
 
-    def stem(self, z_t, t, text_kw, cond=None):
-        """Stage 0: (x, t6, text, text_len) from latents, t and the text-encoder inputs."""
+    def stem(self, z_t, t, text_kw, cond=None, hw=None):
+        """Stage 0: (x, t6, text, text_len) from latents, t and the text-encoder inputs. z_t is [B, C, H, W], or with
+        ``hw`` = (H, W) already token-major [B, H * W, C] (the fused flow-matching input kernel's output)."""
         from ..ops import fused as Fz
         from ..train.flow import LMTextEncoder
-        b, c, h, w = z_t.shape
+        if hw is None:
+            b, c, h, w = z_t.shape
+        else:
+            b, (h, w) = z_t.shape[0], hw
         if isinstance(self.te, LMTextEncoder):
             if getattr(self, "te_checkpoint", False) and torch.is_grad_enabled():  # recomputed in the backward
                 text, valid = torch.utils.checkpoint.checkpoint(
@@ -130,7 +139,7 @@ class StageModel(nn.Module):
                 text, valid = self.te(**text_kw)
         else:
             text, valid = self.te(text_kw["ids"])
-        tok = z_t.flatten(2).transpose(1, 2)
+        tok = z_t.flatten(2).transpose(1, 2) if hw is None else z_t
         if z_t.is_cuda:
             tok = tok.to(torch.bfloat16).contiguous()
             text = text.to(torch.bfloat16)
@@ -160,15 +169,34 @@ class StageModel(nn.Module):
         return _flush(x, pending)
 
 
-class OneFOneB:
-    """1F1B over one pipe. ``pipe`` = global ranks of this replica's stages (pipe[s] is stage s)."""
+def direction_groups(pipes):
+    """{(rank_a, rank_b): group} for every adjacent stage pair of every pipe, one group per direction (a -> b). A
+    collective over the default group: every rank calls it, in the same order."""
+    out = {}
+    for pipe in pipes:
+        for s in range(len(pipe) - 1):
+            a, b = pipe[s], pipe[s + 1]
+            out[(a, b)] = dist.new_group([a, b])  # activations a -> b
+            out[(b, a)] = dist.new_group([a, b])  # gradients b -> a
+    return out
 
-    def __init__(self, stage_model, pipe, stage, micro_shapes, device, group=None):
+
+class OneFOneB:
+    """1F1B over one pipe. ``pipe`` = global ranks of this replica's stages (pipe[s] is stage s); ``links``: the
+    result of ``direction_groups`` (required for more than one stage: a send and a receive between the same two
+    ranks must never share a stream, or each could wait behind the other)."""
+
+    def __init__(self, stage_model, pipe, stage, micro_shapes, device, links=None):
         self.m = stage_model
         self.pipe, self.s, self.pp = pipe, stage, len(pipe)
         self.shapes = micro_shapes  # dict: x, t6, text (shapes), dtypes
         self.device = device
-        self.group = group
+        self.links = links or {}
+        if self.pp > 1:
+            for a, b in ((stage - 1, stage), (stage, stage - 1), (stage, stage + 1), (stage + 1, stage)):
+                if 0 <= a < self.pp and 0 <= b < self.pp and (pipe[a], pipe[b]) not in self.links:
+                    raise ValueError("OneFOneB needs direction_groups(...) links for its neighbours")
+        self._sends = []   # (works, buffers) of sends whose completion is awaited at the end of the step
 
     # ---- communication -----------------------------------------------------------------------------------------
     def _empty_acts(self):
@@ -178,16 +206,38 @@ class OneFOneB:
                 torch.empty(sh["text"], dtype=sh["dtype"], device=self.device),
                 torch.empty(sh["x"][0], dtype=torch.int32, device=self.device)]
 
-    def _run(self, ops):
-        if ops:
-            for r in dist.batch_isend_irecv(ops):
-                r.wait()
+    def _empty_grads(self):
+        sh = self.shapes
+        return [torch.empty(sh[k], dtype=sh["dtype"], device=self.device) for k in ("x", "t6", "text")]
 
-    def _recv_ops(self, bufs, peer):
-        return [dist.P2POp(dist.irecv, b, self.pipe[peer], self.group) for b in bufs]
+    def _link(self, src, dst):
+        return self.links[(self.pipe[src], self.pipe[dst])]
 
-    def _send_ops(self, bufs, peer):
-        return [dist.P2POp(dist.isend, b.contiguous(), self.pipe[peer], self.group) for b in bufs]
+    def _post_recv(self, bufs, peer):
+        """Post receives from stage `peer`; returns a handle for ``_wait``."""
+        g = self._link(peer, self.s)
+        ops = [dist.P2POp(dist.irecv, b, self.pipe[peer], g) for b in bufs]
+        return bufs, dist.batch_isend_irecv(ops)
+
+    @staticmethod
+    def _wait(handle):
+        """The compute stream waits for the posted receives (NCCL: a stream dependency, the host runs on)."""
+        bufs, works = handle
+        for w in works:
+            w.wait()
+        return bufs
+
+    def _send(self, bufs, peer):
+        g = self._link(self.s, peer)
+        bufs = [b.contiguous() for b in bufs]
+        works = dist.batch_isend_irecv([dist.P2POp(dist.isend, b, self.pipe[peer], g) for b in bufs])
+        self._sends.append((works, bufs))  # kept alive; completion awaited at the end of the step
+
+    def _finish_sends(self):
+        for works, _ in self._sends:
+            for w in works:
+                w.wait()
+        self._sends = []
 
     # ---- one step --------------------------------------------------------------------------------------------
     def step(self, M, first_inputs=None, targets=None, side=None, loss_scale=1.0, before_last_backward=None):
@@ -199,11 +249,13 @@ class OneFOneB:
         n_steady = M - n_warm
         saved = {}
         losses = []
+        early = True  # receives posted a micro-batch ahead (one-direction streams make that safe)
 
         def forward(i, acts):
             if first:
                 z, t, kw = first_inputs(i)
-                x, t6, text, tl = self.m.stem(z, t, {k: v for k, v in kw.items() if k != "cond"}, kw.get("cond"))
+                x, t6, text, tl = self.m.stem(z, t, {k: v for k, v in kw.items() if k not in ("cond", "hw")},
+                                              kw.get("cond"), kw.get("hw"))
                 ins = None
             else:
                 x, t6, text, tl = acts
@@ -231,46 +283,57 @@ class OneFOneB:
                 return None
             return [a.grad if a.grad is not None else torch.zeros_like(a) for a in ins]
 
-        def recv_fwd():
+        # posted receives: activations of forward i, gradients of backward i
+        act_h, grad_h = {}, {}
+
+        def post_act(i):
+            if not first and i < M and i not in act_h:
+                act_h[i] = self._post_recv(self._empty_acts(), s - 1)
+
+        def post_grad(i):
+            if not last and i < M and i not in grad_h:
+                grad_h[i] = self._post_recv(self._empty_grads(), s + 1)
+
+        def acts_of(i):
             if first:
                 return None
-            bufs = self._empty_acts()
-            self._run(self._recv_ops(bufs, s - 1))
-            return bufs
+            post_act(i)
+            return self._wait(act_h.pop(i))
+
+        def grads_of(i):
+            if last:
+                return None
+            post_grad(i)
+            return self._wait(grad_h.pop(i))
 
         for i in range(n_warm):
-            out = forward(i, recv_fwd())
-            self._run(self._send_ops(out, s + 1))
-        acts = recv_fwd() if n_steady > 0 else None
+            a = acts_of(i)
+            if early:
+                post_act(i + 1)
+            out = forward(i, a)
+            self._send(out, s + 1)
+        if early:
+            post_grad(0)
         for j in range(n_steady):
             i_f, i_b = n_warm + j, j
-            out = forward(i_f, acts)
-            if last:
-                gr = None
-            else:  # send activations of i_f, receive the gradient of i_b
-                gr = [torch.empty_like(t) for t in out[:3]]
-                self._run(self._send_ops(out, s + 1) + self._recv_ops(gr, s + 1))
-            g_in = backward(i_b, gr)
-            if j == n_steady - 1:
-                acts = None
-                if not first:
-                    self._run(self._send_ops(g_in, s - 1))
-            else:
-                if first:
-                    acts = None
-                else:  # send the gradient of i_b, receive the activations of i_f + 1
-                    nxt = self._empty_acts()
-                    self._run(self._send_ops(g_in, s - 1) + self._recv_ops(nxt, s - 1))
-                    acts = nxt
-        for i in range(n_steady, M):
-            gr = None
+            a = acts_of(i_f)
+            if early:
+                post_act(i_f + 1)
+            out = forward(i_f, a)
             if not last:
-                gr = [torch.empty(self.shapes[k], dtype=self.shapes["dtype"], device=self.device)
-                      for k in ("x", "t6", "text")]
-                self._run(self._recv_ops(gr, s + 1))
-            g_in = backward(i, gr)
+                self._send(out, s + 1)
+            g_in = backward(i_b, grads_of(i_b))
+            if early:
+                post_grad(i_b + 1)
             if not first:
-                self._run(self._send_ops(g_in, s - 1))
+                self._send(g_in, s - 1)
+        for i in range(n_steady, M):
+            g_in = backward(i, grads_of(i))
+            if early:
+                post_grad(i + 1)
+            if not first:
+                self._send(g_in, s - 1)
+        self._finish_sends()
         return torch.stack(losses).sum() if last else None
 
 

@@ -122,20 +122,28 @@ class SnapshotSender:
         self.pb = peer_buffers
         self.version = 0
         self.counter = None
+        self.last_copy = None  # (bytes, device ms) of the last snapshot's peer copies, summed over the actors
         if self.pb is not None:
             self.counter = torch.zeros(1, dtype=torch.int64, device=self.params[0].device)
 
     def send(self):
         self.version += 1
         flat = flat_params(self.params)
+        nbytes, ms = 0, 0.0
         for dst in self.actors:
             dist.send(_hdr(KIND_SNAPSHOT, self.version, self.n), dst=dst, group=self.ctl)
             if self.pb is not None:
                 from ..ops._ext import ext
                 j = self.pb.group_ranks.index(dst)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
                 ext().peer_copy(self.pb.ptrs["flat"][j], flat, self.pb.ptrs["version"][j], self.counter.data_ptr(),
                                 self.version, 64)
+                e1.record()
                 torch.cuda.current_stream().synchronize()
+                nbytes += flat.numel() * flat.element_size()
+                ms += e0.elapsed_time(e1)
+                self.last_copy = (nbytes, ms)
                 dist.send(_hdr(KIND_SNAPSHOT, self.version), dst=dst, group=self.ctl)  # data landed
             else:
                 dist.send(flat, dst=dst)

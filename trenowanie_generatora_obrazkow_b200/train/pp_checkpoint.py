@@ -41,6 +41,8 @@ def _unsplit_order(den_cfg, te_cfg):
 def save(tr, out, step, samples, args, save_group, learner_group, keep=False):
     """Collective over the learner ranks. save_group: Gloo group of replica 0's stages (ranks 0 .. pp - 1)."""
     os.makedirs(out, exist_ok=True)
+    if hasattr(tr, "before_save"):
+        tr.before_save()  # sharded optimizer state into the optimizers (collective over the stage group)
     writes = [(dict(layout=layout(tr), step=step, opts=[o.state_dict() for o in tr.opts]), opt_path(out, tr))]
     latest = os.path.join(out, "latest.pt")
     if tr.replica == 0:
@@ -89,6 +91,8 @@ def resume(tr, out, resume_opt_mismatch=False, log=print):
     if opt is not None and opt.get("layout") == layout(tr) and len(opt["opts"]) == len(tr.opts):
         for o, st in zip(tr.opts, opt["opts"]):
             ckpt.load_opt_state(o, st)
+        if hasattr(tr, "after_load"):
+            tr.after_load()
     elif resume_opt_mismatch:
         log(f"[stage {tr.stage} replica {tr.replica}] optimizer state of {path} does not match this pipeline "
             "layout: starting it fresh (--resume-opt-mismatch)")

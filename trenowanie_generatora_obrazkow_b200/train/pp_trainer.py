@@ -15,17 +15,21 @@ import torch.distributed as dist
 from ..models.text import LMTextEncoder
 from ..optim import EMA, build_optimizers, lr_mult, set_lr
 from ..parallel.ddp import GradBuckets
-from ..parallel.pipeline import (OneFOneB, StageModel, clip_with_norm, grid_layout, pipe_grad_norm, recv_targets,
-                                 send_targets, stage_ranges)
+from ..parallel.pipeline import (OneFOneB, StageModel, clip_with_norm, direction_groups, grid_layout, pipe_grad_norm,
+                                 recv_targets, send_targets, stage_ranges)
+from ..ops import fused as Fz
+from ..optim.adamw import FusedAdamW
+from ..optim.muon import Muon
 from .flow import drop_captions
 from .trainer import TrainConfig
 
 
 def pp_groups(world, pp):
     """Process groups of the PP x DP grid over learner ranks [0, world): (pipe group per replica, stage group per
-    stage). A collective over the default group: every rank calls it, service ranks too."""
+    stage, one-direction links between adjacent stages). A collective over the default group: every rank calls it,
+    service ranks too."""
     _, pipes, stages = grid_layout(world, pp)
-    return [dist.new_group(r) for r in pipes], [dist.new_group(r) for r in stages]
+    return [dist.new_group(r) for r in pipes], [dist.new_group(r) for r in stages], direction_groups(pipes)
 
 
 class PPTrainer:
@@ -41,7 +45,7 @@ class PPTrainer:
         self.dp, pipes, stages = grid_layout(self.world, pp)
         self.stage, self.replica = self.rank % pp, self.rank // pp
         self.pipe = pipes[self.replica]
-        pipe_groups, stage_groups = groups if groups is not None else pp_groups(self.world, pp)
+        pipe_groups, stage_groups, self.links = groups if groups is not None else pp_groups(self.world, pp)
         self.pipe_group, self.stage_group = pipe_groups[self.replica], stage_groups[self.stage]
         self.den_cfg, self.te_cfg = den_cfg, te_cfg
         lo, hi = stage_ranges(den_cfg.depth, pp, te_cost)[self.stage]
@@ -52,7 +56,6 @@ class PPTrainer:
             dist.broadcast(p.data, src=stages[self.stage][0], group=self.stage_group)
         self.named = self.model.full_named_parameters()
         self.params = [p for _, _, p in self.named if p.requires_grad]
-        self.buckets = GradBuckets(self.params, group=self.stage_group, comm=cfg.grad_comm)
         ratio = cfg.global_batch / 256
         lr_scale = 1.0 if cfg.no_lr_batch_scaling else math.sqrt(ratio)
         self.opts, _ = build_optimizers(self.named, optimizer=cfg.optimizer, lr_muon=cfg.lr_muon, lr_emb=cfg.lr_emb,
@@ -60,6 +63,24 @@ class PPTrainer:
                                         beta2=cfg.beta2, momentum=cfg.momentum, ns_steps=cfg.ns_steps,
                                         cmuon=cfg.cmuon, muon_period=cfg.muon_period, muon_gamma=cfg.muon_gamma,
                                         shard=cfg.shard_muon, group=self.stage_group)
+        # Muon over the stage group: with replicas on CUDA, its gradients are reduce-scattered to the owners and
+        # the updates gathered into the parameter update over peer memory (parallel/muon_comm.py); the other
+        # gradients are all-reduced in buckets. Otherwise every gradient goes through the buckets.
+        self.muon = next((o for o in self.opts if isinstance(o, Muon)), None)
+        self.muon_comm = self.muon_buckets = None
+        dense = self.params
+        if (cfg.muon_comm == "sharded" and self.muon is not None and self.dp > 1 and self.device.type == "cuda"
+                and self.muon.world == self.dp):
+            from ..parallel.muon_comm import MuonShardedComm
+            mids = {id(p) for g in self.muon.param_groups for p in g["params"]}
+            transport = "p2p" if cfg.grad_comm == "p2p" else "torch"
+            self.muon_comm = MuonShardedComm(self.muon, group=self.stage_group, device=self.device,
+                                             transport=transport)
+            self.muon_buckets = GradBuckets([p for p in dense if id(p) in mids], group=self.stage_group,
+                                            comm="nccl_bf16", reducer=self.muon_comm.reduce_bucket)
+            self.muon_comm.attach_buckets(self.muon_buckets)
+            dense = [p for p in dense if id(p) not in mids]
+        self.buckets = GradBuckets(dense, group=self.stage_group, comm=cfg.grad_comm)
         ema = cfg.ema if cfg.ema is not None else 0.9995 ** ratio
         self.ema = EMA(self.params, ema) if self.replica == 0 else None
         self.gen = torch.Generator(device=self.device)
@@ -67,11 +88,22 @@ class PPTrainer:
         self.step_idx = 0
         self.sched = None
 
+    def before_save(self):
+        """Every learner rank: bring the owners' sharded Muon momentum into the optimizer state (collective over
+        the stage group)."""
+        if self.muon_comm is not None:
+            self.muon_comm.export_momentum()
+
+    def after_load(self):
+        """Every learner rank, after the optimizers' load_state_dict: take this rank's momentum shards."""
+        if self.muon_comm is not None:
+            self.muon_comm.import_momentum()
+
     def _schedule(self, mb, side, L):
         dt = torch.bfloat16 if self.device.type == "cuda" else torch.float32
         d = self.den_cfg
         shapes = dict(x=(mb, side * side, d.dim), t6=(mb, 6, d.dim), text=(mb, L, d.text_dim), dtype=dt)
-        return OneFOneB(self.model, self.pipe, self.stage, shapes, self.device)
+        return OneFOneB(self.model, self.pipe, self.stage, shapes, self.device, links=self.links)
 
     def step(self, batch):
         """batch (stage 0 of every replica): x0 (M * mb, C, h, w) and lm_states (M * mb, L, D) [+ valid, is_null,
@@ -86,6 +118,9 @@ class PPTrainer:
         L = batch["text_len"]
         C = self.den_cfg.latent_channels
         self.buckets.zero()
+        if self.muon_buckets is not None:
+            self.muon_buckets.zero()
+            self.muon_comm.begin_step()
         inputs, targets = [], None
         if self.first:
             st_all = batch["lm_states"].to(self.device, non_blocking=True)
@@ -101,12 +136,13 @@ class PPTrainer:
                     torch.ones(mb, L, dtype=torch.bool, device=self.device)
                 is_null = batch["is_null"][sl].to(self.device) if batch.get("is_null") is not None else None
                 is_null, valid = drop_captions(is_null, valid, cfg.cfg_drop, self.gen)
-                tt = t.view(-1, 1, 1, 1)
-                kw = dict(lm_states=st_all[sl], valid=valid, is_null=is_null)
+                kw = dict(lm_states=st_all[sl], valid=valid, is_null=is_null, hw=tuple(x0.shape[2:]))
                 if batch.get("cond") is not None:  # micro-conditions (crop windows) of the micro-batch
                     kw["cond"] = batch["cond"][sl].to(self.device)
-                inputs.append(((1 - tt) * x0 + tt * eps, t, kw))
-                targets.append((eps - x0).flatten(2).transpose(1, 2).contiguous())
+                # token-major z_t (bf16 on CUDA) and eps - x0 (fp32) in one pass (the fused kernel on CUDA)
+                z_tok, target = Fz.fm_inputs(x0, eps, t)
+                inputs.append((z_tok, t, kw))
+                targets.append(target.contiguous())
             if self.pp > 1:
                 send_targets(targets, self.pipe)
                 targets = None
@@ -114,15 +150,42 @@ class PPTrainer:
             targets = recv_targets(M, (mb, side * side, C), torch.float32, self.device, self.pipe)
         if self.sched is None or self.sched.shapes["x"][:2] != (mb, side * side) or self.sched.shapes["text"][1] != L:
             self.sched = self._schedule(mb, side, L)
+        def arm():
+            self.buckets.arm()
+            if self.muon_buckets is not None:
+                self.muon_buckets.arm()
+
         loss = self.sched.step(M, (lambda i: inputs[i]) if self.first else None, targets, side, 1.0 / M,
-                               before_last_backward=self.buckets.arm)
+                               before_last_backward=arm)
         self.buckets.finish()
-        norm = pipe_grad_norm(self.params, self.pipe_group)
-        clip_with_norm(self.params, norm, cfg.clip)
+        if self.muon_buckets is not None:
+            self.muon_buckets.finish()
+        # global norm over the pipe: this stage's squared norm (Muon part: the owners' all-reduced squares), summed
+        # over the stages; the optimizers apply the clip coefficient themselves
+        others = [p.grad for p in self.buckets.params if p.grad is not None]
+        sq = torch.stack(torch._foreach_norm(others)).float().square().sum() if others else \
+            torch.zeros((), device=self.device)
+        if self.muon_comm is not None:
+            sq = sq + self.muon_comm.owned_sumsq().reshape(())
+        if self.pp > 1:
+            dist.all_reduce(sq, group=self.pipe_group)
+        norm = sq.sqrt()
+        coef = (cfg.clip / (norm + 1e-6)).clamp(max=1.0)
         set_lr(self.opts, lr_mult(self.step_idx, cfg.steps, cfg.warmup, cfg.schedule))
+        ema = self.ema
+        rate = 1.0 - ema.decay_at(self.step_idx + 1) if ema is not None else 0.0
         for o in self.opts:
-            o.step()
+            if o is self.muon and self.muon_comm is not None:
+                self.muon_comm.step(coef, ema=ema, ema_rate=rate)
+            elif isinstance(o, (Muon, FusedAdamW)):
+                o.step(coef=coef, ema=ema, ema_rate=rate)
+            else:
+                grads = [p.grad for g in o.param_groups for p in g["params"] if p.grad is not None]
+                if grads:
+                    torch._foreach_mul_(grads, coef)
+                o.step()
         self.step_idx += 1
-        if self.ema is not None:
-            self.ema.update(self.step_idx)
+        if ema is not None:
+            ema.update(self.step_idx)  # what the fused launches did not cover
+        self.last_gnorm = norm
         return loss
