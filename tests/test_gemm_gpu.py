@@ -17,7 +17,7 @@ def _rel(x, y):
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 1024), (200, 136, 72), (1000, 384, 520), (64, 8, 8),
-                                   (4096, 2048, 2048)])
+                                   (4096, 2048, 2048), (8192, 6144, 2048)])
 def test_gemm_layouts(a_mn, b_mn, M, N, K):
     from trenowanie_generatora_obrazkow_b200.ops.gemm import gemm
     from trenowanie_generatora_obrazkow_b200.ops._ext import check_errors
@@ -153,3 +153,17 @@ def test_newton_schulz_syrk_matches_reference():
     x = zeropower(g)
     ref = zeropower_reference(g.float())
     assert _rel(x, ref) < 3e-2
+
+
+def test_gemm_production_wgrad_accumulate():
+    """The qkv weight gradient of the 1.24B model at 32 x 1024 tokens: dW (6144 x 2048) += dY^T X over K = 32768,
+    fp32 accumulate into an existing gradient (many tiles per persistent CTA, TMA reduce-add epilogue)."""
+    from trenowanie_generatora_obrazkow_b200.ops.gemm import gemm
+    torch.manual_seed(9)
+    dy = (torch.randn(32768, 6144, device="cuda") * 0.05).bfloat16()
+    x = (torch.randn(32768, 2048, device="cuda") * 0.05).bfloat16()
+    out = torch.randn(6144, 2048, device="cuda")
+    ref = out + _ref(dy, x, True, True)
+    gemm(dy, x, out=out, a_mn=True, b_mn=True, accumulate=True)
+    torch.cuda.synchronize()
+    assert _rel(out, ref) < 1e-3

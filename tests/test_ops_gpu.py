@@ -61,7 +61,8 @@ def test_adanorm(D, T, with_res, with_gate, with_mod):
 @pytest.mark.parametrize("hd,hq,hkv,norm,rope,T,kv_mask", [(128, 4, 4, True, True, 256, False),
                                                           (64, 6, 2, False, True, 77, True),
                                                           (128, 2, 2, True, False, 130, False),
-                                                          (64, 9, 3, False, True, 64, True)])
+                                                          (64, 9, 3, False, True, 64, True),
+                                                          (64, 16, 4, False, True, 128, True)])  # the refiner
 def test_self_attention_core(hd, hq, hkv, norm, rope, T, kv_mask):
     torch.manual_seed(1)
     B = 2
@@ -248,3 +249,49 @@ def test_fm_inputs_and_forward_tokens():
         v_ref = den((1 - tt) * x0 + tt * eps, t, text, valid, tokens_out=True)
     assert v_tok.shape == v_ref.shape
     assert rel(v_tok, v_ref) < 1e-2
+
+
+def _fp32_self_attention(qkv, hq, hkv, hd, qw, kw, cos, sin):
+    """fp32 oracle on the GPU (the production shapes are too large for the CPU)."""
+    B, T, _ = qkv.shape
+    q, k, v = qkv.float().split([hq * hd, hkv * hd, hkv * hd], dim=-1)
+    q, k, v = q.view(B, T, hq, hd), k.view(B, T, hkv, hd), v.view(B, T, hkv, hd)
+    q, k = R.apply_rope(R.rmsnorm(q, qw), cos, sin), R.apply_rope(R.rmsnorm(k, kw), cos, sin)
+    return R.attention(q, k, v, None, hd ** -0.5).reshape(B, T, hq * hd)
+
+
+def test_self_attention_production_shape():
+    """B 4 x T 4096 x 16 heads x 128 (1024 work items of 256 query rows > 148 persistent CTAs: barrier phases and the
+    O hand-off between one item's epilogue and the next item's P V are exercised), 2-D RoPE, q/k norm."""
+    torch.manual_seed(5)
+    B, T, H, hd = 4, 4096, 16, 128
+    qkv = torch.randn(B, T, 3 * H * hd, device="cuda").bfloat16()
+    qw, kw = 1 + 0.1 * torch.randn(hd, device="cuda"), 1 + 0.1 * torch.randn(hd, device="cuda")
+    cos, sin = R.rope_2d_table(64, 64, hd, 0, "cuda")
+    do = torch.randn(B, T, H * hd, device="cuda").bfloat16()
+    a = qkv.clone().requires_grad_()
+    qa, ka = qw.clone().requires_grad_(), kw.clone().requires_grad_()
+    o = Fz.self_attention_core(a, H, H, hd, qa, ka, cos, sin)
+    o.backward(do)
+    b = qkv.float().requires_grad_()
+    qb, kb = qw.clone().requires_grad_(), kw.clone().requires_grad_()
+    ref = _fp32_self_attention(b, H, H, hd, qb, kb, cos, sin)
+    ref.backward(do.float())
+    assert rel(o, ref) < 2e-2
+    assert rel(a.grad, b.grad) < 4e-2
+    assert rel(qa.grad, qb.grad) < 4e-2 and rel(ka.grad, kb.grad) < 4e-2
+
+
+def test_cross_attention_sampling_shape():
+    """16 x 4096 queries against 128 text tokens with per-sample key lengths (the sampling step's cross-attention)."""
+    torch.manual_seed(6)
+    B, T, D, heads, L = 16, 4096, 2048, 16, 128
+    q = torch.randn(B, T, D, device="cuda").bfloat16()
+    kv = torch.randn(B, L, 2 * D, device="cuda").bfloat16()
+    kv_len = torch.randint(1, L + 1, (B,), device="cuda", dtype=torch.int32)
+    with torch.no_grad():
+        o = Fz.cross_attention_core(q, kv, heads, kv_len)
+        k, v = kv.float().chunk(2, dim=-1)
+        ref = R.attention(q.float().view(B, T, heads, D // heads), k.view(B, L, heads, D // heads),
+                          v.view(B, L, heads, D // heads), kv_len, (D // heads) ** -0.5).reshape(B, T, D)
+    assert rel(o, ref) < 2e-2

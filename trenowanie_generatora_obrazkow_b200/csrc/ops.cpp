@@ -779,6 +779,20 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::T
                    c10::optional<at::Tensor> kv_len, double scale, at::Tensor dq, at::Tensor dk, at::Tensor dv,
                    at::Tensor err) {
   const c10::cuda::CUDAGuard guard(q.device());
+  if (g_attention_tc && q.size(3) == 64) {
+    // head dim 64 (the text refiner): the tcgen05 backward on copies zero-padded to head dim 128. Zero columns add
+    // nothing to Q K^T, P, delta = rowsum(dO O) or the log-sum-exp of the forward; the gradients' padded columns
+    // are dropped. (The mma.sync path remains for set_attention_tc(false).)
+    auto pad = [](const at::Tensor& t) { return at::constant_pad_nd(t, {0, 64}).contiguous(); };
+    at::Tensor q2 = pad(q), k2 = pad(k), v2 = pad(v), o2 = pad(o), do2 = pad(dO);
+    at::Tensor dq2 = at::empty(q2.sizes(), q2.options().dtype(dq.scalar_type()));
+    at::Tensor dk2 = at::empty_like(k2), dv2 = at::empty_like(v2);
+    attention_bwd(q2, k2, v2, o2, lse, do2, kv_len, scale, dq2, dk2, dv2, err);
+    dq.copy_(dq2.narrow(3, 0, 64));
+    dk.copy_(dk2.narrow(3, 0, 64));
+    dv.copy_(dv2.narrow(3, 0, 64));
+    return;
+  }
   AttnParams p = attn_params(q, k, v, kv_len, scale);
   attn_check4(o, "o");
   attn_check4(dO, "dO");
