@@ -126,3 +126,11 @@ def test_train_multi_res(tmp_path):
           "--eval-every", "0", "--no-wandb", "--res", "256", "--multi-res", "128", "256", "--multi-res-mbs", "2",
           "1", "--multi-res-mb", "2", "2", "--t-shift-ref", "256", "--workers", "0"])
     assert os.path.exists(os.path.join(out, "latest.pt"))
+
+
+def test_train_selective_activation_checkpointing(tmp_path):
+    """--act-checkpoint selective (and the reference's bare --act-checkpoint = full) run end to end."""
+    out = str(tmp_path / "run")
+    for mode in (["--act-checkpoint", "selective"], ["--act-checkpoint"]):
+        _run(["--synthetic", "16", "--out", out, "--size", "50m", "--te-size", "13m", "--batch", "2",
+              "--micro-batch", "2", "--steps", "1", "--eval-every", "0", "--no-wandb", "--ckpt-every", "0"] + mode)

@@ -117,7 +117,9 @@ def build_parser():
     a("--offload", action="store_true")
     a("--outer-comm", choices=["bf16", "fp32"], default="bf16")
     a("--muon-momentum-dtype", choices=["fp32", "bf16"], default="fp32")
-    a("--act-checkpoint", action="store_true")
+    a("--act-checkpoint", nargs="?", const="full", default=None, choices=["full", "selective"],
+      help="activation checkpointing per block: full recompute, or selective (keep GEMM / attention outputs, "
+           "recompute the norms, q/k-norm + RoPE and SwiGLU in the backward)")
     a("--workers", type=int, default=4)
     a("--seed", type=int, default=0)
     a("--log-every", type=int, default=None)

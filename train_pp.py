@@ -49,7 +49,9 @@ def build_parser():
     a("--microbatches", type=int, default=None, help="micro-batches per step and replica (default 4 x pp)")
     a("--micro-batch", type=int, default=4)
     a("--te-cost", type=float, default=1.0, help="text encoder + stem cost in blocks (stage balancing)")
-    a("--act-checkpoint", action="store_true")
+    a("--act-checkpoint", nargs="?", const="full", default=None, choices=["full", "selective"],
+      help="activation checkpointing per block: full recompute, or selective (keep GEMM / attention outputs, "
+           "recompute the norms, q/k-norm + RoPE and SwiGLU in the backward)")
     a("--te-checkpoint", action="store_true", help="recompute the text encoder in the backward (with --act-checkpoint "
       "the whole first stage is recomputed already)")
     a("--steps", type=int, default=100)
@@ -355,6 +357,7 @@ def run_fm(args, den_cfg, te_cfg, lay, device, ctl, text_group):
                       muon_gamma=args.muon_gamma, clip=args.clip, ema=args.ema, cfg_drop=args.cfg_drop,
                       seed=args.seed, t_shift=args.t_shift, grad_comm=grad_comm)
     tr = PPTrainer(den_cfg, te_cfg, cfg, device, args.pp, M, args.te_cost, world=world, groups=groups)
+    tr.model.act_checkpoint = args.act_checkpoint or False  # per block: "full" or "selective"
     if tr.first and args.te_checkpoint:
         tr.model.te_checkpoint = True
     step, samples = pp_checkpoint.resume(tr, args.out, args.resume_opt_mismatch)

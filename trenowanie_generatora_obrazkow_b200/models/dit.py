@@ -122,7 +122,7 @@ class Denoiser(nn.Module):
         self.norm = RMSNorm(dim)
         self.patch_out = nn.Linear(dim, cfg.latent_channels, bias=False)
         self._rope_cache = {}
-        self.checkpoint_blocks = False
+        self.checkpoint_blocks = False  # activation checkpointing: False, "full" / True or "selective"
 
     # ---------------------------------------------------------------------------------------------- RoPE tables
     def rope(self, h, w, device):
@@ -176,12 +176,9 @@ class Denoiser(nn.Module):
         hidden = None
         hi = len(self.blocks) if hi is None else hi
         for i in range(lo, hi):
-            blk = self.blocks[i]
-            if self.checkpoint_blocks and torch.is_grad_enabled():
-                x, pending = torch.utils.checkpoint.checkpoint(blk, x, pending, t6, text, text_len, cos, sin,
-                                                               use_reentrant=False)
-            else:
-                x, pending = blk(x, pending, t6, text, text_len, cos, sin)
+            # activation checkpointing: False, "full" (True) or "selective" (ops/fused.py run_block)
+            x, pending = Fz.run_block(self.blocks[i], (x, pending, t6, text, text_len, cos, sin),
+                                      self.checkpoint_blocks)
             if i + 1 == hidden_at:
                 hidden = _flush(x, pending)
         return x, pending, hidden

@@ -70,11 +70,8 @@ class TextBlock(nn.Module):
 
 def _run_blocks(blocks, x, lens, cos, sin, final_norm, checkpoint=False):
     pending = None
-    for blk in blocks:
-        if checkpoint and torch.is_grad_enabled():
-            x, pending = torch.utils.checkpoint.checkpoint(blk, x, pending, lens, cos, sin, use_reentrant=False)
-        else:
-            x, pending = blk(x, pending, lens, cos, sin)
+    for blk in blocks:  # checkpoint: False, "full" (True) or "selective" (ops/fused.py run_block)
+        x, pending = Fz.run_block(blk, (x, pending, lens, cos, sin), checkpoint)
     _, h = Fz.adanorm(x, pending, None, final_norm.weight)
     return h
 

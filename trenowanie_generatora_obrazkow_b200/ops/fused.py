@@ -93,6 +93,89 @@ def _notify(p):
 
 
 # ----------------------------------------------------------------------------------------------------------------
+# selective activation checkpointing
+# ----------------------------------------------------------------------------------------------------------------
+# Keep what the backward needs from the GEMMs and attention, rebuild the elementwise results (reference
+# train_pp.py:271-287, whose policy saves matmul / attention outputs and recomputes the rest). Here the elementwise
+# results that autograd functions save are tagged with a recipe: the adanorm output (saved by the next linear), the
+# normalised + rotated q and k (saved by attention) and the SwiGLU output (saved by the down projection). Under
+# ``selective_recompute()`` a saved-tensor hook stores a tagged tensor as its recipe, which the backward runs again
+# from tensors that are saved anyway (the residual stream, q/k/v, the up projection's output); everything else is
+# saved as usual, so no GEMM or attention is recomputed.
+_SAC_ACTIVE = [0]
+
+
+class _Recipe:
+    """Rebuilds one or more tensors at most once (q and k share one kernel launch)."""
+    __slots__ = ("fn", "outs")
+
+    def __init__(self, fn):
+        self.fn, self.outs = fn, None
+
+    def get(self, i):
+        if self.outs is None:
+            self.outs = self.fn()
+        return self.outs[i]
+
+
+class _Rebuild:
+    __slots__ = ("recipe", "index", "shape")
+
+    def __init__(self, recipe, index, shape):
+        self.recipe, self.index, self.shape = recipe, index, shape
+
+
+def _tag(t, recipe, index=0):
+    if _SAC_ACTIVE[0]:
+        t._tgo_recipe = (recipe, index, None)
+    return t
+
+
+def _tag_view(view, base):
+    """A view of a tagged tensor (same storage and start) is rebuilt the same way, then reshaped."""
+    r = getattr(base, "_tgo_recipe", None)
+    if r is not None and view is not base and view.data_ptr() == base.data_ptr():
+        view._tgo_recipe = (r[0], r[1], tuple(view.shape))
+
+
+def _pack(t):
+    r = getattr(t, "_tgo_recipe", None)
+    return t if r is None else _Rebuild(*r)
+
+
+def _unpack(x):
+    if not isinstance(x, _Rebuild):
+        return x
+    out = x.recipe.get(x.index)
+    return out if x.shape is None else out.reshape(x.shape)
+
+
+class selective_recompute:
+    """Context of a block's forward under selective activation checkpointing (see above)."""
+
+    def __enter__(self):
+        self._hooks = torch.autograd.graph.saved_tensors_hooks(_pack, _unpack)
+        self._hooks.__enter__()
+        _SAC_ACTIVE[0] += 1
+        return self
+
+    def __exit__(self, *exc):
+        _SAC_ACTIVE[0] -= 1
+        return self._hooks.__exit__(*exc)
+
+
+def run_block(block, args, mode):
+    """block(*args) with activation checkpointing: mode None / False (none), "full" / True (recompute the whole
+    block in the backward) or "selective" (recompute only its elementwise results)."""
+    if not mode or not torch.is_grad_enabled():
+        return block(*args)
+    if mode == "selective":
+        with selective_recompute():
+            return block(*args)
+    return torch.utils.checkpoint.checkpoint(block, *args, use_reentrant=False)
+
+
+# ----------------------------------------------------------------------------------------------------------------
 # linear
 # ----------------------------------------------------------------------------------------------------------------
 class _LinearFn(torch.autograd.Function):
@@ -103,6 +186,7 @@ class _LinearFn(torch.autograd.Function):
             x2 = x2.to(torch.bfloat16)
         if not x2.is_contiguous():
             x2 = x2.contiguous()
+        _tag_view(x2, x)
         y = gemm(x2, w16)
         ctx.save_for_backward(x2, w16)
         ctx.weight = weight
@@ -211,8 +295,16 @@ def adanorm(x, y, gate, w, shift=None, scale=None, eps=R.EPS):
         return xn, h
     x = x.contiguous()
     if y is None:
-        return x, _NormModFn.apply(x, w, shift, scale, eps)
-    return _AdaNormFn.apply(x, y.contiguous(), gate, w, shift, scale, eps)
+        h = _NormModFn.apply(x, w, shift, scale, eps)
+        x_new = x
+    else:
+        x_new, h = _AdaNormFn.apply(x, y.contiguous(), gate, w, shift, scale, eps)
+    if _SAC_ACTIVE[0]:  # h = rmsnorm(x_new) w (1 + scale) + shift, rebuilt from the residual stream
+        T, xd = x.shape[1], x_new.detach()
+        sd = None if shift is None else shift.detach()
+        cd = None if scale is None else scale.detach()
+        _tag(h, _Recipe(lambda: (ext().adanorm_fwd(xd, None, None, w.detach(), sd, cd, T, eps)[1],)))
+    return x_new, h
 
 
 # ----------------------------------------------------------------------------------------------------------------
@@ -234,6 +326,11 @@ class _SelfAttnFn(torch.autograd.Function):
         k4 = k.view(B, T, hkv, hd)
         v4 = qkv[:, :, (hq + hkv) * hd:(hq + 2 * hkv) * hd].unflatten(-1, (hkv, hd))
         o, lse = ext().attention_fwd(q4, k4, v4, kv_len, scale, None, err_buf(q4.device))
+        if _SAC_ACTIVE[0]:  # normalised + rotated q, k: one kernel rebuilds both from qkv
+            q2d = q2.detach()
+            rec = _Recipe(lambda: ext().qknorm_rope_fwd(q2d, hq, hkv, hd, q_w, k_w, cos, sin, T, eps)[:2])
+            _tag(q, rec, 0)
+            _tag(k, rec, 1)
         ctx.save_for_backward(qkv, q, k, o, lse, rq, rk, q_w, k_w, cos, sin, kv_len)
         ctx.dims = (hq, hkv, hd, scale)
         return o.view(B, T, hq * hd)
@@ -372,4 +469,8 @@ def fm_inputs(x0, eps, t):
 def swiglu(ab):
     if not ab.is_cuda:
         return R.swiglu(ab)
-    return _SwiGLUFn.apply(ab)
+    ab = ab.contiguous()
+    g = _SwiGLUFn.apply(ab)
+    if _SAC_ACTIVE[0]:  # rebuilt from the up projection's output (saved by the SwiGLU backward)
+        _tag(g, _Recipe(lambda: (ext().swiglu_fwd(ab.detach()),)))
+    return g

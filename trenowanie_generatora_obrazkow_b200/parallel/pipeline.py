@@ -82,6 +82,7 @@ class StageModel(nn.Module):
             self.te.init_weights()
             self.te.to(device)
         self._rope = {}
+        self.act_checkpoint = False
 
     # Denoiser.init_stem / init_cond / init_head read these attributes
     @property
@@ -154,10 +155,11 @@ class StageModel(nn.Module):
         return x, t6, text, R.valid_to_len(valid).to(torch.int32)
 
     def run(self, x, t6, text, text_len, side):
+        from ..ops import fused as Fz
         cos, sin = self.rope(side, side, x.device)
         pending = None
-        for blk in self.blocks:
-            x, pending = blk(x, pending, t6, text, text_len, cos, sin)
+        for blk in self.blocks:  # act_checkpoint: False, "full" or "selective" (ops/fused.py run_block)
+            x, pending = Fz.run_block(blk, (x, pending, t6, text, text_len, cos, sin), self.act_checkpoint)
         if self.last:
             from ..ops import fused as Fz
             if x.is_cuda:

@@ -89,7 +89,7 @@ class TrainConfig:
     outer_comm: str = "bf16"
     offload: bool = False
     seed: int = 0
-    act_checkpoint: bool = False
+    act_checkpoint: object = False  # False, "full" (or True) or "selective"
     random_lm: bool = False
     moe_experts: int = 0          # > 0: every moe_every-th block's MLP becomes an MoE layer
     moe_top_k: int = 2
@@ -129,7 +129,8 @@ class Trainer:
         if cfg.moe_experts:
             from ..models.moe import MoEMLP, moe_denoiser
             ep_group = dist.group.WORLD if (cfg.expert_parallel and self.distributed and self.world > 1) else None
-            transport = cfg.moe_transport if not cfg.act_checkpoint else "nccl"  # recomputed blocks: no epochs
+            # fully recomputed blocks would replay the peer exchange (its epochs): those use NCCL
+            transport = cfg.moe_transport if cfg.act_checkpoint in (False, None, "", "selective") else "nccl"
             moe_denoiser(den, cfg.moe_experts, cfg.moe_top_k, cfg.moe_hidden, cfg.moe_every, cfg.moe_capacity, ep_group,
                          transport)
             torch.manual_seed(cfg.seed * 7919 + (self.rank if ep_group is not None else 0))
