@@ -400,7 +400,7 @@ def main():
                 logger.log(res, step)
         if args.merge_every and step >= args.merge_start * args.steps and step % args.merge_every == 0 and master:
             ckpt.save_merge(args.out, step, args.steps, den_cfg, te_cfg, te, den)
-        if step % args.ckpt_every == 0 or step == args.steps:
+        if (args.ckpt_every and step % args.ckpt_every == 0) or step == args.steps:
             save()
             if distributed:
                 dist.barrier()
