@@ -167,3 +167,29 @@ def test_gemm_production_wgrad_accumulate():
     gemm(dy, x, out=out, a_mn=True, b_mn=True, accumulate=True)
     torch.cuda.synchronize()
     assert _rel(out, ref) < 1e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 2048, 32768), (2048, 5504, 32768), (4096, 1024, 4096), (2000, 1000, 20000),
+                                   (6144, 2048, 2048)])
+def test_gemm_wgrad_split_k(M, N, K):
+    """Weight-gradient layout, fp32 accumulate: with split-K (partial tiles reduce-added) and without, against fp32."""
+    from trenowanie_generatora_obrazkow_b200.ops._ext import check_errors, ext
+    from trenowanie_generatora_obrazkow_b200.ops.gemm import gemm
+    torch.manual_seed(10)
+    dy = (torch.randn(K, M, device="cuda") * 0.05).bfloat16()
+    x = (torch.randn(K, N, device="cuda") * 0.05).bfloat16()
+    base = torch.randn(M, N, device="cuda")
+    ref = base + _ref(dy, x, True, True)
+    outs = []
+    for split in (True, False):
+        ext().set_gemm_splitk(split)
+        try:
+            out = base.clone()
+            gemm(dy, x, out=out, a_mn=True, b_mn=True, accumulate=True)
+            torch.cuda.synchronize()
+            check_errors()
+        finally:
+            ext().set_gemm_splitk(True)
+        outs.append(out)
+        assert _rel(out, ref) < 1e-3
+    assert _rel(outs[0], outs[1]) < 1e-4  # different fp32 summation order over K

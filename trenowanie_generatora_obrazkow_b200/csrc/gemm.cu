@@ -545,11 +545,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   const int num_m = (p.M + 255) / 256;
   const int num_n = (p.N + G2_BN - 1) / G2_BN;
   const bool syrk = p.syrk != 0;
-  const int tiles_per_batch = syrk ? num_m * (num_m + 1) / 2 : num_m * num_n;
+  const int splits = (EPI == EPI_F32_ACC && p.splitk > 1) ? p.splitk : 1;
+  const int tiles_per_batch = (syrk ? num_m * (num_m + 1) / 2 : num_m * num_n) * splits;
   const int num_tiles = tiles_per_batch * p.batch;
-  const int num_kb = (p.K + GEMM_BK - 1) / GEMM_BK;
-  // tile index within a batch -> (row block, column block); symmetric mode: the lower triangle, row by row
+  const int num_kb_all = (p.K + GEMM_BK - 1) / GEMM_BK;
+  const int kb_per_split = (num_kb_all + splits - 1) / splits;
+  // split s of a tile covers k-blocks [s * kb_per_split, min(all, (s + 1) * kb_per_split))
+  auto kb_range = [&](int r, int& kb0, int& kb1) {
+    const int sp = r / (tiles_per_batch / splits);
+    kb0 = sp * kb_per_split;
+    kb1 = min(num_kb_all, kb0 + kb_per_split);
+  };
+  // tile index within a batch -> (row block, column block); symmetric mode: the lower triangle, row by row;
+  // split-K: the split index varies slowest
   auto tile_mn = [&](int r, int& mt, int& nt) {
+    r %= tiles_per_batch / splits;
     if (syrk) {
       int i = (int)((sqrtf(8.f * (float)r + 1.f) - 1.f) * 0.5f);
       while ((i + 1) * (i + 2) / 2 <= r) ++i;
@@ -594,10 +604,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       uint32_t phase = 0;
       for (int tile = cluster; tile < num_tiles && !abort_sh; tile += n_clusters) {
         const int b = tile / tiles_per_batch;
-        int mt, nt;
+        int mt, nt, kb0, kb1;
         tile_mn(tile % tiles_per_batch, mt, nt);
+        kb_range(tile % tiles_per_batch, kb0, kb1);
         const int m0 = mt * 256 + rank * 128, n0 = nt * G2_BN + rank * 128;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.err, ERR_MBAR_TIMEOUT_PRODUCER)) {
             abort_sh = 1;
             break;
@@ -647,7 +658,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * G2_BN;
         bool ok = true;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        int kb0, kb1;
+        kb_range(tile % tiles_per_batch, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, p.err, ERR_MBAR_TIMEOUT_MMA)) {
             abort_sh = 1;
             ok = false;
@@ -658,7 +671,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
           const uint64_t bd = sdesc_add(b_desc0, stage * G2_STAGE_BYTES);
 #pragma unroll
           for (int k = 0; k < GEMM_BK / 16; ++k) {
-            umma_f16_pair(d_tmem, ad + k * A_KSTEP, bd + k * B_KSTEP, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_pair(d_tmem, ad + k * A_KSTEP, bd + k * B_KSTEP, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit_pair_mc(&empty_bar[stage], 0x3);  // frees this stage in both CTAs
           if (++stage == G2_STAGES) {
@@ -818,7 +831,8 @@ static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb
     attr_set = true;
   }
   const int nm = (p.M + 255) / 256;
-  const int num_tiles = (p.syrk ? nm * (nm + 1) / 2 : nm * ((p.N + G2_BN - 1) / G2_BN)) * p.batch;
+  const int splits = (EPI == EPI_F32_ACC && p.splitk > 1) ? p.splitk : 1;
+  const int num_tiles = (p.syrk ? nm * (nm + 1) / 2 : nm * ((p.N + G2_BN - 1) / G2_BN)) * p.batch * splits;
   const int grid = std::max(2, std::min(2 * num_tiles, (num_sms() / 2) * 2));
   kern<<<grid, GEMM_THREADS, G2_SMEM, stream>>>(ta, tb, tc != nullptr ? *tc : ta, p);
   return cudaGetLastError();
@@ -892,6 +906,8 @@ cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
                         bool b_mn, int epi, cudaStream_t s, const CUtensorMap* tc) {
   if (p.c_tma != 0 && tc == nullptr) return cudaErrorInvalidValue;  // TMA epilogue needs C's tensor map
   if (p.syrk != 0 && (bn != 0 || epi != EPI_BF16 || p.c_tma == 0 || p.M != p.N)) return cudaErrorInvalidValue;
+  // split-K partial tiles must reduce-add (atomic in L2): 2-CTA kernel, fp32 accumulate through the tensor map
+  if (p.splitk > 1 && (bn != 0 || epi != EPI_F32_ACC || p.c_tma == 0 || p.syrk != 0)) return cudaErrorInvalidValue;
   if (epi == EPI_SWIGLU) {  // forward only (A and B K-major), 256-column tiles
     if (a_mn || b_mn || (bn != 0 && bn != 256) || p.N % 256 != 0) return cudaErrorInvalidValue;
     return bn == 0 ? launch_gemm_pair<false, false, EPI_SWIGLU>(ta, tb, p, s, tc)

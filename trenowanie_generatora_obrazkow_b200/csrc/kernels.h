@@ -48,6 +48,9 @@ struct GemmParams {
   // 256-row tile blocks on or below the diagonal are computed; each off-diagonal tile is stored twice (as itself
   // and transposed). Valid when alpha A B^T + beta D is symmetric (D symmetric or absent).
   int syrk;
+  // split-K (2-CTA kernel, fp32 accumulate through the TMA reduce-add epilogue only): each output tile is computed
+  // as `splitk` partial products over consecutive K ranges, all reduce-added into C (atomic in L2)
+  int splitk;
 };
 constexpr int kMaxGroups = 256;
 // epi: 0 = bf16 store, 1 = fp32 store, 2 = fp32 accumulate (C += alpha * A B^T)

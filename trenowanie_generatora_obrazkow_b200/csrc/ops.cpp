@@ -124,6 +124,23 @@ static bool g_gemm_pair_enabled = true;  // 256 x 256 CTA-pair tiles: 3-6 % fast
 void set_gemm_pair(bool on) { g_gemm_pair_enabled = on; }
 static bool g_gemm_syrk = true;  // symmetric mode of gemm_syrk (off: the full product, for A/B runs)
 void set_gemm_syrk(bool on) { g_gemm_syrk = on; }
+static bool g_gemm_splitk = true;  // split-K of the fp32-accumulating GEMMs (off: one unit per tile, for A/B runs)
+void set_gemm_splitk(bool on) { g_gemm_splitk = on; }
+
+// Smallest split count whose units fill the CTA pairs in waves at >= 92 % (at least 32 k-blocks of 64 per split,
+// at most 16 splits); every split non-empty (the count is derived from the k-blocks per split).
+static int choose_splitk(int64_t tiles, int64_t K) {
+  const int64_t pairs = num_sms() / 2, nkb = (K + 63) / 64;
+  for (int s = 1; s <= 16; ++s) {
+    if (nkb / s < 32) break;
+    const int64_t units = tiles * s, waves = (units + pairs - 1) / pairs;
+    if ((double)units / (double)(waves * pairs) >= 0.92) {
+      const int64_t per = (nkb + s - 1) / s;
+      return (int)((nkb + per - 1) / per);
+    }
+  }
+  return 1;
+}
 
 static int* err_ptr(const at::Tensor& err) {
   TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt && err.numel() >= 1, "err must be a CUDA int32 tensor");
@@ -162,7 +179,18 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor C, bool a_mn, bool b_mn, c10::o
   // 2-CTA kernel (256 x 256 tiles over a CTA pair) when there are enough such tiles to fill the GPU; otherwise
   // the 1-CTA kernel with 128 x 256 (or 128 x 128 for N <= 128) tiles.
   const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256) * batch;
-  const bool use_pair = g_gemm_pair_enabled && M >= 256 && N >= 256 && pair_tiles >= num_sms() / 2;
+  const bool has_d = D.has_value() && D->defined();
+  TORCH_CHECK(C.stride(-2) % 8 == 0 && reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0, "gemm: C alignment");
+  // C's tensor map first: the TMA epilogue (and split-K, which needs its reduce-add) depend on it
+  CUtensorMap tc;
+  const bool c_tma = g_gemm_tma_c && !has_d &&
+                     make_tmap_c(&tc, C.data_ptr(), out_f32, N, M, batch, C.stride(-2), batched ? C.stride(0) : 0);
+  // split-K for the fp32-accumulating GEMMs (weight gradients): partial tiles reduce-add into C (atomic in L2), so
+  // the 2-CTA kernel's work units can fill the 74 CTA pairs in near-whole waves (one wave of 64 tiles uses 86 % of
+  // them, 176 tiles over 3 waves 79 %)
+  const int splitk = (out_f32 && accumulate && c_tma && g_gemm_splitk && g_gemm_pair_enabled && M >= 256 &&
+                      N >= 256) ? choose_splitk(pair_tiles, K) : 1;
+  const bool use_pair = g_gemm_pair_enabled && M >= 256 && N >= 256 && (pair_tiles >= num_sms() / 2 || splitk > 1);
   const int bn = use_pair ? 0 : (N <= 128 ? 128 : 256);
   const uint64_t bsA = batched ? A.stride(0) : 0, bsB = batched ? B.stride(0) : 0;
   CUtensorMap ta = make_tmap_bf16_sw128(A.data_ptr(), A.size(-1), A.size(-2), batch, A.stride(-2), bsA,
@@ -180,7 +208,7 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor C, bool a_mn, bool b_mn, c10::o
   p.D = nullptr;
   p.ldd = 0;
   p.bsd = 0;
-  if (D.has_value() && D->defined()) {
+  if (has_d) {
     TORCH_CHECK(!out_f32 && D->scalar_type() == at::kBFloat16 && D->stride(-1) == 1, "gemm: D must be bf16");
     TORCH_CHECK(D->dim() == C.dim() && D->size(-2) == M && D->size(-1) == N, "gemm: D shape mismatch");
     TORCH_CHECK(D->stride(-2) % 8 == 0 && reinterpret_cast<uintptr_t>(D->data_ptr()) % 16 == 0, "gemm: D align");
@@ -188,14 +216,12 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor C, bool a_mn, bool b_mn, c10::o
     p.ldd = D->stride(-2);
     p.bsd = batched ? D->stride(0) : 0;
   }
-  TORCH_CHECK(p.ldc % 8 == 0 && reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0, "gemm: C alignment");
   p.alpha = (float)alpha;
   p.beta = (float)beta;
   p.err = err_ptr(err);
   const int epi = out_f32 ? (accumulate ? 2 : 1) : 0;
-  CUtensorMap tc;
-  p.c_tma = (g_gemm_tma_c && p.D == nullptr &&
-             make_tmap_c(&tc, C.data_ptr(), out_f32, N, M, batch, p.ldc, p.bsc)) ? 1 : 0;
+  p.c_tma = c_tma ? 1 : 0;
+  p.splitk = splitk;
   TGO_CHECK_LAUNCH(gemm_launch(ta, tb, p, bn, a_mn, b_mn, epi, at::cuda::getCurrentCUDAStream(),
                                p.c_tma ? &tc : nullptr));
 }
@@ -1178,6 +1204,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "GEMM epilogue through TMA stores / reduce-adds (default) or per-row global stores");
   m.def("set_qknorm_bwd_unroll", [](int64_t u) { TORCH_CHECK(tgo::qknorm_set_bwd_unroll((int)u) == cudaSuccess, "2 or 4"); },
         "q/k-norm + RoPE backward: heads in flight per lane group (A/B runs)");
+  m.def("set_gemm_splitk", &tgo::set_gemm_splitk, "enable / disable split-K of the fp32-accumulating GEMMs (A/B runs)");
   m.def("set_gemm_syrk", &tgo::set_gemm_syrk, "enable / disable the symmetric (lower-triangle) GEMM mode (A/B runs)");
   m.def("gemm_syrk", &tgo::gemm_syrk, "symmetric C = alpha A A^T + beta D: lower-triangle tiles, mirrored stores");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");

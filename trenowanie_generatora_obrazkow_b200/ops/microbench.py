@@ -278,6 +278,7 @@ def cases(small):
         "dgrad_qkv": lambda: gemm_case(M, D, 3 * D, b_mn=True),
         "wgrad_qkv": lambda: gemm_case(3 * D, D, M, a_mn=True, b_mn=True, accumulate=True),
         "wgrad_mlp_down": lambda: gemm_case(D, MLP, M, a_mn=True, b_mn=True, accumulate=True),
+        "wgrad_out": lambda: gemm_case(D, D, M, a_mn=True, b_mn=True, accumulate=True),
         "attn_fwd": lambda: attn_case(B, T, H, hd, False),
         "attn_bwd": lambda: attn_case(B, T, H, hd, True),
         "attn_fwd_4k": lambda: attn_case(4 if small else 16, 4096, H, hd, False),  # 1024 px sampling (CFG batch)
@@ -331,6 +332,7 @@ def main(argv=None):
     p.add_argument("--gemm-tma-epilogue", type=int, default=-1, help="1 / 0: force the 2-CTA GEMM's TMA epilogue "
                    "on / off (per-row global stores)")
     p.add_argument("--qknorm-bwd-unroll", type=int, default=0, help="2 / 4: q/k-norm backward heads in flight")
+    p.add_argument("--gemm-splitk", type=int, default=-1, help="1 / 0: split-K of the accumulating GEMMs on / off")
     p.add_argument("--attn-pingpong", default="", help="comma-separated 0 / 1: attention forward softmax groups "
                    "alternate their exponential phases; every op runs once per setting (and per --attn-emu)")
     p.add_argument("--attn-emu", default="", help="comma-separated settings of the attention forward's FMA-pipe "
@@ -343,6 +345,8 @@ def main(argv=None):
         ext().set_gemm_tma_epilogue(bool(a.gemm_tma_epilogue))
     if a.qknorm_bwd_unroll:
         ext().set_qknorm_bwd_unroll(a.qknorm_bwd_unroll)
+    if a.gemm_splitk >= 0:
+        ext().set_gemm_splitk(bool(a.gemm_splitk))
     peaks = measured_peaks()
     table = cases(a.small)
     names = list(table) if a.op == "all" else a.op.split(",")
