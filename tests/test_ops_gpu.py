@@ -295,3 +295,35 @@ def test_cross_attention_sampling_shape():
         ref = R.attention(q.float().view(B, T, heads, D // heads), k.view(B, L, heads, D // heads),
                           v.view(B, L, heads, D // heads), kv_len, (D // heads) ** -0.5).reshape(B, T, D)
     assert rel(o, ref) < 2e-2
+
+
+def test_ops_from_a_fresh_thread():
+    """A thread whose first CUDA work is this extension (an autograd worker thread whose first backward node is the
+    attention, a server thread): tensor-map kernels run there and match the main thread's results."""
+    import threading
+    from trenowanie_generatora_obrazkow_b200.ops._ext import err_buf, ext
+    torch.manual_seed(7)
+    B, T, H, hd = 2, 256, 4, 128
+    q, k, v, do = (torch.randn(B, T, H, hd, device="cuda").bfloat16() for _ in range(4))
+    a = torch.randn(512, 256, device="cuda").bfloat16()
+    w = torch.randn(384, 256, device="cuda").bfloat16()
+    err = err_buf(q.device)
+
+    def run():
+        o, lse = ext().attention_fwd(q, k, v, None, hd ** -0.5, None, err)
+        dq = torch.empty(q.shape, device="cuda", dtype=torch.float32)
+        dk, dv = torch.empty_like(k), torch.empty_like(v)
+        ext().attention_bwd(q, k, v, o, lse, do, None, hd ** -0.5, dq, dk, dv, err)
+        c = torch.empty(512, 384, device="cuda", dtype=torch.bfloat16)
+        ext().gemm(a, w, c, False, False, err=err)
+        torch.cuda.synchronize()
+        return [o, dq, dk, dv, c]
+
+    out = {}
+    t = threading.Thread(target=lambda: out.setdefault("thread", run()))
+    t.start()
+    t.join()
+    main = run()
+    assert "thread" in out and err.sum().item() == 0
+    for x, y in zip(out["thread"], main):
+        torch.testing.assert_close(x, y, rtol=0, atol=1e-3)

@@ -187,7 +187,9 @@ __device__ __forceinline__ FwdItem fwd_item(const AttnParams& p, int item, int n
 template <int HD, int EMU>
 __global__ void __launch_bounds__(THREADS, 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, AttnParams p, int* err, int pingpong) {
+                        const __grid_constant__ CUtensorMap tmV, AttnParams p, int* err, int flags) {
+  const int pingpong = flags & 1;
+  const bool poll_mma = (flags & 2) != 0, poll_sm = (flags & 4) != 0, poll_ld = (flags & 8) != 0;
   using L = FwdSmem<HD>;
   static_assert(sizeof(FwdBars) <= 512, "barrier block");
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int item = blockIdx.x; item < n_items && ok && !*abort_flag; item += gridDim.x) {
         const FwdItem w = fwd_item(p, item, n_qb);
         if (w.n_tiles == 0) continue;
-        if (items > 0 && !mbar_wait(&bars->q_empty, (items - 1) & 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+        if (items > 0 && !mbar_wait_mode(&bars->q_empty, (items - 1) & 1, err, ERR_MBAR_TIMEOUT_PRODUCER, poll_ld)) {
           ok = false;
           break;
         }
@@ -258,7 +260,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // K_j of global tile t goes to ring slot t % K_STAGES; within an item K runs one tile ahead of V
         auto load_k = [&](int t, int jj) -> bool {
           const int st = t % K_STAGES, ph = (t / K_STAGES) & 1;
-          if (!mbar_wait(&bars->k_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) return false;
+          if (!mbar_wait_mode(&bars->k_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER, poll_ld)) return false;
           mbar_expect_tx(&bars->k_full[st], L::KV_BYTES);
 #pragma unroll
           for (int blk = 0; blk < HD / 64; ++blk)
@@ -276,11 +278,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           const int st = gt % V_STAGES, ph = (gt / V_STAGES) & 1;
-          if (!mbar_wait(&bars->v_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+          if (!mbar_wait_mode(&bars->v_empty[st], ph ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER, poll_ld)) {
             ok = false;
             break;
           }
-          ATTN_TRACE(tr, 16, gt);
           mbar_expect_tx(&bars->v_full[st], L::KV_BYTES);
 #pragma unroll
           for (int blk = 0; blk < HD / 64; ++blk)
@@ -320,8 +321,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         const FwdItem w = fwd_item(p, item, n_qb);
         const int n = w.n_tiles;
         if (n == 0) continue;
-        ok = mbar_wait(&bars->q_full, items & 1, err, ERR_MBAR_TIMEOUT_MMA) &&
-             mbar_wait(&bars->k_full[gt % K_STAGES], (gt / K_STAGES) & 1, err, ERR_MBAR_TIMEOUT_MMA);
+        ok = mbar_wait_mode(&bars->q_full, items & 1, err, ERR_MBAR_TIMEOUT_MMA, poll_mma) &&
+             mbar_wait_mode(&bars->k_full[gt % K_STAGES], (gt / K_STAGES) & 1, err, ERR_MBAR_TIMEOUT_MMA, poll_mma);
         if (!ok) break;
         tc_fence_after();
         issue_s(0, gt, false);  // after the previous item's last P_0 V in tensor-pipe order (same TMEM columns)
@@ -331,19 +332,20 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int gj = gt + j;
           const int vs = gj % V_STAGES, vph = (gj / V_STAGES) & 1;
           const int kn = (gj + 1) % K_STAGES, knph = ((gj + 1) / K_STAGES) & 1;
-          if (!mbar_wait(&bars->v_full[vs], vph, err, ERR_MBAR_TIMEOUT_MMA)) {
+          if (!mbar_wait_mode(&bars->v_full[vs], vph, err, ERR_MBAR_TIMEOUT_MMA, poll_mma)) {
             ok = false;
             break;
           }
           const uint64_t vd = sdesc_add(v_desc0, vs * L::KV_BYTES);
 #pragma unroll
           for (int g = 0; g < NQ && ok; ++g) {
-            if (!mbar_wait(&bars->p_full[g], gj & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
+            if (!mbar_wait_mode(&bars->p_full[g], gj & 1, err, ERR_MBAR_TIMEOUT_MMA, poll_mma)) {
               ok = false;
               break;
             }
             // the first P V of an item overwrites O_g: the previous item's epilogue must have read it
-            if (j == 0 && items > 0 && !mbar_wait(&bars->o_free[g], (items - 1) & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
+            if (j == 0 && items > 0 &&
+                !mbar_wait_mode(&bars->o_free[g], (items - 1) & 1, err, ERR_MBAR_TIMEOUT_MMA, poll_mma)) {
               ok = false;
               break;
             }
@@ -356,7 +358,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             umma_commit(&bars->pv_done[g]);
             if (g == NQ - 1) umma_commit(&bars->v_empty[vs]);  // V_j read by both Q tiles
             if (j + 1 < n) {
-              if (g == 0 && !mbar_wait(&bars->k_full[kn], knph, err, ERR_MBAR_TIMEOUT_MMA)) {
+              if (g == 0 && !mbar_wait_mode(&bars->k_full[kn], knph, err, ERR_MBAR_TIMEOUT_MMA, poll_mma)) {
                 ok = false;
                 break;
               }
@@ -381,10 +383,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t o_base = tmem + lane_base + O_COL + g * HD;
     const float sl2 = p.scale * 1.4426950408889634f;
     const bool tw = tr && (threadIdx.x == 64 + g * 128);
+    const bool tw4 = tr && threadIdx.x == 128, tw5 = tr && threadIdx.x == 160;  // the other SMSPs' warps of tile 0
     bool ok = true;
     auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
       int w_ok = 1;
-      if (lane == 0) w_ok = mbar_wait(bar, parity, err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
+      if (lane == 0) w_ok = mbar_wait_mode(bar, parity, err, ERR_MBAR_TIMEOUT_EPILOGUE, poll_sm) ? 1 : 0;
       w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
       __syncwarp();
       return w_ok != 0;
@@ -500,6 +503,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (lane == 0) mbar_arrive(&bars->turn[1 - g]);
         }
         ATTN_TRACE(tw, 25 + 4 * g, gj);
+        ATTN_TRACE(tw5, 16, gj);
         // the other Q tile's P V may still read its A operand from TMEM: let it finish before any tcgen05.st here
         // (tile 0 waits for the P_1 V of the previous KV tile, tile 1 for the P_0 V of this one; the later P V of
         // that tile cannot start before this tile's P is written, so the barrier cannot be a phase ahead)
@@ -508,6 +512,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
+        ATTN_TRACE(tw, 17 + g, gj);
         tc_fence_after();
         if (__any_sync(0xffffffffu, rescale)) {
           // O_g is stable: P_g(j-1) V completed before S_g(j) (tensor-pipe order), P_g(j) V is not issued yet
@@ -528,6 +533,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_before();
         __syncwarp();
         ATTN_TRACE(tw, 26 + 4 * g, gj);
+        ATTN_TRACE(tw5, 19, gj);
+        ATTN_TRACE(tw4, 31, gj);
         if (lane == 0) mbar_arrive(&bars->p_full[g]);  // one arrival per warp, after its stores completed
       }
       if (!ok) break;
@@ -575,6 +582,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 static int g_fwd_pingpong = 0;  // softmax groups alternate their exponential phases
+// barrier waits that poll (test_wait) instead of suspending: bit 0 the MMA thread, bit 1 the softmax / drain
+// warps, bit 2 the TMA producer
+static int g_attn_poll_fwd = 3, g_attn_poll_bwd = 1;
 
 template <int HD, int EMU>
 static cudaError_t fwd_tc_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
@@ -590,7 +600,8 @@ static cudaError_t fwd_tc_impl(const CUtensorMap& tq, const CUtensorMap& tk, con
   if (items <= 0) return cudaSuccess;
   if (items >= (1ll << 31)) return cudaErrorInvalidValue;
   const int grid = (int)std::min<long long>(items, num_sms());
-  flash_fwd_tc_kernel<HD, EMU><<<grid, THREADS, L::TOTAL, s>>>(tq, tk, tv, p, err, g_fwd_pingpong);
+  flash_fwd_tc_kernel<HD, EMU><<<grid, THREADS, L::TOTAL, s>>>(tq, tk, tv, p, err,
+                                                                g_fwd_pingpong | (g_attn_poll_fwd << 1));
   return cudaGetLastError();
 }
 
@@ -688,9 +699,9 @@ struct BwdBars {
 __device__ __forceinline__ void softmax_group_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 __device__ __forceinline__ void drain_group_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code, bool poll) {
   int ok = 1;
-  if (lane_id() == 0) ok = mbar_wait(bar, parity, err, code) ? 1 : 0;
+  if (lane_id() == 0) ok = mbar_wait_mode(bar, parity, err, code, poll) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   __syncwarp();
   return ok != 0;
@@ -703,8 +714,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                         const __grid_constant__ CUtensorMap tmdQ, AttnParams p, const float* __restrict__ delta,
                         const float* __restrict__ lse2, __nv_bfloat16* __restrict__ dk, long long dk_bs, long long dk_ts, long long dk_hs,
-                        __nv_bfloat16* __restrict__ dv, long long dv_bs, long long dv_ts, long long dv_hs, int* err) {
+                        __nv_bfloat16* __restrict__ dv, long long dv_bs, long long dv_ts, long long dv_hs, int* err,
+                        int flags) {
   constexpr int HD = 128;
+  const bool poll_mma = (flags & 2) != 0, poll_sm = (flags & 4) != 0, poll_ld = (flags & 8) != 0;
   using L = BwdSmem;
   static_assert(L::TOTAL <= 232448, "shared memory");
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -767,7 +780,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       for (int i = 0; i < n_it && !*abort_flag; ++i) {
         const int st = i % QST;
         const int h = hk * p.rep + i / n_qt, q0 = (i % n_qt) * BQ;
-        if (!mbar_wait(&bars->q_empty[st], ((i / QST) & 1) ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+        if (!mbar_wait_mode(&bars->q_empty[st], ((i / QST) & 1) ^ 1, err, ERR_MBAR_TIMEOUT_PRODUCER, poll_ld)) {
           *abort_flag = 1;
           break;
         }
@@ -805,9 +818,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const uint64_t dS_mn = sdesc_sw128(smem_u32(smem + L::DS_OFF), 8192, 1024);   // dS^T as MN-major B (dQ^T)
       auto issue_s = [&](int i) -> bool {
         const int st = i % QST;
-        if (!mbar_wait(&bars->q_full[st], (i / QST) & 1, err, ERR_MBAR_TIMEOUT_MMA)) return false;
+        if (!mbar_wait_mode(&bars->q_full[st], (i / QST) & 1, err, ERR_MBAR_TIMEOUT_MMA, poll_mma)) return false;
         ATTN_TRACE(tr, 2, i);
-        if (i > 0 && !mbar_wait(&bars->s_empty, (i - 1) & 1, err, ERR_MBAR_TIMEOUT_MMA)) return false;
+        if (i > 0 && !mbar_wait_mode(&bars->s_empty, (i - 1) & 1, err, ERR_MBAR_TIMEOUT_MMA, poll_mma)) return false;
         ATTN_TRACE(tr, 3, i);
         tc_fence_after();
         const uint32_t so = st * 16384;
@@ -827,25 +840,21 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         ATTN_TRACE(tr, 4, i);
         return true;
       };
-      bool ok = mbar_wait(&bars->kv_full, 0, err, ERR_MBAR_TIMEOUT_MMA) && issue_s(0);
+      bool ok = mbar_wait_mode(&bars->kv_full, 0, err, ERR_MBAR_TIMEOUT_MMA, poll_mma) && issue_s(0);
       for (int i = 0; i < n_it && ok; ++i) {
         const int st = i % QST, pb = i & 1;
         if (i + 1 < n_it && !issue_s(i + 1)) {
           ok = false;
           break;
         }
-        if (!mbar_wait(&bars->p_full, i & 1, err, ERR_MBAR_TIMEOUT_MMA)) {
+        if (!mbar_wait_mode(&bars->p_full, i & 1, err, ERR_MBAR_TIMEOUT_MMA, poll_mma)) {
           ok = false;
           break;
         }
         ATTN_TRACE(tr, 5, i);
-        if (!mbar_wait(&bars->dq_empty, (i & 1) ^ 1, err, ERR_MBAR_TIMEOUT_MMA)) {
-          ok = false;
-          break;
-        }
-        ATTN_TRACE(tr, 6, i);
         tc_fence_after();
         const uint32_t so = st * 16384, dso = pb * 16384;
+        // dV and dK need only this iteration's P^T / dS^T: they run while the dQ drain may still read dQ^T(i-1)
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)  // dV += P^T dO, P^T read from TMEM (8 columns per 16 queries)
           umma_f16_tmem_a(tmem + 256, tmem + 192 + pb * 32 + kk * 8, sdesc_add(dO_mn, so + kk * 2048), id_kv,
@@ -854,6 +863,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         for (int kk = 0; kk < BQ / 16; ++kk)  // dK += dS^T Q
           umma_f16(tmem + 384, sdesc_add(dS_km, dso + kk * 32), sdesc_add(dQ_mn, so + kk * 2048), id_kv,
                    (i > 0 || kk > 0) ? 1u : 0u);
+        if (!mbar_wait_mode(&bars->dq_empty, (i & 1) ^ 1, err, ERR_MBAR_TIMEOUT_MMA, poll_mma)) {
+          ok = false;
+          break;
+        }
+        ATTN_TRACE(tr, 6, i);
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BK_KEYS / 16; ++kk)  // dQ^T = K^T dS^T
           umma_f16(tmem + 128, sdesc_add(dK_mn, kk * 2048), sdesc_add(dS_mn, dso + kk * 2048), id_q,
@@ -891,7 +906,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         }
         softmax_group_sync();
       } else {
-        if (!warp_wait(&bars->q_full[st], (i / QST) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE)) {
+        if (!warp_wait(&bars->q_full[st], (i / QST) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE, poll_sm)) {
           ok = false;  // the bulk-copied rows of this stage have landed
           break;
         }
@@ -904,7 +919,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         }
       }
       ATTN_TRACE(tw, 8, i);
-      if (!warp_wait(&bars->s_full, i & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE)) {
+      if (!warp_wait(&bars->s_full, i & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE, poll_sm)) {
         ok = false;
         break;
       }
@@ -935,7 +950,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         for (int e = 0; e < 16; ++e) pk[e] = dk4[e] = 0u;
       }
       // MMA3-5 of iteration i-1 must be done: they read this dS^T buffer's other use and the P^T TMEM lanes
-      if (i > 0 && !warp_wait(&bars->mma_done, (i - 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE)) {
+      if (i > 0 && !warp_wait(&bars->mma_done, (i - 1) & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE, poll_sm)) {
         ok = false;
         break;
       }
@@ -955,7 +970,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       ATTN_TRACE(tw, 12, i);
       mbar_arrive(&bars->p_full);
     }
-    if (ok && n_it > 0) ok = warp_wait(&bars->acc_done, 0, err, ERR_MBAR_TIMEOUT_EPILOGUE);
+    if (ok && n_it > 0) ok = warp_wait(&bars->acc_done, 0, err, ERR_MBAR_TIMEOUT_EPILOGUE, poll_sm);
     tc_fence_after();
     const int key = k0 + r;
     if (ok) {
@@ -997,7 +1012,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     float* stage = reinterpret_cast<float*>(smem + L::DQ_OFF);  // [2 halves][32 queries][128]
     for (int i = 0; i < n_it; ++i) {
       const int h = hk * p.rep + i / n_qt, q0 = (i % n_qt) * BQ;
-      if (!warp_wait(&bars->dq_full, i & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE)) {
+      if (!warp_wait(&bars->dq_full, i & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE, poll_sm)) {
         *abort_flag = 1;
         break;
       }
@@ -1037,6 +1052,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   }
 }
 
+cudaError_t attention_set_poll(int fwd_mask, int bwd_mask) {
+  if (fwd_mask < 0 || fwd_mask > 7 || bwd_mask < 0 || bwd_mask > 7) return cudaErrorInvalidValue;
+  g_attn_poll_fwd = fwd_mask;
+  g_attn_poll_bwd = bwd_mask;
+  return cudaSuccess;
+}
+
 cudaError_t attention_set_trace(long long* buf, int cta) {
   TraceCfg t{buf, cta};
   return cudaMemcpyToSymbol(g_attn_trace, &t, sizeof(t));
@@ -1056,7 +1078,8 @@ cudaError_t attention_bwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk
   }
   dim3 grid((p.Tk + BK_KEYS - 1) / BK_KEYS, p.Hkv, p.B);
   flash_bwd_tc_kernel<<<grid, BWD_THREADS, BwdSmem::TOTAL, s>>>(tq, tk, tv, tdo, tdq, p, delta, lse2, dk, dk_bs,
-                                                               dk_ts, dk_hs, dv, dv_bs, dv_ts, dv_hs, err);
+                                                               dk_ts, dk_hs, dv, dv_bs, dv_ts, dv_hs, err,
+                                                               g_attn_poll_bwd << 1);
   return cudaGetLastError();
 }
 

@@ -67,6 +67,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   record_error(err, code);
   return false;
 }
+// Non-suspending probe of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait that polls with test_wait instead of letting try_wait suspend the thread (each poll is short, so the
+// bound is a larger poll count: about a second).
+constexpr uint32_t kPollLimit = 1u << 26;
+__device__ __forceinline__ bool mbar_wait_poll(uint64_t* bar, uint32_t parity, int* err, int code) {
+  for (uint32_t i = 0; i < kPollLimit; ++i) {
+    if (mbar_test_wait(bar, parity)) return true;
+  }
+  record_error(err, code);
+  return false;
+}
+__device__ __forceinline__ bool mbar_wait_mode(uint64_t* bar, uint32_t parity, int* err, int code, bool poll) {
+  return poll ? mbar_wait_poll(bar, parity, err, code) : mbar_wait(bar, parity, err, code);
+}
 
 // ---------------------------------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), plain tiled loads into this CTA's shared memory.  No cluster multicast anywhere.

@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+          if (!mbar_wait_mode(&empty_bar[stage], phase ^ 1, p.err, ERR_MBAR_TIMEOUT_PRODUCER, (p.poll & 4) != 0)) {
             abort_sh = 1;
             break;
           }
@@ -398,7 +398,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int tile = blockIdx.x; tile < num_tiles && !abort_sh; tile += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, p.err, ERR_MBAR_TIMEOUT_MMA)) {
+        if (!mbar_wait_mode(&tempty_bar[acc], acc_phase ^ 1, p.err, ERR_MBAR_TIMEOUT_MMA, (p.poll & 1) != 0)) {
           abort_sh = 1;
           break;
         }
@@ -406,7 +406,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, p.err, ERR_MBAR_TIMEOUT_MMA)) {
+          if (!mbar_wait_mode(&full_bar[stage], phase, p.err, ERR_MBAR_TIMEOUT_MMA, (p.poll & 1) != 0)) {
             abort_sh = 1;
             ok = false;
             break;
@@ -435,7 +435,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(&tfull_bar[acc], acc_phase, p.err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
+      if (lane == 0)
+        ok = mbar_wait_mode(&tfull_bar[acc], acc_phase, p.err, ERR_MBAR_TIMEOUT_EPILOGUE, (p.poll & 2) != 0) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         abort_sh = 1;
@@ -609,7 +610,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         kb_range(tile % tiles_per_batch, kb0, kb1);
         const int m0 = mt * 256 + rank * 128, n0 = nt * G2_BN + rank * 128;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.err, ERR_MBAR_TIMEOUT_PRODUCER)) {
+          if (!mbar_wait_mode(&empty_bar[stage], phase ^ 1, p.err, ERR_MBAR_TIMEOUT_PRODUCER, (p.poll & 4) != 0)) {
             abort_sh = 1;
             break;
           }
@@ -651,7 +652,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       for (int tile = cluster; tile < num_tiles && !abort_sh; tile += n_clusters, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, p.err, ERR_MBAR_TIMEOUT_MMA)) {
+        if (!mbar_wait_mode(&tempty_bar[acc], acc_phase ^ 1, p.err, ERR_MBAR_TIMEOUT_MMA, (p.poll & 1) != 0)) {
           abort_sh = 1;
           break;
         }
@@ -661,7 +662,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         int kb0, kb1;
         kb_range(tile % tiles_per_batch, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, p.err, ERR_MBAR_TIMEOUT_MMA)) {
+          if (!mbar_wait_mode(&full_bar[stage], phase, p.err, ERR_MBAR_TIMEOUT_MMA, (p.poll & 1) != 0)) {
             abort_sh = 1;
             ok = false;
             break;
@@ -709,7 +710,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(&tfull_bar[acc], acc_phase, p.err, ERR_MBAR_TIMEOUT_EPILOGUE) ? 1 : 0;
+      if (lane == 0)
+        ok = mbar_wait_mode(&tfull_bar[acc], acc_phase, p.err, ERR_MBAR_TIMEOUT_EPILOGUE, (p.poll & 2) != 0) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         abort_sh = 1;
@@ -793,6 +795,18 @@ int num_sms() {
   return n;
 }
 
+static int g_gemm_poll = 0;
+cudaError_t gemm_set_poll(int mask) {
+  if (mask < 0 || mask > 7) return cudaErrorInvalidValue;
+  g_gemm_poll = mask;
+  return cudaSuccess;
+}
+static GemmParams with_poll(const GemmParams& p) {
+  GemmParams q = p;
+  q.poll = g_gemm_poll;
+  return q;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream,
                                const CUtensorMap* tc = nullptr) {
@@ -806,7 +820,7 @@ static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, con
   }
   const int num_tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * ((p.N + BN - 1) / BN) * p.batch;
   const int grid = std::max(1, std::min(num_tiles, num_sms()));
-  kern<<<grid, GEMM_THREADS, Cfg::SMEM, stream>>>(ta, tb, tc != nullptr ? *tc : ta, p);
+  kern<<<grid, GEMM_THREADS, Cfg::SMEM, stream>>>(ta, tb, tc != nullptr ? *tc : ta, with_poll(p));
   return cudaGetLastError();
 }
 
@@ -834,7 +848,7 @@ static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb
   const int splits = (EPI == EPI_F32_ACC && p.splitk > 1) ? p.splitk : 1;
   const int num_tiles = (p.syrk ? nm * (nm + 1) / 2 : nm * ((p.N + G2_BN - 1) / G2_BN)) * p.batch * splits;
   const int grid = std::max(2, std::min(2 * num_tiles, (num_sms() / 2) * 2));
-  kern<<<grid, GEMM_THREADS, G2_SMEM, stream>>>(ta, tb, tc != nullptr ? *tc : ta, p);
+  kern<<<grid, GEMM_THREADS, G2_SMEM, stream>>>(ta, tb, tc != nullptr ? *tc : ta, with_poll(p));
   return cudaGetLastError();
 }
 
@@ -860,7 +874,7 @@ static cudaError_t launch_gemm_peer(const CUtensorMap& ta, const CUtensorMap& tb
     set = true;
   }
   const int tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * ((p.N + 255) / 256) * p.batch;
-  kern<<<std::min(tiles, num_sms()), GEMM_THREADS, Cfg::SMEM, s>>>(ta, tb, ta, p);
+  kern<<<std::min(tiles, num_sms()), GEMM_THREADS, Cfg::SMEM, s>>>(ta, tb, ta, with_poll(p));
   return cudaGetLastError();
 }
 
@@ -879,7 +893,7 @@ cudaError_t gemm_grouped_launch(const CUtensorMap& ta, const CUtensorMap& tb, co
   // the tile count is known on the device only: a persistent grid, bounded by the worst case
   const long long worst = ((long long)(p.M + GEMM_BM - 1) / GEMM_BM + p.batch) * ((p.N + 255) / 256);
   const int grid = (int)std::max(1LL, std::min<long long>(worst, num_sms()));
-  kern<<<grid, GEMM_THREADS, Cfg::SMEM, s>>>(ta, tb, ta, p);
+  kern<<<grid, GEMM_THREADS, Cfg::SMEM, s>>>(ta, tb, ta, with_poll(p));
   return cudaGetLastError();
 }
 

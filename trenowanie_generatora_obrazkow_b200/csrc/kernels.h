@@ -51,8 +51,12 @@ struct GemmParams {
   // split-K (2-CTA kernel, fp32 accumulate through the TMA reduce-add epilogue only): each output tile is computed
   // as `splitk` partial products over consecutive K ranges, all reduce-added into C (atomic in L2)
   int splitk;
+  // barrier waits that poll (test_wait) instead of suspending: bit 0 the MMA thread, bit 1 the epilogue, bit 2 the
+  // TMA producer (set by the launchers from gemm_set_poll)
+  int poll;
 };
 constexpr int kMaxGroups = 256;
+cudaError_t gemm_set_poll(int mask);
 // epi: 0 = bf16 store, 1 = fp32 store, 2 = fp32 accumulate (C += alpha * A B^T)
 // tc: tensor map of C ({N, M, batch}, box {32, 32, 1}; bf16 with 64-byte or fp32 with 128-byte swizzle) for the
 // TMA epilogue when p.c_tma is set (not for the SwiGLU epilogue of the 1-CTA kernel).
@@ -301,6 +305,8 @@ cudaError_t moe_release_launch(uint32_t* const* free_peer, int rank, int world, 
 cudaError_t attention_set_trace(long long* buf, int cta);  // profiling timeline (null: off)
 cudaError_t attention_set_fwd_split(int wpq);  // softmax warps per TMEM lane quarter in the forward (1 or 2)
 cudaError_t attention_set_fwd_emu(int eighths);
+// attention barrier waits that poll instead of suspending, per kernel: bit 0 MMA thread, 1 softmax / drain, 2 TMA
+cudaError_t attention_set_poll(int fwd_mask, int bwd_mask);
 cudaError_t attention_set_fwd_pingpong(int on);  // forward softmax groups alternate their exponential phases  // forward exponentials on the FMA pipe: 0, 2, 3 or 4 eighths
 cudaError_t muon_rs_launch(const MuonRSParams& p, int blocks, cudaStream_t s);
 cudaError_t muon_seg_momentum_launch(const MuonSegMomentumParams& p, int blocks, cudaStream_t s);

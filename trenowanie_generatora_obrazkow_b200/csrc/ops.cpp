@@ -23,7 +23,21 @@ long long launch_count() { return g_launches.load(); }
   } while (0)
 #define TGO_CHECK_LAUNCH(expr) TGO_CHECK_LAUNCH_N(expr, 1)
 
+// The driver's tensor-map encoder needs a current context. A thread whose first CUDA work is this extension (an
+// autograd worker thread whose first backward node is ours, a server thread) has none yet: the device guard is a
+// no-op when the thread's device index already matches, so cudaSetDevice binds the primary context here, once per
+// thread.
+static void bind_context() {
+  thread_local bool bound = false;
+  if (!bound) {
+    int dev = 0;
+    TORCH_CHECK(cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess, "cudaSetDevice failed");
+    bound = true;
+  }
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  bind_context();
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (fn == nullptr) {
     void* ptr = nullptr;
@@ -116,6 +130,10 @@ void set_attention_fwd_split(int64_t wpq) {
   TORCH_CHECK(attention_set_fwd_split((int)wpq) == cudaSuccess, "attention forward split: 1 or 2");
 }
 void set_attention_fwd_pingpong(bool on) { attention_set_fwd_pingpong(on ? 1 : 0); }
+void set_attention_poll(int64_t fwd_mask, int64_t bwd_mask) {
+  TORCH_CHECK(attention_set_poll((int)fwd_mask, (int)(bwd_mask < 0 ? fwd_mask : bwd_mask)) == cudaSuccess,
+              "set_attention_poll: masks 0..7");
+}
 void set_attention_fwd_emu(int64_t eighths) {
   TORCH_CHECK(attention_set_fwd_emu((int)eighths) == cudaSuccess, "attention forward FMA exponentials: 0, 2, 3, 4 (-1: default)");
 }
@@ -126,6 +144,7 @@ static bool g_gemm_syrk = true;  // symmetric mode of gemm_syrk (off: the full p
 void set_gemm_syrk(bool on) { g_gemm_syrk = on; }
 static bool g_gemm_splitk = true;  // split-K of the fp32-accumulating GEMMs (off: one unit per tile, for A/B runs)
 void set_gemm_splitk(bool on) { g_gemm_splitk = on; }
+void set_gemm_poll(int64_t mask) { TORCH_CHECK(gemm_set_poll((int)mask) == cudaSuccess, "set_gemm_poll: mask 0..7"); }
 
 // Smallest split count whose units fill the CTA pairs in waves at >= 92 % (at least 32 k-blocks of 64 per split,
 // at most 16 splits); every split non-empty (the count is derived from the k-blocks per split).
@@ -1193,6 +1212,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("muon_apply", &tgo::muon_apply, "Muon: parameter update + bf16 shadow refresh from the flat updates");
   m.def("grad_norm", &tgo::grad_norm, "global gradient norm and clip coefficient on the device (one launch)");
   m.def("adamw", &tgo::adamw, "multi-tensor AdamW with clip coefficient, bf16 shadow refresh and EMA fused in");
+  m.def("set_attention_poll", &tgo::set_attention_poll,
+        "attention barrier waits that poll instead of suspending, forward and backward masks (bit 0 MMA thread, "
+        "1 softmax / dQ drain, 2 TMA producer; defaults 3 and 1)",
+        py::arg("fwd_mask"), py::arg("bwd_mask") = -1);
   m.def("set_attention_fwd_pingpong", &tgo::set_attention_fwd_pingpong,
         "attention forward: the two softmax groups take turns for their exponential phases");
   m.def("set_attention_fwd_emu", &tgo::set_attention_fwd_emu,
@@ -1205,6 +1228,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_qknorm_bwd_unroll", [](int64_t u) { TORCH_CHECK(tgo::qknorm_set_bwd_unroll((int)u) == cudaSuccess, "2 or 4"); },
         "q/k-norm + RoPE backward: heads in flight per lane group (A/B runs)");
   m.def("set_gemm_splitk", &tgo::set_gemm_splitk, "enable / disable split-K of the fp32-accumulating GEMMs (A/B runs)");
+  m.def("set_gemm_poll", &tgo::set_gemm_poll,
+        "GEMM barrier waits poll instead of suspending (bit 0 MMA thread, 1 epilogue, 2 TMA producer)");
   m.def("set_gemm_syrk", &tgo::set_gemm_syrk, "enable / disable the symmetric (lower-triangle) GEMM mode (A/B runs)");
   m.def("gemm_syrk", &tgo::gemm_syrk, "symmetric C = alpha A A^T + beta D: lower-triangle tiles, mirrored stores");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");

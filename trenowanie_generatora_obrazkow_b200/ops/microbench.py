@@ -337,6 +337,11 @@ def main(argv=None):
                    "alternate their exponential phases; every op runs once per setting (and per --attn-emu)")
     p.add_argument("--attn-emu", default="", help="comma-separated settings of the attention forward's FMA-pipe "
                    "exponentials (eighths of the key pairs: 0, 2, 3, 4); every op runs once per setting")
+    p.add_argument("--attn-poll", default="", help="comma-separated masks (0..7) of attention barrier waits that "
+                   "poll instead of suspending (1 MMA thread, 2 softmax / dQ drain, 4 TMA producer); every op runs "
+                   "once per mask")
+    p.add_argument("--gemm-poll", default="", help="comma-separated masks (0..7) of GEMM barrier waits that poll "
+                   "(1 MMA thread, 2 epilogue, 4 TMA producer); every op runs once per mask")
     a = p.parse_args(argv)
     torch.manual_seed(0)
     if a.gemm_pair >= 0:
@@ -353,7 +358,13 @@ def main(argv=None):
     rows = []
     settings = [int(v) for v in a.attn_emu.split(",")] if a.attn_emu else [None]
     pps = [int(v) for v in a.attn_pingpong.split(",")] if a.attn_pingpong else [None]
-    for emu, pp in [(e, q) for q in pps for e in settings]:
+    polls = [int(v) for v in a.attn_poll.split(",")] if a.attn_poll else [None]
+    gpolls = [int(v) for v in a.gemm_poll.split(",")] if a.gemm_poll else [None]
+    for emu, pp, poll, gpoll in [(e, q, w, g) for g in gpolls for w in polls for q in pps for e in settings]:
+        if gpoll is not None:
+            ext().set_gemm_poll(gpoll)
+        if poll is not None:
+            ext().set_attention_poll(poll)
         if emu is not None:
             ext().set_attention_fwd_emu(emu)
         if pp is not None:
@@ -365,6 +376,10 @@ def main(argv=None):
                 row["attn_emu"] = emu
             if pp is not None:
                 row["attn_pingpong"] = pp
+            if poll is not None:
+                row["attn_poll"] = poll
+            if gpoll is not None:
+                row["gemm_poll"] = gpoll
             from ._ext import check_errors
             check_errors()
             print(json.dumps(row), flush=True)
