@@ -120,3 +120,91 @@ def test_web_app_generates_png(tmp_path):
     r = client.post("/generate", json={"prompt": "a red fox", "steps": 2, "guidance": 3.0, "seed": 7, "res": 64})
     assert r.status_code == 200 and r.headers["x-seed"] == "7"
     assert Image.open(io.BytesIO(r.content)).size == (4, 4)
+
+
+def test_homeimg_loader_isolates_exports(tmp_path):
+    """homeimg_loader.py: every export is loaded through its own pipeline.py under its own module, the weights are
+    the export's, and the bare ``pipeline`` module name is restored afterwards (reference
+    tests/check_homeimg_loader.py)."""
+    import sys
+
+    import pytest
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from homeimg_loader import load_homeimg_pipeline
+
+    den_cfg = DenoiserConfig(dim=32, depth=1, heads=1, mlp_hidden=64, text_dim=32, latent_channels=16, latent_size=4)
+    te_cfg = TextEncoderConfig(vocab_size=64, dim=32, depth=1, heads=1, kv_heads=1, mlp_hidden=64, max_tokens=8)
+    sentinel = object()
+    sys.modules["pipeline"] = sentinel
+    try:
+        classes = set()
+        for i in range(3):
+            torch.manual_seed(i)
+            te, den = build_models(den_cfg, te_cfg)
+            ck = dict(den_config=asdict(den_cfg), te_config=asdict(te_cfg), te=te.state_dict(), den=den.state_dict(),
+                      ema=None, step=i, args=dict(t_shift=1.0))
+            ex = str(tmp_path / f"export{i}")
+            export_checkpoint(ck, ex)
+            pipe = load_homeimg_pipeline(ex, device="cpu")
+            assert sys.modules["pipeline"] is sentinel
+            assert type(pipe).__module__.startswith("_homeimg_export_")
+            classes.add(type(pipe))
+            for k, v in den.state_dict().items():
+                assert torch.equal(pipe.den.state_dict()[k], v)
+        assert len(classes) == 3
+        # the same export again: the same module (no second import)
+        assert type(load_homeimg_pipeline(str(tmp_path / "export0"), device="cpu")) in classes
+        with pytest.raises(ValueError):
+            load_homeimg_pipeline(str(tmp_path / "export0"), trust_remote_code=False)
+    finally:
+        sys.modules.pop("pipeline", None)
+
+
+def test_eval_suite_parts_resume_and_faces(tmp_path):
+    """eval_suite.py: the fixed-suite split into parts with manifests (dry run, refusal to mix settings, resume of an
+    identical manifest) and the faces grid over two exports (reference tests/homeimg22.py, face_sweep.py)."""
+    import json
+    import sys
+
+    import pytest
+    from PIL import Image
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import eval_suite as E
+
+    den_cfg = DenoiserConfig(dim=32, depth=1, heads=1, mlp_hidden=64, text_dim=32, latent_channels=16, latent_size=4)
+    te_cfg = TextEncoderConfig(vocab_size=64, dim=32, depth=1, heads=1, kv_heads=1, mlp_hidden=64, max_tokens=12)
+    tok = str(tmp_path / "tokenizer.json")
+    _tokenizer(tok)
+    exports = []
+    for i in range(2):
+        torch.manual_seed(i)
+        te, den = build_models(den_cfg, te_cfg)
+        ck = dict(den_config=asdict(den_cfg), te_config=asdict(te_cfg), te=te.state_dict(), den=den.state_dict(),
+                  ema=None, step=i, args=dict(t_shift=1.0))
+        exports.append(str(tmp_path / f"ex{i}"))
+        export_checkpoint(ck, exports[-1], tokenizer_json=tok)
+    prompts = str(tmp_path / "prompts.json")
+    json.dump(["a red fox", "blue sky", "snow over hills"], open(prompts, "w"))
+    settings = str(tmp_path / "settings.json")
+    json.dump(dict(resolution=64, guidance_scale=3.0, time_shift=2.0, num_inference_steps=2, seeds=[0, 1]),
+              open(settings, "w"))
+    out = str(tmp_path / "suite")
+    base = ["suite", exports[0], "--prompts", prompts, "--settings", settings, "--out-dir", out, "--device", "cpu"]
+    m = E.main(base + ["--dry-run", "--parts", "2"])
+    assert [j["file"] for j in m["images"]] == ["prompt_01_seed_0.png", "prompt_02_seed_0.png", "prompt_03_seed_0.png"]
+    for part in (0, 1):
+        E.main(base + ["--parts", "2", "--part", str(part)])
+    files = sorted(f for f in os.listdir(out) if f.endswith(".png"))
+    assert len(files) == 6 and Image.open(os.path.join(out, files[0])).size == (64, 64)
+    with pytest.raises(SystemExit):  # the same part again without --resume
+        E.main(base + ["--parts", "2", "--part", "0"])
+    os.remove(os.path.join(out, "prompt_01_seed_0.png"))
+    E.main(base + ["--parts", "2", "--part", "0", "--resume"])  # regenerates only the missing image
+    assert os.path.exists(os.path.join(out, "prompt_01_seed_0.png"))
+    with pytest.raises(SystemExit):  # another split into the same directory
+        E.main(base + ["--parts", "3", "--part", "0"])
+    paths = E.main(["faces", f"{exports[0]}:3", f"{exports[1]}:1", "--prompts", prompts, "--seeds", "0", "--res",
+                    "64", "--steps", "2", "--cell", "32", "--out-dir", str(tmp_path / "faces"), "--device", "cpu"])
+    assert Image.open(paths[0]).size == (220 + 3 * 32, 2 * 32)

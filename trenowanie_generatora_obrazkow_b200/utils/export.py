@@ -9,6 +9,7 @@ Behaviour of the reference (export.py:28-161, import_homeimg.py:18-67, homeimg_l
     text_encoder/config.json              the text encoder / refiner config (+ "kind")
     text_encoder/diffusion_pytorch_model.safetensors
     scheduler/scheduler_config.json       Euler flow-matching schedule: shift, shift_ref, steps
+    pipeline.py                           the classes model_index.json names (loaded by homeimg_loader.py)
     tokenizer/                            copied when a local tokenizer.json is given
     vae/                                  copied when a local FLUX.2 VAE directory is given
 
@@ -26,6 +27,25 @@ from dataclasses import asdict
 import torch
 
 PIPELINE_CLASS = "HomeIMGPipeline"
+
+# The export's own code module: model_index.json names its components as ("pipeline", class), so the directory
+# carries a pipeline.py defining them. Here they are this framework's classes under the exported names; the loader
+# (homeimg_loader.py) imports the file under a name unique to the export.
+PIPELINE_SOURCE = '''"""Code of a HomeIMG export: the classes that model_index.json names, provided by the
+trenowanie_generatora_obrazkow_b200 package."""
+from trenowanie_generatora_obrazkow_b200.models.dit import Denoiser as AuroraDenoiser
+from trenowanie_generatora_obrazkow_b200.models.text import LMTextEncoder as AuroraLMTextEncoder
+from trenowanie_generatora_obrazkow_b200.models.text import TextEncoder as AuroraTextEncoder
+from trenowanie_generatora_obrazkow_b200.sampling.pipeline import HomeIMGPipeline as _Pipeline
+
+
+class EulerFlowMatch(dict):
+    """The Euler flow-matching schedule of scheduler/scheduler_config.json (shift, shift_ref)."""
+
+
+class HomeIMGPipeline(_Pipeline):
+    """Text -> image pipeline over this export directory (``HomeIMGPipeline.from_pretrained(root)``)."""
+'''
 
 
 def _write_json(path, obj):
@@ -75,6 +95,8 @@ def export_checkpoint(ck, out_dir, use_ema=True, time_shift=None, time_shift_ref
     if vae_dir:
         shutil.copytree(vae_dir, os.path.join(out_dir, "vae"), dirs_exist_ok=True)
         index["vae"] = ["diffusers", "AutoencoderKLFlux2"]
+    with open(os.path.join(out_dir, "pipeline.py"), "w") as f:
+        f.write(PIPELINE_SOURCE)
     _write_json(os.path.join(out_dir, "model_index.json"), index)
     return index
 
