@@ -193,3 +193,38 @@ def test_gemm_wgrad_split_k(M, N, K):
         outs.append(out)
         assert _rel(out, ref) < 1e-3
     assert _rel(outs[0], outs[1]) < 1e-4  # different fp32 summation order over K
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 520, 256), (1024, 768, 2048), (64, 256, 4096)])
+def test_gemm_i8_matches_integer_reference(M, N, K):
+    """tcgen05 kind::i8 GEMM: the int32 products are exact, so C equals the scaled integer product up to the bf16
+    rounding of the output (partial tiles at every edge in the first shape)."""
+    from trenowanie_generatora_obrazkow_b200.ops._ext import err_buf, ext
+    torch.manual_seed(0)
+    a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
+    sa = torch.rand(M, device="cuda") * 1e-3 + 1e-4
+    sb = torch.rand(N, device="cuda") * 1e-3 + 1e-4
+    c = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    err = err_buf(a.device)
+    ext().gemm_i8(a, b, c, sa, sb, err)
+    ref = (a.double() @ b.double().T) * sa.double()[:, None] * sb.double()[None, :]
+    assert err.sum().item() == 0
+    torch.testing.assert_close(c.double(), ref, rtol=8e-3, atol=1e-6)
+
+
+def test_quantize_rows_i8_and_w8a8_linear():
+    from trenowanie_generatora_obrazkow_b200.models.quant import W8A8Linear
+    from trenowanie_generatora_obrazkow_b200.ops._ext import ext
+    torch.manual_seed(1)
+    x = torch.randn(200, 1024, device="cuda").bfloat16()
+    q, s = ext().quantize_rows_i8(x)
+    want_s = x.float().abs().amax(1).clamp_min(1e-12) / 127
+    torch.testing.assert_close(s, want_s, rtol=1e-6, atol=0)
+    want_q = torch.round(x.float() / want_s[:, None]).clamp(-127, 127)
+    assert (q.float() - want_q).abs().max().item() <= 1 and (q.float() != want_q).float().mean().item() < 1e-3
+    lin = torch.nn.Linear(1024, 384).cuda()
+    qlin = W8A8Linear(lin).cuda()
+    y = qlin(x)
+    ref = lin(x.float())
+    assert y.dtype == torch.bfloat16 and ((y.float() - ref).norm() / ref.norm()).item() < 2e-2

@@ -174,6 +174,15 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn, b
          | ((uint32_t)(M >> 4) << 24);       // M / 16
 }
 
+// Signed int8 A and B, int32 accumulator (tcgen05.mma kind::i8), both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N) {
+  return (2u << 4)                           // D format: S32
+         | (1u << 7)                         // A format: signed 8-bit
+         | (1u << 10)                        // B format: signed 8-bit
+         | ((uint32_t)(N >> 3) << 17)        // N / 8
+         | ((uint32_t)(M >> 4) << 24);       // M / 16
+}
+
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version bits.
 //   K-major operand : rows of 128 B (64 bf16 of K), 8-row atoms of 1024 B -> SBO = 1024, LBO unused.
 //   MN-major operand: rows of 128 B (64 bf16 of M/N) per k, 8-k atoms of 1024 B -> SBO = 1024,
@@ -336,6 +345,16 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, u
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// int8 x int8 -> int32, K = 32 per instruction (32 bytes of each operand row, the same byte step as bf16's 16).
+__device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

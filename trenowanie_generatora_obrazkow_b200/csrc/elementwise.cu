@@ -84,4 +84,51 @@ cudaError_t fm_inputs_launch(const float* x0, const float* eps, const float* t, 
   return cudaGetLastError();
 }
 
+// Per-row symmetric int8 quantisation of activations (the W8A8 GEMM's A operand): scale = max |x| / 127 (at least
+// 1e-12), q = round-to-nearest-even(x / scale) clamped to [-127, 127]. One warp per row; the row is read twice, the
+// second time from L1 / L2. K must be a multiple of 8 (16-byte bf16 loads, 8-byte int8 stores).
+__global__ void __launch_bounds__(256) quantize_rows_i8_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restrict__ q,
+                                                               float* __restrict__ scale, int M, int K) {
+  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const __nv_bfloat16* src = x + row * K;
+  float amax = 0.f;
+  for (int c = lane * 8; c < K; c += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src + c);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float s = fmaxf(amax, 1e-12f) / 127.f;
+  const float inv = 1.f / s;
+  if (lane == 0) scale[row] = s;
+  int8_t* dst = q + row * K;
+  for (int c = lane * 8; c < K; c += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src + c);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      const int a = max(-127, min(127, __float2int_rn(f.x * inv)));
+      const int b = max(-127, min(127, __float2int_rn(f.y * inv)));
+      w[i >> 1] |= ((uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8)) << ((i & 1) * 16);
+    }
+    *reinterpret_cast<uint2*>(dst + c) = make_uint2(w[0], w[1]);
+  }
+}
+
+cudaError_t quantize_rows_i8_launch(const __nv_bfloat16* x, int8_t* q, float* scale, int M, int K, cudaStream_t s) {
+  if (M <= 0) return cudaSuccess;
+  if (K <= 0 || K % 8 != 0) return cudaErrorInvalidValue;
+  quantize_rows_i8_kernel<<<(M + 7) / 8, 256, 0, s>>>(x, q, scale, M, K);
+  return cudaGetLastError();
+}
+
 }  // namespace tgo

@@ -25,7 +25,8 @@ constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
 
-enum GemmEpi { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2, EPI_SWIGLU = 3 };
+// EPI_I8: int8 A and B (kind::i8 MMAs, int32 accumulators), bf16 C = acc * alpha * row_scale[m] * col_scale[n]
+enum GemmEpi { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2, EPI_SWIGLU = 3, EPI_I8 = 4 };
 enum GemmPeerMode { PEER_NONE = 0, PEER_WAIT_A = 1, PEER_SCATTER_C = 2, GROUPED = 3 };
 
 
@@ -174,6 +175,26 @@ __device__ __forceinline__ void gemm_stage_chunk(const GemmParams& p, int row, u
       f.w = __uint_as_float(r[j * 4 + 3]) * a;
       *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = f;
     }
+  }
+}
+// int8 GEMM: 32 int32 accumulators of one row -> scaled bf16, staged like EPI_BF16 (64-byte swizzled rows)
+__device__ __forceinline__ void gemm_stage_chunk_i8(const GemmParams& p, int row, int col0, uint8_t* buf, int lane,
+                                                    const uint32_t (&r)[32]) {
+  const float a = (p.row_scale != nullptr && row < p.M) ? p.alpha * p.row_scale[row] : p.alpha;
+  float f[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float cs = (p.col_scale != nullptr && col0 + j < p.N) ? p.col_scale[col0 + j] : 1.f;
+    f[j] = __int2float_rn((int)r[j]) * a * cs;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 u;
+    u.x = pack_bf16x2(f[j * 8 + 0], f[j * 8 + 1]);
+    u.y = pack_bf16x2(f[j * 8 + 2], f[j * 8 + 3]);
+    u.z = pack_bf16x2(f[j * 8 + 4], f[j * 8 + 5]);
+    u.w = pack_bf16x2(f[j * 8 + 6], f[j * 8 + 7]);
+    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = u;
   }
 }
 __device__ __forceinline__ void gemm_stage_swiglu(uint8_t* buf, int lane, const uint32_t (&gt)[32],
@@ -641,7 +662,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---------------- MMA issuer (leader CTA only) ----------------
-      constexpr uint32_t idesc = idesc_bf16_f32(256, G2_BN, A_MN, B_MN);
+      constexpr uint32_t idesc = EPI == EPI_I8 ? idesc_s8_s32(256, G2_BN) : idesc_bf16_f32(256, G2_BN, A_MN, B_MN);
       const uint64_t a_desc0 = A_MN ? sdesc_sw128(smem_u32(smem), 8192, 1024) : sdesc_sw128(smem_u32(smem), 16, 1024);
       const uint64_t b_desc0 = B_MN ? sdesc_sw128(smem_u32(smem) + G2_A_BYTES, 8192, 1024)
                                     : sdesc_sw128(smem_u32(smem) + G2_A_BYTES, 16, 1024);
@@ -672,7 +693,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
           const uint64_t bd = sdesc_add(b_desc0, stage * G2_STAGE_BYTES);
 #pragma unroll
           for (int k = 0; k < GEMM_BK / 16; ++k) {
-            umma_f16_pair(d_tmem, ad + k * A_KSTEP, bd + k * B_KSTEP, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            if constexpr (EPI == EPI_I8)
+              umma_i8_pair(d_tmem, ad + k * A_KSTEP, bd + k * B_KSTEP, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            else
+              umma_f16_pair(d_tmem, ad + k * A_KSTEP, bd + k * B_KSTEP, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit_pair_mc(&empty_bar[stage], 0x3);  // frees this stage in both CTAs
           if (++stage == G2_STAGES) {
@@ -761,10 +785,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
           uint32_t v[32];
           tmem_ld_32x32b_x32(tbase + c * 32, v);
           tmem_ld_wait();
-          if (tma_c)
+          if constexpr (EPI == EPI_I8) {  // TMA epilogue only (the launcher requires C's tensor map)
+            tma_chunk([&](uint8_t* buf) { gemm_stage_chunk_i8(p, row, n0 + c * 32, buf, lane, v); }, n0 + c * 32,
+                      m0 + q * 32, b);
+          } else if (tma_c) {
             tma_chunk([&](uint8_t* buf) { gemm_stage_chunk<EPI>(p, row, buf, lane, v); }, n0 + c * 32, m0 + q * 32, b);
-          else
+          } else {
             gemm_store_chunk<EPI>(p, b, row, n0 + c * 32, v);
+          }
         }
       }
       tc_fence_before();
@@ -922,6 +950,10 @@ cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
   if (p.syrk != 0 && (bn != 0 || epi != EPI_BF16 || p.c_tma == 0 || p.M != p.N)) return cudaErrorInvalidValue;
   // split-K partial tiles must reduce-add (atomic in L2): 2-CTA kernel, fp32 accumulate through the tensor map
   if (p.splitk > 1 && (bn != 0 || epi != EPI_F32_ACC || p.c_tma == 0 || p.syrk != 0)) return cudaErrorInvalidValue;
+  if (epi == EPI_I8) {  // int8 A [M, K] and B [N, K], both K-major; 2-CTA kernel with the TMA epilogue
+    if (a_mn || b_mn || bn != 0 || p.c_tma == 0 || p.syrk != 0 || p.splitk > 1) return cudaErrorInvalidValue;
+    return launch_gemm_pair<false, false, EPI_I8>(ta, tb, p, s, tc);
+  }
   if (epi == EPI_SWIGLU) {  // forward only (A and B K-major), 256-column tiles
     if (a_mn || b_mn || (bn != 0 && bn != 256) || p.N % 256 != 0) return cudaErrorInvalidValue;
     return bn == 0 ? launch_gemm_pair<false, false, EPI_SWIGLU>(ta, tb, p, s, tc)

@@ -44,6 +44,7 @@ struct GemmParams {
   // grouped mode (gemm_grouped_launch): A rows [offsets[g], offsets[g + 1]) use B batch g; C rows as A's
   const int* group_offsets;            // device [batch + 1], batch = groups (<= kMaxGroups)
   const float* row_scale;              // optional [M]: output row r scaled by row_scale[r]
+  const float* col_scale;              // int8 GEMM (EPI_I8): output column n scaled by col_scale[n]
   // symmetric product (2-CTA kernel, bf16 C through its tensor map, M == N, A and B the same operand): only the
   // 256-row tile blocks on or below the diagonal are computed; each off-diagonal tile is stored twice (as itself
   // and transposed). Valid when alpha A B^T + beta D is symmetric (D symmetric or absent).
@@ -105,6 +106,7 @@ struct AdaNormBwdParams {
   int M, D, T, chunks, rows_per_cta;
 };
 cudaError_t adanorm_fwd_launch(const AdaNormFwdParams& p, cudaStream_t s);
+cudaError_t adanorm_set_bwd_rows(int rows);  // rows per block reduction of the backward: 1 or 2 (default)
 cudaError_t adanorm_bwd_launch(const AdaNormBwdParams& p, float* dshift, float* dscale, float* dgate, float* dw,
                                cudaStream_t s);
 
@@ -183,6 +185,8 @@ cudaError_t attention_fwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk
 cudaError_t euler_cfg_launch(const __nv_bfloat16* out, float* z, int B, int T, int C, float dt, float w,
                              cudaStream_t s);
 // flow-matching input (bf16) and target (fp32), token-major [B, T, C], from fp32 x0 / eps [B, C, T] and t [B]
+// per-row int8 quantisation: q = round(x / scale), scale[m] = max |x[m, :]| / 127; K % 8 == 0
+cudaError_t quantize_rows_i8_launch(const __nv_bfloat16* x, int8_t* q, float* scale, int M, int K, cudaStream_t s);
 cudaError_t fm_inputs_launch(const float* x0, const float* eps, const float* t, __nv_bfloat16* z_tok, float* target,
                              int B, int T, int C, cudaStream_t s);
 

@@ -242,6 +242,16 @@ __device__ __forceinline__ float2 block_sum2(float a, float b, float* red, int s
   return make_float2(sa, sb);
 }
 
+__device__ __forceinline__ float block_sum1(float a, float* red, int slot) {
+  a = warp_sum(a);
+  const int nw = (blockDim.x + 31) >> 5;
+  if (lane_id() == 0) red[slot * 64 + warp_id()] = a;
+  __syncthreads();
+  float sa = 0.f;
+  for (int i = 0; i < nw; ++i) sa += red[slot * 64 + i];
+  return sa;
+}
+
 __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
@@ -252,6 +262,7 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
   }
 }
 
+template <int R>
 __global__ void __launch_bounds__(512) adanorm_bwd_kernel(AdaNormBwdParams p) {
   __shared__ float red[128];
   const int c0 = threadIdx.x * 8;
@@ -260,66 +271,96 @@ __global__ void __launch_bounds__(512) adanorm_bwd_kernel(AdaNormBwdParams p) {
   const int row0 = b * p.T + j * p.rows_per_cta;
   const int row1 = min((b + 1) * p.T, row0 + p.rows_per_cta);
   const bool has_dxe = p.dxe != nullptr, has_y = p.y != nullptr && p.gate != nullptr;
-  float w[8], sc1[8], g[8];
-  float a_shift[8], a_scale[8], a_gate[8], a_w[8];
+  // per channel: cw = (1 + scale) w, the gate g; the sums are dshift = sum dh, S = sum dh n (dscale = w S and
+  // dw = (1 + scale) S, formed at the end) and dgate = sum dx y
+  float cw[8], g[8];
+  float a_shift[8], a_s[8], a_gate[8];
+  auto channel_consts = [&](float (&w)[8], float (&sc1)[8]) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    w[i] = active ? p.w[c0 + i] : 0.f;
-    sc1[i] = 1.f;
-    g[i] = 1.f;
-    a_shift[i] = a_scale[i] = a_gate[i] = a_w[i] = 0.f;
-  }
-  if (active && p.scale != nullptr) {
-    load8(p.scale + (long long)b * p.mod_bs + c0, sc1);
+    for (int i = 0; i < 8; ++i) {
+      w[i] = active ? p.w[c0 + i] : 0.f;
+      sc1[i] = 1.f;
+    }
+    if (active && p.scale != nullptr) {
+      load8(p.scale + (long long)b * p.mod_bs + c0, sc1);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) sc1[i] += 1.f;
+      for (int i = 0; i < 8; ++i) sc1[i] += 1.f;
+    }
+  };
+  {
+    float w[8], sc1[8];
+    channel_consts(w, sc1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      cw[i] = sc1[i] * w[i];
+      g[i] = 1.f;
+      a_shift[i] = a_s[i] = a_gate[i] = 0.f;
+    }
   }
   if (active && p.gate != nullptr) load8(p.gate + (long long)b * p.gate_bs + c0, g);
   const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-  int slot = 0;
-  for (int row = row0; row < row1; row += 2, slot ^= 1) {
+  // R rows per block reduction; the next R rows' dh / x_new loads are issued before this group's reduction and
+  // stores, so loads stay in flight across the block barrier (without it every group waited for its loads with
+  // nothing else outstanding)
+  struct Pair {
+    uint4 dh[R], xn[R];
+    float r[R];
+  };
+  auto fetch = [&](int row, Pair& f) {
     const bool two = row + 1 < row1;
-    uint4 u_dh[2], u_xn[2], u_e[2], u_y[2];
-    float r[2];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {  // issue every load of both rows first
+    for (int k = 0; k < R; ++k) {
       const bool ok = active && (k == 0 || two);
       const long long off = (long long)(row + k) * p.D + c0;
-      u_dh[k] = ok ? *reinterpret_cast<const uint4*>(p.dh + off) : zero;
-      u_xn[k] = ok ? *reinterpret_cast<const uint4*>(p.xn + off) : zero;
+      f.dh[k] = ok ? *reinterpret_cast<const uint4*>(p.dh + off) : zero;
+      f.xn[k] = ok ? *reinterpret_cast<const uint4*>(p.xn + off) : zero;
+      f.r[k] = (k == 0 || two) ? p.rstd[row + k] : 0.f;
+    }
+  };
+  Pair cur;
+  if (row0 < row1) fetch(row0, cur);
+  int slot = 0;
+  for (int row = row0; row < row1; row += R, slot ^= 1) {
+    const bool two = R == 2 && row + 1 < row1;
+    const bool more = row + R < row1;
+    Pair nxt;
+    if (more) fetch(row + R, nxt);
+    uint4 u_e[R], u_y[R];  // needed only after the reduction: issued now, they arrive during it
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const bool ok = active && (k == 0 || two);
+      const long long off = (long long)(row + k) * p.D + c0;
       u_e[k] = (ok && has_dxe) ? *reinterpret_cast<const uint4*>(p.dxe + off) : zero;
       u_y[k] = (ok && has_y) ? *reinterpret_cast<const uint4*>(p.y + off) : zero;
-      r[k] = (k == 0 || two) ? p.rstd[row + k] : 0.f;
     }
     float dot[2] = {0.f, 0.f};
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < R; ++k) {
       float dh[8], xn[8];
-      unpack8(u_dh[k], dh);
-      unpack8(u_xn[k], xn);
+      unpack8(cur.dh[k], dh);
+      unpack8(cur.xn[k], xn);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float n = xn[i] * r[k];
-        const float du = dh[i] * sc1[i];
+        const float n = xn[i] * cur.r[k];
+        const float dn = dh[i] * n;
         a_shift[i] += dh[i];
-        a_scale[i] += dh[i] * n * w[i];
-        a_w[i] += du * n;
-        dot[k] += du * w[i] * n;
+        a_s[i] += dn;
+        dot[k] += dn * cw[i];
       }
     }
-    const float2 tot = block_sum2(dot[0], dot[1], red, slot);
+    const float2 tot = R == 2 ? block_sum2(dot[0], dot[1], red, slot) : make_float2(block_sum1(dot[0], red, slot), 0.f);
     const float mdot[2] = {tot.x / p.D, tot.y / p.D};
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < R; ++k) {
       if (!active || (k == 1 && !two)) continue;
       const long long off = (long long)(row + k) * p.D + c0;
       float dh[8], xn[8], dx[8];
-      unpack8(u_dh[k], dh);
-      unpack8(u_xn[k], xn);
+      unpack8(cur.dh[k], dh);
+      unpack8(cur.xn[k], xn);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float n = xn[i] * r[k];
-        dx[i] = r[k] * (dh[i] * sc1[i] * w[i] - n * mdot[k]);
+        const float n = xn[i] * cur.r[k];
+        dx[i] = cur.r[k] * (dh[i] * cw[i] - n * mdot[k]);
       }
       if (has_dxe) {
         float e[8];
@@ -339,15 +380,18 @@ __global__ void __launch_bounds__(512) adanorm_bwd_kernel(AdaNormBwdParams p) {
         store8(p.dy + off, dy);
       }
     }
+    if (more) cur = nxt;
   }
   if (active) {
+    float w[8], sc1[8];
+    channel_consts(w, sc1);
     float* dst = p.partial + ((long long)(b * p.chunks + j) * 4) * p.D + c0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       dst[i] = a_shift[i];
-      dst[p.D + i] = a_scale[i];
+      dst[p.D + i] = w[i] * a_s[i];
       dst[2 * p.D + i] = a_gate[i];
-      dst[3 * p.D + i] = a_w[i];
+      dst[3 * p.D + i] = sc1[i] * a_s[i];
     }
   }
 }
@@ -395,11 +439,21 @@ cudaError_t qknorm_set_bwd_unroll(int u) {
   return cudaSuccess;
 }
 
+// rows per block reduction: 2 (default; 128 registers with a few spilled to L1) measured 0.199 ms at 32 x 1024 x 2048
+// against 0.236 ms for 1 (116 registers, no spills) and 0.216-0.239 ms before the next pair's loads were issued early
+static int g_adanorm_bwd_rows = 2;
+cudaError_t adanorm_set_bwd_rows(int rows) {
+  if (rows != 1 && rows != 2) return cudaErrorInvalidValue;
+  g_adanorm_bwd_rows = rows;
+  return cudaSuccess;
+}
+
 cudaError_t adanorm_bwd_launch(const AdaNormBwdParams& p, float* dshift, float* dscale, float* dgate, float* dw,
                                cudaStream_t s) {
   const int threads = ((p.D / 8 + 31) / 32) * 32;
   dim3 grid(p.chunks, p.M / p.T);
-  adanorm_bwd_kernel<<<grid, threads, 0, s>>>(p);
+  if (g_adanorm_bwd_rows == 1) adanorm_bwd_kernel<1><<<grid, threads, 0, s>>>(p);
+  else adanorm_bwd_kernel<2><<<grid, threads, 0, s>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   adanorm_bwd_reduce_kernel<<<dim3((p.D + 127) / 128, p.M / p.T), 128, 0, s>>>(p.partial, dshift, dscale, dgate,

@@ -144,6 +144,9 @@ static bool g_gemm_syrk = true;  // symmetric mode of gemm_syrk (off: the full p
 void set_gemm_syrk(bool on) { g_gemm_syrk = on; }
 static bool g_gemm_splitk = true;  // split-K of the fp32-accumulating GEMMs (off: one unit per tile, for A/B runs)
 void set_gemm_splitk(bool on) { g_gemm_splitk = on; }
+void set_adanorm_bwd_rows(int64_t rows) {
+  TORCH_CHECK(adanorm_set_bwd_rows((int)rows) == cudaSuccess, "set_adanorm_bwd_rows: 1 or 2");
+}
 void set_gemm_poll(int64_t mask) { TORCH_CHECK(gemm_set_poll((int)mask) == cudaSuccess, "set_gemm_poll: mask 0..7"); }
 
 // Smallest split count whose units fill the CTA pairs in waves at >= 92 % (at least 32 k-blocks of 64 per split,
@@ -249,6 +252,57 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor C, bool a_mn, bool b_mn, c10::o
 // Symmetric product C = alpha A A^T + beta D (D symmetric or absent), A [batch,] M x K K-major, C / D [batch,] M x M
 // bf16: the 2-CTA kernel computes only the tile blocks on and below the diagonal and stores each off-diagonal block
 // twice (csrc/gemm.cu, GemmParams::syrk); shapes too small for the 2-CTA kernel run the full product.
+// int8 GEMM (W8A8): C[M, N] (bf16) = (A[M, K] int8 . B[N, K]^T int8, int32) * a_scale[m] * b_scale[n] on the 2-CTA
+// kind::i8 kernel. The int8 rows go through the bf16 data path as K / 2 bf16 pairs (the bytes TMA moves and the
+// shared-memory layout are identical; only the MMA kind and the epilogue differ).
+void gemm_i8(at::Tensor A, at::Tensor B, at::Tensor C, at::Tensor a_scale, at::Tensor b_scale, at::Tensor err) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm_i8: CUDA tensors");
+  TORCH_CHECK(A.scalar_type() == at::kChar && B.scalar_type() == at::kChar && C.scalar_type() == at::kBFloat16,
+              "gemm_i8: A, B int8, C bf16");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1 &&
+                  C.stride(1) == 1, "gemm_i8: 2-D with a contiguous inner dim");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K && C.size(0) == M && C.size(1) == N, "gemm_i8: shapes");
+  TORCH_CHECK(K % 16 == 0 && A.stride(0) % 16 == 0 && B.stride(0) % 16 == 0, "gemm_i8: K and row strides multiples of 16");
+  TORCH_CHECK(a_scale.scalar_type() == at::kFloat && a_scale.is_contiguous() && a_scale.numel() == M &&
+                  b_scale.scalar_type() == at::kFloat && b_scale.is_contiguous() && b_scale.numel() == N,
+              "gemm_i8: fp32 scales [M] and [N]");
+  const c10::cuda::CUDAGuard guard(A.device());
+  if (M == 0 || N == 0) return;
+  CUtensorMap ta = make_tmap_bf16_sw128(A.data_ptr(), K / 2, M, 1, A.stride(0) / 2, 0, 128);
+  CUtensorMap tb = make_tmap_bf16_sw128(B.data_ptr(), K / 2, N, 1, B.stride(0) / 2, 0, 128);
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)(K / 2);
+  p.batch = 1;
+  p.C = C.data_ptr();
+  p.ldc = C.stride(0);
+  p.alpha = 1.f;
+  p.row_scale = a_scale.data_ptr<float>();
+  p.col_scale = b_scale.data_ptr<float>();
+  p.err = err_ptr(err);
+  p.splitk = 1;
+  CUtensorMap tc;
+  TORCH_CHECK(make_tmap_c(&tc, C.data_ptr(), false, N, M, 1, p.ldc, 0), "gemm_i8: C must be 16-byte aligned");
+  p.c_tma = 1;
+  TGO_CHECK_LAUNCH(gemm_launch(ta, tb, p, 0, false, false, 4 /* EPI_I8 */, at::cuda::getCurrentCUDAStream(), &tc));
+}
+
+// Per-row int8 quantisation of bf16 activations: returns (q int8 [M, K], scale fp32 [M]).
+std::vector<at::Tensor> quantize_rows_i8(at::Tensor x) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.is_contiguous(),
+              "quantize_rows_i8: contiguous bf16 [M, K]");
+  TORCH_CHECK(x.size(1) % 8 == 0, "quantize_rows_i8: K must be a multiple of 8");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto q = at::empty(x.sizes(), x.options().dtype(at::kChar));
+  auto s = at::empty({x.size(0)}, x.options().dtype(at::kFloat));
+  const auto* xb = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  TGO_CHECK_LAUNCH(quantize_rows_i8_launch(xb, q.data_ptr<int8_t>(), s.data_ptr<float>(), (int)x.size(0), (int)x.size(1),
+                                           at::cuda::getCurrentCUDAStream()));
+  return {q, s};
+}
+
 void gemm_syrk(at::Tensor A, at::Tensor C, c10::optional<at::Tensor> D, double alpha, double beta, at::Tensor err) {
   TORCH_CHECK(A.is_cuda() && C.is_cuda() && A.scalar_type() == at::kBFloat16 && C.scalar_type() == at::kBFloat16,
               "gemm_syrk: bf16 CUDA tensors");
@@ -1228,8 +1282,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_qknorm_bwd_unroll", [](int64_t u) { TORCH_CHECK(tgo::qknorm_set_bwd_unroll((int)u) == cudaSuccess, "2 or 4"); },
         "q/k-norm + RoPE backward: heads in flight per lane group (A/B runs)");
   m.def("set_gemm_splitk", &tgo::set_gemm_splitk, "enable / disable split-K of the fp32-accumulating GEMMs (A/B runs)");
+  m.def("set_adanorm_bwd_rows", &tgo::set_adanorm_bwd_rows, "adanorm backward: rows per block reduction (1 or 2)");
   m.def("set_gemm_poll", &tgo::set_gemm_poll,
         "GEMM barrier waits poll instead of suspending (bit 0 MMA thread, 1 epilogue, 2 TMA producer)");
+  m.def("gemm_i8", &tgo::gemm_i8, "int8 W8A8 GEMM on tcgen05 kind::i8: C = (A B^T) * a_scale[m] * b_scale[n] (bf16)",
+        py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_scale"), py::arg("b_scale"), py::arg("err"));
+  m.def("quantize_rows_i8", &tgo::quantize_rows_i8, "per-row symmetric int8 quantisation of bf16 rows -> (q, scale)");
   m.def("set_gemm_syrk", &tgo::set_gemm_syrk, "enable / disable the symmetric (lower-triangle) GEMM mode (A/B runs)");
   m.def("gemm_syrk", &tgo::gemm_syrk, "symmetric C = alpha A A^T + beta D: lower-triangle tiles, mirrored stores");
   m.def("set_gemm_pair", &tgo::set_gemm_pair, "enable / disable the 2-CTA GEMM kernel (for A/B tests)");

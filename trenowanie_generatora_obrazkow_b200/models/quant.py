@@ -4,8 +4,10 @@
   int8 (max |w| / 127) or fp8 e4m3 (max |w| / 448, e4m3's largest normal value); dequantised to the activation dtype
   and multiplied with the framework's GEMM (``ops.fused.linear``: the tcgen05 kernel on CUDA). Halves the weight
   memory of a frozen teacher; the arithmetic stays bf16.
-* ``W8A8Linear``: per-output-channel int8 weights, dynamic per-token int8 activations, int32 accumulation
-  (``torch._int_mm``: a library int8 GEMM, used for the frozen teacher only; the training path never quantises).
+* ``W8A8Linear``: per-output-channel int8 weights, dynamic per-token int8 activations, int32 accumulation. On CUDA
+  the activations are quantised by one kernel and multiplied by the tcgen05 ``kind::i8`` GEMM with both scales
+  applied in its epilogue (``ext().quantize_rows_i8``, ``ext().gemm_i8``); elsewhere ``torch._int_mm``. Used for
+  frozen teachers only; the training path never quantises.
 * ``quantize(module, kind)``: replaces every ``nn.Linear`` below ``module`` in place (kind "int8", "fp8" or
   "w8a8"; w8a8 only where both feature counts are multiples of 8, as the int8 GEMM requires).
 """
@@ -54,6 +56,16 @@ class W8A8Linear(nn.Module):
         self.bias = lin.bias
 
     def forward(self, x):
+        k, n = self.weight_t.shape
+        if x.is_cuda and k % 16 == 0 and n % 8 == 0:
+            from ..ops._ext import err_buf, ext
+            rows = x.reshape(-1, k).to(torch.bfloat16).contiguous()
+            q, a_scale = ext().quantize_rows_i8(rows)
+            out = torch.empty(rows.shape[0], n, device=x.device, dtype=torch.bfloat16)
+            ext().gemm_i8(q, self.weight_t.T, out, a_scale, self.scale, err_buf(x.device))
+            if self.bias is not None:
+                out = out + self.bias.to(out.dtype)
+            return out.to(x.dtype).reshape(*x.shape[:-1], n)
         rows = x.reshape(-1, x.shape[-1]).float()
         a_scale = rows.abs().amax(1, keepdim=True).clamp_min(1e-12) / 127
         q = torch.round(rows / a_scale).clamp_(-127, 127).to(torch.int8)

@@ -90,6 +90,25 @@ def gemm_case(M, N, K, a_mn=False, b_mn=False, accumulate=False):
     return ours, lib, 2.0 * M * N * K, 2 * (M * K + N * K) + out.element_size() * M * N * (2 if accumulate else 1)
 
 
+def gemm_i8_case(M, N, K):
+    """W8A8: our kind::i8 GEMM with the scales in its epilogue vs torch._int_mm + the scaling (the reference's
+    teacher path); counted as 2 M N K integer operations."""
+    a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
+    sa, sb = torch.rand(M, device="cuda"), torch.rand(N, device="cuda")
+    c = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    err = err_buf(a.device)
+    bt = b.T
+
+    def ours():
+        ext().gemm_i8(a, b, c, sa, sb, err)
+
+    def lib():
+        (torch._int_mm(a, bt).float() * sa[:, None] * sb[None, :]).to(torch.bfloat16)
+
+    return ours, lib, 2.0 * M * N * K, M * K + N * K + 2 * M * N
+
+
 def attn_case(B, T, H, hd, backward, Tk=None):
     Tk = Tk or T
     q = _bf16(B, T, H, hd)
@@ -275,6 +294,7 @@ def cases(small):
         "gemm_out": lambda: gemm_case(M, D, D),
         "gemm_mlp_up": lambda: gemm_case(M, 2 * MLP, D),
         "gemm_mlp_down": lambda: gemm_case(M, D, MLP),
+        "gemm_i8": lambda: gemm_i8_case(M, 3 * D, D),  # W8A8 teacher projection (qkv shape)
         "dgrad_qkv": lambda: gemm_case(M, D, 3 * D, b_mn=True),
         "wgrad_qkv": lambda: gemm_case(3 * D, D, M, a_mn=True, b_mn=True, accumulate=True),
         "wgrad_mlp_down": lambda: gemm_case(D, MLP, M, a_mn=True, b_mn=True, accumulate=True),
@@ -342,6 +362,8 @@ def main(argv=None):
                    "once per mask")
     p.add_argument("--gemm-poll", default="", help="comma-separated masks (0..7) of GEMM barrier waits that poll "
                    "(1 MMA thread, 2 epilogue, 4 TMA producer); every op runs once per mask")
+    p.add_argument("--adanorm-bwd-rows", default="", help="comma-separated 1 / 2: adanorm backward rows per block "
+                   "reduction; every op runs once per setting")
     a = p.parse_args(argv)
     torch.manual_seed(0)
     if a.gemm_pair >= 0:
@@ -360,7 +382,11 @@ def main(argv=None):
     pps = [int(v) for v in a.attn_pingpong.split(",")] if a.attn_pingpong else [None]
     polls = [int(v) for v in a.attn_poll.split(",")] if a.attn_poll else [None]
     gpolls = [int(v) for v in a.gemm_poll.split(",")] if a.gemm_poll else [None]
-    for emu, pp, poll, gpoll in [(e, q, w, g) for g in gpolls for w in polls for q in pps for e in settings]:
+    arows = [int(v) for v in a.adanorm_bwd_rows.split(",")] if a.adanorm_bwd_rows else [None]
+    for emu, pp, poll, gpoll, arow in [(e, q, w, g, r) for r in arows for g in gpolls for w in polls for q in pps
+                                       for e in settings]:
+        if arow is not None:
+            ext().set_adanorm_bwd_rows(arow)
         if gpoll is not None:
             ext().set_gemm_poll(gpoll)
         if poll is not None:
@@ -380,6 +406,8 @@ def main(argv=None):
                 row["attn_poll"] = poll
             if gpoll is not None:
                 row["gemm_poll"] = gpoll
+            if arow is not None:
+                row["adanorm_bwd_rows"] = arow
             from ._ext import check_errors
             check_errors()
             print(json.dumps(row), flush=True)
