@@ -17,7 +17,7 @@ def _rel(x, y):
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 1024), (200, 136, 72), (1000, 384, 520), (64, 8, 8),
-                                   (4096, 2048, 2048), (8192, 6144, 2048)])
+                                   (4096, 2048, 2048), (8192, 6144, 2048), (8192, 2048, 520)])
 def test_gemm_layouts(a_mn, b_mn, M, N, K):
     from trenowanie_generatora_obrazkow_b200.ops.gemm import gemm
     from trenowanie_generatora_obrazkow_b200.ops._ext import check_errors
@@ -228,3 +228,24 @@ def test_quantize_rows_i8_and_w8a8_linear():
     y = qlin(x)
     ref = lin(x.float())
     assert y.dtype == torch.bfloat16 and ((y.float() - ref).norm() / ref.norm()).item() < 2e-2
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
+def test_gemm_tail_split_is_exact(a_mn, b_mn):
+    """The 2-CTA kernel's tail split (the last wave's 34 tiles of 8192 x 2048 as 68 half-width units) gives bitwise
+    the products of whole tiles: each output element sums the same K-products in the same order."""
+    from trenowanie_generatora_obrazkow_b200.ops._ext import ext
+    from trenowanie_generatora_obrazkow_b200.ops.gemm import gemm
+    torch.manual_seed(3)
+    M, N, K = 8192, 2048, 1024
+    a = torch.randn(*((K, M) if a_mn else (M, K)), device="cuda").bfloat16()
+    b = torch.randn(*((K, N) if b_mn else (N, K)), device="cuda").bfloat16()
+    try:
+        ext().set_gemm_tail_split(False)
+        whole = gemm(a, b, a_mn=a_mn, b_mn=b_mn)
+        ext().set_gemm_tail_split(True)
+        split = gemm(a, b, a_mn=a_mn, b_mn=b_mn)
+    finally:
+        ext().set_gemm_tail_split(True)
+    assert torch.equal(whole, split)
+    assert _rel(split, _ref(a, b, a_mn, b_mn)) < 1e-2
