@@ -232,8 +232,9 @@ def test_quantize_rows_i8_and_w8a8_linear():
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
 def test_gemm_tail_split_is_exact(a_mn, b_mn):
-    """The 2-CTA kernel's tail split (the last wave's 34 tiles of 8192 x 2048 as 68 half-width units) gives bitwise
-    the products of whole tiles: each output element sums the same K-products in the same order."""
+    """The 2-CTA kernel's tail split (an A/B switch, off by default; the last wave's 34 tiles of 8192 x 2048 as 68
+    half-width units) gives bitwise the products of whole tiles: each output element sums the same K-products in
+    the same order."""
     from trenowanie_generatora_obrazkow_b200.ops._ext import ext
     from trenowanie_generatora_obrazkow_b200.ops.gemm import gemm
     torch.manual_seed(3)
@@ -246,6 +247,6 @@ def test_gemm_tail_split_is_exact(a_mn, b_mn):
         ext().set_gemm_tail_split(True)
         split = gemm(a, b, a_mn=a_mn, b_mn=b_mn)
     finally:
-        ext().set_gemm_tail_split(True)
+        ext().set_gemm_tail_split(False)
     assert torch.equal(whole, split)
     assert _rel(split, _ref(a, b, a_mn, b_mn)) < 1e-2

@@ -594,6 +594,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     }
   };
 
+  // Tail split: the last p.tail_tiles tiles run as two 256 x 128 units each (half = 0 / 1), so a last wave that would
+  // keep at most half of the pairs busy for a whole tile takes about half a tile's time. Units are dealt out
+  // round-robin like the tiles; -1 marks a whole tile.
+  const int n_whole = num_tiles - p.tail_tiles;
+  const int num_units = num_tiles + p.tail_tiles;
+  auto unit_tile = [&](int u, int& tile, int& half) {
+    if (u < n_whole) {
+      tile = u;
+      half = -1;
+    } else {
+      tile = n_whole + (u - n_whole) / 2;
+      half = (u - n_whole) & 1;
+    }
+  };
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < G2_STAGES; ++s) {
       mbar_init(&full_bar[s], 1);   // leader only: one arrive.expect_tx for both CTAs' bytes
@@ -624,12 +639,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       // ---------------- TMA producer (both CTAs) ----------------
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = cluster; tile < num_tiles && !abort_sh; tile += n_clusters) {
+      for (int u = cluster; u < num_units && !abort_sh; u += n_clusters) {
+        int tile, half;
+        unit_tile(u, tile, half);
         const int b = tile / tiles_per_batch;
         int mt, nt, kb0, kb1;
         tile_mn(tile % tiles_per_batch, mt, nt);
         kb_range(tile % tiles_per_batch, kb0, kb1);
-        const int m0 = mt * 256 + rank * 128, n0 = nt * G2_BN + rank * 128;
+        // a half unit's CTA holds 64 columns of B: the 128-row box starting there brings 64 unused rows along
+        const int m0 = mt * 256 + rank * 128;
+        const int n0 = half < 0 ? nt * G2_BN + rank * 128 : nt * G2_BN + half * 128 + rank * 64;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_mode(&empty_bar[stage], phase ^ 1, p.err, ERR_MBAR_TIMEOUT_PRODUCER, (p.poll & 4) != 0)) {
             abort_sh = 1;
@@ -670,7 +689,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
-      for (int tile = cluster; tile < num_tiles && !abort_sh; tile += n_clusters, ++local) {
+      constexpr uint32_t idesc_half = EPI == EPI_I8 ? idesc_s8_s32(256, G2_BN / 2)
+                                                     : idesc_bf16_f32(256, G2_BN / 2, A_MN, B_MN);
+      for (int u = cluster; u < num_units && !abort_sh; u += n_clusters, ++local) {
+        int tile, half;
+        unit_tile(u, tile, half);
+        const uint32_t id = half < 0 ? idesc : idesc_half;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_mode(&tempty_bar[acc], acc_phase ^ 1, p.err, ERR_MBAR_TIMEOUT_MMA, (p.poll & 1) != 0)) {
@@ -694,9 +718,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < GEMM_BK / 16; ++k) {
             if constexpr (EPI == EPI_I8)
-              umma_i8_pair(d_tmem, ad + k * A_KSTEP, bd + k * B_KSTEP, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+              umma_i8_pair(d_tmem, ad + k * A_KSTEP, bd + k * B_KSTEP, id, (kb != kb0 || k != 0) ? 1u : 0u);
             else
-              umma_f16_pair(d_tmem, ad + k * A_KSTEP, bd + k * B_KSTEP, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+              umma_f16_pair(d_tmem, ad + k * A_KSTEP, bd + k * B_KSTEP, id, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit_pair_mc(&empty_bar[stage], 0x3);  // frees this stage in both CTAs
           if (++stage == G2_STAGES) {
@@ -730,7 +754,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       ++cbuf;
     };
     int local = 0;
-    for (int tile = cluster; tile < num_tiles; tile += n_clusters, ++local) {
+    for (int u = cluster; u < num_units; u += n_clusters, ++local) {
+      int tile, half;
+      unit_tile(u, tile, half);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       int ok = 1;
@@ -746,7 +772,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       const int b = tile / tiles_per_batch;
       int mt, nt;
       tile_mn(tile % tiles_per_batch, mt, nt);
-      const int m0 = mt * 256 + rank * 128, n0 = nt * G2_BN;
+      const int m0 = mt * 256 + rank * 128, n0 = nt * G2_BN + (half < 0 ? 0 : half * 128);
+      const int n_chunks = half < 0 ? G2_BN / 32 : G2_BN / 64;  // 32-column chunks of this unit
       const int row = m0 + q * 32 + lane;
       const uint32_t tbase = tmem_base + acc * G2_BN + ((uint32_t)(q * 32) << 16);
       if constexpr (EPI == EPI_BF16) {
@@ -781,7 +808,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < G2_BN / 32; ++c) {
+        for (int c = 0; c < n_chunks; ++c) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tbase + c * 32, v);
           tmem_ld_wait();
@@ -824,6 +851,14 @@ int num_sms() {
 }
 
 static int g_gemm_poll = 0;
+// Off by default: measured slower (8192 x 2048 x 2048 0.196 -> 0.235 ms, x 5504 0.506 -> 0.563 ms, qkv 0.576 ->
+// 0.656 ms): a half unit still loads a full 128-row B box per CTA and all of A, so the last wave is bound by L2 -> SM
+// traffic rather than by the tensor core, and takes about as long as a wave of whole tiles.
+static bool g_gemm_tail = false;
+cudaError_t gemm_set_tail_split(int on) {
+  g_gemm_tail = on != 0;
+  return cudaSuccess;
+}
 cudaError_t gemm_set_poll(int mask) {
   if (mask < 0 || mask > 7) return cudaErrorInvalidValue;
   g_gemm_poll = mask;
@@ -875,8 +910,17 @@ static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb
   const int nm = (p.M + 255) / 256;
   const int splits = (EPI == EPI_F32_ACC && p.splitk > 1) ? p.splitk : 1;
   const int num_tiles = (p.syrk ? nm * (nm + 1) / 2 : nm * ((p.N + G2_BN - 1) / G2_BN)) * p.batch * splits;
-  const int grid = std::max(2, std::min(2 * num_tiles, (num_sms() / 2) * 2));
-  kern<<<grid, GEMM_THREADS, G2_SMEM, stream>>>(ta, tb, tc != nullptr ? *tc : ta, with_poll(p));
+  const int pairs = num_sms() / 2;
+  // tail split: when the tiles of the last wave would occupy at most half of the pairs, they run as half-width units
+  GemmParams q = with_poll(p);
+  q.tail_tiles = 0;
+  if (g_gemm_tail && !p.syrk && splits == 1 && EPI != EPI_SWIGLU) {
+    const int left = num_tiles % pairs;
+    if (left > 0 && 2 * left <= pairs) q.tail_tiles = left;
+  }
+  const int units = num_tiles + q.tail_tiles;
+  const int grid = std::max(2, std::min(2 * units, pairs * 2));
+  kern<<<grid, GEMM_THREADS, G2_SMEM, stream>>>(ta, tb, tc != nullptr ? *tc : ta, q);
   return cudaGetLastError();
 }
 

@@ -55,7 +55,10 @@ struct GemmParams {
   // barrier waits that poll (test_wait) instead of suspending: bit 0 the MMA thread, bit 1 the epilogue, bit 2 the
   // TMA producer (set by the launchers from gemm_set_poll)
   int poll;
+  // 2-CTA kernel: how many of the last tiles run as two 256 x 128 halves (set by its launcher; 0 = none)
+  int tail_tiles;
 };
+cudaError_t gemm_set_tail_split(int on);
 constexpr int kMaxGroups = 256;
 cudaError_t gemm_set_poll(int mask);
 // epi: 0 = bf16 store, 1 = fp32 store, 2 = fp32 accumulate (C += alpha * A B^T)

@@ -147,6 +147,7 @@ void set_gemm_splitk(bool on) { g_gemm_splitk = on; }
 void set_adanorm_bwd_rows(int64_t rows) {
   TORCH_CHECK(adanorm_set_bwd_rows((int)rows) == cudaSuccess, "set_adanorm_bwd_rows: 1 or 2");
 }
+void set_gemm_tail_split(bool on) { gemm_set_tail_split(on ? 1 : 0); }
 void set_gemm_poll(int64_t mask) { TORCH_CHECK(gemm_set_poll((int)mask) == cudaSuccess, "set_gemm_poll: mask 0..7"); }
 
 // Smallest split count whose units fill the CTA pairs in waves at >= 92 % (at least 32 k-blocks of 64 per split,
@@ -1283,6 +1284,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "q/k-norm + RoPE backward: heads in flight per lane group (A/B runs)");
   m.def("set_gemm_splitk", &tgo::set_gemm_splitk, "enable / disable split-K of the fp32-accumulating GEMMs (A/B runs)");
   m.def("set_adanorm_bwd_rows", &tgo::set_adanorm_bwd_rows, "adanorm backward: rows per block reduction (1 or 2)");
+  m.def("set_gemm_tail_split", &tgo::set_gemm_tail_split,
+        "2-CTA GEMM: run a last wave that fills at most half of the SM pairs as half-width tiles (off by default: measured slower)");
   m.def("set_gemm_poll", &tgo::set_gemm_poll,
         "GEMM barrier waits poll instead of suspending (bit 0 MMA thread, 1 epilogue, 2 TMA producer)");
   m.def("gemm_i8", &tgo::gemm_i8, "int8 W8A8 GEMM on tcgen05 kind::i8: C = (A B^T) * a_scale[m] * b_scale[n] (bf16)",

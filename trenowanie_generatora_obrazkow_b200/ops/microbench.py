@@ -353,6 +353,8 @@ def main(argv=None):
                    "on / off (per-row global stores)")
     p.add_argument("--qknorm-bwd-unroll", type=int, default=0, help="2 / 4: q/k-norm backward heads in flight")
     p.add_argument("--gemm-splitk", type=int, default=-1, help="1 / 0: split-K of the accumulating GEMMs on / off")
+    p.add_argument("--gemm-tail", default="", help="comma-separated 1 / 0: the 2-CTA GEMM's tail split on / off; "
+                   "every op runs once per setting")
     p.add_argument("--attn-pingpong", default="", help="comma-separated 0 / 1: attention forward softmax groups "
                    "alternate their exponential phases; every op runs once per setting (and per --attn-emu)")
     p.add_argument("--attn-emu", default="", help="comma-separated settings of the attention forward's FMA-pipe "
@@ -383,8 +385,11 @@ def main(argv=None):
     polls = [int(v) for v in a.attn_poll.split(",")] if a.attn_poll else [None]
     gpolls = [int(v) for v in a.gemm_poll.split(",")] if a.gemm_poll else [None]
     arows = [int(v) for v in a.adanorm_bwd_rows.split(",")] if a.adanorm_bwd_rows else [None]
-    for emu, pp, poll, gpoll, arow in [(e, q, w, g, r) for r in arows for g in gpolls for w in polls for q in pps
-                                       for e in settings]:
+    tails = [int(v) for v in a.gemm_tail.split(",")] if a.gemm_tail else [None]
+    for emu, pp, poll, gpoll, arow, tail in [(e, q, w, g, r, t) for t in tails for r in arows for g in gpolls
+                                             for w in polls for q in pps for e in settings]:
+        if tail is not None:
+            ext().set_gemm_tail_split(bool(tail))
         if arow is not None:
             ext().set_adanorm_bwd_rows(arow)
         if gpoll is not None:
@@ -408,6 +413,8 @@ def main(argv=None):
                 row["gemm_poll"] = gpoll
             if arow is not None:
                 row["adanorm_bwd_rows"] = arow
+            if tail is not None:
+                row["gemm_tail"] = tail
             from ._ext import check_errors
             check_errors()
             print(json.dumps(row), flush=True)
