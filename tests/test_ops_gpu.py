@@ -327,3 +327,26 @@ def test_ops_from_a_fresh_thread():
     assert "thread" in out and err.sum().item() == 0
     for x, y in zip(out["thread"], main):
         torch.testing.assert_close(x, y, rtol=0, atol=1e-3)
+
+
+def test_cross_attention_backward_single_key_block_and_empty_text():
+    """Keys <= 128: the backward stores each dQ tile directly (no accumulator); a sample with no text keys
+    (kv_len 0) gets zero output and exactly zero dQ, the others match the fp32 reference."""
+    torch.manual_seed(8)
+    B, T, D, heads, L = 3, 320, 1024, 8, 96
+    q = torch.randn(B, T, D, device="cuda").bfloat16()
+    kv = torch.randn(B, L, 2 * D, device="cuda").bfloat16()
+    kv_len = torch.tensor([L, 0, 17], device="cuda", dtype=torch.int32)
+    do = torch.randn(B, T, D, device="cuda").bfloat16()
+    qa, kva = q.clone().requires_grad_(), kv.clone().requires_grad_()
+    o = Fz.cross_attention_core(qa, kva, heads, kv_len)
+    o.backward(do)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(o[1]).item() == 0 and torch.count_nonzero(qa.grad[1]).item() == 0
+    keep = torch.tensor([0, 2])
+    qb, kvb = q[keep].float().cpu().requires_grad_(), kv[keep].float().cpu().requires_grad_()
+    ref = Fz.cross_attention_core(qb, kvb, heads, kv_len[keep].cpu())
+    ref.backward(do[keep].float().cpu())
+    assert rel(o[keep].cpu(), ref) < 2e-2
+    assert rel(qa.grad[keep].cpu(), qb.grad) < 4e-2
+    assert rel(kva.grad[keep].cpu(), kvb.grad) < 4e-2

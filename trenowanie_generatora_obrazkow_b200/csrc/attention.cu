@@ -589,7 +589,7 @@ cudaError_t attention_bwd_prep_launch(const AttnParams& p, const bf16* dO, float
   else if (p.hd == 64) flash_bwd_delta_kernel<64><<<delta_grid(items, 64), 256, 0, s>>>(p, dO, delta, lse2);
   else return cudaErrorInvalidValue;
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || dq_acc == nullptr) return e;
   return cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)p.B * p.Tq * p.Hq * p.hd, s);
 }
 

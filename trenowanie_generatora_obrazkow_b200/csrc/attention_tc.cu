@@ -715,7 +715,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                         const __grid_constant__ CUtensorMap tmdQ, AttnParams p, const float* __restrict__ delta,
                         const float* __restrict__ lse2, __nv_bfloat16* __restrict__ dk, long long dk_bs, long long dk_ts, long long dk_hs,
                         __nv_bfloat16* __restrict__ dv, long long dv_bs, long long dv_ts, long long dv_hs, int* err,
-                        int flags) {
+                        int flags, int dq_mode) {
   constexpr int HD = 128;
   const bool poll_mma = (flags & 2) != 0, poll_sm = (flags & 4) != 0, poll_ld = (flags & 8) != 0;
   using L = BwdSmem;
@@ -1010,6 +1010,21 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const bool leader = threadIdx.x == 320;
     float* stage = reinterpret_cast<float*>(smem + L::DQ_OFF);  // [2 halves][32 queries][128]
+    if (dq_mode != 0 && !active && kb == 0) {
+      // stored dQ and no key for this sample (kv_len 0): nothing else writes its rows, so they are stored as zeros
+      for (int i = threadIdx.x - 320; i < 2 * 32 * HD; i += 128) stage[i] = 0.f;
+      fence_proxy_async_smem();
+      drain_group_sync();
+      if (leader) {
+        for (int i = 0; i < p.rep * n_qt; ++i) {
+          const int h = hk * p.rep + i / n_qt, q0 = (i % n_qt) * BQ;
+          for (int half = 0; half < 2 && q0 + half * 32 < p.Tq; ++half) {
+            tma_store_4d(&tmdQ, stage + half * 32 * HD, 0, h, q0 + half * 32, b);
+            bulk_commit_group();
+          }
+        }
+      }
+    }
     for (int i = 0; i < n_it; ++i) {
       const int h = hk * p.rep + i / n_qt, q0 = (i % n_qt) * BQ;
       if (!warp_wait(&bars->dq_full, i & 1, err, ERR_MBAR_TIMEOUT_EPILOGUE, poll_sm)) {
@@ -1030,13 +1045,26 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         if (q0 + half * 32 >= p.Tq) break;
         if (leader) bulk_wait_group_read<1>();  // this half's reduce from the previous iteration has read smem
         drain_group_sync();
-        float* dst = stage + half * 32 * HD + d;
+        if (dq_mode == 2) {  // the only key block: dQ stored as bf16, [32 queries][128] tile
+          __nv_bfloat16* dstb = reinterpret_cast<__nv_bfloat16*>(stage) + half * 32 * HD + d;
 #pragma unroll
-        for (int q = 0; q < 32; ++q) dst[q * HD] = __uint_as_float(v[half][q]) * p.scale;
+          for (int q = 0; q < 32; ++q) dstb[q * HD] = __float2bfloat16_rn(__uint_as_float(v[half][q]) * p.scale);
+        } else {
+          float* dst = stage + half * 32 * HD + d;
+#pragma unroll
+          for (int q = 0; q < 32; ++q) dst[q * HD] = __uint_as_float(v[half][q]) * p.scale;
+        }
         fence_proxy_async_smem();
         drain_group_sync();
         if (leader) {
-          tma_reduce_add_4d(&tmdQ, stage + half * 32 * HD, 0, h, q0 + half * 32, b);
+          if (dq_mode == 0) {
+            tma_reduce_add_4d(&tmdQ, stage + half * 32 * HD, 0, h, q0 + half * 32, b);
+          } else {
+            const void* src = dq_mode == 2 ? static_cast<const void*>(reinterpret_cast<__nv_bfloat16*>(stage) +
+                                                                      half * 32 * HD)
+                                           : static_cast<const void*>(stage + half * 32 * HD);
+            tma_store_4d(&tmdQ, src, 0, h, q0 + half * 32, b);
+          }
           bulk_commit_group();
         }
       }
@@ -1069,8 +1097,10 @@ cudaError_t attention_bwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk
                                     const float* delta, const float* lse2, __nv_bfloat16* dk, long long dk_bs,
                                     long long dk_ts,
                                     long long dk_hs, __nv_bfloat16* dv, long long dv_bs, long long dv_ts,
-                                    long long dv_hs, int* err, cudaStream_t s) {
+                                    long long dv_hs, int* err, cudaStream_t s, int dq_mode) {
   if (p.hd != 128) return cudaErrorInvalidValue;
+  // dq_mode 1 / 2 store the dQ tile (fp32 / bf16) instead of reduce-adding it: only when one key block covers every key
+  if (dq_mode < 0 || dq_mode > 2 || (dq_mode != 0 && p.Tk > BK_KEYS)) return cudaErrorInvalidValue;
   static bool set = false;
   if (!set) {
     cudaFuncSetAttribute(flash_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem::TOTAL);
@@ -1079,7 +1109,7 @@ cudaError_t attention_bwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk
   dim3 grid((p.Tk + BK_KEYS - 1) / BK_KEYS, p.Hkv, p.B);
   flash_bwd_tc_kernel<<<grid, BWD_THREADS, BwdSmem::TOTAL, s>>>(tq, tk, tv, tdo, tdq, p, delta, lse2, dk, dk_bs,
                                                                dk_ts, dk_hs, dv, dv_bs, dv_ts, dv_hs, err,
-                                                               g_attn_poll_bwd << 1);
+                                                               g_attn_poll_bwd << 1, dq_mode);
   return cudaGetLastError();
 }
 

@@ -212,6 +212,13 @@ __device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const 
       "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
 }
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x, int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
 // TMA store / reduction of a shared tile into a 3-D map (GEMM epilogue), tracked by bulk groups. Elements outside
 // the map's extent are not written.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {

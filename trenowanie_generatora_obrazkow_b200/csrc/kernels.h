@@ -168,18 +168,20 @@ cudaError_t attention_bwd_launch(const AttnParams& p, const __nv_bfloat16* dO, f
                                  __nv_bfloat16* dk, long long dk_bs, long long dk_ts, long long dk_hs,
                                  __nv_bfloat16* dv, long long dv_bs, long long dv_ts, long long dv_hs, cudaStream_t s);
 
-// lse2 (optional, [B][Hq][Tq]): receives lse * log2(e) for the tcgen05 backward
+// lse2 (optional, [B][Hq][Tq]): receives lse * log2(e) for the tcgen05 backward; dq_acc nullptr: nothing zeroed
 cudaError_t attention_bwd_prep_launch(const AttnParams& p, const __nv_bfloat16* dO, float* delta, float* dq_acc,
                                       cudaStream_t s, float* lse2 = nullptr);
 cudaError_t attention_dq_convert_launch(const AttnParams& p, const float* dq_acc, __nv_bfloat16* dq, long long bs,
                                         long long ts, long long hs, cudaStream_t s);
-// tcgen05 backward (head dim 128); dq_acc zeroed and delta computed by attention_bwd_prep_launch. tdq: 4-D fp32 map
-// of dq_acc {hd, Hq, Tq, B} with a {128, 1, 32, 1} box, no swizzle (the dQ tiles are TMA reduce-added into it).
+// tcgen05 backward (head dim 128); delta (and, dq_mode 0, the zeroed dq_acc) from attention_bwd_prep_launch. tdq:
+// 4-D map of dQ {hd, Hq, Tq, B} with a {128, 1, 32, 1} box, no swizzle. dq_mode 0: fp32 accumulator, the dQ tiles of
+// every key block are TMA reduce-added into it; 1 / 2 (one key block covers all keys, Tk <= 128): each dQ tile is
+// final and is stored, fp32 / bf16, so nothing needs zeroing or converting.
 cudaError_t attention_bwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                     const CUtensorMap& tdo, const CUtensorMap& tdq, const AttnParams& p,
                                     const float* delta, const float* lse2, __nv_bfloat16* dk, long long dk_bs, long long dk_ts,
                                     long long dk_hs, __nv_bfloat16* dv, long long dv_bs, long long dv_ts,
-                                    long long dv_hs, int* err, cudaStream_t s);
+                                    long long dv_hs, int* err, cudaStream_t s, int dq_mode = 0);
 // tcgen05 forward (attention_tc.cu); tensor maps: 4-D {hd, T, H, B}, boxes {64, 128 | 64, 1, 1}, 128-byte swizzle
 cudaError_t attention_fwd_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                     const AttnParams& p, int* err, cudaStream_t s);

@@ -107,6 +107,24 @@ static CUtensorMap make_tmap_dq(const float* base, uint64_t hd, uint64_t H, uint
   return m;
 }
 
+// 4-D bf16 map of a dQ output [B][Tq][Hq][hd] with element strides (bs, ts, hs) as {hd, Hq, Tq, B}, box
+// {hd, 1, 32, 1}, no swizzle: the backward stores final 32-query dQ tiles into it (one key block covers all keys).
+static CUtensorMap make_tmap_dq_bf16(const void* base, uint64_t hd, uint64_t H, uint64_t T, uint64_t B, uint64_t hs,
+                                     uint64_t ts, uint64_t bs) {
+  CUtensorMap m;
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0 && (hs * 2) % 16 == 0 && (ts * 2) % 16 == 0 &&
+                  (bs * 2) % 16 == 0, "dQ tensor map: 16-byte aligned base and strides");
+  cuuint64_t dims[4] = {hd, H, T, B};
+  cuuint64_t strides[3] = {(H > 1 ? hs : hd) * 2, ts * 2, (B > 1 ? bs : ts * T) * 2};
+  cuuint32_t box[4] = {(cuuint32_t)hd, 1, 32, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = tmap_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (dQ bf16) failed with code ", (int)r);
+  return m;
+}
+
 // 4-D bf16 tensor map {hd, T, H, B} (strides in elements) with a {64, box_rows, 1, 1} box, 128-byte swizzle.
 static CUtensorMap make_tmap_bhtd(const void* base, uint64_t hd, uint64_t T, uint64_t H, uint64_t B, uint64_t ts,
                                   uint64_t hs, uint64_t bs, uint32_t box_rows) {
@@ -922,23 +940,30 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::T
   p.lse = lse.data_ptr<float>();
   at::Tensor delta = at::empty({2, p.B, p.Hq, p.Tq}, q.options().dtype(at::kFloat));  // delta, lse * log2(e)
   float* lse2 = delta.data_ptr<float>() + (long long)p.B * p.Hq * p.Tq;
-  at::Tensor dq_acc = dq_f32 ? dq : at::empty({p.B, p.Tq, p.Hq, p.hd}, q.options().dtype(at::kFloat));
   if (g_attention_tc && p.hd == 128) {
     cudaStream_t st = at::cuda::getCurrentCUDAStream();
+    // one key block covers every key (cross-attention against <= 128 text tokens): each dQ tile is final, so it is
+    // stored straight into dq (no zeroed accumulator, no reduce-add, no conversion pass)
+    const bool single = p.Tk <= 128;
+    const int dq_mode = single ? (dq_f32 ? 1 : 2) : 0;
+    at::Tensor dq_acc = dq_f32 || single ? dq : at::empty({p.B, p.Tq, p.Hq, p.hd}, q.options().dtype(at::kFloat));
     CUtensorMap tq = make_tmap_bhtd(p.q, p.hd, p.Tq, p.Hq, p.B, p.q_ts, p.q_hs, p.q_bs, 64);
     CUtensorMap tk = make_tmap_bhtd(p.k, p.hd, p.Tk, p.Hkv, p.B, p.k_ts, p.k_hs, p.k_bs, 128);
     CUtensorMap tv = make_tmap_bhtd(p.v, p.hd, p.Tk, p.Hkv, p.B, p.v_ts, p.v_hs, p.v_bs, 128);
     CUtensorMap tdo = make_tmap_bhtd(dO.data_ptr(), p.hd, p.Tq, p.Hq, p.B, dO.stride(1), dO.stride(2), dO.stride(0), 64);
-    TGO_CHECK_LAUNCH(attention_bwd_prep_launch(p, bfp(dO), delta.data_ptr<float>(), dq_acc.data_ptr<float>(), st,
-                                               lse2));
-    CUtensorMap tdq = make_tmap_dq(dq_acc.data_ptr<float>(), p.hd, p.Hq, p.Tq, p.B);
+    TGO_CHECK_LAUNCH(attention_bwd_prep_launch(p, bfp(dO), delta.data_ptr<float>(),
+                                               dq_mode == 0 ? dq_acc.data_ptr<float>() : nullptr, st, lse2));
+    CUtensorMap tdq = dq_mode == 2 ? make_tmap_dq_bf16(dq.data_ptr(), p.hd, p.Hq, p.Tq, p.B, dq.stride(2),
+                                                       dq.stride(1), dq.stride(0))
+                                   : make_tmap_dq(dq_acc.data_ptr<float>(), p.hd, p.Hq, p.Tq, p.B);
     TGO_CHECK_LAUNCH(attention_bwd_tc_launch(tq, tk, tv, tdo, tdq, p, delta.data_ptr<float>(), lse2, bfp(dk), dk.stride(0),
                                              dk.stride(1), dk.stride(2), bfp(dv), dv.stride(0), dv.stride(1),
-                                             dv.stride(2), err_ptr(err), st));
-    if (!dq_f32)
+                                             dv.stride(2), err_ptr(err), st, dq_mode));
+    if (dq_mode == 0 && !dq_f32)
       TGO_CHECK_LAUNCH(attention_dq_convert_launch(p, dq_acc.data_ptr<float>(), bfp(dq), dq.stride(0), dq.stride(1),
                                                    dq.stride(2), st));
   } else {
+    at::Tensor dq_acc = dq_f32 ? dq : at::empty({p.B, p.Tq, p.Hq, p.hd}, q.options().dtype(at::kFloat));
     TGO_CHECK_LAUNCH_N(attention_bwd_launch(p, bfp(dO), delta.data_ptr<float>(), dq_acc.data_ptr<float>(), bfp(dq),
                                           dq.stride(0), dq.stride(1), dq.stride(2), bfp(dk), dk.stride(0), dk.stride(1),
                                           dk.stride(2), bfp(dv), dv.stride(0), dv.stride(1), dv.stride(2),

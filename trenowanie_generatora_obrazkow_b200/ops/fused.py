@@ -92,6 +92,25 @@ def _notify(p):
         fn(p)
 
 
+def _weight_grad_target(w):
+    """Where a fused backward accumulates (+=) the gradient of a small fp32 weight (norm weights): the parameter's
+    own gradient buffer, so no zero-filled temporary and no autograd accumulation kernel run per use; the autograd
+    function then returns None for it and calls ``_weight_grad_done``. Falls back to a temporary (returned
+    through autograd) when the buffer cannot take the sum in place."""
+    if w.requires_grad and w.is_leaf and w.dtype == torch.float32 and (w.grad is None or (
+            w.grad.dtype == torch.float32 and w.grad.is_contiguous())):
+        return _grad_buffer(w), True
+    return torch.zeros_like(w, dtype=torch.float32), False
+
+
+def _weight_grad_done(w, direct, g):
+    """(autograd's gradient for w): None when it was accumulated in place (and the ready hooks ran)."""
+    if direct:
+        _notify(w)
+        return None
+    return g if w.requires_grad else None
+
+
 # ----------------------------------------------------------------------------------------------------------------
 # selective activation checkpointing
 # ----------------------------------------------------------------------------------------------------------------
@@ -246,6 +265,7 @@ class _AdaNormFn(torch.autograd.Function):
         ctx.save_for_backward(x_new, rstd, w, scale, y, gate)
         ctx.T = T
         ctx.has_mod = shift is not None
+        ctx.w_param = w
         return x_new, h
 
     @staticmethod
@@ -253,13 +273,13 @@ class _AdaNormFn(torch.autograd.Function):
         x_new, rstd, w, scale, y, gate = ctx.saved_tensors
         if dh is None:
             dh = torch.zeros_like(x_new)
-        dw = torch.zeros_like(w)
+        dw, direct = _weight_grad_target(ctx.w_param)
         dxe = dx_new.contiguous() if dx_new is not None else None
         dx, dy, dshift, dscale, dgate = ext().adanorm_bwd(dh.contiguous(), dxe, x_new, rstd, w, dw, scale, y, gate,
                                                           ctx.T)
         if dy is None:
             dy = dx  # ungated residual: d(branch) == d(x_new)
-        return dx, dy, dgate, dw, dshift, dscale, None
+        return dx, dy, dgate, _weight_grad_done(ctx.w_param, direct, dw), dshift, dscale, None
 
 
 class _NormModFn(torch.autograd.Function):
@@ -271,14 +291,15 @@ class _NormModFn(torch.autograd.Function):
         _, h, rstd = ext().adanorm_fwd(x, None, None, w, shift, scale, T, eps)
         ctx.save_for_backward(x, rstd, w, scale)
         ctx.T = T
+        ctx.w_param = w
         return h
 
     @staticmethod
     def backward(ctx, dh):
         x, rstd, w, scale = ctx.saved_tensors
-        dw = torch.zeros_like(w)
+        dw, direct = _weight_grad_target(ctx.w_param)
         dx, _, dshift, dscale, _ = ext().adanorm_bwd(dh.contiguous(), None, x, rstd, w, dw, scale, None, None, ctx.T)
-        return dx, dw, dshift, dscale, None
+        return dx, _weight_grad_done(ctx.w_param, direct, dw), dshift, dscale, None
 
 
 def adanorm(x, y, gate, w, shift=None, scale=None, eps=R.EPS):
@@ -333,6 +354,7 @@ class _SelfAttnFn(torch.autograd.Function):
             _tag(k, rec, 1)
         ctx.save_for_backward(qkv, q, k, o, lse, rq, rk, q_w, k_w, cos, sin, kv_len)
         ctx.dims = (hq, hkv, hd, scale)
+        ctx.q_param, ctx.k_param = q_w, k_w
         return o.view(B, T, hq * hd)
 
     @staticmethod
@@ -351,10 +373,14 @@ class _SelfAttnFn(torch.autograd.Function):
         v4 = qkv[:, :, (hq + hkv) * hd:(hq + 2 * hkv) * hd].unflatten(-1, (hkv, hd))
         ext().attention_bwd(q4, k4, v4, o, lse, do, kv_len, scale, dq.view(B, T, hq, hd), dk.view(B, T, hkv, hd), dv4,
                             err_buf(q.device))
-        dwq = torch.zeros_like(q_w) if q_w is not None else None
-        dwk = torch.zeros_like(k_w) if k_w is not None else None
+        dwq, dq_direct = _weight_grad_target(ctx.q_param) if q_w is not None else (None, False)
+        dwk, dk_direct = _weight_grad_target(ctx.k_param) if k_w is not None else (None, False)
         ext().qknorm_rope_bwd(qkv.view(B * T, C), hq, hkv, hd, q_w, k_w, cos, sin, T, rq, rk, dq, dk,
                               dqkv.view(B * T, C), dwq, dwk)
+        if q_w is not None:
+            dwq = _weight_grad_done(ctx.q_param, dq_direct, dwq)
+        if k_w is not None:
+            dwk = _weight_grad_done(ctx.k_param, dk_direct, dwk)
         return dqkv, dwq, dwk, None, None, None, None, None, None, None, None
 
 
