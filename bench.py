@@ -131,6 +131,8 @@ def setup_dist(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    from trenowanie_generatora_obrazkow_b200.utils.profiling import arm_stack_dump
+    arm_stack_dump()
     if world > 1:
         torch.cuda.set_device(local)
         from datetime import timedelta

@@ -237,6 +237,8 @@ def main():
                              args.opd_actor_gpus, args.teacher_gpu)
         torch.cuda.set_device(local)
     backend = os.environ.get("DIST_BACKEND", "nccl" if cuda else "gloo")
+    from trenowanie_generatora_obrazkow_b200.utils.profiling import arm_stack_dump
+    arm_stack_dump()
     dist.init_process_group(backend, timeout=timedelta(minutes=args.dist_timeout))
     rank = dist.get_rank()
     device = torch.device("cuda", torch.cuda.current_device()) if cuda else torch.device("cpu")

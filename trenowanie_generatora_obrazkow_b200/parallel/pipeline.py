@@ -171,15 +171,30 @@ class StageModel(nn.Module):
         return _flush(x, pending)
 
 
-def direction_groups(pipes):
+def direction_groups(pipes, device=None):
     """{(rank_a, rank_b): group} for every adjacent stage pair of every pipe, one group per direction (a -> b). A
-    collective over the default group: every rank calls it, in the same order."""
+    collective over the default group: every rank calls it, in the same order.
+
+    NCCL builds a group's communicator at its first operation, and that setup blocks the host until both members
+    take part. Left to the schedule, stage s would block setting up its first gradient receive while stage s + 1,
+    whose GPU already holds a posted receive from stage s, cannot finish the forward that precedes its first gradient
+    send: a deadlock. So every group is set up here with a one-element all-reduce, the groups walked in one global
+    order by every rank (each waits only for groups it belongs to, so the earliest unfinished group always has both
+    members waiting on it)."""
     out = {}
     for pipe in pipes:
         for s in range(len(pipe) - 1):
             a, b = pipe[s], pipe[s + 1]
             out[(a, b)] = dist.new_group([a, b])  # activations a -> b
             out[(b, a)] = dist.new_group([a, b])  # gradients b -> a
+    if dist.get_backend() == "nccl":
+        me = dist.get_rank()
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        one = torch.zeros(1, device=dev)
+        for key in sorted(out):
+            if me in key:
+                dist.all_reduce(one, group=out[key])
+        torch.cuda.synchronize(dev)
     return out
 
 
@@ -199,6 +214,7 @@ class OneFOneB:
                 if 0 <= a < self.pp and 0 <= b < self.pp and (pipe[a], pipe[b]) not in self.links:
                     raise ValueError("OneFOneB needs direction_groups(...) links for its neighbours")
         self._sends = []   # (works, buffers) of sends whose completion is awaited at the end of the step
+        self.early = False
 
     # ---- communication -----------------------------------------------------------------------------------------
     def _empty_acts(self):
@@ -251,7 +267,12 @@ class OneFOneB:
         n_steady = M - n_warm
         saved = {}
         losses = []
-        early = True  # receives posted a micro-batch ahead (one-direction streams make that safe)
+        # receives posted a micro-batch ahead (off by default): with NCCL a receive posted before its peer reaches the
+        # matching send leaves a kernel waiting on the GPU, and a host call that synchronises the device meanwhile
+        # (the caching allocator freeing cached blocks under memory pressure) then waits for a peer that is itself
+        # waiting on this rank. On B200 at 1024 px the 2-stage bench stalled that way; posting each receive right
+        # before it is needed keeps every pending NCCL kernel one whose peer is already on its way to the match.
+        early = self.early
 
         def forward(i, acts):
             if first:

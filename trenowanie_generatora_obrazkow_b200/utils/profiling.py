@@ -117,3 +117,13 @@ class PhaseTimer:
                 out[name] = out.get(name, 0.0) + a.elapsed_time(b)
         self.steps, self._cur = [], None
         return out
+
+
+def arm_stack_dump():
+    """With TGO_STACK_DUMP_S=N in the environment, print every thread's Python stack to stderr once, N seconds from
+    now (faulthandler; the process keeps running): shows where each rank of a stuck multi-rank run waits."""
+    import os
+    secs = os.environ.get("TGO_STACK_DUMP_S")
+    if secs:
+        import faulthandler
+        faulthandler.dump_traceback_later(float(secs), repeat=False)
