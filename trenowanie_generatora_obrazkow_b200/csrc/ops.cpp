@@ -143,6 +143,8 @@ static CUtensorMap make_tmap_bhtd(const void* base, uint64_t hd, uint64_t T, uin
 }
 
 static bool g_attention_tc = true;
+static bool g_attention_dq_store = true;  // one key block: store final dQ tiles (off: zeroed accumulator, for A/B)
+void set_attention_dq_store(bool on) { g_attention_dq_store = on; }
 void set_attention_tc(bool on) { g_attention_tc = on; }
 void set_attention_fwd_split(int64_t wpq) {
   TORCH_CHECK(attention_set_fwd_split((int)wpq) == cudaSuccess, "attention forward split: 1 or 2");
@@ -944,7 +946,7 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::T
     cudaStream_t st = at::cuda::getCurrentCUDAStream();
     // one key block covers every key (cross-attention against <= 128 text tokens): each dQ tile is final, so it is
     // stored straight into dq (no zeroed accumulator, no reduce-add, no conversion pass)
-    const bool single = p.Tk <= 128;
+    const bool single = g_attention_dq_store && p.Tk <= 128;
     const int dq_mode = single ? (dq_f32 ? 1 : 2) : 0;
     at::Tensor dq_acc = dq_f32 || single ? dq : at::empty({p.B, p.Tq, p.Hq, p.hd}, q.options().dtype(at::kFloat));
     CUtensorMap tq = make_tmap_bhtd(p.q, p.hd, p.Tq, p.Hq, p.B, p.q_ts, p.q_hs, p.q_bs, 64);
@@ -1292,6 +1294,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("muon_apply", &tgo::muon_apply, "Muon: parameter update + bf16 shadow refresh from the flat updates");
   m.def("grad_norm", &tgo::grad_norm, "global gradient norm and clip coefficient on the device (one launch)");
   m.def("adamw", &tgo::adamw, "multi-tensor AdamW with clip coefficient, bf16 shadow refresh and EMA fused in");
+  m.def("set_attention_dq_store", &tgo::set_attention_dq_store,
+        "attention backward with one key block: store the final dQ tiles (default) or reduce-add into a zeroed accumulator");
   m.def("set_attention_poll", &tgo::set_attention_poll,
         "attention barrier waits that poll instead of suspending, forward and backward masks (bit 0 MMA thread, "
         "1 softmax / dQ drain, 2 TMA producer; defaults 3 and 1)",

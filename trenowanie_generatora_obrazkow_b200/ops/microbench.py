@@ -303,6 +303,7 @@ def cases(small):
         "attn_bwd": lambda: attn_case(B, T, H, hd, True),
         "attn_fwd_4k": lambda: attn_case(4 if small else 16, 4096, H, hd, False),  # 1024 px sampling (CFG batch)
         "attn_cross_4k": lambda: attn_case(4 if small else 16, 4096, H, hd, False, Tk=128),  # text cross-attention
+        "attn_cross_bwd": lambda: attn_case(B, T, H, hd, True, Tk=128),  # training cross-attention backward
         "adanorm_fwd": lambda: adanorm_case(B, T, D, False),
         "adanorm_bwd": lambda: adanorm_case(B, T, D, True),
         "qknorm_rope_fwd": lambda: qknorm_case(B, T, H, hd, False),
@@ -364,6 +365,8 @@ def main(argv=None):
                    "once per mask")
     p.add_argument("--gemm-poll", default="", help="comma-separated masks (0..7) of GEMM barrier waits that poll "
                    "(1 MMA thread, 2 epilogue, 4 TMA producer); every op runs once per mask")
+    p.add_argument("--attn-dq-store", default="", help="comma-separated 1 / 0: attention backward with one key block "
+                   "stores final dQ tiles (1) or reduce-adds into a zeroed accumulator (0); every op runs per setting")
     p.add_argument("--adanorm-bwd-rows", default="", help="comma-separated 1 / 2: adanorm backward rows per block "
                    "reduction; every op runs once per setting")
     a = p.parse_args(argv)
@@ -386,8 +389,11 @@ def main(argv=None):
     gpolls = [int(v) for v in a.gemm_poll.split(",")] if a.gemm_poll else [None]
     arows = [int(v) for v in a.adanorm_bwd_rows.split(",")] if a.adanorm_bwd_rows else [None]
     tails = [int(v) for v in a.gemm_tail.split(",")] if a.gemm_tail else [None]
-    for emu, pp, poll, gpoll, arow, tail in [(e, q, w, g, r, t) for t in tails for r in arows for g in gpolls
-                                             for w in polls for q in pps for e in settings]:
+    stores = [int(v) for v in a.attn_dq_store.split(",")] if a.attn_dq_store else [None]
+    for emu, pp, poll, gpoll, arow, tail, store in [(e, q, w, g, r, t, d) for d in stores for t in tails for r in arows
+                                                    for g in gpolls for w in polls for q in pps for e in settings]:
+        if store is not None:
+            ext().set_attention_dq_store(bool(store))
         if tail is not None:
             ext().set_gemm_tail_split(bool(tail))
         if arow is not None:
@@ -415,6 +421,8 @@ def main(argv=None):
                 row["adanorm_bwd_rows"] = arow
             if tail is not None:
                 row["gemm_tail"] = tail
+            if store is not None:
+                row["attn_dq_store"] = store
             from ._ext import check_errors
             check_errors()
             print(json.dumps(row), flush=True)
