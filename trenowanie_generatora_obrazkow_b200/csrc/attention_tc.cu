@@ -617,7 +617,7 @@ cudaError_t attention_set_fwd_pingpong(int on) {
 
 cudaError_t attention_set_fwd_emu(int eighths) {  // -1: the built-in default
   if (eighths == -1) eighths = kDefaultFwdEmu;
-  if (eighths != 0 && eighths != 2 && eighths != 3 && eighths != 4) return cudaErrorInvalidValue;
+  if (eighths < 0 || eighths > 4) return cudaErrorInvalidValue;
   g_fwd_emu = eighths;
   return cudaSuccess;
 }
@@ -626,6 +626,7 @@ template <int HD>
 static cudaError_t fwd_tc_dispatch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                    const AttnParams& p, int* err, cudaStream_t s) {
   switch (g_fwd_emu) {
+    case 1: return fwd_tc_impl<HD, 1>(tq, tk, tv, p, err, s);
     case 2: return fwd_tc_impl<HD, 2>(tq, tk, tv, p, err, s);
     case 3: return fwd_tc_impl<HD, 3>(tq, tk, tv, p, err, s);
     case 4: return fwd_tc_impl<HD, 4>(tq, tk, tv, p, err, s);

@@ -155,7 +155,7 @@ void set_attention_poll(int64_t fwd_mask, int64_t bwd_mask) {
               "set_attention_poll: masks 0..7");
 }
 void set_attention_fwd_emu(int64_t eighths) {
-  TORCH_CHECK(attention_set_fwd_emu((int)eighths) == cudaSuccess, "attention forward FMA exponentials: 0, 2, 3, 4 (-1: default)");
+  TORCH_CHECK(attention_set_fwd_emu((int)eighths) == cudaSuccess, "attention forward FMA exponentials: 0 .. 4 eighths (-1: default)");
 }
 
 static bool g_gemm_pair_enabled = true;  // 256 x 256 CTA-pair tiles: 3-6 % faster on the training shapes
@@ -1303,7 +1303,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_attention_fwd_pingpong", &tgo::set_attention_fwd_pingpong,
         "attention forward: the two softmax groups take turns for their exponential phases");
   m.def("set_attention_fwd_emu", &tgo::set_attention_fwd_emu,
-        "eighths of the key pairs whose forward exponentials run as FMA-pipe polynomials (0, 2, 3, 4)");
+        "eighths of the key pairs whose forward exponentials run as FMA-pipe polynomials (0 .. 4)");
   m.def("set_attention_fwd_split", &tgo::set_attention_fwd_split,
         "softmax warps per TMEM lane quarter in the tcgen05 attention forward (1 or 2)");
   m.def("set_attention_tc", &tgo::set_attention_tc, "use the tcgen05 attention forward (default) or mma.sync");
