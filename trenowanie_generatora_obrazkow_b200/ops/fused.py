@@ -6,8 +6,11 @@ autograd. Each CUDA op is a ``torch.autograd.Function`` whose backward is a hand
 * ``linear``        tcgen05 GEMM forward / dgrad; the weight gradient is accumulated in fp32 straight into
                     ``weight.grad`` by the GEMM epilogue (the grad never exists in bf16). Weights are read from a
                     bf16 shadow copy refreshed whenever the fp32 master changes (``bf16_weight``).
-* ``adanorm``       residual update + RMSNorm + adaLN modulation (DenoiserBlock, reference aurora/model.py:204-210).
-* ``self_attention_core``  per-head q/k RMSNorm + RoPE + flash attention, reading q/k/v from the fused qkv rows.
+* ``adanorm``       residual update + RMSNorm + adaLN modulation (DenoiserBlock, reference aurora/model.py:204-210);
+                    the norm weight's gradient is accumulated in place into ``weight.grad`` (fp32) like the linear
+                    weights', so ``torch.autograd.grad`` does not return it: read ``weight.grad``.
+* ``self_attention_core``  per-head q/k RMSNorm + RoPE + flash attention, reading q/k/v from the fused qkv rows (the
+                    q / k norm weights' gradients likewise go to their ``.grad``).
 * ``cross_attention_core`` flash attention against text keys/values with a key-length mask.
 * ``swiglu``        silu(a) * b.
 * ``varlen_attention`` packed variable-length (causal) attention for the frozen caption LM (inference only).
