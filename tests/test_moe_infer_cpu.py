@@ -1,5 +1,6 @@
 """Fused MoE inference (stacked experts, grouped GEMM, routing weight in the epilogue) against the per-expert loop of
 a transformers-style MoE block, on CPU (the grouped GEMM's CPU path)."""
+import pytest
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
@@ -60,3 +61,49 @@ def test_fused_moe_int8_close():
         want = blk(x) - blk.shared_experts(x)
         got = FusedMoE.from_block(blk, quant="int8")(x)
     assert ((got - want).norm() / want.norm()).item() < 2e-2
+
+
+def _tiny_qwen3_moe():
+    from transformers import Qwen3MoeConfig, Qwen3MoeForCausalLM
+    cfg = Qwen3MoeConfig(vocab_size=128, hidden_size=64, intermediate_size=128, moe_intermediate_size=32,
+                         num_hidden_layers=3, num_attention_heads=4, num_key_value_heads=2, head_dim=16, num_experts=4,
+                         num_experts_per_tok=2, decoder_sparse_step=1, max_position_embeddings=64)
+    torch.manual_seed(3)
+    m = Qwen3MoeForCausalLM(cfg).eval()
+    with torch.no_grad():
+        for p in m.parameters():  # the init leaves some tensors at zero (routers, experts): give every one values
+            p.add_(0.05 * torch.randn_like(p))
+    return m
+
+
+def test_fused_moe_patches_transformers5_fused_experts():
+    """transformers 5 keeps a block's experts as one module with stacked gate_up_proj / down_proj tensors and a
+    top-k router module; the patched forward matches the library's per-expert loop."""
+    pytest.importorskip("transformers")
+    m = _tiny_qwen3_moe()
+    ids = torch.randint(0, 128, (2, 11))
+    with torch.no_grad():
+        want = m.model(input_ids=ids).last_hidden_state
+        assert patch_moe_blocks(m.model) == 3
+        got = m.model(input_ids=ids).last_hidden_state
+    assert torch.allclose(got, want, atol=1e-4), (got - want).abs().max()
+
+
+def test_hf_frozen_lm_loads_a_local_model(tmp_path):
+    """HFFrozenLM (models/frozen_lm.py): a local transformers causal LM directory, the last layers skipped, MoE
+    blocks fused; states equal the library model's truncated forward."""
+    pytest.importorskip("transformers")
+    from trenowanie_generatora_obrazkow_b200.models.frozen_lm import LM_PAD, HFFrozenLM
+    m = _tiny_qwen3_moe()
+    m.save_pretrained(str(tmp_path / "lm"))
+    lm = HFFrozenLM(str(tmp_path / "lm"), skip_last=1, device="cpu")
+    assert len(lm.model.layers) == 2
+    ids = torch.randint(0, 128, (2, 9))
+    ids[1, 6:] = LM_PAD
+    ref = m.model.to(torch.bfloat16)
+    ref.layers = ref.layers[:2]
+    with torch.no_grad():
+        want = ref(input_ids=ids.masked_fill(ids.eq(LM_PAD), 0)).last_hidden_state.float()
+        got = lm.states(ids).float()
+    assert got.shape == (2, 9, 64)
+    assert ((got - want).norm() / want.norm()).item() < 3e-2

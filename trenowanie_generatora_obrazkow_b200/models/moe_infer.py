@@ -9,8 +9,11 @@ scale -> rows summed back per token. The grouped GEMM's tile schedule comes from
 (ops/gemm.py:gemm_grouped), so there is no host synchronisation and one launch per projection, whatever the
 routing.
 
-``patch_moe_blocks(model)`` finds transformers-style MoE blocks (a ``gate`` linear router and an ``experts`` list
-of gate_proj / up_proj / down_proj MLPs, plus optional ``shared_experts``) and replaces their forward.
+``patch_moe_blocks(model)`` finds transformers-style MoE blocks and replaces their forward. Two expert layouts:
+an ``experts`` list of gate_proj / up_proj / down_proj MLPs (transformers 4), or one fused ``experts`` module
+holding ``gate_up_proj`` (E, 2I, H; gate rows first) and ``down_proj`` (E, H, I) tensors with a ``gate`` router module
+carrying ``weight``, ``top_k`` and ``norm_topk_prob`` (transformers 5). Shared experts: ``shared_experts`` (added),
+or ``shared_expert`` scaled by ``sigmoid(shared_expert_gate(x))``.
 """
 import torch
 import torch.nn.functional as F
@@ -38,12 +41,21 @@ class FusedMoE:
 
     @classmethod
     def from_block(cls, block, top_k=None, norm_topk=None, quant=""):
-        ex = block.experts
-        gate_up = torch.stack([torch.cat([e.gate_proj.weight, e.up_proj.weight], 0) for e in ex]).detach()
-        down = torch.stack([e.down_proj.weight for e in ex]).detach()
-        k = top_k or getattr(block, "top_k", None) or getattr(getattr(block, "config", None), "num_experts_per_tok", 2)
-        norm = norm_topk if norm_topk is not None else getattr(getattr(block, "config", None), "norm_topk_prob", True)
-        return cls(block.gate.weight.detach(), gate_up, down, k, norm, quant)
+        ex, gate = block.experts, block.gate
+        if _fused_experts(ex):
+            gate_up, down = ex.gate_up_proj.detach(), ex.down_proj.detach()
+        else:
+            gate_up = torch.stack([torch.cat([e.gate_proj.weight, e.up_proj.weight], 0) for e in ex]).detach()
+            down = torch.stack([e.down_proj.weight for e in ex]).detach()
+        cfg = getattr(block, "config", None)
+        k = top_k or getattr(block, "top_k", None) or getattr(gate, "top_k", None) or \
+            getattr(cfg, "num_experts_per_tok", 2)
+        norm = norm_topk
+        if norm is None:
+            norm = getattr(gate, "norm_topk_prob", None)
+        if norm is None:
+            norm = getattr(cfg, "norm_topk_prob", True)
+        return cls(gate.weight.detach(), gate_up, down, int(k), bool(norm), quant)
 
     def to(self, device):
         cuda = torch.device(device).type == "cuda"
@@ -90,23 +102,43 @@ class FusedMoE:
         return out.to(x.dtype).view(shape)
 
 
+def _fused_experts(ex):
+    return isinstance(getattr(ex, "gate_up_proj", None), torch.Tensor) and \
+        isinstance(getattr(ex, "down_proj", None), torch.Tensor)
+
+
+def _expert_list(ex):
+    try:
+        items = list(ex)
+    except TypeError:
+        return False
+    return len(items) > 0 and all(hasattr(e, a) for e in items for a in ("gate_proj", "up_proj", "down_proj"))
+
+
 def patch_moe_blocks(model, quant=""):
     """Replace the forward of every transformers-style MoE block of ``model`` by FusedMoE (+ its shared experts).
     Returns the number of blocks patched."""
     n = 0
-    for mod in model.modules():
+    for mod in list(model.modules()):
         ex = getattr(mod, "experts", None)
         gate = getattr(mod, "gate", None)
-        if ex is None or gate is None or not hasattr(gate, "weight") or len(ex) == 0:
+        if ex is None or gate is None or not isinstance(getattr(gate, "weight", None), torch.Tensor):
             continue
-        if not all(hasattr(e, a) for e in ex for a in ("gate_proj", "up_proj", "down_proj")):
+        if not (_fused_experts(ex) or _expert_list(ex)):
             continue
         fused = FusedMoE.from_block(mod, quant=quant).to(gate.weight.device)
         shared = getattr(mod, "shared_experts", None)
+        shared_one = getattr(mod, "shared_expert", None)
+        shared_gate = getattr(mod, "shared_expert_gate", None)
 
-        def forward(hidden_states, *a, _f=fused, _s=shared, **k):
+        def forward(hidden_states, *a, _f=fused, _s=shared, _s1=shared_one, _g=shared_gate, **k):
             out = _f(hidden_states)
-            return out + _s(hidden_states) if _s is not None else out
+            if _s is not None:
+                out = out + _s(hidden_states)
+            if _s1 is not None:
+                y = _s1(hidden_states)
+                out = out + (torch.sigmoid(_g(hidden_states)) * y if _g is not None else y)
+            return out
         mod.forward = forward
         mod._fused_moe = fused
         n += 1
