@@ -107,3 +107,73 @@ def test_hf_frozen_lm_loads_a_local_model(tmp_path):
         got = lm.states(ids).float()
     assert got.shape == (2, 9, 64)
     assert ((got - want).norm() / want.norm()).item() < 3e-2
+
+
+class _SelfRoutingBlock(nn.Module):
+    """DeepSeek / Bailing-style block: its forward routes (sigmoid scores, group-limited top-k, scaled weights: a
+    routing FusedMoE does not reimplement) and calls moe_infer for the experts."""
+
+    def __init__(self, E=6, H=32, I=16, k=2):
+        super().__init__()
+        self.gate = nn.Linear(H, E, bias=False)
+        self.experts = nn.ModuleList(_Expert(H, I) for _ in range(E))
+        self.k, self.groups = k, 2
+
+    def forward(self, x):
+        x2 = x.reshape(-1, x.shape[-1])
+        s = torch.sigmoid(self.gate(x2).float())
+        g = s.view(len(x2), self.groups, -1).amax(-1)                 # best score per expert group
+        keep = g.topk(1, dim=-1).indices                                # one group per token
+        mask = torch.zeros_like(g).scatter_(1, keep, 1).repeat_interleave(s.shape[1] // self.groups, 1)
+        w, idx = (s * mask).topk(self.k, dim=-1)
+        w = 2.5 * w / w.sum(-1, keepdim=True)
+        return self.moe_infer(x2, idx, w).view(x.shape)
+
+    def moe_infer(self, x, idx, w):
+        out = torch.zeros_like(x)
+        for m in range(len(x)):
+            for j in range(idx.shape[1]):
+                out[m] += w[m, j] * self.experts[int(idx[m, j])](x[m])
+        return out
+
+
+def test_fused_moe_keeps_the_blocks_own_routing():
+    torch.manual_seed(4)
+    blk = _SelfRoutingBlock()
+    x = torch.randn(2, 9, 32)
+    with torch.no_grad():
+        want = blk(x)
+        assert patch_moe_blocks(blk) == 1
+        assert len(blk.experts) == 6 and not isinstance(blk.experts, nn.ModuleList)  # per-expert modules dropped
+        got = blk(x)
+    assert torch.allclose(got, want, atol=1e-4), (got - want).abs().max()
+
+
+def test_transformers5_compat_and_rope_refresh():
+    """Shims for transformers-4 remote code: the "default" RoPE init reads theta / partial factor also from the
+    rope dicts; RoPE buffers left uninitialised by meta-device loading are recomputed from the init function."""
+    pytest.importorskip("transformers")
+    import types
+
+    import transformers.modeling_rope_utils as rope_utils
+    from trenowanie_generatora_obrazkow_b200.models.frozen_lm import refresh_rope_buffers, transformers5_compat
+    transformers5_compat()
+    import transformers.utils.import_utils as import_utils
+    assert import_utils.is_torch_fx_available() is False
+    cfg = types.SimpleNamespace(hidden_size=64, num_attention_heads=4, head_dim=None, rope_theta=None,
+                                partial_rotary_factor=None, rope_scaling={"rope_theta": 5000.0,
+                                                                          "partial_rotary_factor": 0.5})
+    inv, scale = rope_utils.ROPE_INIT_FUNCTIONS["default"](cfg, "cpu")
+    want = 1.0 / 5000.0 ** (torch.arange(0, 8, 2).float() / 8)
+    assert scale == 1.0 and torch.allclose(inv, want)
+    class Rotary(nn.Module):  # a transformers-4 style rotary module (what old remote code builds)
+        def __init__(self, config):
+            super().__init__()
+            self.config, self.rope_init_fn = config, rope_utils.ROPE_INIT_FUNCTIONS["default"]
+            inv, self.attention_scaling = self.rope_init_fn(config, None)
+            self.register_buffer("inv_freq", torch.full_like(inv, float("nan")), persistent=False)  # "uninitialised"
+            self.original_inv_freq = self.inv_freq
+
+    m = nn.Sequential(nn.Linear(4, 4), Rotary(cfg))
+    assert refresh_rope_buffers(m) == 1
+    assert torch.allclose(m[1].inv_freq, want) and torch.allclose(m[1].original_inv_freq, want)

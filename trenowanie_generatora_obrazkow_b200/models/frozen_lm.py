@@ -6,8 +6,10 @@ aurora/slayer.py:30-146, :238-432) on each caption batch, outside the trainable 
 * ``slayer`` the Slayer GPT (models/slayer.py) from a local directory (config.json + model.safetensors): the
              residual stream after ``n_layer - skip_last`` blocks, as the reference's LMTextEncoder reads it.
 * ``hf``     a transformers causal LM loaded from a local directory (``cfg.repo`` must be a path or a cached
-             model id; there is no network on the training boxes): first ``num_layers - skip_last`` layers, bf16,
-             the last hidden state.
+             model id; there is no network on the training boxes): first ``num_layers - skip_last`` layers (the
+             others are never loaded), bf16, SDPA attention, the last hidden state; MoE blocks fused
+             (models/moe_infer.py). Remote code written for transformers 4 (the Poziomka BailingMoeV2 model) runs
+             under transformers 5 through ``transformers5_compat`` (reference aurora/hf_compat.py:21-59).
 * ``random`` a fixed random embedding table of the LM's width (seeded): stands in for a pretrained LM in smoke
              runs and tests where no weights exist. Rows of PAD / NULL ids get zeros.
 * ``states`` none: the caller passes states directly (the synthetic benchmarks).
@@ -34,18 +36,67 @@ class RandomFrozenLM:
         return h.masked_fill(special[..., None], 0)
 
 
+def _rope_inv_freq(config, device=None):
+    """Plain RoPE inverse frequencies theta^(-2i / d), i < d / 2, with d = head_dim * partial_rotary_factor; theta and
+    the factor are read from the config, or from the rope_scaling / rope_parameters dicts where transformers 5 keeps
+    them. Returns (inv_freq, attention scaling 1.0), the signature of transformers' RoPE init functions."""
+    extra = {}
+    for name in ("rope_parameters", "rope_scaling"):
+        d = getattr(config, name, None)
+        if isinstance(d, dict):
+            extra.update(d)
+    theta = getattr(config, "rope_theta", None) or extra.get("rope_theta", 10000.0)
+    factor = getattr(config, "partial_rotary_factor", None) or extra.get("partial_rotary_factor", 1.0)
+    head_dim = getattr(config, "head_dim", None) or config.hidden_size // config.num_attention_heads
+    dim = int(head_dim * factor)
+    exponents = torch.arange(0, dim, 2, dtype=torch.float32, device=device) / dim
+    return 1.0 / (float(theta) ** exponents), 1.0
+
+
+def transformers5_compat():
+    """Let transformers-4 remote code run under transformers 5 (idempotent): the removed
+    ``import_utils.is_torch_fx_available`` answers False, and RoPE init type "default" (gone from
+    ``ROPE_INIT_FUNCTIONS``) is the plain rotary embedding of ``_rope_inv_freq``."""
+    import transformers.modeling_rope_utils as rope_utils
+    import transformers.utils.import_utils as import_utils
+    if not hasattr(import_utils, "is_torch_fx_available"):
+        import_utils.is_torch_fx_available = lambda: False
+    if "default" not in rope_utils.ROPE_INIT_FUNCTIONS:
+        rope_utils.ROPE_INIT_FUNCTIONS["default"] = lambda config, device=None, *a, **k: _rope_inv_freq(config, device)
+
+
+def refresh_rope_buffers(model, device=None):
+    """Models are built on the meta device and loaded from weights, so a RoPE module's non-persistent ``inv_freq``
+    buffer (not in the checkpoint) may hold uninitialised memory: recompute it from the module's own init function.
+    Returns the number of modules refreshed."""
+    n = 0
+    for mod in model.modules():
+        fn = getattr(mod, "rope_init_fn", None)
+        if callable(fn) and isinstance(getattr(mod, "inv_freq", None), torch.Tensor):
+            dev = device if device is not None else mod.inv_freq.device
+            inv, scale = fn(mod.config, dev)
+            mod.inv_freq = inv
+            if hasattr(mod, "original_inv_freq"):
+                mod.original_inv_freq = inv
+            mod.attention_scaling = scale
+            n += 1
+    return n
+
+
 class HFFrozenLM:
     """fused_moe: the LM's mixture-of-experts blocks run as stacked experts + grouped GEMMs (models/moe_infer.py),
     optionally with int8 expert weights (quant="int8")."""
 
     def __init__(self, repo, skip_last=0, device=None, fused_moe=True, quant=""):
-        from transformers import AutoModelForCausalLM
-        model = AutoModelForCausalLM.from_pretrained(repo, torch_dtype=torch.bfloat16, trust_remote_code=True,
-                                                     local_files_only=True)
-        layers = model.model.layers
-        keep = len(layers) - skip_last
-        model.model.layers = layers[:keep]
+        from transformers import AutoConfig, AutoModelForCausalLM
+        transformers5_compat()
+        cfg = AutoConfig.from_pretrained(repo, trust_remote_code=True, local_files_only=True)
+        keep = cfg.num_hidden_layers - skip_last
+        model = AutoModelForCausalLM.from_pretrained(repo, dtype=torch.bfloat16, trust_remote_code=True,
+                                                     local_files_only=True, attn_implementation="sdpa",
+                                                     num_hidden_layers=keep)
         self.model = model.model.to(device).eval().requires_grad_(False)
+        refresh_rope_buffers(self.model)
         if fused_moe:
             from .moe_infer import patch_moe_blocks
             patch_moe_blocks(self.model, quant=quant)

@@ -9,7 +9,8 @@ scale -> rows summed back per token. The grouped GEMM's tile schedule comes from
 (ops/gemm.py:gemm_grouped), so there is no host synchronisation and one launch per projection, whatever the
 routing.
 
-``patch_moe_blocks(model)`` finds transformers-style MoE blocks and replaces their forward. Two expert layouts:
+``patch_moe_blocks(model)`` finds transformers-style MoE blocks and replaces their forward (or, for blocks that route
+themselves and call ``moe_infer(x, topk_ids, topk_weight)``, only that method). Two expert layouts:
 an ``experts`` list of gate_proj / up_proj / down_proj MLPs (transformers 4), or one fused ``experts`` module
 holding ``gate_up_proj`` (E, 2I, H; gate rows first) and ``down_proj`` (E, H, I) tensors with a ``gate`` router module
 carrying ``weight``, ``top_k`` and ``norm_topk_prob`` (transformers 5). Shared experts: ``shared_experts`` (added),
@@ -84,22 +85,28 @@ class FusedMoE:
     def __call__(self, x):
         shape = x.shape
         x2 = x.reshape(-1, shape[-1])
-        N = x2.shape[0]
         w, idx = self.route(x2)
+        return self.combine(x2, idx, w).view(shape)
+
+    @torch.no_grad()
+    def combine(self, x2, idx, w):
+        """The expert part for a given routing: x2 (N, H), idx / w (N, k) expert ids and weights -> (N, H)."""
+        shape = x2.shape
+        N, k = idx.shape
         flat = idx.reshape(-1)
         order = flat.argsort(stable=True)
-        tok = order // self.k
+        tok = order // k
         counts = torch.bincount(flat, minlength=self.E)
-        offsets = torch.zeros(self.E + 1, dtype=torch.int32, device=x.device)
+        offsets = torch.zeros(self.E + 1, dtype=torch.int32, device=x2.device)
         offsets[1:] = counts.cumsum(0)
-        xs = x2.to(torch.bfloat16 if x.is_cuda else torch.float32)[tok]
+        xs = x2.to(torch.bfloat16 if x2.is_cuda else torch.float32)[tok]
         gu, dn = (w_.to(xs.dtype) for w_ in self._weights())
         ab = gemm_grouped(xs, gu, offsets)
         h = Fz.swiglu(ab)
         y = gemm_grouped(h.to(xs.dtype), dn, offsets, row_scale=w.reshape(-1)[order])
-        out = torch.zeros(N, shape[-1], dtype=torch.float32, device=x.device)
+        out = torch.zeros(N, shape[-1], dtype=torch.float32, device=x2.device)
         out.index_add_(0, tok, y.float())
-        return out.to(x.dtype).view(shape)
+        return out.to(x2.dtype)
 
 
 def _fused_experts(ex):
@@ -127,6 +134,20 @@ def patch_moe_blocks(model, quant=""):
         if not (_fused_experts(ex) or _expert_list(ex)):
             continue
         fused = FusedMoE.from_block(mod, quant=quant).to(gate.weight.device)
+        if callable(getattr(mod, "moe_infer", None)) and _expert_list(ex):
+            # DeepSeek / Bailing-style block: its forward routes (grouped top-k, scaling, ...) and then calls
+            # moe_infer(x, topk_ids, topk_weight) for the experts: only that part is replaced, the routing stays
+            # the model's own; the per-expert modules are dropped (the stacked weights replace them)
+            def moe_infer(x, topk_ids, topk_weight, _f=fused):
+                x2 = x.reshape(-1, x.shape[-1])
+                n = x2.shape[0]
+                return _f.combine(x2, topk_ids.reshape(n, -1), topk_weight.reshape(n, -1)).to(x.dtype)
+            mod.moe_infer = moe_infer
+            del mod.experts  # a registered child module: removed before a plain attribute can take the name
+            mod.experts = list(range(fused.E))  # len(self.experts) keeps working for the block's own code
+            mod._fused_moe = fused
+            n += 1
+            continue
         shared = getattr(mod, "shared_experts", None)
         shared_one = getattr(mod, "shared_expert", None)
         shared_gate = getattr(mod, "shared_expert_gate", None)
