@@ -21,10 +21,13 @@ def main(argv=None):
     p.add_argument("--time-shift-ref", type=float, default=None)
     p.add_argument("--vae-dir", default=None, help="local diffusers AutoencoderKLFlux2 directory to copy into vae/")
     p.add_argument("--tokenizer-json", default=None)
+    p.add_argument("--lm-dir", default=None, help="local Slayer LM directory (config.json + model.safetensors): "
+                   "its blocks the refiner reads are packed into text_encoder/, with its tokenizer.json")
     a = p.parse_args(argv)
     ck = ckpt.load(a.ckpt)
     index = export_checkpoint(ck, a.out, use_ema=not a.no_ema, time_shift=a.time_shift,
-                              time_shift_ref=a.time_shift_ref, vae_dir=a.vae_dir, tokenizer_json=a.tokenizer_json)
+                              time_shift_ref=a.time_shift_ref, vae_dir=a.vae_dir, tokenizer_json=a.tokenizer_json,
+                              lm_dir=a.lm_dir)
     print(f"exported step {index['step']} ({index['weights']} weights) to {a.out}")
 
 

@@ -208,3 +208,49 @@ def test_eval_suite_parts_resume_and_faces(tmp_path):
     paths = E.main(["faces", f"{exports[0]}:3", f"{exports[1]}:1", "--prompts", prompts, "--seeds", "0", "--res",
                     "64", "--steps", "2", "--cell", "32", "--out-dir", str(tmp_path / "faces"), "--device", "cpu"])
     assert Image.open(paths[0]).size == (220 + 3 * 32, 2 * 32)
+
+
+def test_export_packs_the_frozen_slayer_lm(tmp_path):
+    """export --lm-dir: the LM blocks the refiner reads (token embedding + n_layer - skip_last blocks) travel inside
+    text_encoder/ with their description and tokenizer; the export's pipeline samples from them alone and matches
+    sampling with the original LM directory."""
+    import json
+
+    from safetensors.torch import load_file, save_model
+
+    from trenowanie_generatora_obrazkow_b200.models import LMEncoderConfig
+    from trenowanie_generatora_obrazkow_b200.models.frozen_lm import SlayerFrozenLM
+    from trenowanie_generatora_obrazkow_b200.models.slayer import GPT, GPTConfig
+    torch.manual_seed(5)
+    gcfg = dict(vocab=64, n_layer=3, n_embd=48, n_head=2, block=64)
+    lm_dir = tmp_path / "slayer"
+    lm_dir.mkdir()
+    json.dump(gcfg, open(lm_dir / "config.json", "w"))
+    gpt = GPT(GPTConfig(**gcfg)).eval()
+    with torch.no_grad():
+        for p in gpt.parameters():
+            p.add_(0.02 * torch.randn_like(p))
+    save_model(gpt, str(lm_dir / "model.safetensors"))
+    _tokenizer(str(lm_dir / "tokenizer.json"))
+    den_cfg = DenoiserConfig(dim=64, depth=1, heads=1, mlp_hidden=128, text_dim=64, latent_channels=16, latent_size=4)
+    te_cfg = LMEncoderConfig(repo=str(lm_dir), tok_suffix="", lm_dim=48, skip_last=1, dim=64, depth=1, heads=1,
+                             kv_heads=1, head_dim=64, mlp_hidden=128, max_tokens=10, backend="slayer")
+    te, den = build_models(den_cfg, te_cfg)
+    ck = dict(den_config=asdict(den_cfg), te_config=asdict(te_cfg), te=te.state_dict(), den=den.state_dict(),
+              ema=None, step=3, args=dict(t_shift=1.0))
+    ex = str(tmp_path / "export")
+    export_checkpoint(ck, ex, lm_dir=str(lm_dir))
+    tensors = load_file(os.path.join(ex, "text_encoder", "diffusion_pytorch_model.safetensors"))
+    lm_keys = {k for k in tensors if k.startswith("lm.")}
+    assert "lm.tok.weight" in lm_keys and any(k.startswith("lm.blocks.1.") for k in lm_keys)
+    assert not any(k.startswith("lm.blocks.2.") for k in lm_keys)  # skip_last = 1: the last block is not packed
+    cfg = json.load(open(os.path.join(ex, "text_encoder", "config.json")))
+    assert cfg["lm_arch"] == "slayer" and cfg["lm_blocks"] == 2
+    assert os.path.exists(os.path.join(ex, "tokenizer", "tokenizer.json"))
+    pipe = HomeIMGPipeline.from_pretrained(ex, device="cpu")
+    prompts = ["a red fox in the snow"]
+    out = pipe(prompts, height=64, num_inference_steps=3, guidance_scale=3.0, seed=2, output_type="latent")
+    ref = HomeIMGPipeline.from_pretrained(ex, device="cpu",
+                                          frozen_lm=SlayerFrozenLM(str(lm_dir), skip_last=1, dtype=torch.float32))
+    want = ref(prompts, height=64, num_inference_steps=3, guidance_scale=3.0, seed=2, output_type="latent")
+    assert torch.allclose(out.latents, want.latents, atol=1e-5)

@@ -153,8 +153,10 @@ def make_configs(size: str, te_size: str, te_dim: int = None, te_depth: int = No
 
 
 def te_config_from_dict(d):
-    """Checkpoints from before te_config existed used the released text encoder."""
-    return LMEncoderConfig(**d) if d.get("kind") == "lm" else TextEncoderConfig(**d)
+    """Checkpoints from before te_config existed used the released text encoder. Keys that are not config fields
+    (an export's packed-LM description: lm_arch, lm_blocks, ...) are ignored."""
+    cls = LMEncoderConfig if d.get("kind") == "lm" else TextEncoderConfig
+    return cls(**{k: v for k, v in d.items() if k in cls.__dataclass_fields__})
 
 
 def configs_from_ckpt(ck):

@@ -58,6 +58,15 @@ class HomeIMGPipeline:
         if os.path.exists(tp):
             from tokenizers import Tokenizer
             tok = Tokenizer.from_file(tp)
+        if frozen_lm is None and isinstance(te, LMTextEncoder):  # the frozen LM blocks packed into the export
+            from safetensors.torch import load_file
+
+            from ..utils.export import packed_lm
+            with open(os.path.join(path, "text_encoder", "config.json")) as f:
+                te_json = json.load(f)
+            if te_json.get("lm_arch"):
+                frozen_lm = packed_lm(te_json, load_file(os.path.join(path, "text_encoder",
+                                                                      "diffusion_pytorch_model.safetensors")), device)
         if frozen_lm is None and isinstance(te, LMTextEncoder) and getattr(te_cfg, "backend", "states") != "states":
             try:
                 frozen_lm = build_frozen_lm(te_cfg, torch.device(device))
