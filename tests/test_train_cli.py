@@ -134,3 +134,45 @@ def test_train_selective_activation_checkpointing(tmp_path):
     for mode in (["--act-checkpoint", "selective"], ["--act-checkpoint"]):
         _run(["--synthetic", "16", "--out", out, "--size", "50m", "--te-size", "13m", "--batch", "2",
               "--micro-batch", "2", "--steps", "1", "--eval-every", "0", "--no-wandb", "--ckpt-every", "0"] + mode)
+
+
+def test_fid_per_shard_and_export_init(shards, tmp_path):
+    """--fid-every / --fid-at-start: Fréchet distance of EMA samples of held-out prompts during training (the
+    offline latent features); --eval-only --per-shard: the loss per held-out and training shard; --load-hf: start
+    from an export directory."""
+    out = str(tmp_path / "run")
+    common = ["--data", shards, "--fraction", "1", "--out", out, "--size", "nano", "--te-size", "13m", "--batch", "4",
+              "--micro-batch", "2", "--log-every", "1", "--eval-every", "0", "--ckpt-every", "2", "--val-samples",
+              "8", "--workers", "0", "--no-wandb"]
+    log = _run(common + ["--steps", "2", "--fid-every", "2", "--fid-at-start", "--fid-samples", "6", "--fid-steps",
+                         "2"])
+    fds = [line for line in log.splitlines() if " FD " in line]
+    assert len(fds) == 2 and "step 0 FD" in fds[0] and "step 2 FD" in fds[1], log[-2000:]
+    log = _run(common + ["--steps", "2", "--eval-only", "--per-shard", "4"])
+    assert log.count("per-shard") == 3 and "val" in log  # 1 held-out shard + the first / middle training shard
+    ex = str(tmp_path / "export")
+    subprocess.run([sys.executable, os.path.join(ROOT, "export.py"), os.path.join(out, "latest.pt"), ex], cwd=ROOT,
+                   check=True, capture_output=True, env=dict(os.environ, CUDA_VISIBLE_DEVICES=""))
+    log = _run(["--data", shards, "--fraction", "1", "--out", str(tmp_path / "run2"), "--size", "nano", "--te-size",
+                "13m", "--batch", "4", "--micro-batch", "2", "--steps", "1", "--eval-every", "0",
+                "--workers", "0", "--no-wandb", "--load-hf", ex, "--no-compile"])
+    assert "weights from the export" in log
+
+
+def test_diloco_gradient_noise_scale(shards, tmp_path):
+    """--diloco with --gns-every: two Gloo workers estimate the gradient noise scale on the first step after an
+    outer sync."""
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", "2", "--master-addr",
+           "127.0.0.1", "--master-port", str(port), os.path.join(ROOT, "train.py"), "--data", shards, "--fraction",
+           "1", "--out", str(tmp_path / "run"), "--size", "nano", "--te-size", "13m", "--batch", "4",
+           "--micro-batch", "2", "--steps", "4", "--diloco", "2", "--gns-every", "2", "--log-every",
+           "1", "--eval-every", "0", "--workers", "0", "--no-wandb", "--optimizer", "adamw"]
+    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=600,
+                       env=dict(os.environ, CUDA_VISIBLE_DEVICES="", DIST_BACKEND="gloo"))
+    assert r.returncode == 0, r.stderr[-3000:]
+    assert r.stdout.count("gradient noise scale") == 2, r.stdout[-2000:]

@@ -22,7 +22,7 @@ from dataclasses import asdict, replace
 import torch
 import torch.distributed as dist
 
-from trenowanie_generatora_obrazkow_b200.data.shards import (ShardStore, TrainStream, load_val, select_shards,
+from trenowanie_generatora_obrazkow_b200.data.shards import (ShardStore, TrainStream, load_val, select_shards, subsets,
                                                              val_groups)
 from trenowanie_generatora_obrazkow_b200.models import (SIZES, TE_SIZES, DenoiserConfig, LMEncoderConfig,
                                                         make_configs, te_config_from_dict)
@@ -134,7 +134,22 @@ def build_parser():
     a("--no-wandb", action="store_true")
     a("--eval-only", action="store_true")
     a("--init", default="", help="start from this checkpoint's EMA weights (ignored on resume)")
+    a("--load-hf", default="", help="start from an export directory (export.py layout; its weights, as --init)")
     a("--freeze-den", action="store_true")
+    a("--fid-every", type=int, default=0, help="Fréchet distance of EMA samples of held-out prompts every N steps "
+      "(features: DINOv2 of decoded images with --vae, else the offline latent stand-in); 0 = off")
+    a("--fid-at-start", action="store_true", help="also measure it before the first step")
+    a("--fid-samples", type=int, default=4096, help="held-out prompts per measurement (<= --val-samples)")
+    a("--fid-steps", type=int, default=50, help="Euler steps of the samples")
+    a("--fid-cfg", type=float, default=3.0, help="guidance scale of the samples")
+    a("--vae", default="", help="local FLUX.2 VAE directory: decoder of the DINOv2 features (FD) and REPA targets")
+    a("--repa-encoder", default="vit_base_patch14_reg4_dinov2.lvd142m", help="timm encoder of the DINOv2 features")
+    a("--gns-every", type=int, default=None, help="with --diloco: gradient noise scale (B_noise) from one worker's "
+      "vs the all-worker gradient on the first step after an outer sync, every N steps (default 8 x --diloco; "
+      "0 = off)")
+    a("--per-shard", type=int, default=0, help="--eval-only: also the loss of N samples of every held-out shard and "
+      "of the first and a middle training shard of every subset (generalisation vs memorisation)")
+    a("--no-compile", action="store_true", help="accepted for command-line compatibility: nothing is compiled here")
     return p
 
 
@@ -162,10 +177,15 @@ def resolve_defaults(args, world=1):
         args.mlm_weight = 0.0
     if args.repa_layer is None:
         args.repa_layer = max(1, round(0.3 * (args.depth or SIZES[args.size].depth)))
+    if args.gns_every is None:
+        args.gns_every = 8 * args.diloco
+    if args.vae and args.repa_target == "latent":
+        args.repa_target = args.vae
     if args.diloco:
         up = lambda n: n and -(-n // args.diloco) * args.diloco
         args.eval_every, args.ckpt_every = up(args.eval_every), up(args.ckpt_every)
         args.merge_every, args.keep_every = up(args.merge_every), up(args.keep_every)
+        args.fid_every = up(args.fid_every)
     return args
 
 
@@ -276,6 +296,12 @@ def main():
         init = ckpt.load(args.init)
         ckpt.load_weights(init, te, den, use_ema=bool(init.get("ema")))
         log(f"init: weights from {args.init} (step {init.get('step')})")
+    elif args.load_hf:
+        from trenowanie_generatora_obrazkow_b200.utils.export import load_export
+        xte, xden, _, _, _ = load_export(args.load_hf)
+        te.load_state_dict(xte.state_dict())
+        den.load_state_dict(xden.state_dict())
+        log(f"init: weights from the export {args.load_hf}")
     del resume
     n_den, n_te = tr.n_params()
     log(f"params: denoiser {n_den / 1e6:.1f}M, text encoder {n_te / 1e6:.1f}M (trainable)")
@@ -317,6 +343,30 @@ def main():
         log(f"train: {len(train_names)} shards / {len(store):,} images, val: {len(val_names)} shards")
     lm_states_key = isinstance(te_cfg, LMEncoderConfig) and te_cfg.backend == "states"
 
+    # ---- Fréchet distance of samples during training (every rank generates a slice of the held-out prompts) ------
+    fid = None
+    if args.fid_every or args.fid_at_start:
+        from trenowanie_generatora_obrazkow_b200.train.fid import (DinoFeatures, LatentFeatures, TrainingFD,
+                                                                   my_prompts)
+        if args.synthetic:
+            held = next(iter(SyntheticStream(args.synthetic, side, te_cfg, min(args.val_samples, 64), 10 ** 6,
+                                             args.seed + 1)))
+        else:
+            held = load_val(args.data, val_names, args.val_samples, tok_suffix, null_row) if val_names else None
+        if held is None:
+            log("--fid-every: no held-out shards, Fréchet distance off")
+        else:
+            lat, prompts = held
+            n = min(args.fid_samples, len(lat))
+            mine = my_prompts(n, rank, world)
+            feats = DinoFeatures(args.vae, args.repa_encoder, device) if args.vae else \
+                LatentFeatures(den_cfg.latent_channels, seed=args.seed)
+            fd_shift = args.res / args.t_shift_ref if args.t_shift_ref else args.t_shift
+            fid = TrainingFD(lat[mine].float(), prompts[mine], n, feats, args.fid_steps, args.fid_cfg, fd_shift,
+                             args.seed, lm=isinstance(te_cfg, LMEncoderConfig), frozen_lm=tr.frozen_lm)
+            log(f"Fréchet distance of {n} held-out prompts every {args.fid_every} steps "
+                f"({'DINOv2 ' + args.repa_encoder if args.vae else 'latent stand-in'} features)")
+
     logger = RunLogger(args.out, vars(args), enabled=master and not args.no_wandb, project=args.wandb)
     peak = args.peak_tflops or (peak_tflops(torch.cuda.get_device_name(device)) if device.type == "cuda" else 0)
     flops_sample = train_flops_per_sample(den_cfg, te_cfg, side * side)
@@ -331,24 +381,50 @@ def main():
         if args.keep_every and step % args.keep_every == 0:
             ckpt.save_snapshot(args.out, step, den_cfg, te_cfg, te, den, tr.ema)
 
-    def run_eval():
-        if val is None:
-            return {}
+    def with_ema(fn):
+        """fn() with the EMA weights in place of the live ones (restored afterwards)."""
         swap = [p.detach().clone() for p in tr.params] if tr.ema is not None else None
         if swap is not None:
             tr.ema.copy_to()
-        res = evaluate(te, den, val, device, groups=groups)
-        if swap is not None:
-            with torch.no_grad():
-                for p, s in zip(tr.params, swap):
-                    p.copy_(s)
-        return res
+        try:
+            return fn()
+        finally:
+            if swap is not None:
+                with torch.no_grad():
+                    for p, s in zip(tr.params, swap):
+                        p.copy_(s)
+
+    def run_eval():
+        if val is None:
+            return {}
+        return with_ema(lambda: evaluate(te, den, val, device, groups=groups))
+
+    def run_fid():
+        fd = with_ema(lambda: fid(te, den, device))
+        log(f"step {step} FD {fd:.3f}")
+        logger.log({"val/fd": fd}, step)
 
     if args.eval_only:
         log(json.dumps(run_eval(), indent=1))
+        if args.per_shard and master and not args.synthetic:
+            # held-out shards, then the first and a middle training shard of every subset: a loss much lower on
+            # the training shards than on the held-out ones means memorisation rather than generalisation
+            picks = [("val", n) for n in val_names]
+            for sub, names in sorted(subsets(train_names).items()):
+                for n in dict.fromkeys([names[0], names[len(names) // 2]]):
+                    picks.append((f"train {sub}", n))
+            for kind, name in picks:
+                shard_val = load_val(args.data, [name], args.per_shard, tok_suffix, null_row)
+                loss = with_ema(lambda: evaluate(te, den, shard_val, device))["val/loss"]
+                log(f"per-shard {kind:>16s} {name}: loss {loss:.4f} ({len(shard_val[0])} samples)")
+        if fid is not None:
+            run_fid()
         if distributed:
             dist.destroy_process_group()
         return
+
+    if fid is not None and args.fid_at_start:
+        run_fid()
 
     t0, acc, nacc = time.time(), 0.0, 0
     def gather(micros):
@@ -368,8 +444,15 @@ def main():
             batch = {"groups": groups}
         else:
             batch = gather([next(loader) for _ in range(tr.accum)])
+        if args.diloco and distributed and args.gns_every and step % args.diloco == 0 and step % args.gns_every == 0:
+            tr.gns_request = True  # the first step after an outer sync: all workers start from the same weights
         loss = tr.step(batch)
         step += 1
+        if tr.last_gns is not None:
+            log(f"step {step} gradient noise scale B_noise {tr.last_gns['b_noise']:.1f} (|G|^2 "
+                f"{tr.last_gns['g2']:.3e}, tr S {tr.last_gns['trace']:.3e})")
+            logger.log({"train/gns_b_noise": tr.last_gns["b_noise"]}, step)
+            tr.last_gns = None
         samples += args.batch
         acc += loss.detach()
         nacc += 1
@@ -398,6 +481,8 @@ def main():
             if res:
                 log(" ".join(f"{k} {v:.4f}" for k, v in res.items()))
                 logger.log(res, step)
+        if fid is not None and args.fid_every and (step % args.fid_every == 0 or step == args.steps):
+            run_fid()  # collective: every rank samples its slice
         if args.merge_every and step >= args.merge_start * args.steps and step % args.merge_every == 0 and master:
             ckpt.save_merge(args.out, step, args.steps, den_cfg, te_cfg, te, den)
         if (args.ckpt_every and step % args.ckpt_every == 0) or step == args.steps:

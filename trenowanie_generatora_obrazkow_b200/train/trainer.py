@@ -162,6 +162,7 @@ class Trainer:
         if self.repa_proj is not None:  # projector: AdamW, outside the EMA and the exported model
             self.named += [("repa_proj", n, p) for n, p in self.repa_proj.named_parameters()]
         self.params = [p for _, _, p in self.named if p.requires_grad]
+        self.gns_request, self.last_gns = False, None  # set gns_request before a step to measure the noise scale
         reduce_grads = not cfg.diloco
         eids = {id(p) for p in self.expert_params}
         mdt = torch.bfloat16 if cfg.muon_momentum_dtype == "bf16" else None
@@ -381,6 +382,15 @@ class Trainer:
             self.muon_buckets.finish()
         if self.expert_params and self.world > 1:  # their gradients summed every rank's loss: make it the mean
             torch._foreach_mul_([p.grad for p in self.expert_params if p.grad is not None], 1.0 / self.world)
+        if self.gns_request and cfg.diloco and self.world > 1:
+            # gradient noise scale (McCandlish et al. 2018): this worker's gradient (its share of the batch) against
+            # the mean over workers (the global batch), one extra bucketed all-reduce (reference train.py:937-960)
+            from .evaluate import grad_sq_norms, noise_scale
+            grads = [p.grad for p in self.params if p.grad is not None]
+            small, big = grad_sq_norms(grads, self.world, group=self.group)
+            g2, sig = noise_scale(small, big, total, total * self.world)
+            self.last_gns = dict(b_noise=(sig / g2.clamp_min(1e-30)).item(), g2=g2.item(), trace=sig.item())
+            self.gns_request = False
         if timer is not None:
             timer.mark("grad_sync_exposed")  # reductions still running after the last backward kernel
         coef = None
