@@ -5,6 +5,7 @@
   python prepare_data.py tokenize --data data/x --tokenizer path/tokenizer.json
   python prepare_data.py tokenize --data data/x --encoder slayer149 --tokenizer path/tokenizer.json [--lang pl]
   python prepare_data.py tokenize-parquet --parquet-dir data/monet --encoder poziomka --tokenizer tok.json
+  python prepare_data.py tokenize-hf --src captions_pl/ --out data/x --encoder poziomka --tokenizer tok.json
 
 convert: every <name>.npz with ``lat`` (N, 128, 16, 16) and ``caps`` becomes <name>.lat.npy (float16) and
 <name>.caps.json (the caption entries flattened to lists of strings), written through .tmp files with the .lat.npy
@@ -107,6 +108,10 @@ def cmd_convert(a):
                          "elsewhere and pass --src")
     os.makedirs(a.out, exist_ok=True)
     files = sorted(glob.glob(os.path.join(a.src, "**", "*.npz"), recursive=True))
+    if a.include:
+        files = [f for f in files if a.include in f]
+    if a.limit:
+        files = files[: a.limit]
     by_name = {os.path.basename(f)[: -len(".npz")]: f for f in files}
     save_json(os.path.join(a.out, "manifest.json"), {"shards": sorted(by_name)}, indent=0)
     keep = pick_fraction(list(by_name), a.fraction)
@@ -177,6 +182,78 @@ def cmd_tokenize(a):
             print(f"[{i + 1}/{len(futs)}] {name}: {n} images, {c} captions", flush=True)
 
 
+def tokenize_caption_table(path, out, tokenizer, encoder, caps_only=False):
+    """One parquet of translated captions (columns shard, row, captions_en, captions_pl, pl_flagged: one row per
+    image that has captions) -> for every shard named in it, in the layout ``tokenize`` writes: <shard>.caps.json
+    (per image its English captions), and unless caps_only <shard>.off.npy, .tok_<encoder>.npy (English) and
+    .tok_<encoder>_pl.npy (Polish; a flagged or empty translation falls back to its English caption). The image
+    count of a shard comes from its .img.off.npy when present, else from the largest row. Returns
+    [(shard, images, captions, English fallbacks)]."""
+    import pyarrow.parquet as pq
+    table = pq.read_table(path).to_pylist()
+    shards = {}
+    for r in table:
+        shards.setdefault(r["shard"], {})[int(r["row"])] = r
+    width, bos, pad = ENCODERS[encoder]["width"], ENCODERS[encoder]["bos"], ENCODERS[encoder]["pad"]
+    tok = None
+    if not caps_only:
+        from tokenizers import Tokenizer
+        tok = Tokenizer.from_file(tokenizer)
+    done = []
+    for shard in sorted(shards):
+        rows = shards[shard]
+        img_off = os.path.join(out, shard + ".img.off.npy")
+        n = len(np.load(img_off)) - 1 if os.path.exists(img_off) else max(rows) + 1
+        if max(rows) >= n:
+            raise ValueError(f"{shard}: a caption for image {max(rows)} but the shard has {n} images")
+        caps, en, pl, fallback = [], [], [], 0
+        off = np.zeros(n + 1, dtype=np.int64)
+        for i in range(n):
+            mine = []
+            r = rows.get(i)
+            if r is not None:
+                flags = r.get("pl_flagged") or [False] * len(r["captions_en"])
+                for e, t, bad in zip(r["captions_en"], r.get("captions_pl") or [None] * len(r["captions_en"]), flags):
+                    e = " ".join((e or "").split())
+                    if not e:
+                        continue
+                    use_en = bool(bad) or not (t and str(t).strip())
+                    mine.append(e)
+                    en.append(e)
+                    pl.append(e if use_en else " ".join(str(t).split()))
+                    fallback += use_en
+            caps.append(mine)
+            off[i + 1] = len(en)
+        save_json(os.path.join(out, shard + ".caps.json"), caps, ensure_ascii=False)
+        if not caps_only:
+            for texts, suffix in ((en, f".tok_{encoder}.npy"), (pl, f".tok_{encoder}_pl.npy")):
+                rows_np = np.full((len(texts), width), pad, dtype=np.uint16)
+                for j, e in enumerate(tok.encode_batch(texts, add_special_tokens=False) if texts else []):
+                    ids = e.ids[: width - 1]
+                    rows_np[j, 0], rows_np[j, 1:1 + len(ids)] = bos, ids
+                save_npy(os.path.join(out, shard + suffix), rows_np)
+            save_npy(os.path.join(out, shard + ".off.npy"), off)  # last: the shard is tokenised
+        done.append((shard, n, len(en), fallback))
+    return done
+
+
+def cmd_tokenize_hf(a):
+    if a.download:
+        raise SystemExit("tokenize-hf --download needs the Hugging Face Hub (no network here): download the caption "
+                         "parquets elsewhere and pass --src")
+    if not a.caps_only and not a.tokenizer:
+        raise SystemExit("tokenize-hf: --tokenizer (the encoder's tokenizer.json) is needed unless --caps-only")
+    files = sorted(glob.glob(os.path.join(a.src, "**", "*.parquet"), recursive=True))
+    os.makedirs(a.out, exist_ok=True)
+    print(f"{len(files)} caption parquets -> {a.out}", flush=True)
+    with ProcessPoolExecutor(a.workers) as ex:
+        futs = [ex.submit(tokenize_caption_table, f, a.out, a.tokenizer, a.encoder, a.caps_only) for f in files]
+        for i, fut in enumerate(as_completed(futs)):
+            got = fut.result()
+            print(f"[{i + 1}/{len(futs)}] {len(got)} shards, {sum(g[1] for g in got):,} images, "
+                  f"{sum(g[2] for g in got):,} captions, {sum(g[3] for g in got):,} Polish -> English", flush=True)
+
+
 def cmd_tokenize_parquet(a):
     import pyarrow.parquet as pq
     files = sorted(f for f in glob.glob(os.path.join(a.parquet_dir, "**", "*.parquet"), recursive=True)
@@ -203,6 +280,8 @@ def main(argv=None):
     s.add_argument("--out", default="data/aurora")
     s.add_argument("--src", required=True)
     s.add_argument("--download", action="store_true")
+    s.add_argument("--include", default="", help="only shards whose path contains this string")
+    s.add_argument("--limit", type=int, default=0, help="only the first N shards (tests)")
     s.add_argument("--fraction", type=float, default=0.1)
     s.add_argument("--delete-raw", action="store_true")
     s.add_argument("--workers", type=int, default=4)
@@ -213,6 +292,16 @@ def main(argv=None):
     s.add_argument("--lang", default="")
     s.add_argument("--workers", type=int, default=8)
     s.add_argument("--force", action="store_true")
+    s = sub.add_parser("tokenize-hf", help="translated-caption parquets (shard, row, captions_en, captions_pl, "
+                       "pl_flagged) -> captions + English and Polish token rows per shard")
+    s.add_argument("--out", required=True)
+    s.add_argument("--src", default="", help="local directory of the caption parquets (no Hub download offline)")
+    s.add_argument("--download", action="store_true")
+    s.add_argument("--caps-only", action="store_true",
+                   help="only <shard>.caps.json (English captions for OPD), when the token rows already exist")
+    s.add_argument("--encoder", choices=sorted(ENCODERS), default="poziomka")
+    s.add_argument("--tokenizer", default="", help="the encoder's tokenizer.json")
+    s.add_argument("--workers", type=int, default=8)
     s = sub.add_parser("tokenize-parquet")
     s.add_argument("--parquet-dir", required=True)
     s.add_argument("--tokenizer", required=True)
@@ -221,7 +310,7 @@ def main(argv=None):
     s.add_argument("--lang", default="")
     a = p.parse_args(argv)
     {"inspect": cmd_inspect, "convert": cmd_convert, "tokenize": cmd_tokenize,
-     "tokenize-parquet": cmd_tokenize_parquet}[a.cmd](a)
+     "tokenize-parquet": cmd_tokenize_parquet, "tokenize-hf": cmd_tokenize_hf}[a.cmd](a)
 
 
 if __name__ == "__main__":

@@ -67,3 +67,45 @@ def test_pack_images_roundtrip(tmp_path):
     from trenowanie_generatora_obrazkow_b200.data.shards import decode_image
     img = decode_image(data, 16)
     assert np.asarray(img).shape[-1] in (3, 16) or np.asarray(img).size > 0
+
+
+def test_convert_filters_and_tokenize_hf(tmp_path):
+    """convert --include / --limit pick source shards; tokenize-hf turns translated-caption parquets into the
+    captions, offsets and English / Polish token rows of each shard (flagged or empty translations fall back to
+    English, images without a row get no captions), --caps-only only the captions."""
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+    raw, out = tmp_path / "raw", tmp_path / "data"
+    raw.mkdir()
+    rng = np.random.default_rng(1)
+    for s in range(4):
+        np.savez(raw / f"{'a' if s < 2 else 'b'}-{s:05d}-of-00004.npz",
+                 lat=rng.standard_normal((2, 128, 16, 16)).astype(np.float32),
+                 caps=np.array(['["w6"]', '["w7"]'], dtype=object))
+    prepare_data.main(["convert", "--src", str(raw), "--out", str(out), "--fraction", "1", "--workers", "1",
+                       "--include", "b-", "--limit", "1"])
+    assert sorted(p.name for p in out.glob("*.lat.npy")) == ["b-00002-of-00004.lat.npy"]
+    src = tmp_path / "caps"
+    src.mkdir()
+    table = pa.table({"shard": ["s1", "s1", "s2"], "row": [0, 2, 1],
+                      "captions_en": [["w6 w7", "w8"], ["w9"], ["w10 w11"]],
+                      "captions_pl": [["w12", ""], ["w13"], ["w14"]],
+                      "pl_flagged": [[False, False], [True], [False]]})
+    pq.write_table(table, src / "part-0.parquet")
+    tok = _tokenizer(str(tmp_path / "tok.json"))
+    hf = tmp_path / "hf"
+    prepare_data.main(["tokenize-hf", "--src", str(src), "--out", str(hf), "--encoder", "slayer149", "--tokenizer", tok,
+                       "--workers", "1"])
+    caps = json.load(open(hf / "s1.caps.json"))
+    assert caps == [["w6 w7", "w8"], [], ["w9"]]
+    off = np.load(hf / "s1.off.npy")
+    assert off.tolist() == [0, 2, 2, 3]
+    en, pl = np.load(hf / "s1.tok_slayer149.npy"), np.load(hf / "s1.tok_slayer149_pl.npy")
+    assert en.shape == pl.shape == (3, 96) and en[0, 0] == 12285
+    assert en[0, 1:3].tolist() == [6, 7] and pl[0, 1] == 12            # translated
+    assert pl[1, 1] == 8 and pl[2, 1] == 9                             # empty / flagged -> English
+    assert json.load(open(hf / "s2.caps.json")) == [[], ["w10 w11"]]
+    only = tmp_path / "only"
+    prepare_data.main(["tokenize-hf", "--src", str(src), "--out", str(only), "--encoder", "slayer149", "--caps-only",
+                       "--workers", "1"])
+    assert (only / "s1.caps.json").exists() and not (only / "s1.off.npy").exists()
