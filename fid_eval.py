@@ -29,6 +29,12 @@ def main(argv=None):
     p.add_argument("--data", required=True)
     p.add_argument("--features", choices=["dino", "latent"], default="dino")
     p.add_argument("--vae", default="", help="local FLUX.2 VAE directory (--features dino)")
+    p.add_argument("--ref-vae", default="", help="decoder of the held-out (real) latents (default: --vae); fixing it "
+                   "while --vae changes compares decoders against one reference")
+    p.add_argument("--encoder", default="vit_base_patch14_reg4_dinov2.lvd142m", help="timm encoder (--features dino)")
+    p.add_argument("--lang", default="", help="caption language of the held-out prompts ('' = the original; pl = "
+                   "<shard>.tok_<enc>_pl.npy, frozen-LM text encoders only); images, noise and reference stay")
+    p.add_argument("--random-lm", action="store_true", help="frozen-LM encoders: random stand-in LM (smoke runs)")
     p.add_argument("--samples", type=int, default=4096)
     p.add_argument("--val-samples", type=int, default=4096)
     p.add_argument("--steps", type=int, default=50)
@@ -61,21 +67,33 @@ def main(argv=None):
         step = ck.get("step")
         del ck
         te.to(device).eval(), den.to(device).eval()
-        if isinstance(te_cfg, LMEncoderConfig):
-            raise SystemExit("fid_eval.py: frozen-LM text encoders need the LM's states; evaluate from train.py")
-        key = getattr(te_cfg, "tok_suffix", "")
+        lm = isinstance(te_cfg, LMEncoderConfig)
+        if a.lang and not lm:
+            raise SystemExit("fid_eval.py: --lang needs a frozen-LM text encoder (translated token rows)")
+        base = getattr(te_cfg, "tok_suffix", "")
+        key = base + (f"_{a.lang}" if a.lang else "")
         if key not in cache:
-            _, val_names = select_shards(a.data, 1.0, key)
+            # the held-out shards and images are chosen with the original rows; only the prompt rows change
+            _, val_names = select_shards(a.data, 1.0, base)
             lat, ids = load_val(a.data, val_names, a.val_samples, key, te.null_ids())
             n = min(a.samples, len(ids))
             mine = my_prompts(n, rank, world)
             cache[key] = (lat[mine], ids[mine], n)
         real, ids, n = cache[key]
-        feats = LatentFeatures(den_cfg.latent_channels, seed=a.seed) if a.features == "latent" else \
-            DinoFeatures(a.vae, device=device)
+        if a.features == "latent":
+            feats = ref_feats = LatentFeatures(den_cfg.latent_channels, seed=a.seed)
+        else:
+            feats = DinoFeatures(a.vae, a.encoder, device=device)
+            ref_feats = DinoFeatures(a.ref_vae, a.encoder, device=device) if a.ref_vae else feats
+        kw = dict(ids=ids.to(device))
+        if lm:  # frozen-LM refiner: the LM's states of the prompt rows
+            from trenowanie_generatora_obrazkow_b200.models.frozen_lm import LM_PAD, build_frozen_lm
+            flm = build_frozen_lm(te_cfg, device, allow_random=a.random_lm)
+            rows = ids.to(device)
+            kw = dict(lm_states=flm.states(rows), valid=rows.ne(LM_PAD))
         with torch.no_grad():  # noise fixed by (seed, batch of this rank's prompts), as the reference
-            z = sample(te, den, a.steps, a.cfg, a.seed, a.shift, batch=a.batch, ids=ids.to(device))
-        fd = fd_of_samples(z.cpu() if a.features == "latent" else z, real, n, feats)
+            z = sample(te, den, a.steps, a.cfg, a.seed, a.shift, batch=a.batch, **kw)
+        fd = fd_of_samples(z.cpu() if a.features == "latent" else z, real, n, feats, real_features=ref_feats)
         if rank == 0:
             res = dict(ckpt=path, step=step, weights="ema" if ema else "raw", fd=round(fd, 3), features=a.features,
                        samples=n, steps=a.steps, cfg=a.cfg)

@@ -75,3 +75,31 @@ def test_fid_eval_cli_latent_features(tmp_path):
     import json
     res = json.loads(open(out).read().splitlines()[0])
     assert res["samples"] == 6 and np.isfinite(res["fd"])
+
+
+def test_fid_eval_cli_frozen_lm_encoder_and_lang(tmp_path):
+    """fid_eval.py with a frozen-LM refiner: prompts through the LM's states (random stand-in LM), --lang reads the
+    translated token rows of the same held-out images."""
+    import json
+    import shutil
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    data = str(tmp_path / "data")
+    from trenowanie_generatora_obrazkow_b200.data.shards import write_synthetic_shards
+    names = write_synthetic_shards(data, n_shards=2, per_shard=8, side=16, lm_suffix="slayer149")
+    for n in names:
+        shutil.copy(os.path.join(data, f"{n}.tok_slayer149.npy"), os.path.join(data, f"{n}.tok_slayer149_pl.npy"))
+    run = str(tmp_path / "run")
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "train.py"), "--data", data, "--out", run, "--size", "nano",
+                        "--te-size", "slayer149", "--random-lm", "--batch", "2", "--micro-batch", "2", "--steps", "1",
+                        "--eval-every", "0", "--no-wandb", "--workers", "0"], cwd=ROOT, capture_output=True, text=True,
+                       env=env, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    out = str(tmp_path / "fd.jsonl")
+    for lang in ("", "pl"):
+        r = subprocess.run([sys.executable, os.path.join(ROOT, "fid_eval.py"), os.path.join(run, "latest.pt"), "--data",
+                            data, "--features", "latent", "--samples", "4", "--steps", "2", "--random-lm", "--lang",
+                            lang, "--out", out], cwd=ROOT, capture_output=True, text=True, env=env, timeout=600)
+        assert r.returncode == 0, r.stderr[-2000:]
+    res = [json.loads(line) for line in open(out).read().splitlines()]
+    assert len(res) == 2 and all(np.isfinite(x["fd"]) for x in res)
+    assert abs(res[0]["fd"] - res[1]["fd"]) < 1e-6  # identical rows under both names: the same distance
