@@ -97,6 +97,8 @@ def main(argv=None):
     p.add_argument("--host", default="0.0.0.0")
     p.add_argument("--gpu", type=int, default=0)
     p.add_argument("--res", type=int, default=1024)
+    p.add_argument("--cfg", type=float, default=3.0, help="default guidance value of the page; 1 for guidance-distilled "
+                   "models (train_pp.py --dance-opd / --diffusion-opd)")
     a = p.parse_args(argv)
     import torch
     import uvicorn
@@ -105,7 +107,7 @@ def main(argv=None):
     device = f"cuda:{a.gpu}" if torch.cuda.is_available() else "cpu"
     pipe = HomeIMGPipeline.from_pretrained(a.model, device=device)
     print(f"serving {a.model} on http://{lan_ip()}:{a.port}", flush=True)
-    uvicorn.run(build_app(pipe, a.res), host=a.host, port=a.port)
+    uvicorn.run(build_app(pipe, a.res, guidance=a.cfg), host=a.host, port=a.port)
 
 
 if __name__ == "__main__":

@@ -2,11 +2,12 @@
 is rewritten to --out (same relative path) without the embedding_* columns (and any other --drop prefixes), with a
 `caption_short` column: the shortest non-empty VLM caption of the row, by word count (the one to translate).
 
-  python prepare_monet.py --src raw/monet/z-image --out data/monet_z_image --workers 8
+  python prepare_monet.py --src raw/monet/v1.2.0/synthetic --source z-image --out data/monet_z_image --workers 8
 
 The reference reads the parquets straight from the Hugging Face Hub; there is no network here, so --src is a local
-copy of the dataset folder. Files already written are skipped (resume); each is written to a temporary name, zstd
-compressed, and renamed.
+copy of the dataset folder (with --source, the folder holding one directory per synthetic source, as on the Hub:
+z-image, flux-klein, flux-schnell). --max-files takes only the first N parquets (a test). Files already written
+are skipped (resume); each is written to a temporary name, zstd compressed, and renamed.
 """
 import argparse
 import glob
@@ -48,9 +49,18 @@ def main(argv=None):
     p.add_argument("--out", required=True)
     p.add_argument("--workers", type=int, default=8)
     p.add_argument("--drop", nargs="*", default=["embedding_"], help="column name prefixes to leave out")
+    p.add_argument("--source", default="", choices=["", "z-image", "flux-klein", "flux-schnell"],
+                   help="the synthetic source directory under --src (empty: --src is one source's folder)")
+    p.add_argument("--max-files", type=int, default=0, help="only the first N parquets (a test)")
     a = p.parse_args(argv)
-    files = sorted(glob.glob(os.path.join(a.src, "**", "*.parquet"), recursive=True))
-    jobs = [(f, os.path.join(a.out, os.path.relpath(f, a.src))) for f in files]
+    src = os.path.join(a.src, a.source) if a.source else a.src
+    if not os.path.isdir(src):
+        p.error(f"no such source folder: {src}")
+    files = sorted(glob.glob(os.path.join(src, "**", "*.parquet"), recursive=True))
+    if a.max_files:
+        files = files[:a.max_files]
+    print(f"{a.source or src}: {len(files)} parquet files -> {a.out}", flush=True)
+    jobs = [(f, os.path.join(a.out, os.path.relpath(f, src))) for f in files]
     rows = skipped = 0
     with ThreadPoolExecutor(a.workers) as ex:
         futs = [ex.submit(slim_one, s, d, tuple(a.drop)) for s, d in jobs]

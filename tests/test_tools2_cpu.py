@@ -116,3 +116,78 @@ def test_translate_and_export_captions(tmp_path):
     import pyarrow.parquet as pq
     rows = pq.read_table(tmp_path / "export" / "data" / "train-00000.parquet").to_pylist()
     assert n == 2 and rows[1]["captions_pl"][1] == "A CAT" and os.path.exists(tmp_path / "export" / "README.md")
+
+
+def test_blimp_eval_hf_overrides_and_int8_experts(tmp_path):
+    """An "hf:" transformers MoE model with --set (a config override: one active expert) and --quant int8 (stacked
+    int8 experts); the per-phenomenon summary comes from the rows' linguistics_term."""
+    import pytest
+    pytest.importorskip("transformers")
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import Qwen3MoeConfig, Qwen3MoeForCausalLM
+
+    blimp_eval = _script("blimp_eval")
+    words = "the cat dog sees sleep sleeps a".split()
+    vocab = {"<|endoftext|>": 0, "[UNK]": 1, **{w: i + 2 for i, w in enumerate(words)}}
+    tok = Tokenizer(models.WordLevel(vocab, unk_token="[UNK]"))
+    tok.pre_tokenizer = pre_tokenizers.Whitespace()
+    tok.save(str(tmp_path / "tok.json"))
+    cfg = Qwen3MoeConfig(vocab_size=32, hidden_size=64, intermediate_size=128, moe_intermediate_size=32,
+                         num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=16, num_experts=4,
+                         num_experts_per_tok=2, decoder_sparse_step=1, max_position_embeddings=64)
+    torch.manual_seed(0)
+    Qwen3MoeForCausalLM(cfg).save_pretrained(str(tmp_path / "moe"))
+    data = tmp_path / "blimp"
+    data.mkdir()
+    with open(data / "agreement.jsonl", "w") as f:
+        for g, b in [("the cat sleeps", "the cat sleep"), ("a dog sees the cat", "a dog see the cat")]:
+            f.write(json.dumps({"sentence_good": g, "sentence_bad": b, "UID": "agr",
+                                "linguistics_term": "subject_verb_agreement"}) + "\n")
+    spec = "hf:" + str(tmp_path / "moe")
+    sc = blimp_eval.Scorer(spec, str(tmp_path / "tok.json"), "cpu", overrides={"num_experts_per_tok": 1},
+                           quant="int8")
+    assert sc.model.config.num_experts_per_tok == 1
+    fused = [m._fused_moe for m in sc.model.modules() if hasattr(m, "_fused_moe")]
+    assert len(fused) == 2 and all(f.quant == "int8" and f.k == 1 for f in fused)
+    res = blimp_eval.main([spec, "--data", str(data), "--tokenizer", str(tmp_path / "tok.json"), "--device", "cpu",
+                           "--set", "num_experts_per_tok=1", "--quant", "int8"])
+    (key, r), = res.items()
+    assert key == spec + " {'num_experts_per_tok': 1} int8"
+    assert set(r["phenomena"]) == {"subject_verb_agreement"} and set(r["paradigms"]) == {"agr"}
+    assert blimp_eval.parse_overrides(["a=1", "b=x", "c=[1,2]"]) == {"a": 1, "b": "x", "c": [1, 2]}
+
+
+def test_prepare_monet_source_folder_and_max_files(tmp_path):
+    """--source picks one synthetic source's folder under --src (the Hub's layout); --max-files keeps the first N."""
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+
+    prepare_monet = _script("prepare_monet")
+    for src in ("z-image", "flux-klein"):
+        for i in range(3):
+            d = tmp_path / "synthetic" / src / f"part-{i}"
+            d.mkdir(parents=True)
+            pq.write_table(pa.table({"prompt": [f"{src}{i}"], "caption_florence-2-large": ["a cat"]}), d / "f.parquet")
+    prepare_monet.main(["--src", str(tmp_path / "synthetic"), "--source", "flux-klein", "--max-files", "2",
+                        "--out", str(tmp_path / "out"), "--workers", "1"])
+    got = sorted(os.listdir(tmp_path / "out"))
+    assert got == ["part-0", "part-1"]
+    assert pq.read_table(tmp_path / "out" / "part-1" / "f.parquet")["prompt"].to_pylist() == ["flux-klein1"]
+
+
+def test_export_captions_shards_per_file_and_card(tmp_path):
+    """--shards-per-file cuts the parquet files at shard boundaries; --repo / --source reach the dataset card."""
+    ex = _script("export_captions")
+    d = tmp_path / "shards"
+    d.mkdir()
+    for i, n in enumerate((2, 3, 1)):
+        json.dump([[f"cap {i}.{j}"] for j in range(n)], open(d / f"s{i}.caps.json", "w"))
+        json.dump([[f"PODPIS {i}.{j}"] for j in range(n)], open(d / f"s{i}.caps_pl.json", "w"))
+    n = ex.main(["--data", str(d), "--out", str(tmp_path / "e"), "--shards-per-file", "2",
+                 "--repo", "someone/captions-pl", "--source", "z-image"])
+    import pyarrow.parquet as pq
+    f0 = pq.read_table(tmp_path / "e" / "data" / "train-00000.parquet").to_pylist()
+    f1 = pq.read_table(tmp_path / "e" / "data" / "train-00001.parquet").to_pylist()
+    assert n == 6 and [r["shard"] for r in f0] == ["s0"] * 2 + ["s1"] * 3 and [r["shard"] for r in f1] == ["s2"]
+    card = open(tmp_path / "e" / "README.md").read()
+    assert 'load_dataset("someone/captions-pl"' in card and "MONET `z-image`" in card and "# captions-pl" in card

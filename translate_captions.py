@@ -176,9 +176,13 @@ def main(argv=None, translator=None):
     p.add_argument("--world", type=int, default=1)
     p.add_argument("--max-tokens", type=int, default=768)
     p.add_argument("--pilot", type=int, default=0, help="translate this many captions of the first shard, print pairs")
+    p.add_argument("--gpu-mem", type=float, default=0.85, help="fraction of GPU memory the engine may take")
+    p.add_argument("--max-num-seqs", type=int, default=1024, help="sequences decoded at once (engine default 256)")
+    p.add_argument("--max-batched-tokens", type=int, default=16384, help="tokens per scheduler step (prefill chunk)")
     a = p.parse_args(argv)
     assert bool(a.data) != bool(a.parquet_dir), "give --data or --parquet-dir"
-    translate = translator or vllm_translator(a.model, a.src, a.tgt, a.max_tokens)
+    translate = translator or vllm_translator(a.model, a.src, a.tgt, a.max_tokens, a.gpu_mem, a.max_num_seqs,
+                                              a.max_batched_tokens)
     if a.pilot:
         if a.data:
             caps = json.load(open(sorted(glob.glob(os.path.join(a.data, "*.caps.json")))[0]))
