@@ -13,6 +13,16 @@ Methods:
 Shards are split over the ranks (RANK / WORLD_SIZE, no collectives); finished outputs are skipped, so an interrupted
 run resumes; files are written to a temporary name and renamed; the next shard is read and the last one written by
 an I/O thread while the current one converts. --bench N times N batches of the first shard and writes nothing.
+
+VAE options (reference prepare_lowres.py:96-125):
+  --decoder DIR       decode with another AutoencoderKLFlux2's decoder (e.g. the small one, cheaper; its differences
+                      mostly vanish after the downscale); the encoder and the latent statistics stay --vae's.
+  --channels-last     NHWC activations for the VAE convolutions.
+  --cudnn-benchmark   let cuDNN time and pick its convolution algorithms.
+  --cpu-threads N     torch CPU threads per rank (torchrun sets 1; 0 leaves the setting alone).
+  --compile [MODE]    capture the decoder and the encoder into CUDA graphs, one per batch shape (the last batch of a
+                      shard is padded, so there is one shape); this project replays graphs where the reference
+                      uses torch.compile, and MODE is accepted for the same command line but has no effect.
 """
 import argparse
 import glob
@@ -25,10 +35,52 @@ import torch
 import torch.nn.functional as F
 
 
+class GraphedCall:
+    """fn(x) replayed from a CUDA graph captured per input shape / dtype (warm-up on a side stream, then capture);
+    the input is copied into the graph's static buffer and the returned tensor is the graph's static output, so
+    it is consumed before the next call. Off CUDA it calls fn directly."""
+
+    def __init__(self, fn):
+        self.fn, self.graphs = fn, {}
+
+    def __call__(self, x):
+        if x.device.type != "cuda":
+            return self.fn(x)
+        key = (tuple(x.shape), x.dtype)
+        if key not in self.graphs:
+            static = x.clone()
+            side = torch.cuda.Stream(x.device)
+            side.wait_stream(torch.cuda.current_stream(x.device))
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    self.fn(static)
+            torch.cuda.current_stream(x.device).wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                out = self.fn(static)
+            self.graphs[key] = (g, static, out)
+        g, static, out = self.graphs[key]
+        static.copy_(x)
+        g.replay()
+        return out
+
+
 class VaeResizer:
-    def __init__(self, vae_dir, device):
+    """decode (``dec``) -> bicubic antialiased downscale -> encode (``enc``), both sampling/vae.py objects. A
+    separate ``decoder_dir`` decodes with another VAE's decoder but the encoder's latent statistics."""
+
+    def __init__(self, vae_dir, device, decoder_dir="", channels_last=False, graphs=False, dec=None, enc=None):
         from trenowanie_generatora_obrazkow_b200.sampling.vae import LatentDecoder, LatentEncoder
-        self.dec, self.enc, self.device = LatentDecoder(vae_dir, device), LatentEncoder(vae_dir, device), device
+        self.enc = enc if enc is not None else LatentEncoder(vae_dir, device)
+        self.dec = dec if dec is not None else LatentDecoder(decoder_dir or vae_dir, device)
+        self.dec.mean, self.dec.std = self.enc.mean, self.enc.std  # one latent normalisation: the encoder's
+        self.device = device
+        if channels_last:
+            for m in (self.dec, self.enc):
+                m.vae.to(memory_format=torch.channels_last)
+        if graphs:
+            self.dec.vae.decode = GraphedCall(self.dec.vae.decode)
+            self.enc.vae.encode = GraphedCall(self.enc.vae.encode)
 
     @torch.no_grad()
     def __call__(self, lat, sizes):
@@ -85,12 +137,26 @@ def main(argv=None):
     p.add_argument("--batch", type=int, default=32)
     p.add_argument("--bench", type=int, default=0)
     p.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
+    p.add_argument("--decoder", default="", help="another AutoencoderKLFlux2 whose decoder makes the 256 px images")
+    p.add_argument("--channels-last", action="store_true", help="NHWC activations for the VAE")
+    p.add_argument("--cudnn-benchmark", action="store_true", help="let cuDNN pick its fastest conv algorithms")
+    p.add_argument("--cpu-threads", type=int, default=0, help="torch CPU threads per rank (0: leave torch's setting; "
+                   "torchrun sets 1, and 3 x 8 ranks suits a 24-core host)")
+    p.add_argument("--compile", nargs="?", const="default", default="",
+                   help="replay the VAE decoder / encoder from CUDA graphs (MODE has no effect)")
     a = p.parse_args(argv)
     assert all(s % 16 == 0 and s < 256 for s in a.sizes), "sizes must be multiples of 16, below 256"
     assert bool(a.vae) != a.latent_pool, "pick one method: --vae DIR or --latent-pool"
+    assert not (a.latent_pool and (a.decoder or a.channels_last or a.compile)), "VAE options need --vae"
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    if a.cpu_threads > 0:
+        torch.set_num_threads(a.cpu_threads)
+    torch.backends.cudnn.benchmark = a.cudnn_benchmark
     device = torch.device(a.device if a.device != "cuda" else f"cuda:{int(os.environ.get('LOCAL_RANK', 0))}")
-    conv = VaeResizer(a.vae, device) if a.vae else LatentPool(device)
+    if device.type == "cuda":
+        torch.cuda.set_device(device)
+    conv = (VaeResizer(a.vae, device, a.decoder, a.channels_last, bool(a.compile)) if a.vae
+            else LatentPool(device))
     shards = sorted(glob.glob(os.path.join(a.data, "*.lat.npy")))[rank::world]
     if a.bench:
         lat = np.load(shards[0], mmap_mode="r")

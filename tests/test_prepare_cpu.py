@@ -109,3 +109,37 @@ def test_convert_filters_and_tokenize_hf(tmp_path):
     prepare_data.main(["tokenize-hf", "--src", str(src), "--out", str(only), "--encoder", "slayer149", "--caps-only",
                        "--workers", "1"])
     assert (only / "s1.caps.json").exists() and not (only / "s1.off.npy").exists()
+
+
+def test_prepare_images_flux_reason_and_monet(tmp_path):
+    """flux-reason: the held-out shard always, --fraction of the training shards, staged through --tmp (left
+    empty), one worker process per shard, image counts checked against the caption offsets of --data; a second
+    run skips finished shards; monet packs the thumbnail column next to each parquet."""
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+
+    src, data = tmp_path / "src", tmp_path / "lat"
+    data.mkdir()
+    names = [f"art-{i:05d}-of-00004" for i in range(4)]
+    for i, n in enumerate(names):
+        (src / "art").mkdir(parents=True, exist_ok=True)
+        rows = [{"bytes": bytes([i, j]) * (j + 1)} for j in range(3)]
+        pq.write_table(pa.table({"image": rows}), src / "art" / f"{n}.parquet")
+        np.save(data / f"{n}.off.npy", np.arange(4, dtype=np.int64))
+    out, tmp = tmp_path / "out", tmp_path / "stage"
+    argv = ["flux-reason", "--src", str(src), "--out", str(out), "--data", str(data), "--fraction", "0.34",
+            "--workers", "2", "--tmp", str(tmp)]
+    assert prepare_images.main(argv) == 6  # 1 of 3 training shards (evenly spaced) + the held-out one, 3 images each
+    got = sorted(f[: -len(".img.off.npy")] for f in os.listdir(out) if f.endswith(".img.off.npy"))
+    assert got == [names[0], names[3]] and os.listdir(tmp) == []
+    assert prepare_images.read_packed(str(out / names[3]), 2) == bytes([3, 2]) * 3
+    assert prepare_images.main(argv) == 0  # resumed: nothing packed again
+    np.save(data / f"{names[1]}.off.npy", np.arange(3, dtype=np.int64))  # 2 caption rows for 3 images
+    with pytest.raises(ValueError, match="caption rows"):
+        prepare_images.main(["flux-reason", "--src", str(src), "--out", str(out), "--data", str(data),
+                             "--workers", "1", "--max-shards", "2"])
+    mon = tmp_path / "monet" / "part-0"
+    mon.mkdir(parents=True)
+    pq.write_table(pa.table({"thumbnail": [{"bytes": b"abc"}, {"bytes": b"de"}]}), mon / "f.parquet")
+    prepare_images.main(["monet", "--parquet-dir", str(tmp_path / "monet")])
+    assert prepare_images.read_packed(str(mon / "f"), 1) == b"de"

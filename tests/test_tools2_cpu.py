@@ -191,3 +191,54 @@ def test_export_captions_shards_per_file_and_card(tmp_path):
     assert n == 6 and [r["shard"] for r in f0] == ["s0"] * 2 + ["s1"] * 3 and [r["shard"] for r in f1] == ["s2"]
     card = open(tmp_path / "e" / "README.md").read()
     assert 'load_dataset("someone/captions-pl"' in card and "MONET `z-image`" in card and "# captions-pl" in card
+
+
+def test_prepare_lowres_vae_options_with_stand_in_vaes(tmp_path):
+    """VaeResizer with stand-in VAE objects: --decoder decodes with another object but the encoder's latent
+    statistics, --channels-last reaches both modules, --compile wraps the calls (direct calls off CUDA); the
+    latent-pool method rejects VAE options."""
+    import pytest
+    prepare_lowres = _script("prepare_lowres")
+
+    class Mod(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.w = torch.nn.Parameter(torch.ones(1, 1, 1, 1))
+            self.formats = []
+
+        def to(self, *a, memory_format=None, **k):
+            self.formats.append(memory_format)
+            return self
+
+        def decode(self, x):
+            return x
+
+        def encode(self, x):
+            return x
+
+    class Dec:
+        def __init__(self):
+            self.vae, self.mean, self.std = Mod(), None, None
+
+        def decode(self, z):  # uses the statistics it was given
+            img = (z * self.std + self.mean).mean(1, keepdim=True).repeat(1, 3, 16, 16)
+            return img.clamp(0, 255).permute(0, 2, 3, 1).to(torch.uint8).numpy()
+
+    class Enc:
+        def __init__(self):
+            self.vae, self.mean, self.std = Mod(), torch.tensor(7.0), torch.tensor(2.0)
+
+        def __call__(self, img):
+            return img.float()[:, :1].repeat(1, 128, 1, 1)[..., ::16, ::16]
+
+    dec, enc = Dec(), Enc()
+    r = prepare_lowres.VaeResizer("unused", "cpu", channels_last=True, graphs=True, dec=dec, enc=enc)
+    assert dec.mean is enc.mean and dec.std is enc.std
+    assert dec.vae.formats == [torch.channels_last] and enc.vae.formats == [torch.channels_last]
+    assert isinstance(dec.vae.decode, prepare_lowres.GraphedCall) and isinstance(enc.vae.encode,
+                                                                                 prepare_lowres.GraphedCall)
+    assert torch.equal(dec.vae.decode(torch.ones(2)), torch.ones(2))  # off CUDA: a direct call
+    out = r(np.zeros((2, 128, 16, 16), np.float32), [128])
+    assert out[128].shape == (2, 128, 8, 8) and np.allclose(out[128], 7.0)  # 0 * std + mean
+    with pytest.raises(AssertionError):
+        prepare_lowres.main(["--data", str(tmp_path), "--latent-pool", "--channels-last", "--device", "cpu"])

@@ -74,6 +74,16 @@ def test_export_import_roundtrip(tmp_path):
     assert index["transformer"][1] == "AuroraDenoiser" and index["weights"] == "EMA"
     tcfg = json.load(open(os.path.join(ex, "transformer", "config.json")))
     assert tcfg["time_shift"] == 3.0 and tcfg["dim"] == 640
+    # --ref: another export's vae/ and tokenizer/ are carried over
+    ref_dir = tmp_path / "released"
+    (ref_dir / "vae").mkdir(parents=True)
+    (ref_dir / "tokenizer").mkdir()
+    json.dump({"_class_name": "AutoencoderKLFlux2"}, open(ref_dir / "vae" / "config.json", "w"))
+    json.dump({"model": {"type": "BPE"}}, open(ref_dir / "tokenizer" / "tokenizer.json", "w"))
+    ex2 = str(tmp_path / "export2")
+    _py("export.py", os.path.join(run, "latest.pt"), ex2, "--ref", str(ref_dir))
+    assert json.load(open(os.path.join(ex2, "vae", "config.json")))["_class_name"] == "AutoencoderKLFlux2"
+    assert json.load(open(os.path.join(ex2, "tokenizer", "tokenizer.json")))["model"]["type"] == "BPE"
     init = str(tmp_path / "init.pt")
     _py("import_homeimg.py", ex, init)
     ck = torch.load(os.path.join(run, "latest.pt"), weights_only=False)
