@@ -254,3 +254,39 @@ def test_export_packs_the_frozen_slayer_lm(tmp_path):
                                           frozen_lm=SlayerFrozenLM(str(lm_dir), skip_last=1, dtype=torch.float32))
     want = ref(prompts, height=64, num_inference_steps=3, guidance_scale=3.0, seed=2, output_type="latent")
     assert torch.allclose(out.latents, want.latents, atol=1e-5)
+
+
+def test_sample_grid_from_an_export(tmp_path):
+    """sample.py: the 4 x 2 showcase grid from an export, one call per prompt with the same seed (a cell equals a
+    lone call of the pipeline), Polish prompts with --lang pl, latent previews without a VAE."""
+    import sys
+
+    import numpy as np
+    from PIL import Image
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import importlib.util
+
+    import eval_suite
+    spec = importlib.util.spec_from_file_location("_repo_sample", os.path.join(sys.path[0], "sample.py"))
+    S = importlib.util.module_from_spec(spec)  # by path: the installed reference has a sample.py of its own
+    spec.loader.exec_module(S)
+
+    den_cfg = DenoiserConfig(dim=32, depth=1, heads=1, mlp_hidden=64, text_dim=32, latent_channels=16, latent_size=4)
+    te_cfg = TextEncoderConfig(vocab_size=64, dim=32, depth=1, heads=1, kv_heads=1, mlp_hidden=64, max_tokens=12)
+    tok = str(tmp_path / "tokenizer.json")
+    _tokenizer(tok)
+    torch.manual_seed(0)
+    te, den = build_models(den_cfg, te_cfg)
+    ck = dict(den_config=asdict(den_cfg), te_config=asdict(te_cfg), te=te.state_dict(), den=den.state_dict(),
+              ema=None, step=0, args=dict(t_shift=1.0))
+    ex = str(tmp_path / "ex")
+    export_checkpoint(ck, ex, tokenizer_json=tok)
+    out = S.main([ex, "--out", str(tmp_path / "g" / "grid.png"), "--steps", "2", "--res", "64", "--seed", "3",
+                  "--lang", "pl", "--device", "cpu"])
+    g = np.asarray(Image.open(out))
+    assert g.shape == (2 * 64, 4 * 64, 3) and len(S.PROMPTS) == len(S.PROMPTS_PL) == 8
+    pipe = eval_suite.open_pipeline(ex, "cpu")
+    settings = dict(resolution=64, guidance_scale=3.0, time_shift=None, num_inference_steps=2)
+    cell = np.asarray(Image.fromarray(eval_suite.render(pipe, [S.PROMPTS_PL[5]], 3, settings)[0][0]).resize((64, 64)))
+    assert np.array_equal(g[64:, 64:128], cell)  # row 2, column 2: prompt 6 alone with seed 3
