@@ -242,6 +242,8 @@ def main():
                                    args.te_experts, args.te_quant)
     den_cfg = replace(den_cfg, latent_size=args.res // 16, rope_ref=args.rope_ref, micro_cond=args.micro_cond)
     ckpt_path = os.path.join(args.out, "latest.pt")
+    if master:  # a save cut short leaves only a temporary: removed, the previous latest.pt is the checkpoint
+        ckpt.recover_commit(args.out, log)
     resume = ckpt.load(ckpt_path) if os.path.exists(ckpt_path) else None
     if resume is not None:  # the checkpoint's architecture wins
         den_cfg = DenoiserConfig(**resume["den_config"])

@@ -362,7 +362,7 @@ def run_fm(args, den_cfg, te_cfg, lay, device, ctl, text_group):
     tr.model.act_checkpoint = args.act_checkpoint or False  # per block: "full" or "selective"
     if tr.first and args.te_checkpoint:
         tr.model.te_checkpoint = True
-    step, samples = pp_checkpoint.resume(tr, args.out, args.resume_opt_mismatch)
+    step, samples = pp_checkpoint.resume(tr, args.out, args.resume_opt_mismatch, group=learner_group)
     if step and tr.first and tr.replica == 0:
         print(f"[stage 0] resumed from {os.path.join(args.out, 'latest.pt')} at step {step}", flush=True)
     side, L = den_cfg.latent_size, te_cfg.max_tokens

@@ -5,11 +5,14 @@ names) to global rank 0 over a Gloo group; rank 0 writes ``latest.pt`` in the la
 export.py and merge.py read (te / den state dicts, the flat EMA list in the unsplit model's ``parameters()``
 order). Every learner rank writes its optimizer state to ``opt_stage{s}_rep{r}.pt`` together with the pipeline
 layout it belongs to. The commit is two-phase (every ``.tmp`` first, then the renames), so a crash mid-save leaves
-the previous checkpoint intact.
+the previous checkpoint intact; the ranks agree on the outcome of phase 1 (a rank whose write fails makes every rank
+drop its temporaries and raise), and a resume first finishes or undoes a commit a crash interrupted between its phases
+(utils/checkpoint.recover_commit).
 
 Resume (reference train_pp.py:1453-1500): any pipeline layout loads the weights and the EMA of ``latest.pt`` by
 name; the optimizer state only when the rank's file exists and its layout matches (pp, dp, the stage's block
-range); otherwise the run stops, unless ``resume_opt_mismatch`` asks for fresh optimizer state.
+range) and it was written at the step of ``latest.pt``; otherwise the run stops, unless ``resume_opt_mismatch`` asks
+for fresh optimizer state.
 """
 import os
 from dataclasses import asdict
@@ -65,15 +68,21 @@ def save(tr, out, step, samples, args, save_group, learner_group, keep=False):
                       opts=None, ema=[ema.get(k, params[k]) for k in order], args=dict(args or {}),
                       outer=None, repa_proj=None, pp_layout=dict(pp=tr.pp, dp=tr.dp))
             writes.append((ck, latest))
-    ckpt.two_phase_commit(writes, barrier=lambda: dist.barrier(group=learner_group))
+    ckpt.two_phase_commit(writes, agree=ckpt.agree_all(learner_group))
     if keep and dist.get_rank() == 0:
         ckpt.keep_hardlink(latest, step, out)
     dist.barrier(group=learner_group)
 
 
 @torch.no_grad()
-def resume(tr, out, resume_opt_mismatch=False, log=print):
-    """Load latest.pt (if any) into this rank's stage. Returns (step, samples) or (0, 0) without a checkpoint."""
+def resume(tr, out, resume_opt_mismatch=False, log=print, group=None):
+    """Load latest.pt (if any) into this rank's stage. Returns (step, samples) or (0, 0) without a checkpoint.
+    Collective over ``group`` (the learner ranks) when it is given: global rank 0 first repairs an interrupted commit
+    and the others wait for it."""
+    if group is not None:
+        if dist.get_rank() == 0 and os.path.isdir(out):
+            ckpt.recover_commit(out, log)
+        dist.barrier(group=group)
     latest = os.path.join(out, "latest.pt")
     if not os.path.exists(latest):
         return 0, 0
@@ -88,7 +97,8 @@ def resume(tr, out, resume_opt_mismatch=False, log=print):
             s.copy_(ema_by_name.get(k, ck[k[0]][k[1]]).to(s.device, s.dtype))
     path = opt_path(out, tr)
     opt = ckpt.load(path) if os.path.exists(path) else None
-    if opt is not None and opt.get("layout") == layout(tr) and len(opt["opts"]) == len(tr.opts):
+    same_step = opt is not None and int(opt.get("step", -1)) == int(ck.get("step", 0))
+    if opt is not None and opt.get("layout") == layout(tr) and len(opt["opts"]) == len(tr.opts) and same_step:
         for o, st in zip(tr.opts, opt["opts"]):
             ckpt.load_opt_state(o, st)
         if hasattr(tr, "after_load"):
@@ -97,8 +107,10 @@ def resume(tr, out, resume_opt_mismatch=False, log=print):
         log(f"[stage {tr.stage} replica {tr.replica}] optimizer state of {path} does not match this pipeline "
             "layout: starting it fresh (--resume-opt-mismatch)")
     else:
-        raise RuntimeError(f"{path}: optimizer state missing or written by another pipeline layout; pass "
-                           "--resume-opt-mismatch to resume the weights with fresh optimizer state")
+        why = ("missing" if opt is None else "written at another step than latest.pt" if not same_step else
+               "written by another pipeline layout")
+        raise RuntimeError(f"{path}: optimizer state {why}; pass --resume-opt-mismatch to resume the weights with "
+                           "fresh optimizer state")
     step = int(ck.get("step", 0))
     tr.step_idx = step
     return step, int(ck.get("samples", 0))

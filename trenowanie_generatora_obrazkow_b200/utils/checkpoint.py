@@ -7,11 +7,31 @@ optimizer) and repa_proj. ``snap_<step>.pt`` keeps weights + EMA; ``merge/step_<
 WSM merging. Pipeline runs write one ``opt_stage{s}.pt`` per stage and commit in two phases (all ``.tmp`` files
 first, then the renames), so a failed write leaves the previous state intact. Every write is ``.tmp`` +
 ``os.replace``.
+
+Failures (the reference stops on them and is rerun; train.py:819-831, train_pp.py:1749-1785): a write that fails
+(a full disk, a killed process) removes its partial ``.tmp`` and re-raises; in a multi-rank commit every rank learns
+through ``agree`` whether all parts were written, so a failure on one rank makes every rank drop its temporaries and
+raise instead of waiting at a barrier for a rank that will not come. ``recover_commit`` (run before a resume)
+finishes or undoes a commit that was interrupted between or during its phases, and an unreadable checkpoint (a
+truncated file) raises ``CheckpointError`` naming the file and the checkpoints that are still there.
 """
+import glob
 import os
+import pickle
 from dataclasses import asdict
 
 import torch
+
+
+class CheckpointError(RuntimeError):
+    pass
+
+
+def _remove(path):
+    try:
+        os.remove(path)
+    except FileNotFoundError:
+        pass
 
 
 def _sd(module):
@@ -19,9 +39,15 @@ def _sd(module):
 
 
 def atomic_save(obj, path):
+    """torch.save to ``path`` + ".tmp", then an atomic rename; on any failure the partial temporary is removed and
+    the previous ``path`` is left as it was."""
     tmp = path + ".tmp"
-    torch.save(obj, tmp)
-    os.replace(tmp, path)
+    try:
+        torch.save(obj, tmp)
+        os.replace(tmp, path)
+    except BaseException:
+        _remove(tmp)
+        raise
 
 
 def ema_list(te, den, ema):
@@ -61,15 +87,92 @@ def save_merge(out_dir, step, total_steps, den_cfg, te_cfg, te, den):
     return path
 
 
-def two_phase_commit(writes, barrier=None):
-    """writes: [(obj, path)] written to .tmp; after ``barrier()`` (every rank's temporaries are complete) all are
-    renamed. A crash before the renames leaves every previous file untouched."""
-    for obj, path in writes:
-        torch.save(obj, path + ".tmp")
-    if barrier is not None:
+def two_phase_commit(writes, barrier=None, agree=None):
+    """writes: [(obj, path)] written to .tmp (phase 1), then all renamed (phase 2). A crash before the renames leaves
+    every previous file untouched.
+
+    agree(ok) -> bool (every rank's phase 1 succeeded; a collective, see ``agree_all``) replaces ``barrier``: when any
+    rank failed, every rank removes its temporaries and raises (the failing rank its own error, the others
+    CheckpointError), so no rank is left waiting and nothing is committed. Without ``agree`` a failing rank removes
+    its temporaries and raises before the barrier."""
+    err = None
+    try:
+        for obj, path in writes:
+            torch.save(obj, path + ".tmp")
+    except Exception as e:  # a full disk, an unpicklable object, ...
+        err = e
+    ok = agree(err is None) if agree is not None else err is None
+    if not ok:
+        for _, path in writes:
+            _remove(path + ".tmp")
+        if err is not None:
+            raise err
+        raise CheckpointError("checkpoint not committed: another rank failed to write its part (the previous "
+                              "checkpoint is kept)")
+    if agree is None and barrier is not None:
         barrier()
     for _, path in writes:
         os.replace(path + ".tmp", path)
+
+
+def agree_all(group=None):
+    """``agree`` for two_phase_commit: an all-reduce of the ranks' failure flags over ``group`` (CPU tensor on
+    Gloo, the current CUDA device on NCCL)."""
+    import torch.distributed as dist
+
+    def agree(ok):
+        dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" else "cpu"
+        bad = torch.tensor([0 if ok else 1], dtype=torch.int32, device=dev)
+        dist.all_reduce(bad, group=group)
+        return int(bad.item()) == 0
+    return agree
+
+
+# files of the two-phase commit set: latest.pt and the per-rank optimizer files of pipeline runs
+COMMIT_SET = ("latest.pt", "opt_stage*_rep*.pt")
+
+
+def step_of(path):
+    """The ``step`` recorded in a checkpoint file, or None when the file is missing or unreadable."""
+    try:
+        return int(torch.load(path, map_location="cpu", weights_only=False, mmap=True).get("step", -1))
+    except Exception:
+        return None
+
+
+def recover_commit(out, log=print):
+    """Finish or undo a two-phase commit in ``out`` that a crash interrupted; run once (one rank) before resuming.
+
+    S = the newest step among readable commit-set temporaries. When some final file already holds step S, phase 2
+    had begun, which happens only after every rank's temporary was complete: the temporaries of step S are renamed
+    into place (roll forward). Otherwise the commit never reached phase 2: every temporary is removed and the
+    previous checkpoint stays (roll back). Leftover temporaries of single-file saves (snap_, merge/, step_) are
+    removed. Returns ("clean" | "forward" | "back", S)."""
+    tmps = sorted({t for pat in COMMIT_SET for t in glob.glob(os.path.join(out, pat + ".tmp"))})
+    for t in glob.glob(os.path.join(out, "*.pt.tmp")) + glob.glob(os.path.join(out, "merge", "*.pt.tmp")):
+        if t not in tmps:
+            _remove(t)
+    if not tmps:
+        return "clean", None
+    tmp_steps = {t: step_of(t) for t in tmps}
+    valid = [s for s in tmp_steps.values() if s is not None]
+    S = max(valid) if valid else None
+    finals = sorted({f for pat in COMMIT_SET for f in glob.glob(os.path.join(out, pat))})
+    final_steps = [step_of(f) for f in finals]
+    began = S is not None and S in final_steps and S >= max((s for s in final_steps if s is not None), default=S)
+    if began:
+        for t, s in tmp_steps.items():
+            if s == S:
+                os.replace(t, t[:-len(".tmp")])
+            else:
+                _remove(t)
+        log(f"{out}: finished an interrupted checkpoint commit of step {S}")
+        return "forward", S
+    for t in tmps:
+        _remove(t)
+    log(f"{out}: removed the temporaries of an unfinished checkpoint commit (step {S}); the previous checkpoint "
+        "is kept")
+    return "back", S
 
 
 def keep_hardlink(path, step, out_dir):
@@ -84,7 +187,18 @@ def keep_hardlink(path, step, out_dir):
 
 
 def load(path, map_location="cpu"):
-    return torch.load(path, map_location=map_location, weights_only=False, mmap=True)
+    """torch.load of a checkpoint (memory-mapped). A truncated or corrupt file raises CheckpointError naming the
+    checkpoints of its directory that remain."""
+    try:
+        return torch.load(path, map_location=map_location, weights_only=False, mmap=True)
+    except FileNotFoundError:
+        raise
+    except (RuntimeError, EOFError, OSError, ValueError, pickle.UnpicklingError) as e:
+        d = os.path.dirname(os.path.abspath(path))
+        others = sorted(os.path.basename(f) for f in glob.glob(os.path.join(d, "*.pt"))
+                        if os.path.abspath(f) != os.path.abspath(path))
+        raise CheckpointError(f"{path}: unreadable checkpoint ({type(e).__name__}: {str(e)[:200]}); it may have been "
+                              f"cut short by a crash or a full disk. Other checkpoints here: {others or 'none'}") from e
 
 
 def load_opt_state(opt, state):
