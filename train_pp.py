@@ -231,7 +231,7 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     lay = RankLayout(world_all, actors=actor_count(args), teachers=args.teacher_ranks, lm_servers=args.lm_rank,
                      vae_servers=args.vae_rank)
-    cuda = torch.cuda.is_available()
+    cuda = torch.cuda.is_available() and not os.environ.get("PP_CPU")  # PP_CPU=1: a CPU (Gloo) run on a GPU box
     if cuda:
         local = local_device(local_rank, torch.cuda.device_count(), lay, args.skip_gpus, args.lm_gpu, args.vae_gpu,
                              args.opd_actor_gpus, args.teacher_gpu)

@@ -3,7 +3,10 @@
 ``TrainingProfile`` costs nothing when disabled (no CUDA events, no synchronisation). When enabled it runs a
 ``torch.profiler`` window of ``steps`` optimizer steps starting at ``start`` on the selected ranks and labels the
 phases of a step with ``record_function('train/<phase>')``. ``export_profile`` writes a chrome trace, a per-kernel
-table that excludes the user annotations (so time is not double counted) and a per-op table with shapes.
+table that excludes the user annotations (so time is not double counted) and a per-op table with shapes. With
+``stacks`` (or PROFILE_STACK=1 in the environment) the profiler also records Python stacks, and ``stacks_rank<r>.txt``
+holds the collapsed stacks weighted by device time (CPU time on a CPU run; flame-graph input), while
+``ops_by_frame_rank<r>.txt`` lists the ops with the Python frame that issued them.
 """
 import contextlib
 import json
@@ -13,9 +16,10 @@ import torch
 
 
 class TrainingProfile:
-    def __init__(self, out_dir=None, start=0, steps=0, ranks=(0,), rank=0):
+    def __init__(self, out_dir=None, start=0, steps=0, ranks=(0,), rank=0, stacks=None):
         self.enabled = bool(out_dir) and steps > 0 and rank in ranks
         self.out_dir, self.start, self.steps, self.rank = out_dir, start, steps, rank
+        self.stacks = bool(os.environ.get("PROFILE_STACK")) if stacks is None else stacks
         self.prof = None
 
     def phase(self, name):
@@ -29,7 +33,8 @@ class TrainingProfile:
         acts = [torch.profiler.ProfilerActivity.CPU]
         if torch.cuda.is_available():
             acts.append(torch.profiler.ProfilerActivity.CUDA)
-        self.prof = torch.profiler.profile(activities=acts, record_shapes=True)
+        self.prof = torch.profiler.profile(activities=acts, record_shapes=True, with_stack=self.stacks,
+                                           experimental_config=_stack_config() if self.stacks else None)
         self.prof.__enter__()
 
     def step_end(self, step):
@@ -38,7 +43,7 @@ class TrainingProfile:
         if torch.cuda.is_available():
             torch.cuda.synchronize()
         self.prof.__exit__(None, None, None)
-        export_profile(self.prof, self.out_dir, self.rank)
+        export_profile(self.prof, self.out_dir, self.rank, stacks=self.stacks)
         self.prof = None
         self.enabled = False
 
@@ -59,7 +64,12 @@ def kernel_table(prof, top=40):
     return out[:top], total
 
 
-def export_profile(prof, out_dir, rank=0):
+def _stack_config():
+    """Keep Python stacks for every op (needed by export_stacks)."""
+    return torch._C._profiler._ExperimentalConfig(verbose=True)
+
+
+def export_profile(prof, out_dir, rank=0, stacks=False):
     os.makedirs(out_dir, exist_ok=True)
     prof.export_chrome_trace(os.path.join(out_dir, f"trace_rank{rank}.json"))
     table, total = kernel_table(prof, top=200)
@@ -69,6 +79,12 @@ def export_profile(prof, out_dir, rank=0):
     ops = prof.key_averages(group_by_input_shape=True)
     with open(os.path.join(out_dir, f"ops_rank{rank}.txt"), "w") as f:
         f.write(ops.table(sort_by="self_cpu_time_total", row_limit=200))
+    if stacks:
+        metric = "self_cuda_time_total" if torch.cuda.is_available() else "self_cpu_time_total"
+        prof.export_stacks(os.path.join(out_dir, f"stacks_rank{rank}.txt"), metric)
+        by_frame = prof.key_averages(group_by_stack_n=5)
+        with open(os.path.join(out_dir, f"ops_by_frame_rank{rank}.txt"), "w") as f:
+            f.write(by_frame.table(sort_by="self_cpu_time_total", row_limit=100))
     return table, total
 
 
