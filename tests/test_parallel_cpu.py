@@ -93,3 +93,27 @@ def test_grad_buckets_average():
     for a, b, r0g, r1g in zip(g0, g1, grads[0], grads[1]):
         assert torch.allclose(a, b)
         assert torch.allclose(a, (r0g + r1g) / 2, atol=1e-5)
+
+
+def _comm_check_worker(rank, world, port, out_dir):
+    _init(rank, world, port)
+    from trenowanie_generatora_obrazkow_b200.parallel import comm_check
+    res = comm_check.main(["--sizes", "0.25", "1", "--iters", "2", "--warmup", "1", "--model-params", "1e6"])
+    torch.save(res, os.path.join(out_dir, f"cc_{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_comm_check_on_gloo_ranks():
+    """parallel/comm_check.py (the reference's tests/check_nccl.py): correctness checks pass, bandwidth rows and a
+    per-step gradient estimate are reported, with the same (max-over-ranks) times on every rank."""
+    from trenowanie_generatora_obrazkow_b200.parallel import comm_check
+    assert comm_check.bus_bandwidth(2 ** 30, 1.0, 8) == pytest.approx(2 ** 30 * 2 * 7 / 8 / 1e9)
+    assert comm_check.grad_allreduce_ms(1e9, 100.0, 2) == pytest.approx(1e9 * 2 * 2 * 0.5 / 100e9 * 1e3)
+    assert comm_check.grad_allreduce_ms(1e9, 100.0, 1) == 0.0
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_comm_check_worker, args=(2, _free_port(), d), nprocs=2, join=True)
+        r0, r1 = (torch.load(os.path.join(d, f"cc_{r}.pt")) for r in range(2))
+    assert r0["world"] == 2 and r0["backend"] == "gloo" and [r["mb"] for r in r0["allreduce"]] == [0.25, 1]
+    assert all(r["busbw_gbs"] > 0 for r in r0["allreduce"])
+    assert [r["ms"] for r in r0["allreduce"]] == [r["ms"] for r in r1["allreduce"]]
+    assert r0["grad_allreduce_ms"]["pg:1e+06"] > 0
