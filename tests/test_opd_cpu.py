@@ -82,3 +82,31 @@ def test_learner_fresh_then_replay():
     assert learner.cache is first and torch.isfinite(torch.as_tensor(l1)) and torch.isfinite(torch.as_tensor(l2))
     learner.step_grads(2, st, valid, noise)  # reuse exhausted: fresh batch
     assert learner.cache is not first
+
+
+def test_installed_cache_with_deferred_teacher_matches_the_direct_path():
+    """The prefetch path (rollout_states, a deferred teacher request computed in chunks, install) trains on the same
+    states and targets as a fresh batch prepared inside step_grads, and a replay step needs no batch."""
+    grads = []
+    for deferred in (False, True):
+        te, den = _models(1)
+        tte, tden = _models(2)
+        teacher = DiTTeacher(tte, tden, cfg=3.0)
+        learner = OPDLearner(te, den, teacher, K=4, m=2, method="dance", shift=2.0, mb=2, reuse=2)
+        st = torch.randn(3, 8, 32, generator=torch.Generator().manual_seed(5))
+        valid = torch.ones(3, 8, dtype=torch.bool)
+        noise = torch.randn(3, 16, 4, 4, generator=torch.Generator().manual_seed(6))
+        if deferred:
+            states, t, kw = learner.rollout_states(0, st, valid, noise, 2.0)
+            learner.install(states, t, teacher.collect(teacher.request(states, t, kw, chunks=4)), kw)
+            assert not learner.needs_fresh
+            learner.step_grads(0)
+        else:
+            learner.step_grads(0, st, valid, noise, 2.0)
+        grads.append([p.grad.clone() for p in den.parameters() if p.grad is not None])
+        for p in den.parameters():
+            p.grad = None
+        learner.step_grads(1)  # replay: no batch arguments
+        assert learner.needs_fresh
+    for a, b in zip(*grads):
+        assert torch.allclose(a, b, rtol=1e-4, atol=1e-6)

@@ -125,3 +125,41 @@ def test_merge_assemble_streams_a_weighted_sum(tmp_path):
     assert torch.allclose(targets["den"]["b"].float(), torch.arange(4.0) * 1.75)
     table = M.candidate_table([0, 10, 20], 100, [0.15], ["mean"], ["wsm", "qam"])
     assert [sorted(c.weights) for c in table] == [[1, 2], [1, 2]]
+
+
+def test_ckpt_tools_info_block_norms_and_resume_cmd(tmp_path):
+    """ckpt_tools.py (the reference's tests/block_norms.py and tests/resume_cmd.py): block norms relative to the old
+    blocks, raw and EMA; a continuation command that keeps the stored settings, lets `--` flags replace them and
+    runs (here one step on CPU) from a copy of the checkpoint."""
+    import importlib.util
+    import shlex
+    import shutil
+
+    spec = importlib.util.spec_from_file_location("_repo_ckpt_tools", os.path.join(ROOT, "ckpt_tools.py"))
+    T = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(T)
+    run = str(tmp_path / "run")
+    _py("train.py", "--synthetic", "32", "--out", run, "--size", "nano", "--te-size", "13m", "--batch", "2",
+        "--micro-batch", "2", "--steps", "2", "--eval-every", "0", "--no-wandb", "--wd", "0.05")
+    latest = os.path.join(run, "latest.pt")
+    ck = torch.load(latest, weights_only=False)
+    res = T.main(["info", latest])
+    assert res["step"] == 2 and res["ema"] and res["den_params"] > 0
+    norms, depth = T.block_norms(ck, 2)
+    assert set(norms) == {"raw", "EMA"} and depth == 4
+    raw = dict(norms["raw"])
+    want = ck["den"]["blocks.3.mlp.out_proj.weight"].float().pow(2).mean().sqrt().item()
+    assert abs(raw[3]["mlp.out_proj.weight"][0] - want) < 1e-7
+    mean_old = sum(raw[i]["attn.out.weight"][0] for i in range(2)) / 2
+    assert abs(raw[0]["attn.out.weight"][1] - raw[0]["attn.out.weight"][0] / mean_old) < 1e-6
+    cont = str(tmp_path / "cont")
+    cmd = T.main(["resume-cmd", latest, "--out", cont, "--extra-steps", "1", "--nproc", "1", "--", "--wd", "0.1"])
+    args = shlex.split(cmd)
+    assert args[:6] == ["torchrun", "--nproc-per-node", "1", "--master-addr", "127.0.0.1", "train.py"]
+    assert "--size" in args and args[args.index("--size") + 1] == "nano"
+    assert args.count("--wd") == 1 and args[args.index("--wd") + 1] == "0.1"  # the `--` flag replaces the stored one
+    assert args[args.index("--steps") + 1] == "3" and args[args.index("--out") + 1] == cont
+    os.makedirs(cont)
+    shutil.copy(latest, os.path.join(cont, "latest.pt"))
+    _py(*args[5:])  # the same flags through the plain interpreter (one process)
+    assert torch.load(os.path.join(cont, "latest.pt"), weights_only=False)["step"] == 3

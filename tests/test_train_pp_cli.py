@@ -150,3 +150,15 @@ def test_pipeline_packed_images_local_encode(tmp_path):
                     "128", "--steps", "2", "--log-every", "2", "--random-lm", "--lm-layers", "2", "--workers", "0",
                     "--enc-chunk", "2")
     assert "step 2/2" in log and "data: images from" in log
+
+
+def test_opd_prefetch_with_a_teacher_rank(tmp_path):
+    """--opd-prefetch: the next cycle's rollouts are made after the first update of a cache and the teacher's reply
+    (computed in --opd-parts chunks on the teacher rank) is collected when that cycle starts; with reuse 2 over 5
+    steps the fresh batches start at steps 0, 2 and 4: step 0 as two --opd-parts requests, steps 2 and 4 prefetched
+    as one chunked request each, so the teacher serves 4 requests."""
+    out = _torchrun(2, "--out", str(tmp_path), "--size", "nano", "--te-size", "states-nano", "--dance-opd",
+                    "--teacher-ranks", "1", "--teacher-size", "nano", "--res", "128", "--batch", "4",
+                    "--micro-batch", "2", "--steps", "5", "--log-every", "1", "--opd-reuse", "2",
+                    "--opd-rollout-steps", "4", "--opd-prefetch", "--opd-parts", "2", "--opd-learner-profile")
+    assert "step 5/5" in out and "[teacher 1] served 4 requests" in out and "prefetch" in out

@@ -107,8 +107,9 @@ def build_parser():
     a("--opd-captions-only", action="store_true", help="OPD reads only captions from the shards (no latents)")
     a("--opd-balance-rollouts", action="store_true", help="round-robin the learners' rollout jobs over the actors")
     a("--opd-sort-rollouts", action="store_true", help="caption-length-sorted rollout batches")
-    a("--opd-prefetch", action="store_true", help="(rollout prefetch; not run here: rollouts are requested when the "
-      "replay budget of the cached ones is spent)")
+    a("--opd-prefetch", action="store_true", help="after a cache's first update, roll out the next cycle's batch and "
+      "leave its teacher request in flight during the replay updates; needs --opd-reuse > 1, local rollouts; the "
+      "rollouts are stale by reuse - 1 updates")
     a("--opd-parts", type=int, default=1, help="split each rollout batch into this many teacher requests")
     a("--teacher-ranks", type=int, default=0)
     a("--teacher-size", default="teacher-4b", choices=sorted(SIZES))
@@ -147,8 +148,7 @@ UNSUPPORTED = dict(diloco=(0, "DiLoCo / MuLoCo outer steps"), repa_weight=(0.0, 
                    "encoder"), te_quant=(None, "quantized text encoder"), pl_prob=(0.0, "Polish captions"),
                    rope_random=(False, "RPE-2D random positions"), length_sort=(False, "--length-sort"),
                    val_per_shard=(False, "validation per shard group (train.py --eval-every)"),
-                   img_extra=("", "a second image directory"), img_extra_val=(False, "validation on --img-extra"),
-                   opd_prefetch=(False, "rollout prefetch"))
+                   img_extra=("", "a second image directory"), img_extra_val=(False, "validation on --img-extra"))
 
 
 def check_flags(args):
@@ -166,6 +166,9 @@ def check_flags(args):
     if args.enc_vae and not args.vae:
         args.vae = args.enc_vae
     assert not args.crop_res or args.micro_cond, "--crop-res needs --micro-cond"
+    assert not args.opd_prefetch or ((args.dance_opd or args.diffusion_opd) and args.opd_reuse > 1
+                                     and not args.opd_actor), \
+        "--opd-prefetch needs OPD with --opd-reuse > 1 and local rollouts (no --opd-actor)"
     return args
 
 
@@ -578,21 +581,18 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         return cap_cache[step]
 
     lookahead = None
-    if args.opd_text_ahead:
+    if args.opd_text_ahead:  # fresh batches only: one every --opd-reuse steps
         lookahead = TextLookahead(lambda at: dict(ids=caption_ids(at), texts=[], step=at),
                                   lambda job: encode_remote(job, lay.lm_server_of(lrank), ctl, text_group),
-                                  0, args.steps, 1, args.opd_text_ahead)
-    version = 0
-    t0 = time.time()
-    for step in range(args.steps):
+                                  0, args.steps, args.opd_reuse, args.opd_text_ahead)
+
+    def fresh_data(step):
+        """(noise, LM states, valid) of the fresh batch that starts at ``step`` (replay steps draw nothing); seeded
+        by the step, so a prefetch draws the same batch the loop would."""
         res, B = batch_shape(step)
         side = res // 16
-        shift = resolution_shift(res, args.opd_resolutions, args.opd_res_shifts, args.t_shift_ref, args.t_shift,
-                                 args.res)
-        if args.opd_res_mb and args.opd_resolutions:
-            learner.mb = args.opd_res_mb[list(args.opd_resolutions).index(res)]
-        tp = time.time()
-        noise = torch.randn(B, den_cfg.latent_channels, side, side, generator=g).to(device)
+        gs = torch.Generator().manual_seed(args.seed * 1_000_003 + 7919 * rank + step)
+        noise = torch.randn(B, den_cfg.latent_channels, side, side, generator=gs).to(device)
         if lookahead is not None:
             job = lookahead.take(step)
             st, valid = job["lm"].to(device), job["ids"].ne(LM_PAD).to(device)
@@ -604,37 +604,66 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
             st = torch.cat([local_lm.states(c.to(device)).to(torch.bfloat16) for c in ids.split(args.micro_batch)])
             valid = ids.ne(LM_PAD).to(device)
         else:
-            st = torch.randn(B, L, te_cfg.lm_dim, generator=g).to(device)
+            st = torch.randn(B, L, te_cfg.lm_dim, generator=gs).to(device)
             valid = torch.ones(B, L, dtype=torch.bool, device=device)
         cap_cache.pop(step, None)
         if args.opd_sort_rollouts:  # caption-length-sorted batch (similar lengths share rollout micro-batches)
             order = valid.sum(1).argsort(stable=True)
             st, valid, noise = st[order], valid[order], noise[order]
-        if args.opd_balance_rollouts and actors:
-            actor = actors[(lrank + step) % len(actors)]
-        t_data = time.time() - tp
-        t_roll = t_teach = 0.0
+        return noise, st, valid
+
+    def step_shift(step):
+        res = batch_shape(step)[0]
+        return resolution_shift(res, args.opd_resolutions, args.opd_res_shifts, args.t_shift_ref, args.t_shift,
+                                args.res)
+
+    def teacher_targets(states, t, kw):
+        """Synchronous teacher targets of a fresh batch, in --opd-parts pieces."""
+        bounds = [(i * len(states) // args.opd_parts, (i + 1) * len(states) // args.opd_parts)
+                  for i in range(args.opd_parts)]
+        return torch.cat([teacher.velocity(states[a:b], t[a:b], {k: v[a:b] for k, v in kw.items()})
+                          for a, b in bounds if b > a])
+
+    version = 0
+    pending = None  # --opd-prefetch: the next cycle's rollouts, their teacher request in flight
+    t0 = time.time()
+    for step in range(args.steps):
+        res, B = batch_shape(step)
+        side = res // 16
+        shift = step_shift(step)
+        if args.opd_res_mb and args.opd_resolutions:
+            learner.mb = args.opd_res_mb[list(args.opd_resolutions).index(res)]
+        tp = time.time()
+        fresh = learner.needs_fresh
+        t_data = t_roll = t_teach = 0.0
         for p in params:
             p.grad = None
-        if actor is not None and (learner.cache is None or learner.uses >= learner.reuse):
-            if sender is not None:
-                version = sender.send()
-            tr0 = time.time()
-            states, t = actor.rollouts(noise, st, valid, step, version)
-            t_roll = time.time() - tr0
-            rep = lambda a: a.repeat_interleave(args.opd_states, dim=0)
-            kw_all = dict(lm_states=rep(st), valid=rep(valid))
+        if fresh and pending is not None:  # prepared during the last cycle's replay: collect the teacher's reply
+            assert pending["step"] == step, "a prefetched OPD batch must start the next cycle"
             tt0 = time.time()
-            bounds = [(i * len(states) // args.opd_parts, (i + 1) * len(states) // args.opd_parts)
-                      for i in range(args.opd_parts)]
-            target = torch.cat([teacher.velocity(states[a:b], t[a:b], {k: v[a:b] for k, v in kw_all.items()})
-                                for a, b in bounds if b > a])
+            learner.install(pending["x"], pending["t"], teacher.collect(pending["handle"]), pending["kw"])
             t_teach = time.time() - tt0
-            learner.cache = dict(x=states, t=t, target=target, text_kw=dict(lm_states=rep(st), valid=rep(valid)),
-                                 errors=None)
-            learner.uses = 0
+            pending = None
+        elif fresh:
+            noise, st, valid = fresh_data(step)
+            t_data = time.time() - tp
+            if args.opd_balance_rollouts and actors:
+                actor = actors[(lrank + step) % len(actors)]
+            rep = lambda a: a.repeat_interleave(args.opd_states, dim=0)
+            tr0 = time.time()
+            if actor is not None:
+                if sender is not None:
+                    version = sender.send()
+                states, t = actor.rollouts(noise, st, valid, step, version)
+                kw_all = dict(lm_states=rep(st), valid=rep(valid))
+            else:
+                states, t, kw_all = learner.rollout_states(step, st, valid, noise, shift)
+            t_roll = time.time() - tr0
+            tt0 = time.time()
+            learner.install(states, t, teacher_targets(states, t, kw_all), kw_all)
+            t_teach = time.time() - tt0
         tl0 = time.time()
-        loss = learner.step_grads(step, st, valid, noise, shift)
+        loss = learner.step_grads(step)
         t_learn = time.time() - tl0
         if n_learn > 1:
             for p in params:
@@ -645,6 +674,20 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         set_lr(opts, 1.0)
         for o in opts:
             o.step()
+        t_pref = 0.0
+        if args.opd_prefetch and pending is None and learner.uses == 1 and step + learner.reuse < args.steps:
+            # after the first update of a cache: the next cycle's rollouts with the weights of now (stale by
+            # reuse - 1 updates when trained on), its teacher request left in flight through the replay updates
+            tf0, nxt = time.time(), step + learner.reuse
+            mb_now = learner.mb
+            if args.opd_res_mb and args.opd_resolutions:
+                learner.mb = args.opd_res_mb[list(args.opd_resolutions).index(batch_shape(nxt)[0])]
+            noise_n, st_n, valid_n = fresh_data(nxt)
+            states_n, t_n, kw_n = learner.rollout_states(nxt, st_n, valid_n, noise_n, step_shift(nxt))
+            learner.mb = mb_now
+            pending = dict(step=nxt, x=states_n, t=t_n, kw=kw_n,
+                           handle=teacher.request(states_n, t_n, kw_n, chunks=args.opd_parts))
+            t_pref = time.time() - tf0
         if args.bench and lrank == 0:  # learner throughput: student latent tokens trained per second
             torch.cuda.synchronize(device) if device.type == "cuda" else None
             dt = time.time() - tp
@@ -660,7 +703,8 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
                   f"{(time.time() - t0) / args.log_every:.2f} s/step", flush=True)
             if args.opd_learner_profile:
                 print(f"[learner profile] captions {t_data * 1e3:.0f} ms, rollouts {t_roll * 1e3:.0f} ms, teacher "
-                      f"{t_teach * 1e3:.0f} ms ({args.opd_parts} parts), student {t_learn * 1e3:.0f} ms", flush=True)
+                      f"{t_teach * 1e3:.0f} ms ({args.opd_parts} parts), student {t_learn * 1e3:.0f} ms, prefetch "
+                      f"{t_pref * 1e3:.0f} ms", flush=True)
             t0 = time.time()
         if args.opd_actor_profile and actor is not None and t_roll:
             print(f"[actor profile] learner {lrank} step {step + 1}: {len(noise)} rollouts of "

@@ -5,9 +5,11 @@ Layout: ranks [0, L) learners, [L, L + A) rollout actors, [L + A, world) teacher
 headers) travel over a Gloo group, so servers can receive from any learner; tensors travel over the default group
 (NCCL on GPUs). Protocols:
 
-* Teacher: header [KIND_VELOCITY, B, C, h, w, L, D] from a learner, then x (B, C, h, w) fp32, t (B,), LM states
-  (B, L, D), valid (B, L) uint8; reply: the teacher's CFG velocity (B, C, h, w) fp32. A learner spreads a batch over
-  the teacher ranks (a rotating first rank per request). KIND_STOP ends the server.
+* Teacher: header [KIND_VELOCITY, B, C, h, w, L, D, chunks] from a learner, then x (B, C, h, w) fp32, t (B,), LM
+  states (B, L, D), valid (B, L) uint8; reply: the teacher's CFG velocity (B, C, h, w) fp32, computed in ``chunks``
+  row chunks (bounded teacher memory; 0 or 1 = the whole part at once). A learner spreads a batch over the teacher
+  ranks (a rotating first rank per request) and may defer reading the reply (``request`` / ``collect``) while it
+  trains, with at most one request outstanding per teacher. KIND_STOP ends the server.
 * Actor: header [KIND_ROLLOUT, B, C, h, w, L, D, step, version] with noise / LM states / valid; the actor generates
   the rollout states with the snapshot it holds and replies with (states (B m, C, h, w), t (B m,)). It refuses a
   job whose required snapshot version is newer than its own (the learner always sends the snapshot first).
@@ -50,7 +52,7 @@ class TeacherServer:
         while True:
             h = torch.zeros(HDR, dtype=torch.int64)
             src = dist.recv(h, group=self.ctl)
-            kind, B, C, hh, w, L, D = h[:7].tolist()
+            kind, B, C, hh, w, L, D, chunks = h[:8].tolist()
             if kind == KIND_STOP:
                 return served
             x = torch.empty(B, C, hh, w, device=self.device)
@@ -59,9 +61,19 @@ class TeacherServer:
             valid = torch.empty(B, L, device=self.device, dtype=torch.uint8)
             for buf in (x, t, st, valid):
                 dist.recv(buf, src=src)
-            v = self.teacher.velocity(x, t, dict(lm_states=st, valid=valid.bool())).float().contiguous()
-            dist.send(v, dst=src)
+            v = chunked_velocity(self.teacher, x, t, dict(lm_states=st, valid=valid.bool()), chunks)
+            dist.send(v.float().contiguous(), dst=src)
             served += 1
+
+
+def chunked_velocity(teacher, x, t, text_kw, chunks=1):
+    """teacher.velocity over ``chunks`` row chunks of the batch (concatenated in order)."""
+    B = x.shape[0]
+    n = max(1, min(int(chunks), B))
+    if n == 1:
+        return teacher.velocity(x, t, text_kw)
+    cuts = [(i * B // n, (i + 1) * B // n) for i in range(n)]
+    return torch.cat([teacher.velocity(x[a:b], t[a:b], {k: v[a:b] for k, v in text_kw.items()}) for a, b in cuts])
 
 
 class TeacherClient:
@@ -71,6 +83,13 @@ class TeacherClient:
 
     def velocity(self, x, t, text_kw):
         """Split the batch over the teacher ranks, send every part, then collect the replies in order."""
+        return self.collect(self.request(x, t, text_kw))
+
+    def request(self, x, t, text_kw, chunks=1):
+        """Send the parts of a batch to the teachers (one part per teacher, computed there in ``chunks`` row
+        chunks) and return a handle; the targets are read by ``collect``, so the teachers compute while the caller
+        works on. Each teacher holds its reply until it is collected: a learner keeps at most one request per
+        teacher outstanding (a second send could wait on a teacher that waits on the first reply)."""
         st, valid = text_kw["lm_states"], text_kw["valid"]
         B = x.shape[0]
         n = len(self.teachers)
@@ -82,14 +101,18 @@ class TeacherClient:
             if b1 <= b0:
                 continue
             xs = x[b0:b1].float().contiguous()
-            dist.send(_hdr(KIND_VELOCITY, b1 - b0, *xs.shape[1:], *st.shape[1:]), dst=dst, group=self.ctl)
+            dist.send(_hdr(KIND_VELOCITY, b1 - b0, *xs.shape[1:], *st.shape[1:], chunks), dst=dst, group=self.ctl)
             for buf in (xs, t[b0:b1].float().contiguous(), st[b0:b1].contiguous(),
                         valid[b0:b1].to(torch.uint8).contiguous()):
                 dist.send(buf, dst=dst)
             replies.append((b0, b1, dst))
-        out = torch.empty(B, *x.shape[1:], device=x.device)
+        return replies, B, tuple(x.shape[1:]), x.device
+
+    def collect(self, handle):
+        replies, B, shape, device = handle
+        out = torch.empty(B, *shape, device=device)
         for b0, b1, dst in replies:
-            buf = torch.empty(b1 - b0, *x.shape[1:], device=x.device)
+            buf = torch.empty(b1 - b0, *shape, device=device)
             dist.recv(buf, src=dst)
             out[b0:b1] = buf
         return out

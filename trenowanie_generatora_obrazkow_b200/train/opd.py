@@ -92,6 +92,15 @@ class DiTTeacher:
     def __init__(self, te, den, cfg=3.0):
         self.te, self.den, self.cfg = te.eval().requires_grad_(False), den.eval().requires_grad_(False), cfg
 
+    def request(self, x, t, text_kw, chunks=1):
+        """Same interface as a remote teacher's deferred request: computed here (in ``chunks`` row chunks),
+        returned by ``collect``."""
+        from ..parallel.roles import chunked_velocity
+        return chunked_velocity(self, x, t, text_kw, chunks)
+
+    def collect(self, handle):
+        return handle
+
     @torch.no_grad()
     def velocity(self, x, t, text_kw):
         from ..sampling.euler import encode_prompts
@@ -157,7 +166,8 @@ class OPDLearner:
         self.cache = None
         self.uses = 0
 
-    def _prepare(self, step, lm_states, valid, noise, shift):
+    def rollout_states(self, step, lm_states, valid, noise, shift):
+        """The student's own states of a fresh batch: (states (B m, C, h, w), t (B m), text_kw repeated per state)."""
         B = noise.shape[0]
         g = torch.Generator().manual_seed(self.seed * 1_000_003 + self.replica * 1009 + step + 7)
         if self.method == "dance":
@@ -172,15 +182,27 @@ class OPDLearner:
         states = rollout(self.den, text, valid_to_len(v), noise, ts, picks, self.mb).flatten(0, 1)
         t = ts[picks.to(noise.device)].flatten()
         rep = lambda a: a.repeat_interleave(self.m, dim=0)
-        text_kw = dict(lm_states=rep(lm_states), valid=rep(valid))
-        target = self.teacher.velocity(states, t, text_kw)
-        return dict(x=states, t=t, target=target, text_kw=text_kw, errors=None)
+        return states, t, dict(lm_states=rep(lm_states), valid=rep(valid))
 
-    def step_grads(self, step, lm_states, valid, noise, shift=None):
-        """Accumulate the gradient of one OPD update (fresh batch or replay); returns the mean MSE."""
-        if self.cache is None or self.uses >= self.reuse:
-            self.cache = self._prepare(step, lm_states, valid, noise, shift or self.shift)
-            self.uses = 0
+    @property
+    def needs_fresh(self):
+        return self.cache is None or self.uses >= self.reuse
+
+    def install(self, states, t, target, text_kw):
+        """A fresh cache (states, times, teacher targets) for the next ``reuse`` updates."""
+        self.cache = dict(x=states, t=t, target=target, text_kw=text_kw, errors=None)
+        self.uses = 0
+
+    def _prepare(self, step, lm_states, valid, noise, shift):
+        states, t, text_kw = self.rollout_states(step, lm_states, valid, noise, shift)
+        self.install(states, t, self.teacher.velocity(states, t, text_kw), text_kw)
+
+    def step_grads(self, step, lm_states=None, valid=None, noise=None, shift=None):
+        """Accumulate the gradient of one OPD update (fresh batch or replay); returns the mean MSE. The batch
+        arguments are only read when a fresh cache is due and none was installed."""
+        if self.needs_fresh:
+            assert noise is not None, "a fresh OPD batch is due: pass its noise and text states (or install one)"
+            self._prepare(step, lm_states, valid, noise, shift or self.shift)
         c = self.cache
         weights = state_weights(torch.cat(c["errors"]), c["t"]) if (self.weighting and c["errors"]) else None
         errors = [] if self.weighting else None
