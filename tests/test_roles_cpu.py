@@ -94,3 +94,47 @@ def test_opd_roles_round_trip():
     tgt = DiTTeacher(tte, tden, 3.0).velocity(states, res["t"], dict(lm_states=res["st"].repeat_interleave(2, 0),
                                                                       valid=valid.repeat_interleave(2, 0)))
     assert torch.allclose(tgt, res["tgt"], atol=1e-5)
+
+
+def _deferred_worker(rank, world, port, d):
+    """Ranks 0, 1 learners, rank 2 the teacher. Both learners leave a deferred request with the teacher, run a
+    gradient-style all-reduce among themselves, then collect; a plain request follows."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    ctl = dist.new_group(backend="gloo")
+    learners = dist.new_group([0, 1])
+    from trenowanie_generatora_obrazkow_b200.parallel.roles import TeacherClient, TeacherServer
+    from trenowanie_generatora_obrazkow_b200.train.opd import DiTTeacher
+    if rank == 2:
+        tte, tden = _models(2)
+        served = TeacherServer(DiTTeacher(tte, tden, 3.0), "cpu", ctl).serve()
+        torch.save(served, os.path.join(d, "served.pt"))
+    else:
+        teacher = TeacherClient([2], ctl, rank)
+        g = torch.Generator().manual_seed(10 + rank)
+        x, t = torch.randn(3, 16, 4, 4, generator=g), torch.rand(3, generator=g)
+        kw = dict(lm_states=torch.randn(3, 8, 32, generator=g), valid=torch.ones(3, 8, dtype=torch.bool))
+        h = teacher.request(x, t, kw, chunks=2, deferred=True)
+        s = torch.ones(4)
+        dist.all_reduce(s, group=learners)  # the learners meet while both replies are held
+        deferred = teacher.collect(h)
+        plain = teacher.velocity(x, t, kw)
+        torch.save(dict(x=x, t=t, kw=kw, deferred=deferred, plain=plain, s=s), os.path.join(d, f"l{rank}.pt"))
+        dist.barrier(group=learners)
+        if rank == 0:
+            teacher.stop()
+    dist.destroy_process_group()
+
+
+def test_deferred_teacher_requests_from_two_learners():
+    from trenowanie_generatora_obrazkow_b200.train.opd import DiTTeacher
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_deferred_worker, args=(3, _port(), d), nprocs=3, join=True)
+        tte, tden = _models(2)
+        local = DiTTeacher(tte, tden, 3.0)
+        for r in range(2):
+            got = torch.load(os.path.join(d, f"l{r}.pt"))
+            want = local.velocity(got["x"], got["t"], got["kw"])
+            assert torch.allclose(got["deferred"], want, atol=1e-5) and torch.allclose(got["plain"], want, atol=1e-5)
+            assert torch.equal(got["s"], torch.full((4,), 2.0))
+        assert torch.load(os.path.join(d, "served.pt")) == 4

@@ -686,7 +686,7 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
             states_n, t_n, kw_n = learner.rollout_states(nxt, st_n, valid_n, noise_n, step_shift(nxt))
             learner.mb = mb_now
             pending = dict(step=nxt, x=states_n, t=t_n, kw=kw_n,
-                           handle=teacher.request(states_n, t_n, kw_n, chunks=args.opd_parts))
+                           handle=teacher.request(states_n, t_n, kw_n, chunks=args.opd_parts, deferred=True))
             t_pref = time.time() - tf0
         if args.bench and lrank == 0:  # learner throughput: student latent tokens trained per second
             torch.cuda.synchronize(device) if device.type == "cuda" else None

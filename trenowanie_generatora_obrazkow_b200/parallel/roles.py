@@ -5,11 +5,14 @@ Layout: ranks [0, L) learners, [L, L + A) rollout actors, [L + A, world) teacher
 headers) travel over a Gloo group, so servers can receive from any learner; tensors travel over the default group
 (NCCL on GPUs). Protocols:
 
-* Teacher: header [KIND_VELOCITY, B, C, h, w, L, D, chunks] from a learner, then x (B, C, h, w) fp32, t (B,), LM
-  states (B, L, D), valid (B, L) uint8; reply: the teacher's CFG velocity (B, C, h, w) fp32, computed in ``chunks``
-  row chunks (bounded teacher memory; 0 or 1 = the whole part at once). A learner spreads a batch over the teacher
-  ranks (a rotating first rank per request) and may defer reading the reply (``request`` / ``collect``) while it
-  trains, with at most one request outstanding per teacher. KIND_STOP ends the server.
+* Teacher: header [KIND_VELOCITY, B, C, h, w, L, D, chunks, deferred] from a learner, then x (B, C, h, w) fp32, t
+  (B,), LM states (B, L, D), valid (B, L) uint8; reply: the teacher's CFG velocity (B, C, h, w) fp32, computed in
+  ``chunks`` row chunks (bounded teacher memory; 0 or 1 = the whole part at once). A learner spreads a batch over
+  the teacher ranks (a rotating first rank per request). A deferred request (``request(..., deferred=True)``, then
+  ``collect``) is computed at once but its reply is held by the teacher until the learner sends [KIND_COLLECT] and
+  waits for it: the teacher never leaves a send pending on its stream, where it would hold up the next learner's
+  request while that learner's stream (and through the gradient all-reduce, every learner) waits on it. One deferred
+  request per learner and teacher at a time. KIND_STOP ends the server.
 * Actor: header [KIND_ROLLOUT, B, C, h, w, L, D, step, version] with noise / LM states / valid; the actor generates
   the rollout states with the snapshot it holds and replies with (states (B m, C, h, w), t (B m,)). It refuses a
   job whose required snapshot version is newer than its own (the learner always sends the snapshot first).
@@ -20,7 +23,7 @@ headers) travel over a Gloo group, so servers can receive from any learner; tens
 import torch
 import torch.distributed as dist
 
-KIND_STOP, KIND_VELOCITY, KIND_ROLLOUT, KIND_SNAPSHOT = 0, 1, 2, 3
+KIND_STOP, KIND_VELOCITY, KIND_ROLLOUT, KIND_SNAPSHOT, KIND_COLLECT = 0, 1, 2, 3, 4
 HDR = 10
 
 
@@ -49,12 +52,18 @@ class TeacherServer:
 
     def serve(self):
         served = 0
+        held = {}  # learner rank -> the reply of its deferred request
         while True:
             h = torch.zeros(HDR, dtype=torch.int64)
             src = dist.recv(h, group=self.ctl)
-            kind, B, C, hh, w, L, D, chunks = h[:8].tolist()
+            kind, B, C, hh, w, L, D, chunks, deferred = h[:9].tolist()
             if kind == KIND_STOP:
                 return served
+            if kind == KIND_COLLECT:
+                if src not in held:
+                    raise RuntimeError(f"teacher: rank {src} collects a reply it never requested")
+                dist.send(held.pop(src), dst=src)
+                continue
             x = torch.empty(B, C, hh, w, device=self.device)
             t = torch.empty(B, device=self.device)
             st = torch.empty(B, L, D, device=self.device, dtype=self.dtype)
@@ -62,8 +71,14 @@ class TeacherServer:
             for buf in (x, t, st, valid):
                 dist.recv(buf, src=src)
             v = chunked_velocity(self.teacher, x, t, dict(lm_states=st, valid=valid.bool()), chunks)
-            dist.send(v.float().contiguous(), dst=src)
+            v = v.float().contiguous()
             served += 1
+            if deferred:
+                if src in held:
+                    raise RuntimeError(f"teacher: rank {src} sent a second deferred request before collecting")
+                held[src] = v
+            else:
+                dist.send(v, dst=src)
 
 
 def chunked_velocity(teacher, x, t, text_kw, chunks=1):
@@ -85,11 +100,11 @@ class TeacherClient:
         """Split the batch over the teacher ranks, send every part, then collect the replies in order."""
         return self.collect(self.request(x, t, text_kw))
 
-    def request(self, x, t, text_kw, chunks=1):
+    def request(self, x, t, text_kw, chunks=1, deferred=False):
         """Send the parts of a batch to the teachers (one part per teacher, computed there in ``chunks`` row
-        chunks) and return a handle; the targets are read by ``collect``, so the teachers compute while the caller
-        works on. Each teacher holds its reply until it is collected: a learner keeps at most one request per
-        teacher outstanding (a second send could wait on a teacher that waits on the first reply)."""
+        chunks) and return a handle for ``collect``. Not deferred: the teachers send their replies at once and the
+        caller must collect next. Deferred: the teachers hold the replies until ``collect`` asks for them, so the
+        caller trains meanwhile (one deferred request per teacher at a time)."""
         st, valid = text_kw["lm_states"], text_kw["valid"]
         B = x.shape[0]
         n = len(self.teachers)
@@ -101,17 +116,20 @@ class TeacherClient:
             if b1 <= b0:
                 continue
             xs = x[b0:b1].float().contiguous()
-            dist.send(_hdr(KIND_VELOCITY, b1 - b0, *xs.shape[1:], *st.shape[1:], chunks), dst=dst, group=self.ctl)
+            dist.send(_hdr(KIND_VELOCITY, b1 - b0, *xs.shape[1:], *st.shape[1:], chunks, int(deferred)), dst=dst,
+                      group=self.ctl)
             for buf in (xs, t[b0:b1].float().contiguous(), st[b0:b1].contiguous(),
                         valid[b0:b1].to(torch.uint8).contiguous()):
                 dist.send(buf, dst=dst)
             replies.append((b0, b1, dst))
-        return replies, B, tuple(x.shape[1:]), x.device
+        return replies, B, tuple(x.shape[1:]), x.device, deferred
 
     def collect(self, handle):
-        replies, B, shape, device = handle
+        replies, B, shape, device, deferred = handle
         out = torch.empty(B, *shape, device=device)
         for b0, b1, dst in replies:
+            if deferred:
+                dist.send(_hdr(KIND_COLLECT), dst=dst, group=self.ctl)
             buf = torch.empty(b1 - b0, *shape, device=device)
             dist.recv(buf, src=dst)
             out[b0:b1] = buf

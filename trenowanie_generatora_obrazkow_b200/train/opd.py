@@ -92,7 +92,7 @@ class DiTTeacher:
     def __init__(self, te, den, cfg=3.0):
         self.te, self.den, self.cfg = te.eval().requires_grad_(False), den.eval().requires_grad_(False), cfg
 
-    def request(self, x, t, text_kw, chunks=1):
+    def request(self, x, t, text_kw, chunks=1, deferred=False):
         """Same interface as a remote teacher's deferred request: computed here (in ``chunks`` row chunks),
         returned by ``collect``."""
         from ..parallel.roles import chunked_velocity
