@@ -138,3 +138,37 @@ def test_deferred_teacher_requests_from_two_learners():
             assert torch.allclose(got["deferred"], want, atol=1e-5) and torch.allclose(got["plain"], want, atol=1e-5)
             assert torch.equal(got["s"], torch.full((4,), 2.0))
         assert torch.load(os.path.join(d, "served.pt")) == 4
+
+
+def _deferred_actor_worker(rank, world, port, d):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    ctl = dist.new_group(backend="gloo")
+    from trenowanie_generatora_obrazkow_b200.parallel.roles import (ActorClient, RoleLayout, RolloutActor,
+                                                                    SnapshotSender)
+    lay = RoleLayout(world, 1, 1, 0)
+    if lay.role(rank) == "actor":
+        te, den = _models(99)
+        jobs = RolloutActor(te, den, list(te.parameters()) + list(den.parameters()), "cpu", ctl, KW).serve()
+        torch.save(jobs, os.path.join(d, "jobs.pt"))
+    else:
+        te, den = _models(1)
+        client = ActorClient(lay.actors[0], ctl, KW["m"])
+        v = SnapshotSender(list(te.parameters()) + list(den.parameters()), lay.actors, ctl).send()
+        g = torch.Generator().manual_seed(4)
+        noise, st = torch.randn(2, 16, 4, 4, generator=g), torch.randn(2, 8, 32, generator=g)
+        valid = torch.ones(2, 8, dtype=torch.bool)
+        job = client.request(noise, st, valid, 5, v, deferred=True)  # held by the actor ...
+        plain = client.rollouts(noise, st, valid, 5, v)  # ... while a plain job of the same batch goes through
+        held = client.collect(job)
+        torch.save(dict(plain=plain, held=held), os.path.join(d, "out.pt"))
+        client.stop()
+    dist.destroy_process_group()
+
+
+def test_deferred_actor_job_equals_a_plain_one():
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_deferred_actor_worker, args=(2, _port(), d), nprocs=2, join=True)
+        out = torch.load(os.path.join(d, "out.pt"))
+        assert torch.equal(out["plain"][0], out["held"][0]) and torch.equal(out["plain"][1], out["held"][1])
+        assert torch.load(os.path.join(d, "jobs.pt")) == 2

@@ -35,7 +35,9 @@ def test_opd_mode_with_actor_and_teacher(tmp_path):
                     "--opd-actor", "--teacher-ranks", "1", "--teacher-size", "nano", "--res", "128",
                     "--batch", "8", "--micro-batch", "2", "--steps", "3", "--log-every", "1", "--opd-reuse", "2",
                     "--opd-rollout-steps", "4")
-    assert "step 3/3" in out and "served" in out and "rollout jobs" in out
+    # two learners, reuse 2: fresh batches at steps 0 (rolled out while the learners wait) and 2 (requested at
+    # step 0 and rolled out during the cycle; its teacher request goes out at step 1, the last replay step)
+    assert "step 3/3" in out and "[actor 2] 4 rollout jobs" in out and "[teacher 3] served 4 requests" in out
 
 
 def test_pipeline_with_distributed_lm_states(tmp_path):

@@ -625,7 +625,20 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
                           for a, b in bounds if b > a])
 
     version = 0
-    pending = None  # --opd-prefetch: the next cycle's rollouts, their teacher request in flight
+    # the next cycle's batch in preparation: {"step", "kw"} plus either "actor": (client, job) while the actor rolls
+    # it out, or "x", "t", "teacher" (a deferred teacher request) once the states are here
+    pending = None
+    rep = lambda a: a.repeat_interleave(args.opd_states, dim=0)
+
+    def actor_for(step):
+        return actors[(lrank + step) % len(actors)] if args.opd_balance_rollouts else actor
+
+    def states_to_teacher(p):
+        """Actor job collected; the teacher's deferred request starts on its states."""
+        client, job = p.pop("actor")
+        p["x"], p["t"] = client.collect(job)
+        p["teacher"] = teacher.request(p["x"], p["t"], p["kw"], chunks=args.opd_parts, deferred=True)
+
     t0 = time.time()
     for step in range(args.steps):
         res, B = batch_shape(step)
@@ -638,23 +651,23 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         t_data = t_roll = t_teach = 0.0
         for p in params:
             p.grad = None
-        if fresh and pending is not None:  # prepared during the last cycle's replay: collect the teacher's reply
-            assert pending["step"] == step, "a prefetched OPD batch must start the next cycle"
+        sent = False
+        if fresh and pending is not None:  # prepared during the last cycle (actor job or --opd-prefetch)
+            assert pending["step"] == step, "a prepared OPD batch must start the next cycle"
             tt0 = time.time()
-            learner.install(pending["x"], pending["t"], teacher.collect(pending["handle"]), pending["kw"])
+            if "actor" in pending:
+                states_to_teacher(pending)
+            learner.install(pending["x"], pending["t"], teacher.collect(pending["teacher"]), pending["kw"])
             t_teach = time.time() - tt0
             pending = None
         elif fresh:
             noise, st, valid = fresh_data(step)
             t_data = time.time() - tp
-            if args.opd_balance_rollouts and actors:
-                actor = actors[(lrank + step) % len(actors)]
-            rep = lambda a: a.repeat_interleave(args.opd_states, dim=0)
             tr0 = time.time()
             if actor is not None:
                 if sender is not None:
-                    version = sender.send()
-                states, t = actor.rollouts(noise, st, valid, step, version)
+                    version, sent = sender.send(), True
+                states, t = actor_for(step).rollouts(noise, st, valid, step, version)
                 kw_all = dict(lm_states=rep(st), valid=rep(valid))
             else:
                 states, t, kw_all = learner.rollout_states(step, st, valid, noise, shift)
@@ -662,6 +675,18 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
             tt0 = time.time()
             learner.install(states, t, teacher_targets(states, t, kw_all), kw_all)
             t_teach = time.time() - tt0
+        if fresh and actor is not None and step + learner.reuse < args.steps:
+            # the actor rolls out the next cycle's batch with the weights of now while this cycle trains (states
+            # reuse .. 2 reuse - 1 updates old when trained on, as the reference's actor cache)
+            if sender is not None and not sent:
+                version = sender.send()
+            nxt = step + learner.reuse
+            noise_n, st_n, valid_n = fresh_data(nxt)
+            client = actor_for(nxt)
+            pending = dict(step=nxt, kw=dict(lm_states=rep(st_n), valid=rep(valid_n)),
+                           actor=(client, client.request(noise_n, st_n, valid_n, nxt, version, deferred=True)))
+        elif pending is not None and "actor" in pending and step == pending["step"] - 1:
+            states_to_teacher(pending)  # last replay update of the cycle: the teacher scores meanwhile
         tl0 = time.time()
         loss = learner.step_grads(step)
         t_learn = time.time() - tl0
@@ -686,7 +711,7 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
             states_n, t_n, kw_n = learner.rollout_states(nxt, st_n, valid_n, noise_n, step_shift(nxt))
             learner.mb = mb_now
             pending = dict(step=nxt, x=states_n, t=t_n, kw=kw_n,
-                           handle=teacher.request(states_n, t_n, kw_n, chunks=args.opd_parts, deferred=True))
+                           teacher=teacher.request(states_n, t_n, kw_n, chunks=args.opd_parts, deferred=True))
             t_pref = time.time() - tf0
         if args.bench and lrank == 0:  # learner throughput: student latent tokens trained per second
             torch.cuda.synchronize(device) if device.type == "cuda" else None

@@ -13,9 +13,11 @@ headers) travel over a Gloo group, so servers can receive from any learner; tens
   waits for it: the teacher never leaves a send pending on its stream, where it would hold up the next learner's
   request while that learner's stream (and through the gradient all-reduce, every learner) waits on it. One deferred
   request per learner and teacher at a time. KIND_STOP ends the server.
-* Actor: header [KIND_ROLLOUT, B, C, h, w, L, D, step, version] with noise / LM states / valid; the actor generates
-  the rollout states with the snapshot it holds and replies with (states (B m, C, h, w), t (B m,)). It refuses a
-  job whose required snapshot version is newer than its own (the learner always sends the snapshot first).
+* Actor: header [KIND_ROLLOUT, B, C, h, w, L, D, step, version, deferred] with noise / LM states / valid; the actor
+  generates the rollout states with the snapshot it holds and replies with (states (B m, C, h, w), t (B m,)); a
+  deferred job's reply is held until the learner's [KIND_COLLECT] (one job per learner at a time), so a learner
+  trains while its next batch is rolled out. It refuses a job whose required snapshot version is newer than its own
+  (the learner always sends the snapshot first).
 * Snapshot: learner 0 flattens the student's parameters and streams them into every actor's mapped buffer with the
   peer-copy kernel (NVLink stores, then a version word), then tells each actor (Gloo) the version; on CPU the flat
   tensor is sent over the process group instead. Versions only grow; an actor applies a snapshot only between jobs.
@@ -218,6 +220,7 @@ class RolloutActor:
         from ..ops.reference import valid_to_len
         from ..train.opd import dance_picks, diffusion_picks, opd_grid, rollout
         jobs = 0
+        held = {}  # learner rank -> (states, t) of its deferred job
         while True:
             h = torch.zeros(HDR, dtype=torch.int64)
             src = dist.recv(h, group=self.ctl)
@@ -227,7 +230,13 @@ class RolloutActor:
             if kind == KIND_SNAPSHOT:
                 self._apply_snapshot(src, int(h[1]))
                 continue
-            _, B, C, hh, w, L, D, step, need = h[:9].tolist()
+            if kind == KIND_COLLECT:
+                if src not in held:
+                    raise RuntimeError(f"actor: rank {src} collects a job it never submitted")
+                for buf in held.pop(src):
+                    dist.send(buf, dst=src)
+                continue
+            _, B, C, hh, w, L, D, step, need, deferred = h[:10].tolist()
             if need > self.version:
                 raise RuntimeError(f"actor holds snapshot {self.version}, job needs {need}")
             noise = torch.empty(B, C, hh, w, device=self.device)
@@ -243,9 +252,14 @@ class RolloutActor:
             text, v = self.te(lm_states=st, valid=valid.bool())
             states = rollout(self.den, text, valid_to_len(v), noise, ts, picks, self.kw["mb"]).flatten(0, 1)
             t = ts[picks.to(self.device)].flatten().contiguous()
+            jobs += 1
+            if deferred:
+                if src in held:
+                    raise RuntimeError(f"actor: rank {src} submitted a second deferred job before collecting")
+                held[src] = (states.contiguous(), t)
+                continue
             dist.send(states.contiguous(), dst=src)
             dist.send(t, dst=src)
-            jobs += 1
 
 
 class ActorClient:
@@ -253,13 +267,24 @@ class ActorClient:
         self.actor, self.ctl, self.m = actor, control_group, m
 
     def rollouts(self, noise, lm_states, valid, step, version):
+        return self.collect(self.request(noise, lm_states, valid, step, version))
+
+    def request(self, noise, lm_states, valid, step, version, deferred=False):
+        """Submit a rollout job; ``collect`` returns (states, t). Deferred: the actor holds the result until it is
+        collected (one deferred job per learner and actor at a time)."""
         B = noise.shape[0]
-        dist.send(_hdr(KIND_ROLLOUT, B, *noise.shape[1:], *lm_states.shape[1:], step, version), dst=self.actor,
-                  group=self.ctl)
+        dist.send(_hdr(KIND_ROLLOUT, B, *noise.shape[1:], *lm_states.shape[1:], step, version, int(deferred)),
+                  dst=self.actor, group=self.ctl)
         for buf in (noise.float().contiguous(), lm_states.contiguous(), valid.to(torch.uint8).contiguous()):
             dist.send(buf, dst=self.actor)
-        states = torch.empty(B * self.m, *noise.shape[1:], device=noise.device)
-        t = torch.empty(B * self.m, device=noise.device)
+        return B, tuple(noise.shape[1:]), noise.device, deferred
+
+    def collect(self, handle):
+        B, shape, device, deferred = handle
+        if deferred:
+            dist.send(_hdr(KIND_COLLECT), dst=self.actor, group=self.ctl)
+        states = torch.empty(B * self.m, *shape, device=device)
+        t = torch.empty(B * self.m, device=device)
         dist.recv(states, src=self.actor)
         dist.recv(t, src=self.actor)
         return states, t
