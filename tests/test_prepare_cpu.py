@@ -143,3 +143,42 @@ def test_prepare_images_flux_reason_and_monet(tmp_path):
     pq.write_table(pa.table({"thumbnail": [{"bytes": b"abc"}, {"bytes": b"de"}]}), mon / "f.parquet")
     prepare_images.main(["monet", "--parquet-dir", str(tmp_path / "monet")])
     assert prepare_images.read_packed(str(mon / "f"), 1) == b"de"
+
+
+def test_shard_viewer_pages_and_images(tmp_path):
+    """shard_viewer.py over synthetic shards: the index lists them, a shard page shows its captions (filtered), an
+    item page its translated captions, and images are the packed originals or PNG latent previews."""
+    import threading
+    import urllib.error
+    import urllib.request
+
+    import shard_viewer as V
+    from trenowanie_generatora_obrazkow_b200.data.shards import write_synthetic_shards
+    root = str(tmp_path / "data")
+    names = write_synthetic_shards(root, n_shards=2, per_shard=4, side=16)
+    json.dump([[f"podpis {i}"] for i in range(4)], open(os.path.join(root, f"{names[0]}.caps_pl.json"), "w"))
+    w = prepare_images.PackWriter(os.path.join(root, names[1]))
+    w.add([b"\xff\xd8\xff" + bytes([i]) * 10 for i in range(4)])
+    w.close()
+    server = V.serve(root, port=0)
+    threading.Thread(target=server.serve_forever, daemon=True).start()
+    base = f"http://127.0.0.1:{server.server_address[1]}"
+    get = lambda path: urllib.request.urlopen(base + path, timeout=30)
+    try:
+        index = get("/").read().decode()
+        assert all(n in index for n in names) and "2 shards" in index
+        page = get(f"/shard?name={names[0]}&q=caption").read().decode()
+        assert f"caption {names[0]} 3 0" in page and "4 of 4 images" in page
+        page = get(f"/shard?name={names[0]}&q=nothing-matches").read().decode()
+        assert "0 of 4 images" in page
+        item = get(f"/item?name={names[0]}&i=2").read().decode()
+        assert "podpis 2" in item and "[128, 16, 16]" in item
+        r = get(f"/img?name={names[0]}&i=1")
+        assert r.headers["Content-Type"] == "image/png" and r.read()[:4] == b"\x89PNG"
+        r = get(f"/img?name={names[1]}&i=3")
+        assert r.headers["Content-Type"] == "image/jpeg" and r.read() == b"\xff\xd8\xff" + bytes([3]) * 10
+        with pytest.raises(urllib.error.HTTPError):
+            get("/img?name=missing&i=0")
+    finally:
+        server.shutdown()
+        server.server_close()
