@@ -242,3 +242,41 @@ def test_prepare_lowres_vae_options_with_stand_in_vaes(tmp_path):
     assert out[128].shape == (2, 128, 8, 8) and np.allclose(out[128], 7.0)  # 0 * std + mean
     with pytest.raises(AssertionError):
         prepare_lowres.main(["--data", str(tmp_path), "--latent-pool", "--channels-last", "--device", "cpu"])
+
+
+def test_translate_launch_restarts_crashed_workers(tmp_path):
+    """translate_launch.py with a stand-in worker script: one worker per GPU index with CUDA_VISIBLE_DEVICES set,
+    rank / world and the `--` arguments passed, a crashed worker restarted until it succeeds, a worker that keeps
+    failing stopped after --max-restarts; progress counts translated shards."""
+    tl = _script("translate_launch")
+    data = tmp_path / "shards"
+    data.mkdir()
+    for i in range(3):
+        (data / f"s{i}.caps.json").write_text("[]")
+    worker = tmp_path / "worker.py"
+    worker.write_text(
+        "import json, os, sys\n"
+        "a = sys.argv[1:]\n"
+        "rank = int(a[a.index('--rank') + 1])\n"
+        "state = os.path.join(os.environ['OUT'], f'attempts{rank}')\n"
+        "n = int(open(state).read()) + 1 if os.path.exists(state) else 1\n"
+        "open(state, 'w').write(str(n))\n"
+        "json.dump(dict(argv=a, gpu=os.environ['CUDA_VISIBLE_DEVICES']),"
+        " open(os.path.join(os.environ['OUT'], f'args{rank}.json'), 'w'))\n"
+        "if rank == 0 and n < 2: sys.exit(3)\n"  # crashes once
+        "if rank == 2: sys.exit(5)\n"  # keeps failing
+        "open(os.path.join(a[a.index('--data') + 1], f's{rank}.caps_pl.json'), 'w').write('[]')\n")
+    os.environ["OUT"] = str(tmp_path)
+    try:
+        codes = tl.main(["--gpus", "4", "5", "6", "--data", str(data), "--script", str(worker), "--restart-delay",
+                         "0", "--max-restarts", "2", "--progress-every", "0", "--log-dir", str(tmp_path / "logs"),
+                         "--", "--max-tokens", "99"])
+    finally:
+        os.environ.pop("OUT")
+    assert codes == {0: 0, 1: 0, 2: 5}
+    attempts = [int((tmp_path / f"attempts{r}").read_text()) for r in range(3)]
+    assert attempts == [2, 1, 3]  # rank 2: the first run and two restarts
+    args = json.load(open(tmp_path / "args1.json"))
+    assert args["gpu"] == "5" and args["argv"][-2:] == ["--max-tokens", "99"] and "--world" in args["argv"]
+    assert tl.progress(str(data)) == (2, 3)
+    assert sorted(os.listdir(tmp_path / "logs")) == ["gpu4.log", "gpu5.log", "gpu6.log"]
