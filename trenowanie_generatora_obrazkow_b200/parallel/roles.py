@@ -13,6 +13,12 @@ headers) travel over a Gloo group, so servers can receive from any learner; tens
   waits for it: the teacher never leaves a send pending on its stream, where it would hold up the next learner's
   request while that learner's stream (and through the gradient all-reduce, every learner) waits on it. One deferred
   request per learner and teacher at a time. KIND_STOP ends the server.
+* Every tensor send of these protocols (a learner's request data, a server's reply) is an ``isend`` whose handle
+  (and tensor) is kept until the exchange is over, never a blocking ``send``: on NCCL a ``send`` makes the sender's
+  compute stream wait until the receiver takes the data, and with several learners and several servers those waits
+  can close a cycle (learner X's stream waits on its send to server 2, which waits on server 2's send to learner Y,
+  which waits on Y's send to server 1, which waits on server 1's send to X). With ``isend`` a compute stream waits
+  only on the receives its own work reads, and the protocols' data dependencies form no cycle.
 * Actor: header [KIND_ROLLOUT, B, C, h, w, L, D, step, version, deferred] with noise / LM states / valid; the actor
   generates the rollout states with the snapshot it holds and replies with (states (B m, C, h, w), t (B m,)); a
   deferred job's reply is held until the learner's [KIND_COLLECT] (one job per learner at a time), so a learner
@@ -48,6 +54,22 @@ def _hdr(*vals):
     return h
 
 
+class _Outgoing:
+    """Sends in flight: (work, tensor) kept until complete, so neither the stream nor the buffer is waited on early."""
+
+    def __init__(self):
+        self.items = []
+
+    def send(self, tensor, dst):
+        self.items.append((dist.isend(tensor, dst=dst), tensor))
+        self.items = [(w, t) for w, t in self.items if not w.is_completed()]
+
+    def wait(self):
+        for w, _ in self.items:
+            w.wait()
+        self.items = []
+
+
 class TeacherServer:
     def __init__(self, teacher, device, control_group, dtype=torch.float32):
         self.teacher, self.device, self.ctl, self.dtype = teacher, device, control_group, dtype
@@ -55,16 +77,18 @@ class TeacherServer:
     def serve(self):
         served = 0
         held = {}  # learner rank -> the reply of its deferred request
+        out = _Outgoing()
         while True:
             h = torch.zeros(HDR, dtype=torch.int64)
             src = dist.recv(h, group=self.ctl)
             kind, B, C, hh, w, L, D, chunks, deferred = h[:9].tolist()
             if kind == KIND_STOP:
+                out.wait()
                 return served
             if kind == KIND_COLLECT:
                 if src not in held:
                     raise RuntimeError(f"teacher: rank {src} collects a reply it never requested")
-                dist.send(held.pop(src), dst=src)
+                out.send(held.pop(src), src)
                 continue
             x = torch.empty(B, C, hh, w, device=self.device)
             t = torch.empty(B, device=self.device)
@@ -80,7 +104,7 @@ class TeacherServer:
                     raise RuntimeError(f"teacher: rank {src} sent a second deferred request before collecting")
                 held[src] = v
             else:
-                dist.send(v, dst=src)
+                out.send(v, src)
 
 
 def chunked_velocity(teacher, x, t, text_kw, chunks=1):
@@ -113,7 +137,7 @@ class TeacherClient:
         parts = [(i * B // n, (i + 1) * B // n) for i in range(n)]
         order = [self.teachers[(self.turn + i) % n] for i in range(n)]
         self.turn += 1
-        replies = []
+        replies, sends = [], _Outgoing()
         for (b0, b1), dst in zip(parts, order):
             if b1 <= b0:
                 continue
@@ -122,12 +146,12 @@ class TeacherClient:
                       group=self.ctl)
             for buf in (xs, t[b0:b1].float().contiguous(), st[b0:b1].contiguous(),
                         valid[b0:b1].to(torch.uint8).contiguous()):
-                dist.send(buf, dst=dst)
+                sends.send(buf, dst)
             replies.append((b0, b1, dst))
-        return replies, B, tuple(x.shape[1:]), x.device, deferred
+        return replies, B, tuple(x.shape[1:]), x.device, deferred, sends
 
     def collect(self, handle):
-        replies, B, shape, device, deferred = handle
+        replies, B, shape, device, deferred, sends = handle
         out = torch.empty(B, *shape, device=device)
         for b0, b1, dst in replies:
             if deferred:
@@ -135,6 +159,7 @@ class TeacherClient:
             buf = torch.empty(b1 - b0, *shape, device=device)
             dist.recv(buf, src=dst)
             out[b0:b1] = buf
+        sends.wait()  # long complete: each teacher replied after receiving its part
         return out
 
     def stop(self):
@@ -221,11 +246,13 @@ class RolloutActor:
         from ..train.opd import dance_picks, diffusion_picks, opd_grid, rollout
         jobs = 0
         held = {}  # learner rank -> (states, t) of its deferred job
+        out = _Outgoing()
         while True:
             h = torch.zeros(HDR, dtype=torch.int64)
             src = dist.recv(h, group=self.ctl)
             kind = int(h[0])
             if kind == KIND_STOP:
+                out.wait()
                 return jobs
             if kind == KIND_SNAPSHOT:
                 self._apply_snapshot(src, int(h[1]))
@@ -234,7 +261,7 @@ class RolloutActor:
                 if src not in held:
                     raise RuntimeError(f"actor: rank {src} collects a job it never submitted")
                 for buf in held.pop(src):
-                    dist.send(buf, dst=src)
+                    out.send(buf, src)
                 continue
             _, B, C, hh, w, L, D, step, need, deferred = h[:10].tolist()
             if need > self.version:
@@ -258,8 +285,8 @@ class RolloutActor:
                     raise RuntimeError(f"actor: rank {src} submitted a second deferred job before collecting")
                 held[src] = (states.contiguous(), t)
                 continue
-            dist.send(states.contiguous(), dst=src)
-            dist.send(t, dst=src)
+            out.send(states.contiguous(), src)
+            out.send(t, src)
 
 
 class ActorClient:
@@ -275,18 +302,20 @@ class ActorClient:
         B = noise.shape[0]
         dist.send(_hdr(KIND_ROLLOUT, B, *noise.shape[1:], *lm_states.shape[1:], step, version, int(deferred)),
                   dst=self.actor, group=self.ctl)
+        sends = _Outgoing()
         for buf in (noise.float().contiguous(), lm_states.contiguous(), valid.to(torch.uint8).contiguous()):
-            dist.send(buf, dst=self.actor)
-        return B, tuple(noise.shape[1:]), noise.device, deferred
+            sends.send(buf, self.actor)
+        return B, tuple(noise.shape[1:]), noise.device, deferred, sends
 
     def collect(self, handle):
-        B, shape, device, deferred = handle
+        B, shape, device, deferred, sends = handle
         if deferred:
             dist.send(_hdr(KIND_COLLECT), dst=self.actor, group=self.ctl)
         states = torch.empty(B * self.m, *shape, device=device)
         t = torch.empty(B * self.m, device=device)
         dist.recv(states, src=self.actor)
         dist.recv(t, src=self.actor)
+        sends.wait()  # long complete: the actor replied after receiving the job
         return states, t
 
     def stop(self):
