@@ -93,3 +93,16 @@ def test_profile_stacks_map_ops_to_python_frames(tmp_path, monkeypatch):
     prof.step_end(0)
     assert {"stacks_rank0.txt", "ops_by_frame_rank0.txt"} <= set(os.listdir(tmp_path))
     assert "my_training_phase" in open(tmp_path / "ops_by_frame_rank0.txt").read()
+
+
+def test_component_bench_harness_on_cpu():
+    """ops/component_bench.py (the reference's tests/bench_ckpt.py and bench_te.py) runs its patterns on a tiny
+    case: one row per checkpointing mode and per LM depth (CPU wall clock, no memory figures)."""
+    from trenowanie_generatora_obrazkow_b200.ops import component_bench as C
+    rows = C.ckpt_bench(size="nano", blocks=2, mb=2, inflight=2, res=128, text_len=8, modes=("none", "full"),
+                        iters=1, warmup=0, device="cpu", log=lambda s: None)
+    assert [r["mode"] for r in rows] == ["none", "full"] and all(r["ms_per_microbatch"] > 0 for r in rows)
+    assert rows[0]["peak_mb"] is None
+    rows = C.te_bench(layers=(1, 2), batch=3, tokens=8, n_embd=64, n_head=2, iters=1, warmup=0, device="cpu",
+                      log=lambda s: None)
+    assert [r["layers"] for r in rows] == [1, 2] and rows[1]["weights_mb"] > rows[0]["weights_mb"]
