@@ -176,3 +176,53 @@ def test_diloco_gradient_noise_scale(shards, tmp_path):
                        env=dict(os.environ, CUDA_VISIBLE_DEVICES="", DIST_BACKEND="gloo"))
     assert r.returncode == 0, r.stderr[-3000:]
     assert r.stdout.count("gradient noise scale") == 2, r.stdout[-2000:]
+
+
+def test_init_by_name_with_growth_and_a_new_text_encoder():
+    """utils/checkpoint.init_named: EMA weights by name; blocks past the checkpoint's depth start as identity blocks
+    (zeroed attn.out / cross.out / mlp.out_proj, the rest of their fresh init kept); a text encoder of another shape
+    stays fresh; a denoiser of another width is refused."""
+    from dataclasses import asdict, replace
+
+    from trenowanie_generatora_obrazkow_b200.models import build_models
+    from trenowanie_generatora_obrazkow_b200.models.config import make_configs
+    from trenowanie_generatora_obrazkow_b200.utils import checkpoint as ckpt
+    den_cfg, te_cfg = make_configs("nano", "13m")
+    torch.manual_seed(0)
+    te, den = build_models(den_cfg, te_cfg)
+    params = list(te.parameters()) + list(den.parameters())
+    ema = [torch.randn_like(p) for p in params]  # distinguishable from the raw weights
+    ck = dict(step=7, den_config=asdict(den_cfg), te_config=asdict(te_cfg), te=te.state_dict(), den=den.state_dict(),
+              ema=ema)
+    te2_cfg = replace(te_cfg, dim=256, heads=4, mlp_hidden=512)
+    torch.manual_seed(1)
+    te2, den2 = build_models(replace(den_cfg, depth=6, text_dim=256), te2_cfg)
+    fresh_mlp = den2.blocks[5].mlp.in_proj.weight.clone()
+    named = [("te", n, p) for n, p in te2.named_parameters()] + [("den", n, p) for n, p in den2.named_parameters()]
+    with pytest.raises(ValueError, match="another shape"):  # text_dim 256 changes the cross-attention kv width
+        ckpt.init_named(ck, named, log=lambda *a: None)
+    torch.manual_seed(1)  # the same width, another MLP: the text encoder's MLP weights stay fresh
+    te2, den2 = build_models(replace(den_cfg, depth=6), replace(te_cfg, mlp_hidden=512))
+    fresh_mlp = den2.blocks[5].mlp.in_proj.weight.clone()
+    named = [("te", n, p) for n, p in te2.named_parameters()] + [("den", n, p) for n, p in den2.named_parameters()]
+    res = ckpt.init_named(ck, named, log=lambda *a: None)
+    by_name = dict(zip([n for n, _ in den.named_parameters()], ema[len(list(te.parameters())):]))
+    assert torch.equal(den2.blocks[3].attn.qkv.weight, by_name["blocks.3.attn.qkv.weight"])
+    assert res["grown"] == [4, 5] and res["fresh"] and all(f.startswith("te.") for f in res["fresh"])
+    for i in (4, 5):
+        for name in ckpt.GROW_ZERO:
+            assert den2.blocks[i].get_parameter(name).abs().max() == 0
+    assert torch.equal(den2.blocks[5].mlp.in_proj.weight, fresh_mlp)
+
+
+def test_train_init_grows_depth(tmp_path):
+    """train.py --init with a larger --depth: the grown run starts and trains."""
+    a = str(tmp_path / "a")
+    _run(["--synthetic", "16", "--out", a, "--size", "nano", "--te-size", "13m", "--batch", "2", "--micro-batch", "2",
+          "--steps", "1", "--eval-every", "0", "--no-wandb"])
+    out = _run(["--synthetic", "16", "--out", str(tmp_path / "b"), "--size", "nano", "--depth", "6", "--te-size", "13m",
+                "--batch", "2", "--micro-batch", "2", "--steps", "1", "--eval-every", "0", "--no-wandb", "--init",
+                os.path.join(a, "latest.pt")])
+    assert "blocks 4-5 grown as identity blocks" in out
+    ck = torch.load(str(tmp_path / "b" / "latest.pt"), weights_only=False)
+    assert ck["den_config"]["depth"] == 6

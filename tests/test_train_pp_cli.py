@@ -164,3 +164,43 @@ def test_opd_prefetch_with_a_teacher_rank(tmp_path):
                     "--micro-batch", "2", "--steps", "5", "--log-every", "1", "--opd-reuse", "2",
                     "--opd-rollout-steps", "4", "--opd-prefetch", "--opd-parts", "2", "--opd-learner-profile")
     assert "step 5/5" in out and "[teacher 1] served 4 requests" in out and "prefetch" in out
+
+
+def test_opd_init_checkpoint_and_resume(tmp_path):
+    """OPD learners: the student starts from a flow-matching checkpoint (--init, one block grown), checkpoints
+    carry the EMA and per-learner optimizer files, and a rerun resumes from latest.pt (with a fresh batch first)."""
+    import torch
+    fm = str(tmp_path / "fm")
+    _torchrun(1, "--out", fm, "--size", "nano", "--te-size", "states-nano", "--res", "128", "--batch", "2",
+              "--micro-batch", "2", "--steps", "1", "--log-every", "1", "--ckpt-every", "1")
+    opd = str(tmp_path / "opd")
+    common = ["--out", opd, "--size", "nano", "--depth", "5", "--te-size", "states-nano", "--dance-opd",
+              "--teacher-size", "nano", "--res", "128", "--batch", "4", "--micro-batch", "2", "--log-every", "1",
+              "--opd-reuse", "2", "--opd-rollout-steps", "2", "--ckpt-every", "2"]
+    out = _torchrun(2, *common, "--steps", "3", "--init", os.path.join(fm, "latest.pt"))
+    assert "step 3/3" in out and "blocks 4-4 grown as identity blocks" in out
+    ck = torch.load(os.path.join(opd, "latest.pt"), weights_only=False)
+    assert ck["step"] == 3 and ck["ema"] and ck["den_config"]["depth"] == 5 and "opd_caption_micro" in ck["extra"]
+    assert sorted(f for f in os.listdir(opd) if f.startswith("opt_")) == ["opt_stage0_rep0.pt", "opt_stage0_rep1.pt"]
+    out = _torchrun(2, *common, "--steps", "5")
+    assert "resumed from" in out and "at step 3" in out and "step 5/5" in out and "step 1/5" not in out
+    assert torch.load(os.path.join(opd, "latest.pt"), weights_only=False)["step"] == 5
+
+
+def test_opd_caption_position_survives_a_resume(tmp_path):
+    """OPD on shard captions: the checkpoint records how many caption micro-batches the trained fresh batches
+    used (2 fresh batches of 4 captions in micro-batches of 2 = 4), and a resume continues the caption stream."""
+    import torch
+
+    from trenowanie_generatora_obrazkow_b200.data.shards import write_synthetic_shards
+    data = str(tmp_path / "shards")
+    write_synthetic_shards(data, n_shards=2, per_shard=8, side=8)
+    out = str(tmp_path / "opd")
+    common = ["--out", out, "--data", data, "--fraction", "1", "--size", "nano", "--te-size", "states-nano",
+              "--dance-opd", "--teacher-size", "nano", "--res", "128", "--batch", "4", "--micro-batch", "2",
+              "--log-every", "1", "--opd-reuse", "2", "--opd-rollout-steps", "2", "--random-lm", "--lm-layers", "1",
+              "--ckpt-every", "3", "--workers", "0"]
+    _torchrun(1, *common, "--steps", "3")
+    assert torch.load(os.path.join(out, "latest.pt"), weights_only=False)["extra"]["opd_caption_micro"] == 4
+    _torchrun(1, *common, "--steps", "4")  # one more fresh batch from the resumed stream
+    assert torch.load(os.path.join(out, "latest.pt"), weights_only=False)["extra"]["opd_caption_micro"] == 6

@@ -294,10 +294,12 @@ def main():
         step, samples = int(resume["step"]), int(resume.get("samples", 0))
         tr.step_idx = step
         log(f"resumed from {ckpt_path} at step {step}")
-    elif args.init:
+    elif args.init:  # EMA weights by name; a larger --depth grows identity blocks, a new text encoder stays fresh
         init = ckpt.load(args.init)
-        ckpt.load_weights(init, te, den, use_ema=bool(init.get("ema")))
-        log(f"init: weights from {args.init} (step {init.get('step')})")
+        named = [("te", n, p) for n, p in te.named_parameters()] + [("den", n, p) for n, p in den.named_parameters()]
+        ckpt.init_named(init, named, log)
+        ckpt.reset_ema(tr.ema)
+        log(f"init: weights from {args.init}")
     elif args.load_hf:
         from trenowanie_generatora_obrazkow_b200.utils.export import load_export
         xte, xden, _, _, _ = load_export(args.load_hf)

@@ -368,6 +368,11 @@ def run_fm(args, den_cfg, te_cfg, lay, device, ctl, text_group):
     step, samples = pp_checkpoint.resume(tr, args.out, args.resume_opt_mismatch, group=learner_group)
     if step and tr.first and tr.replica == 0:
         print(f"[stage 0] resumed from {os.path.join(args.out, 'latest.pt')} at step {step}", flush=True)
+    elif not step and args.init:  # this stage's tensors by name; a larger --depth grows identity blocks
+        quiet = tr.replica != 0
+        ckpt.init_named(ckpt.load(args.init), tr.named,
+                        log=(lambda *a: None) if quiet else (lambda m: print(f"[stage {tr.stage}] {m}", flush=True)))
+        ckpt.reset_ema(tr.ema)
     side, L = den_cfg.latent_size, te_cfg.max_tokens
     n = M * args.micro_batch
     root = args.img_dir or args.data
@@ -508,6 +513,9 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
     n_learn = lay.n_learners
     role = lay.role(rank)
     learner_group = dist.new_group(lay.learners)
+    # checkpoint groups (Gloo): learner 0 alone gathers the weights; all learners agree on the commit
+    save_group = dist.new_group(lay.learners[:1], backend="gloo")
+    ckpt_group = dist.new_group(lay.learners, backend="gloo")
     if role in ("lm", "vae"):
         serve(args, role, lay, te_cfg, device, ctl, text_group, 1)
         return
@@ -534,15 +542,37 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         print(f"[actor {rank}] {jobs} rollout jobs", flush=True)
         return
     # ---- learner ----
+    from types import SimpleNamespace
+
+    from trenowanie_generatora_obrazkow_b200.optim import EMA, lr_mult
+    from trenowanie_generatora_obrazkow_b200.train import pp_checkpoint
     lrank = lay.learners.index(rank)
     named = [(pre, n, p) for pre, mod in (("te", te), ("den", den)) for n, p in mod.named_parameters()]
     opts, _ = build_optimizers(named, lr_muon=args.lr_muon, lr_adam=args.lr_adam, wd=args.wd, group=learner_group)
+    ema = EMA([p for p in params if p.requires_grad], args.ema or 0.9995 ** (args.batch / 256)) if lrank == 0 \
+        else None
+    # what the pipeline checkpoint code reads: one stage (pp 1), one replica per learner (its optimizer file)
+    state = SimpleNamespace(pp=1, dp=n_learn, stage=0, replica=lrank, named=named, ema=ema, opts=opts,
+                            den_cfg=den_cfg, te_cfg=te_cfg, te_cost=0.0, step_idx=0)
+    step0, samples = pp_checkpoint.resume(state, args.out, args.resume_opt_mismatch, group=ckpt_group)
+    extra = getattr(state, "ckpt_extra", {})
+    if step0 and lrank == 0:
+        print(f"[learner] resumed from {os.path.join(args.out, 'latest.pt')} at step {step0} (the replay cache is "
+              "not checkpointed: the first step rolls out a fresh batch)", flush=True)
+    elif not step0 and args.init:  # the student from a trained checkpoint (EMA weights by name; growth as train.py)
+        ckpt.init_named(ckpt.load(args.init), named, log=(lambda m: print(f"[learner] {m}", flush=True))
+                        if lrank == 0 else (lambda *a: None))
+        ckpt.reset_ema(ema)
+    warmup = int(args.warmup_frac * args.steps)
     teacher = TeacherClient(lay.teachers, ctl, rank) if lay.teachers else None
     if teacher is None:
         tcfg = replace(SIZES[args.teacher_size], text_dim=den_cfg.text_dim, latent_size=den_cfg.latent_size)
         torch.manual_seed(1234)
         tte, tden = build_models(tcfg, te_cfg, device=device)
-        randomize_teacher(tden)
+        if args.teacher_ckpt:
+            ckpt.load_weights(ckpt.load(args.teacher_ckpt), tte, tden, use_ema=True)
+        else:
+            randomize_teacher(tden)
         teacher = DiTTeacher(tte, tden, args.opd_cfg)
     actors = [ActorClient(a, ctl, args.opd_states) for a in lay.actors]
     actor = actors[lrank % len(actors)] if actors else None
@@ -564,19 +594,26 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
 
     cap_loader = local_lm = None
     if not args.synthetic and os.path.isdir(args.data):  # shard captions (OPD needs no latents); LM server or here
-        cap_loader = shard_loader(args, te_cfg, den_cfg, args.micro_batch, lrank, n_learn, 0, False)
+        cap_loader = shard_loader(args, te_cfg, den_cfg, args.micro_batch, lrank, n_learn,
+                                  int(extra.get("opd_caption_micro", 0)), False)
         if not args.lm_rank:
             local_lm, _ = build_lm(args, te_cfg, device)
     cap_cache = {}
+    # caption micro-batches read so far (from the resumed position) and where each fresh batch's captions began: a
+    # checkpoint records where the next untrained batch starts, so batches drawn ahead are read again on resume
+    cap_read = [int(extra.get("opd_caption_micro", 0))]
+    cap_start = {}
 
     def caption_ids(step):  # the captions of a step (seeded by step so the lookahead can prepare them)
         B = batch_shape(step)[1]
         if cap_loader is None:
             return synthetic_ids(torch.Generator().manual_seed(args.seed * 7919 + 104729 * rank + step), B, L)
         if step not in cap_cache:  # shard captions in step order (the lookahead asks ahead, the loop later)
+            cap_start[step] = cap_read[0]
             rows = []
             while sum(len(r) for r in rows) < B:
                 rows.append(fit_ids(next(cap_loader)[1], L))
+                cap_read[0] += 1
             cap_cache[step] = torch.cat(rows)[:B]
         return cap_cache[step]
 
@@ -584,7 +621,7 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
     if args.opd_text_ahead:  # fresh batches only: one every --opd-reuse steps
         lookahead = TextLookahead(lambda at: dict(ids=caption_ids(at), texts=[], step=at),
                                   lambda job: encode_remote(job, lay.lm_server_of(lrank), ctl, text_group),
-                                  0, args.steps, args.opd_reuse, args.opd_text_ahead)
+                                  step0, args.steps, args.opd_reuse, args.opd_text_ahead)
 
     def fresh_data(step):
         """(noise, LM states, valid) of the fresh batch that starts at ``step`` (replay steps draw nothing); seeded
@@ -640,7 +677,7 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         p["teacher"] = teacher.request(p["x"], p["t"], p["kw"], chunks=args.opd_parts, deferred=True)
 
     t0 = time.time()
-    for step in range(args.steps):
+    for step in range(step0, args.steps):
         res, B = batch_shape(step)
         side = res // 16
         shift = step_shift(step)
@@ -687,6 +724,8 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
                            actor=(client, client.request(noise_n, st_n, valid_n, nxt, version, deferred=True)))
         elif pending is not None and "actor" in pending and step == pending["step"] - 1:
             states_to_teacher(pending)  # last replay update of the cycle: the teacher scores meanwhile
+        if fresh:
+            samples += B * n_learn
         tl0 = time.time()
         loss = learner.step_grads(step)
         t_learn = time.time() - tl0
@@ -696,9 +735,11 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
                     dist.all_reduce(p.grad, group=learner_group)
                     p.grad /= n_learn
         torch.nn.utils.clip_grad_norm_(params, args.clip)
-        set_lr(opts, 1.0)
+        set_lr(opts, lr_mult(step, args.steps, warmup, args.schedule))
         for o in opts:
             o.step()
+        if ema is not None:
+            ema.update(step + 1)
         t_pref = 0.0
         if args.opd_prefetch and pending is None and learner.uses == 1 and step + learner.reuse < args.steps:
             # after the first update of a cache: the next cycle's rollouts with the weights of now (stale by
@@ -734,6 +775,15 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         if args.opd_actor_profile and actor is not None and t_roll:
             print(f"[actor profile] learner {lrank} step {step + 1}: {len(noise)} rollouts of "
                   f"{args.opd_rollout_steps} steps in {t_roll * 1e3:.0f} ms (request to reply)", flush=True)
+        if args.ckpt_every and ((step + 1) % args.ckpt_every == 0 or step + 1 == args.steps):
+            # the caption position saved is where the next untrained fresh batch starts (batches drawn ahead for
+            # the actor, a prefetch or the lookahead are read again after a resume)
+            nxt = pending["step"] if pending is not None else step + 1 + max(0, learner.reuse - learner.uses)
+            pp_checkpoint.save(state, args.out, step + 1, samples, vars(args), save_group, ckpt_group,
+                               keep=(step + 1) in args.keep_ckpt_steps,
+                               extra=dict(opd_caption_micro=cap_start.get(nxt, cap_read[0])))
+            for k in [k for k in cap_start if k < nxt]:
+                del cap_start[k]
     if lookahead is not None:
         lookahead.close()
     if lm_client is not None:

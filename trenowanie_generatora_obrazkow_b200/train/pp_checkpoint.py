@@ -41,8 +41,9 @@ def _unsplit_order(den_cfg, te_cfg):
     return [("te", n) for n, _ in te.named_parameters()] + [("den", n) for n, _ in den.named_parameters()]
 
 
-def save(tr, out, step, samples, args, save_group, learner_group, keep=False):
-    """Collective over the learner ranks. save_group: Gloo group of replica 0's stages (ranks 0 .. pp - 1)."""
+def save(tr, out, step, samples, args, save_group, learner_group, keep=False, extra=None):
+    """Collective over the learner ranks. save_group: Gloo group of replica 0's stages (ranks 0 .. pp - 1);
+    ``extra``: a dict kept in latest.pt under "extra" (``resume`` puts it on ``tr.ckpt_extra``)."""
     os.makedirs(out, exist_ok=True)
     if hasattr(tr, "before_save"):
         tr.before_save()  # sharded optimizer state into the optimizers (collective over the stage group)
@@ -66,7 +67,7 @@ def save(tr, out, step, samples, args, save_group, learner_group, keep=False):
                       te={n: params[(pre, n)] for pre, n in order if pre == "te"},
                       den={n: params[(pre, n)] for pre, n in order if pre == "den"},
                       opts=None, ema=[ema.get(k, params[k]) for k in order], args=dict(args or {}),
-                      outer=None, repa_proj=None, pp_layout=dict(pp=tr.pp, dp=tr.dp))
+                      outer=None, repa_proj=None, pp_layout=dict(pp=tr.pp, dp=tr.dp), extra=dict(extra or {}))
             writes.append((ck, latest))
     ckpt.two_phase_commit(writes, agree=ckpt.agree_all(learner_group))
     if keep and dist.get_rank() == 0:
@@ -87,6 +88,7 @@ def resume(tr, out, resume_opt_mismatch=False, log=print, group=None):
     if not os.path.exists(latest):
         return 0, 0
     ck = ckpt.load(latest)
+    tr.ckpt_extra = dict(ck.get("extra") or {})
     order = _unsplit_order(tr.den_cfg, tr.te_cfg)
     ema_by_name = dict(zip(order, ck["ema"])) if ck.get("ema") and len(ck["ema"]) == len(order) else {}
     for pre, n, p in tr.named:

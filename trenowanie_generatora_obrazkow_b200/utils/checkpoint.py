@@ -209,6 +209,72 @@ def load_opt_state(opt, state):
         g.update(f)
 
 
+# output projections that start at zero in a block added by growth (each new block starts as the identity)
+GROW_ZERO = ("attn.out.weight", "cross.out.weight", "mlp.out_proj.weight")
+
+
+def _param_order(ck):
+    """[(prefix, name)] of the checkpoint's own models in parameters() order (the flat EMA list's order)."""
+    from ..models import build_models
+    from ..models.config import configs_from_ckpt
+    if "den_config" not in ck:
+        return None
+    den_cfg, te_cfg = configs_from_ckpt(ck)
+    with torch.device("meta"):
+        te, den = build_models(den_cfg, te_cfg)
+    return [("te", n) for n, _ in te.named_parameters()] + [("den", n) for n, _ in den.named_parameters()]
+
+
+@torch.no_grad()
+def init_named(ck, named, log=print):
+    """``--init`` (reference train.py:617-660, train_pp.py:1272-1426): the weights of checkpoint ``ck`` -- its EMA
+    when it has one, else the raw weights -- copied by name into ``named`` = [(prefix "te" | "den", name, tensor)]
+    (a whole model or one pipeline stage's part of it).
+
+    Growth (SANA-1.5 style): denoiser blocks past the checkpoint's depth keep their fresh initialisation with
+    attn.out, cross.out and mlp.out_proj zeroed, so each new block starts as the identity. A text encoder of another
+    shape stays fresh (a new text encoder on a trained denoiser). Any other denoiser tensor that the checkpoint lacks
+    or holds in another shape is an error. Returns dict(loaded, grown (block indices), fresh (names))."""
+    src = {"te": dict(ck.get("te") or {}), "den": dict(ck["den"])}
+    if ck.get("ema"):
+        order = _param_order(ck)
+        if order is not None and len(order) == len(ck["ema"]):
+            for (pre, n), e in zip(order, ck["ema"]):
+                src[pre][n] = e
+        else:
+            log("init: the checkpoint's EMA list does not match its configuration; using its raw weights")
+    old_depth = 1 + max((int(k.split(".")[1]) for k in src["den"] if k.startswith("blocks.")), default=-1)
+    loaded, fresh, grown = 0, [], set()
+    for pre, n, t in named:
+        w = src.get(pre, {}).get(n)
+        if w is not None and tuple(w.shape) == tuple(t.shape):
+            t.copy_(w.to(device=t.device, dtype=t.dtype))
+            loaded += 1
+        elif pre == "den" and n.startswith("blocks.") and int(n.split(".")[1]) >= old_depth:
+            grown.add(int(n.split(".")[1]))
+            if n.endswith(GROW_ZERO):
+                t.zero_()
+        elif pre == "den":
+            raise ValueError(f"--init: denoiser tensor {n} is missing from the checkpoint or has another shape")
+        else:
+            fresh.append(f"{pre}.{n}")
+    what = f"init: {loaded} tensors from step {ck.get('step')} ({'EMA' if ck.get('ema') else 'raw'} weights)"
+    if grown:
+        what += f"; blocks {min(grown)}-{max(grown)} grown as identity blocks"
+    if fresh:
+        what += f"; {len(fresh)} text-encoder tensors kept fresh"
+    log(what)
+    return dict(loaded=loaded, grown=sorted(grown), fresh=fresh)
+
+
+@torch.no_grad()
+def reset_ema(ema):
+    """EMA shadows set to the current weights (after an --init load replaced the weights the EMA was made from)."""
+    if ema is not None:
+        for p, s in zip(ema.params, ema.shadow):
+            s.copy_(p.detach().to(s.device, torch.float32))
+
+
 @torch.no_grad()
 def load_weights(ck, te, den, strict=True, use_ema=False):
     """Load te / den from a checkpoint dict; use_ema: copy the flat EMA list instead of the raw weights."""
