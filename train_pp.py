@@ -548,9 +548,15 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
     from trenowanie_generatora_obrazkow_b200.train import pp_checkpoint
     lrank = lay.learners.index(rank)
     named = [(pre, n, p) for pre, mod in (("te", te), ("den", den)) for n, p in mod.named_parameters()]
-    opts, _ = build_optimizers(named, lr_muon=args.lr_muon, lr_adam=args.lr_adam, wd=args.wd, group=learner_group)
-    ema = EMA([p for p in params if p.requires_grad], args.ema or 0.9995 ** (args.batch / 256)) if lrank == 0 \
-        else None
+    # the same optimizer settings as the flow-matching trainers (TrainConfig.derived: LR scaled by the square root
+    # of the global batch / 256 unless --no-lr-batch-scaling; EMA decay 0.9995 ** (batch / 256) unless --ema)
+    ocfg = TrainConfig(global_batch=args.batch, ema=args.ema, no_lr_batch_scaling=args.no_lr_batch_scaling)
+    lr_scale, ema_decay = ocfg.derived(n_learn)
+    opts, _ = build_optimizers(named, optimizer=args.optimizer, lr_muon=args.lr_muon, lr_emb=args.lr_emb,
+                               lr_adam=args.lr_adam, lr_hidden=args.lr_hidden, lr_scale=lr_scale, wd=args.wd,
+                               beta2=args.beta2, momentum=args.momentum, ns_steps=args.ns_steps, cmuon=args.cmuon,
+                               muon_period=args.muon_period, muon_gamma=args.muon_gamma, group=learner_group)
+    ema = EMA([p for p in params if p.requires_grad], ema_decay) if lrank == 0 else None
     # what the pipeline checkpoint code reads: one stage (pp 1), one replica per learner (its optimizer file)
     state = SimpleNamespace(pp=1, dp=n_learn, stage=0, replica=lrank, named=named, ema=ema, opts=opts,
                             den_cfg=den_cfg, te_cfg=te_cfg, te_cost=0.0, step_idx=0)
