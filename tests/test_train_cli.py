@@ -226,3 +226,24 @@ def test_train_init_grows_depth(tmp_path):
     assert "blocks 4-5 grown as identity blocks" in out
     ck = torch.load(str(tmp_path / "b" / "latest.pt"), weights_only=False)
     assert ck["den_config"]["depth"] == 6
+
+
+def test_train_pl_prob_and_ema_cpu_flags(tmp_path):
+    """--pl-prob draws that share of captions from the Polish token rows (frozen-LM encoder), --ema-cpu needs
+    --diloco and keeps the EMA on the host."""
+    import shutil
+
+    from trenowanie_generatora_obrazkow_b200.data.shards import write_synthetic_shards
+    data = str(tmp_path / "shards")
+    names = write_synthetic_shards(data, n_shards=3, per_shard=8, side=16, lm_suffix="slayer149")
+    for n in names:
+        shutil.copy(os.path.join(data, f"{n}.tok_slayer149.npy"), os.path.join(data, f"{n}.tok_slayer149_pl.npy"))
+    out = _run(["--data", data, "--fraction", "1", "--out", str(tmp_path / "a"), "--size", "nano", "--te-size",
+                "slayer149", "--random-lm", "--pl-prob", "0.5", "--batch", "2", "--micro-batch", "2", "--steps", "1",
+                "--eval-every", "0", "--workers", "0", "--no-wandb"])
+    assert "captions: 50% Polish (slayer149_pl)" in out
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "train.py"), "--synthetic", "8", "--out",
+                        str(tmp_path / "b"), "--size", "nano", "--te-size", "13m", "--batch", "2", "--micro-batch", "2",
+                        "--steps", "1", "--no-wandb", "--ema-cpu"], cwd=ROOT, capture_output=True, text=True,
+                       timeout=600, env=dict(os.environ, CUDA_VISIBLE_DEVICES=""))
+    assert r.returncode != 0 and "--ema-cpu needs --diloco" in r.stderr

@@ -48,8 +48,10 @@ def build_parser():
     a("--te-experts", type=int, default=None)
     a("--te-quant", choices=["", "int8"], default=None)
     a("--random-lm", action="store_true", help="frozen-LM encoders: a fixed random embedding stands in for the LM")
-    a("--ema-cpu", action="store_true")
-    a("--pl-prob", type=float, default=0.0)
+    a("--ema-cpu", action="store_true", help="keep the EMA on the CPU (pinned); needs --diloco, whose EMA is updated "
+      "only at the outer syncs")
+    a("--pl-prob", type=float, default=0.0, help="share of training captions from the Polish token rows "
+      "(<shard>.tok_<enc>_pl.npy, prepare_data.py tokenize --lang pl); validation stays English")
     a("--rope-ref", type=int, default=0,
       help="RoPE position field: 0 = integer positions per grid; N = every resolution spread over an N x N field")
     a("--rope-random", action="store_true",
@@ -249,6 +251,7 @@ def main():
         den_cfg = DenoiserConfig(**resume["den_config"])
         te_cfg = te_config_from_dict(resume["te_config"])
     assert not args.rope_random or den_cfg.rope_ref, "--rope-random needs --rope-ref (the position field)"
+    assert not args.ema_cpu or args.diloco, "--ema-cpu needs --diloco (the host EMA is updated at the outer syncs)"
     assert not args.crop_res or den_cfg.micro_cond, "--crop-res needs --micro-cond"
     cuda = device.type == "cuda"
     transport = args.grad_transport if args.grad_transport != "auto" else ("p2p" if cuda else "nccl")
@@ -262,7 +265,7 @@ def main():
                      no_lr_batch_scaling=args.no_lr_batch_scaling, wd=args.wd, beta2=args.beta2,
                      momentum=args.momentum, ns_steps=args.ns_steps, cmuon=args.cmuon, muon_period=args.muon_period,
                      muon_gamma=args.muon_gamma, muon_momentum_dtype=args.muon_momentum_dtype, clip=args.clip,
-                     ema=args.ema, cfg_drop=args.cfg_drop, t_shift=args.t_shift, mlm_weight=args.mlm_weight,
+                     ema=args.ema, ema_cpu=args.ema_cpu, cfg_drop=args.cfg_drop, t_shift=args.t_shift, mlm_weight=args.mlm_weight,
                      mlm_every=args.mlm_every, mlm_prob=args.mlm_prob,
                      grad_comm=grad_comm, muon_comm=muon_comm, diloco=args.diloco,
                      powersgd_rank=args.powersgd_rank, powersgd_start=max(2, int(args.warmup_frac * args.steps)),
@@ -326,11 +329,17 @@ def main():
     else:
         tok_suffix = getattr(te_cfg, "tok_suffix", "")
         null_row = te.null_ids()
-        train_names, val_names = select_shards(args.data, args.fraction, tok_suffix)
+        # --pl-prob: that share of the training captions from the Polish token rows (<shard>.tok_<enc>_pl.npy);
+        # validation stays English (reference train.py:669-676)
+        alt_suffix = f"{tok_suffix}_pl" if args.pl_prob > 0 else ""
+        assert not alt_suffix or tok_suffix, "--pl-prob needs a frozen-LM text encoder with its own token rows"
+        train_names, val_names = select_shards(args.data, args.fraction, tok_suffix, alt_suffix)
         crops = [("lat" if r == 256 else f"lat{r}", "") for r in args.crop_res]
-        store = ShardStore(args.data, train_names, tok_suffix, null_row,
+        store = ShardStore(args.data, train_names, tok_suffix, null_row, alt_suffix=alt_suffix, alt_prob=args.pl_prob,
                            lat_kind="lat" if side == 16 else f"lat{args.res}", crops=crops, crop_prob=args.crop_prob,
                            cond_base=den_cfg.micro_cond)
+        if alt_suffix:
+            log(f"captions: {100 * args.pl_prob:.0f}% Polish ({alt_suffix}), the rest English")
         stream = TrainStream(store, tr.micro, rank, world, args.seed, start_micro=samples // (tr.micro * world))
         loader = iter(torch.utils.data.DataLoader(stream, batch_size=None, num_workers=args.workers,
                                                   pin_memory=device.type == "cuda",

@@ -144,8 +144,9 @@ def build_parser():
 # train.py flags the pipeline trainer does not run; they stop the run when set away from their defaults
 UNSUPPORTED = dict(diloco=(0, "DiLoCo / MuLoCo outer steps"), repa_weight=(0.0, "REPA"), offload=(False, "offload"),
                    multi_res=([], "mixed-resolution steps (the reference needs --pp 1 for them too)"),
-                   eval_only=(False, "--eval-only"), freeze_den=(False, "--freeze-den"), te_experts=(None, "MoE text "
-                   "encoder"), te_quant=(None, "quantized text encoder"), pl_prob=(0.0, "Polish captions"),
+                   eval_only=(False, "--eval-only"), freeze_den=(False, "--freeze-den"),
+                   te_experts=(None, "MoE text encoder"), te_quant=(None, "quantized text encoder"),
+                   ema_cpu=(False, "--ema-cpu (a host EMA updated at DiLoCo syncs)"),
                    rope_random=(False, "RPE-2D random positions"), length_sort=(False, "--length-sort"),
                    val_per_shard=(False, "validation per shard group (train.py --eval-every)"),
                    img_extra=("", "a second image directory"), img_extra_val=(False, "validation on --img-extra"))
@@ -310,7 +311,9 @@ def shard_loader(args, te_cfg, den_cfg, mb, replica, dp, start_micro, with_data)
     tok_suffix = getattr(te_cfg, "tok_suffix", "")
     with torch.device("meta"):
         null_row = build_text_encoder(te_cfg).null_ids()
-    names, _ = select_shards(root, args.fraction, tok_suffix)
+    alt_suffix = f"{tok_suffix}_pl" if args.pl_prob > 0 else ""  # --pl-prob: Polish token rows for that share
+    assert not alt_suffix or tok_suffix, "--pl-prob needs a frozen-LM text encoder with its own token rows"
+    names, _ = select_shards(root, args.fraction, tok_suffix, alt_suffix)
     side = args.res // 16
     kw = dict(lat_kind="lat" if side == 16 else f"lat{args.res}", lat_root=args.lat_dir)
     if with_data:
@@ -318,7 +321,7 @@ def shard_loader(args, te_cfg, den_cfg, mb, replica, dp, start_micro, with_data)
                   cond_base=den_cfg.micro_cond, img_res=args.res if args.img_dir else 0)
         if args.img_dir:
             kw.pop("crops"), kw.pop("crop_prob")
-    store = ShardStore(root, names, tok_suffix, null_row, **kw)
+    store = ShardStore(root, names, tok_suffix, null_row, alt_suffix, args.pl_prob, **kw)
     stream = TrainStream(store, mb, replica, dp, args.seed, start_micro=start_micro, captions_only=not with_data)
     return iter(torch.utils.data.DataLoader(stream, batch_size=None, num_workers=min(args.workers, 2) if with_data
                                             else 0, persistent_workers=False))

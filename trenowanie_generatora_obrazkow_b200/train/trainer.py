@@ -63,6 +63,7 @@ class TrainConfig:
     muon_momentum_dtype: str = "fp32"
     clip: float = 1.0
     ema: float = None
+    ema_cpu: bool = False         # the EMA in pinned host memory (with DiLoCo: updated only at the outer syncs)
     ema_on_all_ranks: bool = False
     cfg_drop: float = 0.1
     t_shift: float = 1.0
@@ -207,7 +208,8 @@ class Trainer:
             self.global_params = D.make_global(self.params, cfg.offload)
             self.outer_opt = D.make_outer_opt(self.global_params, cfg.outer_lr, cfg.outer_momentum)
         model_params = [p for pre, _, p in self.named if pre in ("te", "den") and p.requires_grad]
-        self.ema = EMA(model_params, ema) if (self.rank == 0 or cfg.ema_on_all_ranks) else None
+        self.ema = EMA(model_params, ema, device="cpu" if cfg.ema_cpu else None) \
+            if (self.rank == 0 or cfg.ema_on_all_ranks) else None
         self.step_idx = 0
         self.gen = torch.Generator(device=self.device)
         self.cpu_gen = torch.Generator().manual_seed(cfg.seed * 7 + self.rank)  # host-side shuffles
