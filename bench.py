@@ -521,8 +521,30 @@ def run_pp(args):
     dist.destroy_process_group()
 
 
+def launch_ranks(args, argv=None):
+    """``--gpus N`` without a launcher: re-run this command under torch.distributed.run with N ranks (one per GPU,
+    rendezvous on 127.0.0.1). Under a launcher the world size must equal --gpus."""
+    world = os.environ.get("WORLD_SIZE")
+    if world is not None:
+        if int(world) != args.gpus and args.gpus != 1:
+            raise SystemExit(f"bench.py --gpus {args.gpus} under a launcher with WORLD_SIZE={world}")
+        return None
+    if args.gpus <= 1:
+        return None
+    import socket
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", str(args.gpus),
+           "--master-addr", "127.0.0.1", "--master-port", str(port), os.path.abspath(__file__)]
+    return cmd + list(sys.argv[1:] if argv is None else argv)
+
+
 def main():
     args = parse()
+    cmd = launch_ranks(args)
+    if cmd is not None:
+        os.execv(sys.executable, cmd)
     if args.pp > 1:
         run_pp(args)
         return

@@ -163,3 +163,23 @@ def test_ckpt_tools_info_block_norms_and_resume_cmd(tmp_path):
     shutil.copy(latest, os.path.join(cont, "latest.pt"))
     _py(*args[5:])  # the same flags through the plain interpreter (one process)
     assert torch.load(os.path.join(cont, "latest.pt"), weights_only=False)["step"] == 3
+
+
+def test_bench_gpus_flag_launches_ranks(monkeypatch):
+    """bench.py --gpus N run directly re-runs itself under torch.distributed.run with N ranks; under a launcher the
+    world size must agree with --gpus."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_repo_bench", os.path.join(ROOT, "bench.py"))
+    B = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(B)
+    args = B.parse.__globals__["argparse"].Namespace(gpus=4)
+    monkeypatch.delenv("WORLD_SIZE", raising=False)
+    cmd = B.launch_ranks(args, ["--gpus", "4", "--steps", "2"])
+    assert cmd[1:4] == ["-m", "torch.distributed.run", "--nnodes"] and cmd[cmd.index("--nproc-per-node") + 1] == "4"
+    assert cmd[-4:] == [os.path.join(ROOT, "bench.py"), "--gpus", "4", "--steps", "2"][-4:]
+    assert "127.0.0.1" in cmd
+    monkeypatch.setenv("WORLD_SIZE", "4")
+    assert B.launch_ranks(args, []) is None
+    monkeypatch.setenv("WORLD_SIZE", "2")
+    with pytest.raises(SystemExit):
+        B.launch_ranks(args, [])
