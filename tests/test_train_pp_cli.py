@@ -204,3 +204,17 @@ def test_opd_caption_position_survives_a_resume(tmp_path):
     assert torch.load(os.path.join(out, "latest.pt"), weights_only=False)["extra"]["opd_caption_micro"] == 4
     _torchrun(1, *common, "--steps", "4")  # one more fresh batch from the resumed stream
     assert torch.load(os.path.join(out, "latest.pt"), weights_only=False)["extra"]["opd_caption_micro"] == 6
+
+
+def test_pipeline_ema_eval_and_merge_checkpoints(tmp_path):
+    """--eval-every: validation loss of the EMA weights on the unsplit model rebuilt on rank 0; --merge-every: raw
+    weights as merge/step_<n>.pt in train.py's layout, gathered from both stages."""
+    import torch
+    out = _torchrun(2, "--out", str(tmp_path), "--size", "nano", "--te-size", "states-nano", "--pp", "2",
+                    "--microbatches", "2", "--micro-batch", "2", "--res", "128", "--steps", "2", "--log-every", "2",
+                    "--eval-every", "2", "--val-samples", "8", "--merge-every", "1", "--merge-start", "0")
+    assert "[eval] step 2 | EMA val/loss=" in out
+    merged = sorted(os.listdir(tmp_path / "merge"))
+    assert merged == ["step_0000001.pt", "step_0000002.pt"]
+    ck = torch.load(tmp_path / "merge" / merged[-1], weights_only=False)
+    assert ck["step"] == 2 and ck["total_steps"] == 2 and "blocks.3.mlp.out_proj.weight" in ck["den"] and ck["te"]

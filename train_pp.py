@@ -327,6 +327,45 @@ def shard_loader(args, te_cfg, den_cfg, mb, replica, dp, start_micro, with_data)
                                             else 0, persistent_workers=False))
 
 
+def pp_val_data(args, te_cfg, den_cfg, tr, lm, lm_client, real, use_ids, device):
+    """Validation set of the EMA evaluation, on global rank 0 (stage 0 of replica 0): --val-samples held-out images
+    with their first captions as LM states (shards), or synthetic latents and states. None (with a note) when the
+    LM runs split over the stages, where rank 0 cannot compute whole states."""
+    from trenowanie_generatora_obrazkow_b200.data.shards import load_val, select_shards
+    from trenowanie_generatora_obrazkow_b200.models.text import build_text_encoder
+    if args.lm_split:
+        print("[eval] skipped: with --lm-split no rank holds the whole LM for the validation captions", flush=True)
+        return None
+    side = den_cfg.latent_size
+    g = torch.Generator().manual_seed(args.seed + 1)
+    if real and not args.img_dir:
+        tok_suffix = getattr(te_cfg, "tok_suffix", "")
+        _, val_names = select_shards(args.data, args.fraction, tok_suffix)
+        if not val_names:
+            print("[eval] skipped: no held-out shard", flush=True)
+            return None
+        with torch.device("meta"):
+            null_row = build_text_encoder(te_cfg).null_ids()
+        lat, ids = load_val(args.data, val_names, args.val_samples, tok_suffix, null_row,
+                            lat_kind="lat" if side == 16 else f"lat{args.res}", lat_root=args.lat_dir)
+    elif real:
+        print("[eval] skipped: packed-image data (the validation latents would need the VAE)", flush=True)
+        return None
+    else:
+        n = min(args.val_samples, 64)
+        lat = torch.randn(n, den_cfg.latent_channels, side, side, generator=g)
+        if not use_ids:
+            return lat, torch.randn(n, te_cfg.max_tokens, te_cfg.lm_dim, generator=g)
+        ids = synthetic_ids(g, n, te_cfg.max_tokens)
+    if lm is not None:
+        states = torch.cat([lm.states(c.to(device)).float().cpu() for c in ids.split(args.micro_batch)])
+    elif lm_client is not None:
+        states = lm_client.collect(lm_client.request(ids)).float().cpu()
+    else:
+        return lat, ids
+    return lat, states
+
+
 def fit_ids(ids, L):
     """Caption rows trimmed / padded (LM PAD) to the text encoder's max_tokens."""
     from trenowanie_generatora_obrazkow_b200.models.frozen_lm import LM_PAD
@@ -433,6 +472,9 @@ def run_fm(args, den_cfg, te_cfg, lay, device, ctl, text_group):
 
     prof = TrainingProfile(args.profile_dir, args.profile_start, args.profile_steps, args.profile_ranks,
                            dist.get_rank()) if args.profile_dir else None
+    eval_every = args.eval_every or 0
+    val = pp_val_data(args, te_cfg, den_cfg, tr, lm, lm_client, real, use_ids, device) \
+        if eval_every and dist.get_rank() == 0 else None
     t0 = time.time()
     while step < args.steps:
         ts = time.time()
@@ -487,6 +529,15 @@ def run_fm(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         if args.ckpt_every and (step % args.ckpt_every == 0 or step == args.steps):
             pp_checkpoint.save(tr, args.out, step, samples, vars(args), save_group, learner_group,
                                keep=step in args.keep_ckpt_steps)
+        if eval_every and (step % eval_every == 0 or step == args.steps):  # EMA weights on the unsplit model
+            res = pp_checkpoint.ema_eval(tr, save_group, val, device)
+            if res is not None:
+                print(f"[eval] step {step} | EMA " + " ".join(f"{k}={v:.4f}" for k, v in res.items()), flush=True)
+            dist.barrier(group=learner_group)
+        if args.merge_every and step >= args.merge_start * args.steps and (
+                step % args.merge_every == 0 or step == args.steps):  # raw weights for merge.py (WSM)
+            pp_checkpoint.merge_save(tr, args.out, step, args.steps, save_group)
+            dist.barrier(group=learner_group)
     for c in {id(c): c for c in (lm_client, vae_client) if c is not None}.values():
         c.stop()
 

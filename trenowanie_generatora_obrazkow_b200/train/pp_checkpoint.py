@@ -116,3 +116,56 @@ def resume(tr, out, resume_opt_mismatch=False, log=print, group=None):
     step = int(ck.get("step", 0))
     tr.step_idx = step
     return step, int(ck.get("samples", 0))
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# WSM merge checkpoints and EMA evaluation of the unsplit model (reference train_pp.py:2450-2462)
+# ---------------------------------------------------------------------------------------------------------------
+def gather_unsplit(tr, save_group, ema=False):
+    """Replica 0's stages send their tensors (``ema``: the EMA where there is one) to global rank 0 under the unsplit
+    names. Collective over ``save_group``; returns (te state, den state) on global rank 0, None elsewhere."""
+    if tr.replica != 0:
+        return None
+    trainable = [(pre, n) for pre, n, p in tr.named if p.requires_grad]
+    part = {(pre, n): p.detach().float().cpu() for pre, n, p in tr.named}
+    if ema and tr.ema is not None:
+        part.update({k: s.detach().float().cpu() for k, s in zip(trainable, tr.ema.shadow)})
+    got = [None] * tr.pp if dist.get_rank() == 0 else None
+    dist.gather_object(part, got, dst=0, group=save_group)
+    if dist.get_rank() != 0:
+        return None
+    merged = {}
+    for g in got:
+        merged.update(g)
+    order = _unsplit_order(tr.den_cfg, tr.te_cfg)
+    return ({n: merged[(pre, n)] for pre, n in order if pre == "te"},
+            {n: merged[(pre, n)] for pre, n in order if pre == "den"})
+
+
+def merge_save(tr, out, step, total_steps, save_group):
+    """WSM: the raw fp32 weights as merge/step_<step>.pt in train.py's layout (utils/checkpoint.save_merge), written
+    by global rank 0. Collective over replica 0's stages."""
+    got = gather_unsplit(tr, save_group, ema=False)
+    if got is None:
+        return None
+    path = os.path.join(out, "merge", f"step_{step:07d}.pt")
+    os.makedirs(os.path.dirname(path), exist_ok=True)
+    ckpt.atomic_save(dict(step=step, total_steps=total_steps, den_config=asdict(tr.den_cfg),
+                          te_config=asdict(tr.te_cfg), te=got[0], den=got[1]), path)
+    return path
+
+
+def ema_eval(tr, save_group, val, device):
+    """Validation loss of the EMA weights (train/evaluate.py: 4 t buckets and the t in 0.9-1.0 slice) on the unsplit
+    model rebuilt on global rank 0. Collective over replica 0's stages; the result dict on rank 0, else None."""
+    got = gather_unsplit(tr, save_group, ema=True)
+    if got is None or val is None:
+        return None
+    from .evaluate import evaluate
+    te, den = build_models(tr.den_cfg, tr.te_cfg, device=device)
+    te.load_state_dict(got[0])
+    den.load_state_dict(got[1])
+    res = evaluate(te, den, val, device)
+    del te, den
+    return res
+
