@@ -177,8 +177,9 @@ def test_opd_init_checkpoint_and_resume(tmp_path):
     common = ["--out", opd, "--size", "nano", "--depth", "5", "--te-size", "states-nano", "--dance-opd",
               "--teacher-size", "nano", "--res", "128", "--batch", "4", "--micro-batch", "2", "--log-every", "1",
               "--opd-reuse", "2", "--opd-rollout-steps", "2", "--ckpt-every", "2"]
-    out = _torchrun(2, *common, "--steps", "3", "--init", os.path.join(fm, "latest.pt"))
-    assert "step 3/3" in out and "blocks 4-4 grown as identity blocks" in out
+    out = _torchrun(2, *common, "--steps", "3", "--init", os.path.join(fm, "latest.pt"), "--eval-every", "3",
+                    "--val-samples", "4")
+    assert "step 3/3" in out and "blocks 4-4 grown as identity blocks" in out and "[eval] step 3 | EMA val/loss=" in out
     ck = torch.load(os.path.join(opd, "latest.pt"), weights_only=False)
     assert ck["step"] == 3 and ck["ema"] and ck["den_config"]["depth"] == 5 and "opd_caption_micro" in ck["extra"]
     assert sorted(f for f in os.listdir(opd) if f.startswith("opt_")) == ["opt_stage0_rep0.pt", "opt_stage0_rep1.pt"]

@@ -721,6 +721,23 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         return torch.cat([teacher.velocity(states[a:b], t[a:b], {k: v[a:b] for k, v in kw.items()})
                           for a, b in bounds if b > a])
 
+    from trenowanie_generatora_obrazkow_b200.train.evaluate import evaluate
+    eval_every = args.eval_every or 0
+    use_ids = cap_loader is not None or te_cfg.backend != "states" or args.lm_rank > 0
+    val = pp_val_data(args, te_cfg, den_cfg, None, local_lm, lm_client, cap_loader is not None, use_ids, device) \
+        if eval_every and lrank == 0 else None
+
+    @torch.no_grad()
+    def ema_eval():
+        """Flow-matching validation loss of the student's EMA (swapped in, the live weights restored after)."""
+        live = [p.detach().clone() for p in ema.params]
+        ema.copy_to()
+        try:
+            return evaluate(te, den, val, device)
+        finally:
+            for p, w in zip(ema.params, live):
+                p.copy_(w)
+
     version = 0
     # the next cycle's batch in preparation: {"step", "kw"} plus either "actor": (client, job) while the actor rolls
     # it out, or "x", "t", "teacher" (a deferred teacher request) once the states are here
@@ -835,6 +852,11 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         if args.opd_actor_profile and actor is not None and t_roll:
             print(f"[actor profile] learner {lrank} step {step + 1}: {len(noise)} rollouts of "
                   f"{args.opd_rollout_steps} steps in {t_roll * 1e3:.0f} ms (request to reply)", flush=True)
+        if eval_every and ((step + 1) % eval_every == 0 or step + 1 == args.steps):
+            if ema is not None and val is not None:
+                res = ema_eval()
+                print(f"[eval] step {step + 1} | EMA " + " ".join(f"{k}={v:.4f}" for k, v in res.items()), flush=True)
+            dist.barrier(group=ckpt_group)
         if args.ckpt_every and ((step + 1) % args.ckpt_every == 0 or step + 1 == args.steps):
             # the caption position saved is where the next untrained fresh batch starts (batches drawn ahead for
             # the actor, a prefetch or the lookahead are read again after a resume)
