@@ -55,9 +55,10 @@ def evaluate(te, den, val, device, seed=1234, chunk=256, groups=(), den_chunk=0,
         buckets[1].index_add_(0, b, torch.ones_like(keep))
     te.train(was_training[0]), den.train(was_training[1])
     out = {"val/loss": tot / max(n, 1)}
-    for k in range(4):
-        out[f"val/loss_t{k / 4:.2f}-{(k + 1) / 4:.2f}"] = (buckets[0][k] / buckets[1][k].clamp(min=1)).item()
-    out["val/loss_t0.90-1.00"] = (hi[0] / hi[1].clamp(min=1)).item()
+    for k in range(4):  # a bucket without samples (small validation sets) reads nan, not a zero loss
+        out[f"val/loss_t{k / 4:.2f}-{(k + 1) / 4:.2f}"] = (buckets[0][k] / buckets[1][k]).item() \
+            if buckets[1][k] > 0 else float("nan")
+    out["val/loss_t0.90-1.00"] = (hi[0] / hi[1]).item() if hi[1] > 0 else float("nan")
     per_all, i = torch.cat(per_all), 0
     for label, count in groups:
         keep = ~hi_mask[i:i + count]
