@@ -6,7 +6,7 @@ seed, resolution).
   python app.py --model exports/homeimg --port 7860
 
 Open http://<this machine's LAN IP>:7860 (printed at startup). GET / serves the form; POST /generate with JSON
-{"prompt", "steps", "guidance", "seed", "res"} returns a PNG: the decoded image when the export carries a FLUX.2 VAE
+{"prompt", "steps", "guidance", "seed", "res", "count"} returns a PNG: the decoded image when the export carries a FLUX.2 VAE
 (and diffusers is importable), otherwise a false-colour preview of the latents.
 """
 import argparse
@@ -29,10 +29,12 @@ steps <input id="s" type="number" value="{steps}" min="1" max="100">
 guidance <input id="g" type="number" value="{guidance}" step="0.5">
 seed <input id="d" type="number" value="-1">
 res <select id="r">{res_options}</select>
+images <input id="n" type="number" value="1" min="1" max="8">
 <button onclick="go()">generate</button><br><img id="o" style="width:100%;margin-top:8px">
 <script>
 async function go() {{
-  const body = {{prompt: p.value, steps: +s.value, guidance: +g.value, seed: +d.value, res: +r.value}};
+  const body = {{prompt: p.value, steps: +s.value, guidance: +g.value, seed: +d.value, res: +r.value,
+                 count: +document.getElementById('n').value}};
   const resp = await fetch('/generate', {{method: 'POST', headers: {{'Content-Type': 'application/json'}},
                                          body: JSON.stringify(body)}});
   o.src = URL.createObjectURL(await resp.blob());
@@ -67,6 +69,7 @@ def build_app(pipe, default_res=1024, steps=30, guidance=3.0):
         guidance: float = d_guidance
         seed: int = -1
         res: int = d_res
+        count: int = 1  # images of the prompt (1-8), one noise draw each, returned as one grid
 
     app = FastAPI()
     options = "".join(f'<option value="{r}"{" selected" if r == default_res else ""}>{r}</option>'
@@ -79,12 +82,18 @@ def build_app(pipe, default_res=1024, steps=30, guidance=3.0):
     @app.post("/generate")
     def generate(req: Req):
         seed = req.seed if req.seed >= 0 else random.randrange(2 ** 31)
+        n = max(1, min(int(req.count), 8))
         with torch.no_grad():
-            out = pipe([req.prompt], height=req.res, num_inference_steps=max(1, min(req.steps, 100)),
+            out = pipe([req.prompt] * n, height=req.res, num_inference_steps=max(1, min(req.steps, 100)),
                        guidance_scale=req.guidance, seed=seed)
-        img = out.images[0] if out.images is not None else latent_preview(out.latents)[0]
+        imgs = [np.asarray(i) for i in (out.images if out.images is not None else latent_preview(out.latents))]
+        cols = min(n, 4)
+        h, w = imgs[0].shape[:2]
+        grid = np.zeros((-(-n // cols) * h, cols * w, 3), dtype=np.uint8)
+        for k, im in enumerate(imgs):  # up to 4 per row
+            grid[(k // cols) * h:(k // cols + 1) * h, (k % cols) * w:(k % cols + 1) * w] = im
         buf = io.BytesIO()
-        Image.fromarray(np.asarray(img)).save(buf, format="PNG")
+        Image.fromarray(grid).save(buf, format="PNG")
         return Response(buf.getvalue(), media_type="image/png", headers={"X-Seed": str(seed)})
 
     return app

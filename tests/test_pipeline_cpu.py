@@ -120,6 +120,8 @@ def test_web_app_generates_png(tmp_path):
     r = client.post("/generate", json={"prompt": "a red fox", "steps": 2, "guidance": 3.0, "seed": 7, "res": 64})
     assert r.status_code == 200 and r.headers["x-seed"] == "7"
     assert Image.open(io.BytesIO(r.content)).size == (4, 4)
+    r = client.post("/generate", json={"prompt": "a red fox", "steps": 2, "seed": 7, "res": 64, "count": 6})
+    assert Image.open(io.BytesIO(r.content)).size == (4 * 4, 2 * 4)  # 6 images, 4 per row
 
 
 def test_homeimg_loader_isolates_exports(tmp_path):
