@@ -150,8 +150,10 @@ def test_pipeline_packed_images_local_encode(tmp_path):
     log = _torchrun(2, "--out", str(tmp_path / "run"), "--img-dir", data, "--fraction", "1", "--size", "nano",
                     "--te-size", "states-nano", "--pp", "2", "--microbatches", "2", "--micro-batch", "2", "--res",
                     "128", "--steps", "2", "--log-every", "2", "--random-lm", "--lm-layers", "2", "--workers", "0",
-                    "--enc-chunk", "2")
-    assert "step 2/2" in log and "data: images from" in log
+                    "--enc-chunk", "2", "--eval-every", "2", "--val-samples", "4")
+    assert "step 2/2" in log and "data: images from" in log and "[eval] step 2 | EMA val/loss=" in log
+    cache = os.listdir(tmp_path / "run" / "val_cache")  # the held-out images encoded once, then read from here
+    assert len(cache) == 1 and cache[0].startswith("val_") and cache[0].endswith(".pt")
 
 
 def test_opd_prefetch_with_a_teacher_rank(tmp_path):

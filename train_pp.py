@@ -348,9 +348,22 @@ def pp_val_data(args, te_cfg, den_cfg, tr, lm, lm_client, real, use_ids, device)
             null_row = build_text_encoder(te_cfg).null_ids()
         lat, ids = load_val(args.data, val_names, args.val_samples, tok_suffix, null_row,
                             lat_kind="lat" if side == 16 else f"lat{args.res}", lat_root=args.lat_dir)
-    elif real:
-        print("[eval] skipped: packed-image data (the validation latents would need the VAE)", flush=True)
-        return None
+    elif real:  # packed images: the held-out images VAE-encoded once per configuration, then read from the cache
+        from trenowanie_generatora_obrazkow_b200.data.shards import load_val_cached
+        tok_suffix = getattr(te_cfg, "tok_suffix", "")
+        _, val_names = select_shards(args.img_dir, args.fraction, tok_suffix)  # captions beside the images
+        if not val_names:
+            print("[eval] skipped: no held-out shard", flush=True)
+            return None
+        with torch.device("meta"):
+            null_row = build_text_encoder(te_cfg).null_ids()
+        enc = build_vae(args, device)
+        encode = (lambda u8: enc(u8.to(device)).float().cpu())
+        lat, ids = load_val_cached(
+            os.path.join(args.out, "val_cache"),
+            dict(names=val_names, n=args.val_samples, res=args.res, vae=args.vae or "patch-encoder", tok=tok_suffix),
+            lambda: load_val(args.img_dir, val_names, args.val_samples, tok_suffix, null_row, img_res=args.res,
+                             encode=encode))
     else:
         n = min(args.val_samples, 64)
         lat = torch.randn(n, den_cfg.latent_channels, side, side, generator=g)

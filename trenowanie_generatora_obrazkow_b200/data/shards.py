@@ -513,6 +513,22 @@ def load_val(root, names, n, tok_suffix="", null_row=None, lat_kind="lat", lat_r
     return torch.cat(lats), torch.cat(ids)
 
 
+def load_val_cached(cache_dir, key_parts, load):
+    """``load()`` (e.g. load_val with a VAE encoder) cached in ``cache_dir`` under the SHA-1 of ``key_parts`` (shard
+    names, sample count, resolution, encoder identity ...), so a validation set that has to be encoded is encoded
+    once per configuration (reference aurora/data.py:337-364). Written to a temporary name and renamed."""
+    import hashlib
+    key = hashlib.sha1(json.dumps(key_parts, sort_keys=True, default=str).encode()).hexdigest()[:16]
+    path = os.path.join(cache_dir, f"val_{key}.pt")
+    if os.path.exists(path):
+        return torch.load(path, weights_only=True)
+    val = load()
+    os.makedirs(cache_dir, exist_ok=True)
+    torch.save(tuple(val), path + ".tmp")
+    os.replace(path + ".tmp", path)
+    return val
+
+
 def write_synthetic_shards(root, n_shards=2, per_shard=16, side=16, caps_per_image=2, tok_len=64, seed=0,
                            lm_suffix="", lm_len=96):
     """Small shard set in the on-disk format (tests and smoke runs; no network needed)."""
