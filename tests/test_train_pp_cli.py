@@ -221,3 +221,6 @@ def test_pipeline_ema_eval_and_merge_checkpoints(tmp_path):
     assert merged == ["step_0000001.pt", "step_0000002.pt"]
     ck = torch.load(tmp_path / "merge" / merged[-1], weights_only=False)
     assert ck["step"] == 2 and ck["total_steps"] == 2 and "blocks.3.mlp.out_proj.weight" in ck["den"] and ck["te"]
+    import json
+    rows = [json.loads(line) for line in open(tmp_path / "log.jsonl")]  # written by the last stage's rank
+    assert any("train/loss" in r and r["step"] == 2 for r in rows)

@@ -488,6 +488,9 @@ def run_fm(args, den_cfg, te_cfg, lay, device, ctl, text_group):
     eval_every = args.eval_every or 0
     val = pp_val_data(args, te_cfg, den_cfg, tr, lm, lm_client, real, use_ids, device) \
         if eval_every and dist.get_rank() == 0 else None
+    from trenowanie_generatora_obrazkow_b200.utils.logging import RunLogger
+    logger = RunLogger(args.out, vars(args), enabled=tr.last and tr.replica == 0 and not args.no_wandb,
+                       project=args.wandb)  # log.jsonl (+ wandb when logged in) on the rank that holds the loss
     t0 = time.time()
     while step < args.steps:
         ts = time.time()
@@ -538,6 +541,8 @@ def run_fm(args, den_cfg, te_cfg, lay, device, ctl, text_group):
             dt = time.time() - t0
             print(f"[stage {tr.stage}] step {step}/{args.steps} loss {loss.item():.4f} "
                   f"{args.log_every * n * dp / dt:.1f} img/s", flush=True)
+            logger.log({"train/loss": loss.item(), "train/img_per_s": args.log_every * n * dp / dt,
+                        "train/samples": samples}, step)
             t0 = time.time()
         if args.ckpt_every and (step % args.ckpt_every == 0 or step == args.steps):
             pp_checkpoint.save(tr, args.out, step, samples, vars(args), save_group, learner_group,
@@ -546,11 +551,13 @@ def run_fm(args, den_cfg, te_cfg, lay, device, ctl, text_group):
             res = pp_checkpoint.ema_eval(tr, save_group, val, device)
             if res is not None:
                 print(f"[eval] step {step} | EMA " + " ".join(f"{k}={v:.4f}" for k, v in res.items()), flush=True)
+                logger.log(res, step)  # enabled only where rank 0 is also the last stage (pp 1)
             dist.barrier(group=learner_group)
         if args.merge_every and step >= args.merge_start * args.steps and (
                 step % args.merge_every == 0 or step == args.steps):  # raw weights for merge.py (WSM)
             pp_checkpoint.merge_save(tr, args.out, step, args.steps, save_group)
             dist.barrier(group=learner_group)
+    logger.close()
     for c in {id(c): c for c in (lm_client, vae_client) if c is not None}.values():
         c.stop()
 
@@ -751,6 +758,8 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
             for p, w in zip(ema.params, live):
                 p.copy_(w)
 
+    from trenowanie_generatora_obrazkow_b200.utils.logging import RunLogger
+    logger = RunLogger(args.out, vars(args), enabled=lrank == 0 and not args.no_wandb, project=args.wandb)
     version = 0
     # the next cycle's batch in preparation: {"step", "kw"} plus either "actor": (client, job) while the actor rolls
     # it out, or "x", "t", "teacher" (a deferred teacher request) once the states are here
@@ -857,6 +866,9 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
         if lrank == 0 and ((step + 1) % args.log_every == 0 or step + 1 == args.steps):
             print(f"[learner] step {step + 1}/{args.steps} opd loss {float(loss):.4f} res {res} "
                   f"{(time.time() - t0) / args.log_every:.2f} s/step", flush=True)
+            logger.log({"opd/loss": float(loss), "opd/resolution": res, "opd/s_per_step":
+                        (time.time() - t0) / args.log_every, "opd/reuse_pass": learner.uses,
+                        "opd/fresh_trajectories": samples}, step + 1)
             if args.opd_learner_profile:
                 print(f"[learner profile] captions {t_data * 1e3:.0f} ms, rollouts {t_roll * 1e3:.0f} ms, teacher "
                       f"{t_teach * 1e3:.0f} ms ({args.opd_parts} parts), student {t_learn * 1e3:.0f} ms, prefetch "
@@ -869,6 +881,7 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
             if ema is not None and val is not None:
                 res = ema_eval()
                 print(f"[eval] step {step + 1} | EMA " + " ".join(f"{k}={v:.4f}" for k, v in res.items()), flush=True)
+                logger.log(res, step + 1)
             dist.barrier(group=ckpt_group)
         if args.ckpt_every and ((step + 1) % args.ckpt_every == 0 or step + 1 == args.steps):
             # the caption position saved is where the next untrained fresh batch starts (batches drawn ahead for
@@ -879,6 +892,7 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
                                extra=dict(opd_caption_micro=cap_start.get(nxt, cap_read[0])))
             for k in [k for k in cap_start if k < nxt]:
                 del cap_start[k]
+    logger.close()
     if lookahead is not None:
         lookahead.close()
     if lm_client is not None:

@@ -30,6 +30,8 @@ class RunLogger:
         self.out_dir = out_dir
         self.enabled = enabled
         self.wb = None
+        if enabled:
+            os.makedirs(out_dir, exist_ok=True)
         self.jsonl = open(os.path.join(out_dir, "log.jsonl"), "a") if enabled else None
         if enabled and wandb_available():
             import wandb
