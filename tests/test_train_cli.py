@@ -150,6 +150,7 @@ def test_fid_per_shard_and_export_init(shards, tmp_path):
     assert len(fds) == 2 and "step 0 FD" in fds[0] and "step 2 FD" in fds[1], log[-2000:]
     log = _run(common + ["--steps", "2", "--eval-only", "--per-shard", "4"])
     assert log.count("per-shard") == 3 and "val" in log  # 1 held-out shard + the first / middle training shard
+    assert '"text_gain"' in log and '"val_no_text/loss"' in log  # the loss with empty prompts, and the gap
     ex = str(tmp_path / "export")
     subprocess.run([sys.executable, os.path.join(ROOT, "export.py"), os.path.join(out, "latest.pt"), ex], cwd=ROOT,
                    check=True, capture_output=True, env=dict(os.environ, CUDA_VISIBLE_DEVICES=""))

@@ -418,7 +418,15 @@ def main():
         logger.log({"val/fd": fd}, step)
 
     if args.eval_only:
-        log(json.dumps(run_eval(), indent=1))
+        res = run_eval()
+        if val is not None and not torch.is_floating_point(val[1]):
+            # the same images with the empty prompt: the gap shows how much the model uses the text
+            # (reference train.py:681-687)
+            null = torch.as_tensor(te.null_ids(), dtype=val[1].dtype).expand_as(val[1]).clone()
+            no_text = with_ema(lambda: evaluate(te, den, (val[0], null), device))
+            res.update({k.replace("val/", "val_no_text/"): v for k, v in no_text.items()})
+            res["text_gain"] = no_text["val/loss"] - res["val/loss"]
+        log(json.dumps(res, indent=1))
         if args.per_shard and master and not args.synthetic:
             # held-out shards, then the first and a middle training shard of every subset: a loss much lower on
             # the training shards than on the held-out ones means memorisation rather than generalisation
