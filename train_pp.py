@@ -743,7 +743,7 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
 
     from trenowanie_generatora_obrazkow_b200.train.evaluate import evaluate
     eval_every = args.eval_every or 0
-    use_ids = cap_loader is not None or te_cfg.backend != "states" or args.lm_rank > 0
+    use_ids = local_lm is not None or lm_client is not None  # else the loop's own random states (synthetic runs)
     val = pp_val_data(args, te_cfg, den_cfg, None, local_lm, lm_client, cap_loader is not None, use_ids, device) \
         if eval_every and lrank == 0 else None
 
