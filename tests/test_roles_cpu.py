@@ -161,7 +161,8 @@ def _deferred_actor_worker(rank, world, port, d):
         job = client.request(noise, st, valid, 5, v, deferred=True)  # held by the actor ...
         plain = client.rollouts(noise, st, valid, 5, v)  # ... while a plain job of the same batch goes through
         held = client.collect(job)
-        torch.save(dict(plain=plain, held=held), os.path.join(d, "out.pt"))
+        shifted = client.rollouts(noise, st, valid, 5, v, shift=3.0)  # the batch resolution's shift
+        torch.save(dict(plain=plain, held=held, shifted=shifted), os.path.join(d, "out.pt"))
         client.stop()
     dist.destroy_process_group()
 
@@ -171,4 +172,9 @@ def test_deferred_actor_job_equals_a_plain_one():
         mp.spawn(_deferred_actor_worker, args=(2, _port(), d), nprocs=2, join=True)
         out = torch.load(os.path.join(d, "out.pt"))
         assert torch.equal(out["plain"][0], out["held"][0]) and torch.equal(out["plain"][1], out["held"][1])
-        assert torch.load(os.path.join(d, "jobs.pt")) == 2
+        from trenowanie_generatora_obrazkow_b200.train.opd import dance_picks, opd_grid
+        g = torch.Generator().manual_seed(KW["seed"] * 1_000_003 + 0 * 1009 + 5 + 7)
+        picks = dance_picks(2, KW["m"], KW["K"], KW["beta"], KW["seed"], 0, 5)
+        want = opd_grid(KW["K"], 3.0, torch.rand((), generator=g).item())[picks].flatten()
+        assert torch.allclose(out["shifted"][1], want) and not torch.allclose(out["shifted"][1], out["plain"][1])
+        assert torch.load(os.path.join(d, "jobs.pt")) == 3

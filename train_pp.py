@@ -803,7 +803,7 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
             if actor is not None:
                 if sender is not None:
                     version, sent = sender.send(), True
-                states, t = actor_for(step).rollouts(noise, st, valid, step, version)
+                states, t = actor_for(step).rollouts(noise, st, valid, step, version, shift=shift)
                 kw_all = dict(lm_states=rep(st), valid=rep(valid))
             else:
                 states, t, kw_all = learner.rollout_states(step, st, valid, noise, shift)
@@ -820,7 +820,8 @@ def run_opd(args, den_cfg, te_cfg, lay, device, ctl, text_group):
             noise_n, st_n, valid_n = fresh_data(nxt)
             client = actor_for(nxt)
             pending = dict(step=nxt, kw=dict(lm_states=rep(st_n), valid=rep(valid_n)),
-                           actor=(client, client.request(noise_n, st_n, valid_n, nxt, version, deferred=True)))
+                           actor=(client, client.request(noise_n, st_n, valid_n, nxt, version, deferred=True,
+                                                         shift=step_shift(nxt))))
         elif pending is not None and "actor" in pending and step == pending["step"] - 1:
             states_to_teacher(pending)  # last replay update of the cycle: the teacher scores meanwhile
         if fresh:

@@ -19,7 +19,8 @@ headers) travel over a Gloo group, so servers can receive from any learner; tens
   can close a cycle (learner X's stream waits on its send to server 2, which waits on server 2's send to learner Y,
   which waits on Y's send to server 1, which waits on server 1's send to X). With ``isend`` a compute stream waits
   only on the receives its own work reads, and the protocols' data dependencies form no cycle.
-* Actor: header [KIND_ROLLOUT, B, C, h, w, L, D, step, version, deferred] with noise / LM states / valid; the actor
+* Actor: header [KIND_ROLLOUT, B, C, h, w, L, D, step, version, deferred, shift x 1000 (0: the actor's default)] with
+  noise / LM states / valid (the shift is the batch resolution's, as a local rollout would use); the actor
   generates the rollout states with the snapshot it holds and replies with (states (B m, C, h, w), t (B m,)); a
   deferred job's reply is held until the learner's [KIND_COLLECT] (one job per learner at a time), so a learner
   trains while its next batch is rolled out. It refuses a job whose required snapshot version is newer than its own
@@ -32,7 +33,7 @@ import torch
 import torch.distributed as dist
 
 KIND_STOP, KIND_VELOCITY, KIND_ROLLOUT, KIND_SNAPSHOT, KIND_COLLECT = 0, 1, 2, 3, 4
-HDR = 10
+HDR = 12
 
 
 class RoleLayout:
@@ -263,7 +264,7 @@ class RolloutActor:
                 for buf in held.pop(src):
                     out.send(buf, src)
                 continue
-            _, B, C, hh, w, L, D, step, need, deferred = h[:10].tolist()
+            _, B, C, hh, w, L, D, step, need, deferred, shift_milli = h[:11].tolist()
             if need > self.version:
                 raise RuntimeError(f"actor holds snapshot {self.version}, job needs {need}")
             noise = torch.empty(B, C, hh, w, device=self.device)
@@ -275,7 +276,8 @@ class RolloutActor:
             g = torch.Generator().manual_seed(self.kw["seed"] * 1_000_003 + src * 1009 + step + 7)
             picks = dance_picks(B, m, K, self.kw["beta"], self.kw["seed"], src, step) if self.kw["method"] == "dance" \
                 else diffusion_picks(B, m, K, g)
-            ts = opd_grid(K, self.kw["shift"], torch.rand((), generator=g).item(), self.device)
+            shift = shift_milli / 1000 if shift_milli > 0 else self.kw["shift"]
+            ts = opd_grid(K, shift, torch.rand((), generator=g).item(), self.device)
             text, v = self.te(lm_states=st, valid=valid.bool())
             states = rollout(self.den, text, valid_to_len(v), noise, ts, picks, self.kw["mb"]).flatten(0, 1)
             t = ts[picks.to(self.device)].flatten().contiguous()
@@ -293,14 +295,15 @@ class ActorClient:
     def __init__(self, actor, control_group, m):
         self.actor, self.ctl, self.m = actor, control_group, m
 
-    def rollouts(self, noise, lm_states, valid, step, version):
-        return self.collect(self.request(noise, lm_states, valid, step, version))
+    def rollouts(self, noise, lm_states, valid, step, version, shift=None):
+        return self.collect(self.request(noise, lm_states, valid, step, version, shift=shift))
 
-    def request(self, noise, lm_states, valid, step, version, deferred=False):
+    def request(self, noise, lm_states, valid, step, version, deferred=False, shift=None):
         """Submit a rollout job; ``collect`` returns (states, t). Deferred: the actor holds the result until it is
         collected (one deferred job per learner and actor at a time)."""
         B = noise.shape[0]
-        dist.send(_hdr(KIND_ROLLOUT, B, *noise.shape[1:], *lm_states.shape[1:], step, version, int(deferred)),
+        dist.send(_hdr(KIND_ROLLOUT, B, *noise.shape[1:], *lm_states.shape[1:], step, version, int(deferred),
+                       round(shift * 1000) if shift else 0),
                   dst=self.actor, group=self.ctl)
         sends = _Outgoing()
         for buf in (noise.float().contiguous(), lm_states.contiguous(), valid.to(torch.uint8).contiguous()):
