@@ -38,7 +38,8 @@ def info(ck):
     out = dict(step=ck.get("step"), samples=ck.get("samples"), den_params=n(den), te_params=n(te),
                ema=ck.get("ema") is not None and len(ck["ema"]) > 0, opts=ck.get("opts") is not None,
                den_config=ck.get("den_config"), te_config=ck.get("te_config"), pp_layout=ck.get("pp_layout"),
-               outer=ck.get("outer") is not None, repa_proj=ck.get("repa_proj") is not None)
+               outer=ck.get("outer") is not None, repa_proj=ck.get("repa_proj") is not None,
+               extra=ck.get("extra") or {})  # e.g. the OPD caption-stream position
     return out
 
 

@@ -144,7 +144,7 @@ def test_ckpt_tools_info_block_norms_and_resume_cmd(tmp_path):
     latest = os.path.join(run, "latest.pt")
     ck = torch.load(latest, weights_only=False)
     res = T.main(["info", latest])
-    assert res["step"] == 2 and res["ema"] and res["den_params"] > 0
+    assert res["step"] == 2 and res["ema"] and res["den_params"] > 0 and res["extra"] == {}
     norms, depth = T.block_norms(ck, 2)
     assert set(norms) == {"raw", "EMA"} and depth == 4
     raw = dict(norms["raw"])
