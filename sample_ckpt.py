@@ -93,31 +93,42 @@ def main():
     for m in den.modules():
         if hasattr(m, "logit_mult"):
             m.logit_mult = a.attn_scale
-    prompts = a.prompt or PROMPTS
+    # the showcase prompts in English and in Polish (the same noise for prompt k in both grids, as the reference's
+    # sampler does), or the user's own prompts
+    if a.prompt:
+        sets = [("", a.prompt)]
+    else:
+        import sample as showcase
+        sets = [("en_", showcase.PROMPTS), ("pl_", showcase.PROMPTS_PL)]
     lm = isinstance(te_cfg, LMEncoderConfig)
-    ids = tokenize(prompts, te_cfg.max_tokens, load_tokenizer(a.tokenizer, getattr(te_cfg, "vocab_size", 8192)),
-                   lm=lm).to(device)
-    with torch.no_grad():
-        if lm:
-            frozen = build_frozen_lm(te_cfg, device, allow_random=a.random_lm)
-            z = sample(te, den, a.steps, a.cfg, a.seed, a.t_shift, batch=a.batch, lm_states=frozen.states(ids),
-                       valid=ids.ne(LM_PAD))
-        else:
-            z = sample(te, den, a.steps, a.cfg, a.seed, a.t_shift, batch=a.batch, ids=ids)
-    torch.save(dict(latents=z.cpu(), prompts=prompts, steps=a.steps, cfg=a.cfg, seed=a.seed),
-               os.path.join(a.out_dir, "latents.pt"))
+    frozen = build_frozen_lm(te_cfg, device, allow_random=a.random_lm) if lm else None
+    tok = load_tokenizer(a.tokenizer, getattr(te_cfg, "vocab_size", 8192))
     from PIL import Image
+    decoder = None
     if a.vae:
         from trenowanie_generatora_obrazkow_b200.sampling.vae import LatentDecoder
-        imgs = LatentDecoder(a.vae, device).decode(z)
-        kind = ""
-    else:
-        imgs = latent_preview(z)
-        kind = "_latent_preview"
-    for i, im in enumerate(imgs):
-        path = os.path.join(a.out_dir, f"{i:02d}{kind}.png")
-        Image.fromarray(im).save(path)
-        print(f"saved {path}: {prompts[i]}")
+        decoder = LatentDecoder(a.vae, device)
+    for prefix, prompts in sets:
+        ids = tokenize(prompts, te_cfg.max_tokens, tok, lm=lm).to(device)
+        with torch.no_grad():
+            if lm:
+                z = sample(te, den, a.steps, a.cfg, a.seed, a.t_shift, batch=a.batch, lm_states=frozen.states(ids),
+                           valid=ids.ne(LM_PAD))
+            else:
+                z = sample(te, den, a.steps, a.cfg, a.seed, a.t_shift, batch=a.batch, ids=ids)
+        torch.save(dict(latents=z.cpu(), prompts=prompts, steps=a.steps, cfg=a.cfg, seed=a.seed),
+                   os.path.join(a.out_dir, f"{prefix}latents.pt"))
+        imgs, kind = (decoder.decode(z), "") if decoder is not None else (latent_preview(z), "_latent_preview")
+        for i, im in enumerate(imgs):
+            Image.fromarray(im).save(os.path.join(a.out_dir, f"{prefix}{i:02d}{kind}.png"))
+        if prefix and len(imgs) == 8:  # the 4 x 2 grid of a showcase set
+            h, w = imgs[0].shape[:2]
+            grid = Image.new("RGB", (4 * w, 2 * h))
+            for i, im in enumerate(imgs):
+                grid.paste(Image.fromarray(im), ((i % 4) * w, (i // 4) * h))
+            grid.save(os.path.join(a.out_dir, f"grid_{prefix[:-1]}{kind}.png"))
+        print(f"saved {len(imgs)} images{' and a grid' if prefix and len(imgs) == 8 else ''} to {a.out_dir} "
+              f"({prefix[:-1] or 'your prompts'})", flush=True)
     if a.export:
         export_weights(te, den, a.out_dir, dict(steps=a.steps, cfg=a.cfg, seed=a.seed, step=info["step"],
                                                 weights=info["weights"]))

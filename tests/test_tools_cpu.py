@@ -57,6 +57,10 @@ def test_train_merge_sample_export_chain(tmp_path):
     assert os.path.exists(os.path.join(so, "transformer", "diffusion_pytorch_model.safetensors"))
     # the export reloads through the directory path
     _py("sample_ckpt.py", so, "--out-dir", str(tmp_path / "s2"), "--steps", "1", "--prompt", "x")
+    # no --prompt: the English and Polish showcase grids, the same noise per prompt in both
+    _py("sample_ckpt.py", so, "--out-dir", str(tmp_path / "s3"), "--steps", "1", "--batch", "8")
+    made = set(os.listdir(tmp_path / "s3"))
+    assert {"grid_en_latent_preview.png", "grid_pl_latent_preview.png", "en_latents.pt", "pl_latents.pt"} <= made
 
 
 def test_export_import_roundtrip(tmp_path):
